@@ -1,0 +1,219 @@
+/*
+ * vvli_cuda.h - C ABI of the B200 (sm_100a) decoder runtime.
+ *
+ * This is the drop-in boundary for VVLI's dense decoder hot path.  The Zig host
+ * (src/main.zig, src/generator.zig) binds these functions with @cImport and
+ * links libvvli_cuda.so from build.zig; every entry point uses plain pointers,
+ * sizes and the plain-C structs below (no C++ or torch types).  Each function
+ * names the reference interface it replaces as path:line inside VVLI.
+ *
+ * Conventions (the reference's own FFI convention, src/gpu/metal_smoke.zig:5-11:
+ * an extern struct for results and an int return code):
+ *   - every function returns int: VVLI_OK (0) on success, a VVLI_ERR_* code
+ *     otherwise; vvli_cuda_strerror() maps codes to text;
+ *   - a context is single-caller (like llm.Runner, src/llm.zig:688-700) and
+ *     every call is synchronous on return;
+ *   - host buffers passed in are only read during the call; output buffers are
+ *     host memory written before the call returns.
+ */
+#ifndef VVLI_CUDA_H
+#define VVLI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Error codes.  1..9 map 1:1 onto llm.Error (src/llm.zig:17-27) and
+ * generator.Error (src/generator.zig:8-12); 20.. are added by this runtime. */
+enum vvli_status {
+  VVLI_OK = 0,
+  VVLI_ERR_CONTEXT_FULL = 1,          /* llm.Error.ContextFull */
+  VVLI_ERR_INVALID_CONFIG = 2,        /* llm.Error.InvalidConfig */
+  VVLI_ERR_INVALID_TOKEN = 3,         /* llm.Error.InvalidToken */
+  VVLI_ERR_INVALID_WEIGHT = 4,        /* llm.Error.InvalidWeight */
+  VVLI_ERR_UNSUPPORTED_DTYPE = 5,     /* llm.Error.UnsupportedDType */
+  VVLI_ERR_UNSUPPORTED_ARCH = 6,      /* llm.Error.UnsupportedModelArchitecture */
+  VVLI_ERR_EMPTY_PROMPT = 7,          /* generator.Error.EmptyPrompt */
+  VVLI_ERR_OUTPUT_TOO_SMALL = 8,      /* generator.Error.OutputTooSmall */
+  VVLI_ERR_INVALID_SAMPLING = 9,      /* generator.Error.InvalidSamplingOptions */
+  VVLI_ERR_CUDA = 20,                 /* a CUDA runtime call failed */
+  VVLI_ERR_NCCL = 21,                 /* an NCCL call failed or NCCL is missing */
+  VVLI_ERR_TIMEOUT = 22,              /* a bounded device-side wait gave up */
+  VVLI_ERR_OOM = 23,                  /* device allocation failed */
+  VVLI_ERR_NOT_LOADED = 24,           /* forward called before weights were loaded */
+  VVLI_ERR_INVALID_ARGUMENT = 25,     /* null pointer, bad size or bad rank */
+  VVLI_ERR_UNIMPLEMENTED = 26
+};
+
+/* llm.Architecture (src/llm.zig:29-43). */
+enum vvli_architecture {
+  VVLI_ARCH_LLAMA = 0,
+  VVLI_ARCH_MISTRAL = 1,
+  VVLI_ARCH_OLMOE = 2,
+  VVLI_ARCH_QWEN2 = 3
+};
+
+/* llm.RopeLayout (src/llm.zig:50-53). */
+enum vvli_rope_layout {
+  VVLI_ROPE_INTERLEAVED = 0,
+  VVLI_ROPE_SPLIT_HALF = 1
+};
+
+/* Extension: rope_scaling from config.json.  The reference ignores it
+ * (src/llm.zig:98-145 never reads it); VVLI_ROPE_SCALING_NONE reproduces the
+ * reference exactly. */
+enum vvli_rope_scaling {
+  VVLI_ROPE_SCALING_NONE = 0,
+  VVLI_ROPE_SCALING_LLAMA3 = 1
+};
+
+/* Mirror of llm.Config (src/llm.zig:77-96) plus the rope_scaling extension. */
+typedef struct vvli_model_config {
+  uint64_t vocab_size;
+  uint64_t hidden_size;
+  uint64_t intermediate_size;
+  uint64_t num_hidden_layers;
+  uint64_t num_attention_heads;
+  uint64_t num_key_value_heads;
+  uint64_t max_position_embeddings;
+  uint64_t num_experts;            /* 0 = dense (FeedForwardKind.dense) */
+  uint64_t num_experts_per_token;
+  uint32_t architecture;           /* enum vvli_architecture */
+  uint32_t rope_layout;            /* enum vvli_rope_layout */
+  float rope_theta;
+  float rms_norm_eps;
+  uint32_t tie_word_embeddings;    /* bool */
+  uint32_t qkv_bias;               /* bool */
+  uint32_t qk_norm;                /* bool; only OLMoE sets it, which is rejected */
+  uint32_t eos_token_id;
+  uint32_t pad_token_id;
+  uint32_t rope_scaling_type;      /* enum vvli_rope_scaling */
+  float rope_scaling_factor;
+  float rope_low_freq_factor;
+  float rope_high_freq_factor;
+  uint32_t _pad0;
+  uint64_t rope_original_max_position;
+} vvli_model_config;
+
+/* Per-call options of the decode path. */
+typedef struct vvli_generate_stats {
+  uint64_t prompt_tokens;
+  uint64_t generated_tokens;
+  int64_t prefill_nanoseconds;     /* generator.Stats (src/generator.zig:25-43) */
+  int64_t decode_nanoseconds;
+  int64_t total_nanoseconds;
+} vvli_generate_stats;
+
+/* generator.Options sampling fields (src/generator.zig:14-23).  eos < 0 means
+ * "no eos" (eos_token_id = null). */
+typedef struct vvli_sample_options {
+  float temperature;
+  float top_p;
+  uint64_t top_k;
+  float repeat_penalty;
+  uint32_t _pad0;
+  uint64_t repeat_last_n;
+} vvli_sample_options;
+
+typedef struct vvli_ctx vvli_ctx;
+
+/* Size of the opaque NCCL unique id blob (ncclUniqueId is 128 bytes). */
+#define VVLI_NCCL_ID_BYTES 128
+
+/* Text for a status code.  Replaces writeAppError's error names
+ * (src/main.zig:438-467).  Never returns NULL. */
+const char* vvli_cuda_strerror(int status);
+
+/* Number of bf16 elements of the host weight blob for `cfg`, with every tensor
+ * at a 64-byte aligned offset.  Replaces llm.storageElementCount
+ * (src/llm.zig:814-837) for kind = .bf16. */
+int vvli_cuda_storage_elements(const vvli_model_config* cfg, uint64_t* out_elements);
+
+/* Fills `id` (VVLI_NCCL_ID_BYTES bytes) with a fresh NCCL unique id, to be
+ * shared by the caller with every tensor-parallel rank before
+ * vvli_cuda_create.  No counterpart in the reference (it has no
+ * collectives); needed for the tensor-parallel split of src/llm.zig:732-766. */
+int vvli_cuda_nccl_unique_id(void* id);
+
+/* Creates a context on `device` for rank `tp_rank` of `tp_size` ranks.
+ * Replaces KVCache.init + Scratch.init + Runner.init
+ * (src/llm.zig:546-562, 626-668, 694-700; called from src/main.zig:161-171).
+ * `max_seq` mirrors KVCache.init's max_seq_len (0 < max_seq <=
+ * max_position_embeddings, else VVLI_ERR_INVALID_CONFIG).  `max_batch` bounds
+ * vvli_cuda_forward_batch and vvli_cuda_prefill chunk sizes.  For tp_size > 1,
+ * `nccl_unique_id` must be the same blob on all ranks. */
+int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int tp_size,
+                     const void* nccl_unique_id, uint64_t max_seq, uint64_t max_batch,
+                     vvli_ctx** out_ctx);
+
+/* Uploads the bf16 weight blob laid out exactly as llm.OwnedModel.storage_bf16
+ * (src/llm.zig:415-537: embedding; per layer [input_norm, q, q_bias?, k,
+ * k_bias?, v, v_bias?, o, post_norm, gate, up, down]; final_norm; lm_head?).
+ * Each rank copies only its own tensor-parallel shard.  Replaces the
+ * safetensors/GGUF loaders' final copy into OwnedModel (src/llm.zig:923-1006);
+ * the caller keeps ownership of `blob`. */
+int vvli_cuda_load_weights(vvli_ctx* ctx, const uint16_t* blob, uint64_t n_elements);
+
+/* Benchmark helper with no counterpart in the reference: fills the device
+ * weights with the seeded synthetic model (every matrix and bias
+ * ~N(0, 0.02) by a 12-term Irwin-Hall sum, norms 1.0), bit-identical to the
+ * host generator that the CPU baseline uses, without a host blob. */
+int vvli_cuda_fill_synthetic(vvli_ctx* ctx, uint64_t seed);
+
+/* Zeroes the KV cache.  Replaces KVCache.clear (src/llm.zig:576-579). */
+int vvli_cuda_reset(vvli_ctx* ctx);
+
+/* One token through all layers at `position`.  Replaces Runner.forwardToken
+ * (src/llm.zig:702-709).  Errors: VVLI_ERR_INVALID_TOKEN when token >= vocab,
+ * VVLI_ERR_CONTEXT_FULL when position >= max_seq.  `logits_out` (vocab floats,
+ * may be NULL) receives the logits the reference returns as a borrowed slice;
+ * `argmax_out` (may be NULL) receives llm.argmax of them (src/llm.zig:778-789,
+ * first index wins ties). */
+int vvli_cuda_forward_token(vvli_ctx* ctx, uint32_t token, uint64_t position,
+                            float* logits_out, uint32_t* argmax_out);
+
+/* Like vvli_cuda_forward_token with a caller-supplied fp32 embedding of
+ * hidden_size floats.  Replaces Runner.forwardEmbedding (src/llm.zig:711-718). */
+int vvli_cuda_forward_embedding(vvli_ctx* ctx, const float* embedding, uint64_t position,
+                                float* logits_out, uint32_t* argmax_out);
+
+/* Runs `n` prompt tokens at positions start_position.. in one batched pass
+ * (tensor-core GEMMs and causal attention).  Equal, within tolerance, to n
+ * sequential vvli_cuda_forward_token calls; only the last token's logits are
+ * returned.  Replaces the per-token prefill loop of
+ * generateGreedyMeasuredInternal (src/generator.zig:243-251). */
+int vvli_cuda_prefill(vvli_ctx* ctx, const uint32_t* tokens, uint64_t n, uint64_t start_position,
+                      float* last_logits_out, uint32_t* argmax_out);
+
+/* Greedy generation entirely on the device: prefill `prompt`, then emit up to
+ * max_new_tokens argmax tokens, each fed back without a host round trip.
+ * Stops after emitting eos when eos_token_id >= 0.  Replaces generateGreedy /
+ * generateGreedyInto / generateGreedyMeasured with --greedy
+ * (src/generator.zig:142-175, 221-325).  `out` holds max_new_tokens entries;
+ * `out_count` receives the number produced; `stats` (may be NULL) receives
+ * the generator.Stats timings measured with the same boundaries. */
+int vvli_cuda_generate_greedy(vvli_ctx* ctx, const uint32_t* prompt, uint64_t n_prompt,
+                              uint64_t max_new_tokens, int64_t eos_token_id, uint32_t* out,
+                              uint64_t* out_count, vvli_generate_stats* stats);
+
+/* Copies the residual stream x after layer `layer` of the last forward call
+ * (hidden_size floats).  Debug entry point for per-layer parity; the
+ * reference keeps it in Scratch.x (src/llm.zig:612, 757, 765).  Requires the
+ * context to have been created with debug capture on (vvli_cuda_set_debug). */
+int vvli_cuda_set_debug(vvli_ctx* ctx, int enabled);
+int vvli_cuda_debug_hidden(vvli_ctx* ctx, int layer, float* out);
+
+/* Device-side timing of the last forward in milliseconds (CUDA events). */
+int vvli_cuda_last_forward_ms(vvli_ctx* ctx, float* out_ms);
+
+/* Destroys the context and frees all device memory. */
+int vvli_cuda_destroy(vvli_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VVLI_CUDA_H */

@@ -1,0 +1,89 @@
+"""ctypes binding of libvvli_cuda.so (the C ABI declared in include/vvli_cuda.h).
+
+The library is built in-tree by vvli_b200/csrc/Makefile.  There is no fallback:
+if the shared library is missing or fails to load, ``lib()`` raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+from .config import CModelConfig
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvvli_cuda.so")
+NCCL_ID_BYTES = 128
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+_cfgp = ctypes.POINTER(CModelConfig)
+_ctx = ctypes.c_void_p
+
+
+class CGenerateStats(ctypes.Structure):
+    _fields_ = [
+        ("prompt_tokens", ctypes.c_uint64),
+        ("generated_tokens", ctypes.c_uint64),
+        ("prefill_nanoseconds", ctypes.c_int64),
+        ("decode_nanoseconds", ctypes.c_int64),
+        ("total_nanoseconds", ctypes.c_int64),
+    ]
+
+
+class CSampleOptions(ctypes.Structure):
+    _fields_ = [
+        ("temperature", ctypes.c_float),
+        ("top_p", ctypes.c_float),
+        ("top_k", ctypes.c_uint64),
+        ("repeat_penalty", ctypes.c_float),
+        ("_pad0", ctypes.c_uint32),
+        ("repeat_last_n", ctypes.c_uint64),
+    ]
+
+
+# name -> (restype, argtypes); every function declared in include/vvli_cuda.h.
+SIGNATURES = {
+    "vvli_cuda_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "vvli_cuda_storage_elements": (ctypes.c_int, [_cfgp, _u64p]),
+    "vvli_cuda_nccl_unique_id": (ctypes.c_int, [ctypes.c_void_p]),
+    "vvli_cuda_create": (ctypes.c_int, [_cfgp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(_ctx)]),
+    "vvli_cuda_load_weights": (ctypes.c_int, [_ctx, _u16p, ctypes.c_uint64]),
+    "vvli_cuda_fill_synthetic": (ctypes.c_int, [_ctx, ctypes.c_uint64]),
+    "vvli_cuda_reset": (ctypes.c_int, [_ctx]),
+    "vvli_cuda_forward_token": (ctypes.c_int, [_ctx, ctypes.c_uint32, ctypes.c_uint64, _f32p, _u32p]),
+    "vvli_cuda_forward_embedding": (ctypes.c_int, [_ctx, _f32p, ctypes.c_uint64, _f32p, _u32p]),
+    "vvli_cuda_prefill": (ctypes.c_int, [_ctx, _u32p, ctypes.c_uint64, ctypes.c_uint64, _f32p, _u32p]),
+    "vvli_cuda_generate_greedy": (ctypes.c_int, [_ctx, _u32p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64,
+                                                 _u32p, _u64p, ctypes.POINTER(CGenerateStats)]),
+    "vvli_cuda_set_debug": (ctypes.c_int, [_ctx, ctypes.c_int]),
+    "vvli_cuda_debug_hidden": (ctypes.c_int, [_ctx, ctypes.c_int, _f32p]),
+    "vvli_cuda_last_forward_ms": (ctypes.c_int, [_ctx, _f32p]),
+    "vvli_cuda_destroy": (ctypes.c_int, [_ctx]),
+}
+
+_lib = None
+
+
+def lib():
+    """Loads libvvli_cuda.so once; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `make -C vvli_b200/csrc` "
+                "(or __graft_entry__.build()); there is no CPU fallback")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def strerror(status: int) -> str:
+    return lib().vvli_cuda_strerror(status).decode()
