@@ -1,0 +1,321 @@
+#!/usr/bin/env python
+"""Decode throughput of the dense decoder on B200, with its roofline and the CPU baseline.
+
+Workload: Llama-3-8B architecture, random-init bf16
+weights (seeded synthetic, ~N(0, 0.02)), a 512-token uniform-random prompt,
+then greedy decode at batch 1, one step = one decode token.  At N GPUs the
+model is tensor-parallel over the N ranks (strong scaling: the same sequence,
+the work of each token split across ranks).  Weights are 15 GB per token,
+larger than L2, so no L2 flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vvli|reference]
+
+Rank 0 prints one JSON line.  --impl reference times the reference's CPU
+decoder (the C++ restatement in oracle/, since the Zig reference cannot be
+built here) on this host's cores for the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s + HBM-roofline fraction at 1/2/4/8 B200 vs host-CPU ref"
+FALLBACK_HBM_GBS = 6650.0
+KERNEL_NAMES = {0: "gemv q|k|v (rmsnorm prologue)", 1: "gemv o_proj (+residual)",
+                2: "gemv gate|up (rmsnorm prologue, silu*mul)", 3: "gemv down_proj (+residual)",
+                4: "gemv lm_head (final norm, argmax)"}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["vvli", "reference"], default="vvli")
+    ap.add_argument("--config", default="llama3-8b")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--kernel-reps", type=int, default=64)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+def ncu_traffic(kernel_key):
+    """DRAM bytes per launch of a kernel from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "ncu_summary.txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch") and kernel_key in line:
+                return float(line.split("=")[-1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+    REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, local_rank):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [v for v in vis.split(",") if v.strip()]
+        self.index = ids[local_rank] if local_rank < len(ids) and ids[local_rank].isdigit() else str(local_rank)
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-i", self.index,
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) == 8:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = sorted({self.REASONS[i] for r in rows for i in range(4) if r[4 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def time_oracle(cfg, seed, seconds, min_tokens=2, max_tokens=None):
+    """Times the CPU oracle's decode forwards (threads = all host cores)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    import numpy as np
+    oracle.build()
+    max_seq = 512
+    t0 = time.perf_counter()
+    r = oracle.RefRunner(cfg, synthetic_seed=seed, max_seq=max_seq, threads=0)
+    gen_s = time.perf_counter() - t0
+    tok = int(np.random.default_rng(1).integers(0, cfg.vocab_size))
+    logits = r.forward_token(tok, 0)  # warm-up (first touch)
+    pos, n, t_start = 1, 0, time.perf_counter()
+    while True:
+        tok = oracle.argmax(logits)
+        logits = r.forward_token(tok, pos)
+        pos += 1
+        n += 1
+        el = time.perf_counter() - t_start
+        if (n >= min_tokens and el >= seconds) or (max_tokens and n >= max_tokens) or pos >= max_seq:
+            break
+    cores = min(os.cpu_count() or 1, 64)  # linearInto spawns at most 64 workers (src/llm.zig:11)
+    sample = (f"{n} greedy decode tokens of the full {cfg.num_hidden_layers}-layer model at positions 1-{n} "
+              f"(weights generated in {gen_s:.1f} s, excluded), {os.cpu_count()} host threads visible")
+    r.close()
+    return n / el, cores, sample
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    from vvli_b200.config import PRESETS
+    cfg = PRESETS[args.config]()
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    import numpy as np
+    oracle.build()
+    t0 = time.perf_counter()
+    r = oracle.RefRunner(cfg, synthetic_seed=args.seed, max_seq=min(cfg.max_position_embeddings, 1024), threads=0)
+    gen_s = time.perf_counter() - t0
+    tok = int(np.random.default_rng(1).integers(0, cfg.vocab_size))
+    pos = 0
+    logits = None
+    tw = time.perf_counter()
+    for _ in range(max(1, args.warmup)):
+        logits = r.forward_token(tok, pos)
+        tok = oracle.argmax(logits)
+        pos += 1
+    per_tok = (time.perf_counter() - tw) / max(1, args.warmup)
+    steps = min(args.steps, max(2, int(150.0 / max(per_tok, 1e-6))), r.max_seq - pos)
+    t = time.perf_counter()
+    for _ in range(steps):
+        logits = r.forward_token(tok, pos)
+        tok = oracle.argmax(logits)
+        pos += 1
+    el = time.perf_counter() - t
+    value = steps / el
+    cores = min(os.cpu_count() or 1, 64)
+    sample = (f"{steps} of {args.steps} requested greedy decode steps (bounded to ~150 s), full model, positions "
+              f"{pos - steps}-{pos - 1}; weights generated in {gen_s:.1f} s (excluded)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": 1000.0 * el / steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, cfg, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample,
+                             "what": "C++ restatement of the reference CPU path (src/llm.zig, src/generator.zig); "
+                                     "the Zig reference cannot be built here"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args, cfg, n):
+    return {"workload": f"{args.config} greedy decode, batch 1, {args.prompt}-token prompt (BASELINE configs[4])",
+            "model": args.config, "global_batch": 1, "seq_len": args.prompt, "ctx": cfg.max_position_embeddings,
+            "parallelism": f"tp{n}", "weights": "bf16 synthetic ~N(0,0.02), seeded", "activations": "f32",
+            "kv_cache": "f32 paged", "l2": "inputs larger than L2 (every step streams all weights, >15 GB)"}
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import vvli_b200
+    from vvli_b200.config import PRESETS, decode_bytes_per_token
+
+    n = world
+    torch.cuda.set_device(local_rank)
+    nccl_id = None
+    if n > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank), timeout=timedelta(seconds=300))
+        obj = [vvli_b200.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+
+    def barrier():
+        if n > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def allmax(v):
+        if n == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = PRESETS[args.config]()
+    max_seq = min(cfg.max_position_embeddings, args.prompt + args.warmup + args.steps + args.e2e_steps + 16)
+    runner = vvli_b200.Runner(cfg, max_seq=max_seq, device=local_rank, tp_rank=rank, tp_size=n, nccl_id=nccl_id)
+    runner.fill_synthetic(args.seed)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, size=args.prompt).astype(np.uint32)
+    runner.prefill(prompt, 0, logits=False)
+    runner.decode(max(3, args.warmup))
+
+    # ---- device-timed decode: K graph replays, inputs resident in HBM
+    clocks = Clocks(local_rank)
+    barrier()
+    clocks.start()
+    pos0 = args.prompt + max(3, args.warmup)
+    barrier()
+    _, ms = runner.decode(args.steps)
+    barrier()
+    clk = clocks.stop()
+    ms = allmax(ms)
+    value = args.steps / (ms / 1000.0)
+    ms_per_step = ms / args.steps
+
+    # ---- end to end through the C ABI: host token in, logits and argmax out, every step
+    tok = runner.last_argmax if runner.last_argmax is not None else 0
+    pos = pos0 + args.steps
+    tok = int(tok)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        runner.forward_token(tok, pos, logits=True)
+        tok = runner.last_argmax
+        pos += 1
+    e2e_s = allmax(time.perf_counter() - t0)
+    e2e = {"value": args.e2e_steps / e2e_s, "unit": "tok/s",
+           "h2d_bytes_per_step": 4 + 32, "d2h_bytes_per_step": cfg.vocab_size * 4 + 32,
+           "api": "vvli_cuda_forward_token (host token in; host logits + argmax out; synchronous)"}
+
+    # ---- roofline of the dominant kernel, timed alone over every layer's weights
+    hbm, peak_src = peaks()
+    per_token = {}
+    for k in range(5):
+        kms, kbytes = runner.time_kernel(k, args.kernel_reps)
+        count = 1 if k == 4 else cfg.num_hidden_layers
+        per_token[k] = (kms * count, kms, kbytes)
+    dom = max(per_token, key=lambda k: per_token[k][0])
+    _, dms, dbytes = per_token[dom]
+    achieved = dbytes / (dms / 1000.0) / 1e9
+    roofline = {"kernel": KERNEL_NAMES[dom], "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": peak_src, "traffic": ncu_traffic(f"kernel{dom}"),
+                "bytes_per_launch": dbytes, "launch_ms": dms,
+                "all_kernels": {KERNEL_NAMES[k]: {"ms": v[1], "GB/s": v[2] / (v[1] / 1000.0) / 1e9}
+                                for k, v in per_token.items()}}
+    mean_pos = pos0 + args.steps // 2
+    step_bytes = decode_bytes_per_token(cfg, mean_pos) / n
+    step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
+    step_roofline = {"bytes_per_token_per_gpu": step_bytes, "achieved": step_gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": step_gbs / hbm, "frac_of_8TBs_spec": step_gbs / 8000.0}
+
+    launches_per_step = 1 + 5 * cfg.num_hidden_layers + 1 + (1 if n > 1 else 0)
+    cpu = None
+    if rank == 0 and n == 1 and not args.no_cpu_baseline:
+        v, cores, sample = time_oracle(cfg, args.seed, args.cpu_seconds)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": n, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, cfg, n),
+                "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches_per_step * args.steps, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    runner.close()
+    if n > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -199,6 +199,23 @@ int vvli_cuda_generate_greedy(vvli_ctx* ctx, const uint32_t* prompt, uint64_t n_
                               uint64_t max_new_tokens, int64_t eos_token_id, uint32_t* out,
                               uint64_t* out_count, vvli_generate_stats* stats);
 
+/* Continues greedy decoding on the device from the state the last forward
+ * left: runs n_steps forwards, each fed the argmax of the one before (the
+ * decode loop of generateGreedyInto, src/generator.zig:311-323, with the
+ * argmax taken on the device).  `out_tokens` (n_steps entries, may be NULL)
+ * receives the argmax of each forward; `device_ms` (may be NULL) the
+ * CUDA-event time of the n_steps forwards.  VVLI_ERR_CONTEXT_FULL when the
+ * last forward would pass max_seq. */
+int vvli_cuda_decode(vvli_ctx* ctx, uint64_t n_steps, uint32_t* out_tokens, float* device_ms);
+
+/* Measurement helper with no counterpart in the reference: times one decode
+ * kernel alone with CUDA events on the context's stream, cycling over every
+ * layer's weights so that no launch finds its weights in L2.  kernel: 0 q|k|v
+ * GEMV, 1 o_proj GEMV, 2 gate|up GEMV, 3 down GEMV, 4 LM-head GEMV.
+ * `avg_ms` receives the mean launch duration, `bytes` the algorithmic HBM
+ * bytes of one launch (weights, norm/bias vectors, input and output). */
+int vvli_cuda_time_kernel(vvli_ctx* ctx, int kernel, int reps, float* avg_ms, double* bytes);
+
 /* Copies the residual stream x after layer `layer` of the last forward call
  * (hidden_size floats).  Debug entry point for per-layer parity; the
  * reference keeps it in Scratch.x (src/llm.zig:612, 757, 765).  Requires the

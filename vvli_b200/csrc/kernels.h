@@ -1,0 +1,91 @@
+// kernels.h - parameter blocks and launchers of the decode kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vvli {
+
+// Device-resident scalars of the current step.  The captured step graph
+// reads them, so one graph serves every position and token.
+struct StepState {
+  int pos;            // position of the token being processed
+  int prompt_len;     // seq_tokens[0, prompt_len) are fixed prompt tokens
+  int max_seq;        // KV capacity in positions
+  int use_embedding;  // 1: x comes from emb_in instead of the embedding table
+  int argmax;         // argmax of the last logits
+  int err;            // non-zero: a kernel found an invalid state (VVLI_ERR_* code)
+  int batch;          // rows of the batched step
+  int pad;
+};
+
+struct RopeParams {
+  float theta;
+  int layout;   // 0 interleaved, 1 split-half
+  int scaling;  // 0 none, 1 llama3
+  float factor, low, high, orig;
+};
+
+enum GemvEpilogue { EPI_PLAIN = 0, EPI_SILU_MUL = 1, EPI_ARGMAX = 2 };
+
+struct GemvParams {
+  const uint16_t* W;       // [rows, K] bf16 row-major; rows of a pair start at W + pair_offset*K
+  int N;                   // output rows
+  int K;                   // input length, multiple of 8
+  int pair_offset;         // EPI_SILU_MUL: row offset of the `up` matrix
+  const float* x;          // input vector [K]
+  const uint16_t* norm_w;  // non-null: x := rmsnorm(x) * norm_w (fused prologue)
+  float eps;
+  const uint16_t* bias;    // [N] or null
+  const float* residual;   // [N] or null: y = residual + W.x
+  float* y;                // [N]
+  // EPI_ARGMAX
+  float* part_val;         // [gridDim.x]
+  int* part_idx;           // [gridDim.x]
+  unsigned* counter;       // last-CTA ticket, reset by the last CTA
+  int row_base;            // global index of row 0 (vocab shard offset)
+  int finalize;            // 1: last CTA publishes argmax and advances StepState
+  float* local_best;       // finalize == 0: {value, index-as-float-bits} for the TP gather
+  StepState* st;
+  int* seq_tokens;
+};
+
+struct AttnParams {
+  const float* qkv;        // [nq*d | nkv*d | nkv*d] of this token (rank-local heads)
+  float* k_cache;          // this layer: [pages][nkv][kPage][d]
+  float* v_cache;
+  const int* page_table;   // [max_pages]
+  float* out;              // [nq*d]
+  float* part;             // [nq][splits][d+2] partial (o, m, l)
+  unsigned* counters;      // [nkv]
+  StepState* st;
+  int nq, nkv, d, group, splits, chunk_cap;
+  float inv_sqrt_d;
+  RopeParams rope;
+};
+
+constexpr int kPage = 64;  // KV positions per page
+
+struct EmbedParams {
+  const uint16_t* table;  // [V, h]
+  const float* emb_in;    // [h] caller embedding
+  const int* seq_tokens;
+  StepState* st;
+  float* x;
+  int h;
+  int vocab;
+};
+
+// Launchers (pdl: launch with a programmatic edge to the previous kernel).
+cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_gemv(int epi, const GemvParams& p, int grid, cudaStream_t s, bool pdl);
+size_t gemv_smem_bytes(int epi, int N, int K, int grid);
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
+size_t attention_smem_bytes(int group, int d, int chunk_cap);
+cudaError_t launch_tp_argmax_finalize(const float* all_best, int ranks, StepState* st, int* seq_tokens,
+                                      cudaStream_t s);
+cudaError_t launch_synth_fill(uint16_t* dst, uint64_t key, uint64_t rows, uint64_t cols, uint64_t src_ld,
+                              uint64_t row0, uint64_t col0, int kind, cudaStream_t s);
+cudaError_t configure_kernels(int max_smem_optin);
+
+}  // namespace vvli

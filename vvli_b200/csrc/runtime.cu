@@ -1,0 +1,933 @@
+// runtime.cu - the C ABI of include/vvli_cuda.h.
+//
+// A context owns one GPU's share of the model: its tensor-parallel weight
+// shard in one device allocation, a paged fp32 KV cache, the activation
+// buffers of one decode step, and a CUDA graph of that step.  The graph
+// reads the token and position from device memory (StepState), so one
+// capture serves every call; generation and prefill replay it back to back
+// without host round trips.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <type_traits>
+#include <vector>
+
+#include "../../include/vvli_cuda.h"
+#include "kernels.h"
+
+using namespace vvli;
+
+static_assert(sizeof(vvli_model_config) == 136, "vvli_model_config layout is part of the ABI");
+
+namespace {
+
+thread_local std::string g_last_error;
+
+// ---------------------------------------------------------------- NCCL (loaded at run time)
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+  static NcclApi api = [] {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      a.why = "libnccl.so.2 not found";
+      return a;
+    }
+    auto sym = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      return fn != nullptr;
+    };
+    a.ok = sym(a.GetUniqueId, "ncclGetUniqueId") && sym(a.CommInitRankConfig, "ncclCommInitRankConfig") &&
+           sym(a.CommGetAsyncError, "ncclCommGetAsyncError") && sym(a.AllReduce, "ncclAllReduce") &&
+           sym(a.AllGather, "ncclAllGather") && sym(a.CommDestroy, "ncclCommDestroy") &&
+           sym(a.CommAbort, "ncclCommAbort") && sym(a.GetErrorString, "ncclGetErrorString");
+    if (!a.ok) a.why = "libnccl is missing a required symbol";
+    return a;
+  }();
+  return api;
+}
+
+// ---------------------------------------------------------------- reference blob layout
+// assignSlices / storageElementCount (src/llm.zig:488-537, 814-837).
+struct LayerOff {
+  uint64_t in_norm, q, qb, k, kb, v, vb, o, post, gate, up, down;
+};
+struct BlobLayout {
+  uint64_t emb = 0, final_norm = 0, lm_head = UINT64_MAX, total = 0;
+  std::vector<LayerOff> layers;
+};
+
+BlobLayout blob_layout(const vvli_model_config& c) {
+  BlobLayout b;
+  uint64_t cur = 0;
+  auto take = [&](uint64_t n) {
+    cur = (cur + 31) / 32 * 32;
+    const uint64_t s = cur;
+    cur += n;
+    return s;
+  };
+  const uint64_t h = c.hidden_size, kv = c.num_key_value_heads * (c.hidden_size / c.num_attention_heads),
+                 I = c.intermediate_size;
+  b.emb = take(c.vocab_size * h);
+  b.layers.resize(c.num_hidden_layers);
+  for (auto& L : b.layers) {
+    L.in_norm = take(h);
+    L.q = take(h * h);
+    L.qb = c.qkv_bias ? take(h) : UINT64_MAX;
+    L.k = take(kv * h);
+    L.kb = c.qkv_bias ? take(kv) : UINT64_MAX;
+    L.v = take(kv * h);
+    L.vb = c.qkv_bias ? take(kv) : UINT64_MAX;
+    L.o = take(h * h);
+    L.post = take(h);
+    L.gate = take(I * h);
+    L.up = take(I * h);
+    L.down = take(h * I);
+  }
+  b.final_norm = take(h);
+  if (!c.tie_word_embeddings) b.lm_head = take(c.vocab_size * h);
+  b.total = cur;
+  return b;
+}
+
+uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+uint64_t tensor_key(uint64_t seed, uint64_t tid) { return mix64(seed ^ mix64(tid + 0x632BE59BD9B4E019ull)); }
+
+// One rectangular piece of a reference tensor copied into the device layout.
+struct Piece {
+  uint64_t dst;        // element offset in the device allocation
+  uint64_t tensor_id;  // blob order id (synthetic generator key)
+  uint64_t src;        // element offset of the tensor in the host blob
+  uint64_t rows, cols, src_ld, row0, col0;
+  int kind;            // 0 matrix/bias, 1 norm weights
+};
+
+struct DevLayer {
+  uint64_t in_norm, w_qkv, b_qkv, w_o, post, w_gu, w_down;
+};
+
+}  // namespace
+
+struct vvli_ctx {
+  vvli_model_config cfg{};
+  int device = 0, tp_rank = 0, tp_size = 1;
+  int sm_count = 148;
+  uint64_t max_seq = 0, max_batch = 1;
+  // dimensions
+  int h = 0, L = 0, nq = 0, nkv = 0, d = 0, group = 0, I = 0, V = 0;
+  int nq_l = 0, nkv_l = 0, q_rows = 0, kv_rows = 0, I_l = 0, V_l = 0, V_lr = 0, v0 = 0;
+  // weights
+  std::vector<Piece> pieces;
+  std::vector<DevLayer> lay;
+  uint64_t off_emb = 0, off_final = 0, off_lm = 0, weight_elems = 0;
+  bool lm_aliases_emb = false;
+  uint16_t* w = nullptr;
+  bool loaded = false;
+  // KV cache and step buffers
+  float* kv = nullptr;
+  size_t kv_layer_floats = 0;  // K (or V) floats per layer
+  int max_pages = 0;
+  int* page_table = nullptr;
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *ff = nullptr, *logits = nullptr, *logits_full = nullptr,
+        *emb_in = nullptr, *hidden = nullptr, *attn_part = nullptr, *amax_val = nullptr, *best = nullptr,
+        *all_best = nullptr;
+  int* amax_idx = nullptr;
+  unsigned* counters = nullptr;  // [nkv_l] attention + [1] argmax
+  int* seq_tokens = nullptr;
+  StepState* st = nullptr;
+  // launch shapes
+  int attn_splits = 1, attn_chunk_cap = 1;
+  int grid_qkv = 1, grid_o = 1, grid_gu = 1, grid_down = 1, grid_lm = 1;
+  // host staging (pinned)
+  StepState* h_st = nullptr;
+  int* h_tok = nullptr;
+  // execution
+  cudaStream_t stream = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  bool debug = false;
+  bool use_pdl = true;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.f;
+  ncclComm_t comm = nullptr;
+};
+
+namespace {
+
+int cuda_fail(cudaError_t e, const char* what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  if (e == cudaErrorMemoryAllocation) return VVLI_ERR_OOM;
+  return VVLI_ERR_CUDA;
+}
+
+#define CK(call)                                                    \
+  do {                                                              \
+    cudaError_t e_ = (call);                                        \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);             \
+  } while (0)
+
+int nccl_wait(vvli_ctx* c, ncclResult_t r, const char* what) {
+  auto& n = nccl();
+  const double limit_s = getenv("VVLI_NCCL_TIMEOUT_S") ? atof(getenv("VVLI_NCCL_TIMEOUT_S")) : 120.0;
+  const auto t0 = std::chrono::steady_clock::now();
+  while (r == ncclInProgress) {
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    if (n.CommGetAsyncError(c->comm, &r) != ncclSuccess) break;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit_s) {
+      g_last_error = std::string(what) + ": timed out";
+      n.CommAbort(c->comm);
+      c->comm = nullptr;
+      return VVLI_ERR_TIMEOUT;
+    }
+  }
+  if (r != ncclSuccess) {
+    g_last_error = std::string(what) + ": " + n.GetErrorString(r);
+    return VVLI_ERR_NCCL;
+  }
+  return VVLI_OK;
+}
+
+int validate_config(const vvli_model_config& c) {  // Config.validate (src/llm.zig:195-216)
+  if (c.vocab_size == 0 || c.hidden_size == 0 || c.intermediate_size == 0 || c.num_hidden_layers == 0 ||
+      c.num_attention_heads == 0 || c.num_key_value_heads == 0 || c.max_position_embeddings == 0)
+    return VVLI_ERR_INVALID_CONFIG;
+  if (c.hidden_size % c.num_attention_heads) return VVLI_ERR_INVALID_CONFIG;
+  if (c.num_attention_heads % c.num_key_value_heads) return VVLI_ERR_INVALID_CONFIG;
+  if ((c.hidden_size / c.num_attention_heads) % 2) return VVLI_ERR_INVALID_CONFIG;
+  if (c.num_experts != 0) {
+    if (c.num_experts_per_token == 0 || c.num_experts_per_token > c.num_experts) return VVLI_ERR_INVALID_CONFIG;
+    return VVLI_ERR_UNSUPPORTED_ARCH;
+  }
+  if (c.num_experts_per_token != 0) return VVLI_ERR_INVALID_CONFIG;
+  if (c.architecture == VVLI_ARCH_OLMOE || c.architecture > VVLI_ARCH_QWEN2) return VVLI_ERR_UNSUPPORTED_ARCH;
+  return VVLI_OK;
+}
+
+uint64_t align128(uint64_t v) { return (v + 127) / 128 * 128; }
+
+// Device layout of this rank's shard and the pieces that fill it.
+void plan_weights(vvli_ctx* c) {
+  const auto& cfg = c->cfg;
+  const BlobLayout b = blob_layout(cfg);
+  const uint64_t h = c->h, r = c->tp_rank;
+  uint64_t cur = 0;
+  auto alloc = [&](uint64_t n) {
+    const uint64_t s = cur;
+    cur = align128(cur + n);
+    return s;
+  };
+  auto mat = [&](uint64_t dst, uint64_t tid, uint64_t src, uint64_t rows, uint64_t cols, uint64_t ld, uint64_t row0,
+                 uint64_t col0, int kind) { c->pieces.push_back({dst, tid, src, rows, cols, ld, row0, col0, kind}); };
+  c->off_emb = alloc(static_cast<uint64_t>(c->V) * h);
+  mat(c->off_emb, 0, b.emb, c->V, h, h, 0, 0, 0);
+  c->lay.resize(c->L);
+  const uint64_t qr = c->q_rows, kr = c->kv_rows, Il = c->I_l;
+  for (int l = 0; l < c->L; ++l) {
+    const auto& B = b.layers[l];
+    auto& D = c->lay[l];
+    const uint64_t base = 1 + 12ull * l;
+    D.in_norm = alloc(h);
+    mat(D.in_norm, base + 0, B.in_norm, 1, h, h, 0, 0, 1);
+    D.w_qkv = alloc((qr + 2 * kr) * h);
+    mat(D.w_qkv, base + 1, B.q, qr, h, h, r * qr, 0, 0);
+    mat(D.w_qkv + qr * h, base + 3, B.k, kr, h, h, r * kr, 0, 0);
+    mat(D.w_qkv + (qr + kr) * h, base + 5, B.v, kr, h, h, r * kr, 0, 0);
+    D.b_qkv = UINT64_MAX;
+    if (cfg.qkv_bias) {
+      D.b_qkv = alloc(qr + 2 * kr);
+      mat(D.b_qkv, base + 2, B.qb, 1, qr, h, 0, r * qr, 0);
+      mat(D.b_qkv + qr, base + 4, B.kb, 1, kr, c->nkv * c->d, 0, r * kr, 0);
+      mat(D.b_qkv + qr + kr, base + 6, B.vb, 1, kr, c->nkv * c->d, 0, r * kr, 0);
+    }
+    D.w_o = alloc(h * qr);
+    mat(D.w_o, base + 7, B.o, h, qr, h, 0, r * qr, 0);
+    D.post = alloc(h);
+    mat(D.post, base + 8, B.post, 1, h, h, 0, 0, 1);
+    D.w_gu = alloc(2 * Il * h);
+    mat(D.w_gu, base + 9, B.gate, Il, h, h, r * Il, 0, 0);
+    mat(D.w_gu + Il * h, base + 10, B.up, Il, h, h, r * Il, 0, 0);
+    D.w_down = alloc(h * Il);
+    mat(D.w_down, base + 11, B.down, h, Il, c->I, 0, r * Il, 0);
+  }
+  c->off_final = alloc(h);
+  mat(c->off_final, 1 + 12ull * c->L, b.final_norm, 1, h, h, 0, 0, 1);
+  if (cfg.tie_word_embeddings && c->tp_size == 1) {
+    c->lm_aliases_emb = true;
+    c->off_lm = c->off_emb;
+  } else {
+    c->off_lm = alloc(static_cast<uint64_t>(c->V_lr) * h);
+    if (cfg.tie_word_embeddings)
+      mat(c->off_lm, 0, b.emb, c->V_lr, h, h, c->v0, 0, 0);
+    else
+      mat(c->off_lm, 2 + 12ull * c->L, b.lm_head, c->V_lr, h, h, c->v0, 0, 0);
+  }
+  c->weight_elems = cur;
+}
+
+int gemv_grid(const vvli_ctx* c, int N) {
+  // Two resident CTAs per SM, never more CTAs than rows.
+  return std::max(1, std::min(N, 2 * c->sm_count));
+}
+
+int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
+  const bool pdl = c->use_pdl && !debug;
+  const bool tp = c->tp_size > 1;
+  const uint16_t* W = c->w;
+  EmbedParams ep{W + c->off_emb, c->emb_in, c->seq_tokens, c->st, c->x, c->h, c->V};
+  CK(launch_embed(ep, s, false));
+  const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
+  RopeParams rope{c->cfg.rope_theta, static_cast<int>(c->cfg.rope_layout), static_cast<int>(c->cfg.rope_scaling_type),
+                  c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
+                  static_cast<float>(c->cfg.rope_original_max_position)};
+  for (int l = 0; l < c->L; ++l) {
+    const DevLayer& D = c->lay[l];
+    GemvParams q{};
+    q.W = W + D.w_qkv;
+    q.N = c->q_rows + 2 * c->kv_rows;
+    q.K = c->h;
+    q.x = c->x;
+    q.norm_w = W + D.in_norm;
+    q.eps = c->cfg.rms_norm_eps;
+    q.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv;
+    q.y = c->qkv;
+    CK(launch_gemv(EPI_PLAIN, q, c->grid_qkv, s, pdl));
+
+    AttnParams a{};
+    a.qkv = c->qkv;
+    a.k_cache = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
+    a.v_cache = a.k_cache + c->kv_layer_floats;
+    a.page_table = c->page_table;
+    a.out = c->attn;
+    a.part = c->attn_part;
+    a.counters = c->counters;
+    a.st = c->st;
+    a.nq = c->nq_l;
+    a.nkv = c->nkv_l;
+    a.d = c->d;
+    a.group = c->group;
+    a.splits = c->attn_splits;
+    a.chunk_cap = c->attn_chunk_cap;
+    a.inv_sqrt_d = inv_sqrt_d;
+    a.rope = rope;
+    CK(launch_attention(a, s, pdl));
+
+    GemvParams o{};
+    o.W = W + D.w_o;
+    o.N = c->h;
+    o.K = c->q_rows;
+    o.x = c->attn;
+    o.residual = c->tp_rank == 0 ? c->x : nullptr;
+    o.y = c->x;
+    CK(launch_gemv(EPI_PLAIN, o, c->grid_o, s, pdl));
+    if (tp) {
+      int st = nccl_wait(c, nccl().AllReduce(c->x, c->x, c->h, ncclFloat32, ncclSum, c->comm, s), "allreduce");
+      if (st) return st;
+    }
+
+    GemvParams gu{};
+    gu.W = W + D.w_gu;
+    gu.N = c->I_l;
+    gu.K = c->h;
+    gu.pair_offset = c->I_l;
+    gu.x = c->x;
+    gu.norm_w = W + D.post;
+    gu.eps = c->cfg.rms_norm_eps;
+    gu.y = c->ff;
+    CK(launch_gemv(EPI_SILU_MUL, gu, c->grid_gu, s, pdl && !tp));
+
+    GemvParams dn{};
+    dn.W = W + D.w_down;
+    dn.N = c->h;
+    dn.K = c->I_l;
+    dn.x = c->ff;
+    dn.residual = c->tp_rank == 0 ? c->x : nullptr;
+    dn.y = c->x;
+    CK(launch_gemv(EPI_PLAIN, dn, c->grid_down, s, pdl));
+    if (tp) {
+      int st = nccl_wait(c, nccl().AllReduce(c->x, c->x, c->h, ncclFloat32, ncclSum, c->comm, s), "allreduce");
+      if (st) return st;
+    }
+    if (debug) CK(cudaMemcpyAsync(c->hidden + static_cast<size_t>(l) * c->h, c->x, c->h * 4, cudaMemcpyDeviceToDevice, s));
+  }
+  GemvParams lm{};
+  lm.W = W + c->off_lm;
+  lm.N = c->V_lr;
+  lm.K = c->h;
+  lm.x = c->x;
+  lm.norm_w = W + c->off_final;
+  lm.eps = c->cfg.rms_norm_eps;
+  lm.y = c->logits;
+  lm.part_val = c->amax_val;
+  lm.part_idx = c->amax_idx;
+  lm.counter = c->counters + c->nkv_l;
+  lm.row_base = c->v0;
+  lm.finalize = tp ? 0 : 1;
+  lm.local_best = c->best;
+  lm.st = c->st;
+  lm.seq_tokens = c->seq_tokens;
+  CK(launch_gemv(EPI_ARGMAX, lm, c->grid_lm, s, pdl && !tp));
+  if (tp) {
+    int st = nccl_wait(c, nccl().AllGather(c->best, c->all_best, 2, ncclFloat32, c->comm, s), "allgather");
+    if (st) return st;
+    CK(launch_tp_argmax_finalize(c->all_best, c->tp_size, c->st, c->seq_tokens, s));
+  }
+  return VVLI_OK;
+}
+
+int build_graph(vvli_ctx* c) {
+  if (c->graph) {
+    cudaGraphExecDestroy(c->graph);
+    c->graph = nullptr;
+  }
+  if (getenv("VVLI_NO_GRAPH")) return VVLI_OK;
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  int st = enqueue_step(c, c->stream, false);
+  cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+  if (st != VVLI_OK) {
+    if (g) cudaGraphDestroy(g);
+    return st;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  e = cudaGraphInstantiate(&c->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    c->graph = nullptr;
+    return cuda_fail(e, "cudaGraphInstantiate");
+  }
+  return VVLI_OK;
+}
+
+// Launches `steps` decode steps (graph replays, or eager steps in debug mode).
+int run_steps(vvli_ctx* c, int steps) {
+  for (int i = 0; i < steps; ++i) {
+    if (c->debug || !c->graph) {
+      int st = enqueue_step(c, c->stream, c->debug);
+      if (st) return st;
+    } else {
+      CK(cudaGraphLaunch(c->graph, c->stream));
+    }
+  }
+  return VVLI_OK;
+}
+
+int stage_state(vvli_ctx* c, int pos, int prompt_len, int use_emb) {
+  StepState* h = c->h_st;
+  h->pos = pos;
+  h->prompt_len = prompt_len;
+  h->max_seq = static_cast<int>(c->max_seq);
+  h->use_embedding = use_emb;
+  h->argmax = -1;
+  h->err = 0;
+  h->batch = 1;
+  CK(cudaMemcpyAsync(c->st, h, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+  return VVLI_OK;
+}
+
+int finish_state(vvli_ctx* c) {
+  CK(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  if (c->h_st->err) {
+    g_last_error = "device step reported an error";
+    return c->h_st->err;
+  }
+  return VVLI_OK;
+}
+
+int copy_logits(vvli_ctx* c, float* out) {
+  if (!out) return VVLI_OK;
+  if (c->tp_size > 1) {
+    int st = nccl_wait(c, nccl().AllGather(c->logits, c->logits_full, c->V_l, ncclFloat32, c->comm, c->stream),
+                       "allgather logits");
+    if (st) return st;
+    CK(cudaMemcpyAsync(out, c->logits_full, static_cast<size_t>(c->V) * 4, cudaMemcpyDeviceToHost, c->stream));
+  } else {
+    CK(cudaMemcpyAsync(out, c->logits, static_cast<size_t>(c->V) * 4, cudaMemcpyDeviceToHost, c->stream));
+  }
+  return VVLI_OK;
+}
+
+void free_ctx(vvli_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->graph) cudaGraphExecDestroy(c->graph);
+  if (c->comm) nccl().CommDestroy(c->comm);
+  void* dev[] = {c->w, c->kv, c->page_table, c->x, c->qkv, c->attn, c->ff, c->logits, c->logits_full, c->emb_in,
+                 c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
+                 c->seq_tokens, c->st};
+  for (void* p : dev)
+    if (p) cudaFree(p);
+  if (c->h_st) cudaFreeHost(c->h_st);
+  if (c->h_tok) cudaFreeHost(c->h_tok);
+  if (c->ev0) cudaEventDestroy(c->ev0);
+  if (c->ev1) cudaEventDestroy(c->ev1);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+template <typename T>
+int dalloc(T** p, size_t count) {
+  CK(cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(T)));
+  CK(cudaMemset(*p, 0, std::max<size_t>(count, 1) * sizeof(T)));
+  return VVLI_OK;
+}
+
+}  // namespace
+
+// ================================================================ C ABI
+extern "C" {
+
+const char* vvli_cuda_strerror(int status) {
+  switch (status) {
+    case VVLI_OK: return "ok";
+    case VVLI_ERR_CONTEXT_FULL: return "ContextFull";
+    case VVLI_ERR_INVALID_CONFIG: return "InvalidConfig";
+    case VVLI_ERR_INVALID_TOKEN: return "InvalidToken";
+    case VVLI_ERR_INVALID_WEIGHT: return "InvalidWeight";
+    case VVLI_ERR_UNSUPPORTED_DTYPE: return "UnsupportedDType";
+    case VVLI_ERR_UNSUPPORTED_ARCH: return "UnsupportedModelArchitecture";
+    case VVLI_ERR_EMPTY_PROMPT: return "EmptyPrompt";
+    case VVLI_ERR_OUTPUT_TOO_SMALL: return "OutputTooSmall";
+    case VVLI_ERR_INVALID_SAMPLING: return "InvalidSamplingOptions";
+    case VVLI_ERR_CUDA: return "CudaError";
+    case VVLI_ERR_NCCL: return "NcclError";
+    case VVLI_ERR_TIMEOUT: return "Timeout";
+    case VVLI_ERR_OOM: return "OutOfMemory";
+    case VVLI_ERR_NOT_LOADED: return "WeightsNotLoaded";
+    case VVLI_ERR_INVALID_ARGUMENT: return "InvalidArgument";
+    case VVLI_ERR_UNIMPLEMENTED: return "Unimplemented";
+    default: return "UnknownError";
+  }
+}
+
+int vvli_cuda_storage_elements(const vvli_model_config* cfg, uint64_t* out) {
+  if (!cfg || !out) return VVLI_ERR_INVALID_ARGUMENT;
+  int st = validate_config(*cfg);
+  if (st == VVLI_ERR_INVALID_CONFIG) return st;
+  *out = blob_layout(*cfg).total;
+  return VVLI_OK;
+}
+
+int vvli_cuda_nccl_unique_id(void* id) {
+  if (!id) return VVLI_ERR_INVALID_ARGUMENT;
+  auto& n = nccl();
+  if (!n.ok) {
+    g_last_error = n.why;
+    return VVLI_ERR_NCCL;
+  }
+  ncclUniqueId uid;
+  ncclResult_t r = n.GetUniqueId(&uid);
+  if (r != ncclSuccess) return VVLI_ERR_NCCL;
+  static_assert(sizeof(ncclUniqueId) == VVLI_NCCL_ID_BYTES, "ncclUniqueId size");
+  std::memcpy(id, &uid, sizeof(uid));
+  return VVLI_OK;
+}
+
+int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int tp_size, const void* nccl_unique_id,
+                     uint64_t max_seq, uint64_t max_batch, vvli_ctx** out_ctx) {
+  if (!cfg || !out_ctx) return VVLI_ERR_INVALID_ARGUMENT;
+  *out_ctx = nullptr;
+  int st = validate_config(*cfg);
+  if (st) return st;
+  if (max_seq == 0 || max_seq > cfg->max_position_embeddings || max_seq > (1u << 30)) return VVLI_ERR_INVALID_CONFIG;
+  if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return VVLI_ERR_INVALID_ARGUMENT;
+  if (tp_size > 1 && !nccl_unique_id) return VVLI_ERR_INVALID_ARGUMENT;
+  const uint64_t d = cfg->hidden_size / cfg->num_attention_heads;
+  // Shapes this runtime's kernels take: 16-byte weight rows and head_dim <= 256.
+  if (cfg->hidden_size % 8 || cfg->intermediate_size % 8 || d > 256) return VVLI_ERR_UNSUPPORTED_ARCH;
+  if (cfg->num_key_value_heads % tp_size || cfg->intermediate_size % (8ull * tp_size)) return VVLI_ERR_INVALID_CONFIG;
+  if (((cfg->num_attention_heads / tp_size) * d) % 8) return VVLI_ERR_INVALID_CONFIG;
+
+  auto* c = new vvli_ctx();
+  c->cfg = *cfg;
+  c->device = device;
+  c->tp_rank = tp_rank;
+  c->tp_size = tp_size;
+  c->max_seq = max_seq;
+  c->max_batch = std::max<uint64_t>(1, max_batch);
+  c->h = static_cast<int>(cfg->hidden_size);
+  c->L = static_cast<int>(cfg->num_hidden_layers);
+  c->nq = static_cast<int>(cfg->num_attention_heads);
+  c->nkv = static_cast<int>(cfg->num_key_value_heads);
+  c->d = static_cast<int>(d);
+  c->group = c->nq / c->nkv;
+  c->I = static_cast<int>(cfg->intermediate_size);
+  c->V = static_cast<int>(cfg->vocab_size);
+  c->nq_l = c->nq / tp_size;
+  c->nkv_l = c->nkv / tp_size;
+  c->q_rows = c->nq_l * c->d;
+  c->kv_rows = c->nkv_l * c->d;
+  c->I_l = c->I / tp_size;
+  c->V_l = (c->V + tp_size - 1) / tp_size;
+  c->v0 = tp_rank * c->V_l;
+  c->V_lr = std::max(0, std::min(c->V, c->v0 + c->V_l) - c->v0);
+  if (c->V_lr <= 0) {
+    delete c;
+    return VVLI_ERR_INVALID_CONFIG;
+  }
+
+  auto fail = [&](int code) {
+    free_ctx(c);
+    return code;
+  };
+  cudaError_t e = cudaSetDevice(device);
+  if (e) return fail(cuda_fail(e, "cudaSetDevice"));
+  int smem_optin = 0;
+  cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+  cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if ((e = configure_kernels(smem_optin))) return fail(cuda_fail(e, "configure_kernels"));
+  if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking))) return fail(cuda_fail(e, "stream"));
+  cudaEventCreate(&c->ev0);
+  cudaEventCreate(&c->ev1);
+
+  plan_weights(c);
+  if ((st = dalloc(&c->w, c->weight_elems))) return fail(st);
+
+  // Paged KV cache: [layer][K|V][page][kv_head][kPage][d] fp32.
+  c->max_pages = static_cast<int>((max_seq + kPage - 1) / kPage) * static_cast<int>(c->max_batch);
+  c->kv_layer_floats = static_cast<size_t>(c->max_pages) * c->nkv_l * kPage * c->d;
+  if ((st = dalloc(&c->kv, 2 * c->kv_layer_floats * c->L))) return fail(st);
+  if ((st = dalloc(&c->page_table, c->max_pages))) return fail(st);
+  std::vector<int> pt(c->max_pages);
+  for (int i = 0; i < c->max_pages; ++i) pt[i] = i;
+  if ((e = cudaMemcpy(c->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice))) return fail(cuda_fail(e, "pt"));
+
+  // Attention split: about two CTAs per SM over the kv heads.
+  c->attn_splits = std::max(1, std::min<int>(static_cast<int>(max_seq), (2 * c->sm_count + c->nkv_l - 1) / c->nkv_l));
+  c->attn_chunk_cap = static_cast<int>((max_seq + c->attn_splits - 1) / c->attn_splits);
+  if (attention_smem_bytes(c->group, c->d, c->attn_chunk_cap) > static_cast<size_t>(smem_optin)) {
+    c->attn_chunk_cap = 1;  // recompute with more splits
+    c->attn_splits = static_cast<int>(max_seq);
+    while (c->attn_splits > 1 &&
+           attention_smem_bytes(c->group, c->d, static_cast<int>((max_seq + c->attn_splits / 2 - 1) / (c->attn_splits / 2))) <=
+               static_cast<size_t>(smem_optin))
+      c->attn_splits /= 2;
+    c->attn_chunk_cap = static_cast<int>((max_seq + c->attn_splits - 1) / c->attn_splits);
+  }
+  c->grid_qkv = gemv_grid(c, c->q_rows + 2 * c->kv_rows);
+  c->grid_o = gemv_grid(c, c->h);
+  c->grid_gu = gemv_grid(c, c->I_l);
+  c->grid_down = gemv_grid(c, c->h);
+  c->grid_lm = gemv_grid(c, c->V_lr);
+
+  const size_t B = c->max_batch;
+  if ((st = dalloc(&c->x, B * c->h)) || (st = dalloc(&c->qkv, B * (c->q_rows + 2 * c->kv_rows))) ||
+      (st = dalloc(&c->attn, B * c->q_rows)) || (st = dalloc(&c->ff, B * c->I_l)) ||
+      (st = dalloc(&c->logits, B * static_cast<size_t>(c->V_l))) ||
+      (st = dalloc(&c->logits_full, static_cast<size_t>(c->V_l) * tp_size)) || (st = dalloc(&c->emb_in, c->h)) ||
+      (st = dalloc(&c->hidden, static_cast<size_t>(c->L) * c->h)) ||
+      (st = dalloc(&c->attn_part, static_cast<size_t>(c->nq_l) * c->attn_splits * (c->d + 2))) ||
+      (st = dalloc(&c->amax_val, 2 * c->sm_count)) || (st = dalloc(&c->amax_idx, 2 * c->sm_count)) ||
+      (st = dalloc(&c->best, 2)) || (st = dalloc(&c->all_best, 2 * tp_size)) ||
+      (st = dalloc(&c->counters, c->nkv_l + 1)) || (st = dalloc(&c->seq_tokens, max_seq + 1)) ||
+      (st = dalloc(&c->st, 1)))
+    return fail(st);
+  if ((e = cudaMallocHost(&c->h_st, sizeof(StepState))) || (e = cudaMallocHost(&c->h_tok, 64 * sizeof(int))))
+    return fail(cuda_fail(e, "cudaMallocHost"));
+
+  if (tp_size > 1) {
+    auto& n = nccl();
+    if (!n.ok) {
+      g_last_error = n.why;
+      return fail(VVLI_ERR_NCCL);
+    }
+    ncclUniqueId uid;
+    std::memcpy(&uid, nccl_unique_id, sizeof(uid));
+    ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
+    ncfg.blocking = 0;
+    ncclResult_t r = n.CommInitRankConfig(&c->comm, tp_size, uid, tp_rank, &ncfg);
+    if ((st = nccl_wait(c, r, "ncclCommInitRankConfig"))) return fail(st);
+  }
+  *out_ctx = c;
+  return VVLI_OK;
+}
+
+static int after_load(vvli_ctx* c) {
+  CK(cudaStreamSynchronize(c->stream));
+  c->loaded = true;
+  return build_graph(c);
+}
+
+int vvli_cuda_load_weights(vvli_ctx* c, const uint16_t* blob, uint64_t n) {
+  if (!c || !blob) return VVLI_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(c->device));
+  if (n < blob_layout(c->cfg).total) return VVLI_ERR_INVALID_WEIGHT;
+  for (const Piece& p : c->pieces) {
+    const uint16_t* src = blob + p.src + p.row0 * p.src_ld + p.col0;
+    if (p.rows == 1) {
+      CK(cudaMemcpyAsync(c->w + p.dst, src, p.cols * 2, cudaMemcpyHostToDevice, c->stream));
+    } else {
+      CK(cudaMemcpy2DAsync(c->w + p.dst, p.cols * 2, src, p.src_ld * 2, p.cols * 2, p.rows, cudaMemcpyHostToDevice,
+                           c->stream));
+    }
+  }
+  return after_load(c);
+}
+
+int vvli_cuda_fill_synthetic(vvli_ctx* c, uint64_t seed) {
+  if (!c) return VVLI_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(c->device));
+  for (const Piece& p : c->pieces)
+    CK(launch_synth_fill(c->w + p.dst, tensor_key(seed, p.tensor_id), p.rows, p.cols, p.src_ld, p.row0, p.col0,
+                         p.kind, c->stream));
+  return after_load(c);
+}
+
+int vvli_cuda_reset(vvli_ctx* c) {  // KVCache.clear (src/llm.zig:576-579)
+  if (!c) return VVLI_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(c->device));
+  CK(cudaMemsetAsync(c->kv, 0, 2 * c->kv_layer_floats * c->L * sizeof(float), c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  return VVLI_OK;
+}
+
+static int forward_common(vvli_ctx* c, uint64_t position, float* logits_out, uint32_t* argmax_out, int use_emb) {
+  int st;
+  if ((st = stage_state(c, static_cast<int>(position), 0, use_emb))) return st;
+  CK(cudaEventRecord(c->ev0, c->stream));
+  if ((st = run_steps(c, 1))) return st;
+  CK(cudaEventRecord(c->ev1, c->stream));
+  if ((st = copy_logits(c, logits_out))) return st;
+  if ((st = finish_state(c))) return st;
+  cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
+  if (argmax_out) *argmax_out = static_cast<uint32_t>(c->h_st->argmax);
+  return VVLI_OK;
+}
+
+int vvli_cuda_forward_token(vvli_ctx* c, uint32_t token, uint64_t position, float* logits_out, uint32_t* argmax_out) {
+  if (!c) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (token >= c->cfg.vocab_size) return VVLI_ERR_INVALID_TOKEN;
+  if (position >= c->max_seq) return VVLI_ERR_CONTEXT_FULL;
+  CK(cudaSetDevice(c->device));
+  c->h_tok[0] = static_cast<int>(token);
+  CK(cudaMemcpyAsync(c->seq_tokens + position, c->h_tok, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+  return forward_common(c, position, logits_out, argmax_out, 0);
+}
+
+int vvli_cuda_forward_embedding(vvli_ctx* c, const float* emb, uint64_t position, float* logits_out,
+                                uint32_t* argmax_out) {
+  if (!c || !emb) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (position >= c->max_seq) return VVLI_ERR_CONTEXT_FULL;
+  CK(cudaSetDevice(c->device));
+  CK(cudaMemcpyAsync(c->emb_in, emb, static_cast<size_t>(c->h) * 4, cudaMemcpyHostToDevice, c->stream));
+  return forward_common(c, position, logits_out, argmax_out, 1);
+}
+
+int vvli_cuda_prefill(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start, float* last_logits,
+                      uint32_t* argmax_out) {
+  if (!c || (!tokens && n)) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (n == 0) return VVLI_ERR_EMPTY_PROMPT;
+  for (uint64_t i = 0; i < n; ++i)
+    if (tokens[i] >= c->cfg.vocab_size) return VVLI_ERR_INVALID_TOKEN;
+  if (start + n > c->max_seq) return VVLI_ERR_CONTEXT_FULL;
+  CK(cudaSetDevice(c->device));
+  CK(cudaMemcpyAsync(c->seq_tokens + start, tokens, n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+  int st;
+  if ((st = stage_state(c, static_cast<int>(start), static_cast<int>(start + n), 0))) return st;
+  CK(cudaEventRecord(c->ev0, c->stream));
+  if ((st = run_steps(c, static_cast<int>(n)))) return st;
+  CK(cudaEventRecord(c->ev1, c->stream));
+  if ((st = copy_logits(c, last_logits))) return st;
+  if ((st = finish_state(c))) return st;
+  cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
+  if (argmax_out) *argmax_out = static_cast<uint32_t>(c->h_st->argmax);
+  return VVLI_OK;
+}
+
+int vvli_cuda_generate_greedy(vvli_ctx* c, const uint32_t* prompt, uint64_t n_prompt, uint64_t max_new, int64_t eos,
+                              uint32_t* out, uint64_t* out_count, vvli_generate_stats* stats) {
+  if (!c || !out_count || (!out && max_new) || (!prompt && n_prompt)) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (n_prompt == 0) return VVLI_ERR_EMPTY_PROMPT;  // generateGreedy, src/generator.zig:148
+  *out_count = 0;
+  using clk = std::chrono::steady_clock;
+  const auto t_start = clk::now();
+  uint32_t first = 0;
+  int st = vvli_cuda_prefill(c, prompt, n_prompt, 0, nullptr, &first);
+  if (st) return st;
+  const auto t_prefill = clk::now();
+  // Decode (src/generator.zig:160-172): emit token k; stop after eos; else
+  // forward token k at position n_prompt + k, whose argmax is token k + 1.
+  // Forward k stores token k + 1 in seq_tokens[n_prompt + k + 1] on the
+  // device, so steps run in chunks and the host only reads tokens back once
+  // per chunk to look for eos.  Forwards past an eos are speculative: their
+  // tokens are dropped.  As in the reference, the last emitted token is
+  // forwarded too.
+  uint64_t known = 0, scanned = 0, forwards = 0, result = 0;
+  if (max_new) {
+    out[0] = first;
+    known = 1;
+  }
+  std::vector<int> buf;
+  for (;;) {
+    bool stop = false;
+    for (; scanned < known; ++scanned)
+      if (eos >= 0 && out[scanned] == static_cast<uint32_t>(eos)) {
+        result = scanned + 1;
+        stop = true;
+        break;
+      }
+    if (stop) break;
+    if (forwards >= max_new) {
+      result = max_new;
+      break;
+    }
+    const uint64_t pos = n_prompt + forwards;
+    if (pos >= c->max_seq) return VVLI_ERR_CONTEXT_FULL;
+    const uint64_t chunk = std::min<uint64_t>({max_new - forwards, c->max_seq - pos, forwards < 8 ? uint64_t{8} : uint64_t{64}});
+    if ((st = run_steps(c, static_cast<int>(chunk)))) return st;
+    buf.resize(chunk);
+    CK(cudaMemcpyAsync(buf.data(), c->seq_tokens + pos + 1, chunk * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    if ((st = finish_state(c))) return st;
+    for (uint64_t i = 0; i < chunk && forwards + 1 + i < max_new; ++i)
+      out[forwards + 1 + i] = static_cast<uint32_t>(buf[i]);
+    forwards += chunk;
+    known = std::min<uint64_t>(max_new, forwards + 1);
+  }
+  *out_count = result;
+  const auto t_end = clk::now();
+  if (stats) {
+    stats->prompt_tokens = n_prompt;
+    stats->generated_tokens = result;
+    stats->prefill_nanoseconds = std::chrono::duration_cast<std::chrono::nanoseconds>(t_prefill - t_start).count();
+    stats->decode_nanoseconds = std::chrono::duration_cast<std::chrono::nanoseconds>(t_end - t_prefill).count();
+    stats->total_nanoseconds = std::chrono::duration_cast<std::chrono::nanoseconds>(t_end - t_start).count();
+  }
+  return VVLI_OK;
+}
+
+int vvli_cuda_decode(vvli_ctx* c, uint64_t n_steps, uint32_t* out_tokens, float* device_ms) {
+  if (!c) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (n_steps == 0) return VVLI_OK;
+  CK(cudaSetDevice(c->device));
+  const uint64_t pos0 = static_cast<uint64_t>(c->h_st->pos);  // next position, left by the last forward
+  if (pos0 + n_steps > c->max_seq) return VVLI_ERR_CONTEXT_FULL;
+  int st;
+  CK(cudaEventRecord(c->ev0, c->stream));
+  if ((st = run_steps(c, static_cast<int>(n_steps)))) return st;
+  CK(cudaEventRecord(c->ev1, c->stream));
+  if (out_tokens)
+    CK(cudaMemcpyAsync(out_tokens, c->seq_tokens + pos0 + 1, n_steps * sizeof(int), cudaMemcpyDeviceToHost,
+                       c->stream));
+  if ((st = finish_state(c))) return st;
+  cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
+  if (device_ms) *device_ms = c->last_ms;
+  return VVLI_OK;
+}
+
+int vvli_cuda_time_kernel(vvli_ctx* c, int kernel, int reps, float* avg_ms, double* bytes) {
+  if (!c || !avg_ms || !bytes || reps <= 0 || kernel < 0 || kernel > 4) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  CK(cudaSetDevice(c->device));
+  const uint16_t* W = c->w;
+  const double h = c->h;
+  auto params = [&](int l, int& epi, int& grid, double& b) {
+    const DevLayer& D = c->lay[l % c->L];
+    GemvParams p{};
+    p.eps = c->cfg.rms_norm_eps;
+    epi = EPI_PLAIN;
+    switch (kernel) {
+      case 0:
+        p.W = W + D.w_qkv, p.N = c->q_rows + 2 * c->kv_rows, p.K = c->h, p.x = c->x, p.norm_w = W + D.in_norm;
+        p.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv, p.y = c->qkv, grid = c->grid_qkv;
+        b = 2.0 * p.N * h + 4 * h + 2 * h + 4.0 * p.N + (p.bias ? 2.0 * p.N : 0);
+        break;
+      case 1:
+        p.W = W + D.w_o, p.N = c->h, p.K = c->q_rows, p.x = c->attn, p.residual = c->x, p.y = c->x, grid = c->grid_o;
+        b = 2.0 * p.N * p.K + 4.0 * p.K + 8.0 * p.N;
+        break;
+      case 2:
+        p.W = W + D.w_gu, p.N = c->I_l, p.K = c->h, p.pair_offset = c->I_l, p.x = c->x, p.norm_w = W + D.post;
+        p.y = c->ff, grid = c->grid_gu, epi = EPI_SILU_MUL;
+        b = 2.0 * 2 * p.N * h + 4 * h + 2 * h + 4.0 * p.N;
+        break;
+      case 3:
+        p.W = W + D.w_down, p.N = c->h, p.K = c->I_l, p.x = c->ff, p.residual = c->x, p.y = c->x, grid = c->grid_down;
+        b = 2.0 * p.N * p.K + 4.0 * p.K + 8.0 * p.N;
+        break;
+      default:
+        p.W = W + c->off_lm, p.N = c->V_lr, p.K = c->h, p.x = c->x, p.norm_w = W + c->off_final, p.y = c->logits;
+        p.part_val = c->amax_val, p.part_idx = c->amax_idx, p.counter = c->counters + c->nkv_l, p.row_base = c->v0;
+        p.finalize = 0, p.local_best = c->best, p.st = c->st, p.seq_tokens = c->seq_tokens;
+        grid = c->grid_lm, epi = EPI_ARGMAX;
+        b = 2.0 * p.N * h + 4 * h + 2 * h + 4.0 * p.N;
+        break;
+    }
+    return p;
+  };
+  int epi = 0, grid = 1;
+  double b = 0;
+  for (int i = 0; i < 3; ++i) {  // warm-up
+    GemvParams p = params(i, epi, grid, b);
+    CK(launch_gemv(epi, p, grid, c->stream, false));
+  }
+  CK(cudaEventRecord(c->ev0, c->stream));
+  for (int i = 0; i < reps; ++i) {
+    GemvParams p = params(i, epi, grid, b);
+    CK(launch_gemv(epi, p, grid, c->stream, false));
+  }
+  CK(cudaEventRecord(c->ev1, c->stream));
+  CK(cudaEventSynchronize(c->ev1));
+  float ms = 0;
+  CK(cudaEventElapsedTime(&ms, c->ev0, c->ev1));
+  *avg_ms = ms / reps;
+  *bytes = b;
+  return VVLI_OK;
+}
+
+int vvli_cuda_set_debug(vvli_ctx* c, int enabled) {
+  if (!c) return VVLI_ERR_INVALID_ARGUMENT;
+  c->debug = enabled != 0;
+  return VVLI_OK;
+}
+
+int vvli_cuda_debug_hidden(vvli_ctx* c, int layer, float* out) {
+  if (!c || !out || layer < 0 || layer >= c->L) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->debug) return VVLI_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(c->device));
+  CK(cudaMemcpy(out, c->hidden + static_cast<size_t>(layer) * c->h, c->h * 4, cudaMemcpyDeviceToHost));
+  return VVLI_OK;
+}
+
+int vvli_cuda_last_forward_ms(vvli_ctx* c, float* out_ms) {
+  if (!c || !out_ms) return VVLI_ERR_INVALID_ARGUMENT;
+  *out_ms = c->last_ms;
+  return VVLI_OK;
+}
+
+int vvli_cuda_destroy(vvli_ctx* c) {
+  if (!c) return VVLI_ERR_INVALID_ARGUMENT;
+  free_ctx(c);
+  return VVLI_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,148 @@
+"""Runner: the host-side mirror of llm.Runner over the CUDA C ABI.
+
+Same operations and error behaviour as the reference's Runner
+(src/llm.zig:688-776): ``forward_token`` and ``forward_embedding`` return the
+logits of one position and raise ``InvalidToken`` / ``ContextFull``; the KV
+cache and scratch buffers live on the GPU inside the context.  Additions
+for the GPU path are batched ``prefill`` and ``generate_greedy``, which run
+the whole token loop on the device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _abi
+from .config import Config
+from .errors import check
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id for vvli_cuda_create's tensor-parallel ranks."""
+    buf = ctypes.create_string_buffer(_abi.NCCL_ID_BYTES)
+    check(_abi.lib().vvli_cuda_nccl_unique_id(buf))
+    return buf.raw
+
+
+class Runner:
+    def __init__(self, cfg: Config, max_seq: int, device: int = 0, tp_rank: int = 0, tp_size: int = 1,
+                 nccl_id: bytes | None = None, max_batch: int = 1):
+        self.cfg = cfg
+        self.max_seq = max_seq
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        self._c = cfg.to_c()
+        self._ctx = ctypes.c_void_p()
+        idbuf = None if nccl_id is None else ctypes.create_string_buffer(nccl_id, _abi.NCCL_ID_BYTES)
+        check(_abi.lib().vvli_cuda_create(ctypes.byref(self._c), device, tp_rank, tp_size, idbuf, max_seq, max_batch,
+                                          ctypes.byref(self._ctx)))
+        self.last_argmax = None
+
+    # ------------------------------------------------------------ lifecycle
+    def close(self):
+        if self._ctx:
+            check(_abi.lib().vvli_cuda_destroy(self._ctx))
+            self._ctx = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_weights(self, blob: np.ndarray):
+        """Uploads this rank's shard of an llm.OwnedModel-layout bf16 blob."""
+        b = np.ascontiguousarray(blob, dtype=np.uint16)
+        check(_abi.lib().vvli_cuda_load_weights(self._ctx, b.ctypes.data_as(_u16p), b.size))
+
+    def fill_synthetic(self, seed: int = 0):
+        check(_abi.lib().vvli_cuda_fill_synthetic(self._ctx, seed))
+
+    def reset(self):
+        """KVCache.clear (src/llm.zig:576-579)."""
+        check(_abi.lib().vvli_cuda_reset(self._ctx))
+
+    # ------------------------------------------------------------ forward
+    def forward_token(self, token: int, position: int, logits: bool = True):
+        """Runner.forwardToken (src/llm.zig:702-709): logits of `token` at `position`."""
+        out = np.empty(self.cfg.vocab_size, dtype=np.float32) if logits else None
+        am = ctypes.c_uint32(0)
+        check(_abi.lib().vvli_cuda_forward_token(self._ctx, token, position,
+                                                 None if out is None else out.ctypes.data_as(_f32p),
+                                                 ctypes.byref(am)))
+        self.last_argmax = int(am.value)
+        return out
+
+    def forward_embedding(self, embedding, position: int, logits: bool = True):
+        """Runner.forwardEmbedding (src/llm.zig:711-718)."""
+        e = np.ascontiguousarray(embedding, dtype=np.float32)
+        if e.size != self.cfg.hidden_size:
+            from .errors import VvliError
+            raise VvliError("InvalidWeight")
+        out = np.empty(self.cfg.vocab_size, dtype=np.float32) if logits else None
+        am = ctypes.c_uint32(0)
+        check(_abi.lib().vvli_cuda_forward_embedding(self._ctx, e.ctypes.data_as(_f32p), position,
+                                                     None if out is None else out.ctypes.data_as(_f32p),
+                                                     ctypes.byref(am)))
+        self.last_argmax = int(am.value)
+        return out
+
+    def prefill(self, tokens, start: int = 0, logits: bool = True):
+        """Runs tokens at positions start.. and returns the last token's logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty(self.cfg.vocab_size, dtype=np.float32) if logits else None
+        am = ctypes.c_uint32(0)
+        check(_abi.lib().vvli_cuda_prefill(self._ctx, t.ctypes.data_as(_u32p), t.size, start,
+                                           None if out is None else out.ctypes.data_as(_f32p), ctypes.byref(am)))
+        self.last_argmax = int(am.value)
+        return out
+
+    def generate_greedy(self, prompt, max_new_tokens: int, eos_token_id: int | None = None):
+        """On-device greedy loop; returns (tokens, vvli_generate_stats)."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max(1, max_new_tokens), dtype=np.uint32)
+        n = ctypes.c_uint64(0)
+        stats = _abi.CGenerateStats()
+        check(_abi.lib().vvli_cuda_generate_greedy(self._ctx, p.ctypes.data_as(_u32p), p.size, max_new_tokens,
+                                                   -1 if eos_token_id is None else int(eos_token_id),
+                                                   out.ctypes.data_as(_u32p), ctypes.byref(n), ctypes.byref(stats)))
+        return out[: n.value].tolist(), stats
+
+    def decode(self, n_steps: int):
+        """Continues greedy decoding on the device; returns (tokens, device_ms)."""
+        out = np.zeros(max(1, n_steps), dtype=np.uint32)
+        ms = ctypes.c_float(0)
+        check(_abi.lib().vvli_cuda_decode(self._ctx, n_steps, out.ctypes.data_as(_u32p), ctypes.byref(ms)))
+        return out[:n_steps].tolist(), float(ms.value)
+
+    def time_kernel(self, kernel: int, reps: int):
+        """(mean ms per launch, algorithmic bytes per launch) of one decode kernel alone."""
+        ms = ctypes.c_float(0)
+        b = ctypes.c_double(0)
+        check(_abi.lib().vvli_cuda_time_kernel(self._ctx, kernel, reps, ctypes.byref(ms), ctypes.byref(b)))
+        return float(ms.value), float(b.value)
+
+    # ------------------------------------------------------------ debug / timing
+    def set_debug(self, enabled: bool):
+        check(_abi.lib().vvli_cuda_set_debug(self._ctx, int(enabled)))
+
+    def debug_hidden(self, layer: int) -> np.ndarray:
+        out = np.empty(self.cfg.hidden_size, dtype=np.float32)
+        check(_abi.lib().vvli_cuda_debug_hidden(self._ctx, layer, out.ctypes.data_as(_f32p)))
+        return out
+
+    def last_forward_ms(self) -> float:
+        v = ctypes.c_float(0)
+        check(_abi.lib().vvli_cuda_last_forward_ms(self._ctx, ctypes.byref(v)))
+        return float(v.value)
