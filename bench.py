@@ -49,6 +49,7 @@ def parse_args():
     ap.add_argument("--kernel-reps", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling small cases)")
     return ap.parse_args()
 
 
@@ -241,6 +242,8 @@ def main():
         return float(t.item())
 
     cfg = PRESETS[args.config]()
+    if args.layers:
+        cfg.num_hidden_layers = args.layers
     max_seq = min(cfg.max_position_embeddings, args.prompt + args.warmup + args.steps + args.e2e_steps + 16)
     runner = vvli_b200.Runner(cfg, max_seq=max_seq, device=local_rank, tp_rank=rank, tp_size=n, nccl_id=nccl_id)
     runner.fill_synthetic(args.seed)

@@ -127,6 +127,10 @@ typedef struct vvli_ctx vvli_ctx;
  * (src/main.zig:438-467).  Never returns NULL. */
 const char* vvli_cuda_strerror(int status);
 
+/* Text of the last failure on the calling thread (the failing call and the
+ * CUDA/NCCL message), or "" if none.  Valid until the next call. */
+const char* vvli_cuda_last_error(void);
+
 /* Number of bf16 elements of the host weight blob for `cfg`, with every tensor
  * at a 64-byte aligned offset.  Replaces llm.storageElementCount
  * (src/llm.zig:814-837) for kind = .bf16. */

@@ -559,17 +559,22 @@ cudaError_t launch_synth_fill(uint16_t* dst, uint64_t key, uint64_t rows, uint64
   return cudaGetLastError();
 }
 
+template <typename Kern>
+static cudaError_t allow_dynamic_smem(Kern k, int max_smem_optin) {
+  // The opt-in limit covers static plus dynamic shared memory.
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, k);
+  if (e) return e;
+  return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              max_smem_optin - static_cast<int>(fa.sharedSizeBytes));
+}
+
 cudaError_t configure_kernels(int max_smem_optin) {
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_optin)))
-    return e;
-  if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_SILU_MUL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                max_smem_optin)))
-    return e;
-  if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                max_smem_optin)))
-    return e;
-  return cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_optin);
+  if ((e = allow_dynamic_smem(gemv_kernel<EPI_PLAIN>, max_smem_optin))) return e;
+  if ((e = allow_dynamic_smem(gemv_kernel<EPI_SILU_MUL>, max_smem_optin))) return e;
+  if ((e = allow_dynamic_smem(gemv_kernel<EPI_ARGMAX>, max_smem_optin))) return e;
+  return allow_dynamic_smem(attention_decode_kernel, max_smem_optin);
 }
 
 }  // namespace vvli

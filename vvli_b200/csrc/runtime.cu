@@ -525,6 +525,8 @@ const char* vvli_cuda_strerror(int status) {
   }
 }
 
+const char* vvli_cuda_last_error(void) { return g_last_error.c_str(); }
+
 int vvli_cuda_storage_elements(const vvli_model_config* cfg, uint64_t* out) {
   if (!cfg || !out) return VVLI_ERR_INVALID_ARGUMENT;
   int st = validate_config(*cfg);

@@ -39,6 +39,12 @@ class VvliError(Exception):
 
 
 def check(status, detail=""):
-    """Raises VvliError for a non-zero C status."""
+    """Raises VvliError for a non-zero C status, with the library's message."""
     if status != OK:
+        if not detail and status >= 20:
+            try:
+                from . import _abi
+                detail = _abi.lib().vvli_cuda_last_error().decode()
+            except Exception:
+                pass
         raise VvliError(CODES.get(status, f"Status{status}"), status, detail)
