@@ -48,6 +48,17 @@ struct GemvParams {
   float* local_best;       // finalize == 0: {value, index-as-float-bits} for the TP gather
   StepState* st;
   int* seq_tokens;
+  // bulk-copy pipeline plan (filled by launch_gemv)
+  int S;            // k-splits per row (1, 2, 4, 8 or 16); warp w owns split w % S
+  int SZ;           // 16-byte chunks per split
+  int cpl;          // chunks per lane per split
+  int R;            // rows per stage (per matrix of a pair)
+  int nst;          // stages in the ring
+  int stage_bytes;  // bytes per stage
+  int part_rows;    // rows reserved per CTA in the partial-sum area
+  // The GEMV that follows in the step: its head is prefetched into L2.
+  const uint16_t* next_W;
+  int next_N, next_K, next_pair_offset;
 };
 
 struct AttnParams {
@@ -59,7 +70,7 @@ struct AttnParams {
   float* part;             // [nq][splits][d+2] partial (o, m, l)
   unsigned* counters;      // [nkv]
   StepState* st;
-  int nq, nkv, d, group, splits, chunk_cap;
+  int nq, nkv, d, group, splits;
   float inv_sqrt_d;
   RopeParams rope;
 };
@@ -78,10 +89,11 @@ struct EmbedParams {
 
 // Launchers (pdl: launch with a programmatic edge to the previous kernel).
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
-cudaError_t launch_gemv(int epi, const GemvParams& p, int grid, cudaStream_t s, bool pdl);
-size_t gemv_smem_bytes(int epi, int N, int K, int grid);
+// Launches the GEMV on `sm_count` SMs: the bulk-copy pipeline kernel when a
+// row fits a stage (K <= 16384), else the register-streaming kernel.
+cudaError_t launch_gemv(int epi, GemvParams p, int sm_count, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
-size_t attention_smem_bytes(int group, int d, int chunk_cap);
+size_t attention_smem_bytes(int group, int d, int splits);
 cudaError_t launch_tp_argmax_finalize(const float* all_best, int ranks, StepState* st, int* seq_tokens,
                                       cudaStream_t s);
 cudaError_t launch_synth_fill(uint16_t* dst, uint64_t key, uint64_t rows, uint64_t cols, uint64_t src_ld,

@@ -161,8 +161,7 @@ struct vvli_ctx {
   int* seq_tokens = nullptr;
   StepState* st = nullptr;
   // launch shapes
-  int attn_splits = 1, attn_chunk_cap = 1;
-  int grid_qkv = 1, grid_o = 1, grid_gu = 1, grid_down = 1, grid_lm = 1;
+  int attn_splits = 1;
   // host staging (pinned)
   StepState* h_st = nullptr;
   int* h_tok = nullptr;
@@ -288,11 +287,6 @@ void plan_weights(vvli_ctx* c) {
   c->weight_elems = cur;
 }
 
-int gemv_grid(const vvli_ctx* c, int N) {
-  // Two resident CTAs per SM, never more CTAs than rows.
-  return std::max(1, std::min(N, 2 * c->sm_count));
-}
-
 int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
   const bool pdl = c->use_pdl && !debug;
   const bool tp = c->tp_size > 1;
@@ -303,9 +297,17 @@ int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
   RopeParams rope{c->cfg.rope_theta, static_cast<int>(c->cfg.rope_layout), static_cast<int>(c->cfg.rope_scaling_type),
                   c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
                   static_cast<float>(c->cfg.rope_original_max_position)};
+  auto next_qkv = [&](GemvParams& g, int l) {  // l = next layer, or L for the LM head
+    if (l < c->L) {
+      g.next_W = W + c->lay[l].w_qkv, g.next_N = c->q_rows + 2 * c->kv_rows, g.next_K = c->h;
+    } else {
+      g.next_W = W + c->off_lm, g.next_N = c->V_lr, g.next_K = c->h;
+    }
+  };
   for (int l = 0; l < c->L; ++l) {
     const DevLayer& D = c->lay[l];
     GemvParams q{};
+    q.next_W = W + D.w_o, q.next_N = c->h, q.next_K = c->q_rows;
     q.W = W + D.w_qkv;
     q.N = c->q_rows + 2 * c->kv_rows;
     q.K = c->h;
@@ -313,8 +315,9 @@ int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
     q.norm_w = W + D.in_norm;
     q.eps = c->cfg.rms_norm_eps;
     q.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv;
+    q.st = c->st;
     q.y = c->qkv;
-    CK(launch_gemv(EPI_PLAIN, q, c->grid_qkv, s, pdl));
+    CK(launch_gemv(EPI_PLAIN, q, c->sm_count, s, pdl));
 
     AttnParams a{};
     a.qkv = c->qkv;
@@ -330,25 +333,27 @@ int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
     a.d = c->d;
     a.group = c->group;
     a.splits = c->attn_splits;
-    a.chunk_cap = c->attn_chunk_cap;
     a.inv_sqrt_d = inv_sqrt_d;
     a.rope = rope;
     CK(launch_attention(a, s, pdl));
 
     GemvParams o{};
+    o.next_W = W + D.w_gu, o.next_N = c->I_l, o.next_K = c->h, o.next_pair_offset = c->I_l;
     o.W = W + D.w_o;
     o.N = c->h;
     o.K = c->q_rows;
     o.x = c->attn;
     o.residual = c->tp_rank == 0 ? c->x : nullptr;
+    o.st = c->st;
     o.y = c->x;
-    CK(launch_gemv(EPI_PLAIN, o, c->grid_o, s, pdl));
+    CK(launch_gemv(EPI_PLAIN, o, c->sm_count, s, pdl));
     if (tp) {
       int st = nccl_wait(c, nccl().AllReduce(c->x, c->x, c->h, ncclFloat32, ncclSum, c->comm, s), "allreduce");
       if (st) return st;
     }
 
     GemvParams gu{};
+    gu.next_W = W + D.w_down, gu.next_N = c->h, gu.next_K = c->I_l;
     gu.W = W + D.w_gu;
     gu.N = c->I_l;
     gu.K = c->h;
@@ -356,17 +361,20 @@ int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
     gu.x = c->x;
     gu.norm_w = W + D.post;
     gu.eps = c->cfg.rms_norm_eps;
+    gu.st = c->st;
     gu.y = c->ff;
-    CK(launch_gemv(EPI_SILU_MUL, gu, c->grid_gu, s, pdl && !tp));
+    CK(launch_gemv(EPI_SILU_MUL, gu, c->sm_count, s, pdl && !tp));
 
     GemvParams dn{};
+    next_qkv(dn, l + 1);
     dn.W = W + D.w_down;
     dn.N = c->h;
     dn.K = c->I_l;
     dn.x = c->ff;
     dn.residual = c->tp_rank == 0 ? c->x : nullptr;
+    dn.st = c->st;
     dn.y = c->x;
-    CK(launch_gemv(EPI_PLAIN, dn, c->grid_down, s, pdl));
+    CK(launch_gemv(EPI_PLAIN, dn, c->sm_count, s, pdl));
     if (tp) {
       int st = nccl_wait(c, nccl().AllReduce(c->x, c->x, c->h, ncclFloat32, ncclSum, c->comm, s), "allreduce");
       if (st) return st;
@@ -389,7 +397,7 @@ int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
   lm.local_best = c->best;
   lm.st = c->st;
   lm.seq_tokens = c->seq_tokens;
-  CK(launch_gemv(EPI_ARGMAX, lm, c->grid_lm, s, pdl && !tp));
+  CK(launch_gemv(EPI_ARGMAX, lm, c->sm_count, s, pdl && !tp));
   if (tp) {
     int st = nccl_wait(c, nccl().AllGather(c->best, c->all_best, 2, ncclFloat32, c->comm, s), "allgather");
     if (st) return st;
@@ -561,7 +569,11 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
   if (tp_size > 1 && !nccl_unique_id) return VVLI_ERR_INVALID_ARGUMENT;
   const uint64_t d = cfg->hidden_size / cfg->num_attention_heads;
   // Shapes this runtime's kernels take: 16-byte weight rows and head_dim <= 256.
-  if (cfg->hidden_size % 8 || cfg->intermediate_size % 8 || d > 256) return VVLI_ERR_UNSUPPORTED_ARCH;
+  // head_dim: a multiple of 4 up to 32, or 64, 128, 256; q heads per kv head x head_dim <= 2048.
+  const bool d_ok = (d <= 32 && d % 4 == 0) || d == 64 || d == 128 || d == 256;
+  if (cfg->hidden_size % 8 || cfg->intermediate_size % 8 || !d_ok ||
+      (cfg->num_attention_heads / cfg->num_key_value_heads) * d > 2048)
+    return VVLI_ERR_UNSUPPORTED_ARCH;
   if (cfg->num_key_value_heads % tp_size || cfg->intermediate_size % (8ull * tp_size)) return VVLI_ERR_INVALID_CONFIG;
   if (((cfg->num_attention_heads / tp_size) * d) % 8) return VVLI_ERR_INVALID_CONFIG;
 
@@ -619,24 +631,16 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
   for (int i = 0; i < c->max_pages; ++i) pt[i] = i;
   if ((e = cudaMemcpy(c->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice))) return fail(cuda_fail(e, "pt"));
 
-  // Attention split: about two CTAs per SM over the kv heads.
-  c->attn_splits = std::max(1, std::min<int>(static_cast<int>(max_seq), (2 * c->sm_count + c->nkv_l - 1) / c->nkv_l));
-  c->attn_chunk_cap = static_cast<int>((max_seq + c->attn_splits - 1) / c->attn_splits);
-  if (attention_smem_bytes(c->group, c->d, c->attn_chunk_cap) > static_cast<size_t>(smem_optin)) {
-    c->attn_chunk_cap = 1;  // recompute with more splits
-    c->attn_splits = static_cast<int>(max_seq);
-    while (c->attn_splits > 1 &&
-           attention_smem_bytes(c->group, c->d, static_cast<int>((max_seq + c->attn_splits / 2 - 1) / (c->attn_splits / 2))) <=
-               static_cast<size_t>(smem_optin))
-      c->attn_splits /= 2;
-    c->attn_chunk_cap = static_cast<int>((max_seq + c->attn_splits - 1) / c->attn_splits);
+  // Attention: one CTA per (kv head, group of 64-position pages); about two
+  // CTAs per SM over the kv heads once the context is long enough.
+  {
+    const int pages = static_cast<int>((max_seq + kPage - 1) / kPage);
+    c->attn_splits = std::max(1, std::min(pages, (2 * c->sm_count + c->nkv_l - 1) / c->nkv_l));
+    if (attention_smem_bytes(c->group, c->d, c->attn_splits) > static_cast<size_t>(smem_optin)) {
+      delete c;
+      return VVLI_ERR_UNSUPPORTED_ARCH;
+    }
   }
-  c->grid_qkv = gemv_grid(c, c->q_rows + 2 * c->kv_rows);
-  c->grid_o = gemv_grid(c, c->h);
-  c->grid_gu = gemv_grid(c, c->I_l);
-  c->grid_down = gemv_grid(c, c->h);
-  c->grid_lm = gemv_grid(c, c->V_lr);
-
   const size_t B = c->max_batch;
   if ((st = dalloc(&c->x, B * c->h)) || (st = dalloc(&c->qkv, B * (c->q_rows + 2 * c->kv_rows))) ||
       (st = dalloc(&c->attn, B * c->q_rows)) || (st = dalloc(&c->ff, B * c->I_l)) ||
@@ -852,50 +856,51 @@ int vvli_cuda_time_kernel(vvli_ctx* c, int kernel, int reps, float* avg_ms, doub
   CK(cudaSetDevice(c->device));
   const uint16_t* W = c->w;
   const double h = c->h;
-  auto params = [&](int l, int& epi, int& grid, double& b) {
+  auto params = [&](int l, int& epi, double& b) {
     const DevLayer& D = c->lay[l % c->L];
     GemvParams p{};
     p.eps = c->cfg.rms_norm_eps;
+    p.st = c->st;
     epi = EPI_PLAIN;
     switch (kernel) {
       case 0:
         p.W = W + D.w_qkv, p.N = c->q_rows + 2 * c->kv_rows, p.K = c->h, p.x = c->x, p.norm_w = W + D.in_norm;
-        p.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv, p.y = c->qkv, grid = c->grid_qkv;
+        p.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv, p.y = c->qkv;
         b = 2.0 * p.N * h + 4 * h + 2 * h + 4.0 * p.N + (p.bias ? 2.0 * p.N : 0);
         break;
       case 1:
-        p.W = W + D.w_o, p.N = c->h, p.K = c->q_rows, p.x = c->attn, p.residual = c->x, p.y = c->x, grid = c->grid_o;
+        p.W = W + D.w_o, p.N = c->h, p.K = c->q_rows, p.x = c->attn, p.residual = c->x, p.y = c->x;
         b = 2.0 * p.N * p.K + 4.0 * p.K + 8.0 * p.N;
         break;
       case 2:
         p.W = W + D.w_gu, p.N = c->I_l, p.K = c->h, p.pair_offset = c->I_l, p.x = c->x, p.norm_w = W + D.post;
-        p.y = c->ff, grid = c->grid_gu, epi = EPI_SILU_MUL;
+        p.y = c->ff, epi = EPI_SILU_MUL;
         b = 2.0 * 2 * p.N * h + 4 * h + 2 * h + 4.0 * p.N;
         break;
       case 3:
-        p.W = W + D.w_down, p.N = c->h, p.K = c->I_l, p.x = c->ff, p.residual = c->x, p.y = c->x, grid = c->grid_down;
+        p.W = W + D.w_down, p.N = c->h, p.K = c->I_l, p.x = c->ff, p.residual = c->x, p.y = c->x;
         b = 2.0 * p.N * p.K + 4.0 * p.K + 8.0 * p.N;
         break;
       default:
         p.W = W + c->off_lm, p.N = c->V_lr, p.K = c->h, p.x = c->x, p.norm_w = W + c->off_final, p.y = c->logits;
         p.part_val = c->amax_val, p.part_idx = c->amax_idx, p.counter = c->counters + c->nkv_l, p.row_base = c->v0;
         p.finalize = 0, p.local_best = c->best, p.st = c->st, p.seq_tokens = c->seq_tokens;
-        grid = c->grid_lm, epi = EPI_ARGMAX;
+        epi = EPI_ARGMAX;
         b = 2.0 * p.N * h + 4 * h + 2 * h + 4.0 * p.N;
         break;
     }
     return p;
   };
-  int epi = 0, grid = 1;
+  int epi = 0;
   double b = 0;
   for (int i = 0; i < 3; ++i) {  // warm-up
-    GemvParams p = params(i, epi, grid, b);
-    CK(launch_gemv(epi, p, grid, c->stream, false));
+    GemvParams p = params(i, epi, b);
+    CK(launch_gemv(epi, p, c->sm_count, c->stream, false));
   }
   CK(cudaEventRecord(c->ev0, c->stream));
   for (int i = 0; i < reps; ++i) {
-    GemvParams p = params(i, epi, grid, b);
-    CK(launch_gemv(epi, p, grid, c->stream, false));
+    GemvParams p = params(i, epi, b);
+    CK(launch_gemv(epi, p, c->sm_count, c->stream, false));
   }
   CK(cudaEventRecord(c->ev1, c->stream));
   CK(cudaEventSynchronize(c->ev1));
