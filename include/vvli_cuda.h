@@ -142,6 +142,18 @@ int vvli_cuda_storage_elements(const vvli_model_config* cfg, uint64_t* out_eleme
  * collectives); needed for the tensor-parallel split of src/llm.zig:732-766. */
 int vvli_cuda_nccl_unique_id(void* id);
 
+/* The tensor-parallel weight plan of rank `tp_rank` of `tp_size`, without a
+ * GPU: one row of 9 uint64 per copied piece {device element offset, tensor id
+ * in blob order, blob element offset of the tensor, rows, cols, source row
+ * length, first source row, first source column, kind (0 matrix/bias, 1 norm)}.
+ * q/k/v and gate/up are split by heads / rows, o_proj and down_proj by
+ * columns, the LM head by vocabulary rows.  Writes at most `cap` rows to `out`
+ * (may be NULL) and the total to `count`.  No counterpart in the reference,
+ * which has no sharding; it describes how this runtime slices the
+ * llm.OwnedModel blob (src/llm.zig:488-537). */
+int vvli_cuda_tp_plan(const vvli_model_config* cfg, int tp_rank, int tp_size, uint64_t* out, uint64_t cap,
+                      uint64_t* count);
+
 /* Creates a context on `device` for rank `tp_rank` of `tp_size` ranks.
  * Replaces KVCache.init + Scratch.init + Runner.init
  * (src/llm.zig:546-562, 626-668, 694-700; called from src/main.zig:161-171).

@@ -49,6 +49,7 @@ SIGNATURES = {
     "vvli_cuda_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vvli_cuda_last_error": (ctypes.c_char_p, []),
     "vvli_cuda_storage_elements": (ctypes.c_int, [_cfgp, _u64p]),
+    "vvli_cuda_tp_plan": (ctypes.c_int, [_cfgp, ctypes.c_int, ctypes.c_int, _u64p, ctypes.c_uint64, _u64p]),
     "vvli_cuda_nccl_unique_id": (ctypes.c_int, [ctypes.c_void_p]),
     "vvli_cuda_create": (ctypes.c_int, [_cfgp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(_ctx)]),

@@ -287,6 +287,31 @@ void plan_weights(vvli_ctx* c) {
   c->weight_elems = cur;
 }
 
+// Model and shard dimensions of rank `tp_rank` of `tp_size` (no CUDA calls).
+int fill_dims(vvli_ctx* c, const vvli_model_config& cfg, int tp_rank, int tp_size) {
+  const uint64_t d = cfg.hidden_size / cfg.num_attention_heads;
+  c->cfg = cfg;
+  c->tp_rank = tp_rank;
+  c->tp_size = tp_size;
+  c->h = static_cast<int>(cfg.hidden_size);
+  c->L = static_cast<int>(cfg.num_hidden_layers);
+  c->nq = static_cast<int>(cfg.num_attention_heads);
+  c->nkv = static_cast<int>(cfg.num_key_value_heads);
+  c->d = static_cast<int>(d);
+  c->group = c->nq / c->nkv;
+  c->I = static_cast<int>(cfg.intermediate_size);
+  c->V = static_cast<int>(cfg.vocab_size);
+  c->nq_l = c->nq / tp_size;
+  c->nkv_l = c->nkv / tp_size;
+  c->q_rows = c->nq_l * c->d;
+  c->kv_rows = c->nkv_l * c->d;
+  c->I_l = c->I / tp_size;
+  c->V_l = (c->V + tp_size - 1) / tp_size;
+  c->v0 = tp_rank * c->V_l;
+  c->V_lr = std::max(0, std::min(c->V, c->v0 + c->V_l) - c->v0);
+  return c->V_lr > 0 ? VVLI_OK : VVLI_ERR_INVALID_CONFIG;
+}
+
 int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
   const bool pdl = c->use_pdl && !debug;
   const bool tp = c->tp_size > 1;
@@ -317,7 +342,7 @@ int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
     q.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv;
     q.st = c->st;
     q.y = c->qkv;
-    CK(launch_gemv(EPI_PLAIN, q, c->sm_count, s, pdl));
+    CK(launch_gemv(EPI_PLAIN, q, c->sm_count, s, pdl && !(tp && l > 0)));  // no PDL edge after a collective
 
     AttnParams a{};
     a.qkv = c->qkv;
@@ -543,6 +568,25 @@ int vvli_cuda_storage_elements(const vvli_model_config* cfg, uint64_t* out) {
   return VVLI_OK;
 }
 
+int vvli_cuda_tp_plan(const vvli_model_config* cfg, int tp_rank, int tp_size, uint64_t* out, uint64_t cap,
+                      uint64_t* count) {
+  if (!cfg || !count || tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return VVLI_ERR_INVALID_ARGUMENT;
+  int st = validate_config(*cfg);
+  if (st) return st;
+  if (cfg->num_key_value_heads % tp_size || cfg->intermediate_size % (8ull * tp_size)) return VVLI_ERR_INVALID_CONFIG;
+  vvli_ctx tmp;
+  if ((st = fill_dims(&tmp, *cfg, tp_rank, tp_size))) return st;
+  plan_weights(&tmp);
+  *count = tmp.pieces.size();
+  for (size_t i = 0; i < tmp.pieces.size() && out && i < cap; ++i) {
+    const Piece& p = tmp.pieces[i];
+    const uint64_t row[9] = {p.dst, p.tensor_id, p.src, p.rows, p.cols, p.src_ld, p.row0, p.col0,
+                             static_cast<uint64_t>(p.kind)};
+    std::memcpy(out + 9 * i, row, sizeof(row));
+  }
+  return VVLI_OK;
+}
+
 int vvli_cuda_nccl_unique_id(void* id) {
   if (!id) return VVLI_ERR_INVALID_ARGUMENT;
   auto& n = nccl();
@@ -568,8 +612,7 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
   if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return VVLI_ERR_INVALID_ARGUMENT;
   if (tp_size > 1 && !nccl_unique_id) return VVLI_ERR_INVALID_ARGUMENT;
   const uint64_t d = cfg->hidden_size / cfg->num_attention_heads;
-  // Shapes this runtime's kernels take: 16-byte weight rows and head_dim <= 256.
-  // head_dim: a multiple of 4 up to 32, or 64, 128, 256; q heads per kv head x head_dim <= 2048.
+  // Shapes the kernels take: 16-byte weight rows; head_dim a multiple of 4 up to 32, or 64, 128, 256; q heads per kv head x head_dim <= 2048.
   const bool d_ok = (d <= 32 && d % 4 == 0) || d == 64 || d == 128 || d == 256;
   if (cfg->hidden_size % 8 || cfg->intermediate_size % 8 || !d_ok ||
       (cfg->num_attention_heads / cfg->num_key_value_heads) * d > 2048)
@@ -578,32 +621,13 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
   if (((cfg->num_attention_heads / tp_size) * d) % 8) return VVLI_ERR_INVALID_CONFIG;
 
   auto* c = new vvli_ctx();
-  c->cfg = *cfg;
-  c->device = device;
-  c->tp_rank = tp_rank;
-  c->tp_size = tp_size;
-  c->max_seq = max_seq;
-  c->max_batch = std::max<uint64_t>(1, max_batch);
-  c->h = static_cast<int>(cfg->hidden_size);
-  c->L = static_cast<int>(cfg->num_hidden_layers);
-  c->nq = static_cast<int>(cfg->num_attention_heads);
-  c->nkv = static_cast<int>(cfg->num_key_value_heads);
-  c->d = static_cast<int>(d);
-  c->group = c->nq / c->nkv;
-  c->I = static_cast<int>(cfg->intermediate_size);
-  c->V = static_cast<int>(cfg->vocab_size);
-  c->nq_l = c->nq / tp_size;
-  c->nkv_l = c->nkv / tp_size;
-  c->q_rows = c->nq_l * c->d;
-  c->kv_rows = c->nkv_l * c->d;
-  c->I_l = c->I / tp_size;
-  c->V_l = (c->V + tp_size - 1) / tp_size;
-  c->v0 = tp_rank * c->V_l;
-  c->V_lr = std::max(0, std::min(c->V, c->v0 + c->V_l) - c->v0);
-  if (c->V_lr <= 0) {
+  if (fill_dims(c, *cfg, tp_rank, tp_size) != VVLI_OK) {
     delete c;
     return VVLI_ERR_INVALID_CONFIG;
   }
+  c->device = device;
+  c->max_seq = max_seq;
+  c->max_batch = std::max<uint64_t>(1, max_batch);
 
   auto fail = [&](int code) {
     free_ctx(c);
