@@ -239,6 +239,19 @@ int vvli_cuda_time_kernel(vvli_ctx* ctx, int kernel, int reps, float* avg_ms, do
 int vvli_cuda_set_debug(vvli_ctx* ctx, int enabled);
 int vvli_cuda_debug_hidden(vvli_ctx* ctx, int layer, float* out);
 
+/* Reads a numeric property of the context: "megakernel" (1 when the step
+ * runs as one persistent kernel), "sm_count", "graph", "mega_ring_bytes",
+ * "mega_phases", "kernels_per_step", "weight_bytes".  No counterpart in the
+ * reference; for benchmarks and tests. */
+int vvli_cuda_query(vvli_ctx* ctx, const char* key, double* out);
+
+/* Megakernel timeline of the last step when the context was created with
+ * VVLI_TRACE=1 in the environment: %globaltimer ns per [phase][CTA][6] =
+ * consumers start, inputs loaded, rows consumed, outputs written, grid
+ * barrier passed, producer's first stage of the phase.  `count` receives the
+ * number of values (0 without tracing); `out` is filled when cap >= count. */
+int vvli_cuda_trace(vvli_ctx* ctx, uint64_t* out, uint64_t cap, uint64_t* count);
+
 /* Device-side timing of the last forward in milliseconds (CUDA events). */
 int vvli_cuda_last_forward_ms(vvli_ctx* ctx, float* out_ms);
 

@@ -10,34 +10,13 @@
 // and the LM head is gemv<ARGMAX> with the final-norm prologue
 // (src/llm.zig:727-728) and llm.argmax fused (src/llm.zig:778-789).
 #include "common.cuh"
+#include "device_fns.cuh"
 #include "kernels.h"
 
 #include <algorithm>
 #include <cstdlib>
 
 namespace vvli {
-
-// ---------------------------------------------------------------- shared helpers
-VVLI_DEV float dot8(uint4 w, const float* x) {
-  float acc = bf16_lo(w.x) * x[0];
-  acc = fmaf(bf16_hi(w.x), x[1], acc);
-  acc = fmaf(bf16_lo(w.y), x[2], acc);
-  acc = fmaf(bf16_hi(w.y), x[3], acc);
-  acc = fmaf(bf16_lo(w.z), x[4], acc);
-  acc = fmaf(bf16_hi(w.z), x[5], acc);
-  acc = fmaf(bf16_lo(w.w), x[6], acc);
-  acc = fmaf(bf16_hi(w.w), x[7], acc);
-  return acc;
-}
-
-// Publishes the step's argmax and advances the device step state: the token
-// following position `pos` is the argmax unless it is a prompt token.
-__device__ void publish_argmax(StepState* st, int* seq_tokens, int best) {
-  st->argmax = best;
-  const int np = st->pos + 1;
-  if (np <= st->max_seq && np >= st->prompt_len) seq_tokens[np] = best;  // seq_tokens has max_seq + 1 slots
-  st->pos = np;
-}
 
 // Row epilogue shared by both GEMV kernels: sums a row's k-split partials in
 // a fixed order, then applies bias / residual (linearRange + addInto,
@@ -132,18 +111,6 @@ __device__ void gemv_epilogue(const GemvParams& p, const float* part, int S, int
 // fixed order (deterministic).  Every mbarrier wait is bounded (2 s) and
 // reports VVLI_ERR_TIMEOUT through StepState.err.
 constexpr int kTmaMaxConsumerWarps = 16;
-
-// Sums a (lanes 0-15 get it) and b (lanes 16-31 get it) over the warp with
-// one butterfly: the first exchange swaps halves, so two reductions cost
-// five shuffles.
-VVLI_DEV float warp_sum2(float a, float b, int lane) {
-  const bool hi = lane & 16;
-  float v = hi ? b : a;
-  v += __shfl_xor_sync(0xffffffffu, hi ? a : b, 16);
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 
 template <int EPI, int MAXC, bool ILP2>
 __global__ void __launch_bounds__((kTmaMaxConsumerWarps + 1) * kWarp, 1) gemv_tma_kernel(const GemvParams p) {
@@ -467,51 +434,6 @@ cudaError_t launch_gemv(int epi, GemvParams p, int sm_count, cudaStream_t s, boo
   }
 }
 
-// ---------------------------------------------------------------- RoPE
-// Inverse frequency of rotary pair `dim_index` (rotatePair, src/llm.zig:1361-1364)
-// with the optional llama3 rope_scaling rule.
-__device__ float rope_inv_freq(const RopeParams& r, int dim_index, int d) {
-  const float exponent = static_cast<float>(dim_index) / static_cast<float>(d);
-  float inv_freq = 1.0f / powf(r.theta, exponent);
-  if (r.scaling == 1) {
-    const float two_pi = 6.283185307179586f;
-    const float low_wavelen = r.orig / r.low;
-    const float high_wavelen = r.orig / r.high;
-    const float wavelen = two_pi / inv_freq;
-    if (wavelen > low_wavelen) {
-      inv_freq = inv_freq / r.factor;
-    } else if (!(wavelen < high_wavelen)) {
-      const float smooth = (r.orig / wavelen - r.low) / (r.high - r.low);
-      inv_freq = (1.0f - smooth) * inv_freq / r.factor + smooth * inv_freq;
-    }
-  }
-  return inv_freq;
-}
-
-// Pair i of a head (0 <= i < d/2): element indices and the frequency index
-// (applyRoPE, src/llm.zig:1337-1359).
-VVLI_DEV void rope_pair(int layout, int i, int d, int& first, int& second, int& dim_index) {
-  if (layout == 0) {
-    first = 2 * i;
-    second = 2 * i + 1;
-  } else {
-    first = i;
-    second = i + d / 2;
-  }
-  dim_index = 2 * i;
-}
-
-VVLI_DEV void rope_rotate(const RopeParams& rp, int pos, int i, int d, const float* src, float* dst) {
-  int a, b, di;
-  rope_pair(rp.layout, i, d, a, b, di);
-  const float ang = static_cast<float>(pos) * rope_inv_freq(rp, di, d);
-  float sn, cs;
-  sincosf(ang, &sn, &cs);
-  const float x0 = src[a], x1 = src[b];
-  dst[a] = x0 * cs - x1 * sn;
-  dst[b] = x0 * sn + x1 * cs;
-}
-
 // ---------------------------------------------------------------- attention (decode)
 // computeAttentionInto (src/llm.zig:1302-1335) for one token over the paged
 // fp32 KV cache.  CTA (g, s) serves kv head g and the pages s, s + A,
@@ -525,11 +447,6 @@ VVLI_DEV void rope_rotate(const RopeParams& rp, int pos, int i, int d, const flo
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / kWarp;
 constexpr int kMaxAcc = 16;  // (group * head_dim) / 128 <= 16
-
-VVLI_DEV size_t kv_off(const int* pt, int t, int g, int nkv, int d) {
-  const int page = pt[t / kPage];
-  return (static_cast<size_t>(page * nkv + g) * kPage + (t % kPage)) * d;
-}
 
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnParams p) {
   extern __shared__ __align__(16) float sm[];

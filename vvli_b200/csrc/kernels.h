@@ -87,6 +87,78 @@ struct EmbedParams {
   int vocab;
 };
 
+// ---------------------------------------------------------------- decode megakernel
+// One cooperative launch runs a whole decode step as a list of phases.
+enum MegaKind { MK_EMBED = 0, MK_GEMV = 1, MK_ATTN = 2 };
+enum MegaEpi { ME_STORE = 0, ME_RESIDUAL = 1, ME_SILU = 2, ME_ARGMAX = 3 };
+constexpr int kMaxTp = 8;
+constexpr int kMegaConsumerWarps = 16;
+constexpr int kMegaThreads = (kMegaConsumerWarps + 1) * 32;
+
+struct MegaPhase {
+  int kind;                // MegaKind
+  int epi;                 // MegaEpi (GEMV phases)
+  int layer;
+  int nphys;               // 2: gate|up pair
+  const uint16_t* W;       // [N (x nphys), K] bf16
+  int N, K, pair_offset;
+  int S, SZ, cpl, R, stage_bytes;  // streaming plan (see launch_gemv)
+  const uint16_t* norm_w;  // non-null: input = rmsnorm(x) * norm_w, x = the residual stream
+  const float* x;          // input vector
+  float* y;                // output vector
+  const uint16_t* bias;
+  float* k_cache;          // MK_ATTN: this layer's K and V pages
+  float* v_cache;
+  int ar_index;            // ME_RESIDUAL: 2*layer (o_proj) or 2*layer+1 (down_proj)
+};
+
+struct MegaParams {
+  const MegaPhase* phases;
+  int nphases;
+  int nst, slot_bytes, part_floats;  // shared-memory ring and partial-sum area
+  int lookahead;           // stages the producer prefetches into L2 beyond the ring
+  StepState* st;
+  int* seq_tokens;
+  const uint16_t* emb;
+  const float* emb_in;
+  int h, vocab;
+  float* x;                // residual stream [h]
+  float* ssq;              // [gridDim.x] per-CTA sums of squares of x
+  float eps;
+  unsigned long long* bar; // grid barrier arrivals (grows forever; see megakernel.cu)
+  unsigned* epoch;         // increases by one per step (tensor-parallel flag values)
+  int n_ar;                // residual phases per step (2 * layers)
+  // attention
+  const float* qkv;
+  float* attn;
+  float* attn_part;
+  unsigned* attn_counters;
+  const int* page_table;
+  int nq, nkv, d, group, splits;
+  float inv_sqrt_d;
+  RopeParams rope;
+  // LM head argmax
+  float* amax_val;
+  int* amax_idx;
+  unsigned* amax_counter;
+  int row_base;
+  float* hidden;           // non-null: x after each layer, [layers][h]
+  uint64_t* trace;         // non-null: %globaltimer per [phase][cta][6] (see megakernel.cu)
+  // tensor parallelism: every peer's receive rows [2][tp][h], flags [2][tp][grid],
+  // argmax slots [tp][2] and their flags [tp]
+  int tp, rank;
+  float* peer_recv[kMaxTp];
+  unsigned* peer_flags[kMaxTp];
+  float* peer_best[kMaxTp];
+  unsigned* peer_best_flag[kMaxTp];
+};
+
+cudaError_t launch_megakernel(const MegaParams& p, int grid, size_t smem, cudaStream_t s);
+cudaError_t configure_megakernel(int max_smem_optin);
+// Streaming plan of one GEMV for the megakernel (16 consumer warps, <= 64 KB stages).
+void plan_mega_gemv(MegaPhase& ph);
+size_t mega_attention_floats(int group, int d, int splits);
+
 // Launchers (pdl: launch with a programmatic edge to the previous kernel).
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
 // Launches the GEMV on `sm_count` SMs: the bulk-copy pipeline kernel when a

@@ -1,0 +1,780 @@
+// megakernel.cu - one persistent, cooperative kernel per decode step.
+//
+// The step of Runner.forwardCurrentEmbedding (src/llm.zig:720-766) is a list
+// of phases: embed, then per layer q|k|v GEMV, attention, o_proj (+residual),
+// gate|up (silu*mul), down_proj (+residual), and the LM head with argmax.
+// One CTA per SM runs them all:
+//   * warp 16 is the producer.  It walks every GEMV phase of the step in
+//     order and streams this CTA's rows of each weight matrix through a ring
+//     of shared-memory stages with cp.async.bulk.  Weights do not depend on
+//     activations, so it never waits for a phase boundary: while the
+//     consumers run attention or wait at a grid barrier, the next matrix is
+//     already arriving.  HBM stays busy across the whole step.
+//   * warps 0-15 consume: they wait at a grid barrier for the phase input,
+//     run the phase (GEMV rows from the ring, or attention items), write
+//     their outputs and meet at the next grid barrier.
+// All cross-CTA data is read through L2 (ld.global.cg).  Every wait (ring
+// stages, grid barrier, tensor-parallel flags) is bounded and reports
+// VVLI_ERR_TIMEOUT in StepState.err.  Under tensor parallelism the
+// all-reduce after o_proj and down_proj is fused into their epilogues: each
+// CTA stores its partial rows into every peer's receive buffer over NVLink,
+// raises a flag on each peer, waits for the peers' flags for its rows and
+// adds the partials in rank order.
+#include "device_fns.cuh"
+#include "kernels.h"
+
+namespace vvli {
+
+constexpr int kCW = kMegaConsumerWarps;
+constexpr int kNC = kCW * kWarp;
+
+// ---------------------------------------------------------------- sync helpers
+VVLI_DEV unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+VVLI_DEV unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+VVLI_DEV void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid barrier of the consumer threads of every CTA (the producers never
+// join).  A 64-bit counter only grows: every CTA adds one per barrier with a
+// fire-and-forget release reduction, and barrier k of step `epoch` is passed
+// once the counter reaches (epoch * barriers_per_step + k + 1) * CTAs.  No
+// CTA waits for its own atomic to return and nothing is reset, so a barrier
+// costs about one memory round trip.  Split in two so a CTA can issue work
+// for its next phase between arriving and waiting.  The wait is bounded.
+VVLI_DEV uint64_t ld_acquire_gpu_u64(const unsigned long long* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ void grid_arrive(unsigned long long* bar) {
+  named_barrier(1, kNC);
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
+}
+
+__device__ bool grid_wait(const unsigned long long* bar, uint64_t target, int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    if (ld_acquire_gpu_u64(bar) < target) {
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t it = 0; ld_acquire_gpu_u64(bar) < target; ++it) {
+        if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+          atomicExch(err, kErrTimeout);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  named_barrier(1, kNC);
+  return ok != 0;
+}
+
+// Bounded wait until *flag == value (a peer's release store over NVLink).
+VVLI_DEV bool wait_flag_sys(const unsigned* flag, unsigned value, int* err) {
+  const uint64_t t0 = global_timer_ns();
+  while (ld_acquire_sys(flag) != value) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(err, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+VVLI_DEV int cta_row0(int N) { return static_cast<int>((static_cast<long long>(blockIdx.x) * N) / gridDim.x); }
+VVLI_DEV int cta_row1(int N) { return static_cast<int>((static_cast<long long>(blockIdx.x + 1) * N) / gridDim.x); }
+
+// Block-wide sum over the consumer threads, result on thread 0.
+__device__ float consumer_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  named_barrier(1, kNC);
+  float t = 0.f;
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kCW; ++i) t += red[i];
+  named_barrier(1, kNC);
+  return t;
+}
+
+// Optional timeline: per phase and CTA, [0] consumers start, [1] inputs
+// loaded, [2] rows consumed, [3] outputs written, [4] grid barrier passed,
+// [5] producer issued the phase's first stage.
+VVLI_DEV void trace_mark(const MegaParams& P, int f, int k) {
+  if (P.trace) P.trace[(static_cast<size_t>(f) * gridDim.x + blockIdx.x) * 6 + k] = global_timer_ns();
+}
+
+// ---------------------------------------------------------------- producer
+// Cursor over this CTA's stages of every GEMV phase of the step, in order.
+struct StageCursor {
+  int f = -1, i = 0, nstages = 0, r0 = 0, nrows = 0;
+  __device__ bool next(const MegaParams& P) {  // moves to the next stage; false at the end
+    ++i;
+    while (i >= nstages) {
+      if (++f >= P.nphases) return false;
+      const MegaPhase& ph = P.phases[f];
+      if (ph.kind != MK_GEMV) continue;
+      r0 = cta_row0(ph.N);
+      nrows = cta_row1(ph.N) - r0;
+      nstages = (nrows + ph.R - 1) / ph.R;
+      i = 0;
+    }
+    return true;
+  }
+};
+
+__device__ void mega_producer(const MegaParams& P, uint8_t* ring, uint64_t* full, uint64_t* empty, int* err) {
+  StageCursor cur, ahead;  // i = 0 >= nstages = 0: the first next() loads the first GEMV phase
+  bool ahead_ok = true;
+  // The L2 lookahead runs `lookahead` stages in front of the copies into the ring.
+  for (int k = 0; k < P.nst + P.lookahead && ahead_ok; ++k) {
+    ahead_ok = ahead.next(P);
+    if (ahead_ok && k >= P.nst) {
+      const MegaPhase& ph = P.phases[ahead.f];
+      const int rows_here = min(ph.R, ahead.nrows - ahead.i * ph.R);
+      const uint32_t bytes = static_cast<uint32_t>(rows_here * ph.K * 2);
+      for (int q = 0; q < ph.nphys; ++q)
+        prefetch_l2_bulk(ph.W + static_cast<size_t>(ahead.r0 + ahead.i * ph.R + q * ph.pair_offset) * ph.K, bytes);
+    }
+  }
+  uint32_t gi = 0;
+  int last_f = -1;
+  while (cur.next(P)) {
+    const MegaPhase& ph = P.phases[cur.f];
+    if (cur.f != last_f) {
+      trace_mark(P, cur.f, 5);
+      last_f = cur.f;
+    }
+    const uint32_t slot = gi % P.nst;
+    if (gi >= static_cast<uint32_t>(P.nst) && !mbar_wait(&empty[slot], ((gi / P.nst) - 1) & 1, err)) break;
+    const size_t row_bytes = static_cast<size_t>(ph.K) * 2;
+    const int rows_here = min(ph.R, cur.nrows - cur.i * ph.R);
+    const uint32_t bytes = static_cast<uint32_t>(rows_here * row_bytes);
+    mbar_arrive_expect_tx(&full[slot], bytes * ph.nphys);
+    for (int q = 0; q < ph.nphys; ++q)
+      bulk_g2s(ring + static_cast<size_t>(slot) * P.slot_bytes + q * ph.R * row_bytes,
+               ph.W + static_cast<size_t>(cur.r0 + cur.i * ph.R + q * ph.pair_offset) * ph.K, bytes, &full[slot]);
+    ++gi;
+    if (ahead_ok && (ahead_ok = ahead.next(P))) {
+      const MegaPhase& pa = P.phases[ahead.f];
+      const int ra = min(pa.R, ahead.nrows - ahead.i * pa.R);
+      const uint32_t ab = static_cast<uint32_t>(ra * pa.K * 2);
+      for (int q = 0; q < pa.nphys; ++q)
+        prefetch_l2_bulk(pa.W + static_cast<size_t>(ahead.r0 + ahead.i * pa.R + q * pa.pair_offset) * pa.K, ab);
+    }
+  }
+  // Every issued copy lands before the CTA exits.
+  const uint32_t first = gi > static_cast<uint32_t>(P.nst) ? gi - P.nst : 0;
+  for (uint32_t i = first; i < gi; ++i) mbar_wait(&full[i % P.nst], (i / P.nst) & 1, err);
+}
+
+// ---------------------------------------------------------------- GEMV phase (consumers)
+template <int MAXC>
+__device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, float* part, uint64_t* full,
+                          uint64_t* empty, uint32_t& gi, float* red, float* wv, int* wi, int* err, unsigned epoch0,
+                          int f) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = ph.K, S = ph.S, R = ph.R, nphys = ph.nphys;
+  const int r0 = cta_row0(ph.N), nrows = cta_row1(ph.N) - r0;
+  const int nstages = (nrows + R - 1) / R;
+  const size_t row_bytes = static_cast<size_t>(K) * 2;
+  // Inputs: this warp's slice of x times the norm weights.  RMSNorm's scale
+  // is one scalar, so it multiplies the finished dot products in the
+  // epilogue: W.(x*w*s) = s * W.(x*w).  Warp 0 sums the per-CTA squares
+  // meanwhile; nothing waits for it before the rows are consumed.
+  const int cpr = K >> 3;
+  const int split = warp % S;
+  const int cbeg = split * ph.SZ;
+  const int cend = min(cpr, cbeg + ph.SZ);
+  float ssq_lane = 0.f;
+  if (ph.norm_w && warp == 0) {
+    float v[8];  // up to 256 CTAs, all loads in flight together
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int b = lane + k * kWarp;
+      v[k] = b < static_cast<int>(gridDim.x) ? __ldcg(P.ssq + b) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ssq_lane += v[k];
+  }
+  float xr[MAXC][8];
+#pragma unroll
+  for (int j = 0; j < MAXC; ++j) {
+    const int c = cbeg + lane + kWarp * j;
+    if (j < ph.cpl && c < cend) {
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(ph.x + c * 8));
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(ph.x + c * 8 + 4));
+      xr[j][0] = a.x, xr[j][1] = a.y, xr[j][2] = a.z, xr[j][3] = a.w;
+      xr[j][4] = b.x, xr[j][5] = b.y, xr[j][6] = b.z, xr[j][7] = b.w;
+      if (ph.norm_w) {
+        const uint4 wn = *reinterpret_cast<const uint4*>(ph.norm_w + c * 8);
+        const float nw[8] = {bf16_lo(wn.x), bf16_hi(wn.x), bf16_lo(wn.y), bf16_hi(wn.y),
+                             bf16_lo(wn.z), bf16_hi(wn.z), bf16_lo(wn.w), bf16_hi(wn.w)};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xr[j][e] = xr[j][e] * nw[e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xr[j][e] = 0.f;
+    }
+  }
+  auto row_dot = [&](const uint8_t* rp) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAXC; ++j) {
+      const int c = cbeg + lane + kWarp * j;
+      if (j < ph.cpl && c < cend) acc += dot8(*reinterpret_cast<const uint4*>(rp + c * 16), xr[j]);
+    }
+    return acc;
+  };
+  if (tid == 0) trace_mark(P, f, 1);
+  if (ph.epi == ME_STORE && P.phases[f + 1].kind == MK_ATTN && tid < 4) {
+    // This CTA's attention item of the next phase: warm L2 with its K and V
+    // pages of positions before `pos` (its own token is written later).
+    const MegaPhase& at = P.phases[f + 1];
+    const int pos = P.st->pos;
+    const int pages = (pos + 1 + kPage - 1) / kPage;
+    const int A = min(P.splits, pages);
+    if (static_cast<int>(blockIdx.x) < P.nkv * A) {
+      const int g = blockIdx.x / A, s0 = blockIdx.x % A;
+      int k = 0;
+      for (int page = s0; page < pages; page += A, ++k) {
+        if ((k & 3) != tid) continue;
+        const size_t off = kv_off(P.page_table, page * kPage, g, P.nkv, P.d);
+        const uint32_t bytes = static_cast<uint32_t>(kPage * P.d * 4);
+        prefetch_l2_bulk(at.k_cache + off, bytes);
+        prefetch_l2_bulk(at.v_cache + off, bytes);
+      }
+    }
+  }
+  const int pairs = R * nphys * S;
+  for (int i = 0; i < nstages; ++i, ++gi) {
+    const uint32_t slot = gi % P.nst;
+    if (!mbar_wait(&full[slot], (gi / P.nst) & 1, err)) break;
+    const int rows_here = min(R, nrows - i * R);
+    const uint8_t* stg = ring + static_cast<size_t>(slot) * P.slot_bytes;
+    for (int pi = warp; pi < pairs; pi += 2 * kCW) {
+      const int pb = pi + kCW;
+      const int ta = pi / S, tb = pb / S;
+      const int pha = nphys == 2 ? (ta & 1) : 0, rowa = nphys == 2 ? (ta >> 1) : ta;
+      const int phb = nphys == 2 ? (tb & 1) : 0, rowb = nphys == 2 ? (tb >> 1) : tb;
+      const bool va = rowa < rows_here;
+      const bool vb = pb < pairs && rowb < rows_here;
+      const float a = va ? row_dot(stg + pha * R * row_bytes + rowa * row_bytes) : 0.f;
+      const float b = vb ? row_dot(stg + phb * R * row_bytes + rowb * row_bytes) : 0.f;
+      const float v = warp_sum2(a, b, lane);
+      if (lane == 0 && va) part[((i * R + rowa) * nphys + pha) * S + split] = v;
+      if (lane == 16 && vb) part[((i * R + rowb) * nphys + phb) * S + split] = v;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  __shared__ float scale_sh;
+  if (warp == 0) {
+    const float t = warp_sum(ssq_lane);
+    if (lane == 0) scale_sh = ph.norm_w ? 1.0f / sqrtf(t / static_cast<float>(K) + P.eps) : 1.0f;
+  }
+  named_barrier(1, kNC);
+  if (tid == 0) trace_mark(P, f, 2);
+  const float scale = scale_sh;
+
+  // ---- epilogue
+  if (ph.epi == ME_STORE || ph.epi == ME_SILU) {
+    for (int rl = tid; rl < nrows; rl += kNC) {
+      const int r = r0 + rl;
+      float a;
+      if (ph.epi == ME_SILU) {
+        float g = 0.f, u = 0.f;
+        for (int s = 0; s < S; ++s) {
+          g += part[(2 * rl) * S + s];
+          u += part[(2 * rl + 1) * S + s];
+        }
+        g *= scale;
+        u *= scale;
+        a = (g / (1.0f + expf(-g))) * u;  // siluMulInto, src/llm.zig:1382-1387
+      } else {
+        a = 0.f;
+        for (int s = 0; s < S; ++s) a += part[rl * S + s];
+        a *= scale;
+        if (ph.bias) a = a + bf16_to_f32(ph.bias[r]);
+      }
+      ph.y[r] = a;
+    }
+    return;
+  }
+  if (ph.epi == ME_RESIDUAL) {
+    // x[r] = x[r] + W.x (addInto, src/llm.zig:757, 765); under tensor
+    // parallelism the partials of all ranks are exchanged first.
+    float ss = 0.f;
+    if (P.tp > 1) {
+      // Flag values grow by one per residual phase: (step * 2L + index + 1).
+      const unsigned epoch = epoch0 * static_cast<unsigned>(P.n_ar) + static_cast<unsigned>(ph.ar_index) + 1u;
+      const int par = ph.ar_index & 1;
+      const size_t slot_off = static_cast<size_t>(par) * P.tp * P.h;
+      for (int rl = tid; rl < nrows; rl += kNC) {
+        float a = 0.f;
+        for (int s = 0; s < S; ++s) a += part[rl * S + s];
+        for (int q = 0; q < P.tp; ++q) P.peer_recv[q][slot_off + static_cast<size_t>(P.rank) * P.h + r0 + rl] = a;
+      }
+      __threadfence_system();
+      named_barrier(1, kNC);
+      const size_t flag_off = static_cast<size_t>(par) * P.tp * gridDim.x;
+      if (tid < P.tp) st_release_sys(P.peer_flags[tid] + flag_off + static_cast<size_t>(P.rank) * gridDim.x + blockIdx.x, epoch);
+      if (tid < P.tp) wait_flag_sys(P.peer_flags[P.rank] + flag_off + static_cast<size_t>(tid) * gridDim.x + blockIdx.x,
+                                    epoch, err);
+      named_barrier(1, kNC);
+      const float* recv = P.peer_recv[P.rank] + slot_off;
+      for (int rl = tid; rl < nrows; rl += kNC) {
+        const int r = r0 + rl;
+        float a = 0.f;
+        for (int q = 0; q < P.tp; ++q) a += __ldcg(recv + static_cast<size_t>(q) * P.h + r);
+        const float xn = __ldcg(P.x + r) + a;
+        P.x[r] = xn;
+        ss = fmaf(xn, xn, ss);
+        if (P.hidden && (ph.ar_index & 1)) P.hidden[static_cast<size_t>(ph.layer) * P.h + r] = xn;
+      }
+    } else {
+      for (int rl = tid; rl < nrows; rl += kNC) {
+        const int r = r0 + rl;
+        float a = 0.f;
+        for (int s = 0; s < S; ++s) a += part[rl * S + s];
+        const float xn = __ldcg(P.x + r) + a;
+        P.x[r] = xn;
+        ss = fmaf(xn, xn, ss);
+        if (P.hidden && (ph.ar_index & 1)) P.hidden[static_cast<size_t>(ph.layer) * P.h + r] = xn;
+      }
+    }
+    ss = consumer_sum(ss, red);
+    if (tid == 0) P.ssq[blockIdx.x] = ss;
+    return;
+  }
+  // ME_ARGMAX: logits and llm.argmax (src/llm.zig:778-789).
+  float best_v = -INFINITY;
+  int best_i = 0x7fffffff;
+  for (int rl = tid; rl < nrows; rl += kNC) {
+    const int r = r0 + rl;
+    float a = 0.f;
+    for (int s = 0; s < S; ++s) a += part[rl * S + s];
+    a *= scale;
+    ph.y[r] = a;
+    if (better(a, r + P.row_base, best_v, best_i)) {
+      best_v = a;
+      best_i = r + P.row_base;
+    }
+  }
+  warp_argmax(best_v, best_i);
+  if (lane == 0) {
+    wv[warp] = best_v;
+    wi[warp] = best_i;
+  }
+  named_barrier(1, kNC);
+  if (tid == 0) {
+    float bv = wv[0];
+    int bi = wi[0];
+    for (int i = 1; i < kCW; ++i)
+      if (better(wv[i], wi[i], bv, bi)) {
+        bv = wv[i];
+        bi = wi[i];
+      }
+    P.amax_val[blockIdx.x] = bv;
+    P.amax_idx[blockIdx.x] = bi;
+    __threadfence();
+    if (atomicAdd(P.amax_counter, 1u) == gridDim.x - 1) {
+      __threadfence();
+      float gv = __ldcg(P.amax_val);
+      int gidx = __ldcg(P.amax_idx);
+      for (unsigned b = 1; b < gridDim.x; ++b) {
+        const float v = __ldcg(P.amax_val + b);
+        const int i = __ldcg(P.amax_idx + b);
+        if (better(v, i, gv, gidx)) {
+          gv = v;
+          gidx = i;
+        }
+      }
+      *P.amax_counter = 0;
+      if (P.tp > 1) {
+        // Exchange (value, index) with every rank; ranks hold increasing vocab shards.
+        const unsigned epoch = epoch0 + 1u;
+        for (int q = 0; q < P.tp; ++q) {
+          P.peer_best[q][2 * P.rank] = gv;
+          P.peer_best[q][2 * P.rank + 1] = __int_as_float(gidx);
+        }
+        __threadfence_system();
+        for (int q = 0; q < P.tp; ++q) st_release_sys(P.peer_best_flag[q] + P.rank, epoch);
+        float bv2 = 0.f;
+        int bi2 = 0;
+        for (int q = 0; q < P.tp; ++q) {
+          wait_flag_sys(P.peer_best_flag[P.rank] + q, epoch, err);
+          const float v = __ldcg(P.peer_best[P.rank] + 2 * q);
+          const int i = __float_as_int(__ldcg(P.peer_best[P.rank] + 2 * q + 1));
+          if (q == 0 || better(v, i, bv2, bi2)) {
+            bv2 = v;
+            bi2 = i;
+          }
+        }
+        gidx = bi2;
+      }
+      publish_argmax(P.st, P.seq_tokens, gidx);
+      *P.epoch = epoch0 + 1u;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- attention phase (consumers)
+// computeAttentionInto (src/llm.zig:1302-1335): work item (kv head g, page
+// group s) of A = min(splits, pages) groups.  Loads are batched so the item
+// costs few dependent memory round trips under full weight streaming: q,
+// the new k and v, and the first page's K rows are fetched together; the
+// new position's k and v come from shared memory, not from the cache that
+// this CTA has just written.  The last CTA of a kv head merges the A
+// partial (o, max, sum) triples, loading them all at once.
+constexpr int kMaxSplitsMerged = 16;
+
+__device__ void mega_attention(const MegaParams& P, const MegaPhase& ph, float* sm, int* err, int f) {
+  __shared__ int last_flag;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = P.group, d = P.d;
+  const int pos = P.st->pos;
+  if (pos < 0 || pos >= P.st->max_seq) {
+    if (blockIdx.x == 0 && tid == 0) atomicExch(err, 1);  // VVLI_ERR_CONTEXT_FULL
+    return;
+  }
+  const int n_ctx = pos + 1;
+  const int pages = (n_ctx + kPage - 1) / kPage;
+  const int A = min(P.splits, pages);
+  const int items = P.nkv * A;
+  float* qs = sm;               // [G][d] rotated q
+  float* kvn = qs + G * d;      // [2][d] rotated new k, new v
+  float* sc = kvn + 2 * d;      // [G][kPage]
+  float* mrun = sc + G * kPage + (kNC / d) * G * d;  // after the P.V reduction area
+  float* lrun = mrun + G;
+  float* alpha = lrun + G;
+  float* wsplit = alpha + G;    // [G][splits]
+  const int half = d / 2;
+  const int EPL = d < 32 ? d : 32;
+  const int LP = d / EPL;
+  const int PPW = kWarp / LP;
+  const int pp = lane / LP, qq = lane % LP;
+  const int nacc = (G * d + kNC - 1) / kNC;  // <= 4
+
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int g = item / A, s = item % A;
+    const bool owns_pos = (pages - 1) % A == s;
+    const float* qg = P.qkv + static_cast<size_t>(g) * G * d;
+    const float* kn = P.qkv + static_cast<size_t>(P.nq) * d + static_cast<size_t>(g) * d;
+    const float* vn = kn + static_cast<size_t>(P.nkv) * d;
+    // RoPE of q and the new k in one pass over the rotary pairs.
+    for (int idx = tid; idx < (G + 1) * half; idx += kNC) {
+      const int hh = idx / half, i = idx % half;
+      int a, b, di;
+      rope_pair(P.rope.layout, i, d, a, b, di);
+      const float* src = hh < G ? qg + hh * d : kn;
+      const float x0 = __ldcg(src + a), x1 = __ldcg(src + b);
+      const float ang = static_cast<float>(pos) * rope_inv_freq(P.rope, di, d);
+      float sn, cs;
+      sincosf(ang, &sn, &cs);
+      float* dst = hh < G ? qs + hh * d : kvn;
+      dst[a] = x0 * cs - x1 * sn;
+      dst[b] = x0 * sn + x1 * cs;
+    }
+    for (int i = tid; i < d; i += kNC) kvn[d + i] = __ldcg(vn + i);
+    for (int hh = tid; hh < G; hh += kNC) {
+      mrun[hh] = -INFINITY;
+      lrun[hh] = 0.f;
+    }
+    named_barrier(1, kNC);
+    if (tid == 0) trace_mark(P, f, 1);
+    if (owns_pos) {  // this token's k and v enter the cache; this CTA reads them back after the barrier
+      const size_t off = kv_off(P.page_table, pos, g, P.nkv, d);
+      for (int i = tid; i < d; i += kNC) {
+        ph.k_cache[off + i] = kvn[i];
+        ph.v_cache[off + i] = kvn[d + i];
+      }
+      named_barrier(1, kNC);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int page = s; page < pages; page += A) {
+      const int t0 = page * kPage;
+      const int n = min(kPage, n_ctx - t0);
+      const size_t page_base = kv_off(P.page_table, t0, g, P.nkv, d);  // [page][kv head][kPage][d]
+      for (int base = warp * PPW; base < n; base += kCW * PPW) {
+        const int i = base + pp;
+        const bool ok = i < n;
+        const float* kr = ph.k_cache + page_base + static_cast<size_t>(ok ? i : 0) * d + qq * EPL;
+        float kv[32];  // this lane's EPL elements of the key, all loads in flight together
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const float4 k4 = (ok && e < EPL) ? *reinterpret_cast<const float4*>(kr + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+          kv[e] = k4.x, kv[e + 1] = k4.y, kv[e + 2] = k4.z, kv[e + 3] = k4.w;
+        }
+        for (int hh = 0; hh < G; ++hh) {
+          const float* qh = qs + hh * d + qq * EPL;
+          float dot = 0.f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e < EPL) dot = fmaf(qh[e], kv[e], dot);
+          for (int o = 1; o < LP; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+          if (ok && qq == 0) sc[hh * kPage + i] = dot * P.inv_sqrt_d;
+        }
+      }
+      named_barrier(1, kNC);
+      for (int hh = warp; hh < G; hh += kCW) {  // online softmax (softmaxInPlace, src/llm.zig:1408-1419)
+        float m = -INFINITY;
+        for (int i = lane; i < n; i += kWarp) m = fmaxf(m, sc[hh * kPage + i]);
+        m = warp_max(m);
+        const float mnew = fmaxf(mrun[hh], m);
+        float l = 0.f;
+        for (int i = lane; i < n; i += kWarp) {
+          const float e = expf(sc[hh * kPage + i] - mnew);
+          sc[hh * kPage + i] = e;
+          l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+          const float a = expf(mrun[hh] - mnew);
+          alpha[hh] = a;
+          lrun[hh] = lrun[hh] * a + l;
+          mrun[hh] = mnew;
+        }
+      }
+      named_barrier(1, kNC);
+      // P.V: thread (position group pg, dim e) loads each V element once for
+      // all q heads of the group; groups meet in shared memory.
+      {
+        const int NPG = kNC / d;
+        float* red = sc + G * kPage;  // [NPG][G][d]
+        if (tid < NPG * d) {
+          const int e = tid % d, pg = tid / d;
+          const float* vb = ph.v_cache + page_base + e;
+          float v[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int i = pg + u * NPG;
+            v[u] = i < n ? vb[static_cast<size_t>(i) * d] : 0.f;
+          }
+          float ah[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int i = pg + u * NPG;
+            if (i < n) {
+#pragma unroll
+              for (int hh = 0; hh < 8; ++hh)
+                if (hh < G) ah[hh] = fmaf(sc[hh * kPage + i], v[u], ah[hh]);
+            }
+          }
+#pragma unroll
+          for (int hh = 0; hh < 8; ++hh)
+            if (hh < G) red[(pg * G + hh) * d + e] = ah[hh];
+        }
+        named_barrier(1, kNC);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int idx = tid + k * kNC;
+          if (k < nacc && idx < G * d) {
+            const int hh = idx / d, e = idx % d;
+            float a = 0.f;
+            for (int pg = 0; pg < NPG; ++pg) a += red[(pg * G + hh) * d + e];
+            acc[k] = acc[k] * alpha[hh] + a;
+          }
+        }
+      }
+      named_barrier(1, kNC);
+    }
+    if (tid == 0) trace_mark(P, f, 2);
+    if (A == 1) {  // one split: normalise directly
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int idx = tid + k * kNC;
+        if (k < nacc && idx < G * d) P.attn[static_cast<size_t>(g * G) * d + idx] = acc[k] / lrun[idx / d];
+      }
+      named_barrier(1, kNC);
+      continue;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int idx = tid + k * kNC;
+      if (k < nacc && idx < G * d) {
+        const int hh = idx / d, e = idx % d;
+        P.attn_part[(static_cast<size_t>(g * G + hh) * P.splits + s) * (d + 2) + e] = acc[k];
+      }
+    }
+    for (int hh = tid; hh < G; hh += kNC) {
+      float* pp2 = P.attn_part + (static_cast<size_t>(g * G + hh) * P.splits + s) * (d + 2);
+      pp2[d] = mrun[hh];
+      pp2[d + 1] = lrun[hh];
+    }
+    __threadfence();
+    named_barrier(1, kNC);
+    if (tid == 0) last_flag = atomicAdd(&P.attn_counters[g], 1u) == static_cast<unsigned>(A) - 1;
+    named_barrier(1, kNC);
+    if (last_flag) {
+      __threadfence();
+      // Weights exp(m_s - M) / L per head and split.  The o partials of the
+      // first element a thread merges are loaded before the weights are
+      // computed, so the merge costs one round trip for G * d <= 512.
+      float ov[kMaxSplitsMerged];
+      auto load_ov = [&](int idx) {
+        const float* base = P.attn_part + static_cast<size_t>(g * G + idx / d) * P.splits * (d + 2) + idx % d;
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplitsMerged; ++sp)
+          if (sp < A) ov[sp] = __ldcg(base + sp * (d + 2));
+      };
+      if (tid < G * d) load_ov(tid);
+      for (int hh = warp; hh < G; hh += kCW) {
+        const float* base = P.attn_part + static_cast<size_t>(g * G + hh) * P.splits * (d + 2);
+        const float m = lane < A ? __ldcg(base + lane * (d + 2) + d) : -INFINITY;
+        const float l = lane < A ? __ldcg(base + lane * (d + 2) + d + 1) : 0.f;
+        const float M = warp_max(m);
+        const float w = lane < A ? expf(m - M) : 0.f;
+        const float L = warp_sum(l * w);
+        if (lane < A) wsplit[hh * P.splits + lane] = w / L;
+      }
+      named_barrier(1, kNC);
+      for (int idx = tid; idx < G * d; idx += kNC) {
+        if (idx != tid) load_ov(idx);
+        const int hh = idx / d;
+        float o = 0.f;
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplitsMerged; ++sp)
+          if (sp < A) o = fmaf(ov[sp], wsplit[hh * P.splits + sp], o);
+        P.attn[static_cast<size_t>(g * G) * d + idx] = o;
+      }
+      if (tid == 0) P.attn_counters[g] = 0;
+    }
+    named_barrier(1, kNC);
+  }
+}
+
+// ---------------------------------------------------------------- embed phase
+// copyEmbeddingToken (src/llm.zig:1373-1380) / forwardEmbedding's copy.
+__device__ void mega_embed(const MegaParams& P, float* red, int* err) {
+  const int tid = threadIdx.x;
+  const int r0 = cta_row0(P.h), r1 = cta_row1(P.h);
+  const int pos = P.st->pos;
+  int tok = (pos >= 0 && pos < P.st->max_seq) ? P.seq_tokens[pos] : 0;
+  if (!P.st->use_embedding && (tok < 0 || tok >= P.vocab)) {
+    if (blockIdx.x == 0 && tid == 0) atomicExch(err, 3);  // VVLI_ERR_INVALID_TOKEN
+    tok = 0;
+  }
+  float ss = 0.f;
+  for (int r = r0 + tid; r < r1; r += kNC) {
+    const float v = P.st->use_embedding ? P.emb_in[r] : bf16_to_f32(P.emb[static_cast<size_t>(tok) * P.h + r]);
+    P.x[r] = v;
+    ss = fmaf(v, v, ss);
+  }
+  ss = consumer_sum(ss, red);
+  if (tid == 0) P.ssq[blockIdx.x] = ss;
+}
+
+// ---------------------------------------------------------------- kernel
+__global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaParams P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float red[kCW];
+  __shared__ float wv[kCW];
+  __shared__ int wi[kCW];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  uint8_t* ring = smem;
+  float* part = reinterpret_cast<float*>(smem + static_cast<size_t>(P.nst) * P.slot_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(part + ((P.part_floats + 1) & ~1));
+  uint64_t* empty = full + P.nst;
+  int* err = &P.st->err;
+
+  if (tid == 0) {
+    for (int i = 0; i < P.nst; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kCW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == kCW) {
+    if ((tid & 31) == 0) mega_producer(P, ring, full, empty, err);
+    return;
+  }
+  uint32_t gi = 0;
+  uint32_t nbar = 0;  // barriers passed in this step
+  const unsigned epoch0 = __ldcg(P.epoch);
+  for (int f = 0; f < P.nphases; ++f) {
+    const MegaPhase& ph = P.phases[f];
+    if (tid == 0) trace_mark(P, f, 0);
+    if (ph.kind == MK_EMBED) {
+      mega_embed(P, red, err);
+    } else if (ph.kind == MK_ATTN) {
+      mega_attention(P, ph, part, err, f);
+    } else {
+      mega_gemv<4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f);  // plans have cpl <= 4
+    }
+    if (tid == 0) trace_mark(P, f, 3);
+    if (f + 1 < P.nphases) {
+      grid_arrive(P.bar);
+      // While the other CTAs arrive: warm L1/L2 with the next phase's
+      // constant vectors (norm weights, biases) of this CTA.
+      const MegaPhase& nx = P.phases[f + 1];
+      if (nx.kind == MK_GEMV) {
+        if (nx.norm_w && (tid + 1) * 64 <= nx.K * 2) prefetch_l2_bulk(nx.norm_w + tid * 32, 64);
+      }
+      // A barrier that gave up ends this CTA; the producer's own bounded
+      // waits then end it too.
+      const uint64_t target = (static_cast<uint64_t>(epoch0) * (P.nphases - 1) + nbar + 1) * gridDim.x;
+      ++nbar;
+      if (!grid_wait(P.bar, target, err)) break;
+    }
+    if (tid == 0) trace_mark(P, f, 4);
+  }
+}
+
+cudaError_t launch_megakernel(const MegaParams& p, int grid, size_t smem, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kMegaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_megakernel, p);
+}
+
+void plan_mega_gemv(MegaPhase& ph) {
+  const int cpr = ph.K / 8;
+  const size_t row_bytes = static_cast<size_t>(ph.K) * 2;
+  int S = 1;
+  while (S < kCW && S * 128 < cpr) S *= 2;
+  ph.S = S;
+  ph.SZ = (cpr + S - 1) / S;
+  ph.cpl = (ph.SZ + kWarp - 1) / kWarp;
+  const int want_pairs = 2 * kCW;
+  int R = (want_pairs + S * ph.nphys - 1) / (S * ph.nphys);
+  while (R > 1 && R * row_bytes * ph.nphys > 65536) R /= 2;
+  ph.R = R < 1 ? 1 : R;
+  ph.stage_bytes = static_cast<int>(ph.R * row_bytes * ph.nphys);
+}
+
+size_t mega_attention_floats(int group, int d, int splits) {
+  // q, new k|v, scores, P.V reduction [threads/d][group][d], running max/sum/alpha, merge weights
+  return static_cast<size_t>(group) * d + 2 * static_cast<size_t>(d) + static_cast<size_t>(group) * kPage +
+         static_cast<size_t>(kNC / d) * group * d + 3 * group + static_cast<size_t>(group) * splits;
+}
+
+cudaError_t configure_megakernel(int max_smem_optin) {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, decode_megakernel);
+  if (e) return e;
+  return cudaFuncSetAttribute(decode_megakernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              max_smem_optin - static_cast<int>(fa.sharedSizeBytes));
+}
+
+}  // namespace vvli

@@ -173,6 +173,17 @@ struct vvli_ctx {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_ms = 0.f;
   ncclComm_t comm = nullptr;
+  // decode megakernel (one cooperative launch per step)
+  bool use_mega = false;
+  std::vector<MegaPhase> h_phases;
+  MegaPhase* d_phases = nullptr;
+  MegaParams mp{};
+  size_t mega_smem = 0;
+  float* ssq = nullptr;
+  unsigned long long* bar = nullptr;  // megakernel barrier arrivals
+  unsigned* epoch = nullptr;
+  int mega_splits = 1;
+  uint64_t* trace = nullptr;  // VVLI_TRACE=1: megakernel timeline
 };
 
 namespace {
@@ -312,7 +323,120 @@ int fill_dims(vvli_ctx* c, const vvli_model_config& cfg, int tp_rank, int tp_siz
   return c->V_lr > 0 ? VVLI_OK : VVLI_ERR_INVALID_CONFIG;
 }
 
+// Phase table and launch parameters of the decode megakernel.  Returns
+// false when a shape is outside what the megakernel takes (the per-kernel
+// path then runs the step).
+bool plan_megakernel(vvli_ctx* c, int smem_optin) {
+  const uint16_t* W = c->w;
+  std::vector<MegaPhase> ph;
+  auto gemv = [&](int epi, int layer, const uint16_t* w, int N, int K, int nphys, const uint16_t* norm,
+                  const float* x, float* y, const uint16_t* bias, int ar_index) {
+    MegaPhase m{};
+    m.kind = MK_GEMV, m.epi = epi, m.layer = layer, m.nphys = nphys, m.W = w, m.N = N, m.K = K;
+    m.pair_offset = nphys == 2 ? N : 0;
+    m.norm_w = norm, m.x = x, m.y = y, m.bias = bias, m.ar_index = ar_index;
+    plan_mega_gemv(m);
+    ph.push_back(m);
+  };
+  MegaPhase e{};
+  e.kind = MK_EMBED;
+  ph.push_back(e);
+  for (int l = 0; l < c->L; ++l) {
+    const DevLayer& D = c->lay[l];
+    gemv(ME_STORE, l, W + D.w_qkv, c->q_rows + 2 * c->kv_rows, c->h, 1, W + D.in_norm, c->x, c->qkv,
+         D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv, 0);
+    MegaPhase a{};
+    a.kind = MK_ATTN, a.layer = l;
+    a.k_cache = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
+    a.v_cache = a.k_cache + c->kv_layer_floats;
+    ph.push_back(a);
+    gemv(ME_RESIDUAL, l, W + D.w_o, c->h, c->q_rows, 1, nullptr, c->attn, c->x, nullptr, 2 * l);
+    gemv(ME_SILU, l, W + D.w_gu, c->I_l, c->h, 2, W + D.post, c->x, c->ff, nullptr, 0);
+    gemv(ME_RESIDUAL, l, W + D.w_down, c->h, c->I_l, 1, nullptr, c->ff, c->x, nullptr, 2 * l + 1);
+  }
+  gemv(ME_ARGMAX, -1, W + c->off_lm, c->V_lr, c->h, 1, W + c->off_final, c->x, c->logits, nullptr, 0);
+
+  const int grid = c->sm_count;
+  int slot = 0;
+  size_t part = mega_attention_floats(c->group, c->d, c->mega_splits);
+  for (const MegaPhase& m : ph) {
+    if (m.kind != MK_GEMV) continue;
+    if (m.cpl > 4) return false;
+    if (c->group > 8 || (kMegaThreads - 32) % c->d || (kMegaThreads - 32) / c->d * 16 < kPage) return false;
+    slot = std::max(slot, m.stage_bytes);
+    part = std::max(part, static_cast<size_t>((m.N + grid - 1) / grid + 1) * m.nphys * m.S);
+  }
+  const size_t fixed = ((part + 1) & ~size_t(1)) * 4 + 2 * 8 * sizeof(uint64_t) + 1024;
+  int nst = static_cast<int>(std::min<size_t>(8, (static_cast<size_t>(smem_optin) - fixed) / slot));
+  // Two stages measured best: a deeper ring keeps more weight copies in
+  // flight, which lengthens every latency-bound access of the phase changes.
+  nst = std::min(nst, getenv("VVLI_MEGA_STAGES") ? std::max(2, atoi(getenv("VVLI_MEGA_STAGES"))) : 2);
+  if (nst < 2) return false;
+  c->mega_smem = static_cast<size_t>(nst) * slot + ((part + 1) & ~size_t(1)) * 4 + 2 * nst * sizeof(uint64_t);
+  if (cudaMalloc(&c->d_phases, ph.size() * sizeof(MegaPhase)) != cudaSuccess) return false;
+  if (cudaMemcpy(c->d_phases, ph.data(), ph.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice) != cudaSuccess)
+    return false;
+  c->h_phases = ph;
+  MegaParams& P = c->mp;
+  P = MegaParams{};
+  P.phases = c->d_phases;
+  P.nphases = static_cast<int>(ph.size());
+  P.nst = nst;
+  P.slot_bytes = slot;
+  // L2 prefetch beyond the ring: off by default (measured slower on B200:
+  // prefetched lines were evicted before the bulk copies read them).
+  P.lookahead = getenv("VVLI_MEGA_LOOKAHEAD") ? atoi(getenv("VVLI_MEGA_LOOKAHEAD")) : 0;
+  P.part_floats = static_cast<int>(part);
+  P.st = c->st;
+  P.seq_tokens = c->seq_tokens;
+  P.emb = W + c->off_emb;
+  P.emb_in = c->emb_in;
+  P.h = c->h;
+  P.vocab = c->V;
+  P.x = c->x;
+  P.ssq = c->ssq;
+  P.eps = c->cfg.rms_norm_eps;
+  P.bar = c->bar;
+  P.epoch = c->epoch;
+  P.n_ar = 2 * c->L;
+  P.qkv = c->qkv;
+  P.attn = c->attn;
+  P.attn_part = c->attn_part;
+  P.attn_counters = c->counters;
+  P.page_table = c->page_table;
+  P.nq = c->nq_l;
+  P.nkv = c->nkv_l;
+  P.d = c->d;
+  P.group = c->group;
+  P.splits = c->mega_splits;
+  P.inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
+  P.rope = RopeParams{c->cfg.rope_theta, static_cast<int>(c->cfg.rope_layout), static_cast<int>(c->cfg.rope_scaling_type),
+                      c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
+                      static_cast<float>(c->cfg.rope_original_max_position)};
+  P.amax_val = c->amax_val;
+  P.amax_idx = c->amax_idx;
+  P.amax_counter = c->counters + c->nkv_l;
+  P.row_base = c->v0;
+  P.tp = c->tp_size;
+  P.rank = c->tp_rank;
+  const char* tr = getenv("VVLI_TRACE");
+  if (tr && tr[0] == '1' &&
+      cudaMalloc(&c->trace, ph.size() * grid * 6 * sizeof(uint64_t)) == cudaSuccess) {
+    cudaMemset(c->trace, 0, ph.size() * grid * 6 * sizeof(uint64_t));
+    P.trace = c->trace;
+  }
+  return true;
+}
+
+int enqueue_mega(vvli_ctx* c, cudaStream_t s, bool debug) {
+  MegaParams P = c->mp;
+  P.hidden = debug ? c->hidden : nullptr;
+  CK(launch_megakernel(P, c->sm_count, c->mega_smem, s));
+  return VVLI_OK;
+}
+
 int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
+  if (c->use_mega) return enqueue_mega(c, s, debug);
   const bool pdl = c->use_pdl && !debug;
   const bool tp = c->tp_size > 1;
   const uint16_t* W = c->w;
@@ -445,12 +569,16 @@ int build_graph(vvli_ctx* c) {
     if (g) cudaGraphDestroy(g);
     return st;
   }
-  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  // A step that cannot be captured still runs, launched directly.
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return VVLI_OK;
+  }
   e = cudaGraphInstantiate(&c->graph, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) {
+    cudaGetLastError();
     c->graph = nullptr;
-    return cuda_fail(e, "cudaGraphInstantiate");
   }
   return VVLI_OK;
 }
@@ -486,6 +614,13 @@ int finish_state(vvli_ctx* c) {
   CK(cudaStreamSynchronize(c->stream));
   if (c->h_st->err) {
     g_last_error = "device step reported an error";
+    // An aborted megakernel step leaves its barrier count and epoch out of
+    // step with each other: start both over.
+    if (c->use_mega) {
+      cudaMemsetAsync(c->bar, 0, sizeof(unsigned long long), c->stream);
+      cudaMemsetAsync(c->epoch, 0, sizeof(unsigned), c->stream);
+      cudaStreamSynchronize(c->stream);
+    }
     return c->h_st->err;
   }
   return VVLI_OK;
@@ -512,7 +647,7 @@ void free_ctx(vvli_ctx* c) {
   if (c->comm) nccl().CommDestroy(c->comm);
   void* dev[] = {c->w, c->kv, c->page_table, c->x, c->qkv, c->attn, c->ff, c->logits, c->logits_full, c->emb_in,
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
-                 c->seq_tokens, c->st};
+                 c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (c->h_st) cudaFreeHost(c->h_st);
@@ -660,6 +795,7 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
   {
     const int pages = static_cast<int>((max_seq + kPage - 1) / kPage);
     c->attn_splits = std::max(1, std::min(pages, (2 * c->sm_count + c->nkv_l - 1) / c->nkv_l));
+    c->mega_splits = std::max(1, std::min({pages, c->sm_count / c->nkv_l, 16}));  // the merge stages <= 16 splits
     if (attention_smem_bytes(c->group, c->d, c->attn_splits) > static_cast<size_t>(smem_optin)) {
       delete c;
       return VVLI_ERR_UNSUPPORTED_ARCH;
@@ -671,7 +807,8 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
       (st = dalloc(&c->logits, B * static_cast<size_t>(c->V_l))) ||
       (st = dalloc(&c->logits_full, static_cast<size_t>(c->V_l) * tp_size)) || (st = dalloc(&c->emb_in, c->h)) ||
       (st = dalloc(&c->hidden, static_cast<size_t>(c->L) * c->h)) ||
-      (st = dalloc(&c->attn_part, static_cast<size_t>(c->nq_l) * c->attn_splits * (c->d + 2))) ||
+      (st = dalloc(&c->attn_part, static_cast<size_t>(c->nq_l) * std::max(c->attn_splits, c->mega_splits) * (c->d + 2))) ||
+      (st = dalloc(&c->ssq, c->sm_count)) || (st = dalloc(&c->bar, 1)) || (st = dalloc(&c->epoch, 1)) ||
       (st = dalloc(&c->amax_val, 2 * c->sm_count)) || (st = dalloc(&c->amax_idx, 2 * c->sm_count)) ||
       (st = dalloc(&c->best, 2)) || (st = dalloc(&c->all_best, 2 * tp_size)) ||
       (st = dalloc(&c->counters, c->nkv_l + 1)) || (st = dalloc(&c->seq_tokens, max_seq + 1)) ||
@@ -692,6 +829,12 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
     ncfg.blocking = 0;
     ncclResult_t r = n.CommInitRankConfig(&c->comm, tp_size, uid, tp_rank, &ncfg);
     if ((st = nccl_wait(c, r, "ncclCommInitRankConfig"))) return fail(st);
+  }
+  const char* mega_env = getenv("VVLI_MEGAKERNEL");
+  const bool want_mega = !(mega_env && mega_env[0] == '0') && tp_size == 1;
+  if (want_mega) {
+    if ((e = configure_megakernel(smem_optin))) return fail(cuda_fail(e, "configure_megakernel"));
+    c->use_mega = plan_megakernel(c, smem_optin);
   }
   *out_ctx = c;
   return VVLI_OK;
@@ -932,6 +1075,31 @@ int vvli_cuda_time_kernel(vvli_ctx* c, int kernel, int reps, float* avg_ms, doub
   CK(cudaEventElapsedTime(&ms, c->ev0, c->ev1));
   *avg_ms = ms / reps;
   *bytes = b;
+  return VVLI_OK;
+}
+
+int vvli_cuda_query(vvli_ctx* c, const char* key, double* out) {
+  if (!c || !key || !out) return VVLI_ERR_INVALID_ARGUMENT;
+  const std::string k(key);
+  if (k == "megakernel") *out = c->use_mega ? 1 : 0;
+  else if (k == "sm_count") *out = c->sm_count;
+  else if (k == "graph") *out = c->graph ? 1 : 0;
+  else if (k == "mega_ring_bytes") *out = c->use_mega ? static_cast<double>(c->mp.nst) * c->mp.slot_bytes : 0;
+  else if (k == "mega_phases") *out = c->use_mega ? c->mp.nphases : 0;
+  else if (k == "kernels_per_step")
+    *out = c->use_mega ? 1 : 1 + 5.0 * c->L + 1 + (c->tp_size > 1 ? 1 : 0);
+  else if (k == "weight_bytes") *out = static_cast<double>(c->weight_elems) * 2;
+  else return VVLI_ERR_INVALID_ARGUMENT;
+  return VVLI_OK;
+}
+
+int vvli_cuda_trace(vvli_ctx* c, uint64_t* out, uint64_t cap, uint64_t* count) {
+  if (!c || !count) return VVLI_ERR_INVALID_ARGUMENT;
+  *count = c->trace ? c->h_phases.size() * c->sm_count * 6 : 0;
+  if (c->trace && out && cap >= *count) {
+    CK(cudaSetDevice(c->device));
+    CK(cudaMemcpy(out, c->trace, *count * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+  }
   return VVLI_OK;
 }
 

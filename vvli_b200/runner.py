@@ -133,6 +133,12 @@ class Runner:
         check(_abi.lib().vvli_cuda_time_kernel(self._ctx, kernel, reps, ctypes.byref(ms), ctypes.byref(b)))
         return float(ms.value), float(b.value)
 
+    def query(self, key: str) -> float:
+        """A numeric property of the context (vvli_cuda_query)."""
+        v = ctypes.c_double(0)
+        check(_abi.lib().vvli_cuda_query(self._ctx, key.encode(), ctypes.byref(v)))
+        return float(v.value)
+
     # ------------------------------------------------------------ debug / timing
     def set_debug(self, enabled: bool):
         check(_abi.lib().vvli_cuda_set_debug(self._ctx, int(enabled)))
