@@ -705,6 +705,32 @@ cudaError_t launch_synth_fill(uint16_t* dst, uint64_t key, uint64_t rows, uint64
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- rotary pair rows
+// dst row (head*d + 2j) <- src row (head*d + j); dst row (head*d + 2j + 1) <- src row (head*d + j + d/2).
+__global__ void pair_rows_kernel(uint16_t* dst, const uint16_t* src, int rows, int K, int d) {
+  const size_t total = static_cast<size_t>(rows) * K;
+  for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(e / K), c = static_cast<int>(e % K);
+    const int head = r / d, i = r % d;
+    const int src_row = head * d + ((i & 1) ? i / 2 + d / 2 : i / 2);
+    dst[e] = src[static_cast<size_t>(src_row) * K + c];
+  }
+}
+
+cudaError_t launch_pair_rows(uint16_t* w, uint16_t* bias, uint16_t* tmp, int rows, int K, int d, cudaStream_t s) {
+  cudaError_t e = cudaMemcpyAsync(tmp, w, static_cast<size_t>(rows) * K * 2, cudaMemcpyDeviceToDevice, s);
+  if (e) return e;
+  pair_rows_kernel<<<148 * 8, 256, 0, s>>>(w, tmp, rows, K, d);
+  if ((e = cudaGetLastError())) return e;
+  if (bias) {
+    if ((e = cudaMemcpyAsync(tmp, bias, static_cast<size_t>(rows) * 2, cudaMemcpyDeviceToDevice, s))) return e;
+    pair_rows_kernel<<<8, 256, 0, s>>>(bias, tmp, rows, 1, d);
+    if ((e = cudaGetLastError())) return e;
+  }
+  return cudaSuccess;
+}
+
 template <typename Kern>
 static cudaError_t allow_dynamic_smem(Kern k, int max_smem_optin) {
   // The opt-in limit covers static plus dynamic shared memory.

@@ -90,7 +90,7 @@ struct EmbedParams {
 // ---------------------------------------------------------------- decode megakernel
 // One cooperative launch runs a whole decode step as a list of phases.
 enum MegaKind { MK_EMBED = 0, MK_GEMV = 1, MK_ATTN = 2 };
-enum MegaEpi { ME_STORE = 0, ME_RESIDUAL = 1, ME_SILU = 2, ME_ARGMAX = 3 };
+enum MegaEpi { ME_STORE = 0, ME_RESIDUAL = 1, ME_SILU = 2, ME_ARGMAX = 3, ME_QKV = 4 };
 constexpr int kMaxTp = 8;
 constexpr int kMegaConsumerWarps = 16;
 constexpr int kMegaThreads = (kMegaConsumerWarps + 1) * 32;
@@ -107,9 +107,10 @@ struct MegaPhase {
   const float* x;          // input vector
   float* y;                // output vector
   const uint16_t* bias;
-  float* k_cache;          // MK_ATTN: this layer's K and V pages
+  float* k_cache;          // MK_ATTN and ME_QKV: this layer's K and V pages
   float* v_cache;
   int ar_index;            // ME_RESIDUAL: 2*layer (o_proj) or 2*layer+1 (down_proj)
+  int row_align;           // CTA row ranges start at multiples of this (2 for ME_QKV: rotary pairs)
 };
 
 struct MegaParams {
@@ -157,7 +158,7 @@ cudaError_t launch_megakernel(const MegaParams& p, int grid, size_t smem, cudaSt
 cudaError_t configure_megakernel(int max_smem_optin);
 // Streaming plan of one GEMV for the megakernel (16 consumer warps, <= 64 KB stages).
 void plan_mega_gemv(MegaPhase& ph);
-size_t mega_attention_floats(int group, int d, int splits);
+size_t mega_attention_floats(int group, int d, int splits, int max_pages);
 
 // Launchers (pdl: launch with a programmatic edge to the previous kernel).
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
@@ -171,5 +172,10 @@ cudaError_t launch_tp_argmax_finalize(const float* all_best, int ranks, StepStat
 cudaError_t launch_synth_fill(uint16_t* dst, uint64_t key, uint64_t rows, uint64_t cols, uint64_t src_ld,
                               uint64_t row0, uint64_t col0, int kind, cudaStream_t s);
 cudaError_t configure_kernels(int max_smem_optin);
+// Reorders the q and k rows (and biases) of a fused q|k|v matrix so that the
+// two elements of every split-half rotary pair (i, i + d/2) sit on adjacent
+// rows (2i, 2i + 1): on the device, split-half RoPE becomes the interleaved
+// rule.  `rows` = q rows + k rows (whole heads of d rows), `tmp` holds rows x K.
+cudaError_t launch_pair_rows(uint16_t* w, uint16_t* bias, uint16_t* tmp, int rows, int K, int d, cudaStream_t s);
 
 }  // namespace vvli

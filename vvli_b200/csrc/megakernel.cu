@@ -92,8 +92,14 @@ VVLI_DEV bool wait_flag_sys(const unsigned* flag, unsigned value, int* err) {
   return true;
 }
 
-VVLI_DEV int cta_row0(int N) { return static_cast<int>((static_cast<long long>(blockIdx.x) * N) / gridDim.x); }
-VVLI_DEV int cta_row1(int N) { return static_cast<int>((static_cast<long long>(blockIdx.x + 1) * N) / gridDim.x); }
+// First row of CTA b's range of N rows; ranges start at multiples of `align`.
+VVLI_DEV int cta_row(int N, int b, int align) {
+  if (b >= static_cast<int>(gridDim.x)) return N;
+  const int r = static_cast<int>((static_cast<long long>(b) * N) / gridDim.x);
+  return r - r % align;
+}
+VVLI_DEV int cta_row0(int N) { return cta_row(N, blockIdx.x, 1); }
+VVLI_DEV int cta_row1(int N) { return cta_row(N, blockIdx.x + 1, 1); }
 
 // Block-wide sum over the consumer threads, result on thread 0.
 __device__ float consumer_sum(float v, float* red) {
@@ -125,8 +131,8 @@ struct StageCursor {
       if (++f >= P.nphases) return false;
       const MegaPhase& ph = P.phases[f];
       if (ph.kind != MK_GEMV) continue;
-      r0 = cta_row0(ph.N);
-      nrows = cta_row1(ph.N) - r0;
+      r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
+      nrows = cta_row(ph.N, blockIdx.x + 1, ph.row_align) - r0;
       nstages = (nrows + ph.R - 1) / ph.R;
       i = 0;
     }
@@ -186,7 +192,8 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
                           int f) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = ph.K, S = ph.S, R = ph.R, nphys = ph.nphys;
-  const int r0 = cta_row0(ph.N), nrows = cta_row1(ph.N) - r0;
+  const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
+  const int nrows = cta_row(ph.N, blockIdx.x + 1, ph.row_align) - r0;
   const int nstages = (nrows + R - 1) / R;
   const size_t row_bytes = static_cast<size_t>(K) * 2;
   // Inputs: this warp's slice of x times the norm weights.  RMSNorm's scale
@@ -239,7 +246,7 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
     return acc;
   };
   if (tid == 0) trace_mark(P, f, 1);
-  if (ph.epi == ME_STORE && P.phases[f + 1].kind == MK_ATTN && tid < 4) {
+  if (ph.epi == ME_QKV && P.phases[f + 1].kind == MK_ATTN && tid < 4) {
     // This CTA's attention item of the next phase: warm L2 with its K and V
     // pages of positions before `pos` (its own token is written later).
     const MegaPhase& at = P.phases[f + 1];
@@ -290,6 +297,49 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
   const float scale = scale_sh;
 
   // ---- epilogue
+  if (ph.epi == ME_QKV) {
+    // q|k|v rows with the bias (src/llm.zig:738-740); q and k rotated
+    // (applyRoPE, src/llm.zig:742-743; rows hold rotary pairs side by side);
+    // k and v go straight into the KV cache at `pos` (src/llm.zig:744-745).
+    const int pos = P.st->pos;
+    const bool pos_ok = pos >= 0 && pos < P.st->max_seq;
+    const int d = P.d, qr = P.nq * d, kr = P.nkv * d;
+    for (int pr = tid; pr < nrows / 2; pr += kNC) {
+      const int ra = r0 + 2 * pr;
+      float a = 0.f, b = 0.f;
+      for (int s = 0; s < S; ++s) {
+        a += part[(2 * pr) * S + s];
+        b += part[(2 * pr + 1) * S + s];
+      }
+      a *= scale;
+      b *= scale;
+      if (ph.bias) {
+        a = a + bf16_to_f32(ph.bias[ra]);
+        b = b + bf16_to_f32(ph.bias[ra + 1]);
+      }
+      if (ra < qr + kr) {
+        const int di = ra % d;  // pair j = di / 2 of the head, frequency index 2j
+        const float ang = static_cast<float>(pos) * rope_inv_freq(P.rope, di, d);
+        float sn, cs;
+        sincosf(ang, &sn, &cs);
+        const float x0 = a, x1 = b;
+        a = x0 * cs - x1 * sn;
+        b = x0 * sn + x1 * cs;
+      }
+      if (ra < qr) {
+        ph.y[ra] = a;
+        ph.y[ra + 1] = b;
+      } else if (pos_ok) {
+        const bool is_k = ra < qr + kr;
+        const int rel = is_k ? ra - qr : ra - qr - kr;
+        const size_t off = kv_off(P.page_table, pos, rel / d, P.nkv, d) + rel % d;
+        float* cache = is_k ? ph.k_cache : ph.v_cache;
+        cache[off] = a;
+        cache[off + 1] = b;
+      }
+    }
+    return;
+  }
   if (ph.epi == ME_STORE || ph.epi == ME_SILU) {
     for (int rl = tid; rl < nrows; rl += kNC) {
       const int r = r0 + rl;
@@ -455,13 +505,12 @@ __device__ void mega_attention(const MegaParams& P, const MegaPhase& ph, float* 
   const int A = min(P.splits, pages);
   const int items = P.nkv * A;
   float* qs = sm;               // [G][d] rotated q
-  float* kvn = qs + G * d;      // [2][d] rotated new k, new v
-  float* sc = kvn + 2 * d;      // [G][kPage]
-  float* mrun = sc + G * kPage + (kNC / d) * G * d;  // after the P.V reduction area
+  float* sc = qs + G * d;       // [G][kPage], then the P.V reduction [kNC/d][G][d]
+  float* mrun = sc + G * kPage + (kNC / d) * G * d;
   float* lrun = mrun + G;
   float* alpha = lrun + G;
   float* wsplit = alpha + G;    // [G][splits]
-  const int half = d / 2;
+  int* pt_sh = reinterpret_cast<int*>(wsplit + G * P.splits);  // page numbers of this item
   const int EPL = d < 32 ? d : 32;
   const int LP = d / EPL;
   const int PPW = kWarp / LP;
@@ -470,74 +519,76 @@ __device__ void mega_attention(const MegaParams& P, const MegaPhase& ph, float* 
 
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
     const int g = item / A, s = item % A;
-    const bool owns_pos = (pages - 1) % A == s;
+    // One round trip: the group's rotated q (written by the q|k|v epilogue)
+    // and the page numbers of this item's pages.
     const float* qg = P.qkv + static_cast<size_t>(g) * G * d;
-    const float* kn = P.qkv + static_cast<size_t>(P.nq) * d + static_cast<size_t>(g) * d;
-    const float* vn = kn + static_cast<size_t>(P.nkv) * d;
-    // RoPE of q and the new k in one pass over the rotary pairs.
-    for (int idx = tid; idx < (G + 1) * half; idx += kNC) {
-      const int hh = idx / half, i = idx % half;
-      int a, b, di;
-      rope_pair(P.rope.layout, i, d, a, b, di);
-      const float* src = hh < G ? qg + hh * d : kn;
-      const float x0 = __ldcg(src + a), x1 = __ldcg(src + b);
-      const float ang = static_cast<float>(pos) * rope_inv_freq(P.rope, di, d);
-      float sn, cs;
-      sincosf(ang, &sn, &cs);
-      float* dst = hh < G ? qs + hh * d : kvn;
-      dst[a] = x0 * cs - x1 * sn;
-      dst[b] = x0 * sn + x1 * cs;
-    }
-    for (int i = tid; i < d; i += kNC) kvn[d + i] = __ldcg(vn + i);
+    for (int idx = tid; idx < G * d; idx += kNC) qs[idx] = __ldcg(qg + idx);
+    for (int k = tid, page = s + tid * A; page < pages; k += kNC, page += kNC * A) pt_sh[k] = __ldcg(P.page_table + page);
     for (int hh = tid; hh < G; hh += kNC) {
       mrun[hh] = -INFINITY;
       lrun[hh] = 0.f;
     }
     named_barrier(1, kNC);
     if (tid == 0) trace_mark(P, f, 1);
-    if (owns_pos) {  // this token's k and v enter the cache; this CTA reads them back after the barrier
-      const size_t off = kv_off(P.page_table, pos, g, P.nkv, d);
-      for (int i = tid; i < d; i += kNC) {
-        ph.k_cache[off + i] = kvn[i];
-        ph.v_cache[off + i] = kvn[d + i];
-      }
-      named_barrier(1, kNC);
-    }
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int page = s; page < pages; page += A) {
+    const int NPG = kNC / d;
+    for (int page = s, pk = 0; page < pages; page += A, ++pk) {
       const int t0 = page * kPage;
       const int n = min(kPage, n_ctx - t0);
-      const size_t page_base = kv_off(P.page_table, t0, g, P.nkv, d);  // [page][kv head][kPage][d]
-      for (int base = warp * PPW; base < n; base += kCW * PPW) {
-        const int i = base + pp;
+      const size_t page_base = (static_cast<size_t>(pt_sh[pk] * P.nkv + g) * kPage) * d;  // [page][kv head][kPage][d]
+      // K rows for the scores and V rows for P.V are loaded together.
+      // Lane qq of a position holds float4 number j * LP + qq of the key, so
+      // the LP lanes of a position read LP * 16 contiguous bytes per load.
+      const int nf4 = EPL / 4;
+      const int i = warp * PPW + pp;  // score position of this lane (first pass)
+      float4 kv[8];
+      {
         const bool ok = i < n;
-        const float* kr = ph.k_cache + page_base + static_cast<size_t>(ok ? i : 0) * d + qq * EPL;
-        float kv[32];  // this lane's EPL elements of the key, all loads in flight together
+        const float4* kr = reinterpret_cast<const float4*>(ph.k_cache + page_base + static_cast<size_t>(ok ? i : 0) * d);
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          const float4 k4 = (ok && e < EPL) ? *reinterpret_cast<const float4*>(kr + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-          kv[e] = k4.x, kv[e + 1] = k4.y, kv[e + 2] = k4.z, kv[e + 3] = k4.w;
+        for (int j = 0; j < 8; ++j) kv[j] = (ok && j < nf4) ? __ldcg(kr + j * LP + qq) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float v[16];
+      const int ve = tid % d, vpg = tid / d;
+      const float* vb = ph.v_cache + page_base + ve;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int iv = vpg + u * NPG;
+        v[u] = (tid < NPG * d && iv < n) ? __ldcg(vb + static_cast<size_t>(iv) * d) : 0.f;
+      }
+      for (int pass = 0, base = warp * PPW; base < n; ++pass, base += kCW * PPW) {
+        const int ip = base + pp;
+        const bool ok = ip < n;
+        if (pass > 0) {  // positions beyond the first pass
+          const float4* kr = reinterpret_cast<const float4*>(ph.k_cache + page_base + static_cast<size_t>(ok ? ip : 0) * d);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) kv[j] = (ok && j < nf4) ? __ldcg(kr + j * LP + qq) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         for (int hh = 0; hh < G; ++hh) {
-          const float* qh = qs + hh * d + qq * EPL;
+          const float4* qh = reinterpret_cast<const float4*>(qs + hh * d);
           float dot = 0.f;
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (e < EPL) dot = fmaf(qh[e], kv[e], dot);
+          for (int j = 0; j < 8; ++j) {
+            if (j < nf4) {
+              const float4 q4 = qh[j * LP + qq];
+              dot = fmaf(q4.x, kv[j].x, fmaf(q4.y, kv[j].y, fmaf(q4.z, kv[j].z, fmaf(q4.w, kv[j].w, dot))));
+            }
+          }
           for (int o = 1; o < LP; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-          if (ok && qq == 0) sc[hh * kPage + i] = dot * P.inv_sqrt_d;
+          if (ok && qq == 0) sc[hh * kPage + ip] = dot * P.inv_sqrt_d;
         }
       }
       named_barrier(1, kNC);
+      if (tid == 0 && pk == 0) trace_mark(P, f, 5);
       for (int hh = warp; hh < G; hh += kCW) {  // online softmax (softmaxInPlace, src/llm.zig:1408-1419)
         float m = -INFINITY;
-        for (int i = lane; i < n; i += kWarp) m = fmaxf(m, sc[hh * kPage + i]);
+        for (int ii = lane; ii < n; ii += kWarp) m = fmaxf(m, sc[hh * kPage + ii]);
         m = warp_max(m);
         const float mnew = fmaxf(mrun[hh], m);
         float l = 0.f;
-        for (int i = lane; i < n; i += kWarp) {
-          const float e = expf(sc[hh * kPage + i] - mnew);
-          sc[hh * kPage + i] = e;
+        for (int ii = lane; ii < n; ii += kWarp) {
+          const float e = expf(sc[hh * kPage + ii] - mnew);
+          sc[hh * kPage + ii] = e;
           l += e;
         }
         l = warp_sum(l);
@@ -549,44 +600,33 @@ __device__ void mega_attention(const MegaParams& P, const MegaPhase& ph, float* 
         }
       }
       named_barrier(1, kNC);
-      // P.V: thread (position group pg, dim e) loads each V element once for
-      // all q heads of the group; groups meet in shared memory.
-      {
-        const int NPG = kNC / d;
-        float* red = sc + G * kPage;  // [NPG][G][d]
-        if (tid < NPG * d) {
-          const int e = tid % d, pg = tid / d;
-          const float* vb = ph.v_cache + page_base + e;
-          float v[16];
+      // P.V: thread (position group vpg, dim ve) uses each V element for all
+      // q heads of the group; groups meet in shared memory.
+      float* red = sc + G * kPage;  // [NPG][G][d]
+      if (tid < NPG * d) {
+        float ah[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int i = pg + u * NPG;
-            v[u] = i < n ? vb[static_cast<size_t>(i) * d] : 0.f;
+        for (int u = 0; u < 16; ++u) {
+          const int iv = vpg + u * NPG;
+          if (iv < n) {
+#pragma unroll
+            for (int hh = 0; hh < 8; ++hh)
+              if (hh < G) ah[hh] = fmaf(sc[hh * kPage + iv], v[u], ah[hh]);
           }
-          float ah[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int i = pg + u * NPG;
-            if (i < n) {
-#pragma unroll
-              for (int hh = 0; hh < 8; ++hh)
-                if (hh < G) ah[hh] = fmaf(sc[hh * kPage + i], v[u], ah[hh]);
-            }
-          }
-#pragma unroll
-          for (int hh = 0; hh < 8; ++hh)
-            if (hh < G) red[(pg * G + hh) * d + e] = ah[hh];
         }
-        named_barrier(1, kNC);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int idx = tid + k * kNC;
-          if (k < nacc && idx < G * d) {
-            const int hh = idx / d, e = idx % d;
-            float a = 0.f;
-            for (int pg = 0; pg < NPG; ++pg) a += red[(pg * G + hh) * d + e];
-            acc[k] = acc[k] * alpha[hh] + a;
-          }
+        for (int hh = 0; hh < 8; ++hh)
+          if (hh < G) red[(vpg * G + hh) * d + ve] = ah[hh];
+      }
+      named_barrier(1, kNC);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int idx = tid + k * kNC;
+        if (k < nacc && idx < G * d) {
+          const int hh = idx / d, e = idx % d;
+          float a = 0.f;
+          for (int pg = 0; pg < NPG; ++pg) a += red[(pg * G + hh) * d + e];
+          acc[k] = acc[k] * alpha[hh] + a;
         }
       }
       named_barrier(1, kNC);
@@ -763,10 +803,11 @@ void plan_mega_gemv(MegaPhase& ph) {
   ph.stage_bytes = static_cast<int>(ph.R * row_bytes * ph.nphys);
 }
 
-size_t mega_attention_floats(int group, int d, int splits) {
-  // q, new k|v, scores, P.V reduction [threads/d][group][d], running max/sum/alpha, merge weights
-  return static_cast<size_t>(group) * d + 2 * static_cast<size_t>(d) + static_cast<size_t>(group) * kPage +
-         static_cast<size_t>(kNC / d) * group * d + 3 * group + static_cast<size_t>(group) * splits;
+size_t mega_attention_floats(int group, int d, int splits, int max_pages) {
+  // q, scores, P.V reduction [threads/d][group][d], running max/sum/alpha, merge weights, page numbers
+  return static_cast<size_t>(group) * d + static_cast<size_t>(group) * kPage +
+         static_cast<size_t>(kNC / d) * group * d + 3 * group + static_cast<size_t>(group) * splits +
+         static_cast<size_t>((max_pages + splits - 1) / splits);
 }
 
 cudaError_t configure_megakernel(int max_smem_optin) {

@@ -334,7 +334,7 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
     MegaPhase m{};
     m.kind = MK_GEMV, m.epi = epi, m.layer = layer, m.nphys = nphys, m.W = w, m.N = N, m.K = K;
     m.pair_offset = nphys == 2 ? N : 0;
-    m.norm_w = norm, m.x = x, m.y = y, m.bias = bias, m.ar_index = ar_index;
+    m.norm_w = norm, m.x = x, m.y = y, m.bias = bias, m.ar_index = ar_index, m.row_align = 1;
     plan_mega_gemv(m);
     ph.push_back(m);
   };
@@ -343,8 +343,11 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   ph.push_back(e);
   for (int l = 0; l < c->L; ++l) {
     const DevLayer& D = c->lay[l];
-    gemv(ME_STORE, l, W + D.w_qkv, c->q_rows + 2 * c->kv_rows, c->h, 1, W + D.in_norm, c->x, c->qkv,
+    gemv(ME_QKV, l, W + D.w_qkv, c->q_rows + 2 * c->kv_rows, c->h, 1, W + D.in_norm, c->x, c->qkv,
          D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv, 0);
+    ph.back().k_cache = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
+    ph.back().v_cache = ph.back().k_cache + c->kv_layer_floats;
+    ph.back().row_align = 2;
     MegaPhase a{};
     a.kind = MK_ATTN, a.layer = l;
     a.k_cache = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
@@ -358,13 +361,13 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
 
   const int grid = c->sm_count;
   int slot = 0;
-  size_t part = mega_attention_floats(c->group, c->d, c->mega_splits);
+  size_t part = mega_attention_floats(c->group, c->d, c->mega_splits, c->max_pages);
   for (const MegaPhase& m : ph) {
     if (m.kind != MK_GEMV) continue;
     if (m.cpl > 4) return false;
     if (c->group > 8 || (kMegaThreads - 32) % c->d || (kMegaThreads - 32) / c->d * 16 < kPage) return false;
     slot = std::max(slot, m.stage_bytes);
-    part = std::max(part, static_cast<size_t>((m.N + grid - 1) / grid + 1) * m.nphys * m.S);
+    part = std::max(part, static_cast<size_t>((m.N + grid - 1) / grid + 2) * m.nphys * m.S);
   }
   const size_t fixed = ((part + 1) & ~size_t(1)) * 4 + 2 * 8 * sizeof(uint64_t) + 1024;
   int nst = static_cast<int>(std::min<size_t>(8, (static_cast<size_t>(smem_optin) - fixed) / slot));
@@ -410,7 +413,7 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   P.group = c->group;
   P.splits = c->mega_splits;
   P.inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
-  P.rope = RopeParams{c->cfg.rope_theta, static_cast<int>(c->cfg.rope_layout), static_cast<int>(c->cfg.rope_scaling_type),
+  P.rope = RopeParams{c->cfg.rope_theta, VVLI_ROPE_INTERLEAVED, static_cast<int>(c->cfg.rope_scaling_type),
                       c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
                       static_cast<float>(c->cfg.rope_original_max_position)};
   P.amax_val = c->amax_val;
@@ -443,7 +446,9 @@ int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
   EmbedParams ep{W + c->off_emb, c->emb_in, c->seq_tokens, c->st, c->x, c->h, c->V};
   CK(launch_embed(ep, s, false));
   const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
-  RopeParams rope{c->cfg.rope_theta, static_cast<int>(c->cfg.rope_layout), static_cast<int>(c->cfg.rope_scaling_type),
+  // q and k rows are stored in rotary-pair order (see after_load): the device
+  // applies the interleaved rule for both layouts.
+  RopeParams rope{c->cfg.rope_theta, VVLI_ROPE_INTERLEAVED, static_cast<int>(c->cfg.rope_scaling_type),
                   c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
                   static_cast<float>(c->cfg.rope_original_max_position)};
   auto next_qkv = [&](GemvParams& g, int l) {  // l = next layer, or L for the LM head
@@ -841,6 +846,23 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
 }
 
 static int after_load(vvli_ctx* c) {
+  // Split-half RoPE: put rotary pairs on adjacent q/k rows (device layout).
+  if (c->cfg.rope_layout == VVLI_ROPE_SPLIT_HALF) {
+    const int rows = c->q_rows + c->kv_rows;
+    uint16_t* tmp = nullptr;
+    CK(cudaMalloc(&tmp, static_cast<size_t>(rows) * c->h * 2));
+    for (int l = 0; l < c->L; ++l) {
+      const DevLayer& D = c->lay[l];
+      cudaError_t e = launch_pair_rows(c->w + D.w_qkv, D.b_qkv == UINT64_MAX ? nullptr : c->w + D.b_qkv, tmp, rows,
+                                       c->h, c->d, c->stream);
+      if (e) {
+        cudaFree(tmp);
+        return cuda_fail(e, "launch_pair_rows");
+      }
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    cudaFree(tmp);
+  }
   CK(cudaStreamSynchronize(c->stream));
   c->loaded = true;
   return build_graph(c);
