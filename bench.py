@@ -249,6 +249,7 @@ def main():
     runner.fill_synthetic(args.seed)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, size=args.prompt).astype(np.uint32)
     runner.prefill(prompt, 0, logits=False)
+    prefill_ms = allmax(runner.last_forward_ms())  # CUDA events around the whole prefill call
     runner.decode(max(3, args.warmup))
 
     # ---- device-timed decode: K graph replays, inputs resident in HBM
@@ -310,6 +311,17 @@ def main():
     step_roofline = {"bytes_per_token_per_gpu": step_bytes, "achieved": step_gbs, "peak": hbm, "unit": "GB/s",
                      "frac": step_gbs / hbm, "frac_of_8TBs_spec": step_gbs / 8000.0}
 
+    # Prefill of the prompt: tensor-core GEMMs (tcgen05) per linear layer.
+    h, kv, inter = cfg.hidden_size, cfg.kv_dim(), cfg.intermediate_size
+    layer_params = h * h + 2 * kv * h + h * h + 3 * inter * h
+    P = args.prompt
+    attn_flops = 4 * cfg.num_attention_heads * cfg.head_dim() * cfg.num_hidden_layers * P * (P + 1) / 2
+    gemm_flops = 2.0 * P * layer_params * cfg.num_hidden_layers
+    prefill = {"tokens": P, "ms": prefill_ms, "tok_per_s": P / (prefill_ms / 1000.0),
+               "algorithmic_tflops": (gemm_flops + attn_flops + 2.0 * h * cfg.vocab_size) / (prefill_ms / 1e3) / 1e12,
+               "tensor_core_gemm": runner.query("tc_prefill") == 1,
+               "note": "activations enter the tensor cores as bf16 hi+lo pairs (2 MMAs per product) for fp32-level "
+                       "parity; attention on CUDA cores"}
     launches_per_step = int(runner.query("kernels_per_step"))
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
@@ -321,6 +333,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, cfg, n),
                 "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "prefill": prefill,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clk}
         print(json.dumps(line), flush=True)
     runner.close()

@@ -241,7 +241,8 @@ int vvli_cuda_debug_hidden(vvli_ctx* ctx, int layer, float* out);
 
 /* Reads a numeric property of the context: "megakernel" (1 when the step
  * runs as one persistent kernel), "sm_count", "graph", "mega_ring_bytes",
- * "mega_phases", "kernels_per_step", "weight_bytes".  No counterpart in the
+ * "mega_phases", "kernels_per_step", "weight_bytes", "tc_prefill" (1 when
+ * prefill runs on the tensor cores).  No counterpart in the
  * reference; for benchmarks and tests. */
 int vvli_cuda_query(vvli_ctx* ctx, const char* key, double* out);
 
@@ -251,6 +252,12 @@ int vvli_cuda_query(vvli_ctx* ctx, const char* key, double* out);
  * barrier passed, producer's first stage of the phase.  `count` receives the
  * number of values (0 without tracing); `out` is filled when cap >= count. */
 int vvli_cuda_trace(vvli_ctx* ctx, uint64_t* out, uint64_t cap, uint64_t* count);
+
+/* Self-test of the tensor-core (tcgen05) prefill GEMM with no counterpart in
+ * the reference: C[M,N] = (A_hi + A_lo)[M,K] . W[N,K]^T on random bf16 data
+ * (two_a = 0: A_hi only) against a SIMT reference on `device`;
+ * `max_rel_err` = max |C - ref| / max |ref|. */
+int vvli_cuda_gemm_selftest(int device, int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err);
 
 /* Device-side timing of the last forward in milliseconds (CUDA events). */
 int vvli_cuda_last_forward_ms(vvli_ctx* ctx, float* out_ms);

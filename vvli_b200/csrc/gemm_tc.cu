@@ -1,0 +1,552 @@
+// gemm_tc.cu - prefill on the tensor cores (tcgen05 + TMEM + TMA) and its SIMT helpers.
+//
+// The reference prefills one token at a time (src/generator.zig:243-251), so
+// every weight matrix is read once per prompt token.  Here a prompt chunk of
+// M tokens runs each linear layer as one GEMM C[M, N] = A[M, K] . W[N, K]^T:
+//   * 128 x 256 output tile per CTA, 64-element k-blocks (128-byte rows,
+//     128-byte swizzle), 3-stage ring of shared-memory stages;
+//   * warp 0: TMA producer (cp.async.bulk.tensor 2-D, no multicast);
+//     warp 1: allocates 256 TMEM columns, one thread issues
+//     tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32 in TMEM) and
+//     frees stages with tcgen05.commit; warps 2-5: epilogue, tcgen05.ld of
+//     the accumulator (TMEM lane = token row);
+//   * activations are fp32 in the reference.  They enter the tensor cores as
+//     two bf16 operands, hi = bf16(a) and lo = bf16(a - hi), and both MMAs
+//     accumulate into the same TMEM tile, so A is represented to about 16
+//     mantissa bits while W (bf16 already) is exact;
+//   * epilogues: q|k|v (+bias, RoPE on q and k, k and v into the paged KV
+//     cache), residual add into the fp32 hidden rows, and silu(g)*u written
+//     as the next GEMM's hi/lo operand.
+// All mbarrier waits are bounded and report VVLI_ERR_TIMEOUT through p.err.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "device_fns.cuh"
+#include "gemm_tc.cuh"
+
+namespace vvli {
+
+constexpr int kGemmStages = 3;
+constexpr uint32_t kTileA = kGemmBM * kGemmBK * 2;   // 16 KB
+constexpr uint32_t kTileB = kGemmBN * kGemmBK * 2;   // 32 KB
+constexpr uint32_t kStageBytes = 2 * kTileA + kTileB;  // A_hi | A_lo | B
+constexpr int kGemmThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+
+// ---------------------------------------------------------------- PTX wrappers
+VVLI_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+VVLI_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+VVLI_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand tile, 128-byte swizzle: rows of 128 bytes, 8-row groups of
+// 1024 bytes (stride byte offset), descriptor version 1, layout SWIZZLE_128B.
+VVLI_DEV uint64_t umma_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(16 >> 4) << 16;    // leading byte offset (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset: next 8-row group
+  d |= static_cast<uint64_t>(1) << 46;          // descriptor version
+  d |= static_cast<uint64_t>(2) << 61;          // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D fp32, A and B bf16, both K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(kGemmBN) >> 3) << 17) |
+                            ((static_cast<uint32_t>(kGemmBM) >> 4) << 24);
+
+VVLI_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+VVLI_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+VVLI_DEV void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+VVLI_DEV void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
+  hi = f32_to_bf16(v);
+  lo = f32_to_bf16(v - bf16_to_f32(hi));
+}
+
+// ---------------------------------------------------------------- GEMM kernel
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
+                   const __grid_constant__ CUtensorMap tm_w, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles want 1024-byte alignment
+  uint8_t* sm = smem_raw + (base - raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kGemmStages * kStageBytes);
+  uint64_t* empty = full + kGemmStages;
+  uint64_t* tmem_full = empty + kGemmStages;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr bool kPair = EPI == GE_SILU;
+  const int m0 = blockIdx.y * kGemmBM;
+  const int n0 = blockIdx.x * (kPair ? kGemmBN / 2 : kGemmBN);  // first output column of the tile
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGemmStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(tmem_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      const uint32_t bytes = (p.two_a ? 2 * kTileA : kTileA) + kTileB;
+      const int rb0 = kPair ? n0 : n0;
+      const int rb1 = kPair ? p.pair_offset + n0 : n0 + kGemmBN / 2;
+      int issued = 0;
+      for (int kb = 0; kb < p.nk; ++kb) {
+        const int s = kb % kGemmStages;
+        if (kb >= kGemmStages && !mbar_wait(&empty[s], ((kb / kGemmStages) - 1) & 1, p.err)) break;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        const uint32_t st = base + s * kStageBytes;
+        const int x = kb * kGemmBK;
+        tma_load_2d(st, &tm_a_hi, x, m0, &full[s]);
+        if (p.two_a) tma_load_2d(st + kTileA, &tm_a_lo, x, m0, &full[s]);
+        tma_load_2d(st + 2 * kTileA, &tm_w, x, rb0, &full[s]);
+        tma_load_2d(st + 2 * kTileA + kTileB / 2, &tm_w, x, rb1, &full[s]);
+        issued = kb + 1;
+      }
+      for (int i = issued > kGemmStages ? issued - kGemmStages : 0; i < issued; ++i)
+        mbar_wait(&full[i % kGemmStages], (i / kGemmStages) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      bool ok = true;
+      for (int kb = 0; kb < p.nk && ok; ++kb) {
+        const int s = kb % kGemmStages;
+        if (!(ok = mbar_wait(&full[s], (kb / kGemmStages) & 1, p.err))) break;
+        tc_fence_after();
+        const uint32_t st = base + s * kStageBytes;
+#pragma unroll
+        for (int k = 0; k < kGemmBK / 16; ++k) {  // UMMA_K = 16 bf16 = 32 bytes
+          const uint64_t bdesc = umma_desc(st + 2 * kTileA + k * 32);
+          umma_bf16(tmem, umma_desc(st + k * 32), bdesc, (kb | k) != 0);
+          if (p.two_a) umma_bf16(tmem, umma_desc(st + kTileA + k * 32), bdesc, 1u);
+        }
+        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      umma_commit(tmem_full);
+    }
+  } else {  // ---- epilogue: warps 2-5, TMEM lanes 32 * (warp % 4) ..
+    const int wq = warp & 3;
+    const int row = m0 + wq * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    if (mbar_wait(tmem_full, 0, p.err)) {
+      tc_fence_after();
+      float v[32];
+      if constexpr (EPI == GE_SILU) {
+        float u[32];
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(trow + c * 32, v);        // gate columns
+          tmem_ld32(trow + 128 + c * 32, u);  // up columns
+          if (row < p.M) {
+            uint16_t* oh = p.out_hi + static_cast<size_t>(row) * p.ld_out;
+            uint16_t* ol = p.out_lo + static_cast<size_t>(row) * p.ld_out;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int n = n0 + c * 32 + i;
+              if (n < p.N) {
+                const float g = v[i];
+                const float f = (g / (1.0f + expf(-g))) * u[i];  // siluMulInto, src/llm.zig:1382-1387
+                split_bf16(f, oh[n], ol[n]);
+              }
+            }
+          }
+        }
+      } else {
+        for (int c = 0; c < kGemmBN / 32; ++c) {
+          tmem_ld32(trow + c * 32, v);
+          if (row >= p.M) continue;
+          const int nb = n0 + c * 32;
+          if constexpr (EPI == GE_RESID) {
+            float* y = p.y + static_cast<size_t>(row) * p.ldy;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (nb + i < p.N) y[nb + i] = (p.add_residual ? y[nb + i] : 0.f) + v[i];  // addInto
+          } else {  // GE_QKV
+            const int pos = p.pos0 + row;
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const int n = nb + i;
+              if (n >= p.N) break;
+              float a = v[i], b = v[i + 1];
+              if (p.bias) {
+                a = a + bf16_to_f32(p.bias[n]);
+                b = b + bf16_to_f32(p.bias[n + 1]);
+              }
+              if (n < p.q_rows + p.kv_rows) {  // q and k rows hold rotary pairs side by side
+                const float ang = static_cast<float>(pos) * rope_inv_freq(p.rope, n % p.d, p.d);
+                float sn, cs;
+                sincosf(ang, &sn, &cs);
+                const float x0 = a, x1 = b;
+                a = x0 * cs - x1 * sn;
+                b = x0 * sn + x1 * cs;
+              }
+              if (n < p.q_rows) {
+                p.y[static_cast<size_t>(row) * p.ldy + n] = a;
+                p.y[static_cast<size_t>(row) * p.ldy + n + 1] = b;
+              } else {
+                const bool is_k = n < p.q_rows + p.kv_rows;
+                const int rel = is_k ? n - p.q_rows : n - p.q_rows - p.kv_rows;
+                const size_t off = kv_off(p.page_table, pos, rel / p.d, p.nkv, p.d) + rel % p.d;
+                float* cache = is_k ? p.k_cache : p.v_cache;
+                cache[off] = a;
+                cache[off + 1] = b;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+constexpr size_t kGemmSmem = kGemmStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& w,
+                           const GemmParams& p, cudaStream_t s) {
+  const int cols = p.epi == GE_SILU ? kGemmBN / 2 : kGemmBN;
+  const dim3 grid((p.N + cols - 1) / cols, (p.M + kGemmBM - 1) / kGemmBM);
+  switch (p.epi) {
+    case GE_QKV: gemm_tc_kernel<GE_QKV><<<grid, kGemmThreads, kGemmSmem, s>>>(a_hi, a_lo, w, p); break;
+    case GE_RESID: gemm_tc_kernel<GE_RESID><<<grid, kGemmThreads, kGemmSmem, s>>>(a_hi, a_lo, w, p); break;
+    default: gemm_tc_kernel<GE_SILU><<<grid, kGemmThreads, kGemmSmem, s>>>(a_hi, a_lo, w, p); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t configure_gemm_tc(int max_smem_optin) {
+  if (static_cast<int>(kGemmSmem) > max_smem_optin) return cudaErrorInvalidValue;
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(gemm_tc_kernel<GE_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem)))
+    return e;
+  if ((e = cudaFuncSetAttribute(gemm_tc_kernel<GE_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem)))
+    return e;
+  return cudaFuncSetAttribute(gemm_tc_kernel<GE_SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+}
+
+// ---------------------------------------------------------------- tensor maps
+cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode),
+                                            cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !encode) return cudaErrorNotSupported;
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------- SIMT helpers
+__global__ void prefill_embed_kernel(const uint16_t* table, const int* tokens, int M, int h, float* x) {
+  const size_t total = static_cast<size_t>(M) * h;
+  for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(e / h), i = static_cast<int>(e % h);
+    x[e] = bf16_to_f32(table[static_cast<size_t>(tokens[m]) * h + i]);
+  }
+}
+
+cudaError_t launch_prefill_embed(const uint16_t* table, const int* tokens, int M, int h, float* x, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(M) * h;
+  const unsigned blocks = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, 148 * 16));
+  prefill_embed_kernel<<<blocks, 256, 0, s>>>(table, tokens, M, h, x);
+  return cudaGetLastError();
+}
+
+// rmsNormInto (src/llm.zig:1287-1300) of every row, written as bf16 hi + lo.
+__global__ void norm_split_kernel(const float* x, const uint16_t* w, float eps, int h, uint16_t* hi, uint16_t* lo) {
+  __shared__ float red[32];
+  const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* xr = x + static_cast<size_t>(m) * h;
+  float ss = 0.f;
+  for (int i = tid; i < h; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < static_cast<int>(blockDim.x / 32); ++i) t += red[i];
+  const float scale = 1.0f / sqrtf(t / static_cast<float>(h) + eps);
+  for (int i = tid; i < h; i += blockDim.x) {
+    const float v = xr[i] * bf16_to_f32(w[i]) * scale;
+    split_bf16(v, hi[static_cast<size_t>(m) * h + i], lo[static_cast<size_t>(m) * h + i]);
+  }
+}
+
+cudaError_t launch_norm_split(const float* x, const uint16_t* w, float eps, int M, int h, uint16_t* hi, uint16_t* lo,
+                              cudaStream_t s) {
+  norm_split_kernel<<<M, 256, 0, s>>>(x, w, eps, h, hi, lo);
+  return cudaGetLastError();
+}
+
+// Causal attention of a prompt chunk (computeAttentionInto per token,
+// src/llm.zig:1302-1335): CTA = (kv head g, block of QB tokens), rows = the
+// group's q heads x tokens; 32-position K/V tiles staged in shared memory
+// (K rows padded by one float against bank conflicts); one warp per row at a
+// time with an online softmax; output as bf16 hi/lo for the o_proj GEMM.
+constexpr int kPaTile = 32;
+constexpr int kPaThreads = 256;
+constexpr int kPaAcc = 32;  // fp32 accumulators per lane: rows_per_warp * dims_per_lane
+
+template <int DPL>  // dims per lane = ceil(head_dim / 32)
+__global__ void __launch_bounds__(kPaThreads) prefill_attention_kernel(const PrefillAttnParams p) {
+  extern __shared__ float pa[];
+  const int d = p.d, G = p.group, g = blockIdx.x;
+  constexpr int dpl = DPL;
+  constexpr int rpw = kPaAcc / DPL;  // rows per warp
+  const int QB = max(1, (rpw * (kPaThreads / 32)) / G);  // tokens per CTA
+  const int t0 = blockIdx.y * QB;
+  const int nt = min(QB, p.M - t0);
+  const int rows = G * nt;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* qs = pa;                                  // [rows][d]
+  float* ks = qs + static_cast<size_t>(G) * QB * d;  // [kPaTile][d + 1]
+  float* vs = ks + kPaTile * (d + 1);              // [kPaTile][d]
+  for (int idx = threadIdx.x; idx < rows * d; idx += kPaThreads) {
+    const int r = idx / d, e = idx % d;
+    const int hh = r % G, t = r / G;
+    qs[idx] = p.q[static_cast<size_t>(t0 + t) * p.nq * d + static_cast<size_t>(g * G + hh) * d + e];
+  }
+  float acc[kPaAcc], mrun[rpw], lrun[rpw];
+#pragma unroll
+  for (int i = 0; i < kPaAcc; ++i) acc[i] = 0.f;
+#pragma unroll
+  for (int i = 0; i < rpw; ++i) {
+    mrun[i] = -INFINITY;
+    lrun[i] = 0.f;
+  }
+  const int last_pos = p.pos0 + t0 + nt - 1;
+  for (int base = 0; base <= last_pos; base += kPaTile) {
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < kPaTile * d; idx += kPaThreads) {
+      const int i = idx / d, e = idx % d;
+      const int pos = base + i;
+      float kv = 0.f, vv = 0.f;
+      if (pos <= last_pos) {
+        const size_t off = kv_off(p.page_table, pos, g, p.nkv, d) + e;
+        kv = p.k_cache[off];
+        vv = p.v_cache[off];
+      }
+      ks[i * (d + 1) + e] = kv;
+      vs[i * d + e] = vv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int rr = 0; rr < rpw; ++rr) {
+      const int r = warp * rpw + rr;
+      if (r >= rows) continue;
+      const int pos_r = p.pos0 + t0 + r / G;  // this row's token position (causal limit)
+      const float* qr = qs + static_cast<size_t>(r) * d;
+      float sc = -INFINITY;
+      if (base + lane <= pos_r) {
+        float dot = 0.f;
+        for (int e = 0; e < d; ++e) dot = fmaf(qr[e], ks[lane * (d + 1) + e], dot);
+        sc = dot * p.inv_sqrt_d;
+      }
+      const float mt = warp_max(sc);
+      const float mnew = fmaxf(mrun[rr], mt);
+      const float pr = sc == -INFINITY ? 0.f : expf(sc - mnew);
+      const float alpha = mrun[rr] == -INFINITY ? 0.f : expf(mrun[rr] - mnew);
+      lrun[rr] = lrun[rr] * alpha + warp_sum(pr);
+      mrun[rr] = mnew;
+#pragma unroll
+      for (int j = 0; j < dpl; ++j) {
+        const int e = lane + 32 * j;
+        float a = acc[rr * dpl + j] * alpha;
+        for (int i = 0; i < kPaTile; ++i) {
+          const float pi = __shfl_sync(0xffffffffu, pr, i);
+          if (e < d) a = fmaf(pi, vs[i * d + e], a);
+        }
+        acc[rr * dpl + j] = a;
+      }
+    }
+  }
+#pragma unroll
+  for (int rr = 0; rr < rpw; ++rr) {
+    const int r = warp * rpw + rr;
+    if (r >= rows) continue;
+    const int hh = r % G, t = r / G;
+    const size_t orow = static_cast<size_t>(t0 + t) * p.nq * d + static_cast<size_t>(g * G + hh) * d;
+#pragma unroll
+    for (int j = 0; j < dpl; ++j) {
+      const int e = lane + 32 * j;
+      if (e < d) split_bf16(acc[rr * dpl + j] / lrun[rr], p.out_hi[orow + e], p.out_lo[orow + e]);
+    }
+  }
+}
+
+template <int DPL>
+static cudaError_t launch_pa(const PrefillAttnParams& p, cudaStream_t s) {
+  constexpr int rpw = kPaAcc / DPL;
+  const int QB = std::max(1, (rpw * (kPaThreads / 32)) / p.group);
+  const dim3 grid(p.nkv, (p.M + QB - 1) / QB);
+  const size_t smem = (static_cast<size_t>(p.group) * QB * p.d + kPaTile * (p.d + 1) + kPaTile * p.d) * 4;
+  cudaError_t e = cudaFuncSetAttribute(prefill_attention_kernel<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e) return e;
+  prefill_attention_kernel<DPL><<<grid, kPaThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_attention(const PrefillAttnParams& p, cudaStream_t s) {
+  const int dpl = (p.d + 31) / 32;
+  if (dpl <= 1) return launch_pa<1>(p, s);
+  if (dpl <= 2) return launch_pa<2>(p, s);
+  if (dpl <= 4) return launch_pa<4>(p, s);
+  return launch_pa<8>(p, s);
+}
+
+// ---------------------------------------------------------------- self-test
+__global__ void fill_bf16_kernel(uint16_t* p, size_t n, uint64_t key, float scale) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint64_t h = mix64(key + (i + 1) * 0x9E3779B97F4A7C15ull);
+    const float u = static_cast<float>(static_cast<int>(h & 0xffff) - 32768) * (1.0f / 32768.0f);
+    p[i] = f32_to_bf16(u * scale);
+  }
+}
+
+__global__ void gemm_ref_kernel(const uint16_t* ahi, const uint16_t* alo, const uint16_t* w, int M, int N, int K,
+                                int two_a, float* c) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+  if (n >= N) return;
+  double acc = 0.0;
+  for (int k = 0; k < K; ++k) {
+    double a = bf16_to_f32(ahi[static_cast<size_t>(m) * K + k]);
+    if (two_a) a += bf16_to_f32(alo[static_cast<size_t>(m) * K + k]);
+    acc += a * bf16_to_f32(w[static_cast<size_t>(n) * K + k]);
+  }
+  c[static_cast<size_t>(m) * N + n] = static_cast<float>(acc);
+}
+
+__global__ void max_rel_err_kernel(const float* a, const float* b, size_t n, float* out) {
+  float worst = 0.f, scale = 0.f;
+  for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
+    worst = fmaxf(worst, fabsf(a[i] - b[i]));
+    scale = fmaxf(scale, fabsf(b[i]));
+  }
+  worst = warp_max(worst);
+  scale = warp_max(scale);
+  __shared__ float w_sh[32], s_sh[32];
+  if ((threadIdx.x & 31) == 0) {
+    w_sh[threadIdx.x >> 5] = worst;
+    s_sh[threadIdx.x >> 5] = scale;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (unsigned i = 1; i < blockDim.x / 32; ++i) {
+      worst = fmaxf(worst, w_sh[i]);
+      scale = fmaxf(scale, s_sh[i]);
+    }
+    *out = worst / fmaxf(scale, 1e-30f);
+  }
+}
+
+// Runs C = A . W^T through the tensor-core GEMM and a SIMT fp64-accumulating
+// reference on random data; *max_rel_err = max |C - ref| / max |ref|.
+cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err) {
+  cudaError_t e;
+  int dev = 0, optin = 0;
+  if ((e = cudaGetDevice(&dev))) return e;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if ((e = configure_gemm_tc(optin))) return e;
+  uint16_t *ahi = nullptr, *alo = nullptr, *w = nullptr;
+  float *c = nullptr, *ref = nullptr, *err_out = nullptr;
+  int* err = nullptr;
+  auto cleanup = [&]() {
+    cudaFree(ahi), cudaFree(alo), cudaFree(w), cudaFree(c), cudaFree(ref), cudaFree(err_out), cudaFree(err);
+  };
+  if ((e = cudaMalloc(&ahi, static_cast<size_t>(M) * K * 2)) || (e = cudaMalloc(&alo, static_cast<size_t>(M) * K * 2)) ||
+      (e = cudaMalloc(&w, static_cast<size_t>(N) * K * 2)) || (e = cudaMalloc(&c, static_cast<size_t>(M) * N * 4)) ||
+      (e = cudaMalloc(&ref, static_cast<size_t>(M) * N * 4)) || (e = cudaMalloc(&err_out, 4)) ||
+      (e = cudaMalloc(&err, 4))) {
+    cleanup();
+    return e;
+  }
+  cudaMemset(err, 0, 4);
+  fill_bf16_kernel<<<256, 256>>>(ahi, static_cast<size_t>(M) * K, seed * 3 + 1, 1.0f);
+  fill_bf16_kernel<<<256, 256>>>(alo, static_cast<size_t>(M) * K, seed * 3 + 2, 1.0f / 256);
+  fill_bf16_kernel<<<256, 256>>>(w, static_cast<size_t>(N) * K, seed * 3 + 3, 0.05f);
+  CUtensorMap mhi, mlo, mw;
+  if ((e = make_tmap_bf16(&mhi, ahi, M, K, kGemmBM)) || (e = make_tmap_bf16(&mlo, alo, M, K, kGemmBM)) ||
+      (e = make_tmap_bf16(&mw, w, N, K, kGemmBN / 2))) {
+    cleanup();
+    return e;
+  }
+  GemmParams p{};
+  p.M = M, p.N = N, p.K = K, p.nk = (K + kGemmBK - 1) / kGemmBK, p.two_a = two_a, p.epi = GE_RESID;
+  p.y = c, p.ldy = N, p.add_residual = 0, p.err = err;
+  if ((e = launch_gemm_tc(mhi, mlo, mw, p, 0))) {
+    cleanup();
+    return e;
+  }
+  gemm_ref_kernel<<<dim3((N + 127) / 128, M), 128>>>(ahi, alo, w, M, N, K, two_a, ref);
+  max_rel_err_kernel<<<1, 1024>>>(c, ref, static_cast<size_t>(M) * N, err_out);
+  int herr = 0;
+  if ((e = cudaMemcpy(max_rel_err, err_out, 4, cudaMemcpyDeviceToHost)) ||
+      (e = cudaMemcpy(&herr, err, 4, cudaMemcpyDeviceToHost))) {
+    cleanup();
+    return e;
+  }
+  cleanup();
+  return herr ? cudaErrorTimeout : cudaSuccess;
+}
+
+}  // namespace vvli

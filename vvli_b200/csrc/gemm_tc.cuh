@@ -1,0 +1,67 @@
+// gemm_tc.cuh - tcgen05 (5th-generation tensor core) GEMM for prefill.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+
+namespace vvli {
+
+enum GemmEpi { GE_QKV = 0, GE_RESID = 1, GE_SILU = 2 };
+
+constexpr int kGemmBM = 128;  // tokens per tile (TMEM lanes)
+constexpr int kGemmBN = 256;  // output columns per tile (TMEM columns)
+constexpr int kGemmBK = 64;   // bf16 elements per k-block (one 128-byte swizzled row)
+
+struct GemmParams {
+  int M, N, K;           // C[M, N] = A[M, K] . W[N, K]^T; N = columns produced (pair: per matrix)
+  int pair_offset;       // GE_SILU: row offset of the `up` rows in W (gate rows first)
+  int nk;                // k-blocks = ceil(K / 64)
+  int two_a;             // 1: A = A_hi + A_lo (two MMAs per k-step, near-fp32 activations)
+  int epi;               // GemmEpi
+  // GE_QKV: q -> y [M, q_rows] fp32 (rotated); k, v -> KV cache at positions pos0 + m
+  float* y;
+  int ldy;
+  const uint16_t* bias;
+  int q_rows, kv_rows, d, nkv, pos0;
+  RopeParams rope;
+  float* k_cache;
+  float* v_cache;
+  const int* page_table;
+  // GE_RESID: x[m, n] = (add_residual ? x[m, n] : 0) + acc (x = y, ld = ldy)
+  int add_residual;
+  // GE_SILU: ff = silu(g) * u written as bf16 hi / lo [M, ld_out]
+  uint16_t* out_hi;
+  uint16_t* out_lo;
+  int ld_out;
+  int* err;              // VVLI_ERR_TIMEOUT on a bounded wait giving up
+};
+
+// Encodes a 2-D bf16 tensor map [rows, cols] (cols contiguous) with a
+// {64, box_rows} box and 128-byte swizzle, the layout the UMMA descriptors use.
+cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
+cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& w,
+                           const GemmParams& p, cudaStream_t s);
+cudaError_t configure_gemm_tc(int max_smem_optin);
+cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err);
+
+// Prefill helpers (SIMT): embedding gather, RMSNorm into bf16 hi/lo, causal attention.
+cudaError_t launch_prefill_embed(const uint16_t* table, const int* tokens, int M, int h, float* x, cudaStream_t s);
+cudaError_t launch_norm_split(const float* x, const uint16_t* w, float eps, int M, int h, uint16_t* hi, uint16_t* lo,
+                              cudaStream_t s);
+struct PrefillAttnParams {
+  const float* q;        // [M, nq*d] rotated
+  const float* k_cache;  // this layer
+  const float* v_cache;
+  const int* page_table;
+  uint16_t* out_hi;      // [M, nq*d] bf16 hi / lo
+  uint16_t* out_lo;
+  int M, nq, nkv, d, group, pos0;
+  float inv_sqrt_d;
+};
+cudaError_t launch_prefill_attention(const PrefillAttnParams& p, cudaStream_t s);
+
+}  // namespace vvli

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/vvli_cuda.h"
+#include "gemm_tc.cuh"
 #include "kernels.h"
 
 using namespace vvli;
@@ -184,6 +185,14 @@ struct vvli_ctx {
   unsigned* epoch = nullptr;
   int mega_splits = 1;
   uint64_t* trace = nullptr;  // VVLI_TRACE=1: megakernel timeline
+  // tensor-core prefill
+  bool tc_prefill = false;
+  int pf_cap = 0;
+  float *pf_x = nullptr, *pf_q = nullptr;
+  uint16_t *pf_ahi = nullptr, *pf_alo = nullptr, *pf_fhi = nullptr, *pf_flo = nullptr;
+  int* pf_tokens = nullptr;
+  CUtensorMap tm_ah_hi{}, tm_ah_lo{}, tm_aq_hi{}, tm_aq_lo{}, tm_f_hi{}, tm_f_lo{};
+  std::vector<CUtensorMap> tm_w;  // per layer: q|k|v, o, gate|up, down
 };
 
 namespace {
@@ -438,6 +447,36 @@ int enqueue_mega(vvli_ctx* c, cudaStream_t s, bool debug) {
   return VVLI_OK;
 }
 
+// Final RMSNorm + LM head + argmax of c->x (src/llm.zig:727-728, 778-789);
+// under tensor parallelism the vocab shards' winners are gathered.
+int enqueue_lm_head(vvli_ctx* c, cudaStream_t s, bool pdl) {
+  const bool tp = c->tp_size > 1;
+  const uint16_t* W = c->w;
+  GemvParams lm{};
+  lm.W = W + c->off_lm;
+  lm.N = c->V_lr;
+  lm.K = c->h;
+  lm.x = c->x;
+  lm.norm_w = W + c->off_final;
+  lm.eps = c->cfg.rms_norm_eps;
+  lm.y = c->logits;
+  lm.part_val = c->amax_val;
+  lm.part_idx = c->amax_idx;
+  lm.counter = c->counters + c->nkv_l;
+  lm.row_base = c->v0;
+  lm.finalize = tp ? 0 : 1;
+  lm.local_best = c->best;
+  lm.st = c->st;
+  lm.seq_tokens = c->seq_tokens;
+  CK(launch_gemv(EPI_ARGMAX, lm, c->sm_count, s, pdl && !tp));
+  if (tp) {
+    int st = nccl_wait(c, nccl().AllGather(c->best, c->all_best, 2, ncclFloat32, c->comm, s), "allgather");
+    if (st) return st;
+    CK(launch_tp_argmax_finalize(c->all_best, c->tp_size, c->st, c->seq_tokens, s));
+  }
+  return VVLI_OK;
+}
+
 int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
   if (c->use_mega) return enqueue_mega(c, s, debug);
   const bool pdl = c->use_pdl && !debug;
@@ -535,29 +574,117 @@ int enqueue_step(vvli_ctx* c, cudaStream_t s, bool debug) {
     }
     if (debug) CK(cudaMemcpyAsync(c->hidden + static_cast<size_t>(l) * c->h, c->x, c->h * 4, cudaMemcpyDeviceToDevice, s));
   }
-  GemvParams lm{};
-  lm.W = W + c->off_lm;
-  lm.N = c->V_lr;
-  lm.K = c->h;
-  lm.x = c->x;
-  lm.norm_w = W + c->off_final;
-  lm.eps = c->cfg.rms_norm_eps;
-  lm.y = c->logits;
-  lm.part_val = c->amax_val;
-  lm.part_idx = c->amax_idx;
-  lm.counter = c->counters + c->nkv_l;
-  lm.row_base = c->v0;
-  lm.finalize = tp ? 0 : 1;
-  lm.local_best = c->best;
-  lm.st = c->st;
-  lm.seq_tokens = c->seq_tokens;
-  CK(launch_gemv(EPI_ARGMAX, lm, c->sm_count, s, pdl && !tp));
-  if (tp) {
-    int st = nccl_wait(c, nccl().AllGather(c->best, c->all_best, 2, ncclFloat32, c->comm, s), "allgather");
-    if (st) return st;
-    CK(launch_tp_argmax_finalize(c->all_best, c->tp_size, c->st, c->seq_tokens, s));
+  return enqueue_lm_head(c, s, pdl);
+}
+
+template <typename T>
+int dalloc(T** p, size_t count) {
+  CK(cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(T)));
+  CK(cudaMemset(*p, 0, std::max<size_t>(count, 1) * sizeof(T)));
+  return VVLI_OK;
+}
+
+// ---------------------------------------------------------------- tensor-core prefill
+// Tensor maps of every weight matrix for the tcgen05 GEMM (K-major rows,
+// 64 x 128 boxes, 128-byte swizzle).
+int plan_tc_prefill(vvli_ctx* c) {
+  c->tm_w.resize(4 * c->L);
+  for (int l = 0; l < c->L; ++l) {
+    const DevLayer& D = c->lay[l];
+    cudaError_t e;
+    if ((e = make_tmap_bf16(&c->tm_w[4 * l + 0], c->w + D.w_qkv, c->q_rows + 2 * c->kv_rows, c->h, 128)) ||
+        (e = make_tmap_bf16(&c->tm_w[4 * l + 1], c->w + D.w_o, c->h, c->q_rows, 128)) ||
+        (e = make_tmap_bf16(&c->tm_w[4 * l + 2], c->w + D.w_gu, 2 * c->I_l, c->h, 128)) ||
+        (e = make_tmap_bf16(&c->tm_w[4 * l + 3], c->w + D.w_down, c->h, c->I_l, 128)))
+      return cuda_fail(e, "make_tmap_bf16 (weights)");
   }
   return VVLI_OK;
+}
+
+// Activation buffers of a prompt chunk of up to pf_cap tokens (allocated on
+// the first tensor-core prefill).
+int ensure_prefill_buffers(vvli_ctx* c) {
+  if (c->pf_cap) return VVLI_OK;
+  const int cap = static_cast<int>(std::min<uint64_t>(c->max_seq, 2048));
+  const size_t ka = std::max(c->h, c->q_rows);
+  int st;
+  if ((st = dalloc(&c->pf_x, static_cast<size_t>(cap) * c->h)) || (st = dalloc(&c->pf_q, static_cast<size_t>(cap) * c->q_rows)) ||
+      (st = dalloc(&c->pf_ahi, cap * ka)) || (st = dalloc(&c->pf_alo, cap * ka)) ||
+      (st = dalloc(&c->pf_fhi, static_cast<size_t>(cap) * c->I_l)) ||
+      (st = dalloc(&c->pf_flo, static_cast<size_t>(cap) * c->I_l)) || (st = dalloc(&c->pf_tokens, cap)))
+    return st;
+  cudaError_t e;
+  if ((e = make_tmap_bf16(&c->tm_ah_hi, c->pf_ahi, cap, c->h, 128)) ||
+      (e = make_tmap_bf16(&c->tm_ah_lo, c->pf_alo, cap, c->h, 128)) ||
+      (e = make_tmap_bf16(&c->tm_aq_hi, c->pf_ahi, cap, c->q_rows, 128)) ||
+      (e = make_tmap_bf16(&c->tm_aq_lo, c->pf_alo, cap, c->q_rows, 128)) ||
+      (e = make_tmap_bf16(&c->tm_f_hi, c->pf_fhi, cap, c->I_l, 128)) ||
+      (e = make_tmap_bf16(&c->tm_f_lo, c->pf_flo, cap, c->I_l, 128)))
+    return cuda_fail(e, "make_tmap_bf16 (activations)");
+  c->pf_cap = cap;
+  return VVLI_OK;
+}
+
+// Runs tokens[0, n) at positions start.. with one tensor-core GEMM per linear
+// layer and chunk (prefill of the reference's per-token loop,
+// src/generator.zig:243-251), then the LM head of the last token.
+int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start) {
+  int st;
+  if ((st = ensure_prefill_buffers(c))) return st;
+  cudaStream_t s = c->stream;
+  const uint16_t* W = c->w;
+  const bool tp = c->tp_size > 1;
+  RopeParams rope{c->cfg.rope_theta, VVLI_ROPE_INTERLEAVED, static_cast<int>(c->cfg.rope_scaling_type),
+                  c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
+                  static_cast<float>(c->cfg.rope_original_max_position)};
+  int* err = &c->st->err;
+  int M = 0;
+  for (uint64_t c0 = 0; c0 < n; c0 += c->pf_cap) {
+    M = static_cast<int>(std::min<uint64_t>(c->pf_cap, n - c0));
+    const int pos0 = static_cast<int>(start + c0);
+    CK(cudaMemcpyAsync(c->pf_tokens, tokens + c0, M * sizeof(int), cudaMemcpyHostToDevice, s));
+    CK(launch_prefill_embed(W + c->off_emb, c->pf_tokens, M, c->h, c->pf_x, s));
+    for (int l = 0; l < c->L; ++l) {
+      const DevLayer& D = c->lay[l];
+      float* kc = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
+      float* vc = kc + c->kv_layer_floats;
+      CK(launch_norm_split(c->pf_x, W + D.in_norm, c->cfg.rms_norm_eps, M, c->h, c->pf_ahi, c->pf_alo, s));
+      GemmParams g{};
+      g.M = M, g.two_a = 1, g.err = err;
+      g.N = c->q_rows + 2 * c->kv_rows, g.K = c->h, g.epi = GE_QKV, g.y = c->pf_q, g.ldy = c->q_rows;
+      g.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv;
+      g.q_rows = c->q_rows, g.kv_rows = c->kv_rows, g.d = c->d, g.nkv = c->nkv_l, g.pos0 = pos0, g.rope = rope;
+      g.k_cache = kc, g.v_cache = vc, g.page_table = c->page_table;
+      g.nk = (g.K + kGemmBK - 1) / kGemmBK;
+      CK(launch_gemm_tc(c->tm_ah_hi, c->tm_ah_lo, c->tm_w[4 * l + 0], g, s));
+      PrefillAttnParams a{c->pf_q, kc, vc, c->page_table, c->pf_ahi, c->pf_alo, M, c->nq_l, c->nkv_l, c->d,
+                          c->group, pos0, 1.0f / sqrtf(static_cast<float>(c->d))};
+      CK(launch_prefill_attention(a, s));
+      GemmParams o{};
+      o.M = M, o.two_a = 1, o.err = err, o.N = c->h, o.K = c->q_rows, o.epi = GE_RESID, o.y = c->pf_x, o.ldy = c->h;
+      o.add_residual = c->tp_rank == 0 ? 1 : 0, o.nk = (o.K + kGemmBK - 1) / kGemmBK;
+      CK(launch_gemm_tc(c->tm_aq_hi, c->tm_aq_lo, c->tm_w[4 * l + 1], o, s));
+      if (tp && (st = nccl_wait(c, nccl().AllReduce(c->pf_x, c->pf_x, static_cast<size_t>(M) * c->h, ncclFloat32,
+                                                     ncclSum, c->comm, s), "allreduce")))
+        return st;
+      CK(launch_norm_split(c->pf_x, W + D.post, c->cfg.rms_norm_eps, M, c->h, c->pf_ahi, c->pf_alo, s));
+      GemmParams gu{};
+      gu.M = M, gu.two_a = 1, gu.err = err, gu.N = c->I_l, gu.K = c->h, gu.epi = GE_SILU, gu.pair_offset = c->I_l;
+      gu.out_hi = c->pf_fhi, gu.out_lo = c->pf_flo, gu.ld_out = c->I_l, gu.nk = (gu.K + kGemmBK - 1) / kGemmBK;
+      CK(launch_gemm_tc(c->tm_ah_hi, c->tm_ah_lo, c->tm_w[4 * l + 2], gu, s));
+      GemmParams dn{};
+      dn.M = M, dn.two_a = 1, dn.err = err, dn.N = c->h, dn.K = c->I_l, dn.epi = GE_RESID, dn.y = c->pf_x;
+      dn.ldy = c->h, dn.add_residual = c->tp_rank == 0 ? 1 : 0, dn.nk = (dn.K + kGemmBK - 1) / kGemmBK;
+      CK(launch_gemm_tc(c->tm_f_hi, c->tm_f_lo, c->tm_w[4 * l + 3], dn, s));
+      if (tp && (st = nccl_wait(c, nccl().AllReduce(c->pf_x, c->pf_x, static_cast<size_t>(M) * c->h, ncclFloat32,
+                                                     ncclSum, c->comm, s), "allreduce")))
+        return st;
+    }
+  }
+  // The last token's hidden state goes through the final norm and LM head.
+  CK(cudaMemcpyAsync(c->x, c->pf_x + static_cast<size_t>(M - 1) * c->h, c->h * sizeof(float),
+                     cudaMemcpyDeviceToDevice, s));
+  return enqueue_lm_head(c, s, false);
 }
 
 int build_graph(vvli_ctx* c) {
@@ -652,7 +779,8 @@ void free_ctx(vvli_ctx* c) {
   if (c->comm) nccl().CommDestroy(c->comm);
   void* dev[] = {c->w, c->kv, c->page_table, c->x, c->qkv, c->attn, c->ff, c->logits, c->logits_full, c->emb_in,
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
-                 c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace};
+                 c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->pf_x, c->pf_q,
+                 c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (c->h_st) cudaFreeHost(c->h_st);
@@ -663,12 +791,6 @@ void free_ctx(vvli_ctx* c) {
   delete c;
 }
 
-template <typename T>
-int dalloc(T** p, size_t count) {
-  CK(cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(T)));
-  CK(cudaMemset(*p, 0, std::max<size_t>(count, 1) * sizeof(T)));
-  return VVLI_OK;
-}
 
 }  // namespace
 
@@ -835,6 +957,12 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
     ncclResult_t r = n.CommInitRankConfig(&c->comm, tp_size, uid, tp_rank, &ncfg);
     if ((st = nccl_wait(c, r, "ncclCommInitRankConfig"))) return fail(st);
   }
+  {
+    const char* tc_env = getenv("VVLI_TC_PREFILL");
+    if (!(tc_env && tc_env[0] == '0') && configure_gemm_tc(smem_optin) == cudaSuccess && plan_tc_prefill(c) == VVLI_OK)
+      c->tc_prefill = true;
+    cudaGetLastError();
+  }
   const char* mega_env = getenv("VVLI_MEGAKERNEL");
   const bool want_mega = !(mega_env && mega_env[0] == '0') && tp_size == 1;
   if (want_mega) {
@@ -946,9 +1074,16 @@ int vvli_cuda_prefill(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t 
   CK(cudaSetDevice(c->device));
   CK(cudaMemcpyAsync(c->seq_tokens + start, tokens, n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
   int st;
-  if ((st = stage_state(c, static_cast<int>(start), static_cast<int>(start + n), 0))) return st;
+  const bool tc = c->tc_prefill && !c->debug && n >= 2;
+  // The tensor-core path ends in the LM head of the last token, which
+  // publishes its argmax and advances the state from position start + n - 1.
+  if ((st = stage_state(c, static_cast<int>(tc ? start + n - 1 : start), static_cast<int>(start + n), 0))) return st;
   CK(cudaEventRecord(c->ev0, c->stream));
-  if ((st = run_steps(c, static_cast<int>(n)))) return st;
+  if (tc) {
+    if ((st = prefill_tc(c, tokens, n, start))) return st;
+  } else if ((st = run_steps(c, static_cast<int>(n)))) {
+    return st;
+  }
   CK(cudaEventRecord(c->ev1, c->stream));
   if ((st = copy_logits(c, last_logits))) return st;
   if ((st = finish_state(c))) return st;
@@ -1111,6 +1246,7 @@ int vvli_cuda_query(vvli_ctx* c, const char* key, double* out) {
   else if (k == "kernels_per_step")
     *out = c->use_mega ? 1 : 1 + 5.0 * c->L + 1 + (c->tp_size > 1 ? 1 : 0);
   else if (k == "weight_bytes") *out = static_cast<double>(c->weight_elems) * 2;
+  else if (k == "tc_prefill") *out = c->tc_prefill ? 1 : 0;
   else return VVLI_ERR_INVALID_ARGUMENT;
   return VVLI_OK;
 }
@@ -1122,6 +1258,18 @@ int vvli_cuda_trace(vvli_ctx* c, uint64_t* out, uint64_t cap, uint64_t* count) {
     CK(cudaSetDevice(c->device));
     CK(cudaMemcpy(out, c->trace, *count * sizeof(uint64_t), cudaMemcpyDeviceToHost));
   }
+  return VVLI_OK;
+}
+
+int vvli_cuda_gemm_selftest(int device, int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err) {
+  if (!max_rel_err || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 2) return VVLI_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(device));
+  cudaError_t e = gemm_tc_selftest(M, N, K, two_a, seed, max_rel_err);
+  if (e == cudaErrorTimeout) {
+    g_last_error = "tensor-core GEMM: a bounded wait gave up";
+    return VVLI_ERR_TIMEOUT;
+  }
+  CK(e);
   return VVLI_OK;
 }
 
