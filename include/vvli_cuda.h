@@ -259,6 +259,40 @@ int vvli_cuda_trace(vvli_ctx* ctx, uint64_t* out, uint64_t cap, uint64_t* count)
  * `max_rel_err` = max |C - ref| / max |ref|. */
 int vvli_cuda_gemm_selftest(int device, int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err);
 
+/* Greedy token choice over `rows` rows of `n` fp32 logits that are already in
+ * device memory (row r at logits + r * n), writing the index of each row's
+ * maximum to tokens[r] (device memory).  It has no counterpart in the
+ * reference; it returns what llm.argmax (src/llm.zig:778-789) returns for each
+ * row: the first maximal index, NaNs never chosen except that a NaN in
+ * element 0 gives 0.
+ *
+ * The library allocates nothing for this call and needs no context: it is for
+ * callers that own the whole device's memory (a serving engine whose pool has
+ * already claimed HBM for its KV cache, where a library cudaMalloc would fail
+ * or eat into the pool) or that cannot afford cudaFree's device-wide
+ * synchronisation.  Its scratch is one static device array of 33,024 bytes
+ * per device, so the limits are rows <= 64 and rows * ceil(n / 4096) <= 4096
+ * (n <= 16,777,216 for one row); larger requests, null or misaligned pointers,
+ * and pointers that are not device memory of `device` (or managed memory)
+ * covering the whole range return VVLI_ERR_INVALID_ARGUMENT with the reason in
+ * vvli_cuda_last_error().
+ *
+ * The work is queued on `stream` (a cudaStream_t; NULL = the legacy default
+ * stream) and tokens[] is valid once that stream has been synchronised.  The
+ * caller's current device is restored before returning.
+ *
+ * The first call on each device does one-time setup (the scratch address is
+ * looked up, which may load this library's device code); make that first
+ * call before any stream capture begins.  The scratch's per-row arrival
+ * counters must be zero when a call starts: they are zero when the device
+ * code loads and every completed call leaves them zero.  Calls that overlap
+ * on one device (two streams, or two host threads, without ordering between
+ * them) share the scratch and race: results are then wrong and the counters
+ * may stay non-zero for later calls.  Order calls on one device, e.g. issue
+ * them all on one stream. */
+int vvli_cuda_argmax_rows_static(int device, const float* logits, uint64_t rows, uint64_t n, int32_t* tokens,
+                                 void* stream);
+
 /* Device-side timing of the last forward in milliseconds (CUDA events). */
 int vvli_cuda_last_forward_ms(vvli_ctx* ctx, float* out_ms);
 

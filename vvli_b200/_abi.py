@@ -68,6 +68,8 @@ SIGNATURES = {
     "vvli_cuda_trace": (ctypes.c_int, [_ctx, _u64p, ctypes.c_uint64, _u64p]),
     "vvli_cuda_gemm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                ctypes.c_uint64, _f32p]),
+    "vvli_cuda_argmax_rows_static": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
+                                                    ctypes.c_void_p, ctypes.c_void_p]),
     "vvli_cuda_set_debug": (ctypes.c_int, [_ctx, ctypes.c_int]),
     "vvli_cuda_debug_hidden": (ctypes.c_int, [_ctx, ctypes.c_int, _f32p]),
     "vvli_cuda_last_forward_ms": (ctypes.c_int, [_ctx, _f32p]),

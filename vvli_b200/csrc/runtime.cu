@@ -31,6 +31,15 @@ namespace {
 
 thread_local std::string g_last_error;
 
+}  // namespace
+
+namespace vvli {
+// Lets other translation units of the library report through vvli_cuda_last_error.
+void set_last_error(const std::string& what) { g_last_error = what; }
+}  // namespace vvli
+
+namespace {
+
 // ---------------------------------------------------------------- NCCL (loaded at run time)
 struct NcclApi {
   bool ok = false;
