@@ -323,6 +323,20 @@ def main():
                "note": "activations enter the tensor cores as bf16 hi+lo pairs (2 MMAs per product) for fp32-level "
                        "parity; attention on CUDA cores"}
     launches_per_step = int(runner.query("kernels_per_step"))
+    # Sampler.next on the device (generator.Options defaults: T 0.8, top-p 0.95, top-k 40, rp 1.1 over 64)
+    # over the last forward's logits, host call to token (includes the synchronising copies).
+    from vvli_b200 import sampler as _smp
+    sopt = vvli_b200.Options()
+    sstate = np.array(_smp.Xoshiro256(1).s, dtype=np.uint64)
+    recent = list(range(1, 65))
+    runner.sample(sopt, recent, sstate)
+    t_s = []
+    for _ in range(50):
+        t0 = time.perf_counter()
+        runner.sample(sopt, recent, sstate)
+        t_s.append(time.perf_counter() - t0)
+    sampler_line = {"us_per_token_median": round(float(np.median(t_s)) * 1e6, 1), "options": "T 0.8, top_p 0.95, "
+                    "top_k 40, repeat_penalty 1.1 over 64", "vocab": cfg.vocab_size}
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
         v, cores, sample = time_oracle(cfg, args.seed, args.cpu_seconds)
@@ -333,7 +347,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, cfg, n),
                 "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "prefill": prefill,
+                "prefill": prefill, "sampler": sampler_line,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clk}
         print(json.dumps(line), flush=True)
     runner.close()

@@ -224,6 +224,22 @@ int vvli_cuda_generate_greedy(vvli_ctx* ctx, const uint32_t* prompt, uint64_t n_
  * last forward would pass max_seq. */
 int vvli_cuda_decode(vvli_ctx* ctx, uint64_t n_steps, uint32_t* out_tokens, float* device_ms);
 
+/* Sampler.next (src/generator.zig:97-126, 338-463) on the device, over
+ * `logits_or_null` (vocab_size host floats, uploaded) or, when it is NULL,
+ * the logits of the last forward call (forward_token / forward_embedding /
+ * prefill / decode), which stay on the device.  `recent` holds the prompt tokens followed by the
+ * generated ones (or at least their last repeat_last_n); repeat penalties
+ * apply to the last repeat_last_n of them.  temperature <= 0: penalised
+ * argmax.  Otherwise top-k by (adjusted logit desc, id asc), exp((l - max)/T),
+ * the top-p cut and the cumulative draw, with the sums in the reference's
+ * order.  `rng_state` is the xoshiro256++ state of std.Random.DefaultPrng; it
+ * is advanced by random.float(f32) exactly when the reference draws (T > 0
+ * and a finite candidate exists).  Invalid options: VVLI_ERR_INVALID_SAMPLING
+ * (validateSamplingOptions, :338-342).  Under tensor parallelism every rank
+ * makes the call with the same state and gets the same token. */
+int vvli_cuda_sample(vvli_ctx* ctx, const vvli_sample_options* options, const float* logits_or_null,
+                     const uint32_t* recent, uint64_t n_recent, uint64_t rng_state[4], uint32_t* out_token);
+
 /* Measurement helper with no counterpart in the reference: times one decode
  * kernel alone with CUDA events on the context's stream, cycling over every
  * layer's weights so that no launch finds its weights in L2.  kernel: 0 q|k|v

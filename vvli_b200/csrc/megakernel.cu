@@ -121,6 +121,27 @@ VVLI_DEV void trace_mark(const MegaParams& P, int f, int k) {
   if (P.trace) P.trace[(static_cast<size_t>(f) * gridDim.x + blockIdx.x) * 6 + k] = global_timer_ns();
 }
 
+// L2 prefetch of rows [ra, rb) of this CTA's share of GEMV phase `ph` (each
+// matrix of a pair), in 64 KB pieces spread over `nlanes` threads.  Used
+// while the ring is full, so HBM keeps streaming weights that the producer
+// will copy from L2 soon after.
+__device__ void prefetch_rows(const MegaPhase& ph, int ra, int rb, int t, int nlanes) {
+  const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
+  const int nrows = cta_row(ph.N, blockIdx.x + 1, ph.row_align) - r0;
+  ra = max(0, min(ra, nrows));
+  rb = min(rb, nrows);
+  if (rb <= ra) return;
+  const size_t total = static_cast<size_t>(rb - ra) * ph.K * 2;
+  constexpr size_t kPiece = 65536;
+  const size_t pieces = (total + kPiece - 1) / kPiece;
+  for (size_t c = t; c < pieces * ph.nphys; c += nlanes) {
+    const int q = static_cast<int>(c / pieces);
+    const size_t off = (c % pieces) * kPiece;
+    const uint8_t* base = reinterpret_cast<const uint8_t*>(ph.W + static_cast<size_t>(r0 + ra + q * ph.pair_offset) * ph.K);
+    prefetch_l2_bulk(base + off, static_cast<uint32_t>(min(kPiece, total - off)));
+  }
+}
+
 // ---------------------------------------------------------------- producer
 // Cursor over this CTA's stages of every GEMV phase of the step, in order.
 struct StageCursor {
@@ -295,6 +316,11 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
   named_barrier(1, kNC);
   if (tid == 0) trace_mark(P, f, 2);
   const float scale = scale_sh;
+  if (P.pf_epi_stages > 0 && warp == 1 && f + 1 < P.nphases && P.phases[f + 1].kind == MK_GEMV) {
+    // The producer has issued the next phase's first nst stages; warm L2 with the following ones.
+    const MegaPhase& nx = P.phases[f + 1];
+    prefetch_rows(nx, P.nst * nx.R, (P.nst + P.pf_epi_stages) * nx.R, lane, kWarp);
+  }
 
   // ---- epilogue
   if (ph.epi == ME_QKV) {
@@ -751,6 +777,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
     if (ph.kind == MK_EMBED) {
       mega_embed(P, red, err);
     } else if (ph.kind == MK_ATTN) {
+      if (warp == kCW - 1 && f + 2 < P.nphases) {
+        // Attention reads little from HBM and the ring is full: prefetch the
+        // next phase's rows beyond the ring and the head of the one after.
+        if (P.pf_attn_next) prefetch_rows(P.phases[f + 1], P.nst * P.phases[f + 1].R, 1 << 30, tid & 31, kWarp);
+        if (P.pf_attn_rows > 0 && P.phases[f + 2].kind == MK_GEMV)
+          prefetch_rows(P.phases[f + 2], 0, P.pf_attn_rows, tid & 31, kWarp);
+      }
       mega_attention(P, ph, part, err, f);
     } else {
       mega_gemv<4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f);  // plans have cpl <= 4

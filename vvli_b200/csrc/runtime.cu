@@ -22,6 +22,7 @@
 #include "../../include/vvli_cuda.h"
 #include "gemm_tc.cuh"
 #include "kernels.h"
+#include "sampler.cuh"
 
 using namespace vvli;
 
@@ -202,6 +203,18 @@ struct vvli_ctx {
   int* pf_tokens = nullptr;
   CUtensorMap tm_ah_hi{}, tm_ah_lo{}, tm_aq_hi{}, tm_aq_lo{}, tm_f_hi{}, tm_f_lo{};
   std::vector<CUtensorMap> tm_w;  // per layer: q|k|v, o, gate|up, down
+  // device sampler (allocated on first use)
+  unsigned* smp_stamp = nullptr;
+  unsigned* smp_key32 = nullptr;
+  unsigned long long *smp_key64 = nullptr, *smp_key64_sorted = nullptr;
+  float* smp_probs = nullptr;
+  float* smp_logits = nullptr;
+  uint32_t* smp_recent = nullptr;
+  SampleState* smp_state = nullptr;
+  SampleState* h_smp_state = nullptr;
+  void* smp_temp = nullptr;
+  size_t smp_temp_bytes = 0;
+  unsigned smp_call = 0;
 };
 
 namespace {
@@ -407,6 +420,9 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   // L2 prefetch beyond the ring: off by default (measured slower on B200:
   // prefetched lines were evicted before the bulk copies read them).
   P.lookahead = getenv("VVLI_MEGA_LOOKAHEAD") ? atoi(getenv("VVLI_MEGA_LOOKAHEAD")) : 0;
+  P.pf_attn_next = getenv("VVLI_MEGA_PF_ATTN_NEXT") ? atoi(getenv("VVLI_MEGA_PF_ATTN_NEXT")) : 0;
+  P.pf_attn_rows = getenv("VVLI_MEGA_PF_ATTN_ROWS") ? atoi(getenv("VVLI_MEGA_PF_ATTN_ROWS")) : 0;
+  P.pf_epi_stages = getenv("VVLI_MEGA_PF_EPI_STAGES") ? atoi(getenv("VVLI_MEGA_PF_EPI_STAGES")) : 0;
   P.part_floats = static_cast<int>(part);
   P.st = c->st;
   P.seq_tokens = c->seq_tokens;
@@ -789,11 +805,13 @@ void free_ctx(vvli_ctx* c) {
   void* dev[] = {c->w, c->kv, c->page_table, c->x, c->qkv, c->attn, c->ff, c->logits, c->logits_full, c->emb_in,
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
                  c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->pf_x, c->pf_q,
-                 c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens};
+                 c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->smp_stamp, c->smp_key32,
+                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_recent, c->smp_state, c->smp_temp};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (c->h_st) cudaFreeHost(c->h_st);
   if (c->h_tok) cudaFreeHost(c->h_tok);
+  if (c->h_smp_state) cudaFreeHost(c->h_smp_state);
   if (c->ev0) cudaEventDestroy(c->ev0);
   if (c->ev1) cudaEventDestroy(c->ev1);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -1180,6 +1198,110 @@ int vvli_cuda_decode(vvli_ctx* c, uint64_t n_steps, uint32_t* out_tokens, float*
   if ((st = finish_state(c))) return st;
   cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
   if (device_ms) *device_ms = c->last_ms;
+  return VVLI_OK;
+}
+
+// ---------------------------------------------------------------- sampling
+namespace {
+constexpr int kSampleRecentCap = 4096;  // recent tokens marked per copy
+
+int ensure_sampler(vvli_ctx* c) {
+  if (c->smp_state) return VVLI_OK;
+  const size_t V = static_cast<size_t>(c->V);
+  int st;
+  auto alloc = [&](void** p, size_t bytes) -> int {
+    const cudaError_t e = cudaMalloc(p, bytes);
+    return e == cudaSuccess ? VVLI_OK : cuda_fail(e, "sampler buffers");
+  };
+  c->smp_temp_bytes = sample_sort_temp_bytes(c->V);
+  if ((st = alloc(reinterpret_cast<void**>(&c->smp_stamp), V * 4)) ||
+      (st = alloc(reinterpret_cast<void**>(&c->smp_key32), V * 4)) ||
+      (st = alloc(reinterpret_cast<void**>(&c->smp_key64), V * 8)) ||
+      (st = alloc(reinterpret_cast<void**>(&c->smp_key64_sorted), V * 8)) ||
+      (st = alloc(reinterpret_cast<void**>(&c->smp_probs), V * 4)) ||
+      (st = alloc(reinterpret_cast<void**>(&c->smp_logits), V * 4)) ||
+      (st = alloc(reinterpret_cast<void**>(&c->smp_recent), kSampleRecentCap * 4)) ||
+      (st = alloc(&c->smp_temp, std::max<size_t>(c->smp_temp_bytes, 16))) ||
+      (st = alloc(reinterpret_cast<void**>(&c->smp_state), sizeof(SampleState))))
+    return st;
+  CK(cudaMallocHost(&c->h_smp_state, sizeof(SampleState)));
+  CK(cudaMemset(c->smp_stamp, 0, V * 4));
+  CK(configure_sampler());
+  c->smp_call = 0;
+  return VVLI_OK;
+}
+}  // namespace
+
+int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* host_logits, const uint32_t* recent,
+                     uint64_t n_recent, uint64_t* rng_state, uint32_t* out_token) {
+  if (!c || !o || !rng_state || !out_token || (n_recent && !recent)) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  // validateSamplingOptions (src/generator.zig:338-342)
+  if (o->temperature < 0.0f || std::isnan(o->temperature) || o->top_p <= 0.0f || o->top_p > 1.0f ||
+      std::isnan(o->top_p) || o->repeat_penalty < 1.0f || std::isnan(o->repeat_penalty))
+    return VVLI_ERR_INVALID_SAMPLING;
+  CK(cudaSetDevice(c->device));
+  int st;
+  if ((st = ensure_sampler(c))) return st;
+  const float* logits = c->logits;
+  if (host_logits) {
+    CK(cudaMemcpyAsync(c->smp_logits, host_logits, static_cast<size_t>(c->V) * 4, cudaMemcpyHostToDevice, c->stream));
+    logits = c->smp_logits;
+  } else if (c->tp_size > 1) {
+    if ((st = nccl_wait(c, nccl().AllGather(c->logits, c->logits_full, c->V_l, ncclFloat32, c->comm, c->stream),
+                        "allgather logits")))
+      return st;
+    logits = c->logits_full;
+  }
+  if (++c->smp_call == 0) {  // the stamps wrapped: start over
+    CK(cudaMemsetAsync(c->smp_stamp, 0, static_cast<size_t>(c->V) * 4, c->stream));
+    c->smp_call = 1;
+  }
+  // buildRepeatCounts (src/generator.zig:344-360): the last repeat_last_n tokens.
+  if (o->repeat_penalty > 1.0f && o->repeat_last_n > 0 && n_recent > 0) {
+    const uint64_t n_use = std::min<uint64_t>(n_recent, o->repeat_last_n);
+    const uint32_t* src = recent + (n_recent - n_use);
+    for (uint64_t done = 0; done < n_use; done += kSampleRecentCap) {
+      const int n = static_cast<int>(std::min<uint64_t>(kSampleRecentCap, n_use - done));
+      CK(cudaMemcpyAsync(c->smp_recent, src + done, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
+      CK(launch_sample_mark(c->smp_recent, n, c->smp_stamp, c->smp_call, c->V, c->stream));
+      if (done + kSampleRecentCap < n_use) CK(cudaStreamSynchronize(c->stream));  // smp_recent is reused
+    }
+  }
+  SampleParams p{};
+  p.logits = logits;
+  p.V = c->V;
+  p.stamp = c->smp_stamp;
+  p.call = c->smp_call;
+  p.temperature = o->temperature;
+  p.top_p = o->top_p;
+  p.repeat_penalty = o->repeat_penalty;
+  p.top_k = o->top_k;
+  p.key32 = c->smp_key32;
+  p.key64 = c->smp_key64;
+  p.key64_sorted = c->smp_key64_sorted;
+  p.probs = c->smp_probs;
+  p.st = c->smp_state;
+  SampleState* h = c->h_smp_state;
+  std::memcpy(h->rng, rng_state, sizeof(h->rng));
+  h->token = -1;
+  h->path = 0;
+  h->k = 0;
+  CK(cudaMemcpyAsync(c->smp_state, h, sizeof(SampleState), cudaMemcpyHostToDevice, c->stream));
+  CK(launch_sample(p, c->stream));
+  CK(cudaMemcpyAsync(h, c->smp_state, sizeof(SampleState), cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  if (h->path == 1) {
+    CK(launch_sample_long(p, c->smp_temp, c->smp_temp_bytes, c->stream));
+    CK(cudaMemcpyAsync(h, c->smp_state, sizeof(SampleState), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+  }
+  if (h->token < 0 || h->token >= static_cast<int>(c->V)) {
+    g_last_error = "sampler produced no token";
+    return VVLI_ERR_CUDA;
+  }
+  std::memcpy(rng_state, h->rng, sizeof(h->rng));
+  *out_token = static_cast<uint32_t>(h->token);
   return VVLI_OK;
 }
 

@@ -1,0 +1,432 @@
+// sampler.cu - Sampler.next (src/generator.zig:97-126, 338-463) on the device.
+//
+// One CTA of 1024 threads does the whole step for candidate lists of up to
+// kSampleSmallK entries (the reference's default top_k is 40):
+//   1. adjusted logits (adjustedLogit, :399-402) from the logits and a
+//      per-token stamp of the last repeat_last_n tokens (only "count != 0"
+//      matters to the reference);
+//   2. temperature <= 0: the penalised argmax (greedyWithPenalties, :362-374);
+//   3. else the top-k candidates by (adjusted logit desc, id asc) - the order
+//      insertTopCandidate/bubbleCandidateUp leave them in (:404-422) - found
+//      by a three-level radix select over order-preserving 32-bit keys, with
+//      ties at the threshold taken in id order, then a bitonic sort in
+//      shared memory;
+//   4. exp((l - max) / T), the sequential fp32 sums, the top-p cut and the
+//      cumulative draw (prepareProbabilities/sampleCandidate, :428-463) on one
+//      thread, in the reference's order, so the sums round the same way.
+// Longer candidate lists (top_k = 0 or > kSampleSmallK) sort the whole
+// vocabulary's keys (CUB radix sort of 64-bit (key, ~id) pairs) and run
+// step 4 over the sorted list.  There, once a probability is below half an
+// ulp of the running sum, every later one is too (the list is sorted), so
+// the sum can no longer change and the scan stops.
+//
+// The uniform draw is random.float(f32) of Zig's DefaultPrng: xoshiro256++
+// (the published generator) with the float built from 23 mantissa bits and a
+// leading-zero count for the exponent.  It is drawn only when the reference
+// draws it: temperature > 0 and at least one finite candidate.
+#include <cub/device/device_radix_sort.cuh>
+
+#include "common.cuh"
+#include "sampler.cuh"
+
+namespace vvli {
+namespace {
+
+constexpr int kST = 1024;   // threads of the sampling CTA
+constexpr int kBins = 4096;  // radix-select histogram (12 bits)
+constexpr size_t kSampleSmem = static_cast<size_t>(kSampleSmallK) * (8 + 4);
+
+// Finite floats -> unsigned keys in the same order (never 0; +0 and -0 equal).
+VVLI_DEV unsigned order_key(float s) {
+  const unsigned u = __float_as_uint(s == 0.0f ? 0.0f : s);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+VVLI_DEV float key_value(unsigned k) { return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k); }
+VVLI_DEV unsigned long long make_key64(unsigned k, int id) {
+  return (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<unsigned>(id));
+}
+VVLI_DEV unsigned key64_id(unsigned long long k) { return 0xffffffffu - static_cast<unsigned>(k & 0xffffffffull); }
+
+VVLI_DEV float adjusted_logit(float l, bool recent, float rp) {  // :399-402
+  if (!recent || rp <= 1.0f) return l;
+  return l < 0.0f ? l * rp : l / rp;
+}
+
+VVLI_DEV unsigned long long rotl64(unsigned long long x, int k) { return (x << k) | (x >> (64 - k)); }
+VVLI_DEV unsigned long long xoshiro_next(unsigned long long* s) {
+  const unsigned long long r = rotl64(s[0] + s[3], 23) + s[0];
+  const unsigned long long t = s[1] << 17;
+  s[2] ^= s[0];
+  s[3] ^= s[1];
+  s[1] ^= s[2];
+  s[0] ^= s[3];
+  s[2] ^= t;
+  s[3] = rotl64(s[3], 45);
+  return r;
+}
+// random.float(f32): uniform in [0, 1) with the exponent from leading zeros.
+VVLI_DEV float xoshiro_float(unsigned long long* s) {
+  const unsigned long long rand = xoshiro_next(s);
+  int lz = __clzll(static_cast<long long>(rand));
+  if (lz >= 41) {
+    lz = 41 + __clzll(static_cast<long long>(xoshiro_next(s)));
+    if (lz == 41 + 64) lz += __clz(static_cast<int>(static_cast<unsigned>(xoshiro_next(s)) | 0x7ffu));
+  }
+  return __uint_as_float((static_cast<unsigned>(126 - lz) << 23) | static_cast<unsigned>(rand & 0x7fffffull));
+}
+
+// exp of an fp32 argument, rounded once to fp32 from a double-precision exp.
+VVLI_DEV float prob_of(float logit, float max_logit, float t) {
+  const float pr = static_cast<float>(exp(static_cast<double>((logit - max_logit) / t)));
+  return isfinite(pr) ? pr : 0.0f;
+}
+
+// Adding p (or anything smaller) to `sum` leaves it unchanged.
+VVLI_DEV bool negligible(float p, float sum) { return p < 0.5f * (nextafterf(sum, INFINITY) - sum); }
+
+// Exclusive prefix sum over the CTA's threads in index order; *total = sum.
+__device__ unsigned block_excl_scan(unsigned v, unsigned* wsum, unsigned* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    unsigned w = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    wsum[lane] = w;
+  }
+  __syncthreads();
+  const unsigned excl = x - v + (warp > 0 ? wsum[warp - 1] : 0u);
+  *total = wsum[31];
+  __syncthreads();
+  return excl;
+}
+
+// Argmax over the CTA (first index of the maximum, NaN never chosen); result on all threads.
+__device__ int block_argmax(float v, int i, float* wv, int* wi) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  warp_argmax(v, i);
+  if (lane == 0) {
+    wv[warp] = v;
+    wi[warp] = i;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    v = wv[lane];
+    i = wi[lane];
+    warp_argmax(v, i);
+    if (lane == 0) wi[0] = i;
+  }
+  __syncthreads();
+  const int r = wi[0];
+  __syncthreads();
+  return r;
+}
+
+__global__ void sample_mark_kernel(const uint32_t* recent, int n, unsigned* stamp, unsigned call, int V) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const uint32_t t = recent[i];
+    if (t < static_cast<uint32_t>(V)) stamp[t] = call;
+  }
+}
+
+__global__ void __launch_bounds__(kST, 1) sample_kernel(const SampleParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);  // [kSampleSmallK]
+  float* probs = reinterpret_cast<float*>(cand + kSampleSmallK);            // [kSampleSmallK]
+  __shared__ unsigned hist[kBins];
+  __shared__ unsigned wsum[32];
+  __shared__ float wv[32];
+  __shared__ int wi[32];
+  __shared__ unsigned found[2];
+  const int tid = threadIdx.x;
+  const int V = p.V;
+  const float rp = p.repeat_penalty;
+  SampleState* st = p.st;
+
+  if (p.temperature <= 0.0f) {
+    // greedyWithPenalties (:362-374): strict '>' from element 0, so a NaN
+    // there is never replaced and NaNs elsewhere never win.
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < V; i += kST) {
+      const float s = adjusted_logit(p.logits[i], p.stamp[i] == p.call, rp);
+      if (better(s, i, bv, bi)) {
+        bv = s;
+        bi = i;
+      }
+    }
+    const int best = block_argmax(bv, bi, wv, wi);
+    if (tid == 0) {
+      const float s0 = adjusted_logit(p.logits[0], p.stamp[0] == p.call, rp);
+      st->token = isnan(s0) || best == 0x7fffffff ? 0 : best;
+      st->path = 0;
+    }
+    return;
+  }
+
+  // Keys of the finite adjusted logits (buildCandidates skips the others, :384, :392).
+  unsigned nfin = 0;
+  for (int i = tid; i < V; i += kST) {
+    const float s = adjusted_logit(p.logits[i], p.stamp[i] == p.call, rp);
+    const bool fin = isfinite(s);
+    p.key32[i] = fin ? order_key(s) : 0u;
+    nfin += fin ? 1u : 0u;
+  }
+  unsigned n_finite;
+  block_excl_scan(nfin, wsum, &n_finite);  // its barriers also publish key32 to the CTA
+  if (n_finite == 0) {
+    // No candidate: llm.argmax of the raw logits (:115).
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < V; i += kST) {
+      const float l = p.logits[i];
+      if (better(l, i, bv, bi)) {
+        bv = l;
+        bi = i;
+      }
+    }
+    const int best = block_argmax(bv, bi, wv, wi);
+    if (tid == 0) {
+      st->token = isnan(p.logits[0]) || best == 0x7fffffff ? 0 : best;
+      st->path = 0;
+    }
+    return;
+  }
+  const unsigned long long limit = p.top_k == 0 ? static_cast<unsigned long long>(V)
+                                                : (p.top_k < static_cast<unsigned long long>(V) ? p.top_k : V);
+  const unsigned k = static_cast<unsigned>(limit < n_finite ? limit : n_finite);
+  if (k > static_cast<unsigned>(kSampleSmallK)) {
+    for (int i = tid; i < V; i += kST) {
+      const unsigned kk = p.key32[i];
+      p.key64[i] = kk ? make_key64(kk, i) : 0ull;
+    }
+    if (tid == 0) {
+      st->path = 1;
+      st->k = static_cast<int>(k);
+    }
+    return;
+  }
+
+  // Radix select: the k-th largest key (threshold tau) in three levels.
+  unsigned prefix = 0, mask = 0, need = k;
+  const int shifts[3] = {20, 8, 0};
+  const int widths[3] = {12, 12, 8};
+  for (int lv = 0; lv < 3; ++lv) {
+    const int nb = 1 << widths[lv], sh = shifts[lv];
+    for (int b = tid; b < nb; b += kST) hist[b] = 0;
+    __syncthreads();
+    for (int i = tid; i < V; i += kST) {
+      const unsigned kk = p.key32[i];
+      if (kk != 0 && (kk & mask) == prefix) atomicAdd(&hist[(kk >> sh) & (nb - 1)], 1u);
+    }
+    __syncthreads();
+    const int bpt = nb >= kST ? nb / kST : 1;
+    const int b0 = tid * bpt;
+    unsigned local = 0;
+    for (int j = 0; j < bpt; ++j)
+      if (b0 + j < nb) local += hist[b0 + j];
+    unsigned total;
+    const unsigned excl = block_excl_scan(local, wsum, &total);
+    unsigned run = total - excl - local;  // keys in the bins of higher-numbered threads
+    for (int j = bpt - 1; j >= 0; --j) {
+      const int b = b0 + j;
+      if (b >= nb) continue;
+      const unsigned h = hist[b];
+      if (run < need && run + h >= need) {
+        found[0] = static_cast<unsigned>(b);
+        found[1] = run;
+      }
+      run += h;
+    }
+    __syncthreads();
+    need -= found[1];
+    prefix |= found[0] << sh;
+    mask |= static_cast<unsigned>(nb - 1) << sh;
+    __syncthreads();
+  }
+  const unsigned tau = prefix;
+  const unsigned c_gt = k - need;  // keys above tau; `need` keys equal to tau are taken, lowest ids first
+
+  // Compaction in id order: thread t scans ids [t*C, (t+1)*C).
+  const int C = (V + kST - 1) / kST;
+  const int i0 = min(V, tid * C), i1 = min(V, i0 + C);
+  unsigned ngt = 0, neq = 0;
+  for (int i = i0; i < i1; ++i) {
+    const unsigned kk = p.key32[i];
+    ngt += kk > tau ? 1u : 0u;
+    neq += kk == tau ? 1u : 0u;
+  }
+  unsigned tot_gt, tot_eq;
+  unsigned og = block_excl_scan(ngt, wsum, &tot_gt);
+  unsigned oe = block_excl_scan(neq, wsum, &tot_eq);
+  for (int i = i0; i < i1; ++i) {
+    const unsigned kk = p.key32[i];
+    if (kk > tau) {
+      cand[og++] = make_key64(kk, i);
+    } else if (kk == tau) {
+      if (oe < need) cand[c_gt + oe] = make_key64(kk, i);
+      ++oe;
+    }
+  }
+  int N = 1;
+  while (N < static_cast<int>(k)) N <<= 1;
+  for (int j = static_cast<int>(k) + tid; j < N; j += kST) cand[j] = 0ull;
+  __syncthreads();
+  // Bitonic sort, descending.
+  for (int size = 2; size <= N; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < N / 2; i += kST) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const unsigned long long a = cand[lo], b = cand[hi];
+        if ((a < b) == desc) {
+          cand[lo] = b;
+          cand[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // prepareProbabilities (:428-449) and sampleCandidate (:451-463).
+  const float t = fmaxf(p.temperature, 1e-6f);
+  const float mx = key_value(static_cast<unsigned>(cand[0] >> 32));
+  for (int j = tid; j < static_cast<int>(k); j += kST) probs[j] = prob_of(key_value(static_cast<unsigned>(cand[j] >> 32)), mx, t);
+  __syncthreads();
+  if (tid == 0) {
+    float total = 0.0f;
+    for (unsigned j = 0; j < k; ++j) total += probs[j];
+    unsigned count = k;
+    if (!(total > 0.0f) || !isfinite(total)) {
+      count = 1;
+    } else if (p.top_p < 1.0f) {
+      float cum = 0.0f;
+      for (unsigned j = 0; j < k; ++j) {
+        cum += probs[j];
+        if (cum / total >= p.top_p) {
+          count = j + 1;
+          break;
+        }
+      }
+    }
+    unsigned long long s[4] = {st->rng[0], st->rng[1], st->rng[2], st->rng[3]};
+    const float u = xoshiro_float(s);
+    float total2 = 0.0f;
+    for (unsigned j = 0; j < count; ++j) total2 += probs[j];
+    unsigned tok = key64_id(cand[0]);
+    if (total2 > 0.0f && isfinite(total2)) {
+      const float target = fminf(u, 0.99999994f) * total2;
+      float cum = 0.0f;
+      tok = key64_id(cand[count - 1]);
+      for (unsigned j = 0; j < count; ++j) {
+        cum += probs[j];
+        if (target <= cum) {
+          tok = key64_id(cand[j]);
+          break;
+        }
+      }
+    }
+    for (int q = 0; q < 4; ++q) st->rng[q] = s[q];
+    st->token = static_cast<int>(tok);
+    st->path = 0;
+  }
+}
+
+// Step 4 over the first st->k keys of the sorted vocabulary.
+__global__ void __launch_bounds__(kST, 1) sample_long_kernel(const SampleParams p) {
+  SampleState* st = p.st;
+  const int k = st->k;
+  const unsigned long long* keys = p.key64_sorted;
+  const float t = fmaxf(p.temperature, 1e-6f);
+  const float mx = key_value(static_cast<unsigned>(keys[0] >> 32));
+  for (int j = threadIdx.x; j < k; j += kST) p.probs[j] = prob_of(key_value(static_cast<unsigned>(keys[j] >> 32)), mx, t);
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const float* pr = p.probs;
+  float total = 0.0f;
+  for (int j = 0; j < k; ++j) {
+    if (negligible(pr[j], total)) break;
+    total += pr[j];
+  }
+  int count = k;
+  float total2 = total;
+  if (!(total > 0.0f) || !isfinite(total)) {
+    count = 1;
+    total2 = pr[0];
+  } else if (p.top_p < 1.0f) {
+    float cum = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      if (negligible(pr[j], cum)) break;
+      cum += pr[j];
+      if (cum / total >= p.top_p) {
+        count = j + 1;
+        break;
+      }
+    }
+    total2 = cum;  // the sum of the first `count` probabilities, added in the same order
+  }
+  unsigned long long s[4] = {st->rng[0], st->rng[1], st->rng[2], st->rng[3]};
+  const float u = xoshiro_float(s);
+  unsigned tok = key64_id(keys[0]);
+  if (total2 > 0.0f && isfinite(total2)) {
+    const float target = fminf(u, 0.99999994f) * total2;
+    float cum = 0.0f;
+    tok = key64_id(keys[count - 1]);
+    for (int j = 0; j < count; ++j) {
+      if (negligible(pr[j], cum)) break;
+      cum += pr[j];
+      if (target <= cum) {
+        tok = key64_id(keys[j]);
+        break;
+      }
+    }
+  }
+  for (int q = 0; q < 4; ++q) st->rng[q] = s[q];
+  st->token = static_cast<int>(tok);
+  st->path = 0;
+}
+
+}  // namespace
+
+cudaError_t launch_sample_mark(const uint32_t* recent, int n, unsigned* stamp, unsigned call, int V, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  sample_mark_kernel<<<(n + 255) / 256, 256, 0, s>>>(recent, n, stamp, call, V);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sample(const SampleParams& p, cudaStream_t s) {
+  sample_kernel<<<1, kST, kSampleSmem, s>>>(p);
+  return cudaGetLastError();
+}
+
+size_t sample_sort_temp_bytes(int V) {
+  size_t bytes = 0;
+  cub::DeviceRadixSort::SortKeysDescending(nullptr, bytes, static_cast<unsigned long long*>(nullptr),
+                                           static_cast<unsigned long long*>(nullptr), V);
+  return bytes;
+}
+
+cudaError_t launch_sample_long(const SampleParams& p, void* temp, size_t temp_bytes, cudaStream_t s) {
+  size_t bytes = temp_bytes;
+  cudaError_t e = cub::DeviceRadixSort::SortKeysDescending(temp, bytes, p.key64, p.key64_sorted, p.V, 0, 64, s);
+  if (e != cudaSuccess) return e;
+  sample_long_kernel<<<1, kST, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t configure_sampler() {
+  return cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSampleSmem));
+}
+
+}  // namespace vvli

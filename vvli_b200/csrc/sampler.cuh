@@ -1,0 +1,47 @@
+// sampler.cuh - Sampler.next (src/generator.zig:97-126, 338-463) on the device.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vvli {
+
+// Candidate lists up to this length are selected and sorted inside one CTA;
+// longer ones (top_k = 0 or large) take the sorted-vocabulary path.
+constexpr int kSampleSmallK = 4096;
+
+struct SampleState {
+  unsigned long long rng[4];  // xoshiro256++ state, advanced when a draw happens
+  int token;                  // result
+  int path;                   // 0: token is final; 1: the long-candidate path must run
+  int k;                      // candidates of the long path
+  int pad;
+};
+
+struct SampleParams {
+  const float* logits;
+  int V;
+  const unsigned* stamp;      // stamp[i] == call: token i is among the last repeat_last_n
+  unsigned call;
+  float temperature, top_p, repeat_penalty;
+  unsigned long long top_k;
+  unsigned* key32;            // [V] scratch: order-preserving keys of the finite adjusted logits, 0 = none
+  unsigned long long* key64;  // [V] scratch: (key32 << 32) | ~id, input of the long path's sort
+  unsigned long long* key64_sorted;
+  float* probs;               // [V] scratch of the long path
+  SampleState* st;
+};
+
+// Marks recent[0, n) (tokens >= V skipped) with `call` (buildRepeatCounts
+// only decides whether a token's count is non-zero).
+cudaError_t launch_sample_mark(const uint32_t* recent, int n, unsigned* stamp, unsigned call, int V, cudaStream_t s);
+// Greedy-with-penalties or the whole short-candidate sampling path; sets
+// st->path = 1 when the candidate list is longer than kSampleSmallK.
+cudaError_t launch_sample(const SampleParams& p, cudaStream_t s);
+// The long-candidate path: sort the vocabulary's keys, then probabilities,
+// top-p and the draw over the first st->k.
+cudaError_t launch_sample_long(const SampleParams& p, void* temp, size_t temp_bytes, cudaStream_t s);
+size_t sample_sort_temp_bytes(int V);
+cudaError_t configure_sampler();
+
+}  // namespace vvli

@@ -3,8 +3,9 @@
 ``generate_greedy`` and ``generate_greedy_measured`` keep the reference's
 names, options, results and errors (src/generator.zig:14-48, 142-325).  With
 the ``--greedy`` settings (temperature 0, repeat penalty 1.0) the token loop
-runs on the GPU through ``Runner.generate_greedy``; other settings fetch the
-logits each step and apply the reference Sampler (vvli_b200.sampler).
+runs on the GPU through ``Runner.generate_greedy``; other settings run
+Sampler.next on the GPU each step (``vvli_b200.sampler.DeviceSampler``) over
+logits that never leave the device.
 """
 
 from __future__ import annotations
@@ -77,17 +78,17 @@ def generate_greedy_measured(runner: Runner, prompt_tokens, options: Options) ->
         return Result(tokens, Stats(s.prompt_tokens, s.generated_tokens, s.prefill_nanoseconds,
                                     s.decode_nanoseconds, s.total_nanoseconds))
     t0 = time.perf_counter_ns()
-    logits = runner.prefill(prompt_tokens, 0)
+    runner.prefill(prompt_tokens, 0, logits=False)
     t1 = time.perf_counter_ns()
-    smp = _sampler.Sampler(runner.cfg.vocab_size, options)
+    smp = _sampler.DeviceSampler(runner.cfg.vocab_size, options)
     out = []
     position = len(prompt_tokens)
     while len(out) < options.max_new_tokens:
-        nxt = smp.next(logits, prompt_tokens, out, options)
+        nxt = smp.next(runner, prompt_tokens, out, options)
         out.append(nxt)
         if options.eos_token_id is not None and nxt == options.eos_token_id:
             break
-        logits = runner.forward_token(nxt, position)
+        runner.forward_token(nxt, position, logits=False)
         position += 1
     t2 = time.perf_counter_ns()
     return Result(out, Stats(len(prompt_tokens), len(out), t1 - t0, t2 - t1, t2 - t0))

@@ -126,6 +126,31 @@ class Runner:
         check(_abi.lib().vvli_cuda_decode(self._ctx, n_steps, out.ctypes.data_as(_u32p), ctypes.byref(ms)))
         return out[:n_steps].tolist(), float(ms.value)
 
+    def sample(self, options, recent, rng_state: np.ndarray, logits=None) -> int:
+        """Sampler.next on the device, over ``logits`` (host, uploaded) or the last forward's logits.
+
+        ``recent``: prompt tokens followed by the generated ones (or their
+        tail); ``rng_state``: uint64[4] xoshiro256++ state, advanced in place.
+        """
+        lg = None
+        if logits is not None:
+            lg = np.ascontiguousarray(logits, dtype=np.float32)
+            if lg.size != self.cfg.vocab_size:
+                from .errors import VvliError
+                raise VvliError("OutputTooSmall")
+        o = _abi.CSampleOptions(temperature=float(options.temperature), top_p=float(options.top_p),
+                                top_k=int(options.top_k), repeat_penalty=float(options.repeat_penalty),
+                                repeat_last_n=int(options.repeat_last_n))
+        n_use = min(len(recent), int(options.repeat_last_n))
+        r = np.ascontiguousarray(list(recent)[len(recent) - n_use:], dtype=np.uint32)
+        assert rng_state.dtype == np.uint64 and rng_state.size == 4 and rng_state.flags["C_CONTIGUOUS"]
+        out = ctypes.c_uint32(0)
+        check(_abi.lib().vvli_cuda_sample(self._ctx, ctypes.byref(o), None if lg is None else lg.ctypes.data_as(_f32p),
+                                          r.ctypes.data_as(_u32p) if r.size else None,
+                                          r.size, rng_state.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
+                                          ctypes.byref(out)))
+        return int(out.value)
+
     def time_kernel(self, kernel: int, reps: int):
         """(mean ms per launch, algorithmic bytes per launch) of one decode kernel alone."""
         ms = ctypes.c_float(0)

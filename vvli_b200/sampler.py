@@ -146,3 +146,27 @@ class Sampler:
             if target <= cum:
                 return int(c)
         return int(cand[-1])
+
+
+class DeviceSampler:
+    """generator.Sampler whose next() runs on the GPU (vvli_cuda_sample).
+
+    Seeding follows Sampler.init (src/generator.zig:74-90): a random seed when
+    none is given, 0 replaced by 0x9e3779b97f4a7c15, SplitMix64 into the
+    xoshiro256++ state, which then lives here between calls.
+    """
+
+    def __init__(self, vocab_size: int, options):
+        seed = options.seed
+        if seed is None:
+            seed = int.from_bytes(np.random.default_rng().bytes(8), "little")
+        if seed == 0:
+            seed = 0x9E3779B97F4A7C15
+        self.vocab_size = vocab_size
+        self.state = np.array(Xoshiro256(seed).s, dtype=np.uint64)
+
+    def next(self, runner, prompt, generated, o) -> int:  # Sampler.next (:97-126)
+        validate_options(o)
+        n = int(o.repeat_last_n)
+        recent = list(prompt) + list(generated)
+        return runner.sample(o, recent[max(0, len(recent) - n):] if n else [], self.state)
