@@ -269,11 +269,29 @@ int vvli_cuda_query(vvli_ctx* ctx, const char* key, double* out);
  * number of values (0 without tracing); `out` is filled when cap >= count. */
 int vvli_cuda_trace(vvli_ctx* ctx, uint64_t* out, uint64_t cap, uint64_t* count);
 
-/* Self-test of the tensor-core (tcgen05) prefill GEMM with no counterpart in
- * the reference: C[M,N] = (A_hi + A_lo)[M,K] . W[N,K]^T on random bf16 data
- * (two_a = 0: A_hi only) against a SIMT reference on `device`;
- * `max_rel_err` = max |C - ref| / max |ref|. */
-int vvli_cuda_gemm_selftest(int device, int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err);
+/* Self-test of the tensor-core (tcgen05) GEMMs, with no counterpart in the
+ * reference: C[M,N] = (A_hi + A_lo)[M,K] . W[N,K]^T on random bf16 data
+ * (two_a = 0: A_hi only) against a SIMT fp64-accumulating reference on
+ * `device`; `max_rel_err` = max |C - ref| / max |ref|.  kernel 0: the prefill
+ * GEMM (128 x 256 tiles); kernel 1: the decode-batch GEMM (M <= 32 rows,
+ * weight rows as the MMA's M operand, split-K over a cluster). */
+int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two_a, uint64_t seed,
+                            float* max_rel_err);
+
+/* One decode step of `batch` independent sequences, with no counterpart in
+ * the reference (which decodes one sequence): row b is sequence slot b, with
+ * its own KV cache (slot 0 is the cache forward_token uses), and computes what
+ * Runner.forwardToken (src/llm.zig:702-709) computes for tokens[b] at
+ * positions[b] on that sequence.  The linear layers run as tensor-core GEMMs
+ * that read every weight once per 32 rows (bf16 hi + lo activations, fp32
+ * accumulation), so rows agree with forward_token to about 1e-3 of the
+ * logits' scale.  `logits_out` [batch][vocab_size] and `argmax_out` [batch]
+ * may be NULL.  batch <= max_batch of vvli_cuda_create; a token >= vocab_size
+ * gives VVLI_ERR_INVALID_TOKEN, a position >= max_seq VVLI_ERR_CONTEXT_FULL.
+ * The single-sequence state (next position, logits used by
+ * vvli_cuda_sample) is not changed. */
+int vvli_cuda_forward_batch(vvli_ctx* ctx, const uint32_t* tokens, const uint64_t* positions, uint64_t batch,
+                            float* logits_out, uint32_t* argmax_out);
 
 /* Greedy token choice over `rows` rows of `n` fp32 logits that are already in
  * device memory (row r at logits + r * n), writing the index of each row's

@@ -1,0 +1,115 @@
+"""vvli_cuda_forward_batch: a decode step of independent sequences against the oracle.
+
+Row b of a batch is sequence slot b with its own KV cache.  Sequences of
+different lengths are built by batch steps in which a finished row keeps
+re-running its last token at its last position (the same K/V are written
+again), so after the last step every row holds the logits of its whole
+sequence, which the oracle computes with Runner.forwardToken one token at a
+time (src/llm.zig:702-709).  The linear layers run on the tensor cores with
+bf16 hi + lo activations, hence the 2e-3 bound (the north-star bound is
+2e-2).
+"""
+
+import dataclasses
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from vvli_b200 import config as C
+from vvli_b200.errors import VvliError
+
+pytestmark = pytest.mark.gpu
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def vv():
+    import vvli_b200
+    return vvli_b200
+
+
+def run_batch(gpu, seqs):
+    """Batch steps until every row has consumed its sequence; returns the last (logits, argmax)."""
+    T = max(len(s) for s in seqs)
+    out = None
+    for t in range(T):
+        toks = [s[min(t, len(s) - 1)] for s in seqs]
+        pos = [min(t, len(s) - 1) for s in seqs]
+        out = gpu.forward_batch(toks, pos)
+    return out
+
+
+def oracle_last(oracle, cfg, seed, seq, max_seq):
+    ref = oracle.RefRunner(cfg, synthetic_seed=seed, max_seq=max_seq)
+    lg = None
+    for pos, t in enumerate(seq):
+        lg = ref.forward_token(t, pos)
+    return lg
+
+
+@pytest.mark.parametrize("name,B", [("qwen2_tiny", 5), ("llama3_tiny_rs", 3), ("llama3_tiny_rs", 40)])
+def test_batch_rows_match_sequential_forward(oracle, vv, name, B):
+    from make_golden import fixture_configs
+    cfg, seed = fixture_configs()[name]
+    max_seq = 64
+    gpu = vv.Runner(cfg, max_seq=max_seq, max_batch=B)
+    gpu.fill_synthetic(seed)
+    rng = np.random.default_rng(B)
+    seqs = [rng.integers(0, cfg.vocab_size, size=int(rng.integers(1, 24))).tolist() for _ in range(B)]
+    logits, am = run_batch(gpu, seqs)
+    for b, s in enumerate(seqs):
+        want = oracle_last(oracle, cfg, seed, s, max_seq)
+        assert np.max(np.abs(logits[b] - want)) < TOL, b
+        assert am[b] == int(np.argmax(logits[b])) and am[b] == oracle.argmax(want), b
+
+
+def test_batch_llama1b_shape_sixteen_rows(oracle, vv):
+    # Llama-3.2-1B layer shapes (h 2048, 32/8 heads, d 64, I 8192, V 128256) with 2 layers.
+    cfg = dataclasses.replace(C.llama3_2_1b(), num_hidden_layers=2)
+    gpu = vv.Runner(cfg, max_seq=128, max_batch=16)
+    gpu.fill_synthetic(0)
+    rng = np.random.default_rng(16)
+    seqs = [rng.integers(0, cfg.vocab_size, size=b + 1).tolist() for b in range(16)]
+    logits, am = run_batch(gpu, seqs)
+    for b, s in enumerate(seqs):
+        want = oracle_last(oracle, cfg, 0, s, 128)
+        assert np.max(np.abs(logits[b] - want)) < TOL, b
+        assert am[b] == oracle.argmax(want), b
+
+
+def test_batch_row0_continues_forward_token_sequence(vv):
+    from make_golden import fixture_configs
+    cfg, seed = fixture_configs()["llama3_tiny_rs"]
+    a = vv.Runner(cfg, max_seq=64, max_batch=2)
+    b = vv.Runner(cfg, max_seq=64)
+    a.fill_synthetic(seed)
+    b.fill_synthetic(seed)
+    toks = [5, 9, 200, 31, 7]
+    for pos, t in enumerate(toks):
+        a.forward_token(t, pos)
+        b.forward_token(t, pos)
+    lb = b.forward_token(42, len(toks))
+    la, am = a.forward_batch([42], [len(toks)])
+    assert np.max(np.abs(la[0] - lb)) < TOL and am[0] == b.last_argmax
+
+
+def test_batch_errors(vv):
+    cfg = C.tiny_qwen()
+    gpu = vv.Runner(cfg, max_seq=8, max_batch=2)
+    gpu.fill_synthetic(0)
+    with pytest.raises(VvliError) as e:
+        gpu.forward_batch([1, 2, 3], [0, 0, 0])
+    assert e.value.name == "InvalidArgument"
+    with pytest.raises(VvliError) as e:
+        gpu.forward_batch([1, cfg.vocab_size], [0, 0])
+    assert e.value.name == "InvalidToken"
+    with pytest.raises(VvliError) as e:
+        gpu.forward_batch([1, 2], [0, 8])
+    assert e.value.name == "ContextFull"
+    logits, am = gpu.forward_batch([1, 2], [0, 0])
+    assert logits.shape == (2, cfg.vocab_size) and len(am) == 2

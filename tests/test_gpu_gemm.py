@@ -1,4 +1,4 @@
-"""The tcgen05 tensor-core GEMM (prefill) against a SIMT reference, through the C ABI."""
+"""The tcgen05 tensor-core GEMMs (prefill and decode batch) against a SIMT reference, through the C ABI."""
 
 import ctypes
 
@@ -18,6 +18,23 @@ pytestmark = pytest.mark.gpu
 def test_gemm_matches_reference(M, N, K, two_a):
     from vvli_b200 import _abi
     err = ctypes.c_float(0)
-    st = _abi.lib().vvli_cuda_gemm_selftest(0, M, N, K, two_a, 7, ctypes.byref(err))
+    st = _abi.lib().vvli_cuda_gemm_selftest(0, 0, M, N, K, two_a, 7, ctypes.byref(err))
     assert st == 0, _abi.lib().vvli_cuda_last_error()
     assert err.value < 1e-4, err.value  # fp32 accumulation over up to 14336 terms
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (1, 256, 64),        # one row, one k-block, no split
+    (5, 4096, 4096),     # 32 weight tiles: K split over clusters of 4
+    (16, 6144, 4096),    # Llama-3-8B q|k|v, clusters of 3
+    (17, 4096, 14336),   # 32-row MMA, long K (down_proj) split 4 ways
+    (32, 28672, 4096),   # gate|up sized, 224 tiles, no split
+    (8, 1152, 896),      # Qwen q|k|v: 9 tiles, clusters of 8 over 14 k-blocks
+    (3, 130, 64),        # ragged weight tile
+])
+def test_decode_batch_gemm_matches_reference(M, N, K):
+    from vvli_b200 import _abi
+    err = ctypes.c_float(0)
+    st = _abi.lib().vvli_cuda_gemm_selftest(0, 1, M, N, K, 1, 11, ctypes.byref(err))
+    assert st == 0, _abi.lib().vvli_cuda_last_error()
+    assert err.value < 1e-4, err.value

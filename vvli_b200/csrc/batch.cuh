@@ -1,0 +1,33 @@
+// batch.cuh - SIMT kernels of a decode batch (see batch_decode.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vvli {
+
+struct BatchAttnParams {
+  const float* q;          // [B][nq * d] rotated q of every row
+  const float* k_cache;    // this layer: [pages][nkv][kPage][d]
+  const float* v_cache;
+  const int* page_table;   // row b uses page_table[b * seq_pages ..]
+  int seq_pages;
+  const int* row_pos;      // [B] position of each row's token
+  float* part;             // [B][nq][splits][d + 2] partial (o, max, sum)
+  unsigned* counters;      // [B][nkv], zero between launches
+  uint16_t* out_hi;        // [B][nq * d] bf16 hi / lo of the attention output
+  uint16_t* out_lo;
+  int nq, nkv, d, group, splits;
+  float inv_sqrt_d;
+};
+
+size_t batch_attention_smem(int group, int d);
+cudaError_t launch_batch_attention(const BatchAttnParams& p, int B, cudaStream_t s);
+// Per-row llm.argmax of B rows of n logits (row stride ld, indices offset by row_base):
+// best[2b] = value, best[2b+1] = index bits.
+cudaError_t launch_rows_argmax(const float* logits, int B, int n, int ld, int row_base, float* best, cudaStream_t s);
+// Winner per row over `ranks` gathered best arrays ([ranks][B][2]).
+cudaError_t launch_rows_argmax_merge(const float* all, int ranks, int B, int* out, cudaStream_t s);
+cudaError_t launch_rows_argmax_index(const float* best, int B, int* out, cudaStream_t s);
+
+}  // namespace vvli

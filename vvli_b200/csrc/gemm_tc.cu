@@ -24,6 +24,7 @@
 
 #include "device_fns.cuh"
 #include "gemm_tc.cuh"
+#include "tc_ptx.cuh"
 
 namespace vvli {
 
@@ -34,66 +35,8 @@ constexpr uint32_t kStageBytes = 2 * kTileA + kTileB;  // A_hi | A_lo | B
 constexpr int kGemmThreads = 192;
 constexpr uint32_t kTmemCols = 256;
 
-// ---------------------------------------------------------------- PTX wrappers
-VVLI_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-VVLI_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-VVLI_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major operand tile, 128-byte swizzle: rows of 128 bytes, 8-row groups of
-// 1024 bytes (stride byte offset), descriptor version 1, layout SWIZZLE_128B.
-VVLI_DEV uint64_t umma_desc(uint32_t smem_addr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((smem_addr & 0x3FFFF) >> 4);
-  d |= static_cast<uint64_t>(16 >> 4) << 16;    // leading byte offset (unused for swizzled K-major)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset: next 8-row group
-  d |= static_cast<uint64_t>(1) << 46;          // descriptor version
-  d |= static_cast<uint64_t>(2) << 61;          // SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor: D fp32, A and B bf16, both K-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(kGemmBN) >> 3) << 17) |
-                            ((static_cast<uint32_t>(kGemmBM) >> 4) << 24);
-
-VVLI_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
-      : "memory");
-}
-
-VVLI_DEV void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-VVLI_DEV void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-VVLI_DEV void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
-  hi = f32_to_bf16(v);
-  lo = f32_to_bf16(v - bf16_to_f32(hi));
-}
+// Instruction descriptor: N = 256, M = 128.
+constexpr uint32_t kIdesc = umma_idesc(kGemmBM, kGemmBN);
 
 // ---------------------------------------------------------------- GEMM kernel
 template <int EPI>
@@ -164,8 +107,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int k = 0; k < kGemmBK / 16; ++k) {  // UMMA_K = 16 bf16 = 32 bytes
           const uint64_t bdesc = umma_desc(st + 2 * kTileA + k * 32);
-          umma_bf16(tmem, umma_desc(st + k * 32), bdesc, (kb | k) != 0);
-          if (p.two_a) umma_bf16(tmem, umma_desc(st + kTileA + k * 32), bdesc, 1u);
+          umma_bf16(tmem, umma_desc(st + k * 32), bdesc, kIdesc, (kb | k) != 0);
+          if (p.two_a) umma_bf16(tmem, umma_desc(st + kTileA + k * 32), bdesc, kIdesc, 1u);
         }
         umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
       }
@@ -175,7 +118,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int wq = warp & 3;
     const int row = m0 + wq * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-    if (mbar_wait(tmem_full, 0, p.err)) {
+    // tcgen05.ld is warp-collective: the warp goes on only if every lane saw the accumulator.
+    if (__all_sync(0xffffffffu, mbar_wait(tmem_full, 0, p.err))) {
       tc_fence_after();
       float v[32];
       if constexpr (EPI == GE_SILU) {
@@ -501,12 +445,13 @@ __global__ void max_rel_err_kernel(const float* a, const float* b, size_t n, flo
 
 // Runs C = A . W^T through the tensor-core GEMM and a SIMT fp64-accumulating
 // reference on random data; *max_rel_err = max |C - ref| / max |ref|.
-cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err) {
+cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int skinny, uint64_t seed, float* max_rel_err) {
   cudaError_t e;
   int dev = 0, optin = 0;
   if ((e = cudaGetDevice(&dev))) return e;
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if ((e = configure_gemm_tc(optin))) return e;
+  if (skinny && (M > kSkinnyMaxRows || (e = configure_gemm_skinny(optin)))) return e ? e : cudaErrorInvalidValue;
   uint16_t *ahi = nullptr, *alo = nullptr, *w = nullptr;
   float *c = nullptr, *ref = nullptr, *err_out = nullptr;
   int* err = nullptr;
@@ -525,7 +470,8 @@ cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, uint64_t seed, floa
   fill_bf16_kernel<<<256, 256>>>(alo, static_cast<size_t>(M) * K, seed * 3 + 2, 1.0f / 256);
   fill_bf16_kernel<<<256, 256>>>(w, static_cast<size_t>(N) * K, seed * 3 + 3, 0.05f);
   CUtensorMap mhi, mlo, mw;
-  if ((e = make_tmap_bf16(&mhi, ahi, M, K, kGemmBM)) || (e = make_tmap_bf16(&mlo, alo, M, K, kGemmBM)) ||
+  const uint32_t box_a = skinny ? static_cast<uint32_t>(skinny_nb(M)) : static_cast<uint32_t>(kGemmBM);
+  if ((e = make_tmap_bf16(&mhi, ahi, M, K, box_a)) || (e = make_tmap_bf16(&mlo, alo, M, K, box_a)) ||
       (e = make_tmap_bf16(&mw, w, N, K, kGemmBN / 2))) {
     cleanup();
     return e;
@@ -533,7 +479,9 @@ cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, uint64_t seed, floa
   GemmParams p{};
   p.M = M, p.N = N, p.K = K, p.nk = (K + kGemmBK - 1) / kGemmBK, p.two_a = two_a, p.epi = GE_RESID;
   p.y = c, p.ldy = N, p.add_residual = 0, p.err = err;
-  if ((e = launch_gemm_tc(mhi, mlo, mw, p, 0))) {
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if ((e = skinny ? launch_gemm_skinny(mhi, mlo, mw, p, skinny_split(N, p.nk, sms), 0) : launch_gemm_tc(mhi, mlo, mw, p, 0))) {
     cleanup();
     return e;
   }

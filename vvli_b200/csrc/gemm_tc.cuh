@@ -37,6 +37,10 @@ struct GemmParams {
   uint16_t* out_lo;
   int ld_out;
   int* err;              // VVLI_ERR_TIMEOUT on a bounded wait giving up
+  // decode batches (gemm_skinny, GE_QKV): row b is sequence slot b at position row_pos[b];
+  // its pages are page_table[b * seq_pages ..]
+  const int* row_pos;
+  int seq_pages;
 };
 
 // Encodes a 2-D bf16 tensor map [rows, cols] (cols contiguous) with a
@@ -46,7 +50,17 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, ui
 cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& w,
                            const GemmParams& p, cudaStream_t s);
 cudaError_t configure_gemm_tc(int max_smem_optin);
-cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err);
+cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int skinny, uint64_t seed, float* max_rel_err);
+
+// Decode-batch GEMM (B <= kSkinnyMaxRows activation rows): C[B, N] = X[B, K] . W[N, K]^T with the
+// weight rows as the MMA's M operand.  X maps: box {64, skinny_nb(B)} rows; W map: box {64, 128}.
+// `split` CTAs of a cluster share K (skinny_split picks it).
+constexpr int kSkinnyMaxRows = 32;
+int skinny_nb(int M);
+int skinny_split(int N, int nk, int sm_count);
+cudaError_t launch_gemm_skinny(const CUtensorMap& x_hi, const CUtensorMap& x_lo, const CUtensorMap& w,
+                               const GemmParams& p, int split, cudaStream_t s);
+cudaError_t configure_gemm_skinny(int max_smem_optin);
 
 // Prefill helpers (SIMT): embedding gather, RMSNorm into bf16 hi/lo, causal attention.
 cudaError_t launch_prefill_embed(const uint16_t* table, const int* tokens, int M, int h, float* x, cudaStream_t s);

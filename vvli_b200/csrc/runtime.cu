@@ -21,6 +21,7 @@
 
 #include "../../include/vvli_cuda.h"
 #include "gemm_tc.cuh"
+#include "batch.cuh"
 #include "kernels.h"
 #include "sampler.cuh"
 
@@ -203,6 +204,16 @@ struct vvli_ctx {
   int* pf_tokens = nullptr;
   CUtensorMap tm_ah_hi{}, tm_ah_lo{}, tm_aq_hi{}, tm_aq_lo{}, tm_f_hi{}, tm_f_lo{};
   std::vector<CUtensorMap> tm_w;  // per layer: q|k|v, o, gate|up, down
+  // decode batches (allocated on first use): chunks of up to kSkinnyMaxRows rows
+  bool bt_ready = false;
+  int bt_splits_max = 0;
+  float *bt_x = nullptr, *bt_q = nullptr, *bt_logits = nullptr, *bt_best = nullptr, *bt_all_best = nullptr,
+        *bt_part = nullptr, *bt_logits_all = nullptr;
+  uint16_t *bt_ahi = nullptr, *bt_alo = nullptr, *bt_fhi = nullptr, *bt_flo = nullptr;
+  int *bt_tokens = nullptr, *bt_pos = nullptr, *bt_idx = nullptr;
+  unsigned* bt_counters = nullptr;
+  CUtensorMap tmb_h[2][2]{}, tmb_q[2][2]{}, tmb_f[2][2]{};  // [nb 16 / 32][hi / lo]
+  CUtensorMap tm_lm{};
   // device sampler (allocated on first use)
   unsigned* smp_stamp = nullptr;
   unsigned* smp_key32 = nullptr;
@@ -712,6 +723,135 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start) 
   return enqueue_lm_head(c, s, false);
 }
 
+// ---------------------------------------------------------------- decode batches
+// Buffers and tensor maps of a batch chunk (kSkinnyMaxRows rows), allocated on first use.
+int ensure_batch_buffers(vvli_ctx* c) {
+  if (c->bt_ready) return VVLI_OK;
+  constexpr int R = kSkinnyMaxRows;
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device);
+  CK(configure_gemm_skinny(optin));
+  if (c->tm_w.empty()) {
+    const int st0 = plan_tc_prefill(c);
+    if (st0) return st0;
+  }
+  const size_t ka = std::max(c->h, c->q_rows);
+  c->bt_splits_max = 16;
+  int st;
+  if ((st = dalloc(&c->bt_x, static_cast<size_t>(R) * c->h)) || (st = dalloc(&c->bt_q, static_cast<size_t>(R) * c->q_rows)) ||
+      (st = dalloc(&c->bt_ahi, R * ka)) || (st = dalloc(&c->bt_alo, R * ka)) ||
+      (st = dalloc(&c->bt_fhi, static_cast<size_t>(R) * c->I_l)) || (st = dalloc(&c->bt_flo, static_cast<size_t>(R) * c->I_l)) ||
+      (st = dalloc(&c->bt_logits, static_cast<size_t>(R) * c->V_l)) ||
+      (st = dalloc(&c->bt_logits_all, c->tp_size > 1 ? static_cast<size_t>(R) * c->V_l * c->tp_size : 1)) ||
+      (st = dalloc(&c->bt_best, 2 * R)) || (st = dalloc(&c->bt_all_best, 2 * R * c->tp_size)) ||
+      (st = dalloc(&c->bt_part, static_cast<size_t>(R) * c->nq_l * c->bt_splits_max * (c->d + 2))) ||
+      (st = dalloc(&c->bt_tokens, R)) || (st = dalloc(&c->bt_pos, R)) || (st = dalloc(&c->bt_idx, R)) ||
+      (st = dalloc(&c->bt_counters, static_cast<size_t>(R) * c->nkv_l)))
+    return st;
+  cudaError_t e;
+  for (int v = 0; v < 2; ++v) {
+    const uint32_t nb = v == 0 ? 16 : 32;
+    if ((e = make_tmap_bf16(&c->tmb_h[v][0], c->bt_ahi, R, c->h, nb)) ||
+        (e = make_tmap_bf16(&c->tmb_h[v][1], c->bt_alo, R, c->h, nb)) ||
+        (e = make_tmap_bf16(&c->tmb_q[v][0], c->bt_ahi, R, c->q_rows, nb)) ||
+        (e = make_tmap_bf16(&c->tmb_q[v][1], c->bt_alo, R, c->q_rows, nb)) ||
+        (e = make_tmap_bf16(&c->tmb_f[v][0], c->bt_fhi, R, c->I_l, nb)) ||
+        (e = make_tmap_bf16(&c->tmb_f[v][1], c->bt_flo, R, c->I_l, nb)))
+      return cuda_fail(e, "make_tmap_bf16 (batch activations)");
+  }
+  if ((e = make_tmap_bf16(&c->tm_lm, c->w + c->off_lm, c->V_lr, c->h, 128)))
+    return cuda_fail(e, "make_tmap_bf16 (lm head)");
+  c->bt_ready = true;
+  return VVLI_OK;
+}
+
+// One chunk of B <= kSkinnyMaxRows rows (row b = sequence slot `slot0 + b`):
+// every linear layer is one skinny tensor-core GEMM that reads its weights
+// once for the whole chunk.  Leaves logits in bt_logits [B][V_l] and the
+// per-row argmax in bt_idx.
+int forward_batch_chunk(vvli_ctx* c, const uint32_t* tokens, const uint64_t* positions, int B, int slot0) {
+  cudaStream_t s = c->stream;
+  const uint16_t* W = c->w;
+  const bool tp = c->tp_size > 1;
+  int* err = &c->st->err;
+  const int pps = static_cast<int>((c->max_seq + kPage - 1) / kPage);  // pages per sequence slot
+  std::vector<int> hbuf(2 * B);
+  int max_pos = 0;
+  for (int b = 0; b < B; ++b) {
+    hbuf[b] = static_cast<int>(tokens[b]);
+    hbuf[B + b] = static_cast<int>(positions[b]);
+    max_pos = std::max(max_pos, hbuf[B + b]);
+  }
+  CK(cudaMemcpyAsync(c->bt_tokens, hbuf.data(), B * sizeof(int), cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(c->bt_pos, hbuf.data() + B, B * sizeof(int), cudaMemcpyHostToDevice, s));
+  const int v = skinny_nb(B) == 16 ? 0 : 1;
+  RopeParams rope{c->cfg.rope_theta, VVLI_ROPE_INTERLEAVED, static_cast<int>(c->cfg.rope_scaling_type),
+                  c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
+                  static_cast<float>(c->cfg.rope_original_max_position)};
+  // Attention splits: about two CTAs per SM over (row, kv head), at least 64 positions each.
+  const int want = std::max(1, (2 * c->sm_count) / std::max(1, B * c->nkv_l));
+  const int splits = std::max(1, std::min({c->bt_splits_max, want, (max_pos + 1 + 63) / 64}));
+  auto gemm = [&](const CUtensorMap* x, const CUtensorMap& w, GemmParams g) -> int {
+    g.M = B, g.two_a = 1, g.err = err, g.nk = (g.K + kGemmBK - 1) / kGemmBK;
+    const int n_rows = g.N;
+    CK(launch_gemm_skinny(x[0], x[1], w, g, skinny_split(n_rows, g.nk, c->sm_count), s));
+    return VVLI_OK;
+  };
+  int st;
+  CK(launch_prefill_embed(W + c->off_emb, c->bt_tokens, B, c->h, c->bt_x, s));
+  for (int l = 0; l < c->L; ++l) {
+    const DevLayer& D = c->lay[l];
+    float* kc = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
+    float* vc = kc + c->kv_layer_floats;
+    CK(launch_norm_split(c->bt_x, W + D.in_norm, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s));
+    GemmParams q{};
+    q.N = c->q_rows + 2 * c->kv_rows, q.K = c->h, q.epi = GE_QKV, q.y = c->bt_q, q.ldy = c->q_rows;
+    q.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv;
+    q.q_rows = c->q_rows, q.kv_rows = c->kv_rows, q.d = c->d, q.nkv = c->nkv_l, q.rope = rope;
+    q.k_cache = kc, q.v_cache = vc, q.page_table = c->page_table + static_cast<size_t>(slot0) * pps;
+    q.row_pos = c->bt_pos, q.seq_pages = pps;
+    if ((st = gemm(c->tmb_h[v], c->tm_w[4 * l + 0], q))) return st;
+    BatchAttnParams a{};
+    a.q = c->bt_q, a.k_cache = kc, a.v_cache = vc, a.page_table = c->page_table + static_cast<size_t>(slot0) * pps;
+    a.seq_pages = pps, a.row_pos = c->bt_pos, a.part = c->bt_part, a.counters = c->bt_counters;
+    a.out_hi = c->bt_ahi, a.out_lo = c->bt_alo, a.nq = c->nq_l, a.nkv = c->nkv_l, a.d = c->d, a.group = c->group;
+    a.splits = splits, a.inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
+    CK(launch_batch_attention(a, B, s));
+    GemmParams o{};
+    o.N = c->h, o.K = c->q_rows, o.epi = GE_RESID, o.y = c->bt_x, o.ldy = c->h, o.add_residual = c->tp_rank == 0;
+    if ((st = gemm(c->tmb_q[v], c->tm_w[4 * l + 1], o))) return st;
+    if (tp && (st = nccl_wait(c, nccl().AllReduce(c->bt_x, c->bt_x, static_cast<size_t>(B) * c->h, ncclFloat32,
+                                                   ncclSum, c->comm, s), "allreduce")))
+      return st;
+    CK(launch_norm_split(c->bt_x, W + D.post, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s));
+    GemmParams gu{};
+    gu.N = c->I_l, gu.K = c->h, gu.epi = GE_SILU, gu.pair_offset = c->I_l;
+    gu.out_hi = c->bt_fhi, gu.out_lo = c->bt_flo, gu.ld_out = c->I_l;
+    if ((st = gemm(c->tmb_h[v], c->tm_w[4 * l + 2], gu))) return st;
+    GemmParams dn{};
+    dn.N = c->h, dn.K = c->I_l, dn.epi = GE_RESID, dn.y = c->bt_x, dn.ldy = c->h, dn.add_residual = c->tp_rank == 0;
+    if ((st = gemm(c->tmb_f[v], c->tm_w[4 * l + 3], dn))) return st;
+    if (tp && (st = nccl_wait(c, nccl().AllReduce(c->bt_x, c->bt_x, static_cast<size_t>(B) * c->h, ncclFloat32,
+                                                   ncclSum, c->comm, s), "allreduce")))
+      return st;
+  }
+  // final norm + LM head of every row (src/llm.zig:727-728), then llm.argmax per row
+  CK(launch_norm_split(c->bt_x, W + c->off_final, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s));
+  GemmParams lm{};
+  lm.N = c->V_lr, lm.K = c->h, lm.epi = GE_RESID, lm.y = c->bt_logits, lm.ldy = c->V_l, lm.add_residual = 0;
+  if ((st = gemm(c->tmb_h[v], c->tm_lm, lm))) return st;
+  CK(launch_rows_argmax(c->bt_logits, B, c->V_lr, c->V_l, c->v0, c->bt_best, s));  // this rank's real rows only
+  if (tp) {
+    if ((st = nccl_wait(c, nccl().AllGather(c->bt_best, c->bt_all_best, 2 * static_cast<size_t>(B), ncclFloat32, c->comm, s),
+                        "allgather")))
+      return st;
+    CK(launch_rows_argmax_merge(c->bt_all_best, c->tp_size, B, c->bt_idx, s));
+  } else {
+    CK(launch_rows_argmax_index(c->bt_best, B, c->bt_idx, s));
+  }
+  return VVLI_OK;
+}
+
 int build_graph(vvli_ctx* c) {
   if (c->graph) {
     cudaGraphExecDestroy(c->graph);
@@ -806,7 +946,9 @@ void free_ctx(vvli_ctx* c) {
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
                  c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->pf_x, c->pf_q,
                  c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->smp_stamp, c->smp_key32,
-                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_recent, c->smp_state, c->smp_temp};
+                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_recent, c->smp_state, c->smp_temp,
+                 c->bt_x, c->bt_q, c->bt_logits, c->bt_best, c->bt_all_best, c->bt_part, c->bt_logits_all, c->bt_ahi,
+                 c->bt_alo, c->bt_fhi, c->bt_flo, c->bt_tokens, c->bt_pos, c->bt_idx, c->bt_counters};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (c->h_st) cudaFreeHost(c->h_st);
@@ -1119,6 +1261,71 @@ int vvli_cuda_prefill(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t 
   return VVLI_OK;
 }
 
+int vvli_cuda_forward_batch(vvli_ctx* c, const uint32_t* tokens, const uint64_t* positions, uint64_t B,
+                            float* logits_out, uint32_t* argmax_out) {
+  if (!c || (B && (!tokens || !positions))) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (B == 0) return VVLI_OK;
+  if (B > c->max_batch) {
+    g_last_error = "batch of " + std::to_string(B) + " rows exceeds the context's max_batch " + std::to_string(c->max_batch);
+    return VVLI_ERR_INVALID_ARGUMENT;
+  }
+  for (uint64_t b = 0; b < B; ++b) {
+    if (tokens[b] >= c->cfg.vocab_size) return VVLI_ERR_INVALID_TOKEN;  // src/llm.zig:704
+    if (positions[b] >= c->max_seq) return VVLI_ERR_CONTEXT_FULL;     // src/llm.zig:705
+  }
+  if (c->group * c->d > 1024 || c->d % 4) {
+    g_last_error = "decode batch: q heads per kv head x head_dim above 1024";
+    return VVLI_ERR_UNIMPLEMENTED;
+  }
+  CK(cudaSetDevice(c->device));
+  int st;
+  if ((st = ensure_batch_buffers(c))) return st;
+  cudaStream_t s = c->stream;
+  CK(cudaMemsetAsync(&c->st->err, 0, sizeof(int), s));
+  CK(cudaEventRecord(c->ev0, s));
+  const size_t V = c->V;
+  for (uint64_t b0 = 0; b0 < B; b0 += kSkinnyMaxRows) {
+    const int n = static_cast<int>(std::min<uint64_t>(kSkinnyMaxRows, B - b0));
+    if ((st = forward_batch_chunk(c, tokens + b0, positions + b0, n, static_cast<int>(b0)))) return st;
+    if (logits_out) {
+      float* dst = logits_out + b0 * V;
+      if (c->tp_size > 1) {
+        if ((st = nccl_wait(c, nccl().AllGather(c->bt_logits, c->bt_logits_all, static_cast<size_t>(n) * c->V_l,
+                                                ncclFloat32, c->comm, s), "allgather logits")))
+          return st;
+        for (int r = 0; r < c->tp_size; ++r) {
+          const int vr = std::max(0, std::min(c->V, (r + 1) * c->V_l) - r * c->V_l);
+          if (vr == 0) continue;
+          CK(cudaMemcpy2DAsync(dst + static_cast<size_t>(r) * c->V_l, V * 4,
+                               c->bt_logits_all + static_cast<size_t>(r) * n * c->V_l, static_cast<size_t>(c->V_l) * 4,
+                               static_cast<size_t>(vr) * 4, n, cudaMemcpyDeviceToHost, s));
+        }
+      } else {
+        CK(cudaMemcpy2DAsync(dst, V * 4, c->bt_logits, static_cast<size_t>(c->V_l) * 4, V * 4, n, cudaMemcpyDeviceToHost, s));
+      }
+    }
+    CK(cudaMemcpyAsync(c->h_tok, c->bt_idx, n * sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (argmax_out)
+      for (int b = 0; b < n; ++b) argmax_out[b0 + b] = static_cast<uint32_t>(c->h_tok[b]);
+  }
+  CK(cudaEventRecord(c->ev1, s));
+  int err = 0;
+  CK(cudaMemcpyAsync(&c->h_st->err, &c->st->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  err = c->h_st->err;
+  if (err) {
+    c->h_st->err = 0;
+    CK(cudaMemsetAsync(&c->st->err, 0, sizeof(int), s));
+    CK(cudaStreamSynchronize(s));
+    g_last_error = "decode batch: a bounded wait gave up";
+    return err;
+  }
+  cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
+  return VVLI_OK;
+}
+
 int vvli_cuda_generate_greedy(vvli_ctx* c, const uint32_t* prompt, uint64_t n_prompt, uint64_t max_new, int64_t eos,
                               uint32_t* out, uint64_t* out_count, vvli_generate_stats* stats) {
   if (!c || !out_count || (!out && max_new) || (!prompt && n_prompt)) return VVLI_ERR_INVALID_ARGUMENT;
@@ -1392,10 +1599,13 @@ int vvli_cuda_trace(vvli_ctx* c, uint64_t* out, uint64_t cap, uint64_t* count) {
   return VVLI_OK;
 }
 
-int vvli_cuda_gemm_selftest(int device, int M, int N, int K, int two_a, uint64_t seed, float* max_rel_err) {
-  if (!max_rel_err || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 2) return VVLI_ERR_INVALID_ARGUMENT;
+int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two_a, uint64_t seed,
+                            float* max_rel_err) {
+  if (!max_rel_err || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 2 || kernel < 0 || kernel > 1 ||
+      (kernel == 1 && M > kSkinnyMaxRows))
+    return VVLI_ERR_INVALID_ARGUMENT;
   CK(cudaSetDevice(device));
-  cudaError_t e = gemm_tc_selftest(M, N, K, two_a, seed, max_rel_err);
+  cudaError_t e = gemm_tc_selftest(M, N, K, two_a, kernel, seed, max_rel_err);
   if (e == cudaErrorTimeout) {
     g_last_error = "tensor-core GEMM: a bounded wait gave up";
     return VVLI_ERR_TIMEOUT;

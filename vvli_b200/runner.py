@@ -108,6 +108,23 @@ class Runner:
         self.last_argmax = int(am.value)
         return out
 
+    def forward_batch(self, tokens, positions, logits: bool = True):
+        """One decode step of len(tokens) sequences: row b is sequence slot b at positions[b].
+
+        Returns (logits [B, vocab] or None, argmax list).
+        """
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint64)
+        if t.size != p.size:
+            raise ValueError("tokens and positions differ in length")
+        out = np.empty((t.size, self.cfg.vocab_size), dtype=np.float32) if logits else None
+        am = np.zeros(max(1, t.size), dtype=np.uint32)
+        check(_abi.lib().vvli_cuda_forward_batch(self._ctx, t.ctypes.data_as(_u32p),
+                                                 p.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), t.size,
+                                                 None if out is None else out.ctypes.data_as(_f32p),
+                                                 am.ctypes.data_as(_u32p)))
+        return out, am[: t.size].tolist()
+
     def generate_greedy(self, prompt, max_new_tokens: int, eos_token_id: int | None = None):
         """On-device greedy loop; returns (tokens, vvli_generate_stats)."""
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
