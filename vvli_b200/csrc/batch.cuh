@@ -18,16 +18,21 @@ struct BatchAttnParams {
   uint16_t* out_hi;        // [B][nq * d] bf16 hi / lo of the attention output
   uint16_t* out_lo;
   int nq, nkv, d, group, splits;
+  int nslots;              // pages in flight per CTA (batch_attention_slots)
   float inv_sqrt_d;
+  int* err;                // VVLI_ERR_TIMEOUT when a page copy never lands
 };
 
-size_t batch_attention_smem(int group, int d);
-cudaError_t launch_batch_attention(const BatchAttnParams& p, int B, cudaStream_t s);
+int batch_attention_slots(int d);
+size_t batch_attention_smem(int group, int d, int slots);
+// pdl: programmatic edge to the previous kernel (earlier pages are fetched before the wait).
+cudaError_t launch_batch_attention(const BatchAttnParams& p, int B, cudaStream_t s, bool pdl = false);
 // Per-row llm.argmax of B rows of n logits (row stride ld, indices offset by row_base):
 // best[2b] = value, best[2b+1] = index bits.
-cudaError_t launch_rows_argmax(const float* logits, int B, int n, int ld, int row_base, float* best, cudaStream_t s);
+cudaError_t launch_rows_argmax(const float* logits, int B, int n, int ld, int row_base, float* best, cudaStream_t s,
+                               bool pdl = false);
 // Winner per row over `ranks` gathered best arrays ([ranks][B][2]).
 cudaError_t launch_rows_argmax_merge(const float* all, int ranks, int B, int* out, cudaStream_t s);
-cudaError_t launch_rows_argmax_index(const float* best, int B, int* out, cudaStream_t s);
+cudaError_t launch_rows_argmax_index(const float* best, int B, int* out, cudaStream_t s, bool pdl = false);
 
 }  // namespace vvli

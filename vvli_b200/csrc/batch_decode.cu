@@ -8,6 +8,8 @@
 // positions over `splits` CTAs per (row, kv head), and the last CTA to finish
 // merges the partial (o, max, sum) triples.  The output is written as the
 // bf16 hi / lo pair the o_proj GEMM reads.
+#include <algorithm>
+
 #include "batch.cuh"
 #include "device_fns.cuh"
 
@@ -16,7 +18,8 @@ namespace vvli {
 namespace {
 
 constexpr int kBaThreads = 256;
-constexpr int kBaTile = 64;
+constexpr int kBaTile = kPage;  // positions per tile: one KV page
+constexpr int kBaMaxSlots = 8;
 
 VVLI_DEV void split_pair(float v, uint16_t* hi, uint16_t* lo) {
   const uint16_t h = f32_to_bf16(v);
@@ -24,51 +27,101 @@ VVLI_DEV void split_pair(float v, uint16_t* hi, uint16_t* lo) {
   *lo = f32_to_bf16(v - bf16_to_f32(h));
 }
 
+// CTA = (split s, kv head g, row b).  Split s owns a contiguous range of the
+// row's 64-position pages; each page's K and V rows ([kPage][d] fp32, one
+// contiguous block per kv head) arrive with two cp.async.bulk copies into a
+// ring of `nslots` shared-memory slots, so several pages per SM are in flight
+// while the oldest is computed.  Scores: a warp takes 8 positions, its lanes
+// split the head dimension and meet with butterfly shuffles; P.V: one
+// (head, dim) output per thread.
 __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const BatchAttnParams p) {
-  extern __shared__ float sm[];
-  const int G = p.group, d = p.d;
-  float* qs = sm;                // [G][d]
-  float* sc = qs + G * d;        // [G][kBaTile]
+  extern __shared__ __align__(128) float sm[];
+  const int G = p.group, d = p.d, nslot = p.nslots;
+  const int page_floats = kPage * d;
+  float* kv = sm;                              // [nslot][K | V][kPage][d]
+  float* qs = kv + nslot * 2 * page_floats;    // [G][d]
+  float* sc = qs + G * d;                      // [G][kBaTile]
   float* mrun = sc + G * kBaTile;
   float* lrun = mrun + G;
   float* alpha = lrun + G;
+  __shared__ __align__(8) uint64_t bar[kBaMaxSlots];
   __shared__ int last_flag;
   const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pos = p.row_pos[b];
   const int n_ctx = pos + 1;
-  const int chunk = (n_ctx + p.splits - 1) / p.splits;
-  const int t_begin = s * chunk, t_end = min(n_ctx, t_begin + chunk);
+  const int np = (n_ctx + kPage - 1) / kPage;
+  const int per = (np + p.splits - 1) / p.splits;
+  const int p_begin = min(np, s * per), p_end = min(np, p_begin + per);
   const int* pt = p.page_table + static_cast<size_t>(b) * p.seq_pages;
   const int qd = p.nq * d;
+  grid_launch_dependents();
+  if (tid == 0) {
+    for (int i = 0; i < nslot; ++i) mbar_init(&bar[i], 1);
+    fence_barrier_init();
+  }
+  auto issue = [&](int page, int slot) {  // thread 0
+    const int rows = min(kPage, n_ctx - page * kPage);
+    const uint32_t bytes = static_cast<uint32_t>(rows * d * 4);
+    const size_t off = kv_off(pt, page * kPage, g, p.nkv, d);
+    float* kb = kv + static_cast<size_t>(slot) * 2 * page_floats;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier reads of the slot come first
+    mbar_arrive_expect_tx(&bar[slot], 2 * bytes);
+    bulk_g2s(kb, p.k_cache + off, bytes, &bar[slot]);
+    bulk_g2s(kb + page_floats, p.v_cache + off, bytes, &bar[slot]);
+  };
+  int issued = 0, waited = 0;
+  // Pages before the row's last one hold earlier positions only, which the
+  // previous kernel (the q|k|v GEMM writing position `pos`) does not touch:
+  // they are fetched before the dependency wait.
+  if (tid == 0)
+    for (; issued < nslot && p_begin + issued < min(p_end, np - 1); ++issued) issue(p_begin + issued, issued);
+  grid_dependency_wait();
   for (int i = tid; i < G * d; i += kBaThreads) qs[i] = p.q[static_cast<size_t>(b) * qd + static_cast<size_t>(g * G) * d + i];
   for (int i = tid; i < G; i += kBaThreads) {
     mrun[i] = -INFINITY;
     lrun[i] = 0.f;
   }
   __syncthreads();
-  const int nacc = (G * d + kBaThreads - 1) / kBaThreads;  // <= 4 (G <= 8, d <= 128)
+  if (tid == 0)
+    for (; issued < nslot && p_begin + issued < p_end; ++issued) issue(p_begin + issued, issued);
+  const int nacc = (G * d + kBaThreads - 1) / kBaThreads;  // <= 4 (G * d <= 1024)
+  const int dpl = (d + 31) / 32;                             // dims per lane (d <= 128)
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int t0 = t_begin; t0 < t_end; t0 += kBaTile) {
-    const int n = min(kBaTile, t_end - t0);
-    // scores: one (head, position) per thread
-    for (int i = tid; i < G * kBaTile; i += kBaThreads) {
-      const int hh = i / kBaTile, j = i % kBaTile;
-      float v = -INFINITY;
-      if (j < n) {
-        const float4* kr = reinterpret_cast<const float4*>(p.k_cache + kv_off(pt, t0 + j, g, p.nkv, d));
-        const float4* qh = reinterpret_cast<const float4*>(qs + hh * d);
-        float dot = 0.f;
-        for (int e = 0; e < d / 4; ++e) {
-          const float4 kk = kr[e], qq = qh[e];
-          dot = fmaf(qq.x, kk.x, dot);
-          dot = fmaf(qq.y, kk.y, dot);
-          dot = fmaf(qq.z, kk.z, dot);
-          dot = fmaf(qq.w, kk.w, dot);
+  bool ok = true;
+  for (int page = p_begin, it = 0; page < p_end; ++page, ++it) {
+    const int slot = it % nslot;
+    ok = __syncthreads_and(mbar_wait(&bar[slot], (it / nslot) & 1, p.err) ? 1 : 0) != 0;
+    ++waited;
+    if (!ok) break;
+    const int n = min(kPage, n_ctx - page * kPage);
+    const float* ks = kv + static_cast<size_t>(slot) * 2 * page_floats;
+    const float* vs = ks + page_floats;
+    // scores
+    for (int jj = 0; jj < kBaTile / (kBaThreads / 32); ++jj) {
+      const int j = warp * (kBaTile / (kBaThreads / 32)) + jj;
+      float kx[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) kx[k] = (k < dpl && j < n && lane + 32 * k < d) ? ks[j * d + lane + 32 * k] : 0.f;
+      float part[8];
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) {
+        part[hh] = 0.f;
+        if (hh < G) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (k < dpl && lane + 32 * k < d) part[hh] = fmaf(qs[hh * d + lane + 32 * k], kx[k], part[hh]);
         }
-        v = dot * p.inv_sqrt_d;
       }
-      sc[hh * kBaTile + j] = v;
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) {
+        if (hh < G) {
+          float v = part[hh];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0) sc[hh * kBaTile + j] = j < n ? v * p.inv_sqrt_d : -INFINITY;
+        }
+      }
     }
     __syncthreads();
     // online softmax, one warp per head (softmaxInPlace, src/llm.zig:1408-1419)
@@ -92,18 +145,29 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
       }
     }
     __syncthreads();
-    // P.V (addScaled, src/llm.zig:1398-1406): output element (head, dim) per thread
+    // P.V (addScaled, src/llm.zig:1398-1406)
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int idx = tid + k * kBaThreads;
       if (k < nacc && idx < G * d) {
         const int hh = idx / d, e = idx % d;
+        const float* pr = sc + hh * kBaTile;
         float a = 0.f;
-        for (int j = 0; j < n; ++j) a = fmaf(sc[hh * kBaTile + j], p.v_cache[kv_off(pt, t0 + j, g, p.nkv, d) + e], a);
+        for (int j = 0; j < n; ++j) a = fmaf(pr[j], vs[j * d + e], a);
         acc[k] = acc[k] * alpha[hh] + a;
       }
     }
     __syncthreads();
+    if (tid == 0 && p_begin + issued < p_end) {  // the slot is free again: next page into it
+      issue(p_begin + issued, slot);
+      ++issued;
+    }
+  }
+  if (!ok) {  // a copy that never landed: let the others in flight finish before exiting
+    if (tid == 0)
+      for (int i = waited; i < issued; ++i) mbar_wait(&bar[i % nslot], (i / nslot) & 1, p.err);
+    __syncthreads();
+    return;
   }
   const size_t out_row = static_cast<size_t>(b) * qd + static_cast<size_t>(g * G) * d;
   if (p.splits == 1) {
@@ -158,6 +222,8 @@ __global__ void __launch_bounds__(1024) rows_argmax_kernel(const float* logits, 
   __shared__ float wv[32];
   __shared__ int wi[32];
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  grid_launch_dependents();
+  grid_dependency_wait();
   const float* v = logits + static_cast<size_t>(b) * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
@@ -193,6 +259,7 @@ __global__ void __launch_bounds__(1024) rows_argmax_kernel(const float* logits, 
 
 // Under tensor parallelism: the winner over the ranks' (value, index) pairs of every row.
 __global__ void rows_argmax_merge_kernel(const float* all, int ranks, int B, int* out) {
+  grid_dependency_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   float bv = all[2 * b];
@@ -209,25 +276,49 @@ __global__ void rows_argmax_merge_kernel(const float* all, int ranks, int B, int
 }
 
 __global__ void rows_argmax_index_kernel(const float* best, int B, int* out) {
+  grid_dependency_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) out[b] = __float_as_int(best[2 * b + 1]);
 }
 
 }  // namespace
 
-size_t batch_attention_smem(int group, int d) {
-  return (static_cast<size_t>(group) * d + static_cast<size_t>(group) * kBaTile + 3 * group) * 4;
+int batch_attention_slots(int d) {
+  const int page_pair = 2 * kPage * d * 4;  // K and V of one page
+  return std::max(2, std::min(kBaMaxSlots, (200 * 1024) / page_pair));
 }
 
-cudaError_t launch_batch_attention(const BatchAttnParams& p, int B, cudaStream_t s) {
-  const dim3 grid(p.splits, p.nkv, B);
-  batch_attention_kernel<<<grid, kBaThreads, batch_attention_smem(p.group, p.d), s>>>(p);
-  return cudaGetLastError();
+size_t batch_attention_smem(int group, int d, int slots) {
+  return (2 * static_cast<size_t>(slots) * kPage * d + static_cast<size_t>(group) * d +
+          static_cast<size_t>(group) * kBaTile + 3 * group) * 4;
 }
 
-cudaError_t launch_rows_argmax(const float* logits, int B, int n, int ld, int row_base, float* best, cudaStream_t s) {
-  rows_argmax_kernel<<<B, 1024, 0, s>>>(logits, n, ld, row_base, best);
-  return cudaGetLastError();
+template <typename Kern, typename... Args>
+static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+cudaError_t launch_batch_attention(const BatchAttnParams& p, int B, cudaStream_t s, bool pdl) {
+  const size_t smem = batch_attention_smem(p.group, p.d, p.nslots);
+  cudaError_t e = cudaFuncSetAttribute(batch_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e) return e;
+  return launch_pdl(batch_attention_kernel, dim3(p.splits, p.nkv, B), dim3(kBaThreads), smem, s, pdl, p);
+}
+
+cudaError_t launch_rows_argmax(const float* logits, int B, int n, int ld, int row_base, float* best, cudaStream_t s,
+                               bool pdl) {
+  return launch_pdl(rows_argmax_kernel, dim3(B), dim3(1024), 0, s, pdl, logits, n, ld, row_base, best);
 }
 
 cudaError_t launch_rows_argmax_merge(const float* all, int ranks, int B, int* out, cudaStream_t s) {
@@ -235,9 +326,8 @@ cudaError_t launch_rows_argmax_merge(const float* all, int ranks, int B, int* ou
   return cudaGetLastError();
 }
 
-cudaError_t launch_rows_argmax_index(const float* best, int B, int* out, cudaStream_t s) {
-  rows_argmax_index_kernel<<<(B + 127) / 128, 128, 0, s>>>(best, B, out);
-  return cudaGetLastError();
+cudaError_t launch_rows_argmax_index(const float* best, int B, int* out, cudaStream_t s, bool pdl) {
+  return launch_pdl(rows_argmax_index_kernel, dim3((B + 127) / 128), dim3(128), 0, s, pdl, best, B, out);
 }
 
 }  // namespace vvli

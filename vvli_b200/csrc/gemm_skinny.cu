@@ -20,6 +20,8 @@
 // result does not depend on timing.  Every mbarrier wait is bounded and
 // reports VVLI_ERR_TIMEOUT through p.err; every thread reaches both cluster
 // barriers whatever happened before.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "device_fns.cuh"
@@ -56,16 +58,6 @@ VVLI_DEV uint32_t cluster_ctarank() {
 }
 VVLI_DEV void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-VVLI_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-VVLI_DEV float ld_dsmem(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
 }
 
 template <int NB>
@@ -121,11 +113,29 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   float acc[NB];
   float accu[kPair ? NB : 1];
   bool have = false;
+  grid_launch_dependents();  // the next kernel may start its own weight stream on free SMs
   if (warp == 0) {
     if (lane == 0) {  // ---- TMA producer
       const uint32_t bytes = L::w_bytes + (p.two_a ? 2 : 1) * L::tile_x;
-      int issued = 0;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      // The weights do not depend on the previous kernel: the first ring's
+      // worth goes out before the dependency wait, the activations after it.
+      const int pre = min(L::stages, kb1 - kb0);
+      for (int i = 0; i < pre; ++i) {
+        const uint32_t st = base + i * L::stage;
+        const int x = (kb0 + i) * kGemmBK;
+        mbar_arrive_expect_tx(&full[i], bytes);
+        tma_load_2d(st, &tm_w, x, r0, &full[i]);
+        if (kPair) tma_load_2d(st + kSkTileW, &tm_w, x, p.pair_offset + r0, &full[i]);
+      }
+      grid_dependency_wait();
+      for (int i = 0; i < pre; ++i) {
+        const uint32_t st = base + i * L::stage;
+        const int x = (kb0 + i) * kGemmBK;
+        tma_load_2d(st + L::w_bytes, &tm_x_hi, x, 0, &full[i]);
+        if (p.two_a) tma_load_2d(st + L::w_bytes + L::tile_x, &tm_x_lo, x, 0, &full[i]);
+      }
+      int issued = pre;
+      for (int kb = kb0 + pre; kb < kb1; ++kb) {
         const int i = kb - kb0, s = i % L::stages;
         if (i >= L::stages && !mbar_wait(&empty[s], ((i / L::stages) - 1) & 1, p.err)) break;
         mbar_arrive_expect_tx(&full[s], bytes);
@@ -166,6 +176,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       umma_commit(tmem_full);
     }
   } else {  // ---- epilogue warps: read this thread's weight row
+    grid_dependency_wait();  // the epilogue reads and writes the previous kernel's outputs
     const int wq = warp & 3;
     const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     // tcgen05.ld is warp-collective: the warp goes on only if every lane saw the accumulator.
@@ -192,13 +203,21 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
     cluster_sync_all();
     if (warp >= 2 && crank == 0) {
-      const uint32_t red_addr = smem_u32(red);
+      // Plain loads through the peers' generic shared-memory addresses: all of
+      // a peer's values are in flight together; peers are added in rank order.
+      cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
       for (int q = 1; q < S; ++q) {
-        const uint32_t peer = mapa_shared(red_addr, static_cast<uint32_t>(q));
+        const float* peer = cluster.map_shared_rank(red, static_cast<unsigned>(q));
+        float pv[NB], pu[kPair ? NB : 1];
 #pragma unroll
         for (int c = 0; c < NB; ++c) {
-          acc[c] += ld_dsmem(peer + static_cast<uint32_t>((c * kSkBM + row_local) * 4));
-          if constexpr (kPair) accu[c] += ld_dsmem(peer + static_cast<uint32_t>(((NB + c) * kSkBM + row_local) * 4));
+          pv[c] = peer[c * kSkBM + row_local];
+          if constexpr (kPair) pu[c] = peer[(NB + c) * kSkBM + row_local];
+        }
+#pragma unroll
+        for (int c = 0; c < NB; ++c) {
+          acc[c] += pv[c];
+          if constexpr (kPair) accu[c] += pu[c];
         }
       }
     }
@@ -230,7 +249,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       }
     } else {  // GE_QKV: batch row b is sequence slot b at position row_pos[b]
       const bool rot = r < p.q_rows + p.kv_rows;
-      const int even = r & ~1;
+      const float inv_freq = rot ? rope_inv_freq(p.rope, (r & ~1) % p.d, p.d) : 0.f;
       const float bias = (p.bias && r < p.N) ? bf16_to_f32(p.bias[r]) : 0.f;
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
@@ -240,7 +259,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const float other = __shfl_xor_sync(0xffffffffu, a, 1);  // the rotary partner row
         const int pos = p.row_pos[b];
         if (rot) {
-          const float ang = static_cast<float>(pos) * rope_inv_freq(p.rope, even % p.d, p.d);
+          const float ang = static_cast<float>(pos) * inv_freq;
           float sn, cs;
           sincosf(ang, &sn, &cs);
           a = (r & 1) ? other * sn + a * cs : a * cs - other * sn;
@@ -269,49 +288,84 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 
 template <int EPI, int NB>
 cudaError_t launch_sk(const CUtensorMap& xh, const CUtensorMap& xl, const CUtensorMap& w, const GemmParams& p, int S,
-                      cudaStream_t s) {
+                      bool pdl, cudaStream_t s) {
   using L = SkLayout<NB, EPI == GE_SILU>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.N + kSkBM - 1) / kSkBM, S);
   cfg.blockDim = dim3(kSkThreads);
   cfg.dynamicSmemBytes = L::smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = S;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<EPI, NB>, xh, xl, w, p);
 }
+
+// Clusters of each size that fit on the device at once (cudaOccupancyMaxActiveClusters),
+// per [epilogue][NB 16 / 32][cluster size].
+int g_max_clusters[3][2][kSkMaxSplit + 1] = {};
 
 template <int EPI, int NB>
 cudaError_t configure_sk() {
   using L = SkLayout<NB, EPI == GE_SILU>;
-  return cudaFuncSetAttribute(gemm_skinny_kernel<EPI, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(L::smem));
+  cudaError_t e = cudaFuncSetAttribute(gemm_skinny_kernel<EPI, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(L::smem));
+  if (e) return e;
+  for (int S = 1; S <= kSkMaxSplit; ++S) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, S);
+    cfg.blockDim = dim3(kSkThreads);
+    cfg.dynamicSmemBytes = L::smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = S;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_skinny_kernel<EPI, NB>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    g_max_clusters[EPI][NB == 16 ? 0 : 1][S] = n;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace
 
 int skinny_nb(int M) { return M <= 16 ? 16 : 32; }
 
-int skinny_split(int N, int nk, int sm_count) {
+// K split: the most CTAs per weight tile such that every cluster of the launch
+// is resident at once (one wave) and no CTA gets an empty K range.
+int skinny_split(int epi, int M, int N, int nk, int sm_count) {
   const int tiles = (N + kSkBM - 1) / kSkBM;
-  int S = std::max(1, std::min(kSkMaxSplit, sm_count / std::max(1, tiles)));
-  return std::max(1, std::min(S, nk));
+  const int* maxc = g_max_clusters[epi < 0 || epi > 2 ? 1 : epi][skinny_nb(M) == 16 ? 0 : 1];
+  int best = 1;
+  for (int S = 2; S <= std::min(kSkMaxSplit, nk); ++S)
+    if (tiles * S <= sm_count && tiles <= maxc[S]) best = S;
+  return best;
 }
 
 cudaError_t launch_gemm_skinny(const CUtensorMap& x_hi, const CUtensorMap& x_lo, const CUtensorMap& w,
-                               const GemmParams& p, int split, cudaStream_t s) {
+                               const GemmParams& p, int split, cudaStream_t s, bool pdl) {
   if (p.M < 1 || p.M > kSkinnyMaxRows || split < 1 || split > kSkMaxSplit) return cudaErrorInvalidValue;
   const bool nb16 = skinny_nb(p.M) == 16;
   switch (p.epi) {
-    case GE_QKV: return nb16 ? launch_sk<GE_QKV, 16>(x_hi, x_lo, w, p, split, s) : launch_sk<GE_QKV, 32>(x_hi, x_lo, w, p, split, s);
+    case GE_QKV:
+      return nb16 ? launch_sk<GE_QKV, 16>(x_hi, x_lo, w, p, split, pdl, s) : launch_sk<GE_QKV, 32>(x_hi, x_lo, w, p, split, pdl, s);
     case GE_RESID:
-      return nb16 ? launch_sk<GE_RESID, 16>(x_hi, x_lo, w, p, split, s) : launch_sk<GE_RESID, 32>(x_hi, x_lo, w, p, split, s);
-    default: return nb16 ? launch_sk<GE_SILU, 16>(x_hi, x_lo, w, p, split, s) : launch_sk<GE_SILU, 32>(x_hi, x_lo, w, p, split, s);
+      return nb16 ? launch_sk<GE_RESID, 16>(x_hi, x_lo, w, p, split, pdl, s)
+                  : launch_sk<GE_RESID, 32>(x_hi, x_lo, w, p, split, pdl, s);
+    default:
+      return nb16 ? launch_sk<GE_SILU, 16>(x_hi, x_lo, w, p, split, pdl, s) : launch_sk<GE_SILU, 32>(x_hi, x_lo, w, p, split, pdl, s);
   }
 }
 

@@ -256,28 +256,57 @@ cudaError_t launch_prefill_embed(const uint16_t* table, const int* tokens, int M
 }
 
 // rmsNormInto (src/llm.zig:1287-1300) of every row, written as bf16 hi + lo.
-__global__ void norm_split_kernel(const float* x, const uint16_t* w, float eps, int h, uint16_t* hi, uint16_t* lo) {
-  __shared__ float red[32];
+// One CTA per row; each thread loads its PER elements at once (a row costs
+// one memory round trip, which matters for the few rows of a decode batch).
+template <int PER>
+__global__ void __launch_bounds__(512) norm_split_kernel(const float* x, const uint16_t* w, float eps, int h,
+                                                          uint16_t* hi, uint16_t* lo) {
+  __shared__ float red[16];
   const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  grid_launch_dependents();
+  grid_dependency_wait();  // no-op without a programmatic edge
   const float* xr = x + static_cast<size_t>(m) * h;
+  float v[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = tid + k * 512;
+    v[k] = i < h ? xr[i] : 0.f;
+  }
   float ss = 0.f;
-  for (int i = tid; i < h; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) ss = fmaf(v[k], v[k], ss);
   ss = warp_sum(ss);
   if (lane == 0) red[warp] = ss;
   __syncthreads();
   float t = 0.f;
-  for (int i = 0; i < static_cast<int>(blockDim.x / 32); ++i) t += red[i];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) t += red[i];
   const float scale = 1.0f / sqrtf(t / static_cast<float>(h) + eps);
-  for (int i = tid; i < h; i += blockDim.x) {
-    const float v = xr[i] * bf16_to_f32(w[i]) * scale;
-    split_bf16(v, hi[static_cast<size_t>(m) * h + i], lo[static_cast<size_t>(m) * h + i]);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = tid + k * 512;
+    if (i < h) split_bf16(v[k] * bf16_to_f32(w[i]) * scale, hi[static_cast<size_t>(m) * h + i], lo[static_cast<size_t>(m) * h + i]);
   }
 }
 
 cudaError_t launch_norm_split(const float* x, const uint16_t* w, float eps, int M, int h, uint16_t* hi, uint16_t* lo,
-                              cudaStream_t s) {
-  norm_split_kernel<<<M, 256, 0, s>>>(x, w, eps, h, hi, lo);
-  return cudaGetLastError();
+                              cudaStream_t s, bool pdl) {
+  const int per = (h + 511) / 512;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M);
+  cfg.blockDim = dim3(512);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (per <= 2) return cudaLaunchKernelEx(&cfg, norm_split_kernel<2>, x, w, eps, h, hi, lo);
+  if (per <= 4) return cudaLaunchKernelEx(&cfg, norm_split_kernel<4>, x, w, eps, h, hi, lo);
+  if (per <= 8) return cudaLaunchKernelEx(&cfg, norm_split_kernel<8>, x, w, eps, h, hi, lo);
+  if (per <= 16) return cudaLaunchKernelEx(&cfg, norm_split_kernel<16>, x, w, eps, h, hi, lo);
+  if (per <= 32) return cudaLaunchKernelEx(&cfg, norm_split_kernel<32>, x, w, eps, h, hi, lo);
+  return cudaErrorInvalidValue;  // hidden sizes above 16384
 }
 
 // Causal attention of a prompt chunk (computeAttentionInto per token,
@@ -481,7 +510,7 @@ cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int skinny, uint64_
   p.y = c, p.ldy = N, p.add_residual = 0, p.err = err;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if ((e = skinny ? launch_gemm_skinny(mhi, mlo, mw, p, skinny_split(N, p.nk, sms), 0) : launch_gemm_tc(mhi, mlo, mw, p, 0))) {
+  if ((e = skinny ? launch_gemm_skinny(mhi, mlo, mw, p, skinny_split(p.epi, M, N, p.nk, sms), 0) : launch_gemm_tc(mhi, mlo, mw, p, 0))) {
     cleanup();
     return e;
   }

@@ -57,15 +57,16 @@ cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int skinny, uint64_
 // `split` CTAs of a cluster share K (skinny_split picks it).
 constexpr int kSkinnyMaxRows = 32;
 int skinny_nb(int M);
-int skinny_split(int N, int nk, int sm_count);
+int skinny_split(int epi, int M, int N, int nk, int sm_count);
+// pdl: programmatic edge to the previous kernel (weights stream before the dependency wait).
 cudaError_t launch_gemm_skinny(const CUtensorMap& x_hi, const CUtensorMap& x_lo, const CUtensorMap& w,
-                               const GemmParams& p, int split, cudaStream_t s);
+                               const GemmParams& p, int split, cudaStream_t s, bool pdl = false);
 cudaError_t configure_gemm_skinny(int max_smem_optin);
 
 // Prefill helpers (SIMT): embedding gather, RMSNorm into bf16 hi/lo, causal attention.
 cudaError_t launch_prefill_embed(const uint16_t* table, const int* tokens, int M, int h, float* x, cudaStream_t s);
 cudaError_t launch_norm_split(const float* x, const uint16_t* w, float eps, int M, int h, uint16_t* hi, uint16_t* lo,
-                              cudaStream_t s);
+                              cudaStream_t s, bool pdl = false);
 struct PrefillAttnParams {
   const float* q;        // [M, nq*d] rotated
   const float* k_cache;  // this layer

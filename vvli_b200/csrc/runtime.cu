@@ -788,13 +788,16 @@ int forward_batch_chunk(vvli_ctx* c, const uint32_t* tokens, const uint64_t* pos
   RopeParams rope{c->cfg.rope_theta, VVLI_ROPE_INTERLEAVED, static_cast<int>(c->cfg.rope_scaling_type),
                   c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
                   static_cast<float>(c->cfg.rope_original_max_position)};
-  // Attention splits: about two CTAs per SM over (row, kv head), at least 64 positions each.
-  const int want = std::max(1, (2 * c->sm_count) / std::max(1, B * c->nkv_l));
-  const int splits = std::max(1, std::min({c->bt_splits_max, want, (max_pos + 1 + 63) / 64}));
-  auto gemm = [&](const CUtensorMap* x, const CUtensorMap& w, GemmParams g) -> int {
+  // Attention splits: about one CTA per SM over (row, kv head, split), at least a page each.
+  const int want = std::max(1, (c->sm_count + B * c->nkv_l / 2) / std::max(1, B * c->nkv_l));
+  const int splits = std::max(1, std::min({c->bt_splits_max, want, (max_pos + kPage) / kPage}));
+  // Programmatic edges between consecutive kernels (weights stream before the
+  // dependency wait); none next to NCCL collectives.
+  const bool pdl = !tp;
+  auto gemm = [&](const CUtensorMap* x, const CUtensorMap& w, GemmParams g, bool edge) -> int {
     g.M = B, g.two_a = 1, g.err = err, g.nk = (g.K + kGemmBK - 1) / kGemmBK;
     const int n_rows = g.N;
-    CK(launch_gemm_skinny(x[0], x[1], w, g, skinny_split(n_rows, g.nk, c->sm_count), s));
+    CK(launch_gemm_skinny(x[0], x[1], w, g, skinny_split(g.epi, B, n_rows, g.nk, c->sm_count), s, edge));
     return VVLI_OK;
   };
   int st;
@@ -803,51 +806,52 @@ int forward_batch_chunk(vvli_ctx* c, const uint32_t* tokens, const uint64_t* pos
     const DevLayer& D = c->lay[l];
     float* kc = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
     float* vc = kc + c->kv_layer_floats;
-    CK(launch_norm_split(c->bt_x, W + D.in_norm, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s));
+    CK(launch_norm_split(c->bt_x, W + D.in_norm, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s, pdl));
     GemmParams q{};
     q.N = c->q_rows + 2 * c->kv_rows, q.K = c->h, q.epi = GE_QKV, q.y = c->bt_q, q.ldy = c->q_rows;
     q.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv;
     q.q_rows = c->q_rows, q.kv_rows = c->kv_rows, q.d = c->d, q.nkv = c->nkv_l, q.rope = rope;
     q.k_cache = kc, q.v_cache = vc, q.page_table = c->page_table + static_cast<size_t>(slot0) * pps;
     q.row_pos = c->bt_pos, q.seq_pages = pps;
-    if ((st = gemm(c->tmb_h[v], c->tm_w[4 * l + 0], q))) return st;
+    if ((st = gemm(c->tmb_h[v], c->tm_w[4 * l + 0], q, pdl))) return st;
     BatchAttnParams a{};
     a.q = c->bt_q, a.k_cache = kc, a.v_cache = vc, a.page_table = c->page_table + static_cast<size_t>(slot0) * pps;
     a.seq_pages = pps, a.row_pos = c->bt_pos, a.part = c->bt_part, a.counters = c->bt_counters;
     a.out_hi = c->bt_ahi, a.out_lo = c->bt_alo, a.nq = c->nq_l, a.nkv = c->nkv_l, a.d = c->d, a.group = c->group;
-    a.splits = splits, a.inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
-    CK(launch_batch_attention(a, B, s));
+    a.splits = splits, a.nslots = batch_attention_slots(c->d), a.inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
+    a.err = err;
+    CK(launch_batch_attention(a, B, s, pdl));
     GemmParams o{};
     o.N = c->h, o.K = c->q_rows, o.epi = GE_RESID, o.y = c->bt_x, o.ldy = c->h, o.add_residual = c->tp_rank == 0;
-    if ((st = gemm(c->tmb_q[v], c->tm_w[4 * l + 1], o))) return st;
+    if ((st = gemm(c->tmb_q[v], c->tm_w[4 * l + 1], o, pdl))) return st;
     if (tp && (st = nccl_wait(c, nccl().AllReduce(c->bt_x, c->bt_x, static_cast<size_t>(B) * c->h, ncclFloat32,
                                                    ncclSum, c->comm, s), "allreduce")))
       return st;
-    CK(launch_norm_split(c->bt_x, W + D.post, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s));
+    CK(launch_norm_split(c->bt_x, W + D.post, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s, pdl));
     GemmParams gu{};
     gu.N = c->I_l, gu.K = c->h, gu.epi = GE_SILU, gu.pair_offset = c->I_l;
     gu.out_hi = c->bt_fhi, gu.out_lo = c->bt_flo, gu.ld_out = c->I_l;
-    if ((st = gemm(c->tmb_h[v], c->tm_w[4 * l + 2], gu))) return st;
+    if ((st = gemm(c->tmb_h[v], c->tm_w[4 * l + 2], gu, pdl))) return st;
     GemmParams dn{};
     dn.N = c->h, dn.K = c->I_l, dn.epi = GE_RESID, dn.y = c->bt_x, dn.ldy = c->h, dn.add_residual = c->tp_rank == 0;
-    if ((st = gemm(c->tmb_f[v], c->tm_w[4 * l + 3], dn))) return st;
+    if ((st = gemm(c->tmb_f[v], c->tm_w[4 * l + 3], dn, pdl))) return st;
     if (tp && (st = nccl_wait(c, nccl().AllReduce(c->bt_x, c->bt_x, static_cast<size_t>(B) * c->h, ncclFloat32,
                                                    ncclSum, c->comm, s), "allreduce")))
       return st;
   }
   // final norm + LM head of every row (src/llm.zig:727-728), then llm.argmax per row
-  CK(launch_norm_split(c->bt_x, W + c->off_final, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s));
+  CK(launch_norm_split(c->bt_x, W + c->off_final, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s, pdl));
   GemmParams lm{};
   lm.N = c->V_lr, lm.K = c->h, lm.epi = GE_RESID, lm.y = c->bt_logits, lm.ldy = c->V_l, lm.add_residual = 0;
-  if ((st = gemm(c->tmb_h[v], c->tm_lm, lm))) return st;
-  CK(launch_rows_argmax(c->bt_logits, B, c->V_lr, c->V_l, c->v0, c->bt_best, s));  // this rank's real rows only
+  if ((st = gemm(c->tmb_h[v], c->tm_lm, lm, pdl))) return st;
+  CK(launch_rows_argmax(c->bt_logits, B, c->V_lr, c->V_l, c->v0, c->bt_best, s, pdl));  // this rank's real rows only
   if (tp) {
     if ((st = nccl_wait(c, nccl().AllGather(c->bt_best, c->bt_all_best, 2 * static_cast<size_t>(B), ncclFloat32, c->comm, s),
                         "allgather")))
       return st;
     CK(launch_rows_argmax_merge(c->bt_all_best, c->tp_size, B, c->bt_idx, s));
   } else {
-    CK(launch_rows_argmax_index(c->bt_best, B, c->bt_idx, s));
+    CK(launch_rows_argmax_index(c->bt_best, B, c->bt_idx, s, pdl));
   }
   return VVLI_OK;
 }
@@ -1274,8 +1278,8 @@ int vvli_cuda_forward_batch(vvli_ctx* c, const uint32_t* tokens, const uint64_t*
     if (tokens[b] >= c->cfg.vocab_size) return VVLI_ERR_INVALID_TOKEN;  // src/llm.zig:704
     if (positions[b] >= c->max_seq) return VVLI_ERR_CONTEXT_FULL;     // src/llm.zig:705
   }
-  if (c->group * c->d > 1024 || c->d % 4) {
-    g_last_error = "decode batch: q heads per kv head x head_dim above 1024";
+  if (c->group * c->d > 1024 || c->group > 8 || c->d > 128 || c->d % 4) {
+    g_last_error = "decode batch: needs head_dim <= 128 (a multiple of 4) and at most 8 q heads per kv head";
     return VVLI_ERR_UNIMPLEMENTED;
   }
   CK(cudaSetDevice(c->device));
@@ -1318,6 +1322,7 @@ int vvli_cuda_forward_batch(vvli_ctx* c, const uint32_t* tokens, const uint64_t*
   if (err) {
     c->h_st->err = 0;
     CK(cudaMemsetAsync(&c->st->err, 0, sizeof(int), s));
+    CK(cudaMemsetAsync(c->bt_counters, 0, static_cast<size_t>(kSkinnyMaxRows) * c->nkv_l * sizeof(unsigned), s));
     CK(cudaStreamSynchronize(s));
     g_last_error = "decode batch: a bounded wait gave up";
     return err;
