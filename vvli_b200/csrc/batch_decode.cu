@@ -17,7 +17,7 @@ namespace vvli {
 
 namespace {
 
-constexpr int kBaThreads = 256;
+constexpr int kBaThreads = 512;
 constexpr int kBaTile = kPage;  // positions per tile: one KV page
 constexpr int kBaMaxSlots = 8;
 
@@ -27,13 +27,37 @@ VVLI_DEV void split_pair(float v, uint16_t* hi, uint16_t* lo) {
   *lo = f32_to_bf16(v - bf16_to_f32(h));
 }
 
+// Sum over the warp of p[0..7] (one partial dot product per q head of the
+// group): three exchange-halving steps leave head (bit2 + 2 bit3 + 4 bit4) of
+// the lane index in each lane, two more finish the sum (9 shuffles in all).
+VVLI_DEV float reduce_heads8(const float* p, int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float q[4], r[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float keep = b4 ? p[i + 4] : p[i], send = b4 ? p[i] : p[i + 4];
+    q[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float keep = b3 ? q[i + 2] : q[i], send = b3 ? q[i] : q[i + 2];
+    r[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float t = (b2 ? r[1] : r[0]) + __shfl_xor_sync(0xffffffffu, b2 ? r[0] : r[1], 4);
+  t += __shfl_xor_sync(0xffffffffu, t, 2);
+  t += __shfl_xor_sync(0xffffffffu, t, 1);
+  return t;
+}
+
 // CTA = (split s, kv head g, row b).  Split s owns a contiguous range of the
 // row's 64-position pages; each page's K and V rows ([kPage][d] fp32, one
 // contiguous block per kv head) arrive with two cp.async.bulk copies into a
 // ring of `nslots` shared-memory slots, so several pages per SM are in flight
-// while the oldest is computed.  Scores: a warp takes 8 positions, its lanes
-// split the head dimension and meet with butterfly shuffles; P.V: one
-// (head, dim) output per thread.
+// while the oldest is computed.  Scores: a warp takes 4 positions, lane l
+// holds dims [l*DPL, (l+1)*DPL) of the key and of every q head (q stays in
+// registers), and the heads' partial dot products meet in reduce_heads8.
+// P.V: one (head, dim) output per thread, 8 independent partial sums.
+template <int DPL>
 __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const BatchAttnParams p) {
   extern __shared__ __align__(128) float sm[];
   const int G = p.group, d = p.d, nslot = p.nslots;
@@ -85,10 +109,17 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
   __syncthreads();
   if (tid == 0)
     for (; issued < nslot && p_begin + issued < p_end; ++issued) issue(p_begin + issued, issued);
-  const int nacc = (G * d + kBaThreads - 1) / kBaThreads;  // <= 4 (G * d <= 1024)
-  const int dpl = (d + 31) / 32;                             // dims per lane (d <= 128)
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  // this lane's slice of every q head of the group
+  const bool lane_on = lane * DPL < d;
+  float qr[8][DPL];
+#pragma unroll
+  for (int hh = 0; hh < 8; ++hh)
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) qr[hh][k] = (hh < G && lane_on) ? qs[hh * d + lane * DPL + k] : 0.f;
+  const int nacc = (G * d + kBaThreads - 1) / kBaThreads;  // <= 2 (G * d <= 1024)
+  float acc[2] = {0.f, 0.f};
   bool ok = true;
+  constexpr int kPosPerWarp = kBaTile / (kBaThreads / 32);
   for (int page = p_begin, it = 0; page < p_end; ++page, ++it) {
     const int slot = it % nslot;
     ok = __syncthreads_and(mbar_wait(&bar[slot], (it / nslot) & 1, p.err) ? 1 : 0) != 0;
@@ -96,32 +127,35 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
     if (!ok) break;
     const int n = min(kPage, n_ctx - page * kPage);
     const float* ks = kv + static_cast<size_t>(slot) * 2 * page_floats;
-    const float* vs = ks + page_floats;
+    float* vs = kv + static_cast<size_t>(slot) * 2 * page_floats + page_floats;
+    // P.V below runs over the whole page: rows past n (never copied) become 0
+    for (int i = n * d + tid; i < page_floats; i += kBaThreads) vs[i] = 0.f;
     // scores
-    for (int jj = 0; jj < kBaTile / (kBaThreads / 32); ++jj) {
-      const int j = warp * (kBaTile / (kBaThreads / 32)) + jj;
-      float kx[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) kx[k] = (k < dpl && j < n && lane + 32 * k < d) ? ks[j * d + lane + 32 * k] : 0.f;
+    for (int jj = 0; jj < kPosPerWarp; ++jj) {
+      const int j = warp * kPosPerWarp + jj;
+      float kx[DPL];
+      if constexpr (DPL == 4) {
+        const float4 t = (j < n && lane_on) ? *reinterpret_cast<const float4*>(ks + j * d + lane * 4)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        kx[0] = t.x, kx[1] = t.y, kx[2] = t.z, kx[3] = t.w;
+      } else if constexpr (DPL == 2) {
+        const float2 t = (j < n && lane_on) ? *reinterpret_cast<const float2*>(ks + j * d + lane * 2) : make_float2(0.f, 0.f);
+        kx[0] = t.x, kx[1] = t.y;
+      } else {
+        kx[0] = (j < n && lane_on) ? ks[j * d + lane] : 0.f;
+      }
       float part[8];
 #pragma unroll
       for (int hh = 0; hh < 8; ++hh) {
-        part[hh] = 0.f;
-        if (hh < G) {
+        float a = 0.f;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            if (k < dpl && lane + 32 * k < d) part[hh] = fmaf(qs[hh * d + lane + 32 * k], kx[k], part[hh]);
-        }
+        for (int k = 0; k < DPL; ++k) a = fmaf(qr[hh][k], kx[k], a);
+        part[hh] = a;
       }
-#pragma unroll
-      for (int hh = 0; hh < 8; ++hh) {
-        if (hh < G) {
-          float v = part[hh];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lane == 0) sc[hh * kBaTile + j] = j < n ? v * p.inv_sqrt_d : -INFINITY;
-        }
-      }
+      const float dot = reduce_heads8(part, lane);
+      const int hh = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+      if ((lane & 3) == 0 && hh < G) sc[hh * kBaTile + j] = j < n ? dot * p.inv_sqrt_d : -INFINITY;
     }
     __syncthreads();
     // online softmax, one warp per head (softmaxInPlace, src/llm.zig:1408-1419)
@@ -145,15 +179,28 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
       }
     }
     __syncthreads();
-    // P.V (addScaled, src/llm.zig:1398-1406)
+    // P.V (addScaled, src/llm.zig:1398-1406): probabilities past n are 0
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < 2; ++k) {
       const int idx = tid + k * kBaThreads;
       if (k < nacc && idx < G * d) {
         const int hh = idx / d, e = idx % d;
-        const float* pr = sc + hh * kBaTile;
-        float a = 0.f;
-        for (int j = 0; j < n; ++j) a = fmaf(pr[j], vs[j * d + e], a);
+        const float4* pr4 = reinterpret_cast<const float4*>(sc + hh * kBaTile);
+        float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j4 = 0; j4 < kBaTile / 4; j4 += 2) {
+          const float4 w0 = pr4[j4], w1 = pr4[j4 + 1];
+          const float* vj = vs + (j4 * 4) * d + e;
+          a8[0] = fmaf(w0.x, vj[0], a8[0]);
+          a8[1] = fmaf(w0.y, vj[d], a8[1]);
+          a8[2] = fmaf(w0.z, vj[2 * d], a8[2]);
+          a8[3] = fmaf(w0.w, vj[3 * d], a8[3]);
+          a8[4] = fmaf(w1.x, vj[4 * d], a8[4]);
+          a8[5] = fmaf(w1.y, vj[5 * d], a8[5]);
+          a8[6] = fmaf(w1.z, vj[6 * d], a8[6]);
+          a8[7] = fmaf(w1.w, vj[7 * d], a8[7]);
+        }
+        const float a = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
         acc[k] = acc[k] * alpha[hh] + a;
       }
     }
@@ -172,7 +219,7 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
   const size_t out_row = static_cast<size_t>(b) * qd + static_cast<size_t>(g * G) * d;
   if (p.splits == 1) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < 2; ++k) {
       const int idx = tid + k * kBaThreads;
       if (k < nacc && idx < G * d) split_pair(acc[k] / lrun[idx / d], p.out_hi + out_row + idx, p.out_lo + out_row + idx);
     }
@@ -181,7 +228,7 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
   // partial (o, m, l) of this split: part[b][head][split][d + 2]
   float* part_b = p.part + static_cast<size_t>(b) * p.nq * p.splits * (d + 2);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < 2; ++k) {
     const int idx = tid + k * kBaThreads;
     if (k < nacc && idx < G * d) {
       const int hh = idx / d, e = idx % d;
@@ -310,10 +357,15 @@ static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaSt
 
 cudaError_t launch_batch_attention(const BatchAttnParams& p, int B, cudaStream_t s, bool pdl) {
   const size_t smem = batch_attention_smem(p.group, p.d, p.nslots);
-  cudaError_t e = cudaFuncSetAttribute(batch_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e) return e;
-  return launch_pdl(batch_attention_kernel, dim3(p.splits, p.nkv, B), dim3(kBaThreads), smem, s, pdl, p);
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(batch_attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) ||
+      (e = cudaFuncSetAttribute(batch_attention_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) ||
+      (e = cudaFuncSetAttribute(batch_attention_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))))
+    return e;
+  const dim3 grid(p.splits, p.nkv, B);
+  if (p.d > 64) return launch_pdl(batch_attention_kernel<4>, grid, dim3(kBaThreads), smem, s, pdl, p);
+  if (p.d > 32) return launch_pdl(batch_attention_kernel<2>, grid, dim3(kBaThreads), smem, s, pdl, p);
+  return launch_pdl(batch_attention_kernel<1>, grid, dim3(kBaThreads), smem, s, pdl, p);
 }
 
 cudaError_t launch_rows_argmax(const float* logits, int B, int n, int ld, int row_base, float* best, cudaStream_t s,
