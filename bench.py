@@ -50,6 +50,7 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling small cases)")
+    ap.add_argument("--batch", type=int, default=16, help="rows of the decode-batch measurement (0: skip)")
     return ap.parse_args()
 
 
@@ -204,6 +205,13 @@ def workload_config(args, cfg, n):
             "kv_cache": "f32 paged", "l2": "inputs larger than L2 (every step streams all weights, >15 GB)"}
 
 
+def _second_id(dist, vvli_b200, rank):
+    """A fresh NCCL unique id shared by all ranks (for a second tensor-parallel context)."""
+    obj = [vvli_b200.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -337,6 +345,28 @@ def main():
         t_s.append(time.perf_counter() - t0)
     sampler_line = {"us_per_token_median": round(float(np.median(t_s)) * 1e6, 1), "options": "T 0.8, top_p 0.95, "
                     "top_k 40, repeat_penalty 1.1 over 64", "vocab": cfg.vocab_size}
+    # ---- decode batch (batch 16): B sequences per step at context ~prompt,
+    # each linear layer one tensor-core GEMM over all rows; device time of whole forward_batch calls.
+    batch = None
+    if args.batch > 0:
+        rb = vvli_b200.Runner(cfg, max_seq=args.prompt + 64, device=local_rank, tp_rank=rank, tp_size=n,
+                              nccl_id=nccl_id if n == 1 else _second_id(dist, vvli_b200, rank), max_batch=args.batch)
+        rb.fill_synthetic(args.seed)
+        btoks = np.random.default_rng(2).integers(0, cfg.vocab_size, size=args.batch).astype(np.uint32)
+        for w in range(3):
+            rb.forward_batch(btoks, [args.prompt + w] * args.batch, logits=False)
+        barrier()
+        bms = []
+        for i in range(16):
+            rb.forward_batch(btoks, [args.prompt + 3 + i] * args.batch, logits=False)
+            bms.append(rb.last_forward_ms())
+        bms_step = allmax(float(np.mean(bms)))
+        batch = {"rows": args.batch, "context": args.prompt, "ms_per_step": bms_step,
+                 "tok_per_s": args.batch / (bms_step / 1000.0), "steps": 16,
+                 "path": "vvli_cuda_forward_batch: tcgen05 GEMMs with weight rows as M and the batch as N, "
+                         "paged attention per row; device time of each call (host token ids in, argmax out)"}
+        rb.close()
+
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
         v, cores, sample = time_oracle(cfg, args.seed, args.cpu_seconds)
@@ -347,7 +377,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, cfg, n),
                 "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "prefill": prefill, "sampler": sampler_line,
+                "prefill": prefill, "sampler": sampler_line, "batch": batch,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clk}
         print(json.dumps(line), flush=True)
     runner.close()
