@@ -669,6 +669,27 @@ cudaError_t launch_tp_argmax_finalize(const float* all_best, int ranks, StepStat
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- transpose
+__global__ void transpose_bf16_kernel(const uint16_t* src, uint16_t* dst, int rows, int cols) {
+  __shared__ uint16_t tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = src[static_cast<size_t>(r) * cols + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[static_cast<size_t>(c) * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+cudaError_t launch_transpose_bf16(const uint16_t* src, uint16_t* dst, int rows, int cols, cudaStream_t s) {
+  const dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+  transpose_bf16_kernel<<<grid, dim3(32, 8), 0, s>>>(src, dst, rows, cols);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- synthetic weights
 __device__ uint16_t synth_value(uint64_t key, uint64_t idx) {
   constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ull;

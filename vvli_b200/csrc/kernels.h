@@ -90,7 +90,12 @@ struct EmbedParams {
 // ---------------------------------------------------------------- decode megakernel
 // One cooperative launch runs a whole decode step as a list of phases.
 enum MegaKind { MK_EMBED = 0, MK_GEMV = 1, MK_ATTN = 2 };
-enum MegaEpi { ME_STORE = 0, ME_RESIDUAL = 1, ME_SILU = 2, ME_ARGMAX = 3, ME_QKV = 4 };
+enum MegaEpi { ME_STORE = 0, ME_RESIDUAL = 1, ME_SILU = 2, ME_ARGMAX = 3, ME_QKV = 4, ME_AXPY = 5 };
+
+// Fixed-point scale of the down_proj accumulators (x contributions are added as
+// round(v * 2^32) in 64-bit integers, so their sum does not depend on the order).
+constexpr double kAccScale = 4294967296.0;
+constexpr int kMaxFfRows = 256;  // gate|up rows per CTA kept in shared memory for ME_AXPY
 constexpr int kMaxTp = 8;
 constexpr int kMegaConsumerWarps = 16;
 constexpr int kMegaThreads = (kMegaConsumerWarps + 1) * 32;
@@ -111,6 +116,15 @@ struct MegaPhase {
   float* v_cache;
   int ar_index;            // ME_RESIDUAL: 2*layer (o_proj) or 2*layer+1 (down_proj)
   int row_align;           // CTA row ranges start at multiples of this (2 for ME_QKV: rotary pairs)
+  // down_proj fused into gate|up (tp = 1): the CTA's silu(g)*u rows stay in shared
+  // memory (ff_smem) and the next phase (ME_AXPY, no grid barrier before it) streams
+  // the matching rows of down_proj^T, adding its h-wide partial into acc_out.
+  int ff_smem;             // ME_SILU: outputs to shared memory instead of y
+  int no_barrier;          // entered straight from the previous phase
+  long long* acc_out;      // ME_AXPY: fixed-point accumulator [h]
+  long long* acc_in;       // prologue: x := x + acc_in * 2^-32, sum of squares computed locally
+  long long* acc_fold;     // ME_RESIDUAL: residual x[r] + acc_fold[r] * 2^-32, then acc_fold[r] = 0
+  int hidden_layer;        // prologue with acc_in and debugging: layer whose output is written to hidden
 };
 
 struct MegaParams {
@@ -133,6 +147,8 @@ struct MegaParams {
   unsigned long long* bar; // grid barrier arrivals (grows forever; see megakernel.cu)
   unsigned* epoch;         // increases by one per step (tensor-parallel flag values)
   int n_ar;                // residual phases per step (2 * layers)
+  int bars_per_step;       // grid barriers per step (phases entered without one are not counted)
+  long long* acc_zero;     // [h] accumulator the embed phase clears (the last layer's)
   // attention
   const float* qkv;
   float* attn;
@@ -181,5 +197,7 @@ cudaError_t configure_kernels(int max_smem_optin);
 // rows (2i, 2i + 1): on the device, split-half RoPE becomes the interleaved
 // rule.  `rows` = q rows + k rows (whole heads of d rows), `tmp` holds rows x K.
 cudaError_t launch_pair_rows(uint16_t* w, uint16_t* bias, uint16_t* tmp, int rows, int K, int d, cudaStream_t s);
+// dst[cols][rows] = src[rows][cols]^T (bf16).
+cudaError_t launch_transpose_bf16(const uint16_t* src, uint16_t* dst, int rows, int cols, cudaStream_t s);
 
 }  // namespace vvli

@@ -142,6 +142,15 @@ __device__ void prefetch_rows(const MegaPhase& ph, int ra, int rb, int t, int nl
   }
 }
 
+// Fixed-point accumulators of the fused down_proj (see MegaPhase::acc_out):
+// v -> round(v * 2^32) as a 64-bit integer; integer sums do not depend on
+// the order of the adds, so the result is the same on every run.
+VVLI_DEV long long to_fixed(float v) {
+  const double t = static_cast<double>(v) * kAccScale;
+  return __double2ll_rn(fmin(fmax(t, -9.0e18), 9.0e18));
+}
+VVLI_DEV float from_fixed(long long v) { return static_cast<float>(static_cast<double>(v) * (1.0 / kAccScale)); }
+
 // ---------------------------------------------------------------- producer
 // Cursor over this CTA's stages of every GEMV phase of the step, in order.
 struct StageCursor {
@@ -210,7 +219,7 @@ __device__ void mega_producer(const MegaParams& P, uint8_t* ring, uint64_t* full
 template <int MAXC>
 __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, float* part, uint64_t* full,
                           uint64_t* empty, uint32_t& gi, float* red, float* wv, int* wi, int* err, unsigned epoch0,
-                          int f) {
+                          int f, float* ffs) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = ph.K, S = ph.S, R = ph.R, nphys = ph.nphys;
   const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
@@ -226,7 +235,7 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
   const int cbeg = split * ph.SZ;
   const int cend = min(cpr, cbeg + ph.SZ);
   float ssq_lane = 0.f;
-  if (ph.norm_w && warp == 0) {
+  if (ph.norm_w && warp == 0 && !ph.acc_in) {
     float v[8];  // up to 256 CTAs, all loads in flight together
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -245,6 +254,19 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
       const float4 b = __ldcg(reinterpret_cast<const float4*>(ph.x + c * 8 + 4));
       xr[j][0] = a.x, xr[j][1] = a.y, xr[j][2] = a.z, xr[j][3] = a.w;
       xr[j][4] = b.x, xr[j][5] = b.y, xr[j][6] = b.z, xr[j][7] = b.w;
+      if (ph.acc_in) {  // the previous layer's down_proj, still in its fixed-point accumulator
+        const longlong2* ap = reinterpret_cast<const longlong2*>(ph.acc_in + c * 8);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const longlong2 t = __ldcg(ap + q);
+          xr[j][2 * q] = xr[j][2 * q] + from_fixed(t.x);
+          xr[j][2 * q + 1] = xr[j][2 * q + 1] + from_fixed(t.y);
+        }
+        if (warp < S) {  // warps 0..S-1 hold each slice of x once: the sum of squares here
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ssq_lane = fmaf(xr[j][e], xr[j][e], ssq_lane);
+        }
+      }
       if (ph.norm_w) {
         const uint4 wn = *reinterpret_cast<const uint4*>(ph.norm_w + c * 8);
         const float nw[8] = {bf16_lo(wn.x), bf16_hi(wn.x), bf16_lo(wn.y), bf16_hi(wn.y),
@@ -266,6 +288,10 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
     }
     return acc;
   };
+  if (P.hidden && ph.acc_in && ph.hidden_layer >= 0) {  // debugging: the finished layer's output
+    for (int r = cta_row0(K) + tid; r < cta_row1(K); r += kNC)
+      P.hidden[static_cast<size_t>(ph.hidden_layer) * K + r] = __ldcg(ph.x + r) + from_fixed(__ldcg(ph.acc_in + r));
+  }
   if (tid == 0) trace_mark(P, f, 1);
   if (ph.epi == ME_QKV && P.phases[f + 1].kind == MK_ATTN && tid < 4) {
     // This CTA's attention item of the next phase: warm L2 with its K and V
@@ -309,7 +335,16 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
   __shared__ float scale_sh;
-  if (warp == 0) {
+  if (ph.acc_in && ph.norm_w) {
+    const float t = warp_sum(ssq_lane);
+    if (lane == 0 && warp < S) red[warp] = t;
+    named_barrier(1, kNC);
+    if (tid == 0) {
+      float tt = 0.f;
+      for (int w = 0; w < S; ++w) tt += red[w];
+      scale_sh = 1.0f / sqrtf(tt / static_cast<float>(K) + P.eps);
+    }
+  } else if (warp == 0) {
     const float t = warp_sum(ssq_lane);
     if (lane == 0) scale_sh = ph.norm_w ? 1.0f / sqrtf(t / static_cast<float>(K) + P.eps) : 1.0f;
   }
@@ -385,7 +420,11 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
         a *= scale;
         if (ph.bias) a = a + bf16_to_f32(ph.bias[r]);
       }
-      ph.y[r] = a;
+      if (ph.ff_smem) {
+        ffs[rl] = a;  // read by the ME_AXPY phase that follows in this CTA
+      } else {
+        ph.y[r] = a;
+      }
     }
     return;
   }
@@ -425,7 +464,12 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
         const int r = r0 + rl;
         float a = 0.f;
         for (int s = 0; s < S; ++s) a += part[rl * S + s];
-        const float xn = __ldcg(P.x + r) + a;
+        float xo = __ldcg(P.x + r);
+        if (ph.acc_fold) {  // the previous layer's down_proj joins the residual stream here
+          xo = xo + from_fixed(__ldcg(ph.acc_fold + r));
+          ph.acc_fold[r] = 0;
+        }
+        const float xn = xo + a;
         P.x[r] = xn;
         ss = fmaf(xn, xn, ss);
         if (P.hidden && (ph.ar_index & 1)) P.hidden[static_cast<size_t>(ph.layer) * P.h + r] = xn;
@@ -503,6 +547,67 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
       }
       publish_argmax(P.st, P.seq_tokens, gidx);
       *P.epoch = epoch0 + 1u;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- fused down_proj (consumers)
+// down_proj = W_down . ff computed as a sum of rows of W_down^T scaled by this
+// CTA's own ff values (the gate|up rows it just produced, kept in shared
+// memory): thread t owns output elements [8t, 8t + 8) (and +4096 when h >
+// 4096), every 16-byte weight chunk is read once, and the CTA's h-wide
+// partial goes to the fixed-point accumulator with 64-bit integer atomics.
+// No grid barrier separates it from gate|up, so the weight ring keeps
+// streaming from one matrix into the next.
+__device__ void mega_axpy(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                          uint32_t& gi, const float* ffs, int* err, int f) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int K = ph.K, R = ph.R;
+  const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
+  const int nrows = cta_row(ph.N, blockIdx.x + 1, ph.row_align) - r0;
+  const int nstages = (nrows + R - 1) / R;
+  const size_t row_bytes = static_cast<size_t>(K) * 2;
+  const int chunks = K >> 3;
+  float acc[2][8];
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[q][e] = 0.f;
+  if (tid == 0) trace_mark(P, f, 1);
+  for (int i = 0; i < nstages; ++i, ++gi) {
+    const uint32_t slot = gi % P.nst;
+    if (!mbar_wait(&full[slot], (gi / P.nst) & 1, err)) break;
+    const int rows_here = min(R, nrows - i * R);
+    const uint8_t* stg = ring + static_cast<size_t>(slot) * P.slot_bytes;
+    for (int j = 0; j < rows_here; ++j) {
+      const float w = ffs[i * R + j];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int c = tid + q * kNC;
+        if (c < chunks) {
+          const uint4 v = *reinterpret_cast<const uint4*>(stg + j * row_bytes + c * 16);
+          acc[q][0] = fmaf(w, bf16_lo(v.x), acc[q][0]);
+          acc[q][1] = fmaf(w, bf16_hi(v.x), acc[q][1]);
+          acc[q][2] = fmaf(w, bf16_lo(v.y), acc[q][2]);
+          acc[q][3] = fmaf(w, bf16_hi(v.y), acc[q][3]);
+          acc[q][4] = fmaf(w, bf16_lo(v.z), acc[q][4]);
+          acc[q][5] = fmaf(w, bf16_hi(v.z), acc[q][5]);
+          acc[q][6] = fmaf(w, bf16_lo(v.w), acc[q][6]);
+          acc[q][7] = fmaf(w, bf16_hi(v.w), acc[q][7]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  if (tid == 0) trace_mark(P, f, 2);
+  unsigned long long* out = reinterpret_cast<unsigned long long*>(ph.acc_out);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int c = tid + q * kNC;
+    if (c < chunks) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) atomicAdd(out + c * 8 + e, static_cast<unsigned long long>(to_fixed(acc[q][e])));
     }
   }
 }
@@ -741,6 +846,8 @@ __device__ void mega_embed(const MegaParams& P, float* red, int* err) {
   }
   ss = consumer_sum(ss, red);
   if (tid == 0) P.ssq[blockIdx.x] = ss;
+  if (P.acc_zero)  // the last step's final down_proj accumulator, read by its LM head
+    for (int r = r0 + tid; r < r1; r += kNC) P.acc_zero[r] = 0;
 }
 
 // ---------------------------------------------------------------- kernel
@@ -749,6 +856,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
   __shared__ float red[kCW];
   __shared__ float wv[kCW];
   __shared__ int wi[kCW];
+  __shared__ float ffs[kMaxFfRows];  // gate|up outputs of this CTA for the fused down_proj
   const int tid = threadIdx.x, warp = tid >> 5;
   uint8_t* ring = smem;
   float* part = reinterpret_cast<float*>(smem + static_cast<size_t>(P.nst) * P.slot_bytes);
@@ -785,11 +893,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
           prefetch_rows(P.phases[f + 2], 0, P.pf_attn_rows, tid & 31, kWarp);
       }
       mega_attention(P, ph, part, err, f);
+    } else if (ph.epi == ME_AXPY) {
+      mega_axpy(P, ph, ring, full, empty, gi, ffs, err, f);
     } else {
-      mega_gemv<4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f);  // plans have cpl <= 4
+      mega_gemv<4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs);  // plans have cpl <= 4
     }
     if (tid == 0) trace_mark(P, f, 3);
-    if (f + 1 < P.nphases) {
+    if (f + 1 < P.nphases && P.phases[f + 1].no_barrier) {
+      named_barrier(1, kNC);  // the next phase reads only what this CTA wrote
+    } else if (f + 1 < P.nphases) {
       grid_arrive(P.bar);
       // While the other CTAs arrive: warm L1/L2 with the next phase's
       // constant vectors (norm weights, biases) of this CTA.
@@ -799,7 +911,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
       }
       // A barrier that gave up ends this CTA; the producer's own bounded
       // waits then end it too.
-      const uint64_t target = (static_cast<uint64_t>(epoch0) * (P.nphases - 1) + nbar + 1) * gridDim.x;
+      const uint64_t target = (static_cast<uint64_t>(epoch0) * P.bars_per_step + nbar + 1) * gridDim.x;
       ++nbar;
       if (!grid_wait(P.bar, target, err)) break;
     }

@@ -196,6 +196,8 @@ struct vvli_ctx {
   unsigned* epoch = nullptr;
   int mega_splits = 1;
   uint64_t* trace = nullptr;  // VVLI_TRACE=1: megakernel timeline
+  uint16_t* w_downT = nullptr;  // fused down_proj: W_down^T per layer [I_l][h]
+  long long* acc = nullptr;     // fused down_proj: fixed-point accumulators [2][h]
   // tensor-core prefill
   bool tc_prefill = false;
   int pf_cap = 0;
@@ -368,6 +370,9 @@ int fill_dims(vvli_ctx* c, const vvli_model_config& cfg, int tp_rank, int tp_siz
 // Phase table and launch parameters of the decode megakernel.  Returns
 // false when a shape is outside what the megakernel takes (the per-kernel
 // path then runs the step).
+template <typename T>
+int dalloc(T** p, size_t count);
+
 bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   const uint16_t* W = c->w;
   std::vector<MegaPhase> ph;
@@ -383,6 +388,22 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   MegaPhase e{};
   e.kind = MK_EMBED;
   ph.push_back(e);
+  // down_proj fused into gate|up (see MegaPhase::acc_out), opt-in with
+  // VVLI_MEGA_FUSED_DOWN=1: it removes a grid barrier per layer, but the 64-bit
+  // integer atomics of the fixed-point reduction (h per CTA) and the wider
+  // accumulator reads cost more than the barrier saves (Llama-3-8B: 4.09 vs
+  // 3.74 ms per token).  Each CTA's gate|up rows must fit the shared-memory ff
+  // buffer and a thread owns at most 16 outputs.
+  const char* fd = getenv("VVLI_MEGA_FUSED_DOWN");
+  const bool fused = fd && fd[0] == '1' && c->h % 8 == 0 && c->h <= 2 * 8 * kMegaConsumerWarps * 32 &&
+                     (c->I_l + c->sm_count - 1) / c->sm_count + 1 <= kMaxFfRows;
+  long long* acc[2] = {nullptr, nullptr};
+  if (fused) {
+    if (dalloc(&c->w_downT, static_cast<size_t>(c->L) * c->I_l * c->h) || dalloc(&c->acc, 2 * static_cast<size_t>(c->h)))
+      return false;
+    acc[0] = c->acc;
+    acc[1] = c->acc + c->h;
+  }
   for (int l = 0; l < c->L; ++l) {
     const DevLayer& D = c->lay[l];
     gemv(ME_QKV, l, W + D.w_qkv, c->q_rows + 2 * c->kv_rows, c->h, 1, W + D.in_norm, c->x, c->qkv,
@@ -390,16 +411,34 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
     ph.back().k_cache = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
     ph.back().v_cache = ph.back().k_cache + c->kv_layer_floats;
     ph.back().row_align = 2;
+    if (fused && l > 0) ph.back().acc_in = acc[(l - 1) & 1], ph.back().hidden_layer = l - 1;
     MegaPhase a{};
     a.kind = MK_ATTN, a.layer = l;
     a.k_cache = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
     a.v_cache = a.k_cache + c->kv_layer_floats;
     ph.push_back(a);
     gemv(ME_RESIDUAL, l, W + D.w_o, c->h, c->q_rows, 1, nullptr, c->attn, c->x, nullptr, 2 * l);
-    gemv(ME_SILU, l, W + D.w_gu, c->I_l, c->h, 2, W + D.post, c->x, c->ff, nullptr, 0);
-    gemv(ME_RESIDUAL, l, W + D.w_down, c->h, c->I_l, 1, nullptr, c->ff, c->x, nullptr, 2 * l + 1);
+    if (fused && l > 0) ph.back().acc_fold = acc[(l - 1) & 1];
+    if (fused) {
+      gemv(ME_SILU, l, W + D.w_gu, c->I_l, c->h, 2, W + D.post, c->x, nullptr, nullptr, 0);
+      ph.back().ff_smem = 1;
+      MegaPhase dn{};
+      dn.kind = MK_GEMV, dn.epi = ME_AXPY, dn.layer = l, dn.nphys = 1, dn.no_barrier = 1, dn.row_align = 1;
+      dn.W = c->w_downT + static_cast<size_t>(l) * c->I_l * c->h, dn.N = c->I_l, dn.K = c->h;
+      dn.S = 1, dn.SZ = 0, dn.cpl = 0;
+      dn.R = std::max(1, 65536 / (2 * c->h));
+      dn.stage_bytes = dn.R * 2 * c->h;
+      dn.acc_out = acc[l & 1];
+      ph.push_back(dn);
+    } else {
+      gemv(ME_SILU, l, W + D.w_gu, c->I_l, c->h, 2, W + D.post, c->x, c->ff, nullptr, 0);
+      gemv(ME_RESIDUAL, l, W + D.w_down, c->h, c->I_l, 1, nullptr, c->ff, c->x, nullptr, 2 * l + 1);
+    }
   }
   gemv(ME_ARGMAX, -1, W + c->off_lm, c->V_lr, c->h, 1, W + c->off_final, c->x, c->logits, nullptr, 0);
+  if (fused) ph.back().acc_in = acc[(c->L - 1) & 1], ph.back().hidden_layer = c->L - 1;
+  for (MegaPhase& m : ph)
+    if (!m.acc_in) m.hidden_layer = -1;
 
   const int grid = c->sm_count;
   int slot = 0;
@@ -447,6 +486,9 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   P.bar = c->bar;
   P.epoch = c->epoch;
   P.n_ar = 2 * c->L;
+  P.bars_per_step = static_cast<int>(ph.size()) - 1;
+  for (const MegaPhase& m : ph) P.bars_per_step -= m.no_barrier ? 1 : 0;
+  P.acc_zero = fused ? acc[(c->L - 1) & 1] : nullptr;
   P.qkv = c->qkv;
   P.attn = c->attn;
   P.attn_part = c->attn_part;
@@ -920,6 +962,7 @@ int finish_state(vvli_ctx* c) {
     if (c->use_mega) {
       cudaMemsetAsync(c->bar, 0, sizeof(unsigned long long), c->stream);
       cudaMemsetAsync(c->epoch, 0, sizeof(unsigned), c->stream);
+      if (c->acc) cudaMemsetAsync(c->acc, 0, 2 * static_cast<size_t>(c->h) * sizeof(long long), c->stream);
       cudaStreamSynchronize(c->stream);
     }
     return c->h_st->err;
@@ -948,7 +991,7 @@ void free_ctx(vvli_ctx* c) {
   if (c->comm) nccl().CommDestroy(c->comm);
   void* dev[] = {c->w, c->kv, c->page_table, c->x, c->qkv, c->attn, c->ff, c->logits, c->logits_full, c->emb_in,
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
-                 c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->pf_x, c->pf_q,
+                 c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->w_downT, c->acc, c->pf_x, c->pf_q,
                  c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->smp_stamp, c->smp_key32,
                  c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_recent, c->smp_state, c->smp_temp,
                  c->bt_x, c->bt_q, c->bt_logits, c->bt_best, c->bt_all_best, c->bt_part, c->bt_logits_all, c->bt_ahi,
@@ -1163,6 +1206,11 @@ static int after_load(vvli_ctx* c) {
     }
     CK(cudaStreamSynchronize(c->stream));
     cudaFree(tmp);
+  }
+  if (c->w_downT) {  // fused down_proj streams W_down^T rows
+    for (int l = 0; l < c->L; ++l)
+      CK(launch_transpose_bf16(c->w + c->lay[l].w_down, c->w_downT + static_cast<size_t>(l) * c->I_l * c->h, c->h,
+                               c->I_l, c->stream));
   }
   CK(cudaStreamSynchronize(c->stream));
   c->loaded = true;
