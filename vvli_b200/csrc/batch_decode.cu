@@ -27,28 +27,6 @@ VVLI_DEV void split_pair(float v, uint16_t* hi, uint16_t* lo) {
   *lo = f32_to_bf16(v - bf16_to_f32(h));
 }
 
-// Sum over the warp of p[0..7] (one partial dot product per q head of the
-// group): three exchange-halving steps leave head (bit2 + 2 bit3 + 4 bit4) of
-// the lane index in each lane, two more finish the sum (9 shuffles in all).
-VVLI_DEV float reduce_heads8(const float* p, int lane) {
-  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-  float q[4], r[2];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float keep = b4 ? p[i + 4] : p[i], send = b4 ? p[i] : p[i + 4];
-    q[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float keep = b3 ? q[i + 2] : q[i], send = b3 ? q[i] : q[i + 2];
-    r[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-  float t = (b2 ? r[1] : r[0]) + __shfl_xor_sync(0xffffffffu, b2 ? r[0] : r[1], 4);
-  t += __shfl_xor_sync(0xffffffffu, t, 2);
-  t += __shfl_xor_sync(0xffffffffu, t, 1);
-  return t;
-}
-
 // CTA = (split s, kv head g, row b).  Split s owns a contiguous range of the
 // row's 64-position pages; each page's K and V rows ([kPage][d] fp32, one
 // contiguous block per kv head) arrive with two cp.async.bulk copies into a

@@ -90,4 +90,26 @@ VVLI_DEV size_t kv_off(const int* pt, int t, int g, int nkv, int d) {
   return (static_cast<size_t>(page * nkv + g) * kPage + (t % kPage)) * d;
 }
 
+// Sum over the warp of p[0..7] (one partial dot product per q head of the
+// group): three exchange-halving steps leave head (bit2 + 2 bit3 + 4 bit4) of
+// the lane index in each lane, two more finish the sum (9 shuffles in all).
+VVLI_DEV float reduce_heads8(const float* p, int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float q[4], r[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float keep = b4 ? p[i + 4] : p[i], send = b4 ? p[i] : p[i + 4];
+    q[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float keep = b3 ? q[i + 2] : q[i], send = b3 ? q[i] : q[i + 2];
+    r[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float t = (b2 ? r[1] : r[0]) + __shfl_xor_sync(0xffffffffu, b2 ? r[0] : r[1], 4);
+  t += __shfl_xor_sync(0xffffffffu, t, 2);
+  t += __shfl_xor_sync(0xffffffffu, t, 1);
+  return t;
+}
+
 }  // namespace vvli

@@ -176,8 +176,8 @@ struct MegaParams {
 
 cudaError_t launch_megakernel(const MegaParams& p, int grid, size_t smem, cudaStream_t s);
 cudaError_t configure_megakernel(int max_smem_optin);
-// Streaming plan of one GEMV for the megakernel (16 consumer warps, <= 64 KB stages).
-void plan_mega_gemv(MegaPhase& ph);
+// Streaming plan of one GEMV for the megakernel (16 consumer warps, stages <= stage_cap bytes).
+void plan_mega_gemv(MegaPhase& ph, int stage_cap);
 size_t mega_attention_floats(int group, int d, int splits, int max_pages);
 
 // Launchers (pdl: launch with a programmatic edge to the previous kernel).

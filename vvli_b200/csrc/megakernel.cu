@@ -933,7 +933,7 @@ cudaError_t launch_megakernel(const MegaParams& p, int grid, size_t smem, cudaSt
   return cudaLaunchKernelEx(&cfg, decode_megakernel, p);
 }
 
-void plan_mega_gemv(MegaPhase& ph) {
+void plan_mega_gemv(MegaPhase& ph, int stage_cap) {
   const int cpr = ph.K / 8;
   const size_t row_bytes = static_cast<size_t>(ph.K) * 2;
   int S = 1;
@@ -943,7 +943,7 @@ void plan_mega_gemv(MegaPhase& ph) {
   ph.cpl = (ph.SZ + kWarp - 1) / kWarp;
   const int want_pairs = 2 * kCW;
   int R = (want_pairs + S * ph.nphys - 1) / (S * ph.nphys);
-  while (R > 1 && R * row_bytes * ph.nphys > 65536) R /= 2;
+  while (R > 1 && R * row_bytes * ph.nphys > static_cast<size_t>(stage_cap)) R /= 2;
   ph.R = R < 1 ? 1 : R;
   ph.stage_bytes = static_cast<int>(ph.R * row_bytes * ph.nphys);
 }

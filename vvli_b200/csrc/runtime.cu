@@ -375,6 +375,9 @@ int dalloc(T** p, size_t count);
 
 bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   const uint16_t* W = c->w;
+  // Ring shape: shared memory taken from the L1 carve-out costs the phase
+  // changes more than a deeper ring gains (measured), see DESIGN.md.
+  const int stage_cap = getenv("VVLI_MEGA_STAGE_CAP") ? std::max(4096, atoi(getenv("VVLI_MEGA_STAGE_CAP"))) : 65536;
   std::vector<MegaPhase> ph;
   auto gemv = [&](int epi, int layer, const uint16_t* w, int N, int K, int nphys, const uint16_t* norm,
                   const float* x, float* y, const uint16_t* bias, int ar_index) {
@@ -382,7 +385,7 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
     m.kind = MK_GEMV, m.epi = epi, m.layer = layer, m.nphys = nphys, m.W = w, m.N = N, m.K = K;
     m.pair_offset = nphys == 2 ? N : 0;
     m.norm_w = norm, m.x = x, m.y = y, m.bias = bias, m.ar_index = ar_index, m.row_align = 1;
-    plan_mega_gemv(m);
+    plan_mega_gemv(m, stage_cap);
     ph.push_back(m);
   };
   MegaPhase e{};
