@@ -28,45 +28,66 @@ def gpu_count():
         return 0
 
 
-def _rank_main(rank, world, nccl_id, cfg, blob, prompt, n_new, q):
+def _rank_main(rank, world, nccl_id, cfg, blob, prompt, n_new, mega, q):
     try:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         os.environ.setdefault("VVLI_NCCL_TIMEOUT_S", "60")
+        os.environ["VVLI_MEGAKERNEL"] = "1" if mega else "0"
+        import time
         import vvli_b200
+        import vvli_b200._abi
+        t0 = time.time()
+
+        def note(what):
+            print(f"[rank {rank} +{time.time() - t0:.1f}s] {what}", file=sys.stderr, flush=True)
+
         r = vvli_b200.Runner(cfg, max_seq=128, device=rank, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
         r.load_weights(blob)
+        used_mega = r.query("megakernel") == 1
+        note(f"created, megakernel={used_mega} ({vvli_b200._abi.lib().vvli_cuda_last_error().decode()})")
         logits = [r.forward_token(t, p) for p, t in enumerate(prompt)]
+        note("forward_token done")
         r.reset()
         tokens, _ = r.generate_greedy(prompt, n_new)
+        note("generate done")
         r.close()
-        q.put((rank, "ok", np.stack(logits), tokens))
+        q.put((rank, "ok", np.stack(logits), tokens, used_mega))
     except Exception as e:  # reported to the parent, which fails the test
-        q.put((rank, repr(e), None, None))
+        q.put((rank, repr(e), None, None, None))
 
 
-def run_tp(cfg, blob, prompt, n_new, world):
+def run_tp(cfg, blob, prompt, n_new, world, mega=True):
+    """Runs every rank; with mega, the decode steps are the tensor-parallel megakernel
+    (partial sums exchanged over NVLink inside the kernel), else the per-kernel step with NCCL."""
     import vvli_b200
     nccl_id = vvli_b200.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, nccl_id, cfg, blob, prompt, n_new, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, nccl_id, cfg, blob, prompt, n_new, mega, q), daemon=True)
              for r in range(world)]
     for p in procs:
         p.start()
     results = {}
-    for _ in range(world):
-        rank, status, logits, tokens = q.get(timeout=300)
-        results[rank] = (status, logits, tokens)
-    for p in procs:
-        p.join(timeout=60)
-    for rank, (status, _, _) in results.items():
+    try:
+        for _ in range(world):
+            rank, status, logits, tokens, used_mega = q.get(timeout=120)
+            results[rank] = (status, logits, tokens, used_mega)
+    finally:
+        for p in procs:  # the ranks this test started, and only those
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
+    for rank, (status, _, _, used_mega) in results.items():
         assert status == "ok", (rank, status)
+        assert used_mega == mega, (rank, used_mega)
     return results
 
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mega", [True, False], ids=["megakernel", "per_kernel"])
 @pytest.mark.parametrize("name", ["qwen2_tiny", "llama3_tiny_rs"])
-def test_tp2_matches_oracle(oracle, name):
+def test_tp2_matches_oracle(oracle, name, mega):
     from make_golden import fixture_configs
     cfg, seed = fixture_configs()[name]
     blob = oracle.synthetic_blob(cfg, seed=seed)
@@ -75,9 +96,9 @@ def test_tp2_matches_oracle(oracle, name):
     ref_logits = np.stack([ref.forward_token(t, p) for p, t in enumerate(prompt)])
     ref.reset()
     ref_tokens = ref.generate_greedy(prompt, 24)
-    res = run_tp(cfg, blob, prompt, 24, 2)
+    res = run_tp(cfg, blob, prompt, 24, 2, mega)
     for rank in range(2):
-        _, logits, tokens = res[rank]
+        _, logits, tokens, _ = res[rank]
         assert np.max(np.abs(logits - ref_logits)) < 1e-4, rank
         assert tokens == ref_tokens, rank
 
@@ -93,6 +114,6 @@ def test_tp2_llama3_2_1b_architecture(oracle):
     ref.reset()
     ref_tokens = ref.generate_greedy(prompt, 16)
     res = run_tp(cfg, blob, prompt, 16, 2)
-    _, logits, tokens = res[0]
+    _, logits, tokens, _ = res[0]
     assert np.max(np.abs(logits - ref_logits)) < 2e-2
     assert tokens == ref_tokens

@@ -196,6 +196,10 @@ struct vvli_ctx {
   unsigned* epoch = nullptr;
   int mega_splits = 1;
   uint64_t* trace = nullptr;  // VVLI_TRACE=1: megakernel timeline
+  // tensor-parallel megakernel: this rank's exchange block (receive rows, flags,
+  // argmax slots) and every rank's block mapped into this process (CUDA IPC)
+  uint8_t* peer_block = nullptr;
+  void* peer_base[kMaxTp] = {};
   uint16_t* w_downT = nullptr;  // fused down_proj: W_down^T per layer [I_l][h]
   long long* acc = nullptr;     // fused down_proj: fixed-point accumulators [2][h]
   // tensor-core prefill
@@ -398,7 +402,7 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   // 3.74 ms per token).  Each CTA's gate|up rows must fit the shared-memory ff
   // buffer and a thread owns at most 16 outputs.
   const char* fd = getenv("VVLI_MEGA_FUSED_DOWN");
-  const bool fused = fd && fd[0] == '1' && c->h % 8 == 0 && c->h <= 2 * 8 * kMegaConsumerWarps * 32 &&
+  const bool fused = fd && fd[0] == '1' && c->tp_size == 1 && c->h % 8 == 0 && c->h <= 2 * 8 * kMegaConsumerWarps * 32 &&
                      (c->I_l + c->sm_count - 1) / c->sm_count + 1 <= kMaxFfRows;
   long long* acc[2] = {nullptr, nullptr};
   if (fused) {
@@ -991,6 +995,9 @@ void free_ctx(vvli_ctx* c) {
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   if (c->graph) cudaGraphExecDestroy(c->graph);
+  for (int q = 0; q < kMaxTp; ++q)
+    if (c->peer_base[q] && c->peer_base[q] != c->peer_block) cudaIpcCloseMemHandle(c->peer_base[q]);
+  if (c->peer_block) cudaFree(c->peer_block);
   if (c->comm) nccl().CommDestroy(c->comm);
   void* dev[] = {c->w, c->kv, c->page_table, c->x, c->qkv, c->attn, c->ff, c->logits, c->logits_full, c->emb_in,
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
@@ -1082,6 +1089,8 @@ int vvli_cuda_nccl_unique_id(void* id) {
   std::memcpy(id, &uid, sizeof(uid));
   return VVLI_OK;
 }
+
+static int setup_tp_peers(vvli_ctx* c);
 
 int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int tp_size, const void* nccl_unique_id,
                      uint64_t max_seq, uint64_t max_batch, vvli_ctx** out_ctx) {
@@ -1183,12 +1192,84 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
     cudaGetLastError();
   }
   const char* mega_env = getenv("VVLI_MEGAKERNEL");
-  const bool want_mega = !(mega_env && mega_env[0] == '0') && tp_size == 1;
+  const bool want_mega = !(mega_env && mega_env[0] == '0') && tp_size <= kMaxTp;
   if (want_mega) {
     if ((e = configure_megakernel(smem_optin))) return fail(cuda_fail(e, "configure_megakernel"));
     c->use_mega = plan_megakernel(c, smem_optin);
+    // Under tensor parallelism the megakernel needs every peer's exchange block;
+    // without it (no peer access) the per-kernel step with NCCL runs instead.
+    if (!c->use_mega) g_last_error = "megakernel: no plan fits this model";
+    if (c->use_mega && tp_size > 1 && setup_tp_peers(c) != VVLI_OK) {
+      c->use_mega = false;  // g_last_error says why
+      cudaGetLastError();
+    }
+  }
+  if (tp_size > 1) {
+    // Every rank must take the same path (a megakernel rank waits for peers'
+    // flags, a per-kernel rank for NCCL): the megakernel runs only if all
+    // ranks could set it up.
+    int* flag = nullptr;
+    int mine = c->use_mega ? 1 : 0, all = 0;
+    if ((e = cudaMalloc(&flag, sizeof(int)))) return fail(cuda_fail(e, "cudaMalloc"));
+    cudaMemcpy(flag, &mine, sizeof(int), cudaMemcpyHostToDevice);
+    st = nccl_wait(c, nccl().AllReduce(flag, flag, 1, ncclInt32, ncclMin, c->comm, c->stream), "allreduce (path)");
+    if (st == VVLI_OK) e = cudaStreamSynchronize(c->stream);
+    if (st == VVLI_OK && e == cudaSuccess) e = cudaMemcpy(&all, flag, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(flag);
+    if (st) return fail(st);
+    c->use_mega = all == 1;
   }
   *out_ctx = c;
+  return VVLI_OK;
+}
+
+// Tensor-parallel megakernel: each rank allocates one exchange block — the
+// receive rows of the o_proj / down_proj partial sums [2 parities][tp][h],
+// their arrival flags [2][tp][CTAs], and the LM-head argmax slots [tp][2] with
+// flags [tp] — exports it as a CUDA IPC handle, gathers every rank's handle
+// over NCCL and maps the peers' blocks.  The megakernel then stores its
+// partials straight into every peer's block over NVLink (plain stores, no
+// multicast) and waits, bounded, on its own flags.
+static int setup_tp_peers(vvli_ctx* c) {
+  const int tp = c->tp_size, grid = c->sm_count;
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t recv_off = 0, recv_bytes = 2ull * tp * c->h * 4;
+  const size_t flag_off = up(recv_off + recv_bytes), flag_bytes = 2ull * tp * grid * 4;
+  const size_t best_off = up(flag_off + flag_bytes), best_bytes = 2ull * tp * 4;
+  const size_t bflag_off = up(best_off + best_bytes), bflag_bytes = static_cast<size_t>(tp) * 4;
+  const size_t total = up(bflag_off + bflag_bytes);
+  CK(cudaMalloc(&c->peer_block, total));
+  CK(cudaMemset(c->peer_block, 0, total));
+  cudaIpcMemHandle_t mine;
+  CK(cudaIpcGetMemHandle(&mine, c->peer_block));
+  uint8_t* ids = nullptr;
+  CK(cudaMalloc(&ids, sizeof(cudaIpcMemHandle_t) * tp));
+  std::vector<cudaIpcMemHandle_t> all(tp);
+  int st = VVLI_OK;
+  cudaError_t e = cudaMemcpy(ids + sizeof(mine) * c->tp_rank, &mine, sizeof(mine), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    st = nccl_wait(c, nccl().AllGather(ids + sizeof(mine) * c->tp_rank, ids, sizeof(mine), ncclChar, c->comm, c->stream),
+                   "allgather ipc handles");
+  // the gather runs on c->stream (non-blocking): wait for it before reading
+  if (e == cudaSuccess && st == VVLI_OK) e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess && st == VVLI_OK) e = cudaMemcpy(all.data(), ids, sizeof(mine) * tp, cudaMemcpyDeviceToHost);
+  cudaFree(ids);
+  if (st) return st;
+  if (e) return cuda_fail(e, "ipc handle exchange");
+  MegaParams& P = c->mp;
+  for (int q = 0; q < tp; ++q) {
+    void* base = c->peer_block;
+    if (q != c->tp_rank) {
+      e = cudaIpcOpenMemHandle(&base, all[q], cudaIpcMemLazyEnablePeerAccess);
+      if (e) return cuda_fail(e, "cudaIpcOpenMemHandle (peer exchange block)");
+    }
+    c->peer_base[q] = base;
+    uint8_t* b = static_cast<uint8_t*>(base);
+    P.peer_recv[q] = reinterpret_cast<float*>(b + recv_off);
+    P.peer_flags[q] = reinterpret_cast<unsigned*>(b + flag_off);
+    P.peer_best[q] = reinterpret_cast<float*>(b + best_off);
+    P.peer_best_flag[q] = reinterpret_cast<unsigned*>(b + bflag_off);
+  }
   return VVLI_OK;
 }
 
