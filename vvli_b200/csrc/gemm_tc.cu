@@ -405,6 +405,182 @@ __global__ void __launch_bounds__(kPaThreads) prefill_attention_kernel(const Pre
   }
 }
 
+// Register-blocked causal attention for head_dim 64 / 128 (flash form).
+// CTA = (kv head g, block of BQ = 128 / G tokens): its 128 query rows are the
+// group's q heads x tokens (row r = token r / G, head r % G).  Key tiles of 64
+// positions (one KV page) are staged transposed (K) and as-is (V) in shared
+// memory; thread t owns query rows 4 (t / 8) .. + 3, and score columns
+// 8 (t % 8) .. + 7 of a tile (32 scores from 3 shared loads per k), then
+// output dims (t % 8) D / 8 .. of its 4 rows for P.V.  Online softmax per row
+// across the row's 8 lanes; causal mask by position.  Output as bf16 hi / lo
+// for the o_proj GEMM.
+constexpr int kFaThreads = 256;
+constexpr int kFaRows = 128;
+constexpr int kFaKeys = 64;
+constexpr int kFaPs = kFaKeys + 1;  // P row stride (bank spread)
+
+template <int D>
+size_t flash_smem_floats() {
+  return static_cast<size_t>(D) * kFaRows + static_cast<size_t>(D) * kFaKeys + static_cast<size_t>(kFaKeys) * D +
+         static_cast<size_t>(kFaRows) * kFaPs;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kFaThreads, 1) prefill_flash_kernel(const PrefillAttnParams p) {
+  extern __shared__ __align__(16) float fa[];
+  constexpr int DD = D / 8;  // output dims per thread
+  float* qt = fa;                           // [D][128]   Q^T
+  float* kt = qt + D * kFaRows;             // [D][64]    K^T
+  float* vs = kt + D * kFaKeys;             // [64][D]
+  float* ps = vs + kFaKeys * D;             // [128][65]  probabilities
+  const int G = p.group, g = blockIdx.x;
+  const int BQ = kFaRows / G;
+  const int t0 = blockIdx.y * BQ;
+  const int nt = min(BQ, p.M - t0);
+  const int rows = G * nt;
+  const int tid = threadIdx.x, rg = tid >> 3, cg = tid & 7;
+  const int qd = p.nq * D;
+  // Q^T: thread reads 4 consecutive dims of a row, writes 4 rows of qt
+  for (int idx = tid; idx < kFaRows * (D / 4); idx += kFaThreads) {
+    const int r = idx % kFaRows, k4 = idx / kFaRows;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < rows) {
+      const int t = r / G, hh = r % G;
+      v = *reinterpret_cast<const float4*>(p.q + static_cast<size_t>(t0 + t) * qd + static_cast<size_t>(g * G + hh) * D + 4 * k4);
+    }
+    qt[(4 * k4 + 0) * kFaRows + r] = v.x;
+    qt[(4 * k4 + 1) * kFaRows + r] = v.y;
+    qt[(4 * k4 + 2) * kFaRows + r] = v.z;
+    qt[(4 * k4 + 3) * kFaRows + r] = v.w;
+  }
+  // this thread's rows: query positions (rows past `rows` are padding)
+  int qpos[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 4 * rg + i;
+    qpos[i] = r < rows ? p.pos0 + t0 + r / G : -1;
+  }
+  float o[4][DD];
+  float m[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DD; ++e) o[i][e] = 0.f;
+  }
+  const int last_pos = p.pos0 + t0 + nt - 1;
+  for (int j0 = 0; j0 <= last_pos; j0 += kFaKeys) {
+    __syncthreads();  // previous tile's K, V and P are no longer read
+    const int nkeys = min(kFaKeys, last_pos + 1 - j0);
+    const size_t base = kv_off(p.page_table, j0, g, p.nkv, D);  // a tile is one page: rows contiguous
+    for (int idx = tid; idx < kFaKeys * (D / 4); idx += kFaThreads) {
+      const int j = idx % kFaKeys, k4 = idx / kFaKeys;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (j < nkeys) {
+        kv = *reinterpret_cast<const float4*>(p.k_cache + base + static_cast<size_t>(j) * D + 4 * k4);
+        vv = *reinterpret_cast<const float4*>(p.v_cache + base + static_cast<size_t>(j) * D + 4 * k4);
+      }
+      kt[(4 * k4 + 0) * kFaKeys + j] = kv.x;
+      kt[(4 * k4 + 1) * kFaKeys + j] = kv.y;
+      kt[(4 * k4 + 2) * kFaKeys + j] = kv.z;
+      kt[(4 * k4 + 3) * kFaKeys + j] = kv.w;
+      *reinterpret_cast<float4*>(vs + j * D + 4 * k4) = vv;
+    }
+    __syncthreads();
+    // S = Q K^T for rows 4rg.., keys 8cg..
+    float sc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) sc[i][c] = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < D; ++k) {
+      const float4 a = *reinterpret_cast<const float4*>(qt + k * kFaRows + 4 * rg);
+      const float4 b0 = *reinterpret_cast<const float4*>(kt + k * kFaKeys + 8 * cg);
+      const float4 b1 = *reinterpret_cast<const float4*>(kt + k * kFaKeys + 8 * cg + 4);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) sc[i][c] = fmaf(av[i], bv[c], sc[i][c]);
+    }
+    // online softmax over the row's 8 lanes (softmaxInPlace, src/llm.zig:1408-1419)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int kp = j0 + 8 * cg + c;
+        sc[i][c] = (kp <= qpos[i] && 8 * cg + c < nkeys) ? sc[i][c] * p.inv_sqrt_d : -INFINITY;
+        mt = fmaxf(mt, sc[i][c]);
+      }
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+      const float mnew = fmaxf(m[i], mt);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float e = mnew == -INFINITY ? 0.f : expf(sc[i][c] - mnew);
+        ps[(4 * rg + i) * kFaPs + 8 * cg + c] = e;
+        sum += e;
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      const float alpha = m[i] == -INFINITY ? 0.f : expf(m[i] - mnew);
+      l[i] = l[i] * alpha + sum;
+      m[i] = mnew;
+#pragma unroll
+      for (int e = 0; e < DD; ++e) o[i][e] *= alpha;
+    }
+    __syncthreads();
+    // O += P V (addScaled, src/llm.zig:1398-1406) for rows 4rg.., dims cg*DD..
+#pragma unroll 2
+    for (int j = 0; j < nkeys; ++j) {
+      float pr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pr[i] = ps[(4 * rg + i) * kFaPs + j];
+      const float4* vr = reinterpret_cast<const float4*>(vs + j * D + cg * DD);
+#pragma unroll
+      for (int e4 = 0; e4 < DD / 4; ++e4) {
+        const float4 v = vr[e4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          o[i][4 * e4 + 0] = fmaf(pr[i], v.x, o[i][4 * e4 + 0]);
+          o[i][4 * e4 + 1] = fmaf(pr[i], v.y, o[i][4 * e4 + 1]);
+          o[i][4 * e4 + 2] = fmaf(pr[i], v.z, o[i][4 * e4 + 2]);
+          o[i][4 * e4 + 3] = fmaf(pr[i], v.w, o[i][4 * e4 + 3]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 4 * rg + i;
+    if (r >= rows) continue;
+    const int t = r / G, hh = r % G;
+    const size_t orow = static_cast<size_t>(t0 + t) * qd + static_cast<size_t>(g * G + hh) * D + cg * DD;
+    const float inv = 1.0f / l[i];
+#pragma unroll
+    for (int e = 0; e < DD; ++e) split_bf16(o[i][e] * inv, p.out_hi[orow + e], p.out_lo[orow + e]);
+  }
+}
+
+template <int D>
+static cudaError_t launch_flash(const PrefillAttnParams& p, cudaStream_t s) {
+  const int BQ = kFaRows / p.group;
+  const dim3 grid(p.nkv, (p.M + BQ - 1) / BQ);
+  const size_t smem = flash_smem_floats<D>() * 4;
+  cudaError_t e = cudaFuncSetAttribute(prefill_flash_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e) return e;
+  prefill_flash_kernel<D><<<grid, kFaThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
 template <int DPL>
 static cudaError_t launch_pa(const PrefillAttnParams& p, cudaStream_t s) {
   constexpr int rpw = kPaAcc / DPL;
@@ -419,6 +595,10 @@ static cudaError_t launch_pa(const PrefillAttnParams& p, cudaStream_t s) {
 }
 
 cudaError_t launch_prefill_attention(const PrefillAttnParams& p, cudaStream_t s) {
+  if (p.group <= 8 && kFaRows / p.group >= 1) {
+    if (p.d == 128) return launch_flash<128>(p, s);
+    if (p.d == 64) return launch_flash<64>(p, s);
+  }
   const int dpl = (p.d + 31) / 32;
   if (dpl <= 1) return launch_pa<1>(p, s);
   if (dpl <= 2) return launch_pa<2>(p, s);
