@@ -14,6 +14,7 @@ pytestmark = pytest.mark.gpu
     (200, 1152, 896, 1),    # ragged M and N tails (Qwen q|k|v shape)
     (512, 4096, 4096, 1),   # Llama-3-8B hidden
     (32, 256, 14336, 1),    # long K (down_proj), few tokens
+    (1536, 2048, 256, 1),   # enough tiles for the 256-wide residual tiles
 ])
 def test_gemm_matches_reference(M, N, K, two_a):
     from vvli_b200 import _abi

@@ -28,21 +28,33 @@
 
 namespace vvli {
 
-constexpr int kGemmStages = 3;
 constexpr uint32_t kTileA = kGemmBM * kGemmBK * 2;   // 16 KB
-constexpr uint32_t kTileB = kGemmBN * kGemmBK * 2;   // 32 KB
-constexpr uint32_t kStageBytes = 2 * kTileA + kTileB;  // A_hi | A_lo | B
 constexpr int kGemmThreads = 192;
-constexpr uint32_t kTmemCols = 256;
 
-// Instruction descriptor: N = 256, M = 128.
-constexpr uint32_t kIdesc = umma_idesc(kGemmBM, kGemmBN);
+// Tile shape per output width BN (256, or 128 for matrices with few column
+// tiles, so the grid still covers the SMs): stages fill ~192 KB.
+template <int BN>
+struct TcLayout {
+  static constexpr uint32_t tile_b = BN * kGemmBK * 2;
+  static constexpr uint32_t stage = 2 * kTileA + tile_b;  // A_hi | A_lo | B
+  static constexpr int stages = (192 * 1024) / stage;
+  static constexpr uint32_t tmem_cols = BN;
+  static constexpr uint32_t idesc = umma_idesc(kGemmBM, BN);
+  static constexpr size_t smem = static_cast<size_t>(stages) * stage + 1024 /*align*/ + 256 /*barriers*/;
+};
 
 // ---------------------------------------------------------------- GEMM kernel
-template <int EPI>
+template <int EPI, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
                    const __grid_constant__ CUtensorMap tm_w, const GemmParams p) {
+  using L = TcLayout<BN>;
+  constexpr int kGemmStages = L::stages;
+  constexpr uint32_t kStageBytes = L::stage;
+  constexpr uint32_t kTileB = L::tile_b;
+  constexpr uint32_t kTmemCols = L::tmem_cols;
+  constexpr uint32_t kIdesc = L::idesc;
+  static_assert(EPI != GE_SILU || BN == 256, "gate|up tiles hold 128 gate and 128 up columns");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles want 1024-byte alignment
@@ -54,7 +66,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr bool kPair = EPI == GE_SILU;
   const int m0 = blockIdx.y * kGemmBM;
-  const int n0 = blockIdx.x * (kPair ? kGemmBN / 2 : kGemmBN);  // first output column of the tile
+  const int n0 = blockIdx.x * (kPair ? BN / 2 : BN);  // first output column of the tile
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemmStages; ++i) {
@@ -79,7 +91,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {  // ---- TMA producer
       const uint32_t bytes = (p.two_a ? 2 * kTileA : kTileA) + kTileB;
       const int rb0 = kPair ? n0 : n0;
-      const int rb1 = kPair ? p.pair_offset + n0 : n0 + kGemmBN / 2;
+      const int rb1 = kPair ? p.pair_offset + n0 : n0 + BN / 2;
       int issued = 0;
       for (int kb = 0; kb < p.nk; ++kb) {
         const int s = kb % kGemmStages;
@@ -90,7 +102,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tma_load_2d(st, &tm_a_hi, x, m0, &full[s]);
         if (p.two_a) tma_load_2d(st + kTileA, &tm_a_lo, x, m0, &full[s]);
         tma_load_2d(st + 2 * kTileA, &tm_w, x, rb0, &full[s]);
-        tma_load_2d(st + 2 * kTileA + kTileB / 2, &tm_w, x, rb1, &full[s]);
+        if (BN == 256) tma_load_2d(st + 2 * kTileA + kTileB / 2, &tm_w, x, rb1, &full[s]);
         issued = kb + 1;
       }
       for (int i = issued > kGemmStages ? issued - kGemmStages : 0; i < issued; ++i)
@@ -142,7 +154,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else {
-        for (int c = 0; c < kGemmBN / 32; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
           tmem_ld32(trow + c * 32, v);
           if (row >= p.M) continue;
           const int nb = n0 + c * 32;
@@ -195,28 +207,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-constexpr size_t kGemmSmem = kGemmStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-
 cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& w,
                            const GemmParams& p, cudaStream_t s) {
-  const int cols = p.epi == GE_SILU ? kGemmBN / 2 : kGemmBN;
-  const dim3 grid((p.N + cols - 1) / cols, (p.M + kGemmBM - 1) / kGemmBM);
+  const int mt = (p.M + kGemmBM - 1) / kGemmBM;
+  // Residual GEMMs (o_proj, down_proj: few output columns) take 128-wide tiles
+  // when 256-wide ones would leave most SMs idle.
+  const bool narrow = p.epi == GE_RESID && ((p.N + 255) / 256) * mt < 96;
+  if (narrow) {
+    const dim3 grid((p.N + 127) / 128, mt);
+    gemm_tc_kernel<GE_RESID, 128><<<grid, kGemmThreads, TcLayout<128>::smem, s>>>(a_hi, a_lo, w, p);
+    return cudaGetLastError();
+  }
+  const int cols = p.epi == GE_SILU ? 128 : 256;
+  const dim3 grid((p.N + cols - 1) / cols, mt);
+  constexpr size_t smem = TcLayout<256>::smem;
   switch (p.epi) {
-    case GE_QKV: gemm_tc_kernel<GE_QKV><<<grid, kGemmThreads, kGemmSmem, s>>>(a_hi, a_lo, w, p); break;
-    case GE_RESID: gemm_tc_kernel<GE_RESID><<<grid, kGemmThreads, kGemmSmem, s>>>(a_hi, a_lo, w, p); break;
-    default: gemm_tc_kernel<GE_SILU><<<grid, kGemmThreads, kGemmSmem, s>>>(a_hi, a_lo, w, p); break;
+    case GE_QKV: gemm_tc_kernel<GE_QKV, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, p); break;
+    case GE_RESID: gemm_tc_kernel<GE_RESID, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, p); break;
+    default: gemm_tc_kernel<GE_SILU, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, p); break;
   }
   return cudaGetLastError();
 }
 
 cudaError_t configure_gemm_tc(int max_smem_optin) {
-  if (static_cast<int>(kGemmSmem) > max_smem_optin) return cudaErrorInvalidValue;
+  if (static_cast<int>(TcLayout<256>::smem) > max_smem_optin || static_cast<int>(TcLayout<128>::smem) > max_smem_optin)
+    return cudaErrorInvalidValue;
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(gemm_tc_kernel<GE_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem)))
+  if ((e = cudaFuncSetAttribute(gemm_tc_kernel<GE_QKV, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TcLayout<256>::smem)) ||
+      (e = cudaFuncSetAttribute(gemm_tc_kernel<GE_RESID, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TcLayout<256>::smem)) ||
+      (e = cudaFuncSetAttribute(gemm_tc_kernel<GE_SILU, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TcLayout<256>::smem)) ||
+      (e = cudaFuncSetAttribute(gemm_tc_kernel<GE_RESID, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TcLayout<128>::smem)))
     return e;
-  if ((e = cudaFuncSetAttribute(gemm_tc_kernel<GE_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem)))
-    return e;
-  return cudaFuncSetAttribute(gemm_tc_kernel<GE_SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  return cudaSuccess;
 }
 
 // ---------------------------------------------------------------- tensor maps
