@@ -210,3 +210,24 @@ def test_errors(oracle, vv):
     # the context stays usable after errors
     gpu.reset()
     assert gpu.forward_token(1, 0).shape == (cfg.vocab_size,)
+
+
+def test_fused_down_proj_plan_matches_oracle(oracle, vv, monkeypatch):
+    # The opt-in megakernel plan that fuses down_proj into gate|up (transposed
+    # down rows, fixed-point reduction) against the oracle, layer by layer.
+    monkeypatch.setenv("VVLI_MEGA_FUSED_DOWN", "1")
+    cfg, seed = fixture_configs()["llama3_tiny_rs"]
+    ref, gpu, _ = make_pair(oracle, vv, cfg, seed, 64)
+    assert gpu.query("megakernel") == 1
+    gpu.set_debug(True)
+    for pos, tok in enumerate([7, 3, 250, 19, 64, 1]):
+        lr = ref.forward_token(tok, pos)
+        lg = gpu.forward_token(tok, pos)
+        for layer in range(cfg.num_hidden_layers):
+            assert rel_l2(gpu.debug_hidden(layer), ref.hidden(layer)) < TIGHT_REL_L2, (pos, layer)
+        assert np.max(np.abs(lg - lr)) < 1e-4
+    gpu.set_debug(False)
+    ref.reset()
+    gpu.reset()
+    prompt = [1, 2, 3, 4]
+    assert gpu.generate_greedy(prompt, 24)[0] == ref.generate_greedy(prompt, 24)

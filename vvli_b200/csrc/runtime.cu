@@ -1632,7 +1632,17 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
   h->path = 0;
   h->k = 0;
   CK(cudaMemcpyAsync(c->smp_state, h, sizeof(SampleState), cudaMemcpyHostToDevice, c->stream));
-  CK(launch_sample(p, c->stream));
+  const uint64_t limit = o->top_k == 0 ? c->V : std::min<uint64_t>(o->top_k, c->V);
+  const int nblk = (c->V + 1023) / 1024;
+  int npow2 = 1;
+  while (npow2 < nblk * static_cast<int>(std::min<uint64_t>(limit, kSampleFastK))) npow2 <<= 1;
+  if (o->temperature > 0.0f && limit <= static_cast<uint64_t>(kSampleFastK) && npow2 <= kSampleFastMaxCand) {
+    // the candidates reuse the long path's buffers (V keys >= ceil(V / 1024) * 64)
+    CK(launch_sample_fast(p, static_cast<int>(limit), c->smp_key64, reinterpret_cast<unsigned*>(c->smp_key32),
+                          c->stream));
+  } else {
+    CK(launch_sample(p, c->stream));
+  }
   CK(cudaMemcpyAsync(h, c->smp_state, sizeof(SampleState), cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   if (h->path == 1) {

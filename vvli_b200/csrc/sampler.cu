@@ -132,6 +132,131 @@ __device__ int block_argmax(float v, int i, float* wv, int* wi) {
   return r;
 }
 
+// prepareProbabilities (:428-449) and sampleCandidate (:451-463) over the k
+// keys cand[0, k), sorted descending, in shared memory; every thread calls it.
+__device__ void finish_sorted(const SampleParams& p, const unsigned long long* cand, float* probs, unsigned k) {
+  const int tid = threadIdx.x;
+  SampleState* st = p.st;
+  const float t = fmaxf(p.temperature, 1e-6f);
+  const float mx = key_value(static_cast<unsigned>(cand[0] >> 32));
+  for (int j = tid; j < static_cast<int>(k); j += blockDim.x) probs[j] = prob_of(key_value(static_cast<unsigned>(cand[j] >> 32)), mx, t);
+  __syncthreads();
+  if (tid == 0) {
+    float total = 0.0f;
+    for (unsigned j = 0; j < k; ++j) total += probs[j];
+    unsigned count = k;
+    if (!(total > 0.0f) || !isfinite(total)) {
+      count = 1;
+    } else if (p.top_p < 1.0f) {
+      float cum = 0.0f;
+      for (unsigned j = 0; j < k; ++j) {
+        cum += probs[j];
+        if (cum / total >= p.top_p) {
+          count = j + 1;
+          break;
+        }
+      }
+    }
+    unsigned long long s[4] = {st->rng[0], st->rng[1], st->rng[2], st->rng[3]};
+    const float u = xoshiro_float(s);
+    float total2 = 0.0f;
+    for (unsigned j = 0; j < count; ++j) total2 += probs[j];
+    unsigned tok = key64_id(cand[0]);
+    if (total2 > 0.0f && isfinite(total2)) {
+      const float target = fminf(u, 0.99999994f) * total2;
+      float cum = 0.0f;
+      tok = key64_id(cand[count - 1]);
+      for (unsigned j = 0; j < count; ++j) {
+        cum += probs[j];
+        if (target <= cum) {
+          tok = key64_id(cand[j]);
+          break;
+        }
+      }
+    }
+    for (int q = 0; q < 4; ++q) st->rng[q] = s[q];
+    st->token = static_cast<int>(tok);
+    st->path = 0;
+  }
+}
+
+// Bitonic sort, descending, of n (a power of two) keys in shared memory by the whole CTA.
+__device__ void bitonic_desc(unsigned long long* a, int n) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const unsigned long long x = a[lo], y = a[hi];
+        if ((x < y) == desc) {
+          a[lo] = y;
+          a[hi] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Small top-k (k <= kSampleFastK), first pass: CTA b sorts the keys of ids
+// [1024 b, 1024 b + 1024) and keeps its best k; the finite count is summed.
+__global__ void __launch_bounds__(512) topk_local_kernel(const SampleParams p, int k, unsigned long long* cand,
+                                                         unsigned* nfin) {
+  __shared__ unsigned long long keys[1024];
+  __shared__ unsigned cnt;
+  const int tid = threadIdx.x;
+  if (tid == 0) cnt = 0;
+  __syncthreads();
+  unsigned mine = 0;
+  for (int i = tid; i < 1024; i += 512) {
+    const int id = blockIdx.x * 1024 + i;
+    unsigned long long key = 0ull;
+    if (id < p.V) {
+      const float s = adjusted_logit(p.logits[id], p.stamp[id] == p.call, p.repeat_penalty);
+      if (isfinite(s)) {
+        key = make_key64(order_key(s), id);
+        ++mine;
+      }
+    }
+    keys[i] = key;
+  }
+  atomicAdd(&cnt, mine);
+  __syncthreads();
+  bitonic_desc(keys, 1024);
+  if (tid == 0) atomicAdd(nfin, cnt);
+  for (int i = tid; i < k; i += 512) cand[static_cast<size_t>(blockIdx.x) * k + i] = keys[i];
+}
+
+// Second pass: sort the CTAs' candidates (padded to a power of two) and finish.
+__global__ void __launch_bounds__(1024) topk_merge_kernel(const SampleParams p, int k_req, int ncand, int npow2,
+                                                          const unsigned long long* cand, const unsigned* nfin) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem);  // [npow2]
+  float* probs = reinterpret_cast<float*>(keys + npow2);                     // [kSampleFastK]
+  const unsigned n_finite = *nfin;
+  SampleState* st = p.st;
+  if (n_finite == 0) {  // no candidate: llm.argmax of the raw logits (:115), rare
+    if (threadIdx.x == 0) {
+      float bv = p.logits[0];
+      int bi = 0;
+      for (int i = 1; i < p.V; ++i)
+        if (p.logits[i] > bv) {
+          bv = p.logits[i];
+          bi = i;
+        }
+      st->token = bi;
+      st->path = 0;
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < npow2; i += blockDim.x) keys[i] = i < ncand ? cand[i] : 0ull;
+  __syncthreads();
+  bitonic_desc(keys, npow2);
+  const unsigned k = min(static_cast<unsigned>(k_req), n_finite);
+  finish_sorted(p, keys, probs, k);
+}
+
 __global__ void sample_mark_kernel(const uint32_t* recent, int n, unsigned* stamp, unsigned call, int V) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) {
@@ -299,48 +424,7 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(const SampleParams p) {
       __syncthreads();
     }
   }
-  // prepareProbabilities (:428-449) and sampleCandidate (:451-463).
-  const float t = fmaxf(p.temperature, 1e-6f);
-  const float mx = key_value(static_cast<unsigned>(cand[0] >> 32));
-  for (int j = tid; j < static_cast<int>(k); j += kST) probs[j] = prob_of(key_value(static_cast<unsigned>(cand[j] >> 32)), mx, t);
-  __syncthreads();
-  if (tid == 0) {
-    float total = 0.0f;
-    for (unsigned j = 0; j < k; ++j) total += probs[j];
-    unsigned count = k;
-    if (!(total > 0.0f) || !isfinite(total)) {
-      count = 1;
-    } else if (p.top_p < 1.0f) {
-      float cum = 0.0f;
-      for (unsigned j = 0; j < k; ++j) {
-        cum += probs[j];
-        if (cum / total >= p.top_p) {
-          count = j + 1;
-          break;
-        }
-      }
-    }
-    unsigned long long s[4] = {st->rng[0], st->rng[1], st->rng[2], st->rng[3]};
-    const float u = xoshiro_float(s);
-    float total2 = 0.0f;
-    for (unsigned j = 0; j < count; ++j) total2 += probs[j];
-    unsigned tok = key64_id(cand[0]);
-    if (total2 > 0.0f && isfinite(total2)) {
-      const float target = fminf(u, 0.99999994f) * total2;
-      float cum = 0.0f;
-      tok = key64_id(cand[count - 1]);
-      for (unsigned j = 0; j < count; ++j) {
-        cum += probs[j];
-        if (target <= cum) {
-          tok = key64_id(cand[j]);
-          break;
-        }
-      }
-    }
-    for (int q = 0; q < 4; ++q) st->rng[q] = s[q];
-    st->token = static_cast<int>(tok);
-    st->path = 0;
-  }
+  finish_sorted(p, cand, probs, k);
 }
 
 // Step 4 over the first st->k keys of the sorted vocabulary.
@@ -425,8 +509,25 @@ cudaError_t launch_sample_long(const SampleParams& p, void* temp, size_t temp_by
   return cudaGetLastError();
 }
 
+cudaError_t launch_sample_fast(const SampleParams& p, int k, unsigned long long* cand, unsigned* nfin, cudaStream_t s) {
+  const int nblk = (p.V + 1023) / 1024;
+  const int ncand = nblk * k;
+  int npow2 = 1;
+  while (npow2 < ncand) npow2 <<= 1;
+  if (k < 1 || k > kSampleFastK || npow2 > kSampleFastMaxCand) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(nfin, 0, sizeof(unsigned), s);
+  if (e) return e;
+  topk_local_kernel<<<nblk, 512, 0, s>>>(p, k, cand, nfin);
+  const size_t smem = static_cast<size_t>(npow2) * 8 + kSampleFastK * 4;
+  topk_merge_kernel<<<1, 1024, smem, s>>>(p, k, ncand, npow2, cand, nfin);
+  return cudaGetLastError();
+}
+
 cudaError_t configure_sampler() {
-  return cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSampleSmem));
+  cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSampleSmem));
+  if (e) return e;
+  return cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(static_cast<size_t>(kSampleFastMaxCand) * 8 + kSampleFastK * 4));
 }
 
 }  // namespace vvli
