@@ -51,6 +51,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling small cases)")
     ap.add_argument("--batch", type=int, default=16, help="rows of the decode-batch measurement (0: skip)")
+    ap.add_argument("--profile", choices=["none", "prefill", "batch", "decode"], default="none",
+                    help="run one call of that kind inside a CUDA profiler range (for ncu --profile-from-start off) "
+                         "on a --layers cut of the model, print nothing, exit")
     return ap.parse_args()
 
 
@@ -212,8 +215,52 @@ def _second_id(dist, vvli_b200, rank):
     return obj[0]
 
 
+def profile_case(args):
+    """One prefill / batch step / decode step inside cudaProfilerStart/Stop, after warm-up calls."""
+    import numpy as np
+    import torch
+    import vvli_b200
+    from vvli_b200.config import PRESETS
+
+    cfg = PRESETS[args.config]()
+    if args.layers:
+        cfg.num_hidden_layers = args.layers
+    torch.cuda.init()
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, size=args.prompt).astype(np.uint32)
+    if args.profile == "batch":
+        B = max(1, args.batch)
+        r = vvli_b200.Runner(cfg, max_seq=args.prompt + 64, max_batch=B)
+        r.fill_synthetic(args.seed)
+        toks = list(range(1, B + 1))
+        for w in range(2):
+            r.forward_batch(toks, [args.prompt + w] * B, logits=False)
+        call = lambda: r.forward_batch(toks, [args.prompt + 2] * B, logits=False)
+    elif args.profile == "prefill":
+        r = vvli_b200.Runner(cfg, max_seq=args.prompt + 64)
+        r.fill_synthetic(args.seed)
+        r.prefill(prompt, 0, logits=False)
+
+        def call():
+            r.reset()
+            r.prefill(prompt, 0, logits=False)
+    else:
+        r = vvli_b200.Runner(cfg, max_seq=args.prompt + 64)
+        r.fill_synthetic(args.seed)
+        r.prefill(prompt, 0, logits=False)
+        r.decode(3)
+        call = lambda: r.decode(2)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    call()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    r.close()
+
+
 def main():
     args = parse_args()
+    if args.profile != "none":
+        return profile_case(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -41,7 +41,7 @@ def _rank_main(rank, world, nccl_id, cfg, blob, prompt, n_new, mega, q):
         def note(what):
             print(f"[rank {rank} +{time.time() - t0:.1f}s] {what}", file=sys.stderr, flush=True)
 
-        r = vvli_b200.Runner(cfg, max_seq=128, device=rank, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+        r = vvli_b200.Runner(cfg, max_seq=128, device=rank, tp_rank=rank, tp_size=world, nccl_id=nccl_id, max_batch=3)
         r.load_weights(blob)
         used_mega = r.query("megakernel") == 1
         note(f"created, megakernel={used_mega} ({vvli_b200._abi.lib().vvli_cuda_last_error().decode()})")
@@ -50,10 +50,13 @@ def _rank_main(rank, world, nccl_id, cfg, blob, prompt, n_new, mega, q):
         r.reset()
         tokens, _ = r.generate_greedy(prompt, n_new)
         note("generate done")
+        # decode batch under tensor parallelism: three sequences' first tokens
+        blogits, bam = r.forward_batch(prompt[:3], [0, 0, 0])
+        note("forward_batch done")
         r.close()
-        q.put((rank, "ok", np.stack(logits), tokens, used_mega))
+        q.put((rank, "ok", np.stack(logits), tokens, used_mega, blogits, bam))
     except Exception as e:  # reported to the parent, which fails the test
-        q.put((rank, repr(e), None, None, None))
+        q.put((rank, repr(e), None, None, None, None, None))
 
 
 def run_tp(cfg, blob, prompt, n_new, world, mega=True):
@@ -70,15 +73,15 @@ def run_tp(cfg, blob, prompt, n_new, world, mega=True):
     results = {}
     try:
         for _ in range(world):
-            rank, status, logits, tokens, used_mega = q.get(timeout=120)
-            results[rank] = (status, logits, tokens, used_mega)
+            rank, status, logits, tokens, used_mega, blogits, bam = q.get(timeout=120)
+            results[rank] = (status, logits, tokens, used_mega, blogits, bam)
     finally:
         for p in procs:  # the ranks this test started, and only those
             p.join(timeout=30)
             if p.is_alive():
                 p.kill()
                 p.join(timeout=10)
-    for rank, (status, _, _, used_mega) in results.items():
+    for rank, (status, _, _, used_mega, _, _) in results.items():
         assert status == "ok", (rank, status)
         assert used_mega == mega, (rank, used_mega)
     return results
@@ -98,9 +101,15 @@ def test_tp2_matches_oracle(oracle, name, mega):
     ref_tokens = ref.generate_greedy(prompt, 24)
     res = run_tp(cfg, blob, prompt, 24, 2, mega)
     for rank in range(2):
-        _, logits, tokens, _ = res[rank]
+        _, logits, tokens, _, blogits, bam = res[rank]
         assert np.max(np.abs(logits - ref_logits)) < 1e-4, rank
         assert tokens == ref_tokens, rank
+        # batch rows b: token prompt[b] at position 0 of its own sequence
+        for b in range(3):
+            ref.reset()
+            want = ref.forward_token(prompt[b], 0)
+            assert np.max(np.abs(blogits[b] - want)) < 2e-3, (rank, b)
+            assert bam[b] == oracle.argmax(want), (rank, b)
 
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
@@ -114,6 +123,6 @@ def test_tp2_llama3_2_1b_architecture(oracle):
     ref.reset()
     ref_tokens = ref.generate_greedy(prompt, 16)
     res = run_tp(cfg, blob, prompt, 16, 2)
-    _, logits, tokens, _ = res[0]
+    _, logits, tokens, _, _, _ = res[0]
     assert np.max(np.abs(logits - ref_logits)) < 2e-2
     assert tokens == ref_tokens
