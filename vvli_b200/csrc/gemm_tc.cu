@@ -437,8 +437,7 @@ __global__ void __launch_bounds__(kPaThreads) prefill_attention_kernel(const Pre
 // positions (one KV page) are staged transposed (K) and as-is (V) in shared
 // memory; thread t owns query rows 4 (t / 8) .. + 3, and score columns
 // 8 (t % 8) .. + 7 of a tile (32 scores from 3 shared loads per k), then
-// output dims 32 q + 4 (t % 8) + {0..3} of its 4 rows for P.V (so the 8 lanes
-// of a row read V rows without bank conflicts).  Online softmax per row
+// output dims (t % 8) D / 8 .. of its 4 rows for P.V.  Online softmax per row
 // across the row's 8 lanes; causal mask by position.  Output as bf16 hi / lo
 // for the o_proj GEMM.
 constexpr int kFaThreads = 256;
@@ -570,10 +569,10 @@ __global__ void __launch_bounds__(kFaThreads, 1) prefill_flash_kernel(const Pref
       float pr[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) pr[i] = ps[(4 * rg + i) * kFaPs + j];
-      const float4* vr = reinterpret_cast<const float4*>(vs + j * D + 4 * cg);
+      const float4* vr = reinterpret_cast<const float4*>(vs + j * D + cg * DD);
 #pragma unroll
       for (int e4 = 0; e4 < DD / 4; ++e4) {
-        const float4 v = vr[8 * e4];  // dims 32 e4 + 4 cg ..: the 8 lanes of a row read 128 contiguous bytes
+        const float4 v = vr[e4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           o[i][4 * e4 + 0] = fmaf(pr[i], v.x, o[i][4 * e4 + 0]);
@@ -589,13 +588,10 @@ __global__ void __launch_bounds__(kFaThreads, 1) prefill_flash_kernel(const Pref
     const int r = 4 * rg + i;
     if (r >= rows) continue;
     const int t = r / G, hh = r % G;
-    const size_t orow = static_cast<size_t>(t0 + t) * qd + static_cast<size_t>(g * G + hh) * D;
+    const size_t orow = static_cast<size_t>(t0 + t) * qd + static_cast<size_t>(g * G + hh) * D + cg * DD;
     const float inv = 1.0f / l[i];
 #pragma unroll
-    for (int e = 0; e < DD; ++e) {
-      const int dim = 32 * (e / 4) + 4 * cg + (e % 4);
-      split_bf16(o[i][e] * inv, p.out_hi[orow + dim], p.out_lo[orow + dim]);
-    }
+    for (int e = 0; e < DD; ++e) split_bf16(o[i][e] * inv, p.out_hi[orow + e], p.out_lo[orow + e]);
   }
 }
 
