@@ -157,7 +157,7 @@ def time_oracle(cfg, seed, seconds, min_tokens=2, max_tokens=None):
     return n / el, cores, sample
 
 
-def run_reference(args, rank):
+def run_reference(args, rank, out_fd=1):
     if rank != 0:
         return 0
     from vvli_b200.config import PRESETS
@@ -197,7 +197,7 @@ def run_reference(args, rank):
                              "what": "C++ restatement of the reference CPU path (src/llm.zig, src/generator.zig); "
                                      "the Zig reference cannot be built here"},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line, out_fd)
     return 0
 
 
@@ -261,11 +261,29 @@ def main():
     args = parse_args()
     if args.profile != "none":
         return profile_case(args)
+    # Libraries (NCCL, torch.distributed) may print to stdout; the JSON line is the
+    # only thing this process writes there: everything else goes to stderr.
+    real_stdout = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    try:
+        return _main(args, real_stdout)
+    finally:
+        sys.stdout.flush()
+        os.dup2(real_stdout, 1)
+
+
+def emit(line: dict, fd: int) -> None:
+    """Writes the result line to the real stdout."""
+    os.write(fd, (json.dumps(line) + "\n").encode())
+
+
+def _main(args, out_fd):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        return run_reference(args, rank)
+        return run_reference(args, rank, out_fd)
 
     import numpy as np
     import torch
@@ -426,7 +444,7 @@ def main():
                 "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "prefill": prefill, "sampler": sampler_line, "batch": batch,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clk}
-        print(json.dumps(line), flush=True)
+        emit(line, out_fd)
     runner.close()
     if n > 1:
         dist.barrier()
