@@ -368,7 +368,9 @@ def _main(args, out_fd):
         achieved = step_bytes / (ms_per_step / 1000.0) / 1e9
         roofline = {"kernel": "decode_megakernel (one launch per token)", "bound": "hbm", "achieved": achieved,
                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "frac_of_8TBs_spec": achieved / 8000.0,
-                    "peak_source": peak_src, "traffic": ncu_traffic("decode_megakernel"),
+                    "peak_source": peak_src,
+                    # the committed capture is of the 1-GPU kernel; ranks of a tensor-parallel run differ
+                    "traffic": ncu_traffic("decode_megakernel") if n == 1 else None,
                     "bytes_per_launch": step_bytes, "launch_ms": ms_per_step,
                     "bytes_per_launch_definition": "all weight matrices (bf16) + norms/biases + fp32 KV read "
                                                    "for positions 0..p + KV row written, p = mean position",
