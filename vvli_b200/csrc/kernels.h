@@ -131,11 +131,6 @@ struct MegaParams {
   const MegaPhase* phases;
   int nphases;
   int nst, slot_bytes, part_floats;  // shared-memory ring and partial-sum area
-  int lookahead;           // stages the producer prefetches into L2 beyond the ring
-  // L2 prefetches issued by the consumers while the ring is full and HBM would idle:
-  int pf_attn_next;        // attention phase: the next GEMV phase's stages beyond the ring (0/1)
-  int pf_attn_rows;        // attention phase: first rows per matrix of the GEMV phase after that
-  int pf_epi_stages;       // end of a GEMV phase: stages of the next phase beyond the ring
   StepState* st;
   int* seq_tokens;
   const uint16_t* emb;

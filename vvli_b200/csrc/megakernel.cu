@@ -121,27 +121,6 @@ VVLI_DEV void trace_mark(const MegaParams& P, int f, int k) {
   if (P.trace) P.trace[(static_cast<size_t>(f) * gridDim.x + blockIdx.x) * 6 + k] = global_timer_ns();
 }
 
-// L2 prefetch of rows [ra, rb) of this CTA's share of GEMV phase `ph` (each
-// matrix of a pair), in 64 KB pieces spread over `nlanes` threads.  Used
-// while the ring is full, so HBM keeps streaming weights that the producer
-// will copy from L2 soon after.
-__device__ void prefetch_rows(const MegaPhase& ph, int ra, int rb, int t, int nlanes) {
-  const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
-  const int nrows = cta_row(ph.N, blockIdx.x + 1, ph.row_align) - r0;
-  ra = max(0, min(ra, nrows));
-  rb = min(rb, nrows);
-  if (rb <= ra) return;
-  const size_t total = static_cast<size_t>(rb - ra) * ph.K * 2;
-  constexpr size_t kPiece = 65536;
-  const size_t pieces = (total + kPiece - 1) / kPiece;
-  for (size_t c = t; c < pieces * ph.nphys; c += nlanes) {
-    const int q = static_cast<int>(c / pieces);
-    const size_t off = (c % pieces) * kPiece;
-    const uint8_t* base = reinterpret_cast<const uint8_t*>(ph.W + static_cast<size_t>(r0 + ra + q * ph.pair_offset) * ph.K);
-    prefetch_l2_bulk(base + off, static_cast<uint32_t>(min(kPiece, total - off)));
-  }
-}
-
 // Fixed-point accumulators of the fused down_proj (see MegaPhase::acc_out):
 // v -> round(v * 2^32) as a 64-bit integer; integer sums do not depend on
 // the order of the adds, so the result is the same on every run.
@@ -171,19 +150,7 @@ struct StageCursor {
 };
 
 __device__ void mega_producer(const MegaParams& P, uint8_t* ring, uint64_t* full, uint64_t* empty, int* err) {
-  StageCursor cur, ahead;  // i = 0 >= nstages = 0: the first next() loads the first GEMV phase
-  bool ahead_ok = true;
-  // The L2 lookahead runs `lookahead` stages in front of the copies into the ring.
-  for (int k = 0; k < P.nst + P.lookahead && ahead_ok; ++k) {
-    ahead_ok = ahead.next(P);
-    if (ahead_ok && k >= P.nst) {
-      const MegaPhase& ph = P.phases[ahead.f];
-      const int rows_here = min(ph.R, ahead.nrows - ahead.i * ph.R);
-      const uint32_t bytes = static_cast<uint32_t>(rows_here * ph.K * 2);
-      for (int q = 0; q < ph.nphys; ++q)
-        prefetch_l2_bulk(ph.W + static_cast<size_t>(ahead.r0 + ahead.i * ph.R + q * ph.pair_offset) * ph.K, bytes);
-    }
-  }
+  StageCursor cur;  // i = 0 >= nstages = 0: the first next() loads the first GEMV phase
   uint32_t gi = 0;
   int last_f = -1;
   while (cur.next(P)) {
@@ -202,13 +169,6 @@ __device__ void mega_producer(const MegaParams& P, uint8_t* ring, uint64_t* full
       bulk_g2s(ring + static_cast<size_t>(slot) * P.slot_bytes + q * ph.R * row_bytes,
                ph.W + static_cast<size_t>(cur.r0 + cur.i * ph.R + q * ph.pair_offset) * ph.K, bytes, &full[slot]);
     ++gi;
-    if (ahead_ok && (ahead_ok = ahead.next(P))) {
-      const MegaPhase& pa = P.phases[ahead.f];
-      const int ra = min(pa.R, ahead.nrows - ahead.i * pa.R);
-      const uint32_t ab = static_cast<uint32_t>(ra * pa.K * 2);
-      for (int q = 0; q < pa.nphys; ++q)
-        prefetch_l2_bulk(pa.W + static_cast<size_t>(ahead.r0 + ahead.i * pa.R + q * pa.pair_offset) * pa.K, ab);
-    }
   }
   // Every issued copy lands before the CTA exits.
   const uint32_t first = gi > static_cast<uint32_t>(P.nst) ? gi - P.nst : 0;
@@ -351,11 +311,6 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
   named_barrier(1, kNC);
   if (tid == 0) trace_mark(P, f, 2);
   const float scale = scale_sh;
-  if (P.pf_epi_stages > 0 && warp == 1 && f + 1 < P.nphases && P.phases[f + 1].kind == MK_GEMV) {
-    // The producer has issued the next phase's first nst stages; warm L2 with the following ones.
-    const MegaPhase& nx = P.phases[f + 1];
-    prefetch_rows(nx, P.nst * nx.R, (P.nst + P.pf_epi_stages) * nx.R, lane, kWarp);
-  }
 
   // ---- epilogue
   if (ph.epi == ME_QKV) {
@@ -885,13 +840,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
     if (ph.kind == MK_EMBED) {
       mega_embed(P, red, err);
     } else if (ph.kind == MK_ATTN) {
-      if (warp == kCW - 1 && f + 2 < P.nphases) {
-        // Attention reads little from HBM and the ring is full: prefetch the
-        // next phase's rows beyond the ring and the head of the one after.
-        if (P.pf_attn_next) prefetch_rows(P.phases[f + 1], P.nst * P.phases[f + 1].R, 1 << 30, tid & 31, kWarp);
-        if (P.pf_attn_rows > 0 && P.phases[f + 2].kind == MK_GEMV)
-          prefetch_rows(P.phases[f + 2], 0, P.pf_attn_rows, tid & 31, kWarp);
-      }
       mega_attention(P, ph, part, err, f);
     } else if (ph.epi == ME_AXPY) {
       mega_axpy(P, ph, ring, full, empty, gi, ffs, err, f);

@@ -474,12 +474,6 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   P.nphases = static_cast<int>(ph.size());
   P.nst = nst;
   P.slot_bytes = slot;
-  // L2 prefetch beyond the ring: off by default (measured slower on B200:
-  // prefetched lines were evicted before the bulk copies read them).
-  P.lookahead = getenv("VVLI_MEGA_LOOKAHEAD") ? atoi(getenv("VVLI_MEGA_LOOKAHEAD")) : 0;
-  P.pf_attn_next = getenv("VVLI_MEGA_PF_ATTN_NEXT") ? atoi(getenv("VVLI_MEGA_PF_ATTN_NEXT")) : 0;
-  P.pf_attn_rows = getenv("VVLI_MEGA_PF_ATTN_ROWS") ? atoi(getenv("VVLI_MEGA_PF_ATTN_ROWS")) : 0;
-  P.pf_epi_stages = getenv("VVLI_MEGA_PF_EPI_STAGES") ? atoi(getenv("VVLI_MEGA_PF_EPI_STAGES")) : 0;
   P.part_floats = static_cast<int>(part);
   P.st = c->st;
   P.seq_tokens = c->seq_tokens;
