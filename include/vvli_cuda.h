@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-/* Error codes.  1..9 map 1:1 onto llm.Error (src/llm.zig:17-27) and
+/* Error codes.  1..10 map 1:1 onto llm.Error (src/llm.zig:17-27) and
  * generator.Error (src/generator.zig:8-12); 20.. are added by this runtime. */
 enum vvli_status {
   VVLI_OK = 0,
@@ -39,6 +39,7 @@ enum vvli_status {
   VVLI_ERR_EMPTY_PROMPT = 7,          /* generator.Error.EmptyPrompt */
   VVLI_ERR_OUTPUT_TOO_SMALL = 8,      /* generator.Error.OutputTooSmall */
   VVLI_ERR_INVALID_SAMPLING = 9,      /* generator.Error.InvalidSamplingOptions */
+  VVLI_ERR_MISSING_TENSOR = 10,       /* llm.Error.MissingSafetensorsTensor */
   VVLI_ERR_CUDA = 20,                 /* a CUDA runtime call failed */
   VVLI_ERR_NCCL = 21,                 /* an NCCL call failed or NCCL is missing */
   VVLI_ERR_TIMEOUT = 22,              /* a bounded device-side wait gave up */
@@ -172,6 +173,17 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
  * safetensors/GGUF loaders' final copy into OwnedModel (src/llm.zig:923-1006);
  * the caller keeps ownership of `blob`. */
 int vvli_cuda_load_weights(vvli_ctx* ctx, const uint16_t* blob, uint64_t n_elements);
+
+/* Loads this rank's weights straight from a safetensors file
+ * (loadOwnedFromSafetensorsFile + loadSafetensorsIntoOwnedModel,
+ * src/llm.zig:859-883, 923-1006): the file is memory-mapped and only the
+ * pieces of this rank's shard are copied to the device; F32 tensors are
+ * rounded to bf16 with the reference's f32ToBf16 on the device.  Errors as
+ * copyTensorIntoWeight: VVLI_ERR_MISSING_TENSOR, VVLI_ERR_UNSUPPORTED_DTYPE
+ * (not BF16 / F32), VVLI_ERR_INVALID_WEIGHT (shape or byte range); a file
+ * that cannot be opened gives VVLI_ERR_INVALID_ARGUMENT.  Same effect as
+ * vvli_cuda_load_weights on the blob the reference would build. */
+int vvli_cuda_load_safetensors(vvli_ctx* ctx, const char* path);
 
 /* Benchmark helper with no counterpart in the reference: fills the device
  * weights with the seeded synthetic model (every matrix and bias

@@ -23,6 +23,7 @@
 #include "gemm_tc.cuh"
 #include "batch.cuh"
 #include "kernels.h"
+#include "loader.h"
 #include "sampler.cuh"
 
 using namespace vvli;
@@ -1307,6 +1308,38 @@ int vvli_cuda_load_weights(vvli_ctx* c, const uint16_t* blob, uint64_t n) {
       CK(cudaMemcpy2DAsync(c->w + p.dst, p.cols * 2, src, p.src_ld * 2, p.cols * 2, p.rows, cudaMemcpyHostToDevice,
                            c->stream));
     }
+  }
+  return after_load(c);
+}
+
+// Element count of the reference tensor with blob order id `id`.
+static uint64_t tensor_elems(const vvli_model_config& cfg, uint64_t id) {
+  const uint64_t h = cfg.hidden_size, kv = cfg.num_key_value_heads * (cfg.hidden_size / cfg.num_attention_heads),
+                 I = cfg.intermediate_size, V = cfg.vocab_size, L = cfg.num_hidden_layers;
+  if (id == 0 || id == 2 + 12 * L) return V * h;
+  if (id == 1 + 12 * L) return h;
+  switch ((id - 1) % 12) {
+    case 0: case 2: case 8: return h;           // norms, q bias
+    case 1: case 7: return h * h;               // q, o
+    case 3: case 5: return kv * h;              // k, v
+    case 4: case 6: return kv;                  // k, v bias
+    default: return I * h;                      // gate, up, down
+  }
+}
+
+int vvli_cuda_load_safetensors(vvli_ctx* c, const char* path) {
+  if (!c || !path) return VVLI_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(c->device));
+  std::vector<LoadPiece> lp;
+  lp.reserve(c->pieces.size());
+  for (const Piece& p : c->pieces)
+    lp.push_back(LoadPiece{p.tensor_id, tensor_elems(c->cfg, p.tensor_id), p.dst, p.rows, p.cols, p.src_ld, p.row0,
+                           p.col0});
+  std::string why;
+  const int st = upload_safetensors(path, lp, c->L, c->w, c->stream, &why);
+  if (st != VVLI_OK) {
+    g_last_error = why;
+    return st;
   }
   return after_load(c);
 }

@@ -16,6 +16,7 @@ CODES = {
     7: "EmptyPrompt",
     8: "OutputTooSmall",
     9: "InvalidSamplingOptions",
+    10: "MissingSafetensorsTensor",
     20: "CudaError",
     21: "NcclError",
     22: "Timeout",

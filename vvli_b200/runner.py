@@ -11,6 +11,7 @@ the whole token loop on the device.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 
@@ -65,6 +66,10 @@ class Runner:
         """Uploads this rank's shard of an llm.OwnedModel-layout bf16 blob."""
         b = np.ascontiguousarray(blob, dtype=np.uint16)
         check(_abi.lib().vvli_cuda_load_weights(self._ctx, b.ctypes.data_as(_u16p), b.size))
+
+    def load_safetensors(self, path: str):
+        """This rank's weights straight from model.safetensors (loadOwnedFromSafetensorsFile)."""
+        check(_abi.lib().vvli_cuda_load_safetensors(self._ctx, os.fsencode(path)))
 
     def fill_synthetic(self, seed: int = 0):
         check(_abi.lib().vvli_cuda_fill_synthetic(self._ctx, seed))

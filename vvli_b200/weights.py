@@ -94,6 +94,31 @@ def _read_header(buf):
     return header, 8 + hlen
 
 
+def _copy_tensor(blob: np.ndarray, off: int, shape, name: str, meta, data: memoryview) -> None:
+    """copyTensorIntoWeight (src/llm.zig:1149-1183) into blob[off:]; views die with this frame."""
+    if meta is None:
+        raise VvliError("MissingSafetensorsTensor", -1, name)
+    dtype = meta.get("dtype")
+    if dtype not in ("BF16", "F32"):
+        raise VvliError("UnsupportedDType", None, name)
+    count = int(np.prod(meta.get("shape", [])))
+    start, end = meta["data_offsets"]
+    if count != int(np.prod(shape)) or end > len(data) or end < start:
+        raise VvliError("InvalidWeight", None, name)
+    raw = data[start:end]
+    try:
+        if dtype == "BF16":
+            if len(raw) != count * 2:
+                raise VvliError("InvalidWeight", None, name)
+            blob[off: off + count] = np.frombuffer(raw, dtype="<u2")
+        else:
+            if len(raw) != count * 4:
+                raise VvliError("InvalidWeight", None, name)
+            blob[off: off + count] = f32_to_bf16(np.frombuffer(raw, dtype="<f4"))
+    finally:
+        raw.release()
+
+
 def load_safetensors(path: str, cfg: Config) -> np.ndarray:
     """Reads model.safetensors into a new bf16 blob (loadSafetensorsIntoOwnedModel)."""
     blob = np.zeros(cfg.storage_element_count(), dtype=np.uint16)
@@ -102,27 +127,11 @@ def load_safetensors(path: str, cfg: Config) -> np.ndarray:
         try:
             header, data_start = _read_header(mm)
             data = memoryview(mm)[data_start:]
-            for name, off, shape, _ in tensor_entries(cfg):
-                meta = header.get(name)
-                if meta is None:
-                    raise VvliError("MissingSafetensorsTensor", -1, name)
-                dtype = meta.get("dtype")
-                if dtype not in ("BF16", "F32"):
-                    raise VvliError("UnsupportedDType", None, name)
-                count = int(np.prod(meta.get("shape", [])))
-                start, end = meta["data_offsets"]
-                if count != int(np.prod(shape)) or end > len(data) or end < start:
-                    raise VvliError("InvalidWeight", None, name)
-                raw = data[start:end]
-                if dtype == "BF16":
-                    if len(raw) != count * 2:
-                        raise VvliError("InvalidWeight", None, name)
-                    blob[off: off + count] = np.frombuffer(raw, dtype="<u2")
-                else:
-                    if len(raw) != count * 4:
-                        raise VvliError("InvalidWeight", None, name)
-                    blob[off: off + count] = f32_to_bf16(np.frombuffer(raw, dtype="<f4"))
-            del data
+            try:
+                for name, off, shape, _ in tensor_entries(cfg):
+                    _copy_tensor(blob, off, shape, name, header.get(name), data)
+            finally:
+                data.release()
         finally:
             mm.close()
     return blob
