@@ -27,7 +27,8 @@ extern "C" {
 #endif
 
 /* Error codes.  1..10 map 1:1 onto llm.Error (src/llm.zig:17-27) and
- * generator.Error (src/generator.zig:8-12); 20.. are added by this runtime. */
+ * generator.Error (src/generator.zig:8-12), 11..13 onto gguf.Error
+ * (src/gguf.zig:7-12); 20.. are added by this runtime. */
 enum vvli_status {
   VVLI_OK = 0,
   VVLI_ERR_CONTEXT_FULL = 1,          /* llm.Error.ContextFull */
@@ -40,6 +41,9 @@ enum vvli_status {
   VVLI_ERR_OUTPUT_TOO_SMALL = 8,      /* generator.Error.OutputTooSmall */
   VVLI_ERR_INVALID_SAMPLING = 9,      /* generator.Error.InvalidSamplingOptions */
   VVLI_ERR_MISSING_TENSOR = 10,       /* llm.Error.MissingSafetensorsTensor */
+  VVLI_ERR_INVALID_GGUF = 11,         /* gguf.Error.InvalidGguf */
+  VVLI_ERR_UNSUPPORTED_GGUF_VERSION = 12, /* gguf.Error.UnsupportedGgufVersion */
+  VVLI_ERR_UNSUPPORTED_METADATA_TYPE = 13, /* gguf.Error.UnsupportedMetadataType */
   VVLI_ERR_CUDA = 20,                 /* a CUDA runtime call failed */
   VVLI_ERR_NCCL = 21,                 /* an NCCL call failed or NCCL is missing */
   VVLI_ERR_TIMEOUT = 22,              /* a bounded device-side wait gave up */
@@ -184,6 +188,21 @@ int vvli_cuda_load_weights(vvli_ctx* ctx, const uint16_t* blob, uint64_t n_eleme
  * that cannot be opened gives VVLI_ERR_INVALID_ARGUMENT.  Same effect as
  * vvli_cuda_load_weights on the blob the reference would build. */
 int vvli_cuda_load_safetensors(vvli_ctx* ctx, const char* path);
+
+/* Loads this rank's weights straight from a GGUF file (loadOwnedFromGgufFile
+ * + loadGgufIntoOwnedModel + copyGgufTensorIntoWeight, src/llm.zig:885-921,
+ * 1008-1138; gguf.parse, src/gguf.zig:234-287).  The context's config must be
+ * the one Config.fromGguf builds from the same file (src/llm.zig:153-193):
+ * rope_layout INTERLEAVED (else VVLI_ERR_INVALID_CONFIG) and no q/k/v biases
+ * (else VVLI_ERR_UNSUPPORTED_ARCH, as the reference).  Tensors may be F32,
+ * F16 or BF16; F32 and F16 are rounded with f32ToBf16 on the device.  Errors:
+ * VVLI_ERR_INVALID_GGUF, VVLI_ERR_UNSUPPORTED_GGUF_VERSION,
+ * VVLI_ERR_UNSUPPORTED_METADATA_TYPE (as gguf.parse), then as
+ * copyGgufTensorIntoWeight: VVLI_ERR_MISSING_TENSOR,
+ * VVLI_ERR_UNSUPPORTED_DTYPE (a quantised type), VVLI_ERR_INVALID_WEIGHT
+ * (element count or byte range); a file that cannot be opened gives
+ * VVLI_ERR_INVALID_ARGUMENT. */
+int vvli_cuda_load_gguf(vvli_ctx* ctx, const char* path);
 
 /* Benchmark helper with no counterpart in the reference: fills the device
  * weights with the seeded synthetic model (every matrix and bias

@@ -48,6 +48,13 @@ def test_strerror_and_storage_elements_without_gpu():
         assert n.value == cfg.storage_element_count()
 
 
+def test_strerror_names_every_status():
+    from vvli_b200 import _abi
+    from vvli_b200.errors import CODES
+    for code, name in CODES.items():
+        assert _abi.strerror(code) == name, code
+
+
 def test_config_struct_matches_c_layout():
     from vvli_b200.config import CModelConfig
     assert ctypes.sizeof(CModelConfig) == 9 * 8 + 14 * 4 + 8 == 136

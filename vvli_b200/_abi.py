@@ -73,6 +73,7 @@ SIGNATURES = {
                                                     ctypes.c_void_p, ctypes.c_void_p]),
     "vvli_cuda_sample": (ctypes.c_int, [_ctx, ctypes.c_void_p, _f32p, _u32p, ctypes.c_uint64, _u64p, _u32p]),
     "vvli_cuda_load_safetensors": (ctypes.c_int, [_ctx, ctypes.c_char_p]),
+    "vvli_cuda_load_gguf": (ctypes.c_int, [_ctx, ctypes.c_char_p]),
     "vvli_cuda_set_debug": (ctypes.c_int, [_ctx, ctypes.c_int]),
     "vvli_cuda_debug_hidden": (ctypes.c_int, [_ctx, ctypes.c_int, _f32p]),
     "vvli_cuda_last_forward_ms": (ctypes.c_int, [_ctx, _f32p]),

@@ -1,6 +1,6 @@
 """Model configuration: the host-side mirror of llm.Config.
 
-Follows src/llm.zig:77-276 (Config, fromJson, validate, headDim, kvDim,
+Follows src/llm.zig:77-276 (Config, fromJson, fromGguf, validate, headDim, kvDim,
 kvGroupSize, layerParameterCount, parameterCount) and src/llm.zig:814-837
 (storageElementCount for the bf16 weight blob).  The one extension is
 ``rope_scaling`` (llama3 type), which the reference never reads; pass
@@ -284,6 +284,52 @@ class Config:
                 cfg.rope_low_freq_factor = _f32(float(rs.get("low_freq_factor", 1.0)))
                 cfg.rope_high_freq_factor = _f32(float(rs.get("high_freq_factor", 4.0)))
                 cfg.rope_original_max_position = int(rs.get("original_max_position_embeddings", 8192))
+        cfg.validate()
+        return cfg
+
+    # ------------------------------------------------------------ Config.fromGguf (src/llm.zig:153-193)
+    @classmethod
+    def from_gguf(cls, file) -> "Config":
+        """The config of a parsed GGUF file (``vvli_b200.gguf.parse``): interleaved RoPE, no q/k/v biases."""
+        from . import gguf as G
+
+        arch_text = file.string("general.architecture")
+        if arch_text is None:
+            raise VvliError(MISSING_JSON_FIELD, -1, "general.architecture")
+        if arch_text not in ARCH_NAMES:
+            raise VvliError("UnsupportedModelArchitecture")
+        arch = ARCH_NAMES[arch_text]
+        prefix = arch_text  # Architecture.ggufPrefix (src/llm.zig:35-42)
+        vocab = file.metadata_value("tokenizer.ggml.tokens")
+        if vocab is None:
+            raise VvliError(MISSING_JSON_FIELD, -1, "tokenizer.ggml.tokens")
+        if vocab[0] != G.ARRAY:
+            raise VvliError("InvalidConfig")
+
+        def required(suffix):
+            v = file.usize_value(f"{prefix}.{suffix}")
+            if v is None:
+                raise VvliError(MISSING_JSON_FIELD, -1, f"{prefix}.{suffix}")
+            return v
+
+        heads = required("attention.head_count")
+        cfg = cls(
+            architecture=arch,
+            vocab_size=vocab[1].len,
+            hidden_size=required("embedding_length"),
+            intermediate_size=required("feed_forward_length"),
+            num_hidden_layers=required("block_count"),
+            num_attention_heads=heads,
+            num_key_value_heads=_v(file.usize_value(f"{prefix}.attention.head_count_kv"), heads),
+            rope_layout=ROPE_INTERLEAVED,
+            max_position_embeddings=required("context_length"),
+            rope_theta=_v(file.f32_value(f"{prefix}.rope.freq_base"), 10000.0),
+            rms_norm_eps=_v(file.f32_value(f"{prefix}.attention.layer_norm_rms_epsilon"), _f32(1e-6)),
+            tie_word_embeddings=file.tensor("output.weight") is None,
+            qkv_bias=False,
+            eos_token_id=_v(file.usize_value("tokenizer.ggml.eos_token_id"), 0),
+            pad_token_id=_v(file.usize_value("tokenizer.ggml.padding_token_id"), 0),
+        )
         cfg.validate()
         return cfg
 

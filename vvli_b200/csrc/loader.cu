@@ -1,4 +1,4 @@
-// loader.cu - weights straight from a safetensors file into this rank's device layout.
+// loader.cu - weights straight from a safetensors or GGUF file into this rank's device layout.
 //
 // loadSafetensorsIntoOwnedModel (src/llm.zig:923-1006) copies every tensor of
 // model.safetensors into one host blob; here each rank reads only the pieces
@@ -14,12 +14,21 @@
 //   * the mapping is page-locked read-only (cudaHostRegister) when the system
 //     allows it, so the copies are DMA from the page cache; otherwise they go
 //     through the driver's pageable path.
+//
+// loadGgufIntoOwnedModel (src/llm.zig:1008-1065) does the same for a GGUF
+// file (src/gguf.zig): the binary header and tensor table are parsed here,
+// tensors are named token_embd / blk.N.* / output_norm / output, and may be
+// F32, F16 or BF16 (copyGgufTensorIntoWeight, :1081-1138); F16 values are
+// widened exactly and rounded with f32ToBf16 on the device.
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cuda_fp16.h>
+
 #include <algorithm>
+#include <functional>
 #include <cstring>
 #include <map>
 #include <string>
@@ -205,6 +214,14 @@ __global__ void f32_to_bf16_kernel(const float* src, uint16_t* dst, size_t n) {
     dst[i] = f32_to_bf16(src[i]);
 }
 
+// f32ToBf16(f16ToF32(bits)) of every element (src/llm.zig:795-803, 1119-1126):
+// the half -> float widening is exact, the rounding is the reference's.
+__global__ void f16_to_bf16_kernel(const uint16_t* src, uint16_t* dst, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = f32_to_bf16(__half2float(__ushort_as_half(src[i])));
+}
+
 struct Mapping {
   int fd = -1;
   void* base = MAP_FAILED;
@@ -215,111 +232,91 @@ struct Mapping {
     if (base != MAP_FAILED) munmap(base, size);
     if (fd >= 0) close(fd);
   }
+  int open_file(const char* path, std::string* why) {
+    fd = open(path, O_RDONLY);
+    if (fd < 0) {
+      *why = std::string("cannot open ") + path;
+      return VVLI_ERR_INVALID_ARGUMENT;
+    }
+    struct stat st;
+    if (fstat(fd, &st) != 0) {
+      *why = std::string("cannot stat ") + path;
+      return VVLI_ERR_INVALID_ARGUMENT;
+    }
+    size = static_cast<size_t>(st.st_size);
+    if (size == 0) return VVLI_OK;  // nothing to map; the format checks reject it
+    base = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (base == MAP_FAILED) {
+      *why = std::string("cannot map ") + path;
+      return VVLI_ERR_INVALID_ARGUMENT;
+    }
+    return VVLI_OK;
+  }
+  const uint8_t* bytes() const { return base == MAP_FAILED ? nullptr : static_cast<const uint8_t*>(base); }
+  // DMA straight from the page cache when the mapping can be page-locked.
+  void lock() {
+    if (base == MAP_FAILED) return;
+    registered = cudaHostRegister(base, size, cudaHostRegisterReadOnly) == cudaSuccess;
+    if (!registered) cudaGetLastError();
+  }
 };
 
-}  // namespace
+enum SrcType { kSrcBF16, kSrcF32, kSrcF16 };
 
-int upload_safetensors(const char* path, const std::vector<LoadPiece>& pieces, int layers, uint16_t* w,
-                       cudaStream_t s, std::string* why) {
-  Mapping m;
-  m.fd = open(path, O_RDONLY);
-  if (m.fd < 0) {
-    *why = std::string("cannot open ") + path;
-    return VVLI_ERR_INVALID_ARGUMENT;
-  }
-  struct stat st;
-  if (fstat(m.fd, &st) != 0 || st.st_size < 8) {
-    *why = std::string("not a safetensors file: ") + path;
-    return VVLI_ERR_INVALID_WEIGHT;
-  }
-  m.size = static_cast<size_t>(st.st_size);
-  m.base = mmap(nullptr, m.size, PROT_READ, MAP_PRIVATE, m.fd, 0);
-  if (m.base == MAP_FAILED) {
-    *why = std::string("cannot map ") + path;
-    return VVLI_ERR_INVALID_ARGUMENT;
-  }
-  const uint8_t* bytes = static_cast<const uint8_t*>(m.base);
-  uint64_t header_len = 0;
-  memcpy(&header_len, bytes, 8);  // little endian on every CUDA host
-  if (8 + header_len > m.size) {
-    *why = "safetensors header runs past the end of the file";
-    return VVLI_ERR_INVALID_WEIGHT;
-  }
-  Json header;
-  if (!Parser(reinterpret_cast<const char*>(bytes + 8), header_len).parse(&header) || header.kind != Json::Obj) {
-    *why = "safetensors header is not a JSON object";
-    return VVLI_ERR_INVALID_WEIGHT;
-  }
-  const uint8_t* data = bytes + 8 + header_len;
-  const size_t data_len = m.size - 8 - header_len;
-  // DMA straight from the page cache when the mapping can be page-locked.
-  m.registered = cudaHostRegister(m.base, m.size, cudaHostRegisterReadOnly) == cudaSuccess;
-  if (!m.registered) cudaGetLastError();
+// A checked source tensor: `count` elements of `type` at `data`.
+struct SrcTensor {
+  int type;
+  uint64_t count;
+  const uint8_t* data;
+};
 
-  float* stage = nullptr;
+inline uint64_t src_elem_bytes(int type) { return type == kSrcF32 ? 4 : 2; }
+
+// Finds and checks the tensor of blob id `id`; returns a vvli_status.
+using Lookup = std::function<int(uint64_t id, uint64_t expect_elems, SrcTensor*, std::string*)>;
+
+// Copies every piece: BF16 rows with one strided copy, F32 / F16 rows through
+// a device staging buffer and a rounding kernel.
+int copy_pieces(const std::vector<LoadPiece>& pieces, const Lookup& lookup, uint16_t* w, cudaStream_t s,
+                std::string* why) {
+  void* stage = nullptr;
   constexpr size_t kStageBytes = 64ull << 20;
   int status = VVLI_OK;
   for (const LoadPiece& p : pieces) {
-    const std::string name = tensor_name(p.tensor_id, layers);
-    auto it = header.obj.find(name);
-    if (it == header.obj.end()) {
-      *why = "missing tensor " + name;
-      status = VVLI_ERR_MISSING_TENSOR;
-      break;
-    }
-    const Json& meta = it->second;
-    auto dt = meta.obj.find("dtype");
-    auto sh = meta.obj.find("shape");
-    auto off = meta.obj.find("data_offsets");
-    if (meta.kind != Json::Obj || dt == meta.obj.end() || sh == meta.obj.end() || off == meta.obj.end() ||
-        sh->second.kind != Json::Arr || off->second.kind != Json::Arr || off->second.arr.size() != 2) {
-      *why = "malformed entry for " + name;
-      status = VVLI_ERR_INVALID_WEIGHT;
-      break;
-    }
-    const bool bf16 = dt->second.str == "BF16", f32 = dt->second.str == "F32";
-    if (!bf16 && !f32) {
-      *why = name + " has dtype " + dt->second.str + " (BF16 or F32 only)";
-      status = VVLI_ERR_UNSUPPORTED_DTYPE;
-      break;
-    }
-    uint64_t count = 1;
-    for (const Json& d : sh->second.arr) count *= static_cast<uint64_t>(d.num);
-    const uint64_t start = static_cast<uint64_t>(off->second.arr[0].num), end = static_cast<uint64_t>(off->second.arr[1].num);
-    const uint64_t esz = bf16 ? 2 : 4;
-    if (count != p.tensor_elems || end < start || end > data_len || end - start != count * esz) {
-      *why = "shape or byte range of " + name + " does not match the model config";
-      status = VVLI_ERR_INVALID_WEIGHT;
-      break;
-    }
-    const uint8_t* src = data + start + (p.row0 * p.src_ld + p.col0) * esz;
+    SrcTensor t{};
+    if ((status = lookup(p.tensor_id, p.tensor_elems, &t, why)) != VVLI_OK) break;
+    const uint64_t esz = src_elem_bytes(t.type);
+    const uint8_t* src = t.data + (p.row0 * p.src_ld + p.col0) * esz;
     uint16_t* dst = w + p.dst;
     cudaError_t e;
-    if (bf16) {
+    if (t.type == kSrcBF16) {
       e = cudaMemcpy2DAsync(dst, p.cols * 2, src, p.src_ld * 2, p.cols * 2, p.rows, cudaMemcpyHostToDevice, s);
     } else {
       if (!stage && (e = cudaMalloc(&stage, kStageBytes)) != cudaSuccess) {
-        *why = "staging buffer for F32 tensors";
+        *why = "staging buffer for F32 / F16 tensors";
         status = VVLI_ERR_OOM;
         break;
       }
-      const uint64_t rows_per = std::max<uint64_t>(1, kStageBytes / (p.cols * 4));
+      const uint64_t rows_per = std::max<uint64_t>(1, kStageBytes / (p.cols * esz));
       e = cudaSuccess;
       for (uint64_t r = 0; r < p.rows && e == cudaSuccess; r += rows_per) {
         const uint64_t n = std::min(rows_per, p.rows - r);
-        e = cudaMemcpy2DAsync(stage, p.cols * 4, src + r * p.src_ld * 4, p.src_ld * 4, p.cols * 4, n,
+        e = cudaMemcpy2DAsync(stage, p.cols * esz, src + r * p.src_ld * esz, p.src_ld * esz, p.cols * esz, n,
                               cudaMemcpyHostToDevice, s);
         if (e == cudaSuccess) {
           const size_t total = n * p.cols;
           const unsigned blocks = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, 4096));
-          f32_to_bf16_kernel<<<blocks, 256, 0, s>>>(stage, dst + r * p.cols, total);
+          if (t.type == kSrcF32)
+            f32_to_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(stage), dst + r * p.cols, total);
+          else
+            f16_to_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(stage), dst + r * p.cols, total);
           e = cudaGetLastError();
           if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // the staging buffer is reused
         }
       }
     }
     if (e != cudaSuccess) {
-      *why = std::string("copying ") + name + ": " + cudaGetErrorString(e);
+      *why = std::string("copying tensor ") + std::to_string(p.tensor_id) + ": " + cudaGetErrorString(e);
       status = VVLI_ERR_CUDA;
       break;
     }
@@ -331,6 +328,289 @@ int upload_safetensors(const char* path, const std::vector<LoadPiece>& pieces, i
     status = VVLI_ERR_CUDA;
   }
   return status;
+}
+
+// ---------------------------------------------------------------- GGUF (src/gguf.zig)
+// The GGUF names of the reference's tensors (loadGgufIntoOwnedModel,
+// src/llm.zig:1008-1065) by blob order id; GGUF models carry no q/k/v biases.
+std::string gguf_tensor_name(uint64_t id, int layers) {
+  if (id == 0) return "token_embd.weight";
+  if (id == 1 + 12ull * layers) return "output_norm.weight";
+  if (id == 2 + 12ull * layers) return "output.weight";
+  const uint64_t l = (id - 1) / 12, k = (id - 1) % 12;
+  static const char* kSuffix[12] = {"attn_norm.weight", "attn_q.weight", "attn_q.bias", "attn_k.weight",
+                                    "attn_k.bias",      "attn_v.weight", "attn_v.bias", "attn_output.weight",
+                                    "ffn_norm.weight",  "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"};
+  return "blk." + std::to_string(l) + "." + kSuffix[k];
+}
+
+struct GgufTensor {
+  uint32_t type;
+  uint64_t count;   // 0 when the element count overflows
+  uint64_t offset;  // from the start of the data section
+};
+
+// gguf.parse (src/gguf.zig:234-287): header, metadata (only general.alignment
+// is kept), tensor table; little-endian reads bounded by the file size.
+class GgufReader {
+ public:
+  GgufReader(const uint8_t* p, size_t n) : p_(p), n_(n) {}
+  size_t index = 0;
+  int status = VVLI_OK;
+
+  bool bytes(size_t len, const uint8_t** out) {
+    if (len > n_ - index) return fail(VVLI_ERR_INVALID_GGUF);
+    *out = p_ + index;
+    index += len;
+    return true;
+  }
+  template <typename T>
+  bool num(T* out) {
+    const uint8_t* b;
+    if (!bytes(sizeof(T), &b)) return false;
+    memcpy(out, b, sizeof(T));  // little endian on every CUDA host
+    return true;
+  }
+  bool str(std::string* out) {
+    uint64_t len;
+    const uint8_t* b;
+    if (!num(&len) || !bytes(len, &b)) return false;
+    out->assign(reinterpret_cast<const char*>(b), len);
+    return true;
+  }
+  bool skip_str() {
+    uint64_t len;
+    const uint8_t* b;
+    return num(&len) && bytes(len, &b);
+  }
+  // gguf.MetadataType (src/gguf.zig:16-30); other values are UnsupportedMetadataType.
+  bool meta_type(uint32_t* t) {
+    if (!num(t)) return false;
+    if (*t > 12) return fail(VVLI_ERR_UNSUPPORTED_METADATA_TYPE);
+    return true;
+  }
+  // Reader.skipMetadataValue (src/gguf.zig:340-355); arrays may nest.
+  bool skip_value(uint32_t t, int depth = 0) {
+    const uint8_t* b;
+    switch (t) {
+      case 0: case 1: case 7: return bytes(1, &b);
+      case 2: case 3: return bytes(2, &b);
+      case 4: case 5: case 6: return bytes(4, &b);
+      case 10: case 11: case 12: return bytes(8, &b);
+      case 8: return skip_str();
+      default: {  // array
+        uint32_t it;
+        uint64_t len;
+        if (depth > 64) return fail(VVLI_ERR_INVALID_GGUF);
+        if (!meta_type(&it) || !num(&len)) return false;
+        const size_t fixed = it == 8 || it == 9 ? 0 : (it <= 1 || it == 7 ? 1 : it <= 3 ? 2 : it <= 6 ? 4 : 8);
+        if (fixed) {  // one bounds check for a whole array of numbers
+          if (len > (n_ - index) / fixed) return fail(VVLI_ERR_INVALID_GGUF);
+          index += len * fixed;
+          return true;
+        }
+        for (uint64_t i = 0; i < len; ++i)
+          if (!skip_value(it, depth + 1)) return false;
+        return true;
+      }
+    }
+  }
+  // File.usizeValue (src/gguf.zig:149-162) of a value of type t; *ok = false
+  // for a type it does not accept (or a negative integer).
+  bool usize_value(uint32_t t, uint64_t* out, bool* ok) {
+    *ok = true;
+    switch (t) {
+      case 0: { uint8_t v; if (!num(&v)) return false; *out = v; return true; }
+      case 2: { uint16_t v; if (!num(&v)) return false; *out = v; return true; }
+      case 4: { uint32_t v; if (!num(&v)) return false; *out = v; return true; }
+      case 10: { uint64_t v; if (!num(&v)) return false; *out = v; return true; }
+      case 1: { int8_t v; if (!num(&v)) return false; *ok = v >= 0; *out = static_cast<uint64_t>(v); return true; }
+      case 3: { int16_t v; if (!num(&v)) return false; *ok = v >= 0; *out = static_cast<uint64_t>(v); return true; }
+      case 5: { int32_t v; if (!num(&v)) return false; *ok = v >= 0; *out = static_cast<uint64_t>(v); return true; }
+      case 11: { int64_t v; if (!num(&v)) return false; *ok = v >= 0; *out = static_cast<uint64_t>(v); return true; }
+      default: *ok = false; return skip_value(t);
+    }
+  }
+
+ private:
+  const uint8_t* p_;
+  size_t n_;
+  bool fail(int st) {
+    if (status == VVLI_OK) status = st;
+    return false;
+  }
+};
+
+// gguf.TensorType (src/gguf.zig:32-72): the values the reference accepts.
+bool gguf_known_tensor_type(uint32_t t) {
+  return t <= 3 || (t >= 6 && t <= 30) || t == 34 || t == 35 || t == 39;
+}
+
+int parse_gguf(const uint8_t* bytes, size_t n, std::map<std::string, GgufTensor>* tensors, uint64_t* data_start,
+               std::string* why) {
+  GgufReader r(bytes, n);
+  const uint8_t* magic;
+  uint32_t version;
+  uint64_t tensor_count, metadata_count;
+  auto bad = [&](const char* what) {
+    *why = what;
+    return r.status != VVLI_OK ? r.status : VVLI_ERR_INVALID_GGUF;
+  };
+  if (!r.bytes(4, &magic) || memcmp(magic, "GGUF", 4) != 0) return bad("not a GGUF file");
+  if (!r.num(&version)) return bad("GGUF header is cut short");
+  if (version < 2 || version > 3) {
+    *why = "GGUF version " + std::to_string(version) + " (2 or 3 only)";
+    return VVLI_ERR_UNSUPPORTED_GGUF_VERSION;
+  }
+  if (!r.num(&tensor_count) || !r.num(&metadata_count)) return bad("GGUF header is cut short");
+  uint64_t alignment = 32;  // gguf.default_alignment
+  bool have_alignment = false;
+  for (uint64_t i = 0; i < metadata_count; ++i) {
+    std::string key;
+    uint32_t t;
+    if (!r.str(&key) || !r.meta_type(&t)) return bad("malformed GGUF metadata");
+    if (key == "general.alignment" && !have_alignment) {  // the first entry of a key wins
+      have_alignment = true;
+      uint64_t v;
+      bool ok;
+      if (!r.usize_value(t, &v, &ok)) return bad("malformed GGUF metadata");
+      if (ok) alignment = v;
+    } else if (!r.skip_value(t)) {
+      return bad("malformed GGUF metadata");
+    }
+  }
+  for (uint64_t i = 0; i < tensor_count; ++i) {
+    std::string name;
+    uint32_t dims;
+    if (!r.str(&name) || !r.num(&dims)) return bad("malformed GGUF tensor table");
+    if (dims == 0 || dims > 8) return bad("GGUF tensor with 0 or more than 8 dimensions");
+    uint64_t count = 1;
+    bool overflow = false;
+    for (uint32_t d = 0; d < dims; ++d) {
+      uint64_t v;
+      if (!r.num(&v)) return bad("malformed GGUF tensor table");
+      overflow |= __builtin_mul_overflow(count, v, &count);
+    }
+    GgufTensor t{};
+    if (!r.num(&t.type)) return bad("malformed GGUF tensor table");
+    if (!gguf_known_tensor_type(t.type)) {  // readEnum(TensorType) fails this way
+      *why = name + " has an unknown GGUF tensor type " + std::to_string(t.type);
+      return VVLI_ERR_UNSUPPORTED_METADATA_TYPE;
+    }
+    if (!r.num(&t.offset)) return bad("malformed GGUF tensor table");
+    t.count = overflow ? 0 : count;
+    tensors->emplace(name, t);  // File.tensor returns the first of a name
+  }
+  if (alignment == 0) return bad("general.alignment is 0");
+  const uint64_t start = (r.index + alignment - 1) / alignment * alignment;
+  if (start < r.index || start > n) return bad("GGUF data section starts past the end of the file");
+  *data_start = start;
+  return VVLI_OK;
+}
+
+}  // namespace
+
+int upload_safetensors(const char* path, const std::vector<LoadPiece>& pieces, int layers, uint16_t* w,
+                       cudaStream_t s, std::string* why) {
+  Mapping m;
+  int st = m.open_file(path, why);
+  if (st != VVLI_OK) return st;
+  if (m.size < 8) {
+    *why = std::string("not a safetensors file: ") + path;
+    return VVLI_ERR_INVALID_WEIGHT;
+  }
+  const uint8_t* bytes = m.bytes();
+  uint64_t header_len = 0;
+  memcpy(&header_len, bytes, 8);  // little endian on every CUDA host
+  if (header_len > m.size - 8) {
+    *why = "safetensors header runs past the end of the file";
+    return VVLI_ERR_INVALID_WEIGHT;
+  }
+  Json header;
+  if (!Parser(reinterpret_cast<const char*>(bytes + 8), header_len).parse(&header) || header.kind != Json::Obj) {
+    *why = "safetensors header is not a JSON object";
+    return VVLI_ERR_INVALID_WEIGHT;
+  }
+  const uint8_t* data = bytes + 8 + header_len;
+  const size_t data_len = m.size - 8 - header_len;
+  m.lock();
+  // copyTensorIntoWeight (src/llm.zig:1149-1183): name, dtype BF16 or F32,
+  // element count and byte range.
+  auto lookup = [&](uint64_t id, uint64_t expect, SrcTensor* t, std::string* err) -> int {
+    const std::string name = tensor_name(id, layers);
+    auto it = header.obj.find(name);
+    if (it == header.obj.end()) {
+      *err = "missing tensor " + name;
+      return VVLI_ERR_MISSING_TENSOR;
+    }
+    const Json& meta = it->second;
+    auto dt = meta.obj.find("dtype");
+    auto sh = meta.obj.find("shape");
+    auto off = meta.obj.find("data_offsets");
+    if (meta.kind != Json::Obj || dt == meta.obj.end() || sh == meta.obj.end() || off == meta.obj.end() ||
+        sh->second.kind != Json::Arr || off->second.kind != Json::Arr || off->second.arr.size() != 2) {
+      *err = "malformed entry for " + name;
+      return VVLI_ERR_INVALID_WEIGHT;
+    }
+    const bool bf16 = dt->second.str == "BF16", f32 = dt->second.str == "F32";
+    if (!bf16 && !f32) {
+      *err = name + " has dtype " + dt->second.str + " (BF16 or F32 only)";
+      return VVLI_ERR_UNSUPPORTED_DTYPE;
+    }
+    uint64_t count = 1;
+    for (const Json& d : sh->second.arr) count *= static_cast<uint64_t>(d.num);
+    const uint64_t start = static_cast<uint64_t>(off->second.arr[0].num);
+    const uint64_t end = static_cast<uint64_t>(off->second.arr[1].num);
+    const uint64_t esz = bf16 ? 2 : 4;
+    if (count != expect || end < start || end > data_len || end - start != count * esz) {
+      *err = "shape or byte range of " + name + " does not match the model config";
+      return VVLI_ERR_INVALID_WEIGHT;
+    }
+    *t = SrcTensor{bf16 ? kSrcBF16 : kSrcF32, count, data + start};
+    return VVLI_OK;
+  };
+  return copy_pieces(pieces, lookup, w, s, why);
+}
+
+int upload_gguf(const char* path, const std::vector<LoadPiece>& pieces, int layers, uint16_t* w, cudaStream_t s,
+                std::string* why) {
+  Mapping m;
+  int st = m.open_file(path, why);
+  if (st != VVLI_OK) return st;
+  std::map<std::string, GgufTensor> tensors;
+  uint64_t data_start = 0;
+  if ((st = parse_gguf(m.bytes(), m.size, &tensors, &data_start, why)) != VVLI_OK) return st;
+  m.lock();
+  // copyGgufTensorIntoWeight (src/llm.zig:1081-1138): name, native float
+  // type (F32, F16, BF16), element count, byte range.
+  auto lookup = [&](uint64_t id, uint64_t expect, SrcTensor* t, std::string* err) -> int {
+    const std::string name = gguf_tensor_name(id, layers);
+    auto it = tensors.find(name);
+    if (it == tensors.end()) {
+      *err = "missing tensor " + name;
+      return VVLI_ERR_MISSING_TENSOR;
+    }
+    const GgufTensor& g = it->second;
+    const int type = g.type == 0 ? kSrcF32 : g.type == 1 ? kSrcF16 : g.type == 30 ? kSrcBF16 : -1;
+    if (type < 0) {
+      *err = name + " has GGUF tensor type " + std::to_string(g.type) + " (F32, F16 or BF16 only)";
+      return VVLI_ERR_UNSUPPORTED_DTYPE;
+    }
+    if (g.count != expect) {
+      *err = "element count of " + name + " does not match the model config";
+      return VVLI_ERR_INVALID_WEIGHT;
+    }
+    const uint64_t len = g.count * src_elem_bytes(type);
+    uint64_t start, end;
+    if (__builtin_add_overflow(data_start, g.offset, &start) || __builtin_add_overflow(start, len, &end) ||
+        end > m.size) {
+      *err = "byte range of " + name + " runs past the end of the file";
+      return VVLI_ERR_INVALID_WEIGHT;
+    }
+    *t = SrcTensor{type, g.count, m.bytes() + start};
+    return VVLI_OK;
+  };
+  return copy_pieces(pieces, lookup, w, s, why);
 }
 
 }  // namespace vvli

@@ -1,4 +1,4 @@
-// loader.h - safetensors file -> device weight layout (see loader.cu).
+// loader.h - safetensors / GGUF file -> device weight layout (see loader.cu).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -20,5 +20,7 @@ struct LoadPiece {
 // Returns a vvli_status; *why says what went wrong.
 int upload_safetensors(const char* path, const std::vector<LoadPiece>& pieces, int layers, uint16_t* w,
                        cudaStream_t s, std::string* why);
+int upload_gguf(const char* path, const std::vector<LoadPiece>& pieces, int layers, uint16_t* w, cudaStream_t s,
+                std::string* why);
 
 }  // namespace vvli

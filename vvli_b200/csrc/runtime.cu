@@ -1030,6 +1030,10 @@ const char* vvli_cuda_strerror(int status) {
     case VVLI_ERR_EMPTY_PROMPT: return "EmptyPrompt";
     case VVLI_ERR_OUTPUT_TOO_SMALL: return "OutputTooSmall";
     case VVLI_ERR_INVALID_SAMPLING: return "InvalidSamplingOptions";
+    case VVLI_ERR_MISSING_TENSOR: return "MissingSafetensorsTensor";
+    case VVLI_ERR_INVALID_GGUF: return "InvalidGguf";
+    case VVLI_ERR_UNSUPPORTED_GGUF_VERSION: return "UnsupportedGgufVersion";
+    case VVLI_ERR_UNSUPPORTED_METADATA_TYPE: return "UnsupportedMetadataType";
     case VVLI_ERR_CUDA: return "CudaError";
     case VVLI_ERR_NCCL: return "NcclError";
     case VVLI_ERR_TIMEOUT: return "Timeout";
@@ -1327,16 +1331,38 @@ static uint64_t tensor_elems(const vvli_model_config& cfg, uint64_t id) {
   }
 }
 
-int vvli_cuda_load_safetensors(vvli_ctx* c, const char* path) {
-  if (!c || !path) return VVLI_ERR_INVALID_ARGUMENT;
-  CK(cudaSetDevice(c->device));
+// This rank's shard plan as file pieces (the loaders read nothing else).
+static std::vector<LoadPiece> load_pieces(const vvli_ctx* c) {
   std::vector<LoadPiece> lp;
   lp.reserve(c->pieces.size());
   for (const Piece& p : c->pieces)
     lp.push_back(LoadPiece{p.tensor_id, tensor_elems(c->cfg, p.tensor_id), p.dst, p.rows, p.cols, p.src_ld, p.row0,
                            p.col0});
+  return lp;
+}
+
+int vvli_cuda_load_safetensors(vvli_ctx* c, const char* path) {
+  if (!c || !path) return VVLI_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(c->device));
   std::string why;
-  const int st = upload_safetensors(path, lp, c->L, c->w, c->stream, &why);
+  const int st = upload_safetensors(path, load_pieces(c), c->L, c->w, c->stream, &why);
+  if (st != VVLI_OK) {
+    g_last_error = why;
+    return st;
+  }
+  return after_load(c);
+}
+
+int vvli_cuda_load_gguf(vvli_ctx* c, const char* path) {
+  if (!c || !path) return VVLI_ERR_INVALID_ARGUMENT;
+  if (c->cfg.qkv_bias) return VVLI_ERR_UNSUPPORTED_ARCH;  // loadGgufIntoOwnedModel (src/llm.zig:1011)
+  if (c->cfg.rope_layout != VVLI_ROPE_INTERLEAVED) {
+    g_last_error = "a GGUF model needs rope_layout INTERLEAVED (Config.fromGguf)";
+    return VVLI_ERR_INVALID_CONFIG;
+  }
+  CK(cudaSetDevice(c->device));
+  std::string why;
+  const int st = upload_gguf(path, load_pieces(c), c->L, c->w, c->stream, &why);
   if (st != VVLI_OK) {
     g_last_error = why;
     return st;

@@ -1,7 +1,8 @@
 """Status codes of the C ABI and the Python exception that carries them.
 
 The names mirror the reference's Zig error sets: llm.Error
-(src/llm.zig:17-27) and generator.Error (src/generator.zig:8-12).  Codes
+(src/llm.zig:17-27), generator.Error (src/generator.zig:8-12) and
+gguf.Error (src/gguf.zig:7-12).  Codes
 20 and above are added by the CUDA runtime (device, NCCL, bounded waits).
 """
 
@@ -17,6 +18,9 @@ CODES = {
     8: "OutputTooSmall",
     9: "InvalidSamplingOptions",
     10: "MissingSafetensorsTensor",
+    11: "InvalidGguf",
+    12: "UnsupportedGgufVersion",
+    13: "UnsupportedMetadataType",
     20: "CudaError",
     21: "NcclError",
     22: "Timeout",

@@ -71,6 +71,11 @@ class Runner:
         """This rank's weights straight from model.safetensors (loadOwnedFromSafetensorsFile)."""
         check(_abi.lib().vvli_cuda_load_safetensors(self._ctx, os.fsencode(path)))
 
+    def load_gguf(self, path: str):
+        """This rank's weights straight from a GGUF file (loadOwnedFromGgufFile); the
+        Runner's config must come from ``Config.from_gguf`` of the same file."""
+        check(_abi.lib().vvli_cuda_load_gguf(self._ctx, os.fsencode(path)))
+
     def fill_synthetic(self, seed: int = 0):
         check(_abi.lib().vvli_cuda_fill_synthetic(self._ctx, seed))
 

@@ -7,6 +7,8 @@ head, every tensor at a 64-byte aligned element offset.  ``load_safetensors``
 follows loadSafetensorsIntoOwnedModel / copyTensorIntoWeight
 (src/llm.zig:923-1006, 1149-1218): tensor names, BF16 copied as is, F32
 rounded with f32ToBf16 (round to nearest even), any other dtype rejected.
+``load_gguf`` does the same for a GGUF file (src/llm.zig:885-921,
+1008-1138): GGUF tensor names, F32 / F16 / BF16 accepted.
 """
 
 from __future__ import annotations
@@ -135,6 +137,85 @@ def load_safetensors(path: str, cfg: Config) -> np.ndarray:
         finally:
             mm.close()
     return blob
+
+
+_GGUF_LAYER_NAMES = {
+    "input_layernorm.weight": "attn_norm.weight",
+    "self_attn.q_proj.weight": "attn_q.weight",
+    "self_attn.k_proj.weight": "attn_k.weight",
+    "self_attn.v_proj.weight": "attn_v.weight",
+    "self_attn.o_proj.weight": "attn_output.weight",
+    "post_attention_layernorm.weight": "ffn_norm.weight",
+    "mlp.gate_proj.weight": "ffn_gate.weight",
+    "mlp.up_proj.weight": "ffn_up.weight",
+    "mlp.down_proj.weight": "ffn_down.weight",
+}
+
+
+def gguf_tensor_name(hf_name: str) -> str:
+    """The GGUF name loadGgufIntoOwnedModel (src/llm.zig:1008-1065) reads for a blob tensor."""
+    if hf_name == "model.embed_tokens.weight":
+        return "token_embd.weight"
+    if hf_name == "model.norm.weight":
+        return "output_norm.weight"
+    if hf_name == "lm_head.weight":
+        return "output.weight"
+    _, _, layer, rest = hf_name.split(".", 3)
+    return f"blk.{layer}.{_GGUF_LAYER_NAMES[rest]}"
+
+
+def _copy_gguf_tensor(blob: np.ndarray, off: int, shape, name: str, file, data) -> None:
+    """copyGgufTensorIntoWeight (src/llm.zig:1081-1138) into blob[off:]."""
+    from . import gguf as G
+
+    info = file.tensor(name)
+    if info is None:
+        raise VvliError("MissingSafetensorsTensor", -1, name)
+    if info.tensor_type not in G.NATIVE_FLOAT:
+        raise VvliError("UnsupportedDType", None, name)
+    count = int(np.prod(shape))
+    if info.element_count() != count:
+        raise VvliError("InvalidWeight", None, name)
+    esz = 4 if info.tensor_type == G.F32 else 2
+    start = file.data_start + info.offset
+    end = start + count * esz
+    if end > len(data):
+        raise VvliError("InvalidWeight", None, name)
+    raw = data[start:end]
+    try:
+        if info.tensor_type == G.BF16:
+            blob[off: off + count] = np.frombuffer(raw, dtype="<u2")
+        elif info.tensor_type == G.F16:  # f32ToBf16(f16ToF32(bits)); the widening is exact
+            blob[off: off + count] = f32_to_bf16(np.frombuffer(raw, dtype="<f2").astype(np.float32))
+        else:
+            blob[off: off + count] = f32_to_bf16(np.frombuffer(raw, dtype="<f4"))
+    finally:
+        raw.release()
+
+
+def load_gguf(path: str):
+    """(config, bf16 blob) of a GGUF file: loadOwnedFromGgufFile (src/llm.zig:885-921) with
+    Config.fromGguf and loadGgufIntoOwnedModel (:153-193, 1008-1065)."""
+    from . import gguf as G
+
+    with open(path, "rb") as f:
+        mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+        try:
+            data = memoryview(mm)
+            try:
+                file = G.parse(data)
+                cfg = Config.from_gguf(file)
+                if not cfg.supports_dense_runner() or cfg.qkv_bias:
+                    raise VvliError("UnsupportedModelArchitecture")
+                blob = np.zeros(cfg.storage_element_count(), dtype=np.uint16)
+                for name, off, shape, _ in tensor_entries(cfg):
+                    _copy_gguf_tensor(blob, off, shape, gguf_tensor_name(name), file, data)
+                file.data = None
+            finally:
+                data.release()
+        finally:
+            mm.close()
+    return cfg, blob
 
 
 def save_safetensors(path: str, cfg: Config, blob: np.ndarray) -> None:
