@@ -98,8 +98,7 @@ constexpr double kAccScale = 4294967296.0;
 constexpr int kMaxFfRows = 256;  // gate|up rows per CTA kept in shared memory for ME_AXPY
 constexpr int kMaxTp = 8;
 constexpr int kMegaConsumerWarps = 16;
-constexpr int kMegaThreads = kMegaConsumerWarps * 32;  // no warp set aside for the weight copies
-constexpr int kMaxRingStages = 4;  // shared-memory stages of the megakernel's weight ring
+constexpr int kMegaThreads = (kMegaConsumerWarps + 1) * 32;
 
 struct MegaPhase {
   int kind;                // MegaKind

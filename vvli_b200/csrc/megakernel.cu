@@ -4,17 +4,15 @@
 // of phases: embed, then per layer q|k|v GEMV, attention, o_proj (+residual),
 // gate|up (silu*mul), down_proj (+residual), and the LM head with argmax.
 // One CTA per SM runs them all:
-//   * this CTA's rows of every weight matrix stream through a ring of
-//     shared-memory stages with cp.async.bulk, in the order of the GEMV
-//     phases.  Weights do not depend on activations, so the ring never waits
-//     for a phase boundary: the warp that finishes reading a stage last
-//     issues the copy of the stage `nst` ahead into it, which may belong to
-//     the next matrix; while the warps run attention or wait at a grid
-//     barrier, that matrix is already arriving.  No warp is set aside for
-//     copying, so the 16 warps may each use 128 registers.
-//   * the 16 warps wait at a grid barrier for the phase input, run the phase
-//     (GEMV rows from the ring, or attention items), write their outputs and
-//     meet at the next grid barrier.
+//   * warp 16 is the producer.  It walks every GEMV phase of the step in
+//     order and streams this CTA's rows of each weight matrix through a ring
+//     of shared-memory stages with cp.async.bulk.  Weights do not depend on
+//     activations, so it never waits for a phase boundary: while the
+//     consumers run attention or wait at a grid barrier, the next matrix is
+//     already arriving.  HBM stays busy across the whole step.
+//   * warps 0-15 consume: they wait at a grid barrier for the phase input,
+//     run the phase (GEMV rows from the ring, or attention items), write
+//     their outputs and meet at the next grid barrier.
 // All cross-CTA data is read through L2 (ld.global.cg).  Every wait (ring
 // stages, grid barrier, tensor-parallel flags) is bounded and reports
 // VVLI_ERR_TIMEOUT in StepState.err.  Under tensor parallelism the
@@ -118,7 +116,7 @@ __device__ float consumer_sum(float v, float* red) {
 
 // Optional timeline: per phase and CTA, [0] consumers start, [1] inputs
 // loaded, [2] rows consumed, [3] outputs written, [4] grid barrier passed,
-// [5] the phase's first weight stage was issued.
+// [5] producer issued the phase's first stage.
 VVLI_DEV void trace_mark(const MegaParams& P, int f, int k) {
   if (P.trace) P.trace[(static_cast<size_t>(f) * gridDim.x + blockIdx.x) * 6 + k] = global_timer_ns();
 }
@@ -132,102 +130,56 @@ VVLI_DEV long long to_fixed(float v) {
 }
 VVLI_DEV float from_fixed(long long v) { return static_cast<float>(static_cast<double>(v) * (1.0 / kAccScale)); }
 
-// ---------------------------------------------------------------- weight ring
-// Stage k of the step (counted over the GEMV phases, this CTA's rows only)
-// uses slot k % nst; its full barrier completes a phase per use.  A refill
-// inside the phase being read takes the phase's parameters from registers;
-// the first nst stages after it (the next matrix) are worked out by one
-// thread while the CTA waits at the phase change before (`tail`), so no
-// refill waits for the phase table in global memory.
-
-// The copies of one stage: rows of the matrix and, for gate|up, the same rows
-// of its second half.
-struct StageSrc {
-  const uint16_t* w0;
-  const uint16_t* w1;  // nullptr: one matrix
-  uint32_t bytes;      // per matrix
-  uint32_t off1;       // shared-memory offset of the second half in the slot
+// ---------------------------------------------------------------- producer
+// Cursor over this CTA's stages of every GEMV phase of the step, in order.
+struct StageCursor {
+  int f = -1, i = 0, nstages = 0, r0 = 0, nrows = 0;
+  __device__ bool next(const MegaParams& P) {  // moves to the next stage; false at the end
+    ++i;
+    while (i >= nstages) {
+      if (++f >= P.nphases) return false;
+      const MegaPhase& ph = P.phases[f];
+      if (ph.kind != MK_GEMV) continue;
+      r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
+      nrows = cta_row(ph.N, blockIdx.x + 1, ph.row_align) - r0;
+      nstages = (nrows + ph.R - 1) / ph.R;
+      i = 0;
+    }
+    return true;
+  }
 };
 
-// This CTA's rows of GEMV phase `ph`: first row, row count; returns the stage count.
-VVLI_DEV int phase_stages(const MegaPhase& ph, int* r0, int* nrows) {
-  *r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
-  *nrows = cta_row(ph.N, blockIdx.x + 1, ph.row_align) - *r0;
-  return (*nrows + ph.R - 1) / ph.R;
-}
-
-VVLI_DEV StageSrc stage_src(const uint16_t* W, int K, int R, int nphys, int pair_offset, int r0, int nrows, int i) {
-  const size_t row_bytes = static_cast<size_t>(K) * 2;
-  const int rows_here = min(R, nrows - i * R);
-  StageSrc s;
-  s.w0 = W + static_cast<size_t>(r0 + i * R) * K;
-  s.w1 = nphys == 2 ? s.w0 + static_cast<size_t>(pair_offset) * K : nullptr;
-  s.bytes = static_cast<uint32_t>(rows_here * row_bytes);
-  s.off1 = static_cast<uint32_t>(R * row_bytes);
-  return s;
-}
-
-VVLI_DEV void issue_src(const MegaParams& P, uint8_t* ring, uint64_t* full, uint32_t slot, const StageSrc& s) {
-  // The slot's last reads (generic proxy) come before this write (async proxy).
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  uint8_t* dst = ring + static_cast<size_t>(slot) * P.slot_bytes;
-  mbar_arrive_expect_tx(&full[slot], s.w1 ? 2 * s.bytes : s.bytes);
-  bulk_g2s(dst, s.w0, s.bytes, &full[slot]);
-  if (s.w1) bulk_g2s(dst + s.off1, s.w1, s.bytes, &full[slot]);
-}
-
-// The first n stages of the step from phase f on (base = number of phase f's
-// first stage) into out[]; returns how many exist (fewer at the step's end).
-__device__ int find_stages(const MegaParams& P, int f, uint32_t k, uint32_t base, int n, StageSrc* out) {
-  int got = 0;
-  for (; f < P.nphases && got < n; ++f) {
-    const MegaPhase& ph = P.phases[f];
-    if (ph.kind != MK_GEMV) continue;
-    int r0, nrows;
-    const uint32_t ns = static_cast<uint32_t>(phase_stages(ph, &r0, &nrows));
-    while (got < n && k < base + ns) {
-      out[got++] = stage_src(ph.W, ph.K, ph.R, ph.nphys, ph.pair_offset, r0, nrows, static_cast<int>(k - base));
-      ++k;
+__device__ void mega_producer(const MegaParams& P, uint8_t* ring, uint64_t* full, uint64_t* empty, int* err) {
+  StageCursor cur;  // i = 0 >= nstages = 0: the first next() loads the first GEMV phase
+  uint32_t gi = 0;
+  int last_f = -1;
+  while (cur.next(P)) {
+    const MegaPhase& ph = P.phases[cur.f];
+    if (cur.f != last_f) {
+      trace_mark(P, cur.f, 5);
+      last_f = cur.f;
     }
-    base += ns;
+    const uint32_t slot = gi % P.nst;
+    if (gi >= static_cast<uint32_t>(P.nst) && !mbar_wait(&empty[slot], ((gi / P.nst) - 1) & 1, err)) break;
+    const size_t row_bytes = static_cast<size_t>(ph.K) * 2;
+    const int rows_here = min(ph.R, cur.nrows - cur.i * ph.R);
+    const uint32_t bytes = static_cast<uint32_t>(rows_here * row_bytes);
+    mbar_arrive_expect_tx(&full[slot], bytes * ph.nphys);
+    for (int q = 0; q < ph.nphys; ++q)
+      bulk_g2s(ring + static_cast<size_t>(slot) * P.slot_bytes + q * ph.R * row_bytes,
+               ph.W + static_cast<size_t>(cur.r0 + cur.i * ph.R + q * ph.pair_offset) * ph.K, bytes, &full[slot]);
+    ++gi;
   }
-  return got;
-}
-
-// Refill state of the GEMV phase being read: its parameters, first stage and
-// stage count, and the stages after it.
-struct RingPhase {
-  const uint16_t* W;
-  int K, R, nphys, pair_offset, r0, nrows;
-  uint32_t base, nstages;
-};
-
-// A warp is done with stage gi.  The last of the 16 warps to get here frees
-// the slot by copying stage gi + nst into it.  Lane 0 calls this after the
-// warp's reads of the stage.
-VVLI_DEV void stage_done(const MegaParams& P, uint8_t* ring, uint64_t* full, unsigned* done, uint32_t gi,
-                         const RingPhase& rp, const StageSrc* tail, int ntail) {
-  const uint32_t slot = gi % P.nst;
-  __threadfence_block();
-  if (atomicAdd(&done[slot], 1u) == kCW - 1) {
-    done[slot] = 0;  // next used after stage gi + nst has landed and been read
-    __threadfence_block();
-    const uint32_t k = gi + P.nst;
-    if (k < rp.base + rp.nstages) {
-      issue_src(P, ring, full, slot,
-                stage_src(rp.W, rp.K, rp.R, rp.nphys, rp.pair_offset, rp.r0, rp.nrows, static_cast<int>(k - rp.base)));
-    } else {
-      const uint32_t j = k - (rp.base + rp.nstages);
-      if (j < static_cast<uint32_t>(ntail)) issue_src(P, ring, full, slot, tail[j]);
-    }
-  }
+  // Every issued copy lands before the CTA exits.
+  const uint32_t first = gi > static_cast<uint32_t>(P.nst) ? gi - P.nst : 0;
+  for (uint32_t i = first; i < gi; ++i) mbar_wait(&full[i % P.nst], (i / P.nst) & 1, err);
 }
 
 // ---------------------------------------------------------------- GEMV phase (consumers)
 template <int MAXC>
 __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, float* part, uint64_t* full,
-                          unsigned* done, uint32_t& gi, float* red, float* wv, int* wi, int* err, unsigned epoch0,
-                          int f, float* ffs, const StageSrc* tail, int ntail) {
+                          uint64_t* empty, uint32_t& gi, float* red, float* wv, int* wi, int* err, unsigned epoch0,
+                          int f, float* ffs) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = ph.K, S = ph.S, R = ph.R, nphys = ph.nphys;
   const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
@@ -321,7 +273,6 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
     }
   }
   const int pairs = R * nphys * S;
-  const RingPhase rp{ph.W, K, R, nphys, ph.pair_offset, r0, nrows, gi, static_cast<uint32_t>(nstages)};
   for (int i = 0; i < nstages; ++i, ++gi) {
     const uint32_t slot = gi % P.nst;
     if (!mbar_wait(&full[slot], (gi / P.nst) & 1, err)) break;
@@ -341,7 +292,7 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
       if (lane == 16 && vb) part[((i * R + rowb) * nphys + phb) * S + split] = v;
     }
     __syncwarp();
-    if (lane == 0) stage_done(P, ring, full, done, gi, rp, tail, ntail);
+    if (lane == 0) mbar_arrive(&empty[slot]);
   }
   __shared__ float scale_sh;
   if (ph.acc_in && ph.norm_w) {
@@ -563,8 +514,8 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
 // partial goes to the fixed-point accumulator with 64-bit integer atomics.
 // No grid barrier separates it from gate|up, so the weight ring keeps
 // streaming from one matrix into the next.
-__device__ void mega_axpy(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, uint64_t* full, unsigned* done,
-                          uint32_t& gi, const float* ffs, int* err, int f, const StageSrc* tail, int ntail) {
+__device__ void mega_axpy(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                          uint32_t& gi, const float* ffs, int* err, int f) {
   const int tid = threadIdx.x, lane = tid & 31;
   const int K = ph.K, R = ph.R;
   const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
@@ -578,7 +529,6 @@ __device__ void mega_axpy(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[q][e] = 0.f;
   if (tid == 0) trace_mark(P, f, 1);
-  const RingPhase rp{ph.W, K, R, ph.nphys, ph.pair_offset, r0, nrows, gi, static_cast<uint32_t>(nstages)};
   for (int i = 0; i < nstages; ++i, ++gi) {
     const uint32_t slot = gi % P.nst;
     if (!mbar_wait(&full[slot], (gi / P.nst) & 1, err)) break;
@@ -603,7 +553,7 @@ __device__ void mega_axpy(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
       }
     }
     __syncwarp();
-    if (lane == 0) stage_done(P, ring, full, done, gi, rp, tail, ntail);
+    if (lane == 0) mbar_arrive(&empty[slot]);
   }
   if (tid == 0) trace_mark(P, f, 2);
   unsigned long long* out = reinterpret_cast<unsigned long long*>(ph.acc_out);
@@ -862,29 +812,25 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
   __shared__ float wv[kCW];
   __shared__ int wi[kCW];
   __shared__ float ffs[kMaxFfRows];  // gate|up outputs of this CTA for the fused down_proj
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5;
   uint8_t* ring = smem;
   float* part = reinterpret_cast<float*>(smem + static_cast<size_t>(P.nst) * P.slot_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(part + ((P.part_floats + 1) & ~1));
-  unsigned* done = reinterpret_cast<unsigned*>(full + P.nst);  // warps done with each slot's current stage
+  uint64_t* empty = full + P.nst;
   int* err = &P.st->err;
 
-  __shared__ StageSrc tail[kMaxRingStages];  // the first stages after the GEMV phase being read
-  __shared__ int ntail;
-  __shared__ uint32_t next_base;  // number of the next GEMV phase's first stage
   if (tid == 0) {
     for (int i = 0; i < P.nst; ++i) {
       mbar_init(&full[i], 1);
-      done[i] = 0;
+      mbar_init(&empty[i], kCW);
     }
     fence_barrier_init();
-    StageSrc first[kMaxRingStages];
-    const int n = find_stages(P, 0, 0, 0, P.nst, first);  // the ring's first fill
-    for (int k = 0; k < n; ++k) issue_src(P, ring, full, k, first[k]);
-    ntail = 0;
-    next_base = 0;
   }
   __syncthreads();
+  if (warp == kCW) {
+    if ((tid & 31) == 0) mega_producer(P, ring, full, empty, err);
+    return;
+  }
   uint32_t gi = 0;
   uint32_t nbar = 0;  // barriers passed in this step
   const unsigned epoch0 = __ldcg(P.epoch);
@@ -896,28 +842,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
     } else if (ph.kind == MK_ATTN) {
       mega_attention(P, ph, part, err, f);
     } else if (ph.epi == ME_AXPY) {
-      mega_axpy(P, ph, ring, full, done, gi, ffs, err, f, tail, ntail);
+      mega_axpy(P, ph, ring, full, empty, gi, ffs, err, f);
     } else {
-      mega_gemv<4>(P, ph, ring, part, full, done, gi, red, wv, wi, err, epoch0, f, ffs, tail, ntail);  // cpl <= 4
+      mega_gemv<4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs);  // plans have cpl <= 4
     }
     if (tid == 0) trace_mark(P, f, 3);
-    // Before the CTA barrier of the phase change: when the next phase is a
-    // GEMV, thread 0 finds the stages after it (its refills' targets beyond
-    // its own rows) while the others arrive.
-    auto plan_tail = [&]() {
-      if (tid != 0 || f + 1 >= P.nphases || P.phases[f + 1].kind != MK_GEMV) return;
-      int r0, nrows;
-      const uint32_t ns = static_cast<uint32_t>(phase_stages(P.phases[f + 1], &r0, &nrows));
-      ntail = find_stages(P, f + 2, next_base + ns, next_base + ns, P.nst, tail);
-      next_base += ns;
-    };
     if (f + 1 < P.nphases && P.phases[f + 1].no_barrier) {
       named_barrier(1, kNC);  // the next phase reads only what this CTA wrote
-      plan_tail();            // (after every warp's last use of the old tail)
-      named_barrier(1, kNC);
     } else if (f + 1 < P.nphases) {
       grid_arrive(P.bar);
-      plan_tail();  // ordered for the others by grid_wait's CTA barrier
       // While the other CTAs arrive: warm L1/L2 with the next phase's
       // constant vectors (norm weights, biases) of this CTA.
       const MegaPhase& nx = P.phases[f + 1];
@@ -928,16 +861,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
       // waits then end it too.
       const uint64_t target = (static_cast<uint64_t>(epoch0) * P.bars_per_step + nbar + 1) * gridDim.x;
       ++nbar;
-      if (!grid_wait(P.bar, target, err)) {
-        // Every copy in flight lands before the CTA ends (the stages after
-        // the ones read so far, up to the ring's depth).
-        if (tid == 0) {
-          StageSrc left[kMaxRingStages];
-          const int n = find_stages(P, 0, gi, 0, P.nst, left);
-          for (int j = 0; j < n; ++j) mbar_wait(&full[(gi + j) % P.nst], ((gi + j) / P.nst) & 1, err);
-        }
-        break;
-      }
+      if (!grid_wait(P.bar, target, err)) break;
     }
     if (tid == 0) trace_mark(P, f, 4);
   }

@@ -454,7 +454,7 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   for (const MegaPhase& m : ph) {
     if (m.kind != MK_GEMV) continue;
     if (m.cpl > 4) return false;
-    if (c->group > 8 || kMegaThreads % c->d || kMegaThreads / c->d * 16 < kPage) return false;
+    if (c->group > 8 || (kMegaThreads - 32) % c->d || (kMegaThreads - 32) / c->d * 16 < kPage) return false;
     slot = std::max(slot, m.stage_bytes);
     part = std::max(part, static_cast<size_t>((m.N + grid - 1) / grid + 2) * m.nphys * m.S);
   }
@@ -463,7 +463,6 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   // Two stages measured best: a deeper ring keeps more weight copies in
   // flight, which lengthens every latency-bound access of the phase changes.
   nst = std::min(nst, getenv("VVLI_MEGA_STAGES") ? std::max(2, atoi(getenv("VVLI_MEGA_STAGES"))) : 2);
-  nst = std::min(nst, kMaxRingStages);
   if (nst < 2) return false;
   c->mega_smem = static_cast<size_t>(nst) * slot + ((part + 1) & ~size_t(1)) * 4 + 2 * nst * sizeof(uint64_t);
   if (cudaMalloc(&c->d_phases, ph.size() * sizeof(MegaPhase)) != cudaSuccess) return false;
