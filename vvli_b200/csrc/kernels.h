@@ -97,6 +97,7 @@ enum MegaEpi { ME_STORE = 0, ME_RESIDUAL = 1, ME_SILU = 2, ME_ARGMAX = 3, ME_QKV
 constexpr double kAccScale = 4294967296.0;
 constexpr int kMaxFfRows = 256;  // gate|up rows per CTA kept in shared memory for ME_AXPY
 constexpr int kMaxTp = 8;
+constexpr int kMaxResRows = 64;  // rows of x a CTA can keep in shared memory (MegaParams::xres)
 constexpr int kMegaConsumerWarps = 16;
 constexpr int kMegaThreads = (kMegaConsumerWarps + 1) * 32;
 
@@ -138,6 +139,7 @@ struct MegaParams {
   int h, vocab;
   float* x;                // residual stream [h]
   float* ssq;              // [gridDim.x] per-CTA sums of squares of x
+  int xres;                // 1: each CTA keeps its rows of x in shared memory across the step
   float eps;
   unsigned long long* bar; // grid barrier arrivals (grows forever; see megakernel.cu)
   unsigned* epoch;         // increases by one per step (tensor-parallel flag values)

@@ -179,7 +179,7 @@ __device__ void mega_producer(const MegaParams& P, uint8_t* ring, uint64_t* full
 template <int MAXC>
 __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, float* part, uint64_t* full,
                           uint64_t* empty, uint32_t& gi, float* red, float* wv, int* wi, int* err, unsigned epoch0,
-                          int f, float* ffs) {
+                          int f, float* ffs, float* xres) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = ph.K, S = ph.S, R = ph.R, nphys = ph.nphys;
   const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
@@ -419,13 +419,14 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
         const int r = r0 + rl;
         float a = 0.f;
         for (int s = 0; s < S; ++s) a += part[rl * S + s];
-        float xo = __ldcg(P.x + r);
+        float xo = P.xres ? xres[rl] : __ldcg(P.x + r);  // this CTA's own rows of x
         if (ph.acc_fold) {  // the previous layer's down_proj joins the residual stream here
           xo = xo + from_fixed(__ldcg(ph.acc_fold + r));
           ph.acc_fold[r] = 0;
         }
         const float xn = xo + a;
         P.x[r] = xn;
+        if (P.xres) xres[rl] = xn;
         ss = fmaf(xn, xn, ss);
         if (P.hidden && (ph.ar_index & 1)) P.hidden[static_cast<size_t>(ph.layer) * P.h + r] = xn;
       }
@@ -784,7 +785,7 @@ __device__ void mega_attention(const MegaParams& P, const MegaPhase& ph, float* 
 
 // ---------------------------------------------------------------- embed phase
 // copyEmbeddingToken (src/llm.zig:1373-1380) / forwardEmbedding's copy.
-__device__ void mega_embed(const MegaParams& P, float* red, int* err) {
+__device__ void mega_embed(const MegaParams& P, float* red, int* err, float* xres) {
   const int tid = threadIdx.x;
   const int r0 = cta_row0(P.h), r1 = cta_row1(P.h);
   const int pos = P.st->pos;
@@ -797,6 +798,7 @@ __device__ void mega_embed(const MegaParams& P, float* red, int* err) {
   for (int r = r0 + tid; r < r1; r += kNC) {
     const float v = P.st->use_embedding ? P.emb_in[r] : bf16_to_f32(P.emb[static_cast<size_t>(tok) * P.h + r]);
     P.x[r] = v;
+    if (P.xres) xres[r - r0] = v;
     ss = fmaf(v, v, ss);
   }
   ss = consumer_sum(ss, red);
@@ -812,6 +814,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
   __shared__ float wv[kCW];
   __shared__ int wi[kCW];
   __shared__ float ffs[kMaxFfRows];  // gate|up outputs of this CTA for the fused down_proj
+  __shared__ float xres[kMaxResRows];  // this CTA's rows of x (MegaParams::xres)
   const int tid = threadIdx.x, warp = tid >> 5;
   uint8_t* ring = smem;
   float* part = reinterpret_cast<float*>(smem + static_cast<size_t>(P.nst) * P.slot_bytes);
@@ -838,13 +841,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
     const MegaPhase& ph = P.phases[f];
     if (tid == 0) trace_mark(P, f, 0);
     if (ph.kind == MK_EMBED) {
-      mega_embed(P, red, err);
+      mega_embed(P, red, err, xres);
     } else if (ph.kind == MK_ATTN) {
       mega_attention(P, ph, part, err, f);
     } else if (ph.epi == ME_AXPY) {
       mega_axpy(P, ph, ring, full, empty, gi, ffs, err, f);
     } else {
-      mega_gemv<4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs);  // plans have cpl <= 4
+      mega_gemv<4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres);  // cpl <= 4
     }
     if (tid == 0) trace_mark(P, f, 3);
     if (f + 1 < P.nphases && P.phases[f + 1].no_barrier) {

@@ -488,6 +488,9 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   P.bar = c->bar;
   P.epoch = c->epoch;
   P.n_ar = 2 * c->L;
+  // Each CTA owns the same rows of x in the embed, o_proj and down_proj
+  // phases, so it can keep them in shared memory instead of reading them back.
+  P.xres = (c->tp_size == 1 && !fused && (c->h + grid - 1) / grid <= kMaxResRows) ? 1 : 0;
   P.bars_per_step = static_cast<int>(ph.size()) - 1;
   for (const MegaPhase& m : ph) P.bars_per_step -= m.no_barrier ? 1 : 0;
   P.acc_zero = fused ? acc[(c->L - 1) & 1] : nullptr;
