@@ -309,6 +309,14 @@ int vvli_cuda_trace(vvli_ctx* ctx, uint64_t* out, uint64_t cap, uint64_t* count)
 int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two_a, uint64_t seed,
                             float* max_rel_err);
 
+/* Self-test of the tensor-core prompt attention, with no counterpart in the
+ * reference: random q, K and V (head_dim d of 64 or 128, `group` q heads per
+ * kv head, 2 kv heads, `tokens` query tokens at positions pos0 .., a
+ * scrambled page table) through the tcgen05 kernel and the SIMT flash kernel
+ * on `device`; `max_rel_err` = max |difference| / max |SIMT output|. */
+int vvli_cuda_attention_selftest(int device, int d, int group, int tokens, int pos0, uint64_t seed,
+                                 float* max_rel_err);
+
 /* One decode step of `batch` independent sequences, with no counterpart in
  * the reference (which decodes one sequence): row b is sequence slot b, with
  * its own KV cache (slot 0 is the cache forward_token uses), and computes what

@@ -68,6 +68,8 @@ SIGNATURES = {
     "vvli_cuda_trace": (ctypes.c_int, [_ctx, _u64p, ctypes.c_uint64, _u64p]),
     "vvli_cuda_gemm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                ctypes.c_int, ctypes.c_uint64, _f32p]),
+    "vvli_cuda_attention_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                    ctypes.c_int, ctypes.c_uint64, _f32p]),
     "vvli_cuda_forward_batch": (ctypes.c_int, [_ctx, _u32p, _u64p, ctypes.c_uint64, _f32p, _u32p]),
     "vvli_cuda_argmax_rows_static": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
                                                     ctypes.c_void_p, ctypes.c_void_p]),

@@ -621,6 +621,12 @@ static cudaError_t launch_pa(const PrefillAttnParams& p, cudaStream_t s) {
 }
 
 cudaError_t launch_prefill_attention(const PrefillAttnParams& p, cudaStream_t s) {
+  static const bool tc = !(getenv("VVLI_ATTN_TC") && getenv("VVLI_ATTN_TC")[0] == '0');
+  if (tc && prefill_attention_tc_supported(p.d, p.group)) return launch_prefill_attention_tc(p, s);
+  return launch_prefill_attention_simt(p, s);
+}
+
+cudaError_t launch_prefill_attention_simt(const PrefillAttnParams& p, cudaStream_t s) {
   if (p.group <= 8 && kFaRows / p.group >= 1) {
     if (p.d == 128) return launch_flash<128>(p, s);
     if (p.d == 64) return launch_flash<64>(p, s);

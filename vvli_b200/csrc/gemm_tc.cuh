@@ -76,7 +76,15 @@ struct PrefillAttnParams {
   uint16_t* out_lo;
   int M, nq, nkv, d, group, pos0;
   float inv_sqrt_d;
+  int* err;              // VVLI_ERR_TIMEOUT when a bounded wait gives up (may be null)
 };
+// Tensor-core kernel when it takes the shape (and VVLI_ATTN_TC is not 0), else the SIMT kernels.
 cudaError_t launch_prefill_attention(const PrefillAttnParams& p, cudaStream_t s);
+cudaError_t launch_prefill_attention_simt(const PrefillAttnParams& p, cudaStream_t s);
+bool prefill_attention_tc_supported(int d, int group);
+cudaError_t launch_prefill_attention_tc(const PrefillAttnParams& p, cudaStream_t s);
+// Random q, K, V (d, group, M tokens after pos0 positions, scrambled page table): the
+// tensor-core kernel against the SIMT flash kernel; *max_rel_err = max |diff| / max |out|.
+cudaError_t attention_tc_selftest(int d, int group, int M, int pos0, uint64_t seed, float* max_rel_err);
 
 }  // namespace vvli

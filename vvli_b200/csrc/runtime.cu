@@ -741,7 +741,7 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start) 
       g.nk = (g.K + kGemmBK - 1) / kGemmBK;
       CK(launch_gemm_tc(c->tm_ah_hi, c->tm_ah_lo, c->tm_w[4 * l + 0], g, s));
       PrefillAttnParams a{c->pf_q, kc, vc, c->page_table, c->pf_ahi, c->pf_alo, M, c->nq_l, c->nkv_l, c->d,
-                          c->group, pos0, 1.0f / sqrtf(static_cast<float>(c->d))};
+                          c->group, pos0, 1.0f / sqrtf(static_cast<float>(c->d)), err};
       CK(launch_prefill_attention(a, s));
       GemmParams o{};
       o.M = M, o.two_a = 1, o.err = err, o.N = c->h, o.K = c->q_rows, o.epi = GE_RESID, o.y = c->pf_x, o.ldy = c->h;
@@ -1799,6 +1799,15 @@ int vvli_cuda_trace(vvli_ctx* c, uint64_t* out, uint64_t cap, uint64_t* count) {
     CK(cudaSetDevice(c->device));
     CK(cudaMemcpy(out, c->trace, *count * sizeof(uint64_t), cudaMemcpyDeviceToHost));
   }
+  return VVLI_OK;
+}
+
+int vvli_cuda_attention_selftest(int device, int d, int group, int tokens, int pos0, uint64_t seed,
+                                 float* max_rel_err) {
+  if (!max_rel_err || tokens <= 0 || pos0 < 0 || !prefill_attention_tc_supported(d, group))
+    return VVLI_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(device));
+  CK(attention_tc_selftest(d, group, tokens, pos0, seed, max_rel_err));
   return VVLI_OK;
 }
 
