@@ -10,19 +10,22 @@
 //     each product is hi.hi + hi.lo + lo.hi: three kind::f16 MMAs into one
 //     fp32 accumulator in TMEM (the dropped lo.lo term is below fp32
 //     rounding of the sum).
-//   * S = Q K^T (128 x 64) lands in TMEM; each of the 128 worker threads owns
+//   * S = Q K^T (128 x 64) lands in TMEM; each of the 128 softmax threads owns
 //     one query row (one TMEM lane), so the online softmax (scale, causal
 //     mask, running max and sum) needs no shuffles.  P (hi / lo) goes to
-//     shared memory as the A operand of P V; P V (128 x d) lands in TMEM and
-//     is added to the row's output kept in registers, O = O * alpha + P V.
+//     shared memory as the A operand of P V, which accumulates O (128 x d) in
+//     TMEM; when a row's max moves, its O is rescaled in TMEM first.
 //   * Operands are written to shared memory by the worker threads in the
 //     layout a 128-byte-swizzled TMA load would produce (rows of 128 bytes,
 //     the 16-byte chunk c of row r stored at chunk c ^ (r % 8), 8-row groups
 //     of 1024 bytes), K-major: Q and K by rows, V transposed (d rows of 64
 //     keys) so it is the K-major B operand of P V.
-//   * Warp 0 allocates TMEM and one of its threads issues the MMAs; warps
-//     1-4 (TMEM lanes 32 (w % 4) ..) convert operands, run the softmax and
-//     keep the output.  Every wait is bounded.
+//   * Warps 0-3 (TMEM lanes 32 w ..) run the softmax and write the output;
+//     warps 4-7 convert Q, K and V into shared memory, K / V double-buffered
+//     so tile j + 1 is converted while tile j is in the softmax; warp 8
+//     allocates TMEM and one of its threads issues the MMAs.  Every wait is
+//     bounded.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -37,10 +40,15 @@ namespace vvli {
 
 namespace {
 
-constexpr int kAtRows = 128;   // query rows per CTA: M of every MMA, TMEM lanes
-constexpr int kAtKeys = 64;    // keys per tile: one KV page
-constexpr int kAtWorkers = 128;
-constexpr int kAtThreads = 32 + kAtWorkers;
+constexpr int kAtRows = 128;        // query rows per CTA: M of every MMA, TMEM lanes
+constexpr int kAtKeys = 64;         // keys per tile: one KV page
+constexpr int kAtSoftmax = 128;     // warps 0-3: one query row (TMEM lane) per thread
+constexpr int kAtConv = 128;        // warps 4-7: Q, K and V into shared memory
+constexpr int kAtThreads = kAtSoftmax + kAtConv + 32;  // warp 8: TMEM and the MMAs
+// A row's reference max moves only when a score exceeds it by more than
+// this (natural log): exp(s - m) then stays below e^8, so the output in TMEM
+// is rescaled rarely; the result is the same up to fp32 rounding.
+constexpr float kAtRescale = 8.0f;
 
 template <int D>
 struct AtLayout {
@@ -48,13 +56,14 @@ struct AtLayout {
   static constexpr uint32_t k_tile = kAtKeys * D * 2;         // D / 64 atoms of 64 rows
   static constexpr uint32_t v_tile = D * kAtKeys * 2;         // one atom of D rows (64 keys)
   static constexpr uint32_t p_tile = kAtRows * kAtKeys * 2;   // one atom of 128 rows
-  static constexpr uint32_t q_hi = 0, q_lo = q_hi + q_tile;
-  static constexpr uint32_t k_hi = q_lo + q_tile, k_lo = k_hi + k_tile;
-  static constexpr uint32_t v_hi = k_lo + k_tile, v_lo = v_hi + v_tile;
-  static constexpr uint32_t p_hi = v_lo + v_tile, p_lo = p_hi + p_tile;
-  static constexpr uint32_t bars = p_lo + p_tile;             // 4 mbarriers + TMEM address
-  static constexpr uint32_t smem = bars + 64 + 1024;          // + alignment slack
-  static constexpr uint32_t tmem_cols = 64 + D <= 128 ? 128 : 256;  // S at column 0, P V at column 64
+  static constexpr uint32_t kv_buf = 2 * k_tile + 2 * v_tile;  // K hi, K lo, V^T hi, V^T lo
+  static constexpr uint32_t k_hi = 0, k_lo = k_tile, v_hi = 2 * k_tile, v_lo = 2 * k_tile + v_tile;  // in a buffer
+  static constexpr uint32_t q_hi = 0, q_lo = q_tile;
+  static constexpr uint32_t kv0 = 2 * q_tile;                 // two K / V buffers (tile j uses j % 2)
+  static constexpr uint32_t p_hi = kv0 + 2 * kv_buf, p_lo = p_hi + p_tile;
+  static constexpr uint32_t bars = p_lo + p_tile;             // 7 mbarriers + TMEM address
+  static constexpr uint32_t smem = bars + 128 + 1024;         // + alignment slack
+  static constexpr uint32_t tmem_cols = 64 + D <= 128 ? 128 : 256;  // S at column 0, O at column 64
   static constexpr uint32_t s_idesc = umma_idesc(kAtRows, kAtKeys);
   static constexpr uint32_t pv_idesc = umma_idesc(kAtRows, D);
 };
@@ -65,22 +74,68 @@ VVLI_DEV uint32_t sw_chunk(int rows, int r, int c) {
   return static_cast<uint32_t>((c >> 3) * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-// hi / lo bf16 pairs of 8 floats, packed as two 16-byte chunks.
+// hi / lo bf16 pairs (round to nearest even) of 8 floats, packed as two 16-byte chunks.
 VVLI_DEV void split8(const float* v, uint4& hi, uint4& lo) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    uint16_t h0, l0, h1, l1;
-    split_bf16(v[2 * i], h0, l0);
-    split_bf16(v[2 * i + 1], h1, l1);
-    h[i] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
-    l[i] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
+    const __nv_bfloat162 hb = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    const float2 hf = __bfloat1622float2(hb);
+    const __nv_bfloat162 lb = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+    h[i] = *reinterpret_cast<const uint32_t*>(&hb);
+    l[i] = *reinterpret_cast<const uint32_t*>(&lb);
   }
   hi = make_uint4(h[0], h[1], h[2], h[3]);
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 VVLI_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+VVLI_DEV void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Rows [r0, r0 + n * 128 / (D / 8)) of a row-major fp32 source -> hi / lo
+// chunks of a swizzled tile: N items per converter thread, item i = (row,
+// chunk) of index ct + i * 128; all loads are issued before the first store.
+template <int D, int N, typename Src>
+VVLI_DEV void convert_rows(Src src, int nrows_valid, int tile_rows, uint8_t* hi, uint8_t* lo, int ct) {
+  float4 a[N][2];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int it = ct + i * kAtConv, r = it / (D / 8), c = it % (D / 8);
+    if (r < nrows_valid) {
+      const float4* p = src(r, c);
+      a[i][0] = __ldcg(p), a[i][1] = __ldcg(p + 1);
+    } else {
+      a[i][0] = a[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int it = ct + i * kAtConv, r = it / (D / 8), c = it % (D / 8);
+    const float v[8] = {a[i][0].x, a[i][0].y, a[i][0].z, a[i][0].w, a[i][1].x, a[i][1].y, a[i][1].z, a[i][1].w};
+    uint4 h, l;
+    split8(v, h, l);
+    const uint32_t off = sw_chunk(tile_rows, r, c);
+    *reinterpret_cast<uint4*>(hi + off) = h;
+    *reinterpret_cast<uint4*>(lo + off) = l;
+  }
+}
 
 template <int D>
 __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const PrefillAttnParams p) {
@@ -89,11 +144,12 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
   const uint32_t raw = smem_u32(at_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles want 1024-byte alignment
   uint8_t* sm = at_raw + (base - raw);
-  uint64_t* kv_ready = reinterpret_cast<uint64_t*>(sm + L::bars);  // workers wrote Q (first tile), K, V
-  uint64_t* s_full = kv_ready + 1;                                  // S = Q K^T is in TMEM
-  uint64_t* p_ready = kv_ready + 2;                                 // workers wrote P
-  uint64_t* pv_full = kv_ready + 3;                                 // P V is in TMEM
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(kv_ready + 4);
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(sm + L::bars);  // [2] converters wrote K / V (and Q)
+  uint64_t* kv_empty = kv_full + 2;                                 // [2] the MMAs that read a buffer are done
+  uint64_t* s_full = kv_full + 4;                                   // S = Q K^T is in TMEM
+  uint64_t* p_ready = kv_full + 5;                                  // softmax wrote P (and rescaled O)
+  uint64_t* pv_full = kv_full + 6;                                  // O += P V is done
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(kv_full + 7);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.group, g = blockIdx.x;
   const int BQ = kAtRows / G;
@@ -105,13 +161,16 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
   const int qd = p.nq * D;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_ready, kAtWorkers);
+    mbar_init(&kv_full[0], kAtConv);
+    mbar_init(&kv_full[1], kAtConv);
+    mbar_init(&kv_empty[0], 1);
+    mbar_init(&kv_empty[1], 1);
     mbar_init(s_full, 1);
-    mbar_init(p_ready, kAtWorkers);
+    mbar_init(p_ready, kAtSoftmax);
     mbar_init(pv_full, 1);
     fence_barrier_init();
   }
-  if (warp == 0) {
+  if (warp == 8) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
                  "r"(L::tmem_cols)
                  : "memory");
@@ -122,97 +181,74 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 0) {
+  if (warp == 8) {
     if (lane == 0) {  // ---- MMA issuer
-      int ns = 0, npv = 0;  // commits issued
+      int done = 0;   // tiles whose MMAs were all issued
       for (int j = 0; j < ntiles; ++j) {
-        if (!mbar_wait(kv_ready, j & 1, p.err)) break;
+        const uint8_t* kvb = sm + L::kv0 + (j & 1) * L::kv_buf;
+        const uint32_t kva = base + L::kv0 + (j & 1) * L::kv_buf;
+        (void)kvb;
+        if (!mbar_wait(&kv_full[j & 1], (j >> 1) & 1, p.err)) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {  // S = Q K^T over d, 16 per MMA
           const uint32_t ka = (ks >> 2) * (kAtRows * 128) + (ks & 3) * 32;
           const uint32_t kb = (ks >> 2) * (kAtKeys * 128) + (ks & 3) * 32;
           const uint64_t qh = umma_desc(base + L::q_hi + ka), ql = umma_desc(base + L::q_lo + ka);
-          const uint64_t kh = umma_desc(base + L::k_hi + kb), kl = umma_desc(base + L::k_lo + kb);
+          const uint64_t kh = umma_desc(kva + L::k_hi + kb), kl = umma_desc(kva + L::k_lo + kb);
           umma_bf16(tmem, qh, kh, L::s_idesc, ks != 0);
           umma_bf16(tmem, qh, kl, L::s_idesc, 1u);
           umma_bf16(tmem, ql, kh, L::s_idesc, 1u);
         }
         umma_commit(s_full);
-        ++ns;
         if (!mbar_wait(p_ready, j & 1, p.err)) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < kAtKeys / 16; ++ks) {  // P V over the tile's keys
+        for (int ks = 0; ks < kAtKeys / 16; ++ks) {  // O += P V over the tile's keys
           const uint64_t ph = umma_desc(base + L::p_hi + ks * 32), pl = umma_desc(base + L::p_lo + ks * 32);
-          const uint64_t vh = umma_desc(base + L::v_hi + ks * 32), vl = umma_desc(base + L::v_lo + ks * 32);
-          umma_bf16(tmem + 64, ph, vh, L::pv_idesc, ks != 0);
+          const uint64_t vh = umma_desc(kva + L::v_hi + ks * 32), vl = umma_desc(kva + L::v_lo + ks * 32);
+          umma_bf16(tmem + 64, ph, vh, L::pv_idesc, (j | ks) != 0);
           umma_bf16(tmem + 64, ph, vl, L::pv_idesc, 1u);
           umma_bf16(tmem + 64, pl, vh, L::pv_idesc, 1u);
         }
         umma_commit(pv_full);
-        ++npv;
+        umma_commit(&kv_empty[j & 1]);
+        done = j + 1;
       }
       // Every MMA has finished before TMEM is released (already so unless a wait gave up).
-      if (ns > 0) mbar_wait(s_full, (ns - 1) & 1, p.err);
-      if (npv > 0) mbar_wait(pv_full, (npv - 1) & 1, p.err);
+      if (done > 0) mbar_wait(&kv_empty[(done - 1) & 1], ((done - 1) >> 1) & 1, p.err);
     }
-  } else {  // ---- workers: row R = TMEM lane
-    const int wt = threadIdx.x - 32;  // 0 .. 127
-    const int R = 32 * (warp & 3) + lane;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
-    const int qpos = R < rows ? p.pos0 + t0 + R / G : -1;
+  } else if (warp >= 4) {  // ---- converters
+    const int ct = threadIdx.x - kAtSoftmax;
     // Q (hi / lo), zero rows past `rows`
-    for (int it = wt; it < kAtRows * (D / 8); it += kAtWorkers) {
-      const int r = it / (D / 8), c = it % (D / 8);
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (r < rows) {
-        const float4* src = reinterpret_cast<const float4*>(
-            p.q + static_cast<size_t>(t0 + r / G) * qd + static_cast<size_t>(g * G + r % G) * D + c * 8);
-        const float4 a = src[0], b = src[1];
-        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-      }
-      uint4 hi, lo;
-      split8(v, hi, lo);
-      const uint32_t off = sw_chunk(kAtRows, r, c);
-      *reinterpret_cast<uint4*>(sm + L::q_hi + off) = hi;
-      *reinterpret_cast<uint4*>(sm + L::q_lo + off) = lo;
-    }
-    float o[D];
+    auto qsrc = [&](int r, int c) {
+      return reinterpret_cast<const float4*>(p.q + static_cast<size_t>(t0 + r / G) * qd +
+                                             static_cast<size_t>(g * G + r % G) * D + c * 8);
+    };
 #pragma unroll
-    for (int e = 0; e < D; ++e) o[e] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < ntiles && ok; ++j) {
+    for (int h = 0; h < D / 64; ++h)  // D / 8 items per thread, 8 at a time
+      convert_rows<D, 8>([&](int r, int c) { return qsrc(r, c); }, rows, kAtRows, sm + L::q_hi, sm + L::q_lo,
+                         ct + h * 8 * kAtConv);
+    for (int j = 0; j < ntiles; ++j) {
       const int j0 = j * kAtKeys;
       const int nkeys = min(kAtKeys, last_pos + 1 - j0);
-      const size_t kvb = kv_off(p.page_table, j0, g, p.nkv, D);  // the tile's rows are contiguous
+      uint8_t* kvb = sm + L::kv0 + (j & 1) * L::kv_buf;
+      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&kv_empty[j & 1], ((j >> 1) - 1) & 1, p.err))) break;
+      const size_t tb = kv_off(p.page_table, j0, g, p.nkv, D);  // the tile's rows are contiguous
       // K by rows (zero past nkeys)
-      for (int it = wt; it < kAtKeys * (D / 8); it += kAtWorkers) {
-        const int r = it / (D / 8), c = it % (D / 8);
-        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (r < nkeys) {
-          const float4* src = reinterpret_cast<const float4*>(p.k_cache + kvb + static_cast<size_t>(r) * D + c * 8);
-          const float4 a = __ldcg(src), b = __ldcg(src + 1);
-          v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-        }
-        uint4 hi, lo;
-        split8(v, hi, lo);
-        const uint32_t off = sw_chunk(kAtKeys, r, c);
-        *reinterpret_cast<uint4*>(sm + L::k_hi + off) = hi;
-        *reinterpret_cast<uint4*>(sm + L::k_lo + off) = lo;
-      }
+      convert_rows<D, D / 16>(
+          [&](int r, int c) { return reinterpret_cast<const float4*>(p.k_cache + tb + static_cast<size_t>(r) * D + c * 8); },
+          nkeys, kAtKeys, kvb + L::k_hi, kvb + L::k_lo, ct);
       // V transposed: item (dims 8eb.., keys 8jc..) -> 8 chunks, one per dim (zero past nkeys)
-      for (int it = wt; it < (D / 8) * (kAtKeys / 8); it += kAtWorkers) {
-        const int eb = it % (D / 8), jc = it / (D / 8);
+      if (ct < D) {
+        const int eb = ct % (D / 8), jc = ct / (D / 8);
         float t[8][8];
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
           const int key = 8 * jc + jj;
           float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
           if (key < nkeys) {
-            const float4* src =
-                reinterpret_cast<const float4*>(p.v_cache + kvb + static_cast<size_t>(key) * D + eb * 8);
+            const float4* src = reinterpret_cast<const float4*>(p.v_cache + tb + static_cast<size_t>(key) * D + eb * 8);
             a = __ldcg(src), b = __ldcg(src + 1);
           }
           t[0][jj] = a.x, t[1][jj] = a.y, t[2][jj] = a.z, t[3][jj] = a.w;
@@ -223,16 +259,23 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
           uint4 hi, lo;
           split8(t[e], hi, lo);
           const uint32_t off = sw_chunk(D, 8 * eb + e, jc);
-          *reinterpret_cast<uint4*>(sm + L::v_hi + off) = hi;
-          *reinterpret_cast<uint4*>(sm + L::v_lo + off) = lo;
+          *reinterpret_cast<uint4*>(kvb + L::v_hi + off) = hi;
+          *reinterpret_cast<uint4*>(kvb + L::v_lo + off) = lo;
         }
       }
       fence_async_smem();  // generic-proxy writes, read by the tensor cores
-      tc_fence_before();   // this thread's TMEM loads of the last tile come first
-      mbar_arrive(kv_ready);
-      // ---- softmax of S (softmaxInPlace, src/llm.zig:1408-1419, online form)
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, p.err));
-      if (!ok) break;
+      mbar_arrive(&kv_full[j & 1]);
+    }
+  } else {  // ---- softmax: row R = TMEM lane (softmaxInPlace, src/llm.zig:1408-1419, online form)
+    const int R = threadIdx.x;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    const int qpos = R < rows ? p.pos0 + t0 + R / G : -1;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int j0 = j * kAtKeys;
+      const int nkeys = min(kAtKeys, last_pos + 1 - j0);
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, p.err)))) break;
       tc_fence_after();
       float s[kAtKeys];
       tmem_ld32(trow, s);
@@ -243,8 +286,22 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
         s[c] = (c < nkeys && j0 + c <= qpos) ? s[c] * p.inv_sqrt_d : -INFINITY;
         mt = fmaxf(mt, s[c]);
       }
-      const float mnew = fmaxf(m, mt);
-      const float alpha = m == -INFINITY ? 0.f : expf(m - mnew);
+      const bool move = mt > m + kAtRescale;  // false while the row has no key yet (mt = -inf)
+      const float mnew = move ? mt : m;
+      const float alpha = move ? (m == -INFINITY ? 0.f : expf(m - mnew)) : 1.f;
+      // P is free and O complete once the last tile's P V is done
+      if (j > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(pv_full, (j - 1) & 1, p.err)))) break;
+      tc_fence_after();
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // O = O * alpha (warp-collective TMEM access)
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          float v[32];
+          tmem_ld32(trow + 64 + cc * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st32(trow + 64 + cc * 32, v);
+        }
+      }
       float sum = 0.f;
 #pragma unroll
       for (int c8 = 0; c8 < kAtKeys / 8; ++c8) {
@@ -265,28 +322,25 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(p_ready);
-      // ---- O = O * alpha + P V (addScaled, src/llm.zig:1398-1406)
-      ok = __all_sync(0xffffffffu, mbar_wait(pv_full, j & 1, p.err));
-      if (!ok) break;
+    }
+    if (ok && __all_sync(0xffffffffu, mbar_wait(pv_full, (ntiles - 1) & 1, p.err))) {
       tc_fence_after();
-#pragma unroll
+      const size_t orow = static_cast<size_t>(t0 + R / G) * qd + static_cast<size_t>(g * G + R % G) * D;
+      const float inv = 1.0f / l;
+#pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float v[32];
         tmem_ld32(trow + 64 + cc * 32, v);
+        if (R < rows) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[cc * 32 + i] = fmaf(o[cc * 32 + i], alpha, v[i]);
+          for (int i = 0; i < 32; ++i) split_bf16(v[i] * inv, p.out_hi[orow + cc * 32 + i], p.out_lo[orow + cc * 32 + i]);
+        }
       }
-    }
-    if (ok && R < rows) {
-      const size_t orow = static_cast<size_t>(t0 + R / G) * qd + static_cast<size_t>(g * G + R % G) * D;
-      const float inv = 1.0f / l;
-#pragma unroll
-      for (int e = 0; e < D; ++e) split_bf16(o[e] * inv, p.out_hi[orow + e], p.out_lo[orow + e]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 8) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::tmem_cols) : "memory");
   }
