@@ -241,7 +241,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
           nkeys, kAtKeys, kvb + L::k_hi, kvb + L::k_lo, ct);
       // V transposed: item (dims 8eb.., keys 8jc..) -> 8 chunks, one per dim (zero past nkeys)
       if (ct < D) {
-        const int eb = ct % (D / 8), jc = ct / (D / 8);
+        // the 8 lanes of a key chunk group write one row's 8 chunks (no bank conflicts)
+        const int jc = ct % 8, eb = ct / 8;
         float t[8][8];
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {

@@ -65,8 +65,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_full + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr bool kPair = EPI == GE_SILU;
-  const int m0 = blockIdx.y * kGemmBM;
-  const int n0 = blockIdx.x * (kPair ? BN / 2 : BN);  // first output column of the tile
+  // Row tiles vary fastest: the CTAs of one weight tile run together and
+  // share its L2 lines, so each weight tile comes from HBM about once.
+  const int m0 = blockIdx.x * kGemmBM;
+  const int n0 = blockIdx.y * (kPair ? BN / 2 : BN);  // first output column of the tile
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemmStages; ++i) {
@@ -214,12 +216,12 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
   // when 256-wide ones would leave most SMs idle.
   const bool narrow = p.epi == GE_RESID && ((p.N + 255) / 256) * mt < 96;
   if (narrow) {
-    const dim3 grid((p.N + 127) / 128, mt);
+    const dim3 grid(mt, (p.N + 127) / 128);
     gemm_tc_kernel<GE_RESID, 128><<<grid, kGemmThreads, TcLayout<128>::smem, s>>>(a_hi, a_lo, w, p);
     return cudaGetLastError();
   }
   const int cols = p.epi == GE_SILU ? 128 : 256;
-  const dim3 grid((p.N + cols - 1) / cols, mt);
+  const dim3 grid(mt, (p.N + cols - 1) / cols);
   constexpr size_t smem = TcLayout<256>::smem;
   switch (p.epi) {
     case GE_QKV: gemm_tc_kernel<GE_QKV, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, p); break;
