@@ -403,7 +403,7 @@ def _main(args, out_fd):
                "algorithmic_tflops": (gemm_flops + attn_flops + 2.0 * h * cfg.vocab_size) / (prefill_ms / 1e3) / 1e12,
                "tensor_core_gemm": runner.query("tc_prefill") == 1,
                "note": "activations enter the tensor cores as bf16 hi+lo pairs (2 MMAs per product) for fp32-level "
-                       "parity; attention on CUDA cores"}
+                       "parity; attention on the tensor cores (q, k, v, p as hi+lo pairs, 3 MMAs per product)"}
     launches_per_step = int(runner.query("kernels_per_step"))
     # Sampler.next on the device (generator.Options defaults: T 0.8, top-p 0.95, top-k 40, rp 1.1 over 64)
     # over the last forward's logits, host call to token (includes the synchronising copies).
