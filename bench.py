@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling small cases)")
     ap.add_argument("--batch", type=int, default=16, help="rows of the decode-batch measurement (0: skip)")
+    ap.add_argument("--long-prompt", type=int, default=4096,
+                    help="tokens of the long-prompt prefill on the Llama-3.2-1B architecture (BASELINE config 3; 0: skip)")
     ap.add_argument("--profile", choices=["none", "prefill", "batch", "decode"], default="none",
                     help="run one call of that kind inside a CUDA profiler range (for ncu --profile-from-start off) "
                          "on a --layers cut of the model, print nothing, exit")
@@ -441,6 +443,30 @@ def _main(args, out_fd):
                          "paged attention per row; device time of each call (host token ids in, argmax out)"}
         rb.close()
 
+    # ---- long-prompt prefill: Llama-3.2-1B architecture, one uniform-random prompt of
+    # --long-prompt tokens (chunks of up to 2,048), tensor-core GEMMs and attention; CUDA events around each call.
+    prefill_long = None
+    if args.long_prompt > 0 and n == 1:
+        lcfg = PRESETS["llama3.2-1b"]()
+        L = args.long_prompt
+        rl = vvli_b200.Runner(lcfg, max_seq=L + 32, device=local_rank)
+        rl.fill_synthetic(args.seed)
+        lprompt = np.random.default_rng(3).integers(0, lcfg.vocab_size, size=L).astype(np.uint32)
+        lms = []
+        for i in range(3):
+            rl.prefill(lprompt, 0, logits=False)
+            if i > 0:
+                lms.append(rl.last_forward_ms())
+        lms_med = float(np.median(lms))
+        lh, lkv, linter = lcfg.hidden_size, lcfg.kv_dim(), lcfg.intermediate_size
+        l_params = lh * lh + 2 * lkv * lh + lh * lh + 3 * linter * lh
+        l_flops = (2.0 * L * l_params * lcfg.num_hidden_layers +
+                   4 * lcfg.num_attention_heads * lcfg.head_dim() * lcfg.num_hidden_layers * L * (L + 1) / 2)
+        prefill_long = {"model": "llama3.2-1b", "tokens": L, "ms": lms_med, "tok_per_s": L / (lms_med / 1000.0),
+                        "algorithmic_tflops": l_flops / (lms_med / 1e3) / 1e12,
+                        "timing": "median of 2 calls after 1 warm-up call"}
+        rl.close()
+
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
         v, cores, sample = time_oracle(cfg, args.seed, args.cpu_seconds)
@@ -451,7 +477,7 @@ def _main(args, out_fd):
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, cfg, n),
                 "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "prefill": prefill, "sampler": sampler_line, "batch": batch,
+                "prefill": prefill, "prefill_long": prefill_long, "sampler": sampler_line, "batch": batch,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clk}
         emit(line, out_fd)
     runner.close()

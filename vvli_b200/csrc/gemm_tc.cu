@@ -38,7 +38,7 @@ struct TcLayout {
   static constexpr uint32_t tile_b = BN * kGemmBK * 2;
   static constexpr uint32_t stage = 2 * kTileA + tile_b;  // A_hi | A_lo | B
   static constexpr int stages = (192 * 1024) / stage;
-  static constexpr uint32_t tmem_cols = BN;
+  static constexpr uint32_t tmem_cols = 2 * BN;  // two accumulators: tile i + 1's MMAs run during tile i's epilogue
   static constexpr uint32_t idesc = umma_idesc(kGemmBM, BN);
   static constexpr size_t smem = static_cast<size_t>(stages) * stage + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -61,21 +61,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sm = smem_raw + (base - raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + kGemmStages * kStageBytes);
   uint64_t* empty = full + kGemmStages;
-  uint64_t* tmem_full = empty + kGemmStages;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  uint64_t* tmem_full = empty + kGemmStages;  // [2] an accumulator holds a finished tile
+  uint64_t* tmem_empty = tmem_full + 2;       // [2] the epilogue has read it
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr bool kPair = EPI == GE_SILU;
-  // Row tiles vary fastest: the CTAs of one weight tile run together and
-  // share its L2 lines, so each weight tile comes from HBM about once.
-  const int m0 = blockIdx.x * kGemmBM;
-  const int n0 = blockIdx.y * (kPair ? BN / 2 : BN);  // first output column of the tile
+  // Persistent: CTA b takes tiles b, b + grid, ...  Row tiles vary fastest,
+  // so the CTAs reading one weight tile run together and share its L2 lines
+  // (each weight tile comes from HBM about once).
+  const int mt = (p.M + kGemmBM - 1) / kGemmBM;
+  const int ntiles = mt * p.n_tiles;
+  auto tile_m0 = [&](int t) { return (t % mt) * kGemmBM; };
+  auto tile_n0 = [&](int t) { return (t / mt) * (kPair ? BN / 2 : BN); };  // first output column
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemmStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(tmem_full, 1);
+    mbar_init(&tmem_full[0], 1);
+    mbar_init(&tmem_full[1], 1);
+    mbar_init(&tmem_empty[0], 128);
+    mbar_init(&tmem_empty[1], 128);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -90,50 +97,66 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = *tmem_holder;
 
   if (warp == 0) {
-    if (lane == 0) {  // ---- TMA producer
+    if (lane == 0) {  // ---- TMA producer: every k-block of every tile of this CTA, one ring
       const uint32_t bytes = (p.two_a ? 2 * kTileA : kTileA) + kTileB;
-      const int rb0 = kPair ? n0 : n0;
-      const int rb1 = kPair ? p.pair_offset + n0 : n0 + BN / 2;
-      int issued = 0;
-      for (int kb = 0; kb < p.nk; ++kb) {
-        const int s = kb % kGemmStages;
-        if (kb >= kGemmStages && !mbar_wait(&empty[s], ((kb / kGemmStages) - 1) & 1, p.err)) break;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        const uint32_t st = base + s * kStageBytes;
-        const int x = kb * kGemmBK;
-        tma_load_2d(st, &tm_a_hi, x, m0, &full[s]);
-        if (p.two_a) tma_load_2d(st + kTileA, &tm_a_lo, x, m0, &full[s]);
-        tma_load_2d(st + 2 * kTileA, &tm_w, x, rb0, &full[s]);
-        if (BN == 256) tma_load_2d(st + 2 * kTileA + kTileB / 2, &tm_w, x, rb1, &full[s]);
-        issued = kb + 1;
+      int issued = 0;  // k-blocks issued over all tiles
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int m0 = tile_m0(t), n0 = tile_n0(t);
+        const int rb0 = n0;
+        const int rb1 = kPair ? p.pair_offset + n0 : n0 + BN / 2;
+        for (int kb = 0; kb < p.nk; ++kb, ++issued) {
+          const int s = issued % kGemmStages;
+          if (issued >= kGemmStages && !(ok = mbar_wait(&empty[s], ((issued / kGemmStages) - 1) & 1, p.err))) break;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          const uint32_t st = base + s * kStageBytes;
+          const int x = kb * kGemmBK;
+          tma_load_2d(st, &tm_a_hi, x, m0, &full[s]);
+          if (p.two_a) tma_load_2d(st + kTileA, &tm_a_lo, x, m0, &full[s]);
+          tma_load_2d(st + 2 * kTileA, &tm_w, x, rb0, &full[s]);
+          if (BN == 256) tma_load_2d(st + 2 * kTileA + kTileB / 2, &tm_w, x, rb1, &full[s]);
+        }
       }
       for (int i = issued > kGemmStages ? issued - kGemmStages : 0; i < issued; ++i)
         mbar_wait(&full[i % kGemmStages], (i / kGemmStages) & 1, p.err);
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // ---- MMA issuer
+    if (lane == 0) {  // ---- MMA issuer: tile i into accumulator i % 2
       bool ok = true;
-      for (int kb = 0; kb < p.nk && ok; ++kb) {
-        const int s = kb % kGemmStages;
-        if (!(ok = mbar_wait(&full[s], (kb / kGemmStages) & 1, p.err))) break;
+      int used = 0;  // k-blocks consumed over all tiles
+      int i = 0;     // tiles of this CTA
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        const uint32_t acc = tmem + static_cast<uint32_t>(buf * BN);
+        if (i >= 2 && !(ok = mbar_wait(&tmem_empty[buf], ((i >> 1) - 1) & 1, p.err))) break;
         tc_fence_after();
-        const uint32_t st = base + s * kStageBytes;
+        for (int kb = 0; kb < p.nk; ++kb, ++used) {
+          const int s = used % kGemmStages;
+          if (!(ok = mbar_wait(&full[s], (used / kGemmStages) & 1, p.err))) break;
+          tc_fence_after();
+          const uint32_t st = base + s * kStageBytes;
 #pragma unroll
-        for (int k = 0; k < kGemmBK / 16; ++k) {  // UMMA_K = 16 bf16 = 32 bytes
-          const uint64_t bdesc = umma_desc(st + 2 * kTileA + k * 32);
-          umma_bf16(tmem, umma_desc(st + k * 32), bdesc, kIdesc, (kb | k) != 0);
-          if (p.two_a) umma_bf16(tmem, umma_desc(st + kTileA + k * 32), bdesc, kIdesc, 1u);
+          for (int k = 0; k < kGemmBK / 16; ++k) {  // UMMA_K = 16 bf16 = 32 bytes
+            const uint64_t bdesc = umma_desc(st + 2 * kTileA + k * 32);
+            umma_bf16(acc, umma_desc(st + k * 32), bdesc, kIdesc, (kb | k) != 0);
+            if (p.two_a) umma_bf16(acc, umma_desc(st + kTileA + k * 32), bdesc, kIdesc, 1u);
+          }
+          umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
-        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        if (ok) umma_commit(&tmem_full[buf]);
       }
-      umma_commit(tmem_full);
     }
   } else {  // ---- epilogue: warps 2-5, TMEM lanes 32 * (warp % 4) ..
     const int wq = warp & 3;
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+    const int buf = i & 1;
+    const int m0 = tile_m0(t), n0 = tile_n0(t);
     const int row = m0 + wq * 32 + lane;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(buf * BN);
     // tcgen05.ld is warp-collective: the warp goes on only if every lane saw the accumulator.
-    if (__all_sync(0xffffffffu, mbar_wait(tmem_full, 0, p.err))) {
+    if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[buf], (i >> 1) & 1, p.err))) break;
+    {
       tc_fence_after();
       float v[32];
       if constexpr (EPI == GE_SILU) {
@@ -200,6 +223,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
+    tc_fence_before();  // this warp's TMEM loads of the tile come before the MMAs that reuse it
+    mbar_arrive(&tmem_empty[buf]);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -215,18 +241,28 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
   // Residual GEMMs (o_proj, down_proj: few output columns) take 128-wide tiles
   // when 256-wide ones would leave most SMs idle.
   const bool narrow = p.epi == GE_RESID && ((p.N + 255) / 256) * mt < 96;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  GemmParams q = p;
   if (narrow) {
-    const dim3 grid(mt, (p.N + 127) / 128);
-    gemm_tc_kernel<GE_RESID, 128><<<grid, kGemmThreads, TcLayout<128>::smem, s>>>(a_hi, a_lo, w, p);
+    q.n_tiles = (p.N + 127) / 128;
+    const int grid = std::min(mt * q.n_tiles, sms);  // persistent: one CTA per SM at most
+    gemm_tc_kernel<GE_RESID, 128><<<grid, kGemmThreads, TcLayout<128>::smem, s>>>(a_hi, a_lo, w, q);
     return cudaGetLastError();
   }
   const int cols = p.epi == GE_SILU ? 128 : 256;
-  const dim3 grid(mt, (p.N + cols - 1) / cols);
+  q.n_tiles = (p.N + cols - 1) / cols;
+  const int grid = std::min(mt * q.n_tiles, sms);
   constexpr size_t smem = TcLayout<256>::smem;
   switch (p.epi) {
-    case GE_QKV: gemm_tc_kernel<GE_QKV, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, p); break;
-    case GE_RESID: gemm_tc_kernel<GE_RESID, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, p); break;
-    default: gemm_tc_kernel<GE_SILU, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, p); break;
+    case GE_QKV: gemm_tc_kernel<GE_QKV, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, q); break;
+    case GE_RESID: gemm_tc_kernel<GE_RESID, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, q); break;
+    default: gemm_tc_kernel<GE_SILU, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, q); break;
   }
   return cudaGetLastError();
 }

@@ -17,6 +17,7 @@ constexpr int kGemmBK = 64;   // bf16 elements per k-block (one 128-byte swizzle
 
 struct GemmParams {
   int M, N, K;           // C[M, N] = A[M, K] . W[N, K]^T; N = columns produced (pair: per matrix)
+  int n_tiles;           // column tiles (set by launch_gemm_tc)
   int pair_offset;       // GE_SILU: row offset of the `up` rows in W (gate rows first)
   int nk;                // k-blocks = ceil(K / 64)
   int two_a;             // 1: A = A_hi + A_lo (two MMAs per k-step, near-fp32 activations)
