@@ -10,7 +10,8 @@
 //     each product is hi.hi + hi.lo + lo.hi: three kind::f16 MMAs into one
 //     fp32 accumulator in TMEM (the dropped lo.lo term is below fp32
 //     rounding of the sum).
-//   * S = Q K^T (128 x 64) lands in TMEM; each of the 128 softmax threads owns
+//   * S = Q K^T (128 x 64) lands in TMEM (two buffers: S of tile j + 2 is
+//     computed while the softmax works on tile j + 1); each of the 128 softmax threads owns
 //     one query row (one TMEM lane), so the online softmax (scale, causal
 //     mask, running max and sum) needs no shuffles.  P (hi / lo) goes to
 //     shared memory as the A operand of P V, which accumulates O (128 x d) in
@@ -61,9 +62,10 @@ struct AtLayout {
   static constexpr uint32_t q_hi = 0, q_lo = q_tile;
   static constexpr uint32_t kv0 = 2 * q_tile;                 // two K / V buffers (tile j uses j % 2)
   static constexpr uint32_t p_hi = kv0 + 2 * kv_buf, p_lo = p_hi + p_tile;
-  static constexpr uint32_t bars = p_lo + p_tile;             // 7 mbarriers + TMEM address
+  static constexpr uint32_t bars = p_lo + p_tile;             // 8 mbarriers + TMEM address
   static constexpr uint32_t smem = bars + 128 + 1024;         // + alignment slack
-  static constexpr uint32_t tmem_cols = 64 + D <= 128 ? 128 : 256;  // S at column 0, O at column 64
+  static constexpr uint32_t o_col = 128;                      // S of even / odd tiles at columns 0 / 64, O at 128
+  static constexpr uint32_t tmem_cols = 256;
   static constexpr uint32_t s_idesc = umma_idesc(kAtRows, kAtKeys);
   static constexpr uint32_t pv_idesc = umma_idesc(kAtRows, D);
 };
@@ -146,10 +148,10 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
   uint8_t* sm = at_raw + (base - raw);
   uint64_t* kv_full = reinterpret_cast<uint64_t*>(sm + L::bars);  // [2] converters wrote K / V (and Q)
   uint64_t* kv_empty = kv_full + 2;                                 // [2] the MMAs that read a buffer are done
-  uint64_t* s_full = kv_full + 4;                                   // S = Q K^T is in TMEM
-  uint64_t* p_ready = kv_full + 5;                                  // softmax wrote P (and rescaled O)
-  uint64_t* pv_full = kv_full + 6;                                  // O += P V is done
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(kv_full + 7);
+  uint64_t* s_full = kv_full + 4;                                   // [2] S = Q K^T of an even / odd tile is in TMEM
+  uint64_t* p_ready = kv_full + 6;                                  // softmax wrote P (and rescaled O)
+  uint64_t* pv_full = kv_full + 7;                                  // O += P V is done
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(kv_full + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.group, g = blockIdx.x;
   const int BQ = kAtRows / G;
@@ -165,7 +167,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
     mbar_init(&kv_full[1], kAtConv);
     mbar_init(&kv_empty[0], 1);
     mbar_init(&kv_empty[1], 1);
-    mbar_init(s_full, 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
     mbar_init(p_ready, kAtSoftmax);
     mbar_init(pv_full, 1);
     fence_barrier_init();
@@ -183,38 +186,65 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
 
   if (warp == 8) {
     if (lane == 0) {  // ---- MMA issuer
-      int done = 0;   // tiles whose MMAs were all issued
-      for (int j = 0; j < ntiles; ++j) {
-        const uint8_t* kvb = sm + L::kv0 + (j & 1) * L::kv_buf;
-        const uint32_t kva = base + L::kv0 + (j & 1) * L::kv_buf;
-        (void)kvb;
-        if (!mbar_wait(&kv_full[j & 1], (j >> 1) & 1, p.err)) break;
+      // The start address is the descriptor's low field (address >> 4, smem < 256 KB):
+      // an operand at base + off has descriptor desc(base) + (off >> 4).
+      const uint64_t dq_hi = umma_desc(base + L::q_hi), dq_lo = umma_desc(base + L::q_lo);
+      const uint64_t dp_hi = umma_desc(base + L::p_hi), dp_lo = umma_desc(base + L::p_lo);
+      const uint64_t dkv0 = umma_desc(base + L::kv0);
+      // S of tile j into columns 64 (j % 2).  The thread issues whichever is
+      // ready first: P V of the next tile once its P is written, or S of a
+      // later tile once its K / V are in and its S buffer has been read (the
+      // P V of the tile two before was issued), so neither waits on the other.
+      auto issue_s = [&](int j) {
         tc_fence_after();
+        const uint32_t kvo = (j & 1) * L::kv_buf;  // this tile's K / V buffer, from kv0
+        const uint32_t sacc = tmem + static_cast<uint32_t>((j & 1) * 64);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {  // S = Q K^T over d, 16 per MMA
           const uint32_t ka = (ks >> 2) * (kAtRows * 128) + (ks & 3) * 32;
           const uint32_t kb = (ks >> 2) * (kAtKeys * 128) + (ks & 3) * 32;
-          const uint64_t qh = umma_desc(base + L::q_hi + ka), ql = umma_desc(base + L::q_lo + ka);
-          const uint64_t kh = umma_desc(kva + L::k_hi + kb), kl = umma_desc(kva + L::k_lo + kb);
-          umma_bf16(tmem, qh, kh, L::s_idesc, ks != 0);
-          umma_bf16(tmem, qh, kl, L::s_idesc, 1u);
-          umma_bf16(tmem, ql, kh, L::s_idesc, 1u);
+          const uint64_t qh = dq_hi + (ka >> 4), ql = dq_lo + (ka >> 4);
+          const uint64_t kh = dkv0 + ((kvo + L::k_hi + kb) >> 4), kl = dkv0 + ((kvo + L::k_lo + kb) >> 4);
+          umma_bf16(sacc, qh, kh, L::s_idesc, ks != 0);
+          umma_bf16(sacc, qh, kl, L::s_idesc, 1u);
+          umma_bf16(sacc, ql, kh, L::s_idesc, 1u);
         }
-        umma_commit(s_full);
-        if (!mbar_wait(p_ready, j & 1, p.err)) break;
+        umma_commit(&s_full[j & 1]);
+      };
+      auto issue_pv = [&](int j) {
         tc_fence_after();
+        const uint32_t kvo = (j & 1) * L::kv_buf;
 #pragma unroll
         for (int ks = 0; ks < kAtKeys / 16; ++ks) {  // O += P V over the tile's keys
-          const uint64_t ph = umma_desc(base + L::p_hi + ks * 32), pl = umma_desc(base + L::p_lo + ks * 32);
-          const uint64_t vh = umma_desc(kva + L::v_hi + ks * 32), vl = umma_desc(kva + L::v_lo + ks * 32);
-          umma_bf16(tmem + 64, ph, vh, L::pv_idesc, (j | ks) != 0);
-          umma_bf16(tmem + 64, ph, vl, L::pv_idesc, 1u);
-          umma_bf16(tmem + 64, pl, vh, L::pv_idesc, 1u);
+          const uint64_t ph = dp_hi + (ks * 32 >> 4), pl = dp_lo + (ks * 32 >> 4);
+          const uint64_t vh = dkv0 + ((kvo + L::v_hi + ks * 32) >> 4), vl = dkv0 + ((kvo + L::v_lo + ks * 32) >> 4);
+          umma_bf16(tmem + L::o_col, ph, vh, L::pv_idesc, (j | ks) != 0);
+          umma_bf16(tmem + L::o_col, ph, vl, L::pv_idesc, 1u);
+          umma_bf16(tmem + L::o_col, pl, vh, L::pv_idesc, 1u);
         }
         umma_commit(pv_full);
         umma_commit(&kv_empty[j & 1]);
-        done = j + 1;
+      };
+      int ns = 0, npv = 0;  // tiles whose S / P V MMAs were issued
+      uint64_t t0 = 0;
+      while (npv < ntiles) {
+        if (ns < ntiles && ns <= npv + 1 && mbar_try_wait(&kv_full[ns & 1], (ns >> 1) & 1)) {
+          issue_s(ns++);
+          t0 = 0;
+        } else if (npv < ns && mbar_try_wait(p_ready, npv & 1)) {
+          issue_pv(npv++);
+          t0 = 0;
+        } else {
+          const uint64_t now = global_timer_ns();
+          if (t0 == 0) {
+            t0 = now;
+          } else if (now - t0 > kWaitLimitNs) {
+            if (p.err) atomicExch(p.err, kErrTimeout);
+            break;
+          }
+        }
       }
+      const int done = npv;
       // Every MMA has finished before TMEM is released (already so unless a wait gave up).
       if (done > 0) mbar_wait(&kv_empty[(done - 1) & 1], ((done - 1) >> 1) & 1, p.err);
     }
@@ -276,11 +306,11 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
     for (int j = 0; j < ntiles; ++j) {
       const int j0 = j * kAtKeys;
       const int nkeys = min(kAtKeys, last_pos + 1 - j0);
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, p.err)))) break;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.err)))) break;
       tc_fence_after();
       float s[kAtKeys];
-      tmem_ld32(trow, s);
-      tmem_ld32(trow + 32, s + 32);
+      tmem_ld32(trow + (j & 1) * 64, s);
+      tmem_ld32(trow + (j & 1) * 64 + 32, s + 32);
       float mt = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kAtKeys; ++c) {
@@ -289,7 +319,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
       }
       const bool move = mt > m + kAtRescale;  // false while the row has no key yet (mt = -inf)
       const float mnew = move ? mt : m;
-      const float alpha = move ? (m == -INFINITY ? 0.f : expf(m - mnew)) : 1.f;
+      const float alpha = move ? (m == -INFINITY ? 0.f : __expf(m - mnew)) : 1.f;
       // P is free and O complete once the last tile's P V is done
       if (j > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(pv_full, (j - 1) & 1, p.err)))) break;
       tc_fence_after();
@@ -297,10 +327,10 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
 #pragma unroll 1
         for (int cc = 0; cc < D / 32; ++cc) {
           float v[32];
-          tmem_ld32(trow + 64 + cc * 32, v);
+          tmem_ld32(trow + L::o_col + cc * 32, v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st32(trow + 64 + cc * 32, v);
+          tmem_st32(trow + L::o_col + cc * 32, v);
         }
       }
       float sum = 0.f;
@@ -309,7 +339,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
         float pv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          pv[i] = mnew == -INFINITY ? 0.f : expf(s[8 * c8 + i] - mnew);
+          pv[i] = mnew == -INFINITY ? 0.f : __expf(s[8 * c8 + i] - mnew);
           sum += pv[i];
         }
         uint4 hi, lo;
@@ -331,7 +361,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float v[32];
-        tmem_ld32(trow + 64 + cc * 32, v);
+        tmem_ld32(trow + L::o_col + cc * 32, v);
         if (R < rows) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) split_bf16(v[i] * inv, p.out_hi[orow + cc * 32 + i], p.out_lo[orow + cc * 32 + i]);
