@@ -21,11 +21,15 @@
 //     the 16-byte chunk c of row r stored at chunk c ^ (r % 8), 8-row groups
 //     of 1024 bytes), K-major: Q and K by rows, V transposed (d rows of 64
 //     keys) so it is the K-major B operand of P V.
+//   * A pre-pass (kv_tiles_kernel) writes every 64-position tile of the
+//     layer's K and V, once, as the hi / lo image of a shared-memory K / V
+//     buffer; an attention CTA fetches each tile with one bulk copy into a
+//     double buffer, so the many query blocks that read a tile do not
+//     convert it again.
 //   * Warps 0-3 (TMEM lanes 32 w ..) run the softmax and write the output;
-//     warps 4-7 convert Q, K and V into shared memory, K / V double-buffered
-//     so tile j + 1 is converted while tile j is in the softmax; warp 8
-//     allocates TMEM and one of its threads issues the MMAs.  Every wait is
-//     bounded.
+//     warps 4-7 convert Q, then one of their threads copies the K / V tiles;
+//     warp 8 allocates TMEM and one of its threads issues the MMAs.  Every
+//     wait is bounded.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -62,7 +66,7 @@ struct AtLayout {
   static constexpr uint32_t q_hi = 0, q_lo = q_tile;
   static constexpr uint32_t kv0 = 2 * q_tile;                 // two K / V buffers (tile j uses j % 2)
   static constexpr uint32_t p_hi = kv0 + 2 * kv_buf, p_lo = p_hi + p_tile;
-  static constexpr uint32_t bars = p_lo + p_tile;             // 8 mbarriers + TMEM address
+  static constexpr uint32_t bars = p_lo + p_tile;             // 9 mbarriers + TMEM address
   static constexpr uint32_t smem = bars + 128 + 1024;         // + alignment slack
   static constexpr uint32_t o_col = 128;                      // S of even / odd tiles at columns 0 / 64, O at 128
   static constexpr uint32_t tmem_cols = 256;
@@ -139,6 +143,57 @@ VVLI_DEV void convert_rows(Src src, int nrows_valid, int tile_rows, uint8_t* hi,
   }
 }
 
+// One tile (64 positions) of kv head g of a layer's K and V into the image of
+// a shared-memory K / V buffer (K hi, K lo by rows; V^T hi, V^T lo), rows past
+// nkeys zero.  128 threads.
+template <int D>
+VVLI_DEV void convert_kv_tile(const float* k_tile, const float* v_tile, int nkeys, uint8_t* kvb, int ct) {
+  using L = AtLayout<D>;
+  // K by rows
+  convert_rows<D, D / 16>(
+      [&](int r, int c) { return reinterpret_cast<const float4*>(k_tile + static_cast<size_t>(r) * D + c * 8); },
+      nkeys, kAtKeys, kvb + L::k_hi, kvb + L::k_lo, ct);
+  // V transposed: item (dims 8eb.., keys 8jc..) -> 8 chunks, one per dim
+  if (ct < D) {
+    // the 8 threads of a key chunk group write one row's 8 chunks (no bank conflicts in shared memory)
+    const int jc = ct % 8, eb = ct / 8;
+    float t[8][8];
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      const int key = 8 * jc + jj;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      if (key < nkeys) {
+        const float4* src = reinterpret_cast<const float4*>(v_tile + static_cast<size_t>(key) * D + eb * 8);
+        a = __ldcg(src), b = __ldcg(src + 1);
+      }
+      t[0][jj] = a.x, t[1][jj] = a.y, t[2][jj] = a.z, t[3][jj] = a.w;
+      t[4][jj] = b.x, t[5][jj] = b.y, t[6][jj] = b.z, t[7][jj] = b.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      uint4 hi, lo;
+      split8(t[e], hi, lo);
+      const uint32_t off = sw_chunk(D, 8 * eb + e, jc);
+      *reinterpret_cast<uint4*>(kvb + L::v_hi + off) = hi;
+      *reinterpret_cast<uint4*>(kvb + L::v_lo + off) = lo;
+    }
+  }
+}
+
+// Pre-pass: every tile (64 positions) of positions [0, npos) of every kv head
+// as the hi / lo image of a K / V buffer, tiles[(tile * nkv + g)], so the
+// attention CTAs (many per tile) copy them instead of converting them again.
+template <int D>
+__global__ void __launch_bounds__(kAtConv) kv_tiles_kernel(const float* k_cache, const float* v_cache,
+                                                           const int* page_table, int npos, int nkv, uint8_t* tiles) {
+  using L = AtLayout<D>;
+  const int j = blockIdx.x, g = blockIdx.y;
+  const int nkeys = min(kAtKeys, npos - j * kAtKeys);
+  const size_t tb = kv_off(page_table, j * kAtKeys, g, nkv, D);  // the tile's rows are contiguous
+  convert_kv_tile<D>(k_cache + tb, v_cache + tb, nkeys, tiles + (static_cast<size_t>(j) * nkv + g) * L::kv_buf,
+                     threadIdx.x);
+}
+
 template <int D>
 __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const PrefillAttnParams p) {
   using L = AtLayout<D>;
@@ -151,7 +206,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
   uint64_t* s_full = kv_full + 4;                                   // [2] S = Q K^T of an even / odd tile is in TMEM
   uint64_t* p_ready = kv_full + 6;                                  // softmax wrote P (and rescaled O)
   uint64_t* pv_full = kv_full + 7;                                  // O += P V is done
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(kv_full + 8);
+  uint64_t* q_ready = kv_full + 8;                                  // converters wrote Q
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(kv_full + 9);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.group, g = blockIdx.x;
   const int BQ = kAtRows / G;
@@ -163,8 +219,9 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
   const int qd = p.nq * D;
 
   if (threadIdx.x == 0) {
-    mbar_init(&kv_full[0], kAtConv);
-    mbar_init(&kv_full[1], kAtConv);
+    mbar_init(&kv_full[0], 1);  // the K / V copy: one arrival with its byte count
+    mbar_init(&kv_full[1], 1);
+    mbar_init(q_ready, kAtConv);
     mbar_init(&kv_empty[0], 1);
     mbar_init(&kv_empty[1], 1);
     mbar_init(&s_full[0], 1);
@@ -227,6 +284,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
       };
       int ns = 0, npv = 0;  // tiles whose S / P V MMAs were issued
       uint64_t t0 = 0;
+      if (!mbar_wait(q_ready, 0, p.err)) npv = ntiles;  // nothing to do
       while (npv < ntiles) {
         if (ns < ntiles && ns <= npv + 1 && mbar_try_wait(&kv_full[ns & 1], (ns >> 1) & 1)) {
           issue_s(ns++);
@@ -259,43 +317,15 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
     for (int h = 0; h < D / 64; ++h)  // D / 8 items per thread, 8 at a time
       convert_rows<D, 8>([&](int r, int c) { return qsrc(r, c); }, rows, kAtRows, sm + L::q_hi, sm + L::q_lo,
                          ct + h * 8 * kAtConv);
-    for (int j = 0; j < ntiles; ++j) {
-      const int j0 = j * kAtKeys;
-      const int nkeys = min(kAtKeys, last_pos + 1 - j0);
-      uint8_t* kvb = sm + L::kv0 + (j & 1) * L::kv_buf;
-      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&kv_empty[j & 1], ((j >> 1) - 1) & 1, p.err))) break;
-      const size_t tb = kv_off(p.page_table, j0, g, p.nkv, D);  // the tile's rows are contiguous
-      // K by rows (zero past nkeys)
-      convert_rows<D, D / 16>(
-          [&](int r, int c) { return reinterpret_cast<const float4*>(p.k_cache + tb + static_cast<size_t>(r) * D + c * 8); },
-          nkeys, kAtKeys, kvb + L::k_hi, kvb + L::k_lo, ct);
-      // V transposed: item (dims 8eb.., keys 8jc..) -> 8 chunks, one per dim (zero past nkeys)
-      if (ct < D) {
-        // the 8 lanes of a key chunk group write one row's 8 chunks (no bank conflicts)
-        const int jc = ct % 8, eb = ct / 8;
-        float t[8][8];
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const int key = 8 * jc + jj;
-          float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-          if (key < nkeys) {
-            const float4* src = reinterpret_cast<const float4*>(p.v_cache + tb + static_cast<size_t>(key) * D + eb * 8);
-            a = __ldcg(src), b = __ldcg(src + 1);
-          }
-          t[0][jj] = a.x, t[1][jj] = a.y, t[2][jj] = a.z, t[3][jj] = a.w;
-          t[4][jj] = b.x, t[5][jj] = b.y, t[6][jj] = b.z, t[7][jj] = b.w;
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          uint4 hi, lo;
-          split8(t[e], hi, lo);
-          const uint32_t off = sw_chunk(D, 8 * eb + e, jc);
-          *reinterpret_cast<uint4*>(kvb + L::v_hi + off) = hi;
-          *reinterpret_cast<uint4*>(kvb + L::v_lo + off) = lo;
-        }
+    fence_async_smem();  // generic-proxy writes, read by the tensor cores
+    mbar_arrive(q_ready);
+    if (ct == 0) {  // the K / V tile images of the pre-pass, one bulk copy per tile
+      for (int j = 0; j < ntiles; ++j) {
+        if (j >= 2 && !mbar_wait(&kv_empty[j & 1], ((j >> 1) - 1) & 1, p.err)) break;
+        mbar_arrive_expect_tx(&kv_full[j & 1], L::kv_buf);
+        bulk_g2s(sm + L::kv0 + (j & 1) * L::kv_buf, p.kv_tiles + (static_cast<size_t>(j) * p.nkv + g) * L::kv_buf,
+                 L::kv_buf, &kv_full[j & 1]);
       }
-      fence_async_smem();  // generic-proxy writes, read by the tensor cores
-      mbar_arrive(&kv_full[j & 1]);
     }
   } else {  // ---- softmax: row R = TMEM lane (softmaxInPlace, src/llm.zig:1408-1419, online form)
     const int R = threadIdx.x;
@@ -379,6 +409,9 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
 
 template <int D>
 cudaError_t launch_at(const PrefillAttnParams& p, cudaStream_t s) {
+  const int npos = p.pos0 + p.M;
+  const dim3 tgrid((npos + kAtKeys - 1) / kAtKeys, p.nkv);
+  kv_tiles_kernel<D><<<tgrid, kAtConv, 0, s>>>(p.k_cache, p.v_cache, p.page_table, npos, p.nkv, p.kv_tiles);
   const int BQ = kAtRows / p.group;
   const dim3 grid(p.nkv, (p.M + BQ - 1) / BQ);
   cudaError_t e = cudaFuncSetAttribute(prefill_attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -436,7 +469,13 @@ cudaError_t attention_tc_selftest(int d, int group, int M, int pos0, uint64_t se
   fill_f32_kernel<<<256, 256>>>(q, qn, seed * 5 + 1, 2.0f);
   fill_f32_kernel<<<256, 256>>>(kc, kvn, seed * 5 + 2, 2.0f);
   fill_f32_kernel<<<256, 256>>>(vc, kvn, seed * 5 + 3, 1.0f);
-  PrefillAttnParams a{q, kc, vc, pt, outs, outs + qn, M, nq, nkv, d, group, pos0, 1.0f / sqrtf(static_cast<float>(d)), err};
+  uint8_t* ws = nullptr;
+  if ((e = cudaMalloc(&ws, prefill_attention_tc_workspace(d, nkv, total)))) {
+    cleanup();
+    return e;
+  }
+  PrefillAttnParams a{q, kc, vc, pt, outs, outs + qn, M, nq, nkv, d, group, pos0, 1.0f / sqrtf(static_cast<float>(d)), err,
+                      ws};
   PrefillAttnParams b = a;
   b.out_hi = outs + 2 * qn, b.out_lo = outs + 3 * qn;
   if ((e = launch_prefill_attention_simt(a, 0)) || (e = launch_prefill_attention_tc(b, 0))) {
@@ -444,6 +483,7 @@ cudaError_t attention_tc_selftest(int d, int group, int M, int pos0, uint64_t se
     return e;
   }
   compare_pairs_kernel<<<256, 256>>>(b.out_hi, b.out_lo, a.out_hi, a.out_lo, qn, res);
+  cudaFree(ws);
   float h[2] = {0.f, 0.f};
   int herr = 0;
   e = cudaMemcpy(h, res, 8, cudaMemcpyDeviceToHost);
@@ -454,10 +494,15 @@ cudaError_t attention_tc_selftest(int d, int group, int M, int pos0, uint64_t se
   return cudaSuccess;
 }
 
+size_t prefill_attention_tc_workspace(int d, int nkv, int max_pos) {
+  const size_t tiles = (static_cast<size_t>(max_pos) + kAtKeys - 1) / kAtKeys;
+  return tiles * nkv * (d == 128 ? AtLayout<128>::kv_buf : AtLayout<64>::kv_buf);
+}
+
 bool prefill_attention_tc_supported(int d, int group) { return (d == 64 || d == 128) && group >= 1 && group <= 8; }
 
 cudaError_t launch_prefill_attention_tc(const PrefillAttnParams& p, cudaStream_t s) {
-  if (!prefill_attention_tc_supported(p.d, p.group)) return cudaErrorInvalidValue;
+  if (!prefill_attention_tc_supported(p.d, p.group) || !p.kv_tiles) return cudaErrorInvalidValue;
   return p.d == 128 ? launch_at<128>(p, s) : launch_at<64>(p, s);
 }
 

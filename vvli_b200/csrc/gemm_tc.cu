@@ -660,7 +660,7 @@ static cudaError_t launch_pa(const PrefillAttnParams& p, cudaStream_t s) {
 
 cudaError_t launch_prefill_attention(const PrefillAttnParams& p, cudaStream_t s) {
   static const bool tc = !(getenv("VVLI_ATTN_TC") && getenv("VVLI_ATTN_TC")[0] == '0');
-  if (tc && prefill_attention_tc_supported(p.d, p.group)) return launch_prefill_attention_tc(p, s);
+  if (tc && p.kv_tiles && prefill_attention_tc_supported(p.d, p.group)) return launch_prefill_attention_tc(p, s);
   return launch_prefill_attention_simt(p, s);
 }
 

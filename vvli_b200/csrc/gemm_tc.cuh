@@ -78,7 +78,9 @@ struct PrefillAttnParams {
   int M, nq, nkv, d, group, pos0;
   float inv_sqrt_d;
   int* err;              // VVLI_ERR_TIMEOUT when a bounded wait gives up (may be null)
+  uint8_t* kv_tiles;     // tensor-core kernel's workspace: prefill_attention_tc_workspace bytes
 };
+size_t prefill_attention_tc_workspace(int d, int nkv, int max_pos);
 // Tensor-core kernel when it takes the shape (and VVLI_ATTN_TC is not 0), else the SIMT kernels.
 cudaError_t launch_prefill_attention(const PrefillAttnParams& p, cudaStream_t s);
 cudaError_t launch_prefill_attention_simt(const PrefillAttnParams& p, cudaStream_t s);

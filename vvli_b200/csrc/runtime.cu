@@ -209,6 +209,7 @@ struct vvli_ctx {
   float *pf_x = nullptr, *pf_q = nullptr;
   uint16_t *pf_ahi = nullptr, *pf_alo = nullptr, *pf_fhi = nullptr, *pf_flo = nullptr;
   int* pf_tokens = nullptr;
+  uint8_t* pf_kvt = nullptr;  // tensor-core attention: hi / lo images of the layer's K / V tiles
   CUtensorMap tm_ah_hi{}, tm_ah_lo{}, tm_aq_hi{}, tm_aq_lo{}, tm_f_hi{}, tm_f_lo{};
   std::vector<CUtensorMap> tm_w;  // per layer: q|k|v, o, gate|up, down
   // decode batches (allocated on first use): chunks of up to kSkinnyMaxRows rows
@@ -694,7 +695,9 @@ int ensure_prefill_buffers(vvli_ctx* c) {
   if ((st = dalloc(&c->pf_x, static_cast<size_t>(cap) * c->h)) || (st = dalloc(&c->pf_q, static_cast<size_t>(cap) * c->q_rows)) ||
       (st = dalloc(&c->pf_ahi, cap * ka)) || (st = dalloc(&c->pf_alo, cap * ka)) ||
       (st = dalloc(&c->pf_fhi, static_cast<size_t>(cap) * c->I_l)) ||
-      (st = dalloc(&c->pf_flo, static_cast<size_t>(cap) * c->I_l)) || (st = dalloc(&c->pf_tokens, cap)))
+      (st = dalloc(&c->pf_flo, static_cast<size_t>(cap) * c->I_l)) || (st = dalloc(&c->pf_tokens, cap)) ||
+      (prefill_attention_tc_supported(c->d, c->group) &&
+       (st = dalloc(&c->pf_kvt, prefill_attention_tc_workspace(c->d, c->nkv_l, static_cast<int>(c->max_seq))))))
     return st;
   cudaError_t e;
   if ((e = make_tmap_bf16(&c->tm_ah_hi, c->pf_ahi, cap, c->h, 128)) ||
@@ -741,7 +744,7 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start) 
       g.nk = (g.K + kGemmBK - 1) / kGemmBK;
       CK(launch_gemm_tc(c->tm_ah_hi, c->tm_ah_lo, c->tm_w[4 * l + 0], g, s));
       PrefillAttnParams a{c->pf_q, kc, vc, c->page_table, c->pf_ahi, c->pf_alo, M, c->nq_l, c->nkv_l, c->d,
-                          c->group, pos0, 1.0f / sqrtf(static_cast<float>(c->d)), err};
+                          c->group, pos0, 1.0f / sqrtf(static_cast<float>(c->d)), err, c->pf_kvt};
       CK(launch_prefill_attention(a, s));
       GemmParams o{};
       o.M = M, o.two_a = 1, o.err = err, o.N = c->h, o.K = c->q_rows, o.epi = GE_RESID, o.y = c->pf_x, o.ldy = c->h;
@@ -1000,7 +1003,7 @@ void free_ctx(vvli_ctx* c) {
   void* dev[] = {c->w, c->kv, c->page_table, c->x, c->qkv, c->attn, c->ff, c->logits, c->logits_full, c->emb_in,
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
                  c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->w_downT, c->acc, c->pf_x, c->pf_q,
-                 c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->smp_stamp, c->smp_key32,
+                 c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->pf_kvt, c->smp_stamp, c->smp_key32,
                  c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_recent, c->smp_state, c->smp_temp,
                  c->bt_x, c->bt_q, c->bt_logits, c->bt_best, c->bt_all_best, c->bt_part, c->bt_logits_all, c->bt_ahi,
                  c->bt_alo, c->bt_fhi, c->bt_flo, c->bt_tokens, c->bt_pos, c->bt_idx, c->bt_counters};
