@@ -11,9 +11,9 @@
 //     fp32 accumulator in TMEM (the dropped lo.lo term is below fp32
 //     rounding of the sum).
 //   * S = Q K^T (128 x 64) lands in TMEM (two buffers: S of tile j + 2 is
-//     computed while the softmax works on tile j + 1); each of the 128 softmax threads owns
-//     one query row (one TMEM lane), so the online softmax (scale, causal
-//     mask, running max and sum) needs no shuffles.  P (hi / lo) goes to
+//     computed while the softmax works on tile j + 1); two softmax threads
+//     own one query row (one TMEM lane), 32 key columns each, so the online
+//     softmax (scale, causal mask, running max and sum) needs no shuffles.  P (hi / lo) goes to
 //     shared memory as the A operand of P V, which accumulates O (128 x d) in
 //     TMEM; when a row's max moves, its O is rescaled in TMEM first.
 //   * Operands are written to shared memory by the worker threads in the
@@ -26,10 +26,11 @@
 //     buffer; an attention CTA fetches each tile with one bulk copy into a
 //     double buffer, so the many query blocks that read a tile do not
 //     convert it again.
-//   * Warps 0-3 (TMEM lanes 32 w ..) run the softmax and write the output;
-//     warps 4-7 convert Q, then one of their threads copies the K / V tiles;
-//     warp 8 allocates TMEM and one of its threads issues the MMAs.  Every
-//     wait is bounded.
+//   * Warps 0-7 convert Q, then run the softmax and write the output: warp w
+//     takes TMEM lanes 32 (w % 4) .. and key columns 32 (w / 4) .., the two
+//     halves of a row meeting once per tile for the row max; warp 8
+//     allocates TMEM and one of its threads issues the K / V copies and the
+//     MMAs, whichever is ready first.  Every wait is bounded.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -47,9 +48,9 @@ namespace {
 
 constexpr int kAtRows = 128;        // query rows per CTA: M of every MMA, TMEM lanes
 constexpr int kAtKeys = 64;         // keys per tile: one KV page
-constexpr int kAtSoftmax = 128;     // warps 0-3: one query row (TMEM lane) per thread
-constexpr int kAtConv = 128;        // warps 4-7: Q, K and V into shared memory
-constexpr int kAtThreads = kAtSoftmax + kAtConv + 32;  // warp 8: TMEM and the MMAs
+constexpr int kAtSoftmax = 256;     // warps 0-7: row 32 (w % 4) + lane, key columns 32 (w / 4) ..
+constexpr int kAtConv = 128;        // threads of the K / V pre-pass
+constexpr int kAtThreads = kAtSoftmax + 32;  // warp 8: TMEM, the K / V copies and the MMAs
 // A row's reference max moves only when a score exceeds it by more than
 // this (natural log): exp(s - m) then stays below e^8, so the output in TMEM
 // is rescaled rarely; the result is the same up to fp32 rounding.
@@ -221,7 +222,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
   if (threadIdx.x == 0) {
     mbar_init(&kv_full[0], 1);  // the K / V copy: one arrival with its byte count
     mbar_init(&kv_full[1], 1);
-    mbar_init(q_ready, kAtConv);
+    mbar_init(q_ready, kAtSoftmax);
     mbar_init(&kv_empty[0], 1);
     mbar_init(&kv_empty[1], 1);
     mbar_init(&s_full[0], 1);
@@ -282,15 +283,31 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
         umma_commit(pv_full);
         umma_commit(&kv_empty[j & 1]);
       };
-      int ns = 0, npv = 0;  // tiles whose S / P V MMAs were issued
+      // The K / V tile images of the pre-pass, one bulk copy per tile into the
+      // double buffer, as soon as the P V of the tile two before has read it.
+      auto issue_copy = [&](int j) {
+        mbar_arrive_expect_tx(&kv_full[j & 1], L::kv_buf);
+        bulk_g2s(sm + L::kv0 + (j & 1) * L::kv_buf, p.kv_tiles + (static_cast<size_t>(j) * p.nkv + g) * L::kv_buf,
+                 L::kv_buf, &kv_full[j & 1]);
+      };
+      int nc = 0, ns = 0, npv = 0;  // tiles copied / whose S / P V MMAs were issued
+      bool qok = false;
       uint64_t t0 = 0;
-      if (!mbar_wait(q_ready, 0, p.err)) npv = ntiles;  // nothing to do
       while (npv < ntiles) {
-        if (ns < ntiles && ns <= npv + 1 && mbar_try_wait(&kv_full[ns & 1], (ns >> 1) & 1)) {
+        bool moved = false;
+        if (nc < ntiles && (nc < 2 || mbar_try_wait(&kv_empty[nc & 1], ((nc >> 1) - 1) & 1))) {
+          issue_copy(nc++);
+          moved = true;
+        }
+        if (!qok) qok = mbar_try_wait(q_ready, 0);
+        if (qok && ns < nc && ns <= npv + 1 && mbar_try_wait(&kv_full[ns & 1], (ns >> 1) & 1)) {
           issue_s(ns++);
-          t0 = 0;
+          moved = true;
         } else if (npv < ns && mbar_try_wait(p_ready, npv & 1)) {
           issue_pv(npv++);
+          moved = true;
+        }
+        if (moved) {
           t0 = 0;
         } else {
           const uint64_t now = global_timer_ns();
@@ -306,66 +323,78 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
       // Every MMA has finished before TMEM is released (already so unless a wait gave up).
       if (done > 0) mbar_wait(&kv_empty[(done - 1) & 1], ((done - 1) >> 1) & 1, p.err);
     }
-  } else if (warp >= 4) {  // ---- converters
-    const int ct = threadIdx.x - kAtSoftmax;
-    // Q (hi / lo), zero rows past `rows`
-    auto qsrc = [&](int r, int c) {
-      return reinterpret_cast<const float4*>(p.q + static_cast<size_t>(t0 + r / G) * qd +
-                                             static_cast<size_t>(g * G + r % G) * D + c * 8);
-    };
+  } else {  // ---- softmax: row R = TMEM lane, key columns 32 h .. (softmaxInPlace, src/llm.zig:1408-1419, online form)
+    __shared__ float xrow[2][kAtRows];  // the two halves' row max, then their row sums
+    const int st = threadIdx.x;         // 0 .. 255
+    const int h = warp >> 2;            // half of the key columns (and of the output dims)
+    const int R = 32 * (warp & 3) + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+    const int qpos = R < rows ? p.pos0 + t0 + R / G : -1;
+    // Q (hi / lo) by all softmax threads, zero rows past `rows`
+    for (int it0 = 0; it0 < kAtRows * (D / 8); it0 += 8 * kAtSoftmax) {
+      float4 a[8][2];
 #pragma unroll
-    for (int h = 0; h < D / 64; ++h)  // D / 8 items per thread, 8 at a time
-      convert_rows<D, 8>([&](int r, int c) { return qsrc(r, c); }, rows, kAtRows, sm + L::q_hi, sm + L::q_lo,
-                         ct + h * 8 * kAtConv);
-    fence_async_smem();  // generic-proxy writes, read by the tensor cores
-    mbar_arrive(q_ready);
-    if (ct == 0) {  // the K / V tile images of the pre-pass, one bulk copy per tile
-      for (int j = 0; j < ntiles; ++j) {
-        if (j >= 2 && !mbar_wait(&kv_empty[j & 1], ((j >> 1) - 1) & 1, p.err)) break;
-        mbar_arrive_expect_tx(&kv_full[j & 1], L::kv_buf);
-        bulk_g2s(sm + L::kv0 + (j & 1) * L::kv_buf, p.kv_tiles + (static_cast<size_t>(j) * p.nkv + g) * L::kv_buf,
-                 L::kv_buf, &kv_full[j & 1]);
+      for (int i = 0; i < 8; ++i) {
+        const int it = it0 + st + i * kAtSoftmax, r = it / (D / 8), c = it % (D / 8);
+        a[i][0] = a[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (it < kAtRows * (D / 8) && r < rows) {
+          const float4* src = reinterpret_cast<const float4*>(p.q + static_cast<size_t>(t0 + r / G) * qd +
+                                                              static_cast<size_t>(g * G + r % G) * D + c * 8);
+          a[i][0] = __ldcg(src), a[i][1] = __ldcg(src + 1);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int it = it0 + st + i * kAtSoftmax, r = it / (D / 8), c = it % (D / 8);
+        if (it >= kAtRows * (D / 8)) continue;
+        const float v[8] = {a[i][0].x, a[i][0].y, a[i][0].z, a[i][0].w, a[i][1].x, a[i][1].y, a[i][1].z, a[i][1].w};
+        uint4 hi, lo;
+        split8(v, hi, lo);
+        const uint32_t off = sw_chunk(kAtRows, r, c);
+        *reinterpret_cast<uint4*>(sm + L::q_hi + off) = hi;
+        *reinterpret_cast<uint4*>(sm + L::q_lo + off) = lo;
       }
     }
-  } else {  // ---- softmax: row R = TMEM lane (softmaxInPlace, src/llm.zig:1408-1419, online form)
-    const int R = threadIdx.x;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
-    const int qpos = R < rows ? p.pos0 + t0 + R / G : -1;
-    float m = -INFINITY, l = 0.f;
+    fence_async_smem();  // generic-proxy writes, read by the tensor cores
+    mbar_arrive(q_ready);
+    float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int j0 = j * kAtKeys;
-      const int nkeys = min(kAtKeys, last_pos + 1 - j0);
+      const int j0 = j * kAtKeys + 32 * h;  // position of this thread's first key column
+      const int nkeys = min(kAtKeys, last_pos + 1 - j * kAtKeys) - 32 * h;
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.err)))) break;
       tc_fence_after();
-      float s[kAtKeys];
-      tmem_ld32(trow + (j & 1) * 64, s);
-      tmem_ld32(trow + (j & 1) * 64 + 32, s + 32);
+      float s[32];
+      tmem_ld32(trow + (j & 1) * 64 + 32 * h, s);
       float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kAtKeys; ++c) {
+      for (int c = 0; c < 32; ++c) {
         s[c] = (c < nkeys && j0 + c <= qpos) ? s[c] * p.inv_sqrt_d : -INFINITY;
         mt = fmaxf(mt, s[c]);
       }
+      xrow[h][R] = mt;
+      named_barrier(1, kAtSoftmax);
+      mt = fmaxf(xrow[0][R], xrow[1][R]);
       const bool move = mt > m + kAtRescale;  // false while the row has no key yet (mt = -inf)
       const float mnew = move ? mt : m;
       const float alpha = move ? (m == -INFINITY ? 0.f : __expf(m - mnew)) : 1.f;
       // P is free and O complete once the last tile's P V is done
       if (j > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(pv_full, (j - 1) & 1, p.err)))) break;
       tc_fence_after();
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // O = O * alpha (warp-collective TMEM access)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // this half of O = O * alpha (warp-collective)
 #pragma unroll 1
-        for (int cc = 0; cc < D / 32; ++cc) {
+        for (int cc = 0; cc < D / 64; ++cc) {
           float v[32];
-          tmem_ld32(trow + L::o_col + cc * 32, v);
+          const uint32_t col = L::o_col + h * (D / 2) + cc * 32;
+          tmem_ld32(trow + col, v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st32(trow + L::o_col + cc * 32, v);
+          tmem_st32(trow + col, v);
         }
       }
       float sum = 0.f;
 #pragma unroll
-      for (int c8 = 0; c8 < kAtKeys / 8; ++c8) {
+      for (int c8 = 0; c8 < 4; ++c8) {
         float pv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -374,7 +403,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
         }
         uint4 hi, lo;
         split8(pv, hi, lo);
-        const uint32_t off = sw_chunk(kAtRows, R, c8);
+        const uint32_t off = sw_chunk(kAtRows, R, 4 * h + c8);
         *reinterpret_cast<uint4*>(sm + L::p_hi + off) = hi;
         *reinterpret_cast<uint4*>(sm + L::p_lo + off) = lo;
       }
@@ -384,17 +413,22 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
       tc_fence_before();
       mbar_arrive(p_ready);
     }
-    if (ok && __all_sync(0xffffffffu, mbar_wait(pv_full, (ntiles - 1) & 1, p.err))) {
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(pv_full, (ntiles - 1) & 1, p.err));
+    named_barrier(1, kAtSoftmax);  // both halves are past their last read of xrow
+    xrow[h][R] = l;
+    named_barrier(1, kAtSoftmax);
+    if (ok) {
       tc_fence_after();
       const size_t orow = static_cast<size_t>(t0 + R / G) * qd + static_cast<size_t>(g * G + R % G) * D;
-      const float inv = 1.0f / l;
+      const float inv = 1.0f / (xrow[0][R] + xrow[1][R]);
 #pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
+      for (int cc = 0; cc < D / 64; ++cc) {
         float v[32];
-        tmem_ld32(trow + L::o_col + cc * 32, v);
+        const int e0 = h * (D / 2) + cc * 32;
+        tmem_ld32(trow + L::o_col + e0, v);
         if (R < rows) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) split_bf16(v[i] * inv, p.out_hi[orow + cc * 32 + i], p.out_lo[orow + cc * 32 + i]);
+          for (int i = 0; i < 32; ++i) split_bf16(v[i] * inv, p.out_hi[orow + e0 + i], p.out_lo[orow + e0 + i]);
         }
       }
     }
