@@ -69,6 +69,26 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
 
 
+def tensor_peak():
+    """Dense bf16 TFLOP/s of this pool's B200s (burst: prefill kernels run for milliseconds)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS burst)"
+    except Exception:
+        return 1590.0, "fallback 1.59 PFLOP/s"
+
+
+def prefill_roofline(gemm_flops, attn_flops, ms, peak, peak_source):
+    """Tensor roofline of a prefill: algorithmic FLOPs (2 per multiply-add of the reference's fp32 math) and the
+    MMA FLOPs actually issued (GEMMs: activations as bf16 hi + lo, 2 MMAs per product; attention: hi.hi + hi.lo +
+    lo.hi, 3 MMAs), both over the measured dense bf16 peak."""
+    s = ms / 1e3
+    achieved = (gemm_flops + attn_flops) / s / 1e12
+    issued = (2.0 * gemm_flops + 3.0 * attn_flops) / s / 1e12
+    return {"bound": "tensor", "achieved": achieved, "issued": issued, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "frac_issued": issued / peak, "peak_source": peak_source}
+
+
 def ncu_traffic(kernel_key):
     """DRAM bytes per launch of a kernel from the committed ncu summary, or None."""
     path = os.path.join(ROOT, "profiles", "ncu_summary.txt")
@@ -401,8 +421,10 @@ def _main(args, out_fd):
     P = args.prompt
     attn_flops = 4 * cfg.num_attention_heads * cfg.head_dim() * cfg.num_hidden_layers * P * (P + 1) / 2
     gemm_flops = 2.0 * P * layer_params * cfg.num_hidden_layers
+    tpeak, tpeak_src = tensor_peak()
     prefill = {"tokens": P, "ms": prefill_ms, "tok_per_s": P / (prefill_ms / 1000.0),
                "algorithmic_tflops": (gemm_flops + attn_flops + 2.0 * h * cfg.vocab_size) / (prefill_ms / 1e3) / 1e12,
+               "roofline": prefill_roofline(gemm_flops, attn_flops, prefill_ms, tpeak, tpeak_src),
                "tensor_core_gemm": runner.query("tc_prefill") == 1,
                "note": "activations enter the tensor cores as bf16 hi+lo pairs (2 MMAs per product) for fp32-level "
                        "parity; attention on the tensor cores (q, k, v, p as hi+lo pairs, 3 MMAs per product)"}
@@ -460,10 +482,13 @@ def _main(args, out_fd):
         lms_med = float(np.median(lms))
         lh, lkv, linter = lcfg.hidden_size, lcfg.kv_dim(), lcfg.intermediate_size
         l_params = lh * lh + 2 * lkv * lh + lh * lh + 3 * linter * lh
-        l_flops = (2.0 * L * l_params * lcfg.num_hidden_layers +
-                   4 * lcfg.num_attention_heads * lcfg.head_dim() * lcfg.num_hidden_layers * L * (L + 1) / 2)
+        l_gemm = 2.0 * L * l_params * lcfg.num_hidden_layers
+        l_attn = 4 * lcfg.num_attention_heads * lcfg.head_dim() * lcfg.num_hidden_layers * L * (L + 1) / 2
+        l_flops = l_gemm + l_attn
+        tpeak, tpeak_src = tensor_peak()
         prefill_long = {"model": "llama3.2-1b", "tokens": L, "ms": lms_med, "tok_per_s": L / (lms_med / 1000.0),
                         "algorithmic_tflops": l_flops / (lms_med / 1e3) / 1e12,
+                        "roofline": prefill_roofline(l_gemm, l_attn, lms_med, tpeak, tpeak_src),
                         "timing": "median of 2 calls after 1 warm-up call"}
         rl.close()
 
