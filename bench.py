@@ -31,6 +31,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s + HBM-roofline fraction at 1/2/4/8 B200 vs host-CPU ref"
 FALLBACK_HBM_GBS = 6650.0
+SHORT_CONTEXT_NOTE = ("the CPU decodes at shorter positions than the GPU arm (which decodes after the "
+                      "prompt): its per-token KV read is smaller, a few percent of an 8B token's bytes at most")
 KERNEL_NAMES = {0: "gemv q|k|v (rmsnorm prologue)", 1: "gemv o_proj (+residual)",
                 2: "gemv gate|up (rmsnorm prologue, silu*mul)", 3: "gemv down_proj (+residual)",
                 4: "gemv lm_head (final norm, argmax)"}
@@ -174,7 +176,8 @@ def time_oracle(cfg, seed, seconds, min_tokens=2, max_tokens=None):
             break
     cores = min(os.cpu_count() or 1, 64)  # linearInto spawns at most 64 workers (src/llm.zig:11)
     sample = (f"{n} greedy decode tokens of the full {cfg.num_hidden_layers}-layer model at positions 1-{n} "
-              f"(weights generated in {gen_s:.1f} s, excluded), {os.cpu_count()} host threads visible")
+              f"(weights generated in {gen_s:.1f} s, excluded), {os.cpu_count()} host threads visible; "
+              f"{SHORT_CONTEXT_NOTE}")
     r.close()
     return n / el, cores, sample
 
@@ -210,7 +213,7 @@ def run_reference(args, rank, out_fd=1):
     value = steps / el
     cores = min(os.cpu_count() or 1, 64)
     sample = (f"{steps} of {args.steps} requested greedy decode steps (bounded to ~150 s), full model, positions "
-              f"{pos - steps}-{pos - 1}; weights generated in {gen_s:.1f} s (excluded)")
+              f"{pos - steps}-{pos - 1}; weights generated in {gen_s:.1f} s (excluded); {SHORT_CONTEXT_NOTE}")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": steps, "warmup": args.warmup, "ms_per_step": 1000.0 * el / steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -228,6 +231,46 @@ def workload_config(args, cfg, n):
             "model": args.config, "global_batch": 1, "seq_len": args.prompt, "ctx": cfg.max_position_embeddings,
             "parallelism": f"tp{n}", "weights": "bf16 synthetic ~N(0,0.02), seeded", "activations": "f32",
             "kv_cache": "f32 paged", "l2": "inputs larger than L2 (every step streams all weights, >15 GB)"}
+
+
+def greedy_stream(runner, prompt, n_tokens):
+    """The first n_tokens greedy tokens after `prompt` (prefill, then on-device decode)."""
+    runner.reset()
+    runner.prefill(prompt, 0, logits=False)
+    first = int(runner.last_argmax)
+    rest, _ = runner.decode(n_tokens - 1)
+    return [first] + list(rest)
+
+
+def stream_check(args, cfg, runner, prompt, n, rank, local_rank, barrier, vvli_b200, n_tokens=32):
+    """Compares this run's greedy stream with a single-GPU stream of the same weights.  Every rank
+    takes part in the tensor-parallel stream; rank 0 alone builds the 1-GPU context (the others wait
+    at the barrier)."""
+    got = greedy_stream(runner, prompt, n_tokens)
+    barrier()
+    out = None
+    if rank == 0:
+        saved = os.environ.get("VVLI_MEGAKERNEL")
+        if n == 1:
+            os.environ["VVLI_MEGAKERNEL"] = "0"  # the per-kernel step (CUDA graph of separate kernels)
+        try:
+            r1 = vvli_b200.Runner(cfg, max_seq=len(prompt) + n_tokens + 8, device=local_rank)
+        finally:
+            if saved is None:
+                os.environ.pop("VVLI_MEGAKERNEL", None)
+            else:
+                os.environ["VVLI_MEGAKERNEL"] = saved
+        r1.fill_synthetic(args.seed)
+        ref_path = "per-kernel step, 1 GPU" if n == 1 else "megakernel, 1 GPU"
+        ref = greedy_stream(r1, prompt, n_tokens)
+        r1.close()
+        first_diff = next((i for i, (a, b) in enumerate(zip(got, ref)) if a != b), None)
+        out = {"equal": got == ref, "tokens": n_tokens, "distinct_tokens": len(set(ref)),
+               "first_divergence": first_diff,
+               "compared": f"{'tensor-parallel decode on ' + str(n) + ' GPUs' if n > 1 else 'megakernel decode'} "
+                           f"vs {ref_path}, greedy tokens after the {len(prompt)}-token prompt"}
+    barrier()
+    return out
 
 
 def _second_id(dist, vvli_b200, rank):
@@ -492,6 +535,11 @@ def _main(args, out_fd):
                         "timing": "median of 2 calls after 1 warm-up call"}
         rl.close()
 
+    # ---- stream check: the greedy stream of this run's decode path after the prompt against a
+    # single-GPU stream of the same weights (N > 1: the tensor-parallel path against a 1-GPU context
+    # on rank 0's GPU; N = 1: the megakernel against the per-kernel step).
+    parity = stream_check(args, cfg, runner, prompt, n, rank, local_rank, barrier, vvli_b200)
+
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
         v, cores, sample = time_oracle(cfg, args.seed, args.cpu_seconds)
@@ -502,6 +550,7 @@ def _main(args, out_fd):
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, cfg, n),
                 "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "tp_parity": parity["equal"] if parity else None, "stream_check": parity,
                 "prefill": prefill, "prefill_long": prefill_long, "sampler": sampler_line, "batch": batch,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clk}
         emit(line, out_fd)

@@ -280,9 +280,10 @@ int vvli_cuda_sample(vvli_ctx* ctx, const vvli_sample_options* options, const fl
 int vvli_cuda_time_kernel(vvli_ctx* ctx, int kernel, int reps, float* avg_ms, double* bytes);
 
 /* Copies the residual stream x after layer `layer` of the last forward call
- * (hidden_size floats).  Debug entry point for per-layer parity; the
- * reference keeps it in Scratch.x (src/llm.zig:612, 757, 765).  Requires the
- * context to have been created with debug capture on (vvli_cuda_set_debug). */
+ * (hidden_size floats); after vvli_cuda_prefill, that of the prompt's last
+ * token.  Debug entry point for per-layer parity; the reference keeps it in
+ * Scratch.x (src/llm.zig:612, 757, 765).  Requires debug capture to be on
+ * (vvli_cuda_set_debug) during that call. */
 int vvli_cuda_set_debug(vvli_ctx* ctx, int enabled);
 int vvli_cuda_debug_hidden(vvli_ctx* ctx, int layer, float* out);
 
@@ -346,9 +347,11 @@ int vvli_cuda_forward_batch(vvli_ctx* ctx, const uint32_t* tokens, const uint64_
  * synchronisation.  Its scratch is one static device array of 33,024 bytes
  * per device, so the limits are rows <= 64 and rows * ceil(n / 4096) <= 4096
  * (n <= 16,777,216 for one row); larger requests, null or misaligned pointers,
- * and pointers that are not device memory of `device` (or managed memory)
- * covering the whole range return VVLI_ERR_INVALID_ARGUMENT with the reason in
- * vvli_cuda_last_error().
+ * and ranges whose first or last byte is not device memory of `device` (or
+ * managed memory) return VVLI_ERR_INVALID_ARGUMENT with the reason in
+ * vvli_cuda_last_error().  Only the two ends are checked, so a buffer that a
+ * virtual-memory pool (cuMemCreate + cuMemMap) maps as several chunks is
+ * accepted.
  *
  * The work is queued on `stream` (a cudaStream_t; NULL = the legacy default
  * stream) and tokens[] is valid once that stream has been synchronised.  The
@@ -356,7 +359,9 @@ int vvli_cuda_forward_batch(vvli_ctx* ctx, const uint32_t* tokens, const uint64_
  *
  * The first call on each device does one-time setup (the scratch address is
  * looked up, which may load this library's device code); make that first
- * call before any stream capture begins.  The scratch's per-row arrival
+ * call before any stream capture begins.  The address is kept for the life of
+ * the process, so resetting a device (cudaDeviceReset) after its first call
+ * is not supported.  The scratch's per-row arrival
  * counters must be zero when a call starts: they are zero when the device
  * code loads and every completed call leaves them zero.  Calls that overlap
  * on one device (two streams, or two host threads, without ordering between

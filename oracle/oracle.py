@@ -63,6 +63,8 @@ def lib():
             "ref_runner_forward_token": (ctypes.c_int, [vp, ctypes.c_uint32, ctypes.c_uint64, _f32p]),
             "ref_runner_forward_embedding": (ctypes.c_int, [vp, _f32p, ctypes.c_uint64, _f32p]),
             "ref_runner_hidden": (None, [vp, ctypes.c_uint64, _f32p]),
+            "ref_runner_set_attention_threads": (None, [vp, ctypes.c_uint64]),
+            "ref_runner_prefill": (ctypes.c_int, [vp, _u32p, ctypes.c_uint64, ctypes.c_uint64, _f32p]),
             "ref_runner_logits": (None, [vp, _f32p]),
             "ref_generate_greedy": (ctypes.c_int, [vp, _u32p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64,
                                                    _u32p, _u64p]),
@@ -218,6 +220,18 @@ class RefRunner:
         e = np.ascontiguousarray(emb, np.float32)
         out = np.empty(self.cfg.vocab_size, dtype=np.float32)
         check(lib().ref_runner_forward_embedding(self.h, f32(e), position, f32(out)))
+        return out
+
+    def set_attention_threads(self, threads: int):
+        """Checker only: attention heads on `threads` threads (bit-identical)."""
+        lib().ref_runner_set_attention_threads(self.h, threads)
+
+    def prefill(self, tokens, start: int = 0) -> np.ndarray:
+        """Checker only: forward_token over tokens at positions start.., the
+        LM head run for the last token alone; returns its logits."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = np.empty(self.cfg.vocab_size, dtype=np.float32)
+        check(lib().ref_runner_prefill(self.h, ptr(t, _u32p), t.size, start, f32(out)))
         return out
 
     def hidden(self, layer: int) -> np.ndarray:

@@ -380,18 +380,23 @@ struct Runner {
   std::vector<float> keys, values;
   std::vector<float> x, residual, norm, q, k, v, attention, projected, gate, up, ff, scores, logits;
   std::vector<float> hidden;  // x after every layer, [layers][hidden]
+  // Checker conveniences (never set by the timed CPU baseline): attention
+  // over q heads on several threads, and a forward that stops before the LM
+  // head.  Neither changes the arithmetic of any value that is produced.
+  size_t attention_threads = 1;
+  bool skip_lm_head = false;
+  std::vector<float> head_scores;  // [attention_threads][max_seq]
 };
 
+// One q head of computeAttentionInto; `used` is that head's score scratch.
 template <int L>
-void attention_into(Runner& r, size_t layer, size_t position) {  // src/llm.zig:1302-1335
+void attention_head(Runner& r, size_t layer, size_t position, size_t qh, float* used) {
   const auto& c = r.cfg;
   const size_t hd = head_dim(c), group = kv_group(c), kvd = kv_dim(c);
   const float inv_sqrt_head = 1.0f / std::sqrt(static_cast<float>(hd));
-  std::fill(r.attention.begin(), r.attention.end(), 0.0f);
-  for (size_t qh = 0; qh < c.num_attention_heads; ++qh) {
+  {
     const size_t kvh = qh / group;
     const float* qs = r.q.data() + qh * hd;
-    float* used = r.scores.data();
     for (size_t t = 0; t <= position; ++t) {
       const float* key = r.keys.data() + (layer * r.max_seq + t) * kvd + kvh * hd;
       used[t] = dot_f32<L>(qs, key, hd) * inv_sqrt_head;
@@ -404,6 +409,25 @@ void attention_into(Runner& r, size_t layer, size_t position) {  // src/llm.zig:
       add_scaled<L>(oh, val, used[t], hd);
     }
   }
+}
+
+template <int L>
+void attention_into(Runner& r, size_t layer, size_t position) {  // src/llm.zig:1302-1335
+  const size_t heads = r.cfg.num_attention_heads;
+  std::fill(r.attention.begin(), r.attention.end(), 0.0f);
+  const size_t T = std::min(r.attention_threads, heads);
+  if (T <= 1) {  // the reference: one thread, heads in order
+    for (size_t qh = 0; qh < heads; ++qh) attention_head<L>(r, layer, position, qh, r.scores.data());
+    return;
+  }
+  // Checker only: heads are independent, so splitting them over threads
+  // gives every output the same arithmetic as the sequential loop.
+  std::vector<std::thread> ts;
+  for (size_t t = 0; t < T; ++t)
+    ts.emplace_back([&, t] {
+      for (size_t qh = t; qh < heads; qh += T) attention_head<L>(r, layer, position, qh, r.head_scores.data() + t * r.max_seq);
+    });
+  for (auto& th : ts) th.join();
 }
 
 template <int L>
@@ -438,6 +462,7 @@ void forward_current(Runner& r, size_t position) {  // src/llm.zig:720-766
     for (size_t i = 0; i < h; ++i) r.x[i] = r.residual[i] + r.projected[i];
     std::copy(r.x.begin(), r.x.end(), r.hidden.begin() + l * h);
   }
+  if (r.skip_lm_head) return;
   rms_norm<L>(r.norm.data(), r.x.data(), B + r.layout.final_norm, nullptr, h, c.rms_norm_eps);
   const uint64_t head = r.layout.lm_head == UINT64_MAX ? r.layout.embedding : r.layout.lm_head;
   linear_into<L>(r.logits.data(), B + head, c.vocab_size, h, r.norm.data(), nullptr, r.opts);
@@ -624,6 +649,29 @@ int ref_runner_forward_embedding(void* p, const float* embedding, uint64_t posit
   std::copy(embedding, embedding + r->cfg.hidden_size, r->x.begin());
   forward_dispatch(*r, position);
   if (logits_out) std::copy(r->logits.begin(), r->logits.end(), logits_out);
+  return VVLI_OK;
+}
+
+// Checker only: runs heads of computeAttentionInto on `threads` threads
+// (1 = the reference's sequential loop).  Results are bit-identical.
+void ref_runner_set_attention_threads(void* p, uint64_t threads) {
+  auto* r = static_cast<Runner*>(p);
+  r->attention_threads = std::max<uint64_t>(1, threads);
+  r->head_scores.assign(r->attention_threads * r->max_seq, 0.0f);
+}
+
+// Checker only: forwardToken over tokens[0, n) at positions start.., with the
+// final norm and LM head run for the last token alone (earlier positions'
+// logits are never read by a prompt loop).  Every hidden state and the last
+// logits are what n forwardToken calls give.
+int ref_runner_prefill(void* p, const uint32_t* tokens, uint64_t n, uint64_t start, float* logits_out) {
+  auto* r = static_cast<Runner*>(p);
+  for (uint64_t i = 0; i < n; ++i) {
+    r->skip_lm_head = i + 1 < n;
+    const int st = ref_runner_forward_token(p, tokens[i], start + i, i + 1 < n ? nullptr : logits_out);
+    r->skip_lm_head = false;
+    if (st) return st;
+  }
   return VVLI_OK;
 }
 

@@ -6,6 +6,7 @@ greedy token streams over the first 32 tokens.  The GPU path computes in fp32
 like the reference, so tighter bounds are asserted too where they hold.
 """
 
+import dataclasses
 import os
 import sys
 
@@ -93,42 +94,146 @@ def test_device_synthetic_weights_match_host_blob(oracle, vv):
         assert np.array_equal(a.forward_token(tok, pos), b.forward_token(tok, pos))
 
 
-def greedy_parity(oracle, vv, cfg, seed, n_prompt, n_new, max_seq, check_layers=True):
+def check_layers(gpu, ref, cfg, where):
+    """Per-layer residual stream of the last forward against the oracle."""
+    worst = 0.0
+    for layer in range(cfg.num_hidden_layers):
+        err = rel_l2(gpu.debug_hidden(layer), ref.hidden(layer))
+        assert err < HIDDEN_REL_L2, (where, layer, err)
+        worst = max(worst, err)
+    return worst
+
+
+def divergence(gpu_tokens, ref_tokens, ref_logits_per_step=None):
+    """Message for the first index where two greedy streams differ, with the
+    oracle's top-2 logit gap at that step when its logits are known."""
+    i = next((i for i, (a, b) in enumerate(zip(gpu_tokens, ref_tokens)) if a != b), None)
+    if i is None:
+        return f"streams differ in length: {len(gpu_tokens)} vs {len(ref_tokens)}"
+    msg = f"first divergence at generated token {i}: gpu {gpu_tokens[i]} vs oracle {ref_tokens[i]}"
+    if ref_logits_per_step is not None and i < len(ref_logits_per_step):
+        top = np.sort(ref_logits_per_step[i])[-2:]
+        msg += f"; oracle top-2 gap {float(top[1] - top[0]):.3e}"
+    return msg
+
+
+def stream_parity(oracle, vv, cfg, seed, n_prompt, n_new, max_seq, min_distinct=8):
+    """The north-star contract on one architecture: every prompt and decode
+    position's per-layer hidden states (1e-2 rel L2, and 1e-4) and logits
+    (2e-2 max-abs, and 1e-4) against the oracle, an identical greedy stream
+    of n_new tokens from the host loop and from the device loop, and a stream
+    that is not degenerate (at least `min_distinct` distinct tokens)."""
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, cfg.vocab_size, size=n_prompt).tolist()
     ref = oracle.RefRunner(cfg, synthetic_seed=seed, max_seq=max_seq)
+    ref.set_attention_threads(os.cpu_count() or 1)
     gpu = vv.Runner(cfg, max_seq=max_seq)
     gpu.fill_synthetic(seed)
-    if check_layers:
-        gpu.set_debug(True)
-        worst_h = worst_l = 0.0
-        for pos, tok in enumerate(prompt):
-            lr = ref.forward_token(tok, pos)
-            lg = gpu.forward_token(tok, pos)
-            for layer in range(cfg.num_hidden_layers):
-                worst_h = max(worst_h, rel_l2(gpu.debug_hidden(layer), ref.hidden(layer)))
-            worst_l = max(worst_l, float(np.max(np.abs(lg - lr))))
-        assert worst_h < HIDDEN_REL_L2 and worst_l < LOGIT_MAX_ABS, (worst_h, worst_l)
-        assert worst_h < TIGHT_REL_L2, worst_h
-        gpu.set_debug(False)
-        ref.reset()
-        gpu.reset()
-    ref_tokens = ref.generate_greedy(prompt, n_new)
+    gpu.set_debug(True)
+    worst_h = worst_l = 0.0
+    for pos, tok in enumerate(prompt):
+        lr = ref.forward_token(tok, pos)
+        lg = gpu.forward_token(tok, pos)
+        worst_h = max(worst_h, check_layers(gpu, ref, cfg, ("prompt", pos)))
+        worst_l = max(worst_l, float(np.max(np.abs(lg - lr))))
+    # greedy decode, host loop: the oracle's argmax is fed to both
+    ref_tokens, ref_logits = [], []
+    for i in range(n_new):
+        tok = oracle.argmax(lr)
+        ref_tokens.append(tok)
+        ref_logits.append(lr)
+        assert gpu.last_argmax == tok, divergence(ref_tokens[:i] + [gpu.last_argmax], ref_tokens, ref_logits)
+        if i + 1 == n_new:
+            break
+        pos = n_prompt + i
+        lr = ref.forward_token(tok, pos)
+        lg = gpu.forward_token(tok, pos)
+        worst_h = max(worst_h, check_layers(gpu, ref, cfg, ("decode", pos)))
+        worst_l = max(worst_l, float(np.max(np.abs(lg - lr))))
+    assert worst_l < LOGIT_MAX_ABS, worst_l
+    assert worst_h < TIGHT_REL_L2 and worst_l < 1e-4, (worst_h, worst_l)
+    assert len(set(ref_tokens)) >= min_distinct, ref_tokens
+    # the device loop (prefill + graph/megakernel replays) gives the same stream
+    gpu.set_debug(False)
+    gpu.reset()
     gpu_tokens, stats = gpu.generate_greedy(prompt, n_new)
     assert stats.generated_tokens == n_new
-    assert gpu_tokens == ref_tokens, next(i for i, (a, b) in enumerate(zip(gpu_tokens, ref_tokens)) if a != b)
+    assert gpu_tokens == ref_tokens, divergence(gpu_tokens, ref_tokens, ref_logits)
 
 
 def test_qwen2_5_0_5b_architecture(oracle, vv):
-    greedy_parity(oracle, vv, C.qwen2_5_0_5b(), seed=0, n_prompt=8, n_new=32, max_seq=512)
+    stream_parity(oracle, vv, C.qwen2_5_0_5b(), seed=0, n_prompt=8, n_new=32, max_seq=512)
 
 
 def test_llama3_2_1b_architecture_with_rope_scaling(oracle, vv):
-    greedy_parity(oracle, vv, C.llama3_2_1b(), seed=0, n_prompt=8, n_new=32, max_seq=512)
+    stream_parity(oracle, vv, C.llama3_2_1b(), seed=0, n_prompt=8, n_new=32, max_seq=512)
 
 
 def test_llama3_8b_architecture(oracle, vv):
-    greedy_parity(oracle, vv, C.llama3_8b(), seed=0, n_prompt=4, n_new=8, max_seq=64, check_layers=False)
+    # The benchmarked configuration: 32-token prompt, 32 greedy tokens, every
+    # layer at every position.
+    stream_parity(oracle, vv, C.llama3_8b(), seed=0, n_prompt=32, n_new=32, max_seq=128)
+
+
+def cut(cfg, layers=2, vocab=32000):
+    """The same layer shapes with fewer layers and a smaller vocabulary, so the
+    oracle can run thousands of positions in seconds."""
+    return dataclasses.replace(cfg, num_hidden_layers=layers, vocab_size=vocab, eos_token_id=None,
+                               pad_token_id=None)
+
+
+def long_context_parity(oracle, vv, cfg, n_prompt, n_new, seed=0):
+    """Tensor-core prefill of a prompt longer than one 2,048-token chunk, then
+    greedy decode at positions past 16 KV pages per split group (1,024
+    positions), against the oracle: the last prompt token's per-layer hidden
+    states and logits, every decode step's hidden states and logits (host
+    loop), and the device decode loop's stream."""
+    max_seq = n_prompt + n_new + 8
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab_size, size=n_prompt).tolist()
+    ref = oracle.RefRunner(cfg, synthetic_seed=seed, max_seq=max_seq)
+    ref.set_attention_threads(os.cpu_count() or 1)
+    a = vv.Runner(cfg, max_seq=max_seq)
+    a.fill_synthetic(seed)
+    b = vv.Runner(cfg, max_seq=max_seq)
+    b.fill_synthetic(seed)
+    assert a.query("tc_prefill") == 1
+    a.set_debug(True)
+    lr = ref.prefill(prompt, 0)
+    la = a.prefill(prompt, 0)
+    lb = b.prefill(prompt, 0)
+    assert np.array_equal(la, lb)
+    check_layers(a, ref, cfg, ("prefill", n_prompt - 1))
+    assert np.max(np.abs(la - lr)) < LOGIT_MAX_ABS
+    ref_tokens, ref_logits = [], []
+    for i in range(n_new):
+        tok = oracle.argmax(lr)
+        ref_tokens.append(tok)
+        ref_logits.append(lr)
+        assert a.last_argmax == tok, divergence(ref_tokens[:i] + [a.last_argmax], ref_tokens, ref_logits)
+        if i + 1 == n_new:
+            break
+        pos = n_prompt + i
+        lr = ref.forward_token(tok, pos)
+        lg = a.forward_token(tok, pos)
+        check_layers(a, ref, cfg, ("decode", pos))
+        assert np.max(np.abs(lg - lr)) < LOGIT_MAX_ABS, pos
+    assert len(set(ref_tokens)) >= 8, ref_tokens
+    # device loop from b's prefilled cache: its first token is the prefill's argmax
+    assert b.last_argmax == ref_tokens[0]
+    got, _ = b.decode(n_new - 1)
+    assert got == ref_tokens[1:], divergence(got, ref_tokens[1:], ref_logits[1:])
+
+
+def test_llama3_8b_shapes_two_chunk_prefill_and_long_decode(oracle, vv):
+    # head_dim 128, group 4: a 2,100-token prompt (chunks of 2,048 + 52), then
+    # decode at positions 2,100-2,131 (34 pages over 16 split groups).
+    long_context_parity(oracle, vv, cut(C.llama3_8b()), n_prompt=2100, n_new=32)
+
+
+def test_llama3_2_1b_shapes_three_chunk_prefill_and_long_decode(oracle, vv):
+    # head_dim 64, group 4, llama3 rope scaling: a 4,100-token prompt (chunks
+    # of 2,048 + 2,048 + 4), then decode at positions 4,100-4,131.
+    long_context_parity(oracle, vv, cut(C.llama3_2_1b()), n_prompt=4100, n_new=32)
 
 
 def test_prefill_equals_sequential_forwards(oracle, vv):
@@ -169,8 +274,8 @@ def test_tensor_core_prefill_long_prompt(oracle, vv):
     for pos in range(len(prompt), len(prompt) + 16):
         ref_tokens.append(tok)
         tok = oracle.argmax(ref.forward_token(tok, pos))
-    got, _ = gpu.decode(16)
-    assert [gpu.last_argmax] and got[:15] == ref_tokens[1:16]
+    got, _ = gpu.decode(15)
+    assert got == ref_tokens[1:16], divergence(got, ref_tokens[1:16])
 
 
 def test_generate_greedy_stops_at_eos(oracle, vv):

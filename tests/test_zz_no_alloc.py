@@ -131,3 +131,58 @@ def test_rejects_out_of_limit_requests_without_launching(torch):
     # still usable afterwards
     x[1, 17] = 1.0
     assert static_argmax(torch, x, 2, CHUNK) == [0, 17]
+
+
+def test_allocates_no_device_memory(torch):
+    # The point of the entry point: after the first call on a device (which
+    # may load this library's device code), calls of any shape leave the
+    # device's free memory unchanged.
+    g = torch.Generator(device="cuda").manual_seed(2)
+    shapes = [(1, 1), (3, 3 * CHUNK + 5), (MAX_ROWS, 64 * CHUNK), (1, MAX_PARTIALS * CHUNK)]
+    inputs = [torch.randn(s, generator=g, device="cuda") for s in shapes]
+    for x in inputs:  # warm-up: one call per shape
+        static_argmax(torch, x, x.shape[0], x.shape[1])
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        for x in inputs:
+            static_argmax(torch, x, x.shape[0], x.shape[1])
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before, (free_before, free_after)
+
+
+VMM_CHILD = r"""
+import ctypes, sys
+import torch
+sys.path.insert(0, sys.argv[1])
+from vvli_b200 import _abi
+n = 48 * 1024 * 1024                      # 192 MB: several chunks of the expandable segment
+pad = torch.empty(3 * 1024 * 1024 + 7, device="cuda")   # moves the next buffer off a chunk boundary
+x = torch.zeros((1, n), device="cuda")
+x[0, n - 3] = 5.0
+x[0, 7] = 4.0
+t = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+s = torch.cuda.current_stream()
+rc = _abi.lib().vvli_cuda_argmax_rows_static(0, ctypes.c_void_p(x.data_ptr()), 1, n,
+                                             ctypes.c_void_p(t.data_ptr()), ctypes.c_void_p(s.cuda_stream))
+assert rc == 0, _abi.lib().vvli_cuda_last_error()
+s.synchronize()
+assert t.item() == n - 3, t.item()
+print("vmm ok")
+"""
+
+
+def test_buffer_from_virtual_memory_pool(torch):
+    # A pool built on cuMemCreate + cuMemMap (torch's expandable segments)
+    # maps a large buffer as several physical chunks; the entry point must
+    # accept such a buffer.  Runs in a child process so the allocator setting
+    # applies from the start.
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PYTORCH_CUDA_ALLOC_CONF="expandable_segments:True")
+    r = subprocess.run([sys.executable, "-c", VMM_CHILD, root], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "vmm ok" in r.stdout, r.stdout + r.stderr

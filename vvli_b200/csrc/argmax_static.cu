@@ -20,7 +20,6 @@
 // order, so the first maximal index wins ties, a NaN never replaces the
 // running best, and a NaN in element 0 makes the answer 0.
 
-#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -157,35 +156,32 @@ int cuda_fail(cudaError_t e, const char* what) {
   return e == cudaErrorMemoryAllocation ? VVLI_ERR_OOM : VVLI_ERR_CUDA;
 }
 
-// True when [p, p + bytes) lies inside one allocation that the device can
-// read: device memory of `device`, or managed memory.
-bool device_range_ok(const void* p, size_t bytes, int device) {
+// True when `p` is memory that `device` can read: device memory of `device`,
+// or managed memory.
+bool device_ptr_ok(const void* p, int device) {
   cudaPointerAttributes a{};
   if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
-  if (!(a.type == cudaMemoryTypeManaged || (a.type == cudaMemoryTypeDevice && a.device == device))) return false;
-  using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
-  static RangeFn range = nullptr;
-  if (!range) {
-    cudaDriverEntryPointQueryResult q;
-    RangeFn f = nullptr;
-    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", reinterpret_cast<void**>(&f), cudaEnableDefault, &q) !=
-            cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || !f)
-      return false;
-    range = f;
-  }
-  CUdeviceptr base = 0;
-  size_t size = 0;
-  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return false;
-  const uintptr_t lo = reinterpret_cast<uintptr_t>(p);
-  return lo >= base && bytes <= size && lo - base <= size - bytes;
+  return a.type == cudaMemoryTypeManaged || (a.type == cudaMemoryTypeDevice && a.device == device);
+}
+
+// True when the first and the last byte of [p, p + bytes) are memory that
+// `device` can read.  Both ends are checked separately rather than asking for
+// one allocation that covers the range: pools built on the virtual memory API
+// (cuMemCreate + cuMemMap, e.g. torch's expandable segments) map a buffer as
+// several physical chunks, and a buffer that spans two of them is valid.
+bool device_range_ok(const void* p, size_t bytes, int device) {
+  if (bytes == 0 || reinterpret_cast<uintptr_t>(p) > UINTPTR_MAX - (bytes - 1)) return false;
+  return device_ptr_ok(p, device) && device_ptr_ok(static_cast<const char*>(p) + (bytes - 1), device);
 }
 
 // One-time setup per device (the device is current): look up the address of
-// the static scratch.  This may load this library's device code.
+// the static scratch.  This may load this library's device code.  The address
+// is kept for the life of the process: a cudaDeviceReset after the first call
+// unloads the device code, and the cached address is then stale, so a device
+// reset is not supported once this entry point has run on that device.
 int scratch_for(int device, void** out) {
   std::lock_guard<std::mutex> lock(g_setup_mu);
   if (!g_scratch_ptr[device]) {
@@ -214,6 +210,11 @@ extern "C" int vvli_cuda_argmax_rows_static(int device, const float* logits, uin
                                             int32_t* tokens, void* stream) {
   if (!logits || !tokens) return fail(VVLI_ERR_INVALID_ARGUMENT, "argmax (static scratch): null pointer");
   if (rows == 0 || n == 0) return fail(VVLI_ERR_INVALID_ARGUMENT, "argmax (static scratch): empty logits");
+  if (n > static_cast<uint64_t>(kMaxPartials) * kChunk)
+    return fail(VVLI_ERR_INVALID_ARGUMENT, "argmax (static scratch): n = " + std::to_string(n) +
+                                               " exceeds the limit of " +
+                                               std::to_string(static_cast<uint64_t>(kMaxPartials) * kChunk) +
+                                               " logits per row");
   if (rows > kMaxRows)
     return fail(VVLI_ERR_INVALID_ARGUMENT, "argmax (static scratch): " + std::to_string(rows) +
                                                " rows exceed the limit of " + std::to_string(kMaxRows) +

@@ -381,8 +381,9 @@ int dalloc(T** p, size_t count);
 
 bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   const uint16_t* W = c->w;
-  // Ring shape: shared memory taken from the L1 carve-out costs the phase
-  // changes more than a deeper ring gains (measured), see DESIGN.md.
+  // Ring shape: two 64 KB stages.  Shared memory taken from the L1 carve-out
+  // slows the latency-bound phase changes more than a deeper ring speeds the
+  // weight stream (measured on Llama-3-8B).
   const int stage_cap = getenv("VVLI_MEGA_STAGE_CAP") ? std::max(4096, atoi(getenv("VVLI_MEGA_STAGE_CAP"))) : 65536;
   std::vector<MegaPhase> ph;
   auto gemv = [&](int epi, int layer, const uint16_t* w, int N, int K, int nphys, const uint16_t* norm,
@@ -765,6 +766,11 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start) 
       if (tp && (st = nccl_wait(c, nccl().AllReduce(c->pf_x, c->pf_x, static_cast<size_t>(M) * c->h, ncclFloat32,
                                                      ncclSum, c->comm, s), "allreduce")))
         return st;
+      // Debug mode: the residual stream of the chunk's last token after each
+      // layer (vvli_cuda_debug_hidden reads the prompt's last token).
+      if (c->debug)
+        CK(cudaMemcpyAsync(c->hidden + static_cast<size_t>(l) * c->h, c->pf_x + static_cast<size_t>(M - 1) * c->h,
+                           c->h * sizeof(float), cudaMemcpyDeviceToDevice, s));
     }
   }
   // The last token's hidden state goes through the final norm and LM head.
@@ -1438,7 +1444,7 @@ int vvli_cuda_prefill(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t 
   CK(cudaSetDevice(c->device));
   CK(cudaMemcpyAsync(c->seq_tokens + start, tokens, n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
   int st;
-  const bool tc = c->tc_prefill && !c->debug && n >= 2;
+  const bool tc = c->tc_prefill && n >= 2;
   // The tensor-core path ends in the LM head of the last token, which
   // publishes its argmax and advances the state from position start + n - 1.
   if ((st = stage_state(c, static_cast<int>(tc ? start + n - 1 : start), static_cast<int>(start + n), 0))) return st;
