@@ -196,7 +196,7 @@ class RefRunner:
         check(st.value)
 
     def close(self):
-        if self.h:
+        if getattr(self, "h", None):
             lib().ref_runner_destroy(self.h)
             self.h = None
 

@@ -178,8 +178,7 @@ def test_llama3_8b_architecture(oracle, vv):
 def cut(cfg, layers=2, vocab=32000):
     """The same layer shapes with fewer layers and a smaller vocabulary, so the
     oracle can run thousands of positions in seconds."""
-    return dataclasses.replace(cfg, num_hidden_layers=layers, vocab_size=vocab, eos_token_id=None,
-                               pad_token_id=None)
+    return dataclasses.replace(cfg, num_hidden_layers=layers, vocab_size=vocab, eos_token_id=0, pad_token_id=0)
 
 
 def long_context_parity(oracle, vv, cfg, n_prompt, n_new, seed=0):
