@@ -51,6 +51,7 @@ def parse_args():
     ap.add_argument("--kernel-reps", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the other BASELINE configs and the op sweep")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling small cases)")
     ap.add_argument("--batch", type=int, default=16, help="rows of the decode-batch measurement (0: skip)")
     ap.add_argument("--long-prompt", type=int, default=4096,
@@ -271,6 +272,119 @@ def stream_check(args, cfg, runner, prompt, n, rank, local_rank, barrier, vvli_b
                            f"vs {ref_path}, greedy tokens after the {len(prompt)}-token prompt"}
     barrier()
     return out
+
+
+def decode_config(vvli_b200, cfg, name, n_prompt, n_new, seed, hbm, local_rank, note):
+    """One BASELINE decode config on one GPU: the reference's own run shape (prompt, then n_new
+    greedy tokens) through vvli_cuda_generate_greedy (host prompt in, host tokens out: the
+    reference's `[N output tokens | X tok/sec | Ys decode]` line, src/main.zig:203-209), and the
+    same decode device-timed (CUDA events around the on-device loop) with its roofline."""
+    import numpy as np
+    from vvli_b200.config import decode_bytes_per_token
+    r = vvli_b200.Runner(cfg, max_seq=n_prompt + n_new + 8, device=local_rank)
+    r.fill_synthetic(seed)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, size=n_prompt).astype(np.uint32)
+    r.generate_greedy(prompt, n_new)  # warm-up (first prefill allocates)
+    r.reset()
+    toks, stats = r.generate_greedy(prompt, n_new)
+    decode_s = stats.decode_nanoseconds / 1e9
+    r.reset()
+    r.prefill(prompt, 0, logits=False)
+    pf_ms = r.last_forward_ms()
+    _, ms = r.decode(n_new - 1)
+    r.close()
+    per_tok = ms / (n_new - 1)
+    mean_pos = n_prompt + n_new // 2
+    b = decode_bytes_per_token(cfg, mean_pos)
+    ach = b / (per_tok / 1e3) / 1e9
+    return {"config": name, "prompt": n_prompt, "generated": len(toks), "distinct_tokens": len(set(toks)),
+            "e2e_generate": {"tok_per_s": (len(toks) - 1) / decode_s if decode_s > 0 else None,
+                             "decode_s": decode_s, "prefill_s": stats.prefill_nanoseconds / 1e9,
+                             "api": "vvli_cuda_generate_greedy (the reference's generation line)"},
+            "decode_tok_per_s": 1000.0 / per_tok, "prefill_ms": pf_ms,
+            "roofline": {"bound": "hbm", "bytes_per_token": b, "achieved": ach, "peak": hbm, "unit": "GB/s",
+                         "frac": ach / hbm, "frac_of_8TBs_spec": ach / 8000.0,
+                         "bytes_definition": f"weights + norms/biases + fp32 KV at mean position {mean_pos}"},
+            "note": note}
+
+
+def prefill_decode_config(vvli_b200, seed, hbm, tpeak, tpeak_src, local_rank, L=4096, n_new=32, batch=8):
+    """Llama-3.2-1B, a 4,096-token prompt, then 32 decode tokens; batch 1 and
+    batch 8 independent sequences (prefilled one after another into their slots, then decoded
+    together with vvli_cuda_forward_batch)."""
+    import numpy as np
+    from vvli_b200.config import PRESETS, decode_bytes_per_token
+    cfg = PRESETS["llama3.2-1b"]()
+    out = {"config": "llama3.2-1b 4096-token prompt + 32 decode tokens (BASELINE configs[3])"}
+    r = vvli_b200.Runner(cfg, max_seq=L + n_new + 8, device=local_rank)
+    r.fill_synthetic(seed)
+    prompt = np.random.default_rng(3).integers(0, cfg.vocab_size, size=L).astype(np.uint32)
+    r.prefill(prompt, 0, logits=False)
+    r.reset()
+    r.prefill(prompt, 0, logits=False)
+    pf = r.last_forward_ms()
+    _, ms = r.decode(n_new - 1)
+    r.close()
+    per_tok = ms / (n_new - 1)
+    b = decode_bytes_per_token(cfg, L + n_new // 2)
+    out["batch1"] = {"prefill_ms": pf, "prefill_tok_per_s": L / (pf / 1e3), "decode_tok_per_s": 1000.0 / per_tok,
+                     "decode_roofline": {"bound": "hbm", "achieved": b / (per_tok / 1e3) / 1e9, "peak": hbm,
+                                         "unit": "GB/s", "frac": b / (per_tok / 1e3) / 1e9 / hbm}}
+    rb = vvli_b200.Runner(cfg, max_seq=L + n_new + 8, device=local_rank, max_batch=batch)
+    rb.fill_synthetic(seed)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, cfg.vocab_size, size=L).astype(np.uint32) for _ in range(batch)]
+    rb.prefill_batch(prompts[:1], logits=False)  # first call allocates
+    _, am = rb.prefill_batch(prompts, logits=False)
+    pfb = rb.last_forward_ms()
+    toks, pos = list(am), [L] * batch
+    bms = []
+    for _ in range(n_new - 1):
+        _, am = rb.forward_batch(toks, pos, logits=False)
+        bms.append(rb.last_forward_ms())
+        toks, pos = list(am), [q + 1 for q in pos]
+    rb.close()
+    step = float(np.mean(bms[2:])) if len(bms) > 4 else float(np.mean(bms))
+    wb = decode_bytes_per_token(cfg, 0) - decode_bytes_per_token(cfg, -1)  # one position of KV
+    bb = decode_bytes_per_token(cfg, -1) + batch * wb * (L + n_new // 2 + 1)  # weights once + every row's KV
+    out[f"batch{batch}"] = {"prefill_ms": pfb, "prefill_tok_per_s": batch * L / (pfb / 1e3),
+                            "decode_ms_per_step": step, "decode_tok_per_s": batch / (step / 1e3),
+                            "decode_roofline": {"bound": "hbm", "bytes_per_step": bb,
+                                                "achieved": bb / (step / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                                                "frac": bb / (step / 1e3) / 1e9 / hbm},
+                            "path": "vvli_cuda_prefill_batch (slot b = sequence b), then vvli_cuda_forward_batch"}
+    return out
+
+
+OP_SHAPES = [(896, 896), (4864, 896), (896, 4864), (151936, 896), (2048, 2048), (8192, 2048), (2048, 8192),
+             (14336, 4096), (4096, 14336), (128256, 4096)]
+
+
+def op_sweep(vvli_b200, hbm, tpeak, local_rank, reps=20):
+    """y = W.x over (N, K) x M, each through the kernel the decoder uses for M rows,
+    weight copies rotated past 2x L2.  GB/s for M <= 64 (HBM-bound), TFLOP/s for M = 512."""
+    import ctypes
+    from vvli_b200 import _abi
+    rows = []
+    kinds = {0: "gemv (bulk-copy)", 1: "tcgen05 skinny GEMM", 2: "tcgen05 skinny GEMM x2 (32 rows each)",
+             3: "tcgen05 prefill GEMM"}
+    for (N, K) in OP_SHAPES:
+        for M in (1, 8, 64, 512):
+            ms, b, f, kind = ctypes.c_float(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+            rc = _abi.lib().vvli_cuda_op_bench(local_rank, M, N, K, reps, ctypes.byref(ms), ctypes.byref(b),
+                                               ctypes.byref(f), ctypes.byref(kind))
+            if rc != 0:
+                rows.append({"N": N, "K": K, "M": M, "error": _abi.lib().vvli_cuda_last_error().decode()})
+                continue
+            sec = ms.value / 1e3
+            gbs = b.value / sec / 1e9
+            tfl = f.value / sec / 1e12
+            row = {"N": N, "K": K, "M": M, "us": round(ms.value * 1e3, 2), "GB/s": round(gbs, 1),
+                   "TFLOP/s": round(tfl, 2), "kernel": kinds[kind.value]}
+            row["frac"] = round(tfl / tpeak, 3) if M == 512 else round(gbs / hbm, 3)
+            row["frac_of"] = "bf16 peak (TFLOP/s)" if M == 512 else "HBM peak (GB/s)"
+            rows.append(row)
+    return rows
 
 
 def _second_id(dist, vvli_b200, rank):
@@ -540,6 +654,21 @@ def _main(args, out_fd):
     # on rank 0's GPU; N = 1: the megakernel against the per-kernel step).
     parity = stream_check(args, cfg, runner, prompt, n, rank, local_rank, barrier, vvli_b200)
 
+    # ---- every BASELINE config (one GPU): decode configs 1 and 3, the prefill + decode config 4 at batch
+    # 1 and 8, and the op sweep of config 2.
+    configs = None
+    if n == 1 and not args.no_configs:
+        configs = {
+            "qwen2.5-0.5b": decode_config(vvli_b200, PRESETS["qwen2.5-0.5b"](), "qwen2.5-0.5b 32-token prompt, "
+                                          "64 greedy tokens (BASELINE configs[0])", 32, 64, args.seed, hbm, local_rank,
+                                          "tied embeddings, q/k/v bias"),
+            "llama3.2-1b": decode_config(vvli_b200, PRESETS["llama3.2-1b"](), "llama3.2-1b 128-token prompt, 256 "
+                                         "greedy tokens (BASELINE configs[2])", 128, 256, args.seed, hbm, local_rank,
+                                         "llama3 rope scaling"),
+            "llama3.2-1b-4096": prefill_decode_config(vvli_b200, args.seed, hbm, tpeak, tpeak_src, local_rank),
+            "op_sweep": op_sweep(vvli_b200, hbm, tpeak, local_rank),
+        }
+
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
         v, cores, sample = time_oracle(cfg, args.seed, args.cpu_seconds)
@@ -552,6 +681,7 @@ def _main(args, out_fd):
                 "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "tp_parity": parity["equal"] if parity else None, "stream_check": parity,
                 "prefill": prefill, "prefill_long": prefill_long, "sampler": sampler_line, "batch": batch,
+                "configs": configs,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clk}
         emit(line, out_fd)
     runner.close()

@@ -310,6 +310,19 @@ int vvli_cuda_trace(vvli_ctx* ctx, uint64_t* out, uint64_t cap, uint64_t* count)
 int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two_a, uint64_t seed,
                             float* max_rel_err);
 
+/* Times the isolated linear op y[M,N] = x[M,K] . W[N,K]^T (W bf16, x and y
+ * fp32; linearInto, src/llm.zig:1228-1285, over M independent rows) on
+ * `device`, through the kernel the decoder uses for M rows: the bulk-copy
+ * GEMV (M = 1, kernel_used 0), the decode-batch tensor-core GEMM (M <= 32,
+ * 1; M <= 64 as two 32-row launches, 2) or the prefill tensor-core GEMM
+ * (M > 64, 3).  Weight copies are rotated so that together they exceed twice
+ * the L2 size.  `avg_ms` = mean time per op over `reps` (CUDA events; the
+ * fp32 -> bf16 hi/lo split of x is included), `bytes` = 2NK + 4MK + 4MN,
+ * `flops` = 2MNK.  Measurement hook (BASELINE op sweep); no counterpart in
+ * the reference.  Needs N even and K a multiple of 8. */
+int vvli_cuda_op_bench(int device, int M, int N, int K, int reps, float* avg_ms, double* bytes, double* flops,
+                       int* kernel_used);
+
 /* Self-test of the tensor-core prompt attention, with no counterpart in the
  * reference: random q, K and V (head_dim d of 64 or 128, `group` q heads per
  * kv head, 2 kv heads, `tokens` query tokens at positions pos0 .., a
@@ -317,6 +330,20 @@ int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two
  * on `device`; `max_rel_err` = max |difference| / max |SIMT output|. */
 int vvli_cuda_attention_selftest(int device, int d, int group, int tokens, int pos0, uint64_t seed,
                                  float* max_rel_err);
+
+/* Prompt prefill of B independent sequences, with no counterpart in the
+ * reference (which prefills one token at a time, src/generator.zig:243-251):
+ * sequence b is tokens[sum(lengths[0..b)), + lengths[b]) at positions
+ * 0..lengths[b]-1 of sequence slot b (the KV pages vvli_cuda_forward_batch
+ * row b uses), each through the tensor-core prefill.  last_logits (may be
+ * NULL) receives B x vocab_size floats, the logits of each sequence's last
+ * token; argmax_out (may be NULL) B greedy tokens.  B <= max_batch; every
+ * length in 1..max_seq.  Decoding continues with vvli_cuda_forward_batch;
+ * slot 0 is also left ready for vvli_cuda_forward_token at position
+ * lengths[0].  VVLI_ERR_UNIMPLEMENTED when the context has no tensor-core
+ * prefill. */
+int vvli_cuda_prefill_batch(vvli_ctx* ctx, const uint32_t* tokens, const uint64_t* lengths, uint64_t B,
+                            float* last_logits, uint32_t* argmax_out);
 
 /* One decode step of `batch` independent sequences, with no counterpart in
  * the reference (which decodes one sequence): row b is sequence slot b, with

@@ -113,3 +113,48 @@ def test_batch_errors(vv):
     assert e.value.name == "ContextFull"
     logits, am = gpu.forward_batch([1, 2], [0, 0])
     assert logits.shape == (2, cfg.vocab_size) and len(am) == 2
+
+
+def test_prefill_batch_then_decode_batch(oracle, vv):
+    # Independent prompts of different lengths prefilled into slots 0..B-1
+    # (tensor-core prefill, one sequence after another), then decode steps of
+    # the whole batch; every row against the oracle's token-by-token forward.
+    cfg = dataclasses.replace(C.llama3_2_1b(), num_hidden_layers=2, vocab_size=4096)
+    B, max_seq, steps = 3, 256, 6
+    gpu = vv.Runner(cfg, max_seq=max_seq, max_batch=B)
+    gpu.fill_synthetic(0)
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, cfg.vocab_size, size=n).tolist() for n in (150, 37, 201)]
+    logits, am = gpu.prefill_batch(prompts)
+    refs = []
+    for b, p in enumerate(prompts):
+        ref = oracle.RefRunner(cfg, synthetic_seed=0, max_seq=max_seq)
+        want = ref.prefill(p, 0)
+        assert np.max(np.abs(logits[b] - want)) < TOL, b
+        assert am[b] == oracle.argmax(want), b
+        refs.append((ref, want))
+    toks = list(am)
+    pos = [len(p) for p in prompts]
+    for _ in range(steps):
+        lg, am = gpu.forward_batch(toks, pos)
+        for b, (ref, _) in enumerate(refs):
+            want = ref.forward_token(toks[b], pos[b])
+            assert np.max(np.abs(lg[b] - want)) < TOL, b
+            assert am[b] == oracle.argmax(want), b
+        toks = list(am)
+        pos = [q + 1 for q in pos]
+    # slot 0 also continues as the single sequence
+    single = gpu.forward_token(toks[0], pos[0])
+    want = refs[0][0].forward_token(toks[0], pos[0])
+    assert np.max(np.abs(single - want)) < TOL
+
+
+def test_prefill_batch_errors(vv):
+    cfg = C.tiny_qwen()
+    gpu = vv.Runner(cfg, max_seq=8, max_batch=2)
+    gpu.fill_synthetic(0)
+    for prompts, name in (([[1], [2], [3]], "InvalidArgument"), ([[1], []], "EmptyPrompt"),
+                          ([[1], [cfg.vocab_size]], "InvalidToken"), ([[1] * 9], "ContextFull")):
+        with pytest.raises(VvliError) as e:
+            gpu.prefill_batch(prompts)
+        assert e.value.name == name

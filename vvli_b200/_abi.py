@@ -66,11 +66,15 @@ SIGNATURES = {
                                              ctypes.POINTER(ctypes.c_double)]),
     "vvli_cuda_query": (ctypes.c_int, [_ctx, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
     "vvli_cuda_trace": (ctypes.c_int, [_ctx, _u64p, ctypes.c_uint64, _u64p]),
+    "vvli_cuda_op_bench": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          _f32p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                                          ctypes.POINTER(ctypes.c_int)]),
     "vvli_cuda_gemm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                ctypes.c_int, ctypes.c_uint64, _f32p]),
     "vvli_cuda_attention_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                     ctypes.c_int, ctypes.c_uint64, _f32p]),
     "vvli_cuda_forward_batch": (ctypes.c_int, [_ctx, _u32p, _u64p, ctypes.c_uint64, _f32p, _u32p]),
+    "vvli_cuda_prefill_batch": (ctypes.c_int, [_ctx, _u32p, _u64p, ctypes.c_uint64, _f32p, _u32p]),
     "vvli_cuda_argmax_rows_static": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
                                                     ctypes.c_void_p, ctypes.c_void_p]),
     "vvli_cuda_sample": (ctypes.c_int, [_ctx, ctypes.c_void_p, _f32p, _u32p, ctypes.c_uint64, _u64p, _u32p]),

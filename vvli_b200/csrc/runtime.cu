@@ -715,10 +715,12 @@ int ensure_prefill_buffers(vvli_ctx* c) {
 // Runs tokens[0, n) at positions start.. with one tensor-core GEMM per linear
 // layer and chunk (prefill of the reference's per-token loop,
 // src/generator.zig:243-251), then the LM head of the last token.
-int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start) {
+int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start, int slot = 0) {
   int st;
   if ((st = ensure_prefill_buffers(c))) return st;
   cudaStream_t s = c->stream;
+  // Sequence slot `slot` owns pages [slot * pps, (slot + 1) * pps) of the page table.
+  const int* page_table = c->page_table + static_cast<size_t>(slot) * ((c->max_seq + kPage - 1) / kPage);
   const uint16_t* W = c->w;
   const bool tp = c->tp_size > 1;
   RopeParams rope{c->cfg.rope_theta, VVLI_ROPE_INTERLEAVED, static_cast<int>(c->cfg.rope_scaling_type),
@@ -741,10 +743,10 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start) 
       g.N = c->q_rows + 2 * c->kv_rows, g.K = c->h, g.epi = GE_QKV, g.y = c->pf_q, g.ldy = c->q_rows;
       g.bias = D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv;
       g.q_rows = c->q_rows, g.kv_rows = c->kv_rows, g.d = c->d, g.nkv = c->nkv_l, g.pos0 = pos0, g.rope = rope;
-      g.k_cache = kc, g.v_cache = vc, g.page_table = c->page_table;
+      g.k_cache = kc, g.v_cache = vc, g.page_table = page_table;
       g.nk = (g.K + kGemmBK - 1) / kGemmBK;
       CK(launch_gemm_tc(c->tm_ah_hi, c->tm_ah_lo, c->tm_w[4 * l + 0], g, s));
-      PrefillAttnParams a{c->pf_q, kc, vc, c->page_table, c->pf_ahi, c->pf_alo, M, c->nq_l, c->nkv_l, c->d,
+      PrefillAttnParams a{c->pf_q, kc, vc, page_table, c->pf_ahi, c->pf_alo, M, c->nq_l, c->nkv_l, c->d,
                           c->group, pos0, 1.0f / sqrtf(static_cast<float>(c->d)), err, c->pf_kvt};
       CK(launch_prefill_attention(a, s));
       GemmParams o{};
@@ -1459,6 +1461,54 @@ int vvli_cuda_prefill(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t 
   if ((st = finish_state(c))) return st;
   cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1);
   if (argmax_out) *argmax_out = static_cast<uint32_t>(c->h_st->argmax);
+  return VVLI_OK;
+}
+
+int vvli_cuda_prefill_batch(vvli_ctx* c, const uint32_t* tokens, const uint64_t* lengths, uint64_t B,
+                            float* last_logits, uint32_t* argmax_out) {
+  if (!c || (B && (!tokens || !lengths))) return VVLI_ERR_INVALID_ARGUMENT;
+  if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (B == 0) return VVLI_OK;
+  if (B > c->max_batch) {
+    g_last_error = "prefill of " + std::to_string(B) + " sequences exceeds the context's max_batch " +
+                   std::to_string(c->max_batch);
+    return VVLI_ERR_INVALID_ARGUMENT;
+  }
+  uint64_t total = 0;
+  for (uint64_t b = 0; b < B; ++b) {
+    if (lengths[b] == 0) return VVLI_ERR_EMPTY_PROMPT;
+    if (lengths[b] > c->max_seq) return VVLI_ERR_CONTEXT_FULL;
+    total += lengths[b];
+  }
+  for (uint64_t i = 0; i < total; ++i)
+    if (tokens[i] >= c->cfg.vocab_size) return VVLI_ERR_INVALID_TOKEN;
+  if (!c->tc_prefill) {
+    g_last_error = "prefill of several sequences needs the tensor-core prefill path";
+    return VVLI_ERR_UNIMPLEMENTED;
+  }
+  CK(cudaSetDevice(c->device));
+  int st;
+  float ms_total = 0.f;
+  uint64_t off = 0;
+  for (uint64_t b = 0; b < B; ++b) {
+    const uint64_t n = lengths[b];
+    // The LM head of the sequence's last token publishes its argmax through the
+    // step state; only sequence 0 (slot 0, the single-sequence slot) also
+    // records it as its next token.
+    if ((st = stage_state(c, static_cast<int>(n - 1), static_cast<int>(b == 0 ? n : n + 1), 0))) return st;
+    CK(cudaEventRecord(c->ev0, c->stream));
+    if ((st = prefill_tc(c, tokens + off, n, 0, static_cast<int>(b)))) return st;
+    CK(cudaEventRecord(c->ev1, c->stream));
+    if ((st = copy_logits(c, last_logits ? last_logits + b * static_cast<size_t>(c->cfg.vocab_size) : nullptr)))
+      return st;
+    if ((st = finish_state(c))) return st;
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    ms_total += ms;
+    if (argmax_out) argmax_out[b] = static_cast<uint32_t>(c->h_st->argmax);
+    off += n;
+  }
+  c->last_ms = ms_total;
   return VVLI_OK;
 }
 

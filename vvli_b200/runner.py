@@ -135,6 +135,24 @@ class Runner:
                                                  am.ctypes.data_as(_u32p)))
         return out, am[: t.size].tolist()
 
+    def prefill_batch(self, prompts, logits: bool = True):
+        """Prefills independent sequences, prompts[b] into sequence slot b.
+
+        Returns (last logits [B, vocab] or None, argmax list); decoding goes on
+        with ``forward_batch`` (row b = slot b at position len(prompts[b]) ...).
+        """
+        lens = np.ascontiguousarray([len(p) for p in prompts], dtype=np.uint64)
+        t = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.uint32) for p in prompts])
+                                 if len(prompts) else np.zeros(0, np.uint32), dtype=np.uint32)
+        B = len(prompts)
+        out = np.empty((B, self.cfg.vocab_size), dtype=np.float32) if logits else None
+        am = np.zeros(max(1, B), dtype=np.uint32)
+        check(_abi.lib().vvli_cuda_prefill_batch(self._ctx, t.ctypes.data_as(_u32p),
+                                                 lens.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), B,
+                                                 None if out is None else out.ctypes.data_as(_f32p),
+                                                 am.ctypes.data_as(_u32p)))
+        return out, am[:B].tolist()
+
     def generate_greedy(self, prompt, max_new_tokens: int, eos_token_id: int | None = None):
         """On-device greedy loop; returns (tokens, vvli_generate_stats)."""
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
