@@ -57,6 +57,8 @@ def lib():
             "ref_runner_create": (vp, [cfgp, _u16p, ctypes.c_uint64, ctypes.c_int64, ctypes.c_uint64,
                                        ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int,
                                        ctypes.POINTER(ctypes.c_int)]),
+            "ref_runner_create_f32": (vp, [cfgp, _f32p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
+                                           ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
             "ref_runner_destroy": (None, [vp]),
             "ref_runner_blob": (_u16p, [vp]),
             "ref_runner_reset": (None, [vp]),
@@ -183,12 +185,22 @@ class RefRunner:
     """The oracle's llm.Runner (src/llm.zig:688-776)."""
 
     def __init__(self, cfg: Config, blob=None, synthetic_seed=None, max_seq=None, threads=0,
-                 min_rows_per_thread=64, lanes=0):
+                 min_rows_per_thread=64, lanes=0, blob_f32=None):
+        """Weights: a bf16 blob (OwnedModel layout), a synthetic seed, or `blob_f32`:
+        f32 weights in the same layout (the reference's .f32 Matrix storage, used for
+        dequantised GGUF tensors)."""
         self.cfg = cfg
         self.max_seq = max_seq or min(cfg.max_position_embeddings, 512)
         self._blob = None if blob is None else np.ascontiguousarray(blob, np.uint16)
         self._c = cfg.to_c()
         st = ctypes.c_int(0)
+        if blob_f32 is not None:
+            self._blob = np.ascontiguousarray(blob_f32, np.float32)
+            self.h = lib().ref_runner_create_f32(ctypes.byref(self._c), f32(self._blob), self._blob.size,
+                                                 self.max_seq, threads, min_rows_per_thread, lanes,
+                                                 ctypes.byref(st))
+            check(st.value)
+            return
         seed = -1 if synthetic_seed is None else int(synthetic_seed)
         self.h = lib().ref_runner_create(ctypes.byref(self._c), ptr(self._blob, _u16p),
                                          0 if self._blob is None else self._blob.size, seed, self.max_seq,

@@ -218,6 +218,15 @@ float dot_f32(const float* a, const float* b, size_t n) {
   return sum;
 }
 
+// One weight element as f32: bf16 bits widened, or an f32 weight as is
+// (Matrix storage .bf16 / .f32 of the reference).
+inline float wval(uint16_t v) { return bf16_to_f32(v); }
+inline float wval(float v) { return v; }
+template <int L>
+float dot_w(const uint16_t* a, const float* b, size_t n) { return dot_bf16<L>(a, b, n); }
+template <int L>
+float dot_w(const float* a, const float* b, size_t n) { return dot_f32<L>(a, b, n); }
+
 template <int L>
 float sum_squares(const float* v, size_t n) {  // src/llm.zig:1421-1431
   float acc[L];
@@ -338,21 +347,20 @@ size_t resolve_worker_count(size_t rows, const RuntimeOptions& o) {
   return std::max<size_t>(1, std::min(std::min(requested, useful), kMaxWorkerThreads));
 }
 
-template <int L>
-void linear_range(float* out, const uint16_t* W, size_t K, const float* x, const uint16_t* bias, size_t start,
-                  size_t end) {
+template <int L, typename T>
+void linear_range(float* out, const T* W, size_t K, const float* x, const T* bias, size_t start, size_t end) {
   for (size_t row = start; row < end; ++row)
-    out[row] = dot_bf16<L>(W + row * K, x, K) + (bias ? bf16_to_f32(bias[row]) : 0.0f);
+    out[row] = dot_w<L>(W + row * K, x, K) + (bias ? wval(bias[row]) : 0.0f);
 }
 
 // A fresh set of OS threads per call, as the reference spawns and joins
 // std.Thread workers inside every linearInto.
-template <int L>
-void linear_into(float* out, const uint16_t* W, size_t N, size_t K, const float* x, const uint16_t* bias,
+template <int L, typename T>
+void linear_into(float* out, const T* W, size_t N, size_t K, const float* x, const T* bias,
                  const RuntimeOptions& o) {
   const size_t workers = resolve_worker_count(N, o);
   if (workers == 1) {
-    linear_range<L>(out, W, K, x, bias, 0, N);
+    linear_range<L, T>(out, W, K, x, bias, 0, N);
     return;
   }
   const size_t per = (N + workers - 1) / workers;
@@ -362,9 +370,9 @@ void linear_into(float* out, const uint16_t* W, size_t N, size_t K, const float*
   for (; spawned + 1 < workers; ++spawned) {
     const size_t start = std::min(spawned * per, N);
     const size_t end = std::min(start + per, N);
-    threads.emplace_back([=] { linear_range<L>(out, W, K, x, bias, start, end); });
+    threads.emplace_back([=] { linear_range<L, T>(out, W, K, x, bias, start, end); });
   }
-  linear_range<L>(out, W, K, x, bias, std::min(spawned * per, N), N);
+  linear_range<L, T>(out, W, K, x, bias, std::min(spawned * per, N), N);
   for (auto& t : threads) t.join();
 }
 
@@ -374,6 +382,10 @@ struct Runner {
   BlobLayout layout;
   std::vector<uint16_t> owned;  // set when the runner generated its own weights
   const uint16_t* blob = nullptr;
+  // f32 weights in the same layout (element offsets of the bf16 blob), used
+  // instead of `blob` when set: the reference's .f32 Matrix storage, which
+  // dequantised GGUF tensors (Q8_0, Q4_0) need.
+  const float* blob_f32 = nullptr;
   size_t max_seq = 0;
   RuntimeOptions opts;
   int lanes = 16;
@@ -430,49 +442,60 @@ void attention_into(Runner& r, size_t layer, size_t position) {  // src/llm.zig:
   for (auto& th : ts) th.join();
 }
 
+// rmsNormInto with a weight of either storage.
 template <int L>
-void forward_current(Runner& r, size_t position) {  // src/llm.zig:720-766
+void rms_norm_w(float* out, const float* in, const uint16_t* w, size_t n, float eps) {
+  rms_norm<L>(out, in, w, nullptr, n, eps);
+}
+template <int L>
+void rms_norm_w(float* out, const float* in, const float* w, size_t n, float eps) {
+  rms_norm<L>(out, in, nullptr, w, n, eps);
+}
+
+template <int L, typename T>
+void forward_current(Runner& r, size_t position, const T* B) {  // src/llm.zig:720-766
   const auto& c = r.cfg;
   const size_t h = c.hidden_size, kvd = kv_dim(c), inter = c.intermediate_size, hd = head_dim(c);
-  const uint16_t* B = r.blob;
   for (size_t l = 0; l < c.num_hidden_layers; ++l) {
     const auto& Lo = r.layout.layers[l];
-    auto bias = [&](uint64_t off) -> const uint16_t* { return off == UINT64_MAX ? nullptr : B + off; };
+    auto bias = [&](uint64_t off) -> const T* { return off == UINT64_MAX ? nullptr : B + off; };
     std::copy(r.x.begin(), r.x.end(), r.residual.begin());
-    rms_norm<L>(r.norm.data(), r.x.data(), B + Lo.input_norm, nullptr, h, c.rms_norm_eps);
-    linear_into<L>(r.q.data(), B + Lo.q, h, h, r.norm.data(), bias(Lo.q_bias), r.opts);
-    linear_into<L>(r.k.data(), B + Lo.k, kvd, h, r.norm.data(), bias(Lo.k_bias), r.opts);
-    linear_into<L>(r.v.data(), B + Lo.v, kvd, h, r.norm.data(), bias(Lo.v_bias), r.opts);
+    rms_norm_w<L>(r.norm.data(), r.x.data(), B + Lo.input_norm, h, c.rms_norm_eps);
+    linear_into<L, T>(r.q.data(), B + Lo.q, h, h, r.norm.data(), bias(Lo.q_bias), r.opts);
+    linear_into<L, T>(r.k.data(), B + Lo.k, kvd, h, r.norm.data(), bias(Lo.k_bias), r.opts);
+    linear_into<L, T>(r.v.data(), B + Lo.v, kvd, h, r.norm.data(), bias(Lo.v_bias), r.opts);
     apply_rope(r.q.data(), c.num_attention_heads, hd, position, c);
     apply_rope(r.k.data(), c.num_key_value_heads, hd, position, c);
     std::copy(r.k.begin(), r.k.end(), r.keys.begin() + (l * r.max_seq + position) * kvd);
     std::copy(r.v.begin(), r.v.end(), r.values.begin() + (l * r.max_seq + position) * kvd);
     attention_into<L>(r, l, position);
-    linear_into<L>(r.projected.data(), B + Lo.o, h, h, r.attention.data(), nullptr, r.opts);
+    linear_into<L, T>(r.projected.data(), B + Lo.o, h, h, r.attention.data(), nullptr, r.opts);
     for (size_t i = 0; i < h; ++i) r.x[i] = r.residual[i] + r.projected[i];
     std::copy(r.x.begin(), r.x.end(), r.residual.begin());
-    rms_norm<L>(r.norm.data(), r.x.data(), B + Lo.post_norm, nullptr, h, c.rms_norm_eps);
-    linear_into<L>(r.gate.data(), B + Lo.gate, inter, h, r.norm.data(), nullptr, r.opts);
-    linear_into<L>(r.up.data(), B + Lo.up, inter, h, r.norm.data(), nullptr, r.opts);
+    rms_norm_w<L>(r.norm.data(), r.x.data(), B + Lo.post_norm, h, c.rms_norm_eps);
+    linear_into<L, T>(r.gate.data(), B + Lo.gate, inter, h, r.norm.data(), nullptr, r.opts);
+    linear_into<L, T>(r.up.data(), B + Lo.up, inter, h, r.norm.data(), nullptr, r.opts);
     for (size_t i = 0; i < inter; ++i) {
       const float g = r.gate[i];
       r.ff[i] = (g / (1.0f + std::exp(-g))) * r.up[i];
     }
-    linear_into<L>(r.projected.data(), B + Lo.down, h, inter, r.ff.data(), nullptr, r.opts);
+    linear_into<L, T>(r.projected.data(), B + Lo.down, h, inter, r.ff.data(), nullptr, r.opts);
     for (size_t i = 0; i < h; ++i) r.x[i] = r.residual[i] + r.projected[i];
     std::copy(r.x.begin(), r.x.end(), r.hidden.begin() + l * h);
   }
   if (r.skip_lm_head) return;
-  rms_norm<L>(r.norm.data(), r.x.data(), B + r.layout.final_norm, nullptr, h, c.rms_norm_eps);
+  rms_norm_w<L>(r.norm.data(), r.x.data(), B + r.layout.final_norm, h, c.rms_norm_eps);
   const uint64_t head = r.layout.lm_head == UINT64_MAX ? r.layout.embedding : r.layout.lm_head;
-  linear_into<L>(r.logits.data(), B + head, c.vocab_size, h, r.norm.data(), nullptr, r.opts);
+  linear_into<L, T>(r.logits.data(), B + head, c.vocab_size, h, r.norm.data(), nullptr, r.opts);
 }
 
 void forward_dispatch(Runner& r, size_t position) {
   switch (r.lanes) {
-    case 4: forward_current<4>(r, position); break;
-    case 8: forward_current<8>(r, position); break;
-    default: forward_current<16>(r, position); break;
+    case 4: r.blob_f32 ? forward_current<4>(r, position, r.blob_f32) : forward_current<4>(r, position, r.blob); break;
+    case 8: r.blob_f32 ? forward_current<8>(r, position, r.blob_f32) : forward_current<8>(r, position, r.blob); break;
+    default:
+      r.blob_f32 ? forward_current<16>(r, position, r.blob_f32) : forward_current<16>(r, position, r.blob);
+      break;
   }
 }
 
@@ -620,6 +643,26 @@ void* ref_runner_create(const vvli_model_config* c, const uint16_t* blob, uint64
   return r.release();
 }
 
+// A runner over f32 weights in the bf16 blob's layout (n_elements f32
+// values, kept by the caller for the runner's life): the reference's .f32
+// Matrix storage, for models whose tensors are dequantised GGUF blocks.
+void* ref_runner_create_f32(const vvli_model_config* c, const float* blob, uint64_t n_elements, uint64_t max_seq,
+                            uint64_t threads, uint64_t min_rows_per_thread, int lanes, int* status) {
+  if (!blob || n_elements < blob_layout(*c).total) {
+    *status = VVLI_ERR_INVALID_WEIGHT;
+    return nullptr;
+  }
+  // The bf16 blob pointer is never read when blob_f32 is set; a dummy keeps
+  // the bf16 creation path's checks.
+  static const uint16_t dummy = 0;
+  auto* r = static_cast<Runner*>(ref_runner_create(c, &dummy, UINT64_MAX, -1, max_seq, threads,
+                                                   min_rows_per_thread, lanes, status));
+  if (!r) return nullptr;
+  r->blob = nullptr;
+  r->blob_f32 = blob;
+  return r;
+}
+
 void ref_runner_destroy(void* p) { delete static_cast<Runner*>(p); }
 
 const uint16_t* ref_runner_blob(void* p) { return static_cast<Runner*>(p)->blob; }
@@ -635,8 +678,9 @@ int ref_runner_forward_token(void* p, uint32_t token, uint64_t position, float* 
   auto* r = static_cast<Runner*>(p);
   if (token >= r->cfg.vocab_size) return VVLI_ERR_INVALID_TOKEN;
   if (position >= r->max_seq) return VVLI_ERR_CONTEXT_FULL;
-  const uint16_t* row = r->blob + r->layout.embedding + static_cast<uint64_t>(token) * r->cfg.hidden_size;
-  for (size_t i = 0; i < r->cfg.hidden_size; ++i) r->x[i] = bf16_to_f32(row[i]);
+  const uint64_t row = r->layout.embedding + static_cast<uint64_t>(token) * r->cfg.hidden_size;
+  for (size_t i = 0; i < r->cfg.hidden_size; ++i)
+    r->x[i] = r->blob_f32 ? r->blob_f32[row + i] : bf16_to_f32(r->blob[row + i]);
   forward_dispatch(*r, position);
   if (logits_out) std::copy(r->logits.begin(), r->logits.end(), logits_out);
   return VVLI_OK;

@@ -115,3 +115,71 @@ def gguf_cfg(cfg):
     return dataclasses.replace(cfg, rope_layout=C.ROPE_INTERLEAVED, qkv_bias=False,
                                rope_scaling_type=C.ROPE_SCALING_NONE, rope_scaling_factor=1.0,
                                rope_low_freq_factor=1.0, rope_high_freq_factor=1.0, rope_original_max_position=0)
+
+
+# ---------------------------------------------------------------- GGML block quantisation (Q8_0, Q4_0)
+# The published GGML block formats that GGUF files carry for tensor types 8 and 2
+# (src/gguf.zig:35, 39 names them; ggml / llama.cpp define them): blocks of 32
+# consecutive weights along a row (the innermost GGUF dimension).
+#   Q8_0: {fp16 d; int8 q[32]}, 34 bytes, weight = d * q;  d = amax / 127,
+#         q = round(x / d).
+#   Q4_0: {fp16 d; uint8 qs[16]}, 18 bytes, weight = d * (n - 8) where
+#         qs[j] holds n of weight j in its low nibble and of weight j + 16 in
+#         its high nibble;  d = m / -8 with m the weight of largest magnitude,
+#         n = min(15, trunc(x / d + 8.5)).
+# Each returns the raw block bytes and the dequantised float32 values (exact:
+# an fp16 scale times a small integer fits a float32).
+
+def quantize_q8_0(values):
+    x = np.ascontiguousarray(values, np.float32).reshape(-1, 32)
+    amax = np.abs(x).max(axis=1)
+    d = (amax / 127.0).astype(np.float32)
+    inv = np.where(d != 0, 1.0 / np.where(d != 0, d, 1), 0).astype(np.float32)
+    q = np.clip(np.round(x * inv[:, None]), -127, 127).astype(np.int8)
+    d16 = d.astype(np.float16)
+    raw = np.zeros((x.shape[0], 34), np.uint8)
+    raw[:, :2] = d16.view(np.uint8).reshape(-1, 2)
+    raw[:, 2:] = q.view(np.uint8)
+    deq = d16.astype(np.float32)[:, None] * q.astype(np.float32)
+    return raw.tobytes(), deq.reshape(-1)
+
+
+def quantize_q4_0(values):
+    x = np.ascontiguousarray(values, np.float32).reshape(-1, 32)
+    idx = np.abs(x).argmax(axis=1)
+    m = x[np.arange(x.shape[0]), idx]
+    d = (m / -8.0).astype(np.float32)
+    inv = np.where(d != 0, 1.0 / np.where(d != 0, d, 1), 0).astype(np.float32)
+    n = np.clip(np.minimum(15, np.trunc(x * inv[:, None] + 8.5)), 0, 15).astype(np.uint8)
+    d16 = d.astype(np.float16)
+    raw = np.zeros((x.shape[0], 18), np.uint8)
+    raw[:, :2] = d16.view(np.uint8).reshape(-1, 2)
+    raw[:, 2:] = n[:, :16] | (n[:, 16:] << 4)
+    deq = d16.astype(np.float32)[:, None] * (n.astype(np.float32) - 8.0)
+    return raw.tobytes(), deq.reshape(-1)
+
+
+def quantized_model(cfg, blob, qtype, matrices=None):
+    """GGUF tensors with every matrix (or those named in `matrices`) quantised to `qtype` and
+    the rest in F32, plus the float32 blob (OwnedModel layout) of the values the file holds
+    -- the oracle's weights for the quantised model."""
+    out, f32 = [], Wt.bf16_to_f32(blob).copy()
+    quant = quantize_q8_0 if qtype == G.Q8_0 else quantize_q4_0
+    for name, off, shape, kind in Wt.tensor_entries(cfg):
+        n = int(np.prod(shape))
+        v = f32[off: off + n]
+        if kind == "mat" and (matrices is None or name in matrices):
+            raw, deq = quant(v)
+            f32[off: off + n] = deq
+            out.append((Wt.gguf_tensor_name(name), tuple(reversed(shape)), qtype, raw))
+        else:
+            out.append((Wt.gguf_tensor_name(name), tuple(reversed(shape)), G.F32, np.asarray(v, "<f4").tobytes()))
+    return out, f32
+
+
+def write_quantized_model(path, cfg, blob, qtype, matrices=None):
+    """Writes the quantised model; returns its float32 blob for the oracle."""
+    tensors, f32 = quantized_model(cfg, blob, qtype, matrices)
+    with open(path, "wb") as f:
+        f.write(gguf_bytes(model_metadata(cfg), tensors))
+    return f32

@@ -36,3 +36,19 @@ def test_parallel_attention_and_prefill_are_bit_identical(oracle):
         t = oracle.argmax(la)
         la, lb = a.forward_token(t, pos), b.forward_token(t, pos)
         assert np.array_equal(la, lb)
+
+
+def test_f32_weight_storage_matches_bf16_blob(oracle):
+    # bf16 -> f32 is exact, and dotF32 has dotBf16's summation order, so the
+    # f32-storage runner (used for dequantised GGUF tensors) must reproduce
+    # the bf16 runner bit for bit.
+    cfg = small_cfg()
+    blob = oracle.synthetic_blob(cfg, seed=5)
+    f32 = (blob.astype(np.uint32) << 16).view(np.float32)
+    a = oracle.RefRunner(cfg, blob=blob, max_seq=64)
+    b = oracle.RefRunner(cfg, blob_f32=f32, max_seq=64)
+    for pos, t in enumerate([3, 999, 17, 250, 4]):
+        la, lb = a.forward_token(t, pos), b.forward_token(t, pos)
+        assert np.array_equal(la, lb)
+        for layer in range(cfg.num_hidden_layers):
+            assert np.array_equal(a.hidden(layer), b.hidden(layer))

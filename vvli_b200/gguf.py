@@ -26,6 +26,7 @@ _SCALAR = {UINT8: "<B", INT8: "<b", UINT16: "<H", INT16: "<h", UINT32: "<I", INT
 
 # gguf.TensorType (src/gguf.zig:32-72)
 F32, F16, BF16 = 0, 1, 30
+Q4_0, Q8_0 = 2, 8  # the block-quantised types the device streams (32 weights and an fp16 scale per block)
 TENSOR_TYPES = {0, 1, 2, 3, *range(6, 31), 34, 35, 39}
 NATIVE_FLOAT = {F32, F16, BF16}  # TensorType.isNativeFloat
 
