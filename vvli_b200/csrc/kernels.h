@@ -98,6 +98,17 @@ constexpr double kAccScale = 4294967296.0;
 constexpr int kMaxFfRows = 256;  // gate|up rows per CTA kept in shared memory for ME_AXPY
 constexpr int kMaxTp = 8;
 constexpr int kMaxResRows = 64;  // rows of x a CTA can keep in shared memory (MegaParams::xres)
+// Weight storage of a matrix.  bf16: rows of K bf16.  Q8_0 / Q4_0 (GGML
+// blocks of 32 weights along a row, an fp16 scale each): a row holds its K
+// int8 quants (Q8_0) or K/2 nibble bytes (Q4_0, GGML's order: byte j of a
+// block carries weight j in the low nibble and weight j + 16 in the high
+// one), then the K/32 fp16 scales, padded to a 16-byte multiple.
+enum WeightFormat { kFmtBF16 = 0, kFmtQ8 = 1, kFmtQ4 = 2 };
+inline __host__ __device__ int quant_bytes(int fmt, int K) { return fmt == kFmtQ8 ? K : K / 2; }
+inline __host__ __device__ int row_bytes_of(int fmt, int K) {
+  return fmt == kFmtBF16 ? 2 * K : (quant_bytes(fmt, K) + K / 16 + 15) / 16 * 16;
+}
+
 constexpr int kMegaConsumerWarps = 16;
 constexpr int kMegaThreads = (kMegaConsumerWarps + 1) * 32;
 
@@ -106,8 +117,9 @@ struct MegaPhase {
   int epi;                 // MegaEpi (GEMV phases)
   int layer;
   int nphys;               // 2: gate|up pair
-  const uint16_t* W;       // [N (x nphys), K] bf16
+  const uint16_t* W;       // [N (x nphys), K] rows in format `fmt`, row_bytes apart
   int N, K, pair_offset;
+  int fmt, row_bytes;      // WeightFormat, bytes per row
   int S, SZ, cpl, R, stage_bytes;  // streaming plan (see launch_gemv)
   const uint16_t* norm_w;  // non-null: input = rmsnorm(x) * norm_w, x = the residual stream
   const float* x;          // input vector
@@ -135,6 +147,7 @@ struct MegaParams {
   StepState* st;
   int* seq_tokens;
   const uint16_t* emb;
+  int emb_fmt, emb_row_bytes;  // the embedding's WeightFormat and bytes per row
   const float* emb_in;
   int h, vocab;
   float* x;                // residual stream [h]
@@ -174,7 +187,8 @@ struct MegaParams {
 cudaError_t launch_megakernel(const MegaParams& p, int grid, size_t smem, cudaStream_t s);
 cudaError_t configure_megakernel(int max_smem_optin);
 // Streaming plan of one GEMV for the megakernel (16 consumer warps, stages <= stage_cap bytes).
-void plan_mega_gemv(MegaPhase& ph, int stage_cap);
+// ph.fmt, ph.K, ph.nphys and ph.row_bytes must be set; false when a row is too long for the plan.
+bool plan_mega_gemv(MegaPhase& ph, int stage_cap);
 size_t mega_attention_floats(int group, int d, int splits, int max_pages);
 
 // Launchers (pdl: launch with a programmatic edge to the previous kernel).

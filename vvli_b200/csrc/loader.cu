@@ -36,6 +36,7 @@
 
 #include "../../include/vvli_cuda.h"
 #include "common.cuh"
+#include "kernels.h"
 #include "loader.h"
 
 namespace vvli {
@@ -261,7 +262,7 @@ struct Mapping {
   }
 };
 
-enum SrcType { kSrcBF16, kSrcF32, kSrcF16 };
+enum SrcType { kSrcBF16, kSrcF32, kSrcF16, kSrcQ8_0, kSrcQ4_0 };
 
 // A checked source tensor: `count` elements of `type` at `data`.
 struct SrcTensor {
@@ -271,6 +272,28 @@ struct SrcTensor {
 };
 
 inline uint64_t src_elem_bytes(int type) { return type == kSrcF32 ? 4 : 2; }
+// Bytes of a GGML block of 32 weights: an fp16 scale and 32 int8 (Q8_0) or 16
+// bytes of nibbles (Q4_0).
+inline uint64_t src_block_bytes(int type) { return type == kSrcQ8_0 ? 34 : 18; }
+inline bool src_quantised(int type) { return type == kSrcQ8_0 || type == kSrcQ4_0; }
+
+// GGML blocks of `rows` rows (nb blocks each, contiguous) -> the device row
+// layout of kernels.h: the quants of every block of the row, then its scales.
+__global__ void repack_blocks_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t rows,
+                                     int nb, int q8, int row_bytes) {
+  const int qb = q8 ? 32 : 16, bb = q8 ? 34 : 18;
+  const uint64_t total = rows * static_cast<uint64_t>(nb);
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t r = i / nb;
+    const int b = static_cast<int>(i % nb);
+    const uint8_t* blk = src + i * bb;
+    uint8_t* row = dst + r * row_bytes;
+    row[nb * qb + 2 * b] = blk[0];  // fp16 scale, little endian
+    row[nb * qb + 2 * b + 1] = blk[1];
+    for (int j = 0; j < qb; ++j) row[b * qb + j] = blk[2 + j];
+  }
+}
 
 // Finds and checks the tensor of blob id `id`; returns a vvli_status.
 using Lookup = std::function<int(uint64_t id, uint64_t expect_elems, SrcTensor*, std::string*)>;
@@ -278,13 +301,56 @@ using Lookup = std::function<int(uint64_t id, uint64_t expect_elems, SrcTensor*,
 // Copies every piece: BF16 rows with one strided copy, F32 / F16 rows through
 // a device staging buffer and a rounding kernel.
 int copy_pieces(const std::vector<LoadPiece>& pieces, const Lookup& lookup, uint16_t* w, cudaStream_t s,
-                std::string* why) {
+                std::string* why, std::vector<int>* piece_fmt = nullptr) {
   void* stage = nullptr;
   constexpr size_t kStageBytes = 64ull << 20;
   int status = VVLI_OK;
-  for (const LoadPiece& p : pieces) {
+  if (piece_fmt) piece_fmt->assign(pieces.size(), kFmtBF16);
+  for (size_t pi = 0; pi < pieces.size(); ++pi) {
+    const LoadPiece& p = pieces[pi];
     SrcTensor t{};
     if ((status = lookup(p.tensor_id, p.tensor_elems, &t, why)) != VVLI_OK) break;
+    if (src_quantised(t.type)) {
+      // Whole rows of blocks (the plan of a single rank): copy the blocks of
+      // each staging chunk of rows, then repack them into the device rows.
+      const int nb = static_cast<int>(p.cols / 32);
+      const uint64_t row_src = static_cast<uint64_t>(nb) * src_block_bytes(t.type);
+      const int fmt = t.type == kSrcQ8_0 ? kFmtQ8 : kFmtQ4;
+      const int rb = row_bytes_of(fmt, static_cast<int>(p.cols));
+      if (p.cols % 32 || p.col0 || p.src_ld != p.cols || p.rows == 1) {
+        *why = "tensor " + std::to_string(p.tensor_id) + ": block-quantised tensors need whole rows of 32-weight "
+               "blocks on one rank (a norm or bias must be F32, F16 or BF16)";
+        status = VVLI_ERR_UNSUPPORTED_DTYPE;
+        break;
+      }
+      if (!stage && cudaMalloc(&stage, kStageBytes) != cudaSuccess) {
+        *why = "staging buffer for quantised tensors";
+        status = VVLI_ERR_OOM;
+        break;
+      }
+      uint8_t* dst = reinterpret_cast<uint8_t*>(w + p.group_base) + p.group_row * static_cast<uint64_t>(rb);
+      const uint8_t* src = t.data + p.row0 * row_src;
+      const uint64_t rows_per = std::max<uint64_t>(1, kStageBytes / row_src);
+      cudaError_t e = cudaSuccess;
+      for (uint64_t r = 0; r < p.rows && e == cudaSuccess; r += rows_per) {
+        const uint64_t n = std::min(rows_per, p.rows - r);
+        e = cudaMemcpyAsync(stage, src + r * row_src, n * row_src, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) {
+          const unsigned blocks = static_cast<unsigned>(std::min<uint64_t>((n * nb + 255) / 256, 4096));
+          repack_blocks_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t*>(stage), dst + r * rb, n, nb,
+                                                      fmt == kFmtQ8, rb);
+          e = cudaGetLastError();
+          if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // the staging buffer is reused
+        }
+      }
+      if (e != cudaSuccess) {
+        *why = std::string("copying tensor ") + std::to_string(p.tensor_id) + ": " + cudaGetErrorString(e);
+        status = e == cudaErrorMemoryAllocation ? VVLI_ERR_OOM : VVLI_ERR_CUDA;
+        break;
+      }
+      if (piece_fmt) (*piece_fmt)[pi] = fmt;
+      continue;
+    }
     const uint64_t esz = src_elem_bytes(t.type);
     const uint8_t* src = t.data + (p.row0 * p.src_ld + p.col0) * esz;
     uint16_t* dst = w + p.dst;
@@ -573,7 +639,7 @@ int upload_safetensors(const char* path, const std::vector<LoadPiece>& pieces, i
 }
 
 int upload_gguf(const char* path, const std::vector<LoadPiece>& pieces, int layers, uint16_t* w, cudaStream_t s,
-                std::string* why) {
+                std::string* why, std::vector<int>* piece_fmt) {
   Mapping m;
   int st = m.open_file(path, why);
   if (st != VVLI_OK) return st;
@@ -591,16 +657,24 @@ int upload_gguf(const char* path, const std::vector<LoadPiece>& pieces, int laye
       return VVLI_ERR_MISSING_TENSOR;
     }
     const GgufTensor& g = it->second;
-    const int type = g.type == 0 ? kSrcF32 : g.type == 1 ? kSrcF16 : g.type == 30 ? kSrcBF16 : -1;
+    // F32, F16, BF16 as in the reference; Q8_0 (8) and Q4_0 (2), which the
+    // reference rejects (src/llm.zig:1083), are kept as blocks for the
+    // matrices (a norm or bias must stay a native float).
+    const int type = g.type == 0 ? kSrcF32 : g.type == 1 ? kSrcF16 : g.type == 30 ? kSrcBF16
+                   : g.type == 8 ? kSrcQ8_0 : g.type == 2 ? kSrcQ4_0 : -1;
     if (type < 0) {
-      *err = name + " has GGUF tensor type " + std::to_string(g.type) + " (F32, F16 or BF16 only)";
+      *err = name + " has GGUF tensor type " + std::to_string(g.type) + " (F32, F16, BF16, Q8_0 or Q4_0 only)";
       return VVLI_ERR_UNSUPPORTED_DTYPE;
     }
     if (g.count != expect) {
       *err = "element count of " + name + " does not match the model config";
       return VVLI_ERR_INVALID_WEIGHT;
     }
-    const uint64_t len = g.count * src_elem_bytes(type);
+    if (src_quantised(type) && g.count % 32) {
+      *err = name + ": a block-quantised tensor must hold whole 32-weight blocks";
+      return VVLI_ERR_INVALID_WEIGHT;
+    }
+    const uint64_t len = src_quantised(type) ? g.count / 32 * src_block_bytes(type) : g.count * src_elem_bytes(type);
     uint64_t start, end;
     if (__builtin_add_overflow(data_start, g.offset, &start) || __builtin_add_overflow(start, len, &end) ||
         end > m.size) {
@@ -610,7 +684,7 @@ int upload_gguf(const char* path, const std::vector<LoadPiece>& pieces, int laye
     *t = SrcTensor{type, g.count, m.bytes() + start};
     return VVLI_OK;
   };
-  return copy_pieces(pieces, lookup, w, s, why);
+  return copy_pieces(pieces, lookup, w, s, why, piece_fmt);
 }
 
 }  // namespace vvli

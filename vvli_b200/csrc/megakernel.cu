@@ -20,6 +20,8 @@
 // CTA stores its partial rows into every peer's receive buffer over NVLink,
 // raises a flag on each peer, waits for the peers' flags for its rows and
 // adds the partials in rank order.
+#include <cuda_fp16.h>
+
 #include "device_fns.cuh"
 #include "kernels.h"
 
@@ -161,13 +163,15 @@ __device__ void mega_producer(const MegaParams& P, uint8_t* ring, uint64_t* full
     }
     const uint32_t slot = gi % P.nst;
     if (gi >= static_cast<uint32_t>(P.nst) && !mbar_wait(&empty[slot], ((gi / P.nst) - 1) & 1, err)) break;
-    const size_t row_bytes = static_cast<size_t>(ph.K) * 2;
+    const size_t row_bytes = static_cast<size_t>(ph.row_bytes);
     const int rows_here = min(ph.R, cur.nrows - cur.i * ph.R);
     const uint32_t bytes = static_cast<uint32_t>(rows_here * row_bytes);
     mbar_arrive_expect_tx(&full[slot], bytes * ph.nphys);
     for (int q = 0; q < ph.nphys; ++q)
       bulk_g2s(ring + static_cast<size_t>(slot) * P.slot_bytes + q * ph.R * row_bytes,
-               ph.W + static_cast<size_t>(cur.r0 + cur.i * ph.R + q * ph.pair_offset) * ph.K, bytes, &full[slot]);
+               reinterpret_cast<const uint8_t*>(ph.W) +
+                   static_cast<size_t>(cur.r0 + cur.i * ph.R + q * ph.pair_offset) * row_bytes,
+               bytes, &full[slot]);
     ++gi;
   }
   // Every issued copy lands before the CTA exits.
@@ -175,22 +179,71 @@ __device__ void mega_producer(const MegaParams& P, uint8_t* ring, uint64_t* full
   for (uint32_t i = first; i < gi; ++i) mbar_wait(&full[i % P.nst], (i / P.nst) & 1, err);
 }
 
+// ---------------------------------------------------------------- weight formats
+// A consumer lane reads 16-byte chunks of a row: 8 bf16 weights, 16 Q8_0
+// quants (half a block) or 32 Q4_0 nibbles (a whole block), and holds the
+// matching input elements in registers (32 floats in every format).
+template <int FMT>
+struct WFmt {
+  static constexpr int EPC = FMT == kFmtBF16 ? 8 : FMT == kFmtQ8 ? 16 : 32;  // weights per chunk
+  static constexpr int MAXC = 32 / EPC;                                      // chunks per lane
+};
+
+// Byte k of `t` as a float: the byte becomes the mantissa of 2^23 + byte, and
+// the bias is subtracted exactly (one permute and one add per weight, on the
+// fp32 pipe).
+VVLI_DEV float byte_as_float(uint32_t t, int k, float bias) {
+  return __int_as_float(__byte_perm(t, 0x4B000000u, 0x7540u + k)) - bias;
+}
+
+// sum_i q_i * x_i over the 16 int8 quants of a chunk (x ^ 0x80 maps q to q + 128).
+VVLI_DEV float dot16_q8(uint4 w, const float* x) {
+  const uint32_t wd[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+  float acc = 0.f;
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc = fmaf(byte_as_float(wd[m], k, 8388736.0f), x[4 * m + k], acc);  // 2^23 + 128
+  return acc;
+}
+
+// sum_i (n_i - 8) * x_i over the 32 nibbles of a Q4_0 block: byte j holds
+// weight j (low nibble) and weight j + 16 (high nibble).
+VVLI_DEV float dot32_q4(uint4 w, const float* x) {
+  const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+  float acc = 0.f;
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const uint32_t lo = wd[m] & 0x0F0F0F0Fu, hi = (wd[m] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      acc = fmaf(byte_as_float(lo, k, 8388616.0f), x[4 * m + k], acc);  // 2^23 + 8
+      acc = fmaf(byte_as_float(hi, k, 8388616.0f), x[16 + 4 * m + k], acc);
+    }
+  }
+  return acc;
+}
+
+VVLI_DEV float half_at(const uint8_t* p) { return __half2float(*reinterpret_cast<const __half*>(p)); }
+
 // ---------------------------------------------------------------- GEMV phase (consumers)
-template <int MAXC>
+template <int MAXC, int FMT>
 __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, float* part, uint64_t* full,
                           uint64_t* empty, uint32_t& gi, float* red, float* wv, int* wi, int* err, unsigned epoch0,
                           int f, float* ffs, float* xres) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int EPC = WFmt<FMT>::EPC;
   const int K = ph.K, S = ph.S, R = ph.R, nphys = ph.nphys;
   const int r0 = cta_row(ph.N, blockIdx.x, ph.row_align);
   const int nrows = cta_row(ph.N, blockIdx.x + 1, ph.row_align) - r0;
   const int nstages = (nrows + R - 1) / R;
-  const size_t row_bytes = static_cast<size_t>(K) * 2;
+  const size_t row_bytes = static_cast<size_t>(ph.row_bytes);
+  const int qbytes = quant_bytes(FMT, K);  // Q formats: the scales follow the quants
   // Inputs: this warp's slice of x times the norm weights.  RMSNorm's scale
   // is one scalar, so it multiplies the finished dot products in the
   // epilogue: W.(x*w*s) = s * W.(x*w).  Warp 0 sums the per-CTA squares
   // meanwhile; nothing waits for it before the rows are consumed.
-  const int cpr = K >> 3;
+  const int cpr = K / EPC;
   const int split = warp % S;
   const int cbeg = split * ph.SZ;
   const int cend = min(cpr, cbeg + ph.SZ);
@@ -205,16 +258,17 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
 #pragma unroll
     for (int k = 0; k < 8; ++k) ssq_lane += v[k];
   }
-  float xr[MAXC][8];
+  float xr[MAXC][EPC];
 #pragma unroll
   for (int j = 0; j < MAXC; ++j) {
     const int c = cbeg + lane + kWarp * j;
     if (j < ph.cpl && c < cend) {
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(ph.x + c * 8));
-      const float4 b = __ldcg(reinterpret_cast<const float4*>(ph.x + c * 8 + 4));
-      xr[j][0] = a.x, xr[j][1] = a.y, xr[j][2] = a.z, xr[j][3] = a.w;
-      xr[j][4] = b.x, xr[j][5] = b.y, xr[j][6] = b.z, xr[j][7] = b.w;
-      if (ph.acc_in) {  // the previous layer's down_proj, still in its fixed-point accumulator
+#pragma unroll
+      for (int q = 0; q < EPC / 4; ++q) {
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
+        xr[j][4 * q] = a.x, xr[j][4 * q + 1] = a.y, xr[j][4 * q + 2] = a.z, xr[j][4 * q + 3] = a.w;
+      }
+      if (FMT == kFmtBF16 && ph.acc_in) {  // the previous layer's down_proj, still in its fixed-point accumulator
         const longlong2* ap = reinterpret_cast<const longlong2*>(ph.acc_in + c * 8);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -228,15 +282,18 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
         }
       }
       if (ph.norm_w) {
-        const uint4 wn = *reinterpret_cast<const uint4*>(ph.norm_w + c * 8);
-        const float nw[8] = {bf16_lo(wn.x), bf16_hi(wn.x), bf16_lo(wn.y), bf16_hi(wn.y),
-                             bf16_lo(wn.z), bf16_hi(wn.z), bf16_lo(wn.w), bf16_hi(wn.w)};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) xr[j][e] = xr[j][e] * nw[e];
+        for (int q = 0; q < EPC / 8; ++q) {
+          const uint4 wn = *reinterpret_cast<const uint4*>(ph.norm_w + c * EPC + 8 * q);
+          const float nw[8] = {bf16_lo(wn.x), bf16_hi(wn.x), bf16_lo(wn.y), bf16_hi(wn.y),
+                               bf16_lo(wn.z), bf16_hi(wn.z), bf16_lo(wn.w), bf16_hi(wn.w)};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) xr[j][8 * q + e] = xr[j][8 * q + e] * nw[e];
+        }
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) xr[j][e] = 0.f;
+      for (int e = 0; e < EPC; ++e) xr[j][e] = 0.f;
     }
   }
   auto row_dot = [&](const uint8_t* rp) {
@@ -244,7 +301,16 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
 #pragma unroll
     for (int j = 0; j < MAXC; ++j) {
       const int c = cbeg + lane + kWarp * j;
-      if (j < ph.cpl && c < cend) acc += dot8(*reinterpret_cast<const uint4*>(rp + c * 16), xr[j]);
+      if (j < ph.cpl && c < cend) {
+        const uint4 w = *reinterpret_cast<const uint4*>(rp + c * 16);
+        if constexpr (FMT == kFmtBF16) {
+          acc += dot8(w, xr[j]);
+        } else if constexpr (FMT == kFmtQ8) {  // weight = d * q, d shared by the two chunks of a block
+          acc = fmaf(dot16_q8(w, xr[j]), half_at(rp + qbytes + (c >> 1) * 2), acc);
+        } else {  // weight = d * (n - 8)
+          acc = fmaf(dot32_q4(w, xr[j]), half_at(rp + qbytes + c * 2), acc);
+        }
+      }
     }
     return acc;
   };
@@ -795,8 +861,21 @@ __device__ void mega_embed(const MegaParams& P, float* red, int* err, float* xre
     tok = 0;
   }
   float ss = 0.f;
+  const uint8_t* erow = reinterpret_cast<const uint8_t*>(P.emb) + static_cast<size_t>(tok) * P.emb_row_bytes;
   for (int r = r0 + tid; r < r1; r += kNC) {
-    const float v = P.st->use_embedding ? P.emb_in[r] : bf16_to_f32(P.emb[static_cast<size_t>(tok) * P.h + r]);
+    float v;
+    if (P.st->use_embedding) {
+      v = P.emb_in[r];
+    } else if (P.emb_fmt == kFmtQ8) {  // d * q
+      v = half_at(erow + P.h + (r >> 5) * 2) * static_cast<float>(static_cast<int8_t>(erow[r]));
+    } else if (P.emb_fmt == kFmtQ4) {  // d * (n - 8), GGML nibble order
+      const int b = r >> 5, e = r & 31;
+      const uint8_t byte = erow[b * 16 + (e & 15)];
+      const int nib = e < 16 ? (byte & 15) : (byte >> 4);
+      v = half_at(erow + P.h / 2 + b * 2) * static_cast<float>(nib - 8);
+    } else {
+      v = bf16_to_f32(reinterpret_cast<const uint16_t*>(erow)[r]);
+    }
     P.x[r] = v;
     if (P.xres) xres[r - r0] = v;
     ss = fmaf(v, v, ss);
@@ -847,7 +926,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
     } else if (ph.epi == ME_AXPY) {
       mega_axpy(P, ph, ring, full, empty, gi, ffs, err, f);
     } else {
-      mega_gemv<4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres);  // cpl <= 4
+      if (ph.fmt == kFmtQ8)
+        mega_gemv<2, kFmtQ8>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres);
+      else if (ph.fmt == kFmtQ4)
+        mega_gemv<1, kFmtQ4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres);
+      else
+        mega_gemv<4, kFmtBF16>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres);
     }
     if (tid == 0) trace_mark(P, f, 3);
     if (f + 1 < P.nphases && P.phases[f + 1].no_barrier) {
@@ -884,19 +968,24 @@ cudaError_t launch_megakernel(const MegaParams& p, int grid, size_t smem, cudaSt
   return cudaLaunchKernelEx(&cfg, decode_megakernel, p);
 }
 
-void plan_mega_gemv(MegaPhase& ph, int stage_cap) {
-  const int cpr = ph.K / 8;
-  const size_t row_bytes = static_cast<size_t>(ph.K) * 2;
+bool plan_mega_gemv(MegaPhase& ph, int stage_cap) {
+  const int epc = ph.fmt == kFmtBF16 ? WFmt<kFmtBF16>::EPC : ph.fmt == kFmtQ8 ? WFmt<kFmtQ8>::EPC : WFmt<kFmtQ4>::EPC;
+  const int maxc = 32 / epc;
+  if (ph.K % (ph.fmt == kFmtBF16 ? 8 : 32)) return false;
+  const int cpr = ph.K / epc;
+  const size_t row_bytes = static_cast<size_t>(ph.row_bytes);
   int S = 1;
-  while (S < kCW && S * 128 < cpr) S *= 2;
+  while (S < kCW && S * kWarp * maxc < cpr) S *= 2;
   ph.S = S;
   ph.SZ = (cpr + S - 1) / S;
   ph.cpl = (ph.SZ + kWarp - 1) / kWarp;
+  if (ph.cpl > maxc) return false;
   const int want_pairs = 2 * kCW;
   int R = (want_pairs + S * ph.nphys - 1) / (S * ph.nphys);
   while (R > 1 && R * row_bytes * ph.nphys > static_cast<size_t>(stage_cap)) R /= 2;
   ph.R = R < 1 ? 1 : R;
   ph.stage_bytes = static_cast<int>(ph.R * row_bytes * ph.nphys);
+  return true;
 }
 
 size_t mega_attention_floats(int group, int d, int splits, int max_pages) {

@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <map>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -138,10 +139,15 @@ struct Piece {
   uint64_t src;        // element offset of the tensor in the host blob
   uint64_t rows, cols, src_ld, row0, col0;
   int kind;            // 0 matrix/bias, 1 norm weights
+  // The fused matrix this piece belongs to (q|k|v, gate|up, or the matrix
+  // itself): its element offset and this piece's first row in it.  A
+  // quantised matrix is stored from the group's offset with its own row size.
+  uint64_t group_base, group_row;
 };
 
 struct DevLayer {
   uint64_t in_norm, w_qkv, b_qkv, w_o, post, w_gu, w_down;
+  int f_qkv = kFmtBF16, f_o = kFmtBF16, f_gu = kFmtBF16, f_down = kFmtBF16;  // WeightFormat of each matrix
 };
 
 }  // namespace
@@ -161,6 +167,14 @@ struct vvli_ctx {
   bool lm_aliases_emb = false;
   uint16_t* w = nullptr;
   bool loaded = false;
+  // Matrix formats (WeightFormat): bf16 unless a GGUF file held Q8_0 / Q4_0
+  // blocks; `quant` when any matrix is block-quantised.
+  int f_emb = kFmtBF16, f_lm = kFmtBF16;
+  bool quant = false;
+  int smem_optin = 0;
+  int plan_sig = 0;              // formats the megakernel plan was made for (0: all bf16)
+  bool want_mega = false;        // megakernel wanted (VVLI_MEGAKERNEL not 0)
+  bool tc_prefill_planned = false;
   // KV cache and step buffers
   float* kv = nullptr;
   size_t kv_layer_floats = 0;  // K (or V) floats per layer
@@ -301,7 +315,10 @@ void plan_weights(vvli_ctx* c) {
     return s;
   };
   auto mat = [&](uint64_t dst, uint64_t tid, uint64_t src, uint64_t rows, uint64_t cols, uint64_t ld, uint64_t row0,
-                 uint64_t col0, int kind) { c->pieces.push_back({dst, tid, src, rows, cols, ld, row0, col0, kind}); };
+                 uint64_t col0, int kind, uint64_t group_base = UINT64_MAX, uint64_t group_row = 0) {
+    c->pieces.push_back({dst, tid, src, rows, cols, ld, row0, col0, kind, group_base == UINT64_MAX ? dst : group_base,
+                         group_row});
+  };
   c->off_emb = alloc(static_cast<uint64_t>(c->V) * h);
   mat(c->off_emb, 0, b.emb, c->V, h, h, 0, 0, 0);
   c->lay.resize(c->L);
@@ -313,9 +330,9 @@ void plan_weights(vvli_ctx* c) {
     D.in_norm = alloc(h);
     mat(D.in_norm, base + 0, B.in_norm, 1, h, h, 0, 0, 1);
     D.w_qkv = alloc((qr + 2 * kr) * h);
-    mat(D.w_qkv, base + 1, B.q, qr, h, h, r * qr, 0, 0);
-    mat(D.w_qkv + qr * h, base + 3, B.k, kr, h, h, r * kr, 0, 0);
-    mat(D.w_qkv + (qr + kr) * h, base + 5, B.v, kr, h, h, r * kr, 0, 0);
+    mat(D.w_qkv, base + 1, B.q, qr, h, h, r * qr, 0, 0, D.w_qkv, 0);
+    mat(D.w_qkv + qr * h, base + 3, B.k, kr, h, h, r * kr, 0, 0, D.w_qkv, qr);
+    mat(D.w_qkv + (qr + kr) * h, base + 5, B.v, kr, h, h, r * kr, 0, 0, D.w_qkv, qr + kr);
     D.b_qkv = UINT64_MAX;
     if (cfg.qkv_bias) {
       D.b_qkv = alloc(qr + 2 * kr);
@@ -328,8 +345,8 @@ void plan_weights(vvli_ctx* c) {
     D.post = alloc(h);
     mat(D.post, base + 8, B.post, 1, h, h, 0, 0, 1);
     D.w_gu = alloc(2 * Il * h);
-    mat(D.w_gu, base + 9, B.gate, Il, h, h, r * Il, 0, 0);
-    mat(D.w_gu + Il * h, base + 10, B.up, Il, h, h, r * Il, 0, 0);
+    mat(D.w_gu, base + 9, B.gate, Il, h, h, r * Il, 0, 0, D.w_gu, 0);
+    mat(D.w_gu + Il * h, base + 10, B.up, Il, h, h, r * Il, 0, 0, D.w_gu, Il);
     D.w_down = alloc(h * Il);
     mat(D.w_down, base + 11, B.down, h, Il, c->I, 0, r * Il, 0);
   }
@@ -386,13 +403,15 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   // weight stream (measured on Llama-3-8B).
   const int stage_cap = getenv("VVLI_MEGA_STAGE_CAP") ? std::max(4096, atoi(getenv("VVLI_MEGA_STAGE_CAP"))) : 65536;
   std::vector<MegaPhase> ph;
+  bool plan_ok = true;
   auto gemv = [&](int epi, int layer, const uint16_t* w, int N, int K, int nphys, const uint16_t* norm,
-                  const float* x, float* y, const uint16_t* bias, int ar_index) {
+                  const float* x, float* y, const uint16_t* bias, int ar_index, int fmt = kFmtBF16) {
     MegaPhase m{};
     m.kind = MK_GEMV, m.epi = epi, m.layer = layer, m.nphys = nphys, m.W = w, m.N = N, m.K = K;
+    m.fmt = fmt, m.row_bytes = row_bytes_of(fmt, K);
     m.pair_offset = nphys == 2 ? N : 0;
     m.norm_w = norm, m.x = x, m.y = y, m.bias = bias, m.ar_index = ar_index, m.row_align = 1;
-    plan_mega_gemv(m, stage_cap);
+    plan_ok = plan_mega_gemv(m, stage_cap) && plan_ok;
     ph.push_back(m);
   };
   MegaPhase e{};
@@ -405,19 +424,22 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   // 3.74 ms per token).  Each CTA's gate|up rows must fit the shared-memory ff
   // buffer and a thread owns at most 16 outputs.
   const char* fd = getenv("VVLI_MEGA_FUSED_DOWN");
-  const bool fused = fd && fd[0] == '1' && c->tp_size == 1 && c->h % 8 == 0 && c->h <= 2 * 8 * kMegaConsumerWarps * 32 &&
+  const bool fused = fd && fd[0] == '1' && c->tp_size == 1 && !c->quant && c->h % 8 == 0 &&
+                     c->h <= 2 * 8 * kMegaConsumerWarps * 32 &&
                      (c->I_l + c->sm_count - 1) / c->sm_count + 1 <= kMaxFfRows;
   long long* acc[2] = {nullptr, nullptr};
-  if (fused) {
+  if (fused && !c->w_downT) {
     if (dalloc(&c->w_downT, static_cast<size_t>(c->L) * c->I_l * c->h) || dalloc(&c->acc, 2 * static_cast<size_t>(c->h)))
       return false;
+  }
+  if (fused) {
     acc[0] = c->acc;
     acc[1] = c->acc + c->h;
   }
   for (int l = 0; l < c->L; ++l) {
     const DevLayer& D = c->lay[l];
     gemv(ME_QKV, l, W + D.w_qkv, c->q_rows + 2 * c->kv_rows, c->h, 1, W + D.in_norm, c->x, c->qkv,
-         D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv, 0);
+         D.b_qkv == UINT64_MAX ? nullptr : W + D.b_qkv, 0, D.f_qkv);
     ph.back().k_cache = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
     ph.back().v_cache = ph.back().k_cache + c->kv_layer_floats;
     ph.back().row_align = 2;
@@ -427,7 +449,7 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
     a.k_cache = c->kv + static_cast<size_t>(2 * l) * c->kv_layer_floats;
     a.v_cache = a.k_cache + c->kv_layer_floats;
     ph.push_back(a);
-    gemv(ME_RESIDUAL, l, W + D.w_o, c->h, c->q_rows, 1, nullptr, c->attn, c->x, nullptr, 2 * l);
+    gemv(ME_RESIDUAL, l, W + D.w_o, c->h, c->q_rows, 1, nullptr, c->attn, c->x, nullptr, 2 * l, D.f_o);
     if (fused && l > 0) ph.back().acc_fold = acc[(l - 1) & 1];
     if (fused) {
       gemv(ME_SILU, l, W + D.w_gu, c->I_l, c->h, 2, W + D.post, c->x, nullptr, nullptr, 0);
@@ -435,17 +457,18 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
       MegaPhase dn{};
       dn.kind = MK_GEMV, dn.epi = ME_AXPY, dn.layer = l, dn.nphys = 1, dn.no_barrier = 1, dn.row_align = 1;
       dn.W = c->w_downT + static_cast<size_t>(l) * c->I_l * c->h, dn.N = c->I_l, dn.K = c->h;
-      dn.S = 1, dn.SZ = 0, dn.cpl = 0;
+      dn.S = 1, dn.SZ = 0, dn.cpl = 0, dn.fmt = kFmtBF16, dn.row_bytes = 2 * c->h;
       dn.R = std::max(1, 65536 / (2 * c->h));
       dn.stage_bytes = dn.R * 2 * c->h;
       dn.acc_out = acc[l & 1];
       ph.push_back(dn);
     } else {
-      gemv(ME_SILU, l, W + D.w_gu, c->I_l, c->h, 2, W + D.post, c->x, c->ff, nullptr, 0);
-      gemv(ME_RESIDUAL, l, W + D.w_down, c->h, c->I_l, 1, nullptr, c->ff, c->x, nullptr, 2 * l + 1);
+      gemv(ME_SILU, l, W + D.w_gu, c->I_l, c->h, 2, W + D.post, c->x, c->ff, nullptr, 0, D.f_gu);
+      gemv(ME_RESIDUAL, l, W + D.w_down, c->h, c->I_l, 1, nullptr, c->ff, c->x, nullptr, 2 * l + 1, D.f_down);
     }
   }
-  gemv(ME_ARGMAX, -1, W + c->off_lm, c->V_lr, c->h, 1, W + c->off_final, c->x, c->logits, nullptr, 0);
+  gemv(ME_ARGMAX, -1, W + c->off_lm, c->V_lr, c->h, 1, W + c->off_final, c->x, c->logits, nullptr, 0, c->f_lm);
+  if (!plan_ok) return false;
   if (fused) ph.back().acc_in = acc[(c->L - 1) & 1], ph.back().hidden_layer = c->L - 1;
   for (MegaPhase& m : ph)
     if (!m.acc_in) m.hidden_layer = -1;
@@ -455,7 +478,6 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   size_t part = mega_attention_floats(c->group, c->d, c->mega_splits, c->max_pages);
   for (const MegaPhase& m : ph) {
     if (m.kind != MK_GEMV) continue;
-    if (m.cpl > 4) return false;
     if (c->group > 8 || (kMegaThreads - 32) % c->d || (kMegaThreads - 32) / c->d * 16 < kPage) return false;
     slot = std::max(slot, m.stage_bytes);
     part = std::max(part, static_cast<size_t>((m.N + grid - 1) / grid + 2) * m.nphys * m.S);
@@ -467,6 +489,8 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   nst = std::min(nst, getenv("VVLI_MEGA_STAGES") ? std::max(2, atoi(getenv("VVLI_MEGA_STAGES"))) : 2);
   if (nst < 2) return false;
   c->mega_smem = static_cast<size_t>(nst) * slot + ((part + 1) & ~size_t(1)) * 4 + 2 * nst * sizeof(uint64_t);
+  if (c->d_phases) cudaFree(c->d_phases);  // a re-plan after a load that changed the weight formats
+  c->d_phases = nullptr;
   if (cudaMalloc(&c->d_phases, ph.size() * sizeof(MegaPhase)) != cudaSuccess) return false;
   if (cudaMemcpy(c->d_phases, ph.data(), ph.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice) != cudaSuccess)
     return false;
@@ -481,6 +505,8 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   P.st = c->st;
   P.seq_tokens = c->seq_tokens;
   P.emb = W + c->off_emb;
+  P.emb_fmt = c->f_emb;
+  P.emb_row_bytes = row_bytes_of(c->f_emb, c->h);
   P.emb_in = c->emb_in;
   P.h = c->h;
   P.vocab = c->V;
@@ -517,6 +543,8 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   P.tp = c->tp_size;
   P.rank = c->tp_rank;
   const char* tr = getenv("VVLI_TRACE");
+  if (c->trace) cudaFree(c->trace);
+  c->trace = nullptr;
   if (tr && tr[0] == '1' &&
       cudaMalloc(&c->trace, ph.size() * grid * 6 * sizeof(uint64_t)) == cudaSuccess) {
     cudaMemset(c->trace, 0, ph.size() * grid * 6 * sizeof(uint64_t));
@@ -1201,11 +1229,13 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
   {
     const char* tc_env = getenv("VVLI_TC_PREFILL");
     if (!(tc_env && tc_env[0] == '0') && configure_gemm_tc(smem_optin) == cudaSuccess && plan_tc_prefill(c) == VVLI_OK)
-      c->tc_prefill = true;
+      c->tc_prefill = c->tc_prefill_planned = true;
     cudaGetLastError();
   }
+  c->smem_optin = smem_optin;
   const char* mega_env = getenv("VVLI_MEGAKERNEL");
   const bool want_mega = !(mega_env && mega_env[0] == '0') && tp_size <= kMaxTp;
+  c->want_mega = want_mega;
   if (want_mega) {
     if ((e = configure_megakernel(smem_optin))) return fail(cuda_fail(e, "configure_megakernel"));
     c->use_mega = plan_megakernel(c, smem_optin);
@@ -1286,7 +1316,81 @@ static int setup_tp_peers(vvli_ctx* c) {
   return VVLI_OK;
 }
 
+// Bytes of every weight matrix of this rank as stored (bf16 rows or quantised
+// rows with their scales): what one decode step streams besides norms and KV.
+static uint64_t weight_stream_bytes(const vvli_ctx* c) {
+  uint64_t b = 0;
+  for (const DevLayer& D : c->lay) {
+    b += static_cast<uint64_t>(c->q_rows + 2 * c->kv_rows) * row_bytes_of(D.f_qkv, c->h);
+    b += static_cast<uint64_t>(c->h) * row_bytes_of(D.f_o, c->q_rows);
+    b += 2ull * c->I_l * row_bytes_of(D.f_gu, c->h);
+    b += static_cast<uint64_t>(c->h) * row_bytes_of(D.f_down, c->I_l);
+  }
+  return b + static_cast<uint64_t>(c->V_lr) * row_bytes_of(c->f_lm, c->h);
+}
+
+// Every matrix back to bf16 (the blob, safetensors and synthetic loads).
+static void set_bf16_formats(vvli_ctx* c) {
+  for (DevLayer& D : c->lay) D.f_qkv = D.f_o = D.f_gu = D.f_down = kFmtBF16;
+  c->f_emb = c->f_lm = kFmtBF16;
+  c->quant = false;
+}
+
+// Formats of a GGUF load from the format each piece was stored in: the pieces
+// of a fused matrix (q|k|v, gate|up) must agree.  Block-quantised matrices
+// run only in the single-GPU decode megakernel.
+static int set_loaded_formats(vvli_ctx* c, const std::vector<int>& piece_fmt) {
+  std::map<uint64_t, int> fmt;  // tensor id -> format
+  for (size_t i = 0; i < c->pieces.size(); ++i) fmt[c->pieces[i].tensor_id] = piece_fmt[i];
+  auto f = [&](uint64_t id) { auto it = fmt.find(id); return it == fmt.end() ? static_cast<int>(kFmtBF16) : it->second; };
+  bool ok = true;
+  c->quant = false;
+  for (int l = 0; l < c->L; ++l) {
+    DevLayer& D = c->lay[l];
+    const uint64_t base = 1 + 12ull * l;
+    D.f_qkv = f(base + 1);
+    ok = ok && f(base + 3) == D.f_qkv && f(base + 5) == D.f_qkv;
+    D.f_o = f(base + 7);
+    D.f_gu = f(base + 9);
+    ok = ok && f(base + 10) == D.f_gu;
+    D.f_down = f(base + 11);
+    c->quant = c->quant || D.f_qkv || D.f_o || D.f_gu || D.f_down;
+  }
+  c->f_emb = f(0);
+  c->f_lm = c->lm_aliases_emb ? c->f_emb : f(2 + 12ull * c->L);
+  c->quant = c->quant || c->f_emb || c->f_lm;
+  if (!ok) {
+    g_last_error = "q, k and v (and gate and up) of a layer must share one tensor type";
+    set_bf16_formats(c);
+    return VVLI_ERR_UNSUPPORTED_DTYPE;
+  }
+  if (c->quant && c->tp_size > 1) {
+    g_last_error = "block-quantised (Q8_0 / Q4_0) GGUF tensors run on one GPU (tp_size 1)";
+    set_bf16_formats(c);
+    return VVLI_ERR_UNSUPPORTED_DTYPE;
+  }
+  return VVLI_OK;
+}
+
 static int after_load(vvli_ctx* c) {
+  // The megakernel plan follows the matrix formats: plan again when a load
+  // changed them (tp = 1 only; quantised loads require it).
+  int sig = c->f_emb * 3 + c->f_lm;
+  for (const DevLayer& D : c->lay) sig = sig * 7 + D.f_qkv * 27 + D.f_o * 9 + D.f_gu * 3 + D.f_down;
+  if (sig != c->plan_sig && c->tp_size == 1 && c->smem_optin) {
+    c->use_mega = c->want_mega && plan_megakernel(c, c->smem_optin);
+    c->plan_sig = sig;
+    // the new plan starts its barrier count and step epoch from zero
+    CK(cudaMemsetAsync(c->bar, 0, sizeof(unsigned long long), c->stream));
+    CK(cudaMemsetAsync(c->epoch, 0, sizeof(unsigned), c->stream));
+  }
+  c->tc_prefill = c->tc_prefill_planned && !c->quant;
+  if (c->quant && !c->use_mega) {
+    g_last_error = "block-quantised weights need the decode megakernel (VVLI_MEGAKERNEL unset and a plan that fits)";
+    set_bf16_formats(c);
+    c->loaded = false;
+    return VVLI_ERR_UNSUPPORTED_DTYPE;
+  }
   // Split-half RoPE: put rotary pairs on adjacent q/k rows (device layout).
   if (c->cfg.rope_layout == VVLI_ROPE_SPLIT_HALF) {
     const int rows = c->q_rows + c->kv_rows;
@@ -1318,6 +1422,7 @@ int vvli_cuda_load_weights(vvli_ctx* c, const uint16_t* blob, uint64_t n) {
   if (!c || !blob) return VVLI_ERR_INVALID_ARGUMENT;
   CK(cudaSetDevice(c->device));
   if (n < blob_layout(c->cfg).total) return VVLI_ERR_INVALID_WEIGHT;
+  set_bf16_formats(c);
   for (const Piece& p : c->pieces) {
     const uint16_t* src = blob + p.src + p.row0 * p.src_ld + p.col0;
     if (p.rows == 1) {
@@ -1351,7 +1456,7 @@ static std::vector<LoadPiece> load_pieces(const vvli_ctx* c) {
   lp.reserve(c->pieces.size());
   for (const Piece& p : c->pieces)
     lp.push_back(LoadPiece{p.tensor_id, tensor_elems(c->cfg, p.tensor_id), p.dst, p.rows, p.cols, p.src_ld, p.row0,
-                           p.col0});
+                           p.col0, p.group_base, p.group_row});
   return lp;
 }
 
@@ -1359,6 +1464,7 @@ int vvli_cuda_load_safetensors(vvli_ctx* c, const char* path) {
   if (!c || !path) return VVLI_ERR_INVALID_ARGUMENT;
   CK(cudaSetDevice(c->device));
   std::string why;
+  set_bf16_formats(c);
   const int st = upload_safetensors(path, load_pieces(c), c->L, c->w, c->stream, &why);
   if (st != VVLI_OK) {
     g_last_error = why;
@@ -1376,17 +1482,21 @@ int vvli_cuda_load_gguf(vvli_ctx* c, const char* path) {
   }
   CK(cudaSetDevice(c->device));
   std::string why;
-  const int st = upload_gguf(path, load_pieces(c), c->L, c->w, c->stream, &why);
+  std::vector<int> piece_fmt;
+  int st = upload_gguf(path, load_pieces(c), c->L, c->w, c->stream, &why, &piece_fmt);
   if (st != VVLI_OK) {
     g_last_error = why;
+    set_bf16_formats(c);
     return st;
   }
+  if ((st = set_loaded_formats(c, piece_fmt))) return st;
   return after_load(c);
 }
 
 int vvli_cuda_fill_synthetic(vvli_ctx* c, uint64_t seed) {
   if (!c) return VVLI_ERR_INVALID_ARGUMENT;
   CK(cudaSetDevice(c->device));
+  set_bf16_formats(c);
   for (const Piece& p : c->pieces)
     CK(launch_synth_fill(c->w + p.dst, tensor_key(seed, p.tensor_id), p.rows, p.cols, p.src_ld, p.row0, p.col0,
                          p.kind, c->stream));
@@ -1468,6 +1578,10 @@ int vvli_cuda_prefill_batch(vvli_ctx* c, const uint32_t* tokens, const uint64_t*
                             float* last_logits, uint32_t* argmax_out) {
   if (!c || (B && (!tokens || !lengths))) return VVLI_ERR_INVALID_ARGUMENT;
   if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (c->quant) {
+    g_last_error = "prefill of several sequences runs on bf16 weights only (this model is block-quantised)";
+    return VVLI_ERR_UNIMPLEMENTED;
+  }
   if (B == 0) return VVLI_OK;
   if (B > c->max_batch) {
     g_last_error = "prefill of " + std::to_string(B) + " sequences exceeds the context's max_batch " +
@@ -1516,6 +1630,10 @@ int vvli_cuda_forward_batch(vvli_ctx* c, const uint32_t* tokens, const uint64_t*
                             float* logits_out, uint32_t* argmax_out) {
   if (!c || (B && (!tokens || !positions))) return VVLI_ERR_INVALID_ARGUMENT;
   if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (c->quant) {
+    g_last_error = "decode batches run on bf16 weights only (this model is block-quantised)";
+    return VVLI_ERR_UNIMPLEMENTED;
+  }
   if (B == 0) return VVLI_OK;
   if (B > c->max_batch) {
     g_last_error = "batch of " + std::to_string(B) + " rows exceeds the context's max_batch " + std::to_string(c->max_batch);
@@ -1777,6 +1895,10 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
 int vvli_cuda_time_kernel(vvli_ctx* c, int kernel, int reps, float* avg_ms, double* bytes) {
   if (!c || !avg_ms || !bytes || reps <= 0 || kernel < 0 || kernel > 4) return VVLI_ERR_INVALID_ARGUMENT;
   if (!c->loaded) return VVLI_ERR_NOT_LOADED;
+  if (c->quant) {
+    g_last_error = "the standalone decode kernels stream bf16 weights only (this model is block-quantised)";
+    return VVLI_ERR_UNIMPLEMENTED;
+  }
   CK(cudaSetDevice(c->device));
   const uint16_t* W = c->w;
   const double h = c->h;
@@ -1847,6 +1969,8 @@ int vvli_cuda_query(vvli_ctx* c, const char* key, double* out) {
     *out = c->use_mega ? 1 : 1 + 5.0 * c->L + 1 + (c->tp_size > 1 ? 1 : 0);
   else if (k == "weight_bytes") *out = static_cast<double>(c->weight_elems) * 2;
   else if (k == "tc_prefill") *out = c->tc_prefill ? 1 : 0;
+  else if (k == "quantized") *out = c->quant ? 1 : 0;
+  else if (k == "weight_stream_bytes") *out = static_cast<double>(weight_stream_bytes(c));
   else return VVLI_ERR_INVALID_ARGUMENT;
   return VVLI_OK;
 }
