@@ -387,6 +387,32 @@ def op_sweep(vvli_b200, hbm, tpeak, local_rank, reps=20):
     return rows
 
 
+def quantized_decode(vvli_b200, cfg, prompt, seed, hbm, local_rank, steps=64, warmup=4):
+    """8B decode with every matrix block-quantised on the device (GGML Q8_0 and Q4_0, the GGUF
+    types the reference names but rejects): the same megakernel streaming the blocks and
+    dequantising them in registers.  Roofline bytes = the stored matrix rows (quants + fp16
+    scales) + norms + fp32 KV."""
+    out = {}
+    for fmt in ("q8_0", "q4_0"):
+        r = vvli_b200.Runner(cfg, max_seq=len(prompt) + warmup + steps + 8, device=local_rank)
+        r.fill_synthetic_quantized(seed, fmt)
+        r.prefill(prompt, 0, logits=False)  # token by token: the tensor-core prefill is bf16-only
+        r.decode(warmup)
+        toks, ms = r.decode(steps)
+        wbytes = r.query("weight_stream_bytes")
+        r.close()
+        per_tok = ms / steps
+        mean_pos = len(prompt) + warmup + steps // 2
+        kv = cfg.num_hidden_layers * (mean_pos + 1) * cfg.kv_dim() * 2 * 4
+        b = wbytes + (2 * cfg.num_hidden_layers + 1) * cfg.hidden_size * 2 + kv
+        ach = b / (per_tok / 1e3) / 1e9
+        out[fmt] = {"decode_tok_per_s": 1000.0 / per_tok, "ms_per_token": per_tok, "distinct_tokens": len(set(toks)),
+                    "roofline": {"bound": "hbm", "bytes_per_token": b, "achieved": ach, "peak": hbm, "unit": "GB/s",
+                                 "frac": ach / hbm},
+                    "weights": "vvli_cuda_fill_synthetic_quantized: the synthetic bf16 model quantised on the device"}
+    return out
+
+
 def _second_id(dist, vvli_b200, rank):
     """A fresh NCCL unique id shared by all ranks (for a second tensor-parallel context)."""
     obj = [vvli_b200.nccl_unique_id() if rank == 0 else None]
@@ -667,6 +693,7 @@ def _main(args, out_fd):
                                          "llama3 rope scaling"),
             "llama3.2-1b-4096": prefill_decode_config(vvli_b200, args.seed, hbm, tpeak, tpeak_src, local_rank),
             "op_sweep": op_sweep(vvli_b200, hbm, tpeak, local_rank),
+            "llama3-8b-quantized": quantized_decode(vvli_b200, cfg, prompt, args.seed, hbm, local_rank),
         }
 
     cpu = None

@@ -210,6 +210,15 @@ int vvli_cuda_load_gguf(vvli_ctx* ctx, const char* path);
  * host generator that the CPU baseline uses, without a host blob. */
 int vvli_cuda_fill_synthetic(vvli_ctx* ctx, uint64_t seed);
 
+/* The same synthetic model with every matrix (embedding, q/k/v, o,
+ * gate/up, down, LM head) block-quantised on the device: format 1 = GGML
+ * Q8_0, 2 = GGML Q4_0 (32 weights and an fp16 scale per block; norms and
+ * biases stay bf16).  The blocks are those a GGUF file of these weights
+ * quantised with the published rules holds, so the model equals a
+ * vvli_cuda_load_gguf of such a file.  No counterpart in the reference (it
+ * rejects quantised tensors, src/llm.zig:1083); tp_size 1 only. */
+int vvli_cuda_fill_synthetic_quantized(vvli_ctx* ctx, uint64_t seed, int format);
+
 /* Zeroes the KV cache.  Replaces KVCache.clear (src/llm.zig:576-579). */
 int vvli_cuda_reset(vvli_ctx* ctx);
 

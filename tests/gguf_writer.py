@@ -122,11 +122,13 @@ def gguf_cfg(cfg):
 # (src/gguf.zig:35, 39 names them; ggml / llama.cpp define them): blocks of 32
 # consecutive weights along a row (the innermost GGUF dimension).
 #   Q8_0: {fp16 d; int8 q[32]}, 34 bytes, weight = d * q;  d = amax / 127,
-#         q = round(x / d).
+#         q = roundf(x * (1 / d)) (halves away from zero).
 #   Q4_0: {fp16 d; uint8 qs[16]}, 18 bytes, weight = d * (n - 8) where
 #         qs[j] holds n of weight j in its low nibble and of weight j + 16 in
 #         its high nibble;  d = m / -8 with m the weight of largest magnitude,
-#         n = min(15, trunc(x / d + 8.5)).
+#         n = min(15, trunc(x * (1 / d) + 8.5)).
+# The steps are single fp32 operations, as the device quantiser
+# (vvli_cuda_fill_synthetic_quantized) performs them, so both give the same blocks.
 # Each returns the raw block bytes and the dequantised float32 values (exact:
 # an fp16 scale times a small integer fits a float32).
 
@@ -135,7 +137,10 @@ def quantize_q8_0(values):
     amax = np.abs(x).max(axis=1)
     d = (amax / 127.0).astype(np.float32)
     inv = np.where(d != 0, 1.0 / np.where(d != 0, d, 1), 0).astype(np.float32)
-    q = np.clip(np.round(x * inv[:, None]), -127, 127).astype(np.int8)
+    t = x * inv[:, None]
+    r = np.trunc(t)
+    r = r + np.sign(t) * (np.abs(t - r) >= 0.5)  # roundf: halves away from zero
+    q = np.clip(r, -127, 127).astype(np.int8)
     d16 = d.astype(np.float16)
     raw = np.zeros((x.shape[0], 34), np.uint8)
     raw[:, :2] = d16.view(np.uint8).reshape(-1, 2)

@@ -10,6 +10,8 @@ per-layer hidden states and logits within 1e-4, identical greedy streams.
 """
 
 
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -131,3 +133,42 @@ def test_quantized_errors(oracle, vv, tmp_path):
     with pytest.raises(VvliError) as e:
         r.prefill_batch([[1, 2], [3]])
     assert e.value.name == "Unimplemented"
+
+
+@pytest.mark.parametrize("qtype,fmt", [(G.Q8_0, "q8_0"), (G.Q4_0, "q4_0")], ids=["q8_0", "q4_0"])
+def test_device_quantised_fill_equals_gguf_file(oracle, vv, tmp_path, qtype, fmt):
+    # vvli_cuda_fill_synthetic_quantized quantises with the same fp32 steps as
+    # the GGUF writer: the two models are the same blocks, bit for bit.
+    cfg = gguf_llama(1024, 16, 4, 2816, 2, 4096)
+    blob = oracle.synthetic_blob(cfg, seed=1)
+    path = str(tmp_path / "model.gguf")
+    write_quantized_model(path, cfg, blob, qtype)
+    a = vv.Runner(cfg, max_seq=32)
+    a.load_gguf(path)
+    b = vv.Runner(cfg, max_seq=32)
+    b.fill_synthetic_quantized(1, fmt)
+    assert b.query("quantized") == 1
+    for pos, t in enumerate([5, 4000, 17, 999]):
+        assert np.array_equal(a.forward_token(t, pos), b.forward_token(t, pos)), pos
+
+
+def test_device_quantised_llama3_8b_shapes_split_half_rope(oracle, vv):
+    # The benchmarked architecture's layer (split-half RoPE, q/k rows re-paired
+    # before quantisation) at Q8_0, against the oracle on the dequantised values.
+    cfg = dataclasses.replace(C.llama3_8b(), num_hidden_layers=1, vocab_size=4096, eos_token_id=0, pad_token_id=0)
+    blob = oracle.synthetic_blob(cfg, seed=0)
+    _, f32 = quantized_model(cfg, blob, G.Q8_0)
+    gpu = vv.Runner(cfg, max_seq=64)
+    gpu.fill_synthetic_quantized(0, "q8_0")
+    ref = oracle.RefRunner(cfg, blob_f32=f32, max_seq=64, threads=4)
+    gpu.set_debug(True)
+    prompt = [11, 3000, 7, 123]
+    for pos, t in enumerate(prompt):
+        lr = ref.forward_token(t, pos)
+        lg = gpu.forward_token(t, pos)
+        assert rel(gpu.debug_hidden(0), ref.hidden(0)) < TIGHT and rel(lg, lr) < TIGHT, pos
+    gpu.set_debug(False)
+    gpu.reset()
+    ref.reset()
+    got, _ = gpu.generate_greedy(prompt, 16)
+    assert got == ref.generate_greedy(prompt, 16)

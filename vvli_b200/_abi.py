@@ -55,6 +55,7 @@ SIGNATURES = {
                                         ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(_ctx)]),
     "vvli_cuda_load_weights": (ctypes.c_int, [_ctx, _u16p, ctypes.c_uint64]),
     "vvli_cuda_fill_synthetic": (ctypes.c_int, [_ctx, ctypes.c_uint64]),
+    "vvli_cuda_fill_synthetic_quantized": (ctypes.c_int, [_ctx, ctypes.c_uint64, ctypes.c_int]),
     "vvli_cuda_reset": (ctypes.c_int, [_ctx]),
     "vvli_cuda_forward_token": (ctypes.c_int, [_ctx, ctypes.c_uint32, ctypes.c_uint64, _f32p, _u32p]),
     "vvli_cuda_forward_embedding": (ctypes.c_int, [_ctx, _f32p, ctypes.c_uint64, _f32p, _u32p]),

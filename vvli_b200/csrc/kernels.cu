@@ -1,3 +1,4 @@
+#include <cuda_fp16.h>
 // kernels.cu - decode-step kernels for sm_100a.
 //
 // One decode token per layer runs five kernels, chained with programmatic
@@ -737,6 +738,62 @@ __global__ void pair_rows_kernel(uint16_t* dst, const uint16_t* src, int rows, i
     const int src_row = head * d + ((i & 1) ? i / 2 + d / 2 : i / 2);
     dst[e] = src[static_cast<size_t>(src_row) * K + c];
   }
+}
+
+// GGML block quantisation of bf16 rows, one thread per 32-weight block, with
+// the published rules in plain fp32 steps (no contraction), so a host
+// restatement with the same steps gives the same blocks:
+//   Q8_0: d = amax / 127, q = roundf(x * (1 / d)) (halves away from zero);
+//   Q4_0: d = m / -8 (m: the first weight of largest magnitude),
+//         n = min(15, trunc(x * (1 / d) + 8.5)).
+// Output rows use the device layout of kernels.h (quants, then fp16 scales).
+__global__ void quantize_rows_kernel(const uint16_t* __restrict__ src, uint64_t rows, int K, int fmt,
+                                     uint8_t* __restrict__ dst, int row_bytes) {
+  const int nb = K / 32;
+  const uint64_t total = rows * static_cast<uint64_t>(nb);
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t r = i / nb;
+    const int b = static_cast<int>(i % nb);
+    const uint16_t* x = src + r * K + b * 32;
+    uint8_t* row = dst + r * row_bytes;
+    float v[32];
+    float amax = 0.f, m = 0.f;
+    for (int j = 0; j < 32; ++j) {
+      v[j] = bf16_to_f32(x[j]);
+      if (fabsf(v[j]) > amax) {
+        amax = fabsf(v[j]);
+        m = v[j];
+      }
+    }
+    if (fmt == kFmtQ8) {
+      const float d = __fdiv_rn(amax, 127.0f);
+      const float inv = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+      for (int j = 0; j < 32; ++j) {
+        const float q = fminf(127.f, fmaxf(-127.f, roundf(__fmul_rn(v[j], inv))));
+        row[b * 32 + j] = static_cast<uint8_t>(static_cast<int8_t>(q));
+      }
+      *reinterpret_cast<__half*>(row + K + 2 * b) = __float2half_rn(d);
+    } else {
+      const float d = __fdiv_rn(m, -8.0f);
+      const float inv = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+      uint8_t n[32];
+      for (int j = 0; j < 32; ++j) {
+        const float t = truncf(__fadd_rn(__fmul_rn(v[j], inv), 8.5f));
+        n[j] = static_cast<uint8_t>(fminf(15.f, fmaxf(0.f, t)));
+      }
+      for (int j = 0; j < 16; ++j) row[b * 16 + j] = static_cast<uint8_t>(n[j] | (n[j + 16] << 4));
+      *reinterpret_cast<__half*>(row + K / 2 + 2 * b) = __float2half_rn(d);
+    }
+  }
+}
+
+cudaError_t launch_quantize_rows(const uint16_t* src, uint64_t rows, int K, int fmt, uint8_t* dst, cudaStream_t s) {
+  if (fmt != kFmtQ8 && fmt != kFmtQ4) return cudaErrorInvalidValue;
+  const uint64_t blocks = rows * (K / 32);
+  const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((blocks + 255) / 256, 8192));
+  quantize_rows_kernel<<<grid, 256, 0, s>>>(src, rows, K, fmt, dst, row_bytes_of(fmt, K));
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pair_rows(uint16_t* w, uint16_t* bias, uint16_t* tmp, int rows, int K, int d, cudaStream_t s) {

@@ -207,6 +207,8 @@ cudaError_t configure_kernels(int max_smem_optin);
 // two elements of every split-half rotary pair (i, i + d/2) sit on adjacent
 // rows (2i, 2i + 1): on the device, split-half RoPE becomes the interleaved
 // rule.  `rows` = q rows + k rows (whole heads of d rows), `tmp` holds rows x K.
+// bf16 rows [rows, K] -> GGML Q8_0 / Q4_0 blocks in the device row layout (K % 32 == 0).
+cudaError_t launch_quantize_rows(const uint16_t* src, uint64_t rows, int K, int fmt, uint8_t* dst, cudaStream_t s);
 cudaError_t launch_pair_rows(uint16_t* w, uint16_t* bias, uint16_t* tmp, int rows, int K, int d, cudaStream_t s);
 // dst[cols][rows] = src[rows][cols]^T (bf16).
 cudaError_t launch_transpose_bf16(const uint16_t* src, uint16_t* dst, int rows, int cols, cudaStream_t s);

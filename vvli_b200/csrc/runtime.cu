@@ -175,6 +175,7 @@ struct vvli_ctx {
   int plan_sig = 0;              // formats the megakernel plan was made for (0: all bf16)
   bool want_mega = false;        // megakernel wanted (VVLI_MEGAKERNEL not 0)
   bool tc_prefill_planned = false;
+  bool rows_paired = false;      // q/k rows already in rotary-pair order (quantised synthetic fill)
   // KV cache and step buffers
   float* kv = nullptr;
   size_t kv_layer_floats = 0;  // K (or V) floats per layer
@@ -1392,7 +1393,7 @@ static int after_load(vvli_ctx* c) {
     return VVLI_ERR_UNSUPPORTED_DTYPE;
   }
   // Split-half RoPE: put rotary pairs on adjacent q/k rows (device layout).
-  if (c->cfg.rope_layout == VVLI_ROPE_SPLIT_HALF) {
+  if (c->cfg.rope_layout == VVLI_ROPE_SPLIT_HALF && !c->rows_paired) {
     const int rows = c->q_rows + c->kv_rows;
     uint16_t* tmp = nullptr;
     CK(cudaMalloc(&tmp, static_cast<size_t>(rows) * c->h * 2));
@@ -1414,6 +1415,7 @@ static int after_load(vvli_ctx* c) {
                                c->I_l, c->stream));
   }
   CK(cudaStreamSynchronize(c->stream));
+  c->rows_paired = false;
   c->loaded = true;
   return build_graph(c);
 }
@@ -1500,6 +1502,71 @@ int vvli_cuda_fill_synthetic(vvli_ctx* c, uint64_t seed) {
   for (const Piece& p : c->pieces)
     CK(launch_synth_fill(c->w + p.dst, tensor_key(seed, p.tensor_id), p.rows, p.cols, p.src_ld, p.row0, p.col0,
                          p.kind, c->stream));
+  return after_load(c);
+}
+
+int vvli_cuda_fill_synthetic_quantized(vvli_ctx* c, uint64_t seed, int format) {
+  if (!c || (format != kFmtQ8 && format != kFmtQ4)) return VVLI_ERR_INVALID_ARGUMENT;
+  if (c->tp_size > 1) {
+    g_last_error = "block-quantised weights run on one GPU (tp_size 1)";
+    return VVLI_ERR_UNSUPPORTED_DTYPE;
+  }
+  if (c->h % 32 || c->I_l % 32 || c->q_rows % 32) {
+    g_last_error = "block quantisation needs hidden, intermediate and q widths that are multiples of 32";
+    return VVLI_ERR_UNSUPPORTED_DTYPE;
+  }
+  CK(cudaSetDevice(c->device));
+  set_bf16_formats(c);
+  c->loaded = false;
+  for (const Piece& p : c->pieces)
+    CK(launch_synth_fill(c->w + p.dst, tensor_key(seed, p.tensor_id), p.rows, p.cols, p.src_ld, p.row0, p.col0,
+                         p.kind, c->stream));
+  // Rotary-pair row order first (it moves whole bf16 rows; blocks lie along rows).
+  if (c->cfg.rope_layout == VVLI_ROPE_SPLIT_HALF) {
+    const int rows = c->q_rows + c->kv_rows;
+    uint16_t* tmp = nullptr;
+    CK(cudaMalloc(&tmp, static_cast<size_t>(rows) * c->h * 2));
+    for (int l = 0; l < c->L; ++l) {
+      const DevLayer& D = c->lay[l];
+      cudaError_t e = launch_pair_rows(c->w + D.w_qkv, D.b_qkv == UINT64_MAX ? nullptr : c->w + D.b_qkv, tmp, rows,
+                                       c->h, c->d, c->stream);
+      if (e) {
+        cudaFree(tmp);
+        return cuda_fail(e, "launch_pair_rows");
+      }
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    cudaFree(tmp);
+  }
+  // Every matrix (embedding, q|k|v, o, gate|up, down, LM head) quantised in
+  // place from a bf16 copy.
+  struct Mat { uint64_t off, rows; int K; };
+  std::vector<Mat> mats;
+  mats.push_back({c->off_emb, static_cast<uint64_t>(c->V), c->h});
+  for (const DevLayer& D : c->lay) {
+    mats.push_back({D.w_qkv, static_cast<uint64_t>(c->q_rows + 2 * c->kv_rows), c->h});
+    mats.push_back({D.w_o, static_cast<uint64_t>(c->h), c->q_rows});
+    mats.push_back({D.w_gu, 2ull * c->I_l, c->h});
+    mats.push_back({D.w_down, static_cast<uint64_t>(c->h), c->I_l});
+  }
+  if (!c->lm_aliases_emb) mats.push_back({c->off_lm, static_cast<uint64_t>(c->V_lr), c->h});
+  size_t big = 0;
+  for (const Mat& m : mats) big = std::max<size_t>(big, m.rows * m.K);
+  uint16_t* stage = nullptr;
+  CK(cudaMalloc(&stage, big * 2));
+  cudaError_t e = cudaSuccess;
+  for (const Mat& m : mats) {
+    if ((e = cudaMemcpyAsync(stage, c->w + m.off, m.rows * m.K * 2, cudaMemcpyDeviceToDevice, c->stream))) break;
+    if ((e = launch_quantize_rows(stage, m.rows, m.K, format, reinterpret_cast<uint8_t*>(c->w + m.off), c->stream)))
+      break;
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  cudaFree(stage);
+  if (e) return cuda_fail(e, "quantise weights");
+  for (DevLayer& D : c->lay) D.f_qkv = D.f_o = D.f_gu = D.f_down = format;
+  c->f_emb = c->f_lm = format;
+  c->quant = true;
+  c->rows_paired = true;
   return after_load(c);
 }
 

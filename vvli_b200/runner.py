@@ -79,6 +79,10 @@ class Runner:
     def fill_synthetic(self, seed: int = 0):
         check(_abi.lib().vvli_cuda_fill_synthetic(self._ctx, seed))
 
+    def fill_synthetic_quantized(self, seed: int = 0, fmt: str = "q8_0"):
+        """The synthetic model with every matrix quantised on the device (GGML Q8_0 or Q4_0)."""
+        check(_abi.lib().vvli_cuda_fill_synthetic_quantized(self._ctx, seed, {"q8_0": 1, "q4_0": 2}[fmt]))
+
     def reset(self):
         """KVCache.clear (src/llm.zig:576-579)."""
         check(_abi.lib().vvli_cuda_reset(self._ctx))
