@@ -246,6 +246,7 @@ struct vvli_ctx {
   uint32_t* smp_recent = nullptr;
   SampleState* smp_state = nullptr;
   SampleState* h_smp_state = nullptr;
+  uint32_t* h_smp_recent = nullptr;  // page-locked staging of the recent tokens
   void* smp_temp = nullptr;
   size_t smp_temp_bytes = 0;
   unsigned smp_call = 0;
@@ -1049,6 +1050,7 @@ void free_ctx(vvli_ctx* c) {
   if (c->h_st) cudaFreeHost(c->h_st);
   if (c->h_tok) cudaFreeHost(c->h_tok);
   if (c->h_smp_state) cudaFreeHost(c->h_smp_state);
+  if (c->h_smp_recent) cudaFreeHost(c->h_smp_recent);
   if (c->ev0) cudaEventDestroy(c->ev0);
   if (c->ev1) cudaEventDestroy(c->ev1);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -1869,6 +1871,7 @@ int ensure_sampler(vvli_ctx* c) {
       (st = alloc(reinterpret_cast<void**>(&c->smp_state), sizeof(SampleState))))
     return st;
   CK(cudaMallocHost(&c->h_smp_state, sizeof(SampleState)));
+  CK(cudaMallocHost(&c->h_smp_recent, kSampleRecentCap * 4));
   CK(cudaMemset(c->smp_stamp, 0, V * 4));
   CK(configure_sampler());
   c->smp_call = 0;
@@ -1907,7 +1910,9 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
     const uint32_t* src = recent + (n_recent - n_use);
     for (uint64_t done = 0; done < n_use; done += kSampleRecentCap) {
       const int n = static_cast<int>(std::min<uint64_t>(kSampleRecentCap, n_use - done));
-      CK(cudaMemcpyAsync(c->smp_recent, src + done, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
+      std::memcpy(c->h_smp_recent, src + done, static_cast<size_t>(n) * 4);  // page-locked: an async copy
+      CK(cudaMemcpyAsync(c->smp_recent, c->h_smp_recent, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice,
+                         c->stream));
       CK(launch_sample_mark(c->smp_recent, n, c->smp_stamp, c->smp_call, c->V, c->stream));
       if (done + kSampleRecentCap < n_use) CK(cudaStreamSynchronize(c->stream));  // smp_recent is reused
     }
@@ -1934,9 +1939,9 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
   CK(cudaMemcpyAsync(c->smp_state, h, sizeof(SampleState), cudaMemcpyHostToDevice, c->stream));
   const uint64_t limit = o->top_k == 0 ? c->V : std::min<uint64_t>(o->top_k, c->V);
   const int nblk = (c->V + 1023) / 1024;
-  int npow2 = 1;
-  while (npow2 < nblk * static_cast<int>(std::min<uint64_t>(limit, kSampleFastK))) npow2 <<= 1;
-  if (o->temperature > 0.0f && limit <= static_cast<uint64_t>(kSampleFastK) && npow2 <= kSampleFastMaxCand) {
+  int nlists = 1;
+  while (nlists < nblk) nlists <<= 1;
+  if (o->temperature > 0.0f && limit <= static_cast<uint64_t>(kSampleFastK) && nlists * 64 <= kSampleFastMaxCand) {
     // the candidates reuse the long path's buffers (V keys >= ceil(V / 1024) * 64)
     CK(launch_sample_fast(p, static_cast<int>(limit), c->smp_key64, reinterpret_cast<unsigned*>(c->smp_key32),
                           c->stream));

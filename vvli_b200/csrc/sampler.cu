@@ -180,62 +180,121 @@ __device__ void finish_sorted(const SampleParams& p, const unsigned long long* c
   }
 }
 
-// Bitonic sort, descending, of n (a power of two) keys in shared memory by the whole CTA.
-__device__ void bitonic_desc(unsigned long long* a, int n) {
-  for (int size = 2; size <= n; size <<= 1) {
+// ---------------------------------------------------------------- small top-k (k <= kSampleFastK)
+// Sorting networks on 64-key lists held two keys per lane (index lane and
+// lane + 32), descending.  Keys are unique (the id is in the low bits) except
+// the zeros of padding and non-finite logits, which sort last.
+VVLI_DEV unsigned long long kmax(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
+VVLI_DEV unsigned long long kmin(unsigned long long a, unsigned long long b) { return a < b ? a : b; }
+
+// One compare-exchange at `stride` (< 32) for the element of index `idx`:
+// the lower index of a pair keeps the larger key when `desc`.
+VVLI_DEV unsigned long long cx_step(unsigned long long v, int idx, int stride, bool desc) {
+  const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, stride);
+  return ((idx & stride) == 0) == desc ? kmax(v, o) : kmin(v, o);
+}
+
+// Bitonic sort of 64 keys, descending.
+VVLI_DEV void warp_sort64(unsigned long long& r0, unsigned long long& r1, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool desc = (lo & size) == 0;
-        const unsigned long long x = a[lo], y = a[hi];
-        if ((x < y) == desc) {
-          a[lo] = y;
-          a[hi] = x;
-        }
+      if (stride == 32) {
+        const unsigned long long hi = kmax(r0, r1), lo = kmin(r0, r1);
+        r0 = hi, r1 = lo;
+      } else {
+        r0 = cx_step(r0, lane, stride, size == 64 || (lane & size) == 0);
+        r1 = cx_step(r1, lane + 32, stride, size == 64 || ((lane + 32) & size) == 0);
       }
-      __syncthreads();
     }
   }
 }
 
-// Small top-k (k <= kSampleFastK), first pass: CTA b sorts the keys of ids
-// [1024 b, 1024 b + 1024) and keeps its best k; the finite count is summed.
+// Top 64 of two descending 64-lists a and b (shared memory), descending, into
+// out (which may be a): max(a[i], b[63 - i]) is a bitonic sequence holding the
+// 64 largest keys, then a bitonic merge sorts it.
+VVLI_DEV void warp_merge64(const unsigned long long* a, const unsigned long long* b, unsigned long long* out,
+                           int lane) {
+  unsigned long long r0 = kmax(a[lane], b[63 - lane]);
+  unsigned long long r1 = kmax(a[lane + 32], b[31 - lane]);
+  __syncwarp();
+  {
+    const unsigned long long hi = kmax(r0, r1), lo = kmin(r0, r1);
+    r0 = hi, r1 = lo;
+  }
+#pragma unroll
+  for (int stride = 16; stride > 0; stride >>= 1) {
+    r0 = cx_step(r0, lane, stride, true);
+    r1 = cx_step(r1, lane + 32, stride, true);
+  }
+  out[lane] = r0;
+  out[lane + 32] = r1;
+}
+
+// Merges n (a power of two) 64-lists lists[i * 64] in place, pairwise by
+// levels, into lists[0]; every thread of the CTA calls it.
+__device__ void merge_lists(unsigned long long* lists, int n) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  for (int step = 1; step < n; step <<= 1) {
+    for (int m = warp; m < n / (2 * step); m += warps) {
+      unsigned long long* a = lists + static_cast<size_t>(2 * step * m) * 64;
+      warp_merge64(a, a + static_cast<size_t>(step) * 64, a, lane);
+    }
+    __syncthreads();
+  }
+}
+
+// First pass: CTA b takes ids [1024 b, 1024 b + 1024); each warp sorts 64 of
+// them, the CTA merges its 16 lists, and the best k go to cand[b * k ...];
+// nfin_part[b] = the CTA's count of finite adjusted logits.
 __global__ void __launch_bounds__(512) topk_local_kernel(const SampleParams p, int k, unsigned long long* cand,
-                                                         unsigned* nfin) {
-  __shared__ unsigned long long keys[1024];
-  __shared__ unsigned cnt;
-  const int tid = threadIdx.x;
-  if (tid == 0) cnt = 0;
-  __syncthreads();
+                                                         unsigned* nfin_part) {
+  __shared__ unsigned long long lists[16 * 64];
+  __shared__ unsigned wcount[16];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long r[2];
   unsigned mine = 0;
-  for (int i = tid; i < 1024; i += 512) {
-    const int id = blockIdx.x * 1024 + i;
-    unsigned long long key = 0ull;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int id = blockIdx.x * 1024 + warp * 64 + lane + 32 * h;
+    r[h] = 0ull;
     if (id < p.V) {
       const float s = adjusted_logit(p.logits[id], p.stamp[id] == p.call, p.repeat_penalty);
       if (isfinite(s)) {
-        key = make_key64(order_key(s), id);
+        r[h] = make_key64(order_key(s), id);
         ++mine;
       }
     }
-    keys[i] = key;
   }
-  atomicAdd(&cnt, mine);
+  mine = __reduce_add_sync(0xffffffffu, mine);
+  if (lane == 0) wcount[warp] = mine;
+  warp_sort64(r[0], r[1], lane);
+  lists[warp * 64 + lane] = r[0];
+  lists[warp * 64 + lane + 32] = r[1];
   __syncthreads();
-  bitonic_desc(keys, 1024);
-  if (tid == 0) atomicAdd(nfin, cnt);
-  for (int i = tid; i < k; i += 512) cand[static_cast<size_t>(blockIdx.x) * k + i] = keys[i];
+  merge_lists(lists, 16);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) cand[static_cast<size_t>(blockIdx.x) * k + i] = lists[i];
+  if (threadIdx.x == 0) {
+    unsigned t = 0;
+    for (int w = 0; w < 16; ++w) t += wcount[w];
+    nfin_part[blockIdx.x] = t;
+  }
 }
 
-// Second pass: sort the CTAs' candidates (padded to a power of two) and finish.
-__global__ void __launch_bounds__(1024) topk_merge_kernel(const SampleParams p, int k_req, int ncand, int npow2,
-                                                          const unsigned long long* cand, const unsigned* nfin) {
+// Second pass: the CTAs' lists (k keys each, padded to 64) merged to the best
+// 64, then probabilities, top-p and the draw.
+__global__ void __launch_bounds__(1024) topk_merge_kernel(const SampleParams p, int k_req, int nblk, int nlists,
+                                                          const unsigned long long* cand, const unsigned* nfin_part) {
   extern __shared__ __align__(16) unsigned char smem[];
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem);  // [npow2]
-  float* probs = reinterpret_cast<float*>(keys + npow2);                     // [kSampleFastK]
-  const unsigned n_finite = *nfin;
+  unsigned long long* lists = reinterpret_cast<unsigned long long*>(smem);  // [nlists][64]
+  float* probs = reinterpret_cast<float*>(lists + static_cast<size_t>(nlists) * 64);  // [kSampleFastK]
+  __shared__ unsigned wsum[32];
   SampleState* st = p.st;
+  unsigned c = 0;
+  for (int b = threadIdx.x; b < nblk; b += blockDim.x) c += nfin_part[b];
+  unsigned n_finite;
+  block_excl_scan(c, wsum, &n_finite);
   if (n_finite == 0) {  // no candidate: llm.argmax of the raw logits (:115), rare
     if (threadIdx.x == 0) {
       float bv = p.logits[0];
@@ -250,11 +309,14 @@ __global__ void __launch_bounds__(1024) topk_merge_kernel(const SampleParams p, 
     }
     return;
   }
-  for (int i = threadIdx.x; i < npow2; i += blockDim.x) keys[i] = i < ncand ? cand[i] : 0ull;
+  for (int i = threadIdx.x; i < nlists * 64; i += blockDim.x) {
+    const int b = i >> 6, j = i & 63;
+    lists[i] = (b < nblk && j < k_req) ? cand[static_cast<size_t>(b) * k_req + j] : 0ull;
+  }
   __syncthreads();
-  bitonic_desc(keys, npow2);
+  merge_lists(lists, nlists);
   const unsigned k = min(static_cast<unsigned>(k_req), n_finite);
-  finish_sorted(p, keys, probs, k);
+  finish_sorted(p, lists, probs, k);
 }
 
 __global__ void sample_mark_kernel(const uint32_t* recent, int n, unsigned* stamp, unsigned call, int V) {
@@ -511,15 +573,12 @@ cudaError_t launch_sample_long(const SampleParams& p, void* temp, size_t temp_by
 
 cudaError_t launch_sample_fast(const SampleParams& p, int k, unsigned long long* cand, unsigned* nfin, cudaStream_t s) {
   const int nblk = (p.V + 1023) / 1024;
-  const int ncand = nblk * k;
-  int npow2 = 1;
-  while (npow2 < ncand) npow2 <<= 1;
-  if (k < 1 || k > kSampleFastK || npow2 > kSampleFastMaxCand) return cudaErrorInvalidValue;
-  cudaError_t e = cudaMemsetAsync(nfin, 0, sizeof(unsigned), s);
-  if (e) return e;
+  int nlists = 1;
+  while (nlists < nblk) nlists <<= 1;
+  if (k < 1 || k > kSampleFastK || nlists * 64 > kSampleFastMaxCand) return cudaErrorInvalidValue;
   topk_local_kernel<<<nblk, 512, 0, s>>>(p, k, cand, nfin);
-  const size_t smem = static_cast<size_t>(npow2) * 8 + kSampleFastK * 4;
-  topk_merge_kernel<<<1, 1024, smem, s>>>(p, k, ncand, npow2, cand, nfin);
+  const size_t smem = static_cast<size_t>(nlists) * 64 * 8 + kSampleFastK * 4;
+  topk_merge_kernel<<<1, 1024, smem, s>>>(p, k, nblk, nlists, cand, nfin);
   return cudaGetLastError();
 }
 

@@ -10,7 +10,9 @@ namespace vvli {
 // longer ones (top_k = 0 or large) take the sorted-vocabulary path.
 constexpr int kSampleSmallK = 4096;
 // top_k <= kSampleFastK (the reference's default is 40) takes a two-pass path:
-// per-1024-id CTA sorts, then one sort of at most kSampleFastMaxCand candidates.
+// per-1024-id CTAs keep their best k (warp sorting networks and a merge tree),
+// one CTA merges those lists (at most kSampleFastMaxCand / 64 of them: a
+// vocabulary of up to 262,144 tokens).
 constexpr int kSampleFastK = 64;
 constexpr int kSampleFastMaxCand = 16384;
 
@@ -46,7 +48,8 @@ cudaError_t launch_sample(const SampleParams& p, cudaStream_t s);
 // top-p and the draw over the first st->k.
 cudaError_t launch_sample_long(const SampleParams& p, void* temp, size_t temp_bytes, cudaStream_t s);
 size_t sample_sort_temp_bytes(int V);
-// top_k in [1, kSampleFastK] with temperature > 0; cand holds ceil(V / 1024) * k keys.
+// top_k in [1, kSampleFastK] with temperature > 0; cand holds ceil(V / 1024) * k keys,
+// nfin ceil(V / 1024) counts.
 cudaError_t launch_sample_fast(const SampleParams& p, int k, unsigned long long* cand, unsigned* nfin, cudaStream_t s);
 cudaError_t configure_sampler();
 
