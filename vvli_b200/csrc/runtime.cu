@@ -1042,15 +1042,14 @@ void free_ctx(vvli_ctx* c) {
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
                  c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->w_downT, c->acc, c->pf_x, c->pf_q,
                  c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->pf_kvt, c->smp_stamp, c->smp_key32,
-                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_recent, c->smp_state, c->smp_temp,
+                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_state, c->smp_temp,
                  c->bt_x, c->bt_q, c->bt_logits, c->bt_best, c->bt_all_best, c->bt_part, c->bt_logits_all, c->bt_ahi,
                  c->bt_alo, c->bt_fhi, c->bt_flo, c->bt_tokens, c->bt_pos, c->bt_idx, c->bt_counters};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (c->h_st) cudaFreeHost(c->h_st);
   if (c->h_tok) cudaFreeHost(c->h_tok);
-  if (c->h_smp_state) cudaFreeHost(c->h_smp_state);
-  if (c->h_smp_recent) cudaFreeHost(c->h_smp_recent);
+  if (c->h_smp_state) cudaFreeHost(c->h_smp_state);  // the recent-token staging lives in the same block
   if (c->ev0) cudaEventDestroy(c->ev0);
   if (c->ev1) cudaEventDestroy(c->ev1);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -1850,6 +1849,8 @@ int vvli_cuda_decode(vvli_ctx* c, uint64_t n_steps, uint32_t* out_tokens, float*
 // ---------------------------------------------------------------- sampling
 namespace {
 constexpr int kSampleRecentCap = 4096;  // recent tokens marked per copy
+constexpr size_t kSampleStateBytes = 64;  // SampleState, padded; the recent tokens follow it
+static_assert(sizeof(SampleState) <= kSampleStateBytes, "the recent tokens follow the step state");
 
 int ensure_sampler(vvli_ctx* c) {
   if (c->smp_state) return VVLI_OK;
@@ -1866,12 +1867,14 @@ int ensure_sampler(vvli_ctx* c) {
       (st = alloc(reinterpret_cast<void**>(&c->smp_key64_sorted), V * 8)) ||
       (st = alloc(reinterpret_cast<void**>(&c->smp_probs), V * 4)) ||
       (st = alloc(reinterpret_cast<void**>(&c->smp_logits), V * 4)) ||
-      (st = alloc(reinterpret_cast<void**>(&c->smp_recent), kSampleRecentCap * 4)) ||
       (st = alloc(&c->smp_temp, std::max<size_t>(c->smp_temp_bytes, 16))) ||
-      (st = alloc(reinterpret_cast<void**>(&c->smp_state), sizeof(SampleState))))
+      (st = alloc(reinterpret_cast<void**>(&c->smp_state), kSampleStateBytes + kSampleRecentCap * 4)))
     return st;
-  CK(cudaMallocHost(&c->h_smp_state, sizeof(SampleState)));
-  CK(cudaMallocHost(&c->h_smp_recent, kSampleRecentCap * 4));
+  // The step state and the recent tokens sit in one block (device and
+  // page-locked host), so one copy sends both.
+  c->smp_recent = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(c->smp_state) + kSampleStateBytes);
+  CK(cudaMallocHost(&c->h_smp_state, kSampleStateBytes + kSampleRecentCap * 4));
+  c->h_smp_recent = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(c->h_smp_state) + kSampleStateBytes);
   CK(cudaMemset(c->smp_stamp, 0, V * 4));
   CK(configure_sampler());
   c->smp_call = 0;
@@ -1900,14 +1903,24 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
       return st;
     logits = c->logits_full;
   }
-  if (++c->smp_call == 0) {  // the stamps wrapped: start over
+  const uint64_t limit = o->top_k == 0 ? c->V : std::min<uint64_t>(o->top_k, c->V);
+  const int nblk = (c->V + 1023) / 1024;
+  int nlists = 1;
+  while (nlists < nblk) nlists <<= 1;
+  const bool fast = o->temperature > 0.0f && limit <= static_cast<uint64_t>(kSampleFastK) &&
+                    nlists * 64 <= kSampleFastMaxCand;
+  // buildRepeatCounts (src/generator.zig:344-360): the last repeat_last_n tokens.
+  const bool penalise = o->repeat_penalty > 1.0f && o->repeat_last_n > 0 && n_recent > 0;
+  const uint64_t n_use = penalise ? std::min<uint64_t>(n_recent, o->repeat_last_n) : 0;
+  const uint32_t* src = recent + (n_recent - n_use);
+  // The top-k path reads the recent tokens itself (they travel with the step
+  // state); the other paths read per-token stamps marked here.
+  const bool fold = fast && n_use <= static_cast<uint64_t>(kSampleRecentCap);
+  if (!fold && ++c->smp_call == 0) {  // the stamps wrapped: start over
     CK(cudaMemsetAsync(c->smp_stamp, 0, static_cast<size_t>(c->V) * 4, c->stream));
     c->smp_call = 1;
   }
-  // buildRepeatCounts (src/generator.zig:344-360): the last repeat_last_n tokens.
-  if (o->repeat_penalty > 1.0f && o->repeat_last_n > 0 && n_recent > 0) {
-    const uint64_t n_use = std::min<uint64_t>(n_recent, o->repeat_last_n);
-    const uint32_t* src = recent + (n_recent - n_use);
+  if (!fold && n_use > 0) {
     for (uint64_t done = 0; done < n_use; done += kSampleRecentCap) {
       const int n = static_cast<int>(std::min<uint64_t>(kSampleRecentCap, n_use - done));
       std::memcpy(c->h_smp_recent, src + done, static_cast<size_t>(n) * 4);  // page-locked: an async copy
@@ -1931,17 +1944,20 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
   p.key64_sorted = c->smp_key64_sorted;
   p.probs = c->smp_probs;
   p.st = c->smp_state;
+  if (fold) {
+    p.stamp = nullptr;
+    p.recent = c->smp_recent;
+    p.n_recent = static_cast<int>(n_use);
+    if (n_use) std::memcpy(c->h_smp_recent, src, n_use * 4);
+  }
   SampleState* h = c->h_smp_state;
   std::memcpy(h->rng, rng_state, sizeof(h->rng));
   h->token = -1;
   h->path = 0;
   h->k = 0;
-  CK(cudaMemcpyAsync(c->smp_state, h, sizeof(SampleState), cudaMemcpyHostToDevice, c->stream));
-  const uint64_t limit = o->top_k == 0 ? c->V : std::min<uint64_t>(o->top_k, c->V);
-  const int nblk = (c->V + 1023) / 1024;
-  int nlists = 1;
-  while (nlists < nblk) nlists <<= 1;
-  if (o->temperature > 0.0f && limit <= static_cast<uint64_t>(kSampleFastK) && nlists * 64 <= kSampleFastMaxCand) {
+  CK(cudaMemcpyAsync(c->smp_state, h, kSampleStateBytes + (fold ? n_use * 4 : 0), cudaMemcpyHostToDevice,
+                     c->stream));
+  if (fast) {
     // the candidates reuse the long path's buffers (V keys >= ceil(V / 1024) * 64)
     CK(launch_sample_fast(p, static_cast<int>(limit), c->smp_key64, reinterpret_cast<unsigned*>(c->smp_key32),
                           c->stream));

@@ -252,15 +252,28 @@ __global__ void __launch_bounds__(512) topk_local_kernel(const SampleParams p, i
                                                          unsigned* nfin_part) {
   __shared__ unsigned long long lists[16 * 64];
   __shared__ unsigned wcount[16];
+  __shared__ unsigned recent_bits[32];  // ids [1024 b, 1024 b + 1024) among the recent tokens
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = blockIdx.x * 1024;
+  if (!p.stamp) {
+    if (threadIdx.x < 32) recent_bits[threadIdx.x] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < p.n_recent; i += blockDim.x) {
+      const int t = static_cast<int>(p.recent[i]) - base;
+      if (t >= 0 && t < 1024) atomicOr(&recent_bits[t >> 5], 1u << (t & 31));
+    }
+    __syncthreads();
+  }
   unsigned long long r[2];
   unsigned mine = 0;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const int id = blockIdx.x * 1024 + warp * 64 + lane + 32 * h;
+    const int id = base + warp * 64 + lane + 32 * h;
     r[h] = 0ull;
     if (id < p.V) {
-      const float s = adjusted_logit(p.logits[id], p.stamp[id] == p.call, p.repeat_penalty);
+      const int t = id - base;
+      const bool rec = p.stamp ? p.stamp[id] == p.call : ((recent_bits[t >> 5] >> (t & 31)) & 1u) != 0;
+      const float s = adjusted_logit(p.logits[id], rec, p.repeat_penalty);
       if (isfinite(s)) {
         r[h] = make_key64(order_key(s), id);
         ++mine;

@@ -29,6 +29,9 @@ struct SampleParams {
   int V;
   const unsigned* stamp;      // stamp[i] == call: token i is among the last repeat_last_n
   unsigned call;
+  // top-k path: when stamp is null, the last repeat_last_n tokens themselves
+  const uint32_t* recent;
+  int n_recent;
   float temperature, top_p, repeat_penalty;
   unsigned long long top_k;
   unsigned* key32;            // [V] scratch: order-preserving keys of the finite adjusted logits, 0 = none
