@@ -617,7 +617,7 @@ def _main(args, out_fd):
     from vvli_b200 import sampler as _smp
     sopt = vvli_b200.Options()
     sstate = np.array(_smp.Xoshiro256(1).s, dtype=np.uint64)
-    recent = list(range(1, 65))
+    recent = np.arange(1, 65, dtype=np.uint32)  # the prompt + generated tokens, as a caller keeps them
     runner.sample(sopt, recent, sstate)
     t_s = []
     for _ in range(50):
@@ -642,8 +642,16 @@ def _main(args, out_fd):
             rb.forward_batch(btoks, [args.prompt + 3 + i] * args.batch, logits=False)
             bms.append(rb.last_forward_ms())
         bms_step = allmax(float(np.mean(bms)))
+        # weights once per step + every row's fp32 KV over its context (positions prompt + 3 .. + 18)
+        kv_pos = cfg.num_hidden_layers * cfg.kv_dim() * 2 * 4
+        bbytes = (decode_bytes_per_token(cfg, -1) + args.batch * kv_pos * (args.prompt + 3 + 8 + 1)) / n
+        bach = bbytes / (bms_step / 1e3) / 1e9
         batch = {"rows": args.batch, "context": args.prompt, "ms_per_step": bms_step,
                  "tok_per_s": args.batch / (bms_step / 1000.0), "steps": 16,
+                 "roofline": {"bound": "hbm", "bytes_per_step_per_gpu": bbytes, "achieved": bach, "peak": hbm,
+                              "unit": "GB/s", "frac": bach / hbm,
+                              "bytes_definition": "all weight matrices once + each row's fp32 KV read at its mean "
+                                                  "position"},
                  "path": "vvli_cuda_forward_batch: tcgen05 GEMMs with weight rows as M and the batch as N, "
                          "paged attention per row; device time of each call (host token ids in, argmax out)"}
         rb.close()

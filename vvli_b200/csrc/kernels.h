@@ -110,6 +110,7 @@ inline __host__ __device__ int row_bytes_of(int fmt, int K) {
 }
 
 constexpr int kMegaConsumerWarps = 16;
+constexpr int kMegaXStageMax = 4096;  // longest GEMV input staged in shared memory
 constexpr int kMegaThreads = (kMegaConsumerWarps + 1) * 32;
 
 struct MegaPhase {
@@ -144,6 +145,7 @@ struct MegaParams {
   const MegaPhase* phases;
   int nphases;
   int nst, slot_bytes, part_floats;  // shared-memory ring and partial-sum area
+  int xstage_floats;       // shared-memory staging of GEMV inputs (phases with S <= 2), 0: none
   StepState* st;
   int* seq_tokens;
   const uint16_t* emb;

@@ -22,6 +22,8 @@
 // adds the partials in rank order.
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "device_fns.cuh"
 #include "kernels.h"
 
@@ -29,6 +31,7 @@ namespace vvli {
 
 constexpr int kCW = kMegaConsumerWarps;
 constexpr int kNC = kCW * kWarp;
+
 
 // ---------------------------------------------------------------- sync helpers
 VVLI_DEV unsigned ld_acquire_gpu(const unsigned* p) {
@@ -196,32 +199,70 @@ VVLI_DEV float byte_as_float(uint32_t t, int k, float bias) {
   return __int_as_float(__byte_perm(t, 0x4B000000u, 0x7540u + k)) - bias;
 }
 
-// sum_i q_i * x_i over the 16 int8 quants of a chunk (x ^ 0x80 maps q to q + 128).
-VVLI_DEV float dot16_q8(uint4 w, const float* x) {
+// Packed fp32 pairs (sm_100 f32x2 instructions: one issue, two lanes of
+// fp32 arithmetic, each rounded like the scalar instruction).
+typedef unsigned long long f32x2;
+VVLI_DEV f32x2 pack_f2(float a, float b) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+VVLI_DEV f32x2 pack_u2(uint32_t a, uint32_t b) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+  return r;
+}
+VVLI_DEV f32x2 fma_f2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+VVLI_DEV f32x2 add_f2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+VVLI_DEV float sum_f2(f32x2 a) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(a));
+  return lo + hi;
+}
+
+// Bytes k and k + 1 of `t` as the pair (2^23 + byte) - bias, exactly.
+VVLI_DEV f32x2 bytes_as_f2(uint32_t t, int k, f32x2 neg_bias) {
+  return add_f2(pack_u2(__byte_perm(t, 0x4B000000u, 0x7540u + k), __byte_perm(t, 0x4B000000u, 0x7540u + k + 1)),
+                neg_bias);
+}
+
+// sum_i q_i * x_i over the 16 int8 quants of a chunk (x ^ 0x80 maps q to
+// q + 128); x2 holds the 16 inputs as 8 pairs.
+VVLI_DEV float dot16_q8(uint4 w, const f32x2* x2) {
   const uint32_t wd[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
-  float acc = 0.f;
+  const f32x2 nb = pack_f2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+  f32x2 acc = 0ull;
 #pragma unroll
-  for (int m = 0; m < 4; ++m)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc = fmaf(byte_as_float(wd[m], k, 8388736.0f), x[4 * m + k], acc);  // 2^23 + 128
-  return acc;
+  for (int m = 0; m < 4; ++m) {
+    acc = fma_f2(bytes_as_f2(wd[m], 0, nb), x2[2 * m], acc);
+    acc = fma_f2(bytes_as_f2(wd[m], 2, nb), x2[2 * m + 1], acc);
+  }
+  return sum_f2(acc);
 }
 
 // sum_i (n_i - 8) * x_i over the 32 nibbles of a Q4_0 block: byte j holds
-// weight j (low nibble) and weight j + 16 (high nibble).
-VVLI_DEV float dot32_q4(uint4 w, const float* x) {
+// weight j (low nibble) and weight j + 16 (high nibble); x2 holds 16 pairs.
+VVLI_DEV float dot32_q4(uint4 w, const f32x2* x2) {
   const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
-  float acc = 0.f;
+  const f32x2 nb = pack_f2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
+  f32x2 acc = 0ull;
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     const uint32_t lo = wd[m] & 0x0F0F0F0Fu, hi = (wd[m] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      acc = fmaf(byte_as_float(lo, k, 8388616.0f), x[4 * m + k], acc);  // 2^23 + 8
-      acc = fmaf(byte_as_float(hi, k, 8388616.0f), x[16 + 4 * m + k], acc);
-    }
+    acc = fma_f2(bytes_as_f2(lo, 0, nb), x2[2 * m], acc);
+    acc = fma_f2(bytes_as_f2(lo, 2, nb), x2[2 * m + 1], acc);
+    acc = fma_f2(bytes_as_f2(hi, 0, nb), x2[8 + 2 * m], acc);
+    acc = fma_f2(bytes_as_f2(hi, 2, nb), x2[8 + 2 * m + 1], acc);
   }
-  return acc;
+  return sum_f2(acc);
 }
 
 VVLI_DEV float half_at(const uint8_t* p) { return __half2float(*reinterpret_cast<const __half*>(p)); }
@@ -230,7 +271,7 @@ VVLI_DEV float half_at(const uint8_t* p) { return __half2float(*reinterpret_cast
 template <int MAXC, int FMT>
 __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* ring, float* part, uint64_t* full,
                           uint64_t* empty, uint32_t& gi, float* red, float* wv, int* wi, int* err, unsigned epoch0,
-                          int f, float* ffs, float* xres) {
+                          int f, float* ffs, float* xres, float4* xs) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int EPC = WFmt<FMT>::EPC;
   const int K = ph.K, S = ph.S, R = ph.R, nphys = ph.nphys;
@@ -258,6 +299,16 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
 #pragma unroll
     for (int k = 0; k < 8; ++k) ssq_lane += v[k];
   }
+  // With S <= 2 splits, eight or more warps hold each slice of x: the CTA
+  // then reads x from L2 once into shared memory and the warps take their
+  // slices there (measured: Qwen2.5-0.5B's prologue 6.2 -> 3.8 us; with S = 4
+  // the Llama-3-8B step was slower).
+  const bool staged = S <= 2 && !ph.acc_in && K <= P.xstage_floats;
+  if (staged) {
+    const float4* x4 = reinterpret_cast<const float4*>(ph.x);
+    for (int i = tid; i < K / 4; i += kNC) xs[i] = __ldcg(x4 + i);
+    named_barrier(1, kNC);
+  }
   float xr[MAXC][EPC];
 #pragma unroll
   for (int j = 0; j < MAXC; ++j) {
@@ -265,7 +316,7 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
     if (j < ph.cpl && c < cend) {
 #pragma unroll
       for (int q = 0; q < EPC / 4; ++q) {
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
+        const float4 a = staged ? xs[c * (EPC / 4) + q] : __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
         xr[j][4 * q] = a.x, xr[j][4 * q + 1] = a.y, xr[j][4 * q + 2] = a.z, xr[j][4 * q + 3] = a.w;
       }
       if (FMT == kFmtBF16 && ph.acc_in) {  // the previous layer's down_proj, still in its fixed-point accumulator
@@ -296,6 +347,14 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
       for (int e = 0; e < EPC; ++e) xr[j][e] = 0.f;
     }
   }
+  // Q formats: the inputs as fp32 pairs for the f32x2 dot products.
+  f32x2 x2[FMT == kFmtBF16 ? 1 : MAXC][EPC / 2];
+  if constexpr (FMT != kFmtBF16) {
+#pragma unroll
+    for (int j = 0; j < MAXC; ++j)
+#pragma unroll
+      for (int e = 0; e < EPC / 2; ++e) x2[j][e] = pack_f2(xr[j][2 * e], xr[j][2 * e + 1]);
+  }
   auto row_dot = [&](const uint8_t* rp) {
     float acc = 0.f;
 #pragma unroll
@@ -306,9 +365,9 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
         if constexpr (FMT == kFmtBF16) {
           acc += dot8(w, xr[j]);
         } else if constexpr (FMT == kFmtQ8) {  // weight = d * q, d shared by the two chunks of a block
-          acc = fmaf(dot16_q8(w, xr[j]), half_at(rp + qbytes + (c >> 1) * 2), acc);
+          acc = fmaf(dot16_q8(w, x2[j]), half_at(rp + qbytes + (c >> 1) * 2), acc);
         } else {  // weight = d * (n - 8)
-          acc = fmaf(dot32_q4(w, xr[j]), half_at(rp + qbytes + c * 2), acc);
+          acc = fmaf(dot32_q4(w, x2[j]), half_at(rp + qbytes + c * 2), acc);
         }
       }
     }
@@ -899,6 +958,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
   float* part = reinterpret_cast<float*>(smem + static_cast<size_t>(P.nst) * P.slot_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(part + ((P.part_floats + 1) & ~1));
   uint64_t* empty = full + P.nst;
+  // a GEMV phase's input vector (P.xstage_floats; see mega_gemv), 16-byte aligned
+  float4* xstage = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(empty + P.nst) + 15) & ~uintptr_t(15));
   int* err = &P.st->err;
 
   if (tid == 0) {
@@ -927,11 +988,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_megakernel(const MegaP
       mega_axpy(P, ph, ring, full, empty, gi, ffs, err, f);
     } else {
       if (ph.fmt == kFmtQ8)
-        mega_gemv<2, kFmtQ8>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres);
+        mega_gemv<2, kFmtQ8>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres, xstage);
       else if (ph.fmt == kFmtQ4)
-        mega_gemv<1, kFmtQ4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres);
+        mega_gemv<1, kFmtQ4>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres, xstage);
       else
-        mega_gemv<4, kFmtBF16>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres);
+        mega_gemv<4, kFmtBF16>(P, ph, ring, part, full, empty, gi, red, wv, wi, err, epoch0, f, ffs, xres, xstage);
     }
     if (tid == 0) trace_mark(P, f, 3);
     if (f + 1 < P.nphases && P.phases[f + 1].no_barrier) {
@@ -983,6 +1044,9 @@ bool plan_mega_gemv(MegaPhase& ph, int stage_cap) {
   const int want_pairs = 2 * kCW;
   int R = (want_pairs + S * ph.nphys - 1) / (S * ph.nphys);
   while (R > 1 && R * row_bytes * ph.nphys > static_cast<size_t>(stage_cap)) R /= 2;
+  // Shorter rows (block-quantised ones) take more rows per stage, so the ring
+  // keeps as many bytes in flight as with bf16 rows.
+  R = std::max(R, static_cast<int>(static_cast<size_t>(stage_cap) / (row_bytes * ph.nphys)));
   ph.R = R < 1 ? 1 : R;
   ph.stage_bytes = static_cast<int>(ph.R * row_bytes * ph.nphys);
   return true;

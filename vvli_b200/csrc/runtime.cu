@@ -490,7 +490,13 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   // flight, which lengthens every latency-bound access of the phase changes.
   nst = std::min(nst, getenv("VVLI_MEGA_STAGES") ? std::max(2, atoi(getenv("VVLI_MEGA_STAGES"))) : 2);
   if (nst < 2) return false;
-  c->mega_smem = static_cast<size_t>(nst) * slot + ((part + 1) & ~size_t(1)) * 4 + 2 * nst * sizeof(uint64_t);
+  // GEMV inputs that eight or more warps share (S <= 2) are staged in shared memory.
+  int xstage = 0;
+  for (const MegaPhase& m : ph)
+    if (m.kind == MK_GEMV && m.S <= 2 && !m.acc_in && m.epi != ME_AXPY && m.K <= kMegaXStageMax)
+      xstage = std::max(xstage, m.K);
+  c->mega_smem = static_cast<size_t>(nst) * slot + ((part + 1) & ~size_t(1)) * 4 + 2 * nst * sizeof(uint64_t) +
+                 (xstage ? 16 + static_cast<size_t>(xstage) * 4 : 0);
   if (c->d_phases) cudaFree(c->d_phases);  // a re-plan after a load that changed the weight formats
   c->d_phases = nullptr;
   if (cudaMalloc(&c->d_phases, ph.size() * sizeof(MegaPhase)) != cudaSuccess) return false;
@@ -504,6 +510,7 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   P.nst = nst;
   P.slot_bytes = slot;
   P.part_floats = static_cast<int>(part);
+  P.xstage_floats = xstage;
   P.st = c->st;
   P.seq_tokens = c->seq_tokens;
   P.emb = W + c->off_emb;

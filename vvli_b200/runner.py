@@ -191,7 +191,8 @@ class Runner:
                                 top_k=int(options.top_k), repeat_penalty=float(options.repeat_penalty),
                                 repeat_last_n=int(options.repeat_last_n))
         n_use = min(len(recent), int(options.repeat_last_n))
-        r = np.ascontiguousarray(list(recent)[len(recent) - n_use:], dtype=np.uint32)
+        tail = recent[len(recent) - n_use:] if n_use else recent[:0]  # a view for numpy arrays
+        r = np.ascontiguousarray(tail, dtype=np.uint32)
         assert rng_state.dtype == np.uint64 and rng_state.size == 4 and rng_state.flags["C_CONTIGUOUS"]
         out = ctypes.c_uint32(0)
         check(_abi.lib().vvli_cuda_sample(self._ctx, ctypes.byref(o), None if lg is None else lg.ctypes.data_as(_f32p),
