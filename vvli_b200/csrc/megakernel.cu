@@ -309,51 +309,68 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
     for (int i = tid; i < K / 4; i += kNC) xs[i] = __ldcg(x4 + i);
     named_barrier(1, kNC);
   }
-  float xr[MAXC][EPC];
+  // bf16: the inputs as floats; Q formats: as fp32 pairs for the f32x2 dots.
+  constexpr bool kBf = FMT == kFmtBF16;
+  float xr[kBf ? MAXC : 1][kBf ? EPC : 1];
+  f32x2 x2[kBf ? 1 : MAXC][kBf ? 1 : EPC / 2];
 #pragma unroll
   for (int j = 0; j < MAXC; ++j) {
     const int c = cbeg + lane + kWarp * j;
-    if (j < ph.cpl && c < cend) {
+    const bool live = j < ph.cpl && c < cend;
+    if constexpr (kBf) {
+      if (live) {
 #pragma unroll
-      for (int q = 0; q < EPC / 4; ++q) {
-        const float4 a = staged ? xs[c * (EPC / 4) + q] : __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
-        xr[j][4 * q] = a.x, xr[j][4 * q + 1] = a.y, xr[j][4 * q + 2] = a.z, xr[j][4 * q + 3] = a.w;
-      }
-      if (FMT == kFmtBF16 && ph.acc_in) {  // the previous layer's down_proj, still in its fixed-point accumulator
-        const longlong2* ap = reinterpret_cast<const longlong2*>(ph.acc_in + c * 8);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const longlong2 t = __ldcg(ap + q);
-          xr[j][2 * q] = xr[j][2 * q] + from_fixed(t.x);
-          xr[j][2 * q + 1] = xr[j][2 * q + 1] + from_fixed(t.y);
+        for (int q = 0; q < EPC / 4; ++q) {
+          const float4 a = staged ? xs[c * (EPC / 4) + q] : __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
+          xr[j][4 * q] = a.x, xr[j][4 * q + 1] = a.y, xr[j][4 * q + 2] = a.z, xr[j][4 * q + 3] = a.w;
         }
-        if (warp < S) {  // warps 0..S-1 hold each slice of x once: the sum of squares here
+        if (ph.acc_in) {  // the previous layer's down_proj, still in its fixed-point accumulator
+          const longlong2* ap = reinterpret_cast<const longlong2*>(ph.acc_in + c * 8);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) ssq_lane = fmaf(xr[j][e], xr[j][e], ssq_lane);
+          for (int q = 0; q < 4; ++q) {
+            const longlong2 t = __ldcg(ap + q);
+            xr[j][2 * q] = xr[j][2 * q] + from_fixed(t.x);
+            xr[j][2 * q + 1] = xr[j][2 * q + 1] + from_fixed(t.y);
+          }
+          if (warp < S) {  // warps 0..S-1 hold each slice of x once: the sum of squares here
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ssq_lane = fmaf(xr[j][e], xr[j][e], ssq_lane);
+          }
         }
-      }
-      if (ph.norm_w) {
-#pragma unroll
-        for (int q = 0; q < EPC / 8; ++q) {
-          const uint4 wn = *reinterpret_cast<const uint4*>(ph.norm_w + c * EPC + 8 * q);
+        if (ph.norm_w) {
+          const uint4 wn = *reinterpret_cast<const uint4*>(ph.norm_w + c * EPC);
           const float nw[8] = {bf16_lo(wn.x), bf16_hi(wn.x), bf16_lo(wn.y), bf16_hi(wn.y),
                                bf16_lo(wn.z), bf16_hi(wn.z), bf16_lo(wn.w), bf16_hi(wn.w)};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) xr[j][8 * q + e] = xr[j][8 * q + e] * nw[e];
+          for (int e = 0; e < 8; ++e) xr[j][e] = xr[j][e] * nw[e];
         }
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) xr[j][e] = 0.f;
       }
     } else {
+      if (live) {
 #pragma unroll
-      for (int e = 0; e < EPC; ++e) xr[j][e] = 0.f;
+        for (int q = 0; q < EPC / 4; ++q) {
+          const float4 a = staged ? xs[c * (EPC / 4) + q] : __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
+          x2[j][2 * q] = pack_f2(a.x, a.y);
+          x2[j][2 * q + 1] = pack_f2(a.z, a.w);
+        }
+        if (ph.norm_w) {  // x * w, rounded once per element like the scalar product
+#pragma unroll
+          for (int q = 0; q < EPC / 8; ++q) {
+            const uint4 wn = *reinterpret_cast<const uint4*>(ph.norm_w + c * EPC + 8 * q);
+            const uint32_t ww[4] = {wn.x, wn.y, wn.z, wn.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              x2[j][4 * q + t] = fma_f2(x2[j][4 * q + t], pack_f2(bf16_lo(ww[t]), bf16_hi(ww[t])), 0ull);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPC / 2; ++e) x2[j][e] = 0ull;
+      }
     }
-  }
-  // Q formats: the inputs as fp32 pairs for the f32x2 dot products.
-  f32x2 x2[FMT == kFmtBF16 ? 1 : MAXC][EPC / 2];
-  if constexpr (FMT != kFmtBF16) {
-#pragma unroll
-    for (int j = 0; j < MAXC; ++j)
-#pragma unroll
-      for (int e = 0; e < EPC / 2; ++e) x2[j][e] = pack_f2(xr[j][2 * e], xr[j][2 * e + 1]);
   }
   auto row_dot = [&](const uint8_t* rp) {
     float acc = 0.f;
