@@ -7,7 +7,7 @@
 // padding rows and every weight byte is read once per batch.
 //   * warp 0: TMA producer (W tile 128 x 64 and the X hi / lo tiles NB x 64
 //     per k-block, 128-byte swizzle, no multicast), a ring of stages filling
-//     about 100 KB of shared memory (two CTAs per SM);
+//     about 200 KB of shared memory;
 //   * warp 1: TMEM allocation and the MMA issuer
 //     (tcgen05.mma.cta_group::1.kind::f16, two MMAs per k-step for the hi and
 //     lo halves of the fp32 activations, a second accumulator for the up rows
@@ -42,9 +42,7 @@ struct SkLayout {
   static constexpr uint32_t tile_x = NB * kGemmBK * 2;  // NB rows of 128 bytes
   static constexpr uint32_t w_bytes = (PAIR ? 2 : 1) * kSkTileW;
   static constexpr uint32_t stage = w_bytes + 2 * tile_x;
-  // About 100 KB of stages, so two CTAs share an SM: a matrix with few
-  // 128-row tiles then splits K over twice as many CTAs in one wave.
-  static constexpr int stages = (100 * 1024) / stage < 12 ? (100 * 1024) / stage : 12;
+  static constexpr int stages = (200 * 1024) / stage < 12 ? (200 * 1024) / stage : 12;
   static constexpr int acc_cols = PAIR ? 2 * NB : NB;
   static constexpr uint32_t tmem_cols = acc_cols < 32 ? 32 : acc_cols;
   static constexpr size_t smem = static_cast<size_t>(stages) * stage + 1024 + 256;
@@ -72,7 +70,7 @@ VVLI_DEV void tmem_ld_nb(uint32_t taddr, float* v) {
 }
 
 template <int EPI, int NB>
-__global__ void __launch_bounds__(kSkThreads, 2)
+__global__ void __launch_bounds__(kSkThreads, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tm_x_hi, const __grid_constant__ CUtensorMap tm_x_lo,
                        const __grid_constant__ CUtensorMap tm_w, const GemmParams p) {
   constexpr bool kPair = EPI == GE_SILU;
@@ -352,7 +350,7 @@ int skinny_split(int epi, int M, int N, int nk, int sm_count) {
   const int* maxc = g_max_clusters[epi < 0 || epi > 2 ? 1 : epi][skinny_nb(M) == 16 ? 0 : 1];
   int best = 1;
   for (int S = 2; S <= std::min(kSkMaxSplit, nk); ++S)
-    if (tiles * S <= 2 * sm_count && tiles <= maxc[S]) best = S;
+    if (tiles * S <= sm_count && tiles <= maxc[S]) best = S;
   return best;
 }
 

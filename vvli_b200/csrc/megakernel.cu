@@ -239,13 +239,13 @@ VVLI_DEV f32x2 bytes_as_f2(uint32_t t, int k, f32x2 neg_bias) {
 VVLI_DEV float dot16_q8(uint4 w, const f32x2* x2) {
   const uint32_t wd[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
   const f32x2 nb = pack_f2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-  f32x2 acc = 0ull;
+  f32x2 acc[2] = {0ull, 0ull};  // two independent chains
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
-    acc = fma_f2(bytes_as_f2(wd[m], 0, nb), x2[2 * m], acc);
-    acc = fma_f2(bytes_as_f2(wd[m], 2, nb), x2[2 * m + 1], acc);
+    acc[0] = fma_f2(bytes_as_f2(wd[m], 0, nb), x2[2 * m], acc[0]);
+    acc[1] = fma_f2(bytes_as_f2(wd[m], 2, nb), x2[2 * m + 1], acc[1]);
   }
-  return sum_f2(acc);
+  return sum_f2(add_f2(acc[0], acc[1]));
 }
 
 // sum_i (n_i - 8) * x_i over the 32 nibbles of a Q4_0 block: byte j holds
@@ -253,16 +253,16 @@ VVLI_DEV float dot16_q8(uint4 w, const f32x2* x2) {
 VVLI_DEV float dot32_q4(uint4 w, const f32x2* x2) {
   const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
   const f32x2 nb = pack_f2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
-  f32x2 acc = 0ull;
+  f32x2 acc[4] = {0ull, 0ull, 0ull, 0ull};  // four independent chains
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     const uint32_t lo = wd[m] & 0x0F0F0F0Fu, hi = (wd[m] >> 4) & 0x0F0F0F0Fu;
-    acc = fma_f2(bytes_as_f2(lo, 0, nb), x2[2 * m], acc);
-    acc = fma_f2(bytes_as_f2(lo, 2, nb), x2[2 * m + 1], acc);
-    acc = fma_f2(bytes_as_f2(hi, 0, nb), x2[8 + 2 * m], acc);
-    acc = fma_f2(bytes_as_f2(hi, 2, nb), x2[8 + 2 * m + 1], acc);
+    acc[0] = fma_f2(bytes_as_f2(lo, 0, nb), x2[2 * m], acc[0]);
+    acc[1] = fma_f2(bytes_as_f2(lo, 2, nb), x2[2 * m + 1], acc[1]);
+    acc[2] = fma_f2(bytes_as_f2(hi, 0, nb), x2[8 + 2 * m], acc[2]);
+    acc[3] = fma_f2(bytes_as_f2(hi, 2, nb), x2[8 + 2 * m + 1], acc[3]);
   }
-  return sum_f2(acc);
+  return sum_f2(add_f2(add_f2(acc[0], acc[1]), add_f2(acc[2], acc[3])));
 }
 
 VVLI_DEV float half_at(const uint8_t* p) { return __half2float(*reinterpret_cast<const __half*>(p)); }
@@ -303,10 +303,19 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
   // then reads x from L2 once into shared memory and the warps take their
   // slices there (measured: Qwen2.5-0.5B's prologue 6.2 -> 3.8 us; with S = 4
   // the Llama-3-8B step was slower).
-  const bool staged = S <= 2 && !ph.acc_in && K <= P.xstage_floats;
+  // Block-quantised phases stage x too: a lane's 16 or 32 inputs lie 64 or
+  // 128 bytes apart from its neighbours', a pattern that serves L2 poorly.
+  // Shared memory holds chunk c's float4 q at c * P4 + (q ^ sw(c)), so the 8
+  // lanes of one 128-bit access hit different banks.
+  constexpr int P4 = EPC / 4;  // float4s per chunk
+  const bool staged = (S <= 2 || FMT != kFmtBF16) && !ph.acc_in && K <= P.xstage_floats;
+  auto sw = [](int c) { return P4 == 8 ? (c & 7) : P4 == 4 ? ((c >> 1) & 3) : ((c >> 2) & 1); };
   if (staged) {
     const float4* x4 = reinterpret_cast<const float4*>(ph.x);
-    for (int i = tid; i < K / 4; i += kNC) xs[i] = __ldcg(x4 + i);
+    for (int i = tid; i < K / 4; i += kNC) {
+      const int c = i / P4, q = i % P4;
+      xs[c * P4 + (q ^ sw(c))] = __ldcg(x4 + i);
+    }
     named_barrier(1, kNC);
   }
   // bf16: the inputs as floats; Q formats: as fp32 pairs for the f32x2 dots.
@@ -321,7 +330,7 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
       if (live) {
 #pragma unroll
         for (int q = 0; q < EPC / 4; ++q) {
-          const float4 a = staged ? xs[c * (EPC / 4) + q] : __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
+          const float4 a = staged ? xs[c * P4 + (q ^ sw(c))] : __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
           xr[j][4 * q] = a.x, xr[j][4 * q + 1] = a.y, xr[j][4 * q + 2] = a.z, xr[j][4 * q + 3] = a.w;
         }
         if (ph.acc_in) {  // the previous layer's down_proj, still in its fixed-point accumulator
@@ -352,7 +361,7 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
       if (live) {
 #pragma unroll
         for (int q = 0; q < EPC / 4; ++q) {
-          const float4 a = staged ? xs[c * (EPC / 4) + q] : __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
+          const float4 a = staged ? xs[c * P4 + (q ^ sw(c))] : __ldcg(reinterpret_cast<const float4*>(ph.x + c * EPC + 4 * q));
           x2[j][2 * q] = pack_f2(a.x, a.y);
           x2[j][2 * q + 1] = pack_f2(a.z, a.w);
         }

@@ -490,10 +490,12 @@ bool plan_megakernel(vvli_ctx* c, int smem_optin) {
   // flight, which lengthens every latency-bound access of the phase changes.
   nst = std::min(nst, getenv("VVLI_MEGA_STAGES") ? std::max(2, atoi(getenv("VVLI_MEGA_STAGES"))) : 2);
   if (nst < 2) return false;
-  // GEMV inputs that eight or more warps share (S <= 2) are staged in shared memory.
+  // GEMV inputs that eight or more warps share (S <= 2), and those of
+  // block-quantised phases, are staged in shared memory.
   int xstage = 0;
   for (const MegaPhase& m : ph)
-    if (m.kind == MK_GEMV && m.S <= 2 && !m.acc_in && m.epi != ME_AXPY && m.K <= kMegaXStageMax)
+    if (m.kind == MK_GEMV && (m.S <= 2 || m.fmt != kFmtBF16) && !m.acc_in && m.epi != ME_AXPY &&
+        m.K <= kMegaXStageMax)
       xstage = std::max(xstage, m.K);
   c->mega_smem = static_cast<size_t>(nst) * slot + ((part + 1) & ~size_t(1)) * 4 + 2 * nst * sizeof(uint64_t) +
                  (xstage ? 16 + static_cast<size_t>(xstage) * 4 : 0);
