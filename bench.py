@@ -56,7 +56,9 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=16, help="rows of the decode-batch measurement (0: skip)")
     ap.add_argument("--long-prompt", type=int, default=4096,
                     help="tokens of the long-prompt prefill on the Llama-3.2-1B architecture (BASELINE config 3; 0: skip)")
-    ap.add_argument("--profile", choices=["none", "prefill", "batch", "decode"], default="none",
+    ap.add_argument("--format", choices=["bf16", "q8_0", "q4_0"], default="bf16",
+                    help="weight format of the --profile decode case (block-quantised on the device)")
+    ap.add_argument("--profile", choices=["none", "prefill", "batch", "decode", "sample"], default="none",
                     help="run one call of that kind inside a CUDA profiler range (for ncu --profile-from-start off) "
                          "on a --layers cut of the model, print nothing, exit")
     return ap.parse_args()
@@ -448,9 +450,23 @@ def profile_case(args):
         def call():
             r.reset()
             r.prefill(prompt, 0, logits=False)
-    else:
+    elif args.profile == "sample":
+        # Sampler.next with the reference's default options over the last forward's logits
         r = vvli_b200.Runner(cfg, max_seq=args.prompt + 64)
         r.fill_synthetic(args.seed)
+        r.prefill(prompt, 0, logits=False)
+        sopt = vvli_b200.Options()
+        recent = np.arange(1, 65, dtype=np.uint32)
+        state = np.array([1, 2, 3, 4], dtype=np.uint64)
+        for _ in range(3):
+            r.sample(sopt, recent, state)
+        call = lambda: r.sample(sopt, recent, state)
+    else:
+        r = vvli_b200.Runner(cfg, max_seq=args.prompt + 64)
+        if args.format == "bf16":
+            r.fill_synthetic(args.seed)
+        else:
+            r.fill_synthetic_quantized(args.seed, args.format)
         r.prefill(prompt, 0, logits=False)
         r.decode(3)
         call = lambda: r.decode(2)

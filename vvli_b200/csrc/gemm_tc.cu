@@ -40,7 +40,8 @@ struct TcLayout {
   static constexpr int stages = (192 * 1024) / stage;
   static constexpr uint32_t tmem_cols = 2 * BN;  // two accumulators: tile i + 1's MMAs run during tile i's epilogue
   static constexpr uint32_t idesc = umma_idesc(kGemmBM, BN);
-  static constexpr size_t smem = static_cast<size_t>(stages) * stage + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr size_t smem =
+      static_cast<size_t>(stages) * stage + 1024 /*align*/ + 256 /*barriers*/ + 4 * 32 * 33 * 4 /*epilogue tiles*/;
 };
 
 // ---------------------------------------------------------------- GEMM kernel
@@ -64,6 +65,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tmem_full = empty + kGemmStages;  // [2] an accumulator holds a finished tile
   uint64_t* tmem_empty = tmem_full + 2;       // [2] the epilogue has read it
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  // epilogue warps' 32 x 33 transpose tiles, after the 256 bytes of barriers
+  float* epi_t = reinterpret_cast<float*>(sm + kGemmStages * kStageBytes + 256) + ((threadIdx.x >> 5) & 3) * 32 * 33;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr bool kPair = EPI == GE_SILU;
   // Persistent: CTA b takes tiles b, b + grid, ...  Row tiles vary fastest,
@@ -152,72 +155,88 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
     const int buf = i & 1;
     const int m0 = tile_m0(t), n0 = tile_n0(t);
-    const int row = m0 + wq * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(buf * BN);
     // tcgen05.ld is warp-collective: the warp goes on only if every lane saw the accumulator.
     if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[buf], (i >> 1) & 1, p.err))) break;
     {
+      // The accumulator arrives one row per lane (TMEM lane = row); each
+      // 32 x 32 chunk is turned around in this warp's shared tile so that the
+      // lanes then walk a row's 32 consecutive columns: every global load
+      // and store of the epilogue is a coalesced row segment.
       tc_fence_after();
       float v[32];
+      const int wrow0 = m0 + wq * 32;  // first row of this warp's 32
+      auto transpose_in = [&](const float* src) {
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) epi_t[lane * 33 + j] = src[j];
+        __syncwarp();
+      };
       if constexpr (EPI == GE_SILU) {
         float u[32];
         for (int c = 0; c < 4; ++c) {
           tmem_ld32(trow + c * 32, v);        // gate columns
           tmem_ld32(trow + 128 + c * 32, u);  // up columns
-          if (row < p.M) {
-            uint16_t* oh = p.out_hi + static_cast<size_t>(row) * p.ld_out;
-            uint16_t* ol = p.out_lo + static_cast<size_t>(row) * p.ld_out;
+          float g[32];
+          transpose_in(v);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int n = n0 + c * 32 + i;
-              if (n < p.N) {
-                const float g = v[i];
-                const float f = (g / (1.0f + expf(-g))) * u[i];  // siluMulInto, src/llm.zig:1382-1387
-                split_bf16(f, oh[n], ol[n]);
-              }
+          for (int r = 0; r < 32; ++r) g[r] = epi_t[r * 33 + lane];
+          transpose_in(u);
+          const int n = n0 + c * 32 + lane;
+          if (n < p.N) {
+#pragma unroll
+            for (int r = 0; r < 32; ++r) {
+              const int row_r = wrow0 + r;
+              if (row_r >= p.M) break;
+              const float f = (g[r] / (1.0f + expf(-g[r]))) * epi_t[r * 33 + lane];  // siluMulInto, src/llm.zig:1382-1387
+              const size_t o = static_cast<size_t>(row_r) * p.ld_out + n;
+              split_bf16(f, p.out_hi[o], p.out_lo[o]);
             }
           }
         }
       } else {
         for (int c = 0; c < BN / 32; ++c) {
           tmem_ld32(trow + c * 32, v);
-          if (row >= p.M) continue;
-          const int nb = n0 + c * 32;
+          transpose_in(v);
+          const int n = n0 + c * 32 + lane;
           if constexpr (EPI == GE_RESID) {
-            float* y = p.y + static_cast<size_t>(row) * p.ldy;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (nb + i < p.N) y[nb + i] = (p.add_residual ? y[nb + i] : 0.f) + v[i];  // addInto
-          } else {  // GE_QKV
-            const int pos = p.pos0 + row;
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const int n = nb + i;
-              if (n >= p.N) break;
-              float a = v[i], b = v[i + 1];
-              if (p.bias) {
-                a = a + bf16_to_f32(p.bias[n]);
-                b = b + bf16_to_f32(p.bias[n + 1]);
+            if (n < p.N) {
+#pragma unroll 4
+              for (int r = 0; r < 32; ++r) {
+                const int row_r = wrow0 + r;
+                if (row_r >= p.M) break;
+                float* y = p.y + static_cast<size_t>(row_r) * p.ldy + n;
+                *y = (p.add_residual ? *y : 0.f) + epi_t[r * 33 + lane];  // addInto
               }
-              if (n < p.q_rows + p.kv_rows) {  // q and k rows hold rotary pairs side by side
-                const float ang = static_cast<float>(pos) * rope_inv_freq(p.rope, n % p.d, p.d);
+            }
+          } else {  // GE_QKV: column n of rows wrow0 ..; rotary pairs (n, n ^ 1) sit in neighbouring lanes
+            const bool live = n < p.N;
+            const bool rot = n < p.q_rows + p.kv_rows;  // q and k rows hold rotary pairs side by side
+            const bool odd = n & 1;
+            const float bias = live && p.bias ? bf16_to_f32(p.bias[n]) : 0.f;
+            const float inv_freq = rot ? rope_inv_freq(p.rope, (n & ~1) % p.d, p.d) : 0.f;
+            const bool is_k = !(n < p.q_rows) && rot;
+            const int rel = n < p.q_rows ? 0 : (is_k ? n - p.q_rows : n - p.q_rows - p.kv_rows);
+            float* cache = is_k ? p.k_cache : p.v_cache;
+            for (int r = 0; r < 32; ++r) {
+              const int row_r = wrow0 + r;
+              if (row_r >= p.M) break;
+              float x = epi_t[r * 33 + lane];
+              if (p.bias) x = x + bias;
+              const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
+              const int pos = p.pos0 + row_r;
+              if (rot) {
+                const float ang = static_cast<float>(pos) * inv_freq;
                 float sn, cs;
                 sincosf(ang, &sn, &cs);
-                const float x0 = a, x1 = b;
-                a = x0 * cs - x1 * sn;
-                b = x0 * sn + x1 * cs;
+                const float x0 = odd ? partner : x, x1 = odd ? x : partner;
+                x = odd ? x0 * sn + x1 * cs : x0 * cs - x1 * sn;
               }
-              if (n < p.q_rows) {
-                p.y[static_cast<size_t>(row) * p.ldy + n] = a;
-                p.y[static_cast<size_t>(row) * p.ldy + n + 1] = b;
-              } else {
-                const bool is_k = n < p.q_rows + p.kv_rows;
-                const int rel = is_k ? n - p.q_rows : n - p.q_rows - p.kv_rows;
-                const size_t off = kv_off(p.page_table, pos, rel / p.d, p.nkv, p.d) + rel % p.d;
-                float* cache = is_k ? p.k_cache : p.v_cache;
-                cache[off] = a;
-                cache[off + 1] = b;
-              }
+              if (!live) continue;
+              if (n < p.q_rows)
+                p.y[static_cast<size_t>(row_r) * p.ldy + n] = x;
+              else
+                cache[kv_off(p.page_table, pos, rel / p.d, p.nkv, p.d) + rel % p.d] = x;
             }
           }
         }
