@@ -247,8 +247,6 @@ struct vvli_ctx {
   SampleState* smp_state = nullptr;
   SampleState* h_smp_state = nullptr;
   uint32_t* h_smp_recent = nullptr;  // page-locked staging of the recent tokens
-  void* smp_temp = nullptr;
-  size_t smp_temp_bytes = 0;
   unsigned smp_call = 0;
 };
 
@@ -1051,7 +1049,7 @@ void free_ctx(vvli_ctx* c) {
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
                  c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->w_downT, c->acc, c->pf_x, c->pf_q,
                  c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->pf_kvt, c->smp_stamp, c->smp_key32,
-                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_state, c->smp_temp,
+                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_state,
                  c->bt_x, c->bt_q, c->bt_logits, c->bt_best, c->bt_all_best, c->bt_part, c->bt_logits_all, c->bt_ahi,
                  c->bt_alo, c->bt_fhi, c->bt_flo, c->bt_tokens, c->bt_pos, c->bt_idx, c->bt_counters};
   for (void* p : dev)
@@ -1869,14 +1867,12 @@ int ensure_sampler(vvli_ctx* c) {
     const cudaError_t e = cudaMalloc(p, bytes);
     return e == cudaSuccess ? VVLI_OK : cuda_fail(e, "sampler buffers");
   };
-  c->smp_temp_bytes = sample_sort_temp_bytes(c->V);
   if ((st = alloc(reinterpret_cast<void**>(&c->smp_stamp), V * 4)) ||
       (st = alloc(reinterpret_cast<void**>(&c->smp_key32), V * 4)) ||
       (st = alloc(reinterpret_cast<void**>(&c->smp_key64), V * 8)) ||
       (st = alloc(reinterpret_cast<void**>(&c->smp_key64_sorted), V * 8)) ||
       (st = alloc(reinterpret_cast<void**>(&c->smp_probs), V * 4)) ||
       (st = alloc(reinterpret_cast<void**>(&c->smp_logits), V * 4)) ||
-      (st = alloc(&c->smp_temp, std::max<size_t>(c->smp_temp_bytes, 16))) ||
       (st = alloc(reinterpret_cast<void**>(&c->smp_state), kSampleStateBytes + kSampleRecentCap * 4)))
     return st;
   // The step state and the recent tokens sit in one block (device and
@@ -1964,6 +1960,7 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
   h->token = -1;
   h->path = 0;
   h->k = 0;
+  h->n_sort = 0;
   CK(cudaMemcpyAsync(c->smp_state, h, kSampleStateBytes + (fold ? n_use * 4 : 0), cudaMemcpyHostToDevice,
                      c->stream));
   if (fast) {
@@ -1976,7 +1973,7 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
   CK(cudaMemcpyAsync(h, c->smp_state, sizeof(SampleState), cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   if (h->path == 1) {
-    CK(launch_sample_long(p, c->smp_temp, c->smp_temp_bytes, c->stream));
+    CK(launch_sample_long(p, h->n_sort, c->stream));
     CK(cudaMemcpyAsync(h, c->smp_state, sizeof(SampleState), cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
   }

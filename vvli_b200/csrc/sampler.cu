@@ -14,18 +14,19 @@
 //   4. exp((l - max) / T), the sequential fp32 sums, the top-p cut and the
 //      cumulative draw (prepareProbabilities/sampleCandidate, :428-463) on one
 //      thread, in the reference's order, so the sums round the same way.
-// Longer candidate lists (top_k = 0 or > kSampleSmallK) sort the whole
-// vocabulary's keys (CUB radix sort of 64-bit (key, ~id) pairs) and run
-// step 4 over the sorted list.  There, once a probability is below half an
-// ulp of the running sum, every later one is too (the list is sorted), so
-// the sum can no longer change and the scan stops.
+// Longer candidate lists (top_k = 0 or > kSampleSmallK) run step 4 over the
+// sorted list, where the scan stops at the first probability below half an
+// ulp of its running sum (every later one is smaller: the sum can no longer
+// change).  The running sum is >= 1 from the first candidate on (the maximum,
+// exp(0)), so a candidate with (l - max) / T < -17.5 (probability below
+// 2.6e-8 < 2^-24) is never reached: only the keys above that cut are sorted,
+// in 8,192-key chunks in shared memory, each key then placed by its rank
+// among the other chunks (binary searches).
 //
 // The uniform draw is random.float(f32) of Zig's DefaultPrng: xoshiro256++
 // (the published generator) with the float built from 23 mantissa bits and a
 // leading-zero count for the exponent.  It is drawn only when the reference
 // draws it: temperature > 0 and at least one finite candidate.
-#include <cub/device/device_radix_sort.cuh>
-
 #include "common.cuh"
 #include "sampler.cuh"
 
@@ -35,6 +36,8 @@ namespace {
 constexpr int kST = 1024;   // threads of the sampling CTA
 constexpr int kBins = 4096;  // radix-select histogram (12 bits)
 constexpr size_t kSampleSmem = static_cast<size_t>(kSampleSmallK) * (8 + 4);
+constexpr int kSortChunk = 8192;       // keys sorted per CTA on the long path
+constexpr float kLongCut = -17.5f;     // (l - max) / T below this: never reached by the long path's scan
 
 // Finite floats -> unsigned keys in the same order (never 0; +0 and -0 equal).
 VVLI_DEV unsigned order_key(float s) {
@@ -407,13 +410,30 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(const SampleParams p) {
                                                 : (p.top_k < static_cast<unsigned long long>(V) ? p.top_k : V);
   const unsigned k = static_cast<unsigned>(limit < n_finite ? limit : n_finite);
   if (k > static_cast<unsigned>(kSampleSmallK)) {
-    for (int i = tid; i < V; i += kST) {
-      const unsigned kk = p.key32[i];
-      p.key64[i] = kk ? make_key64(kk, i) : 0ull;
-    }
+    // The keys that the long path's scan can reach, compacted in id order.
+    unsigned km = 0;
+    for (int i = tid; i < V; i += kST) km = max(km, p.key32[i]);
+    km = __reduce_max_sync(0xffffffffu, km);
+    if ((tid & 31) == 0) wsum[tid >> 5] = km;
+    __syncthreads();
+    km = 0;
+    for (int w = 0; w < kST / 32; ++w) km = max(km, wsum[w]);
+    __syncthreads();
+    const float mx = key_value(km);
+    const float t = fmaxf(p.temperature, 1e-6f);
+    auto keep = [&](unsigned kk) { return kk != 0 && (key_value(kk) - mx) / t >= kLongCut; };
+    const int C = (V + kST - 1) / kST;
+    const int i0 = min(V, tid * C), i1 = min(V, i0 + C);
+    unsigned nk = 0;
+    for (int i = i0; i < i1; ++i) nk += keep(p.key32[i]) ? 1u : 0u;
+    unsigned n_keep;
+    unsigned o = block_excl_scan(nk, wsum, &n_keep);
+    for (int i = i0; i < i1; ++i)
+      if (keep(p.key32[i])) p.key64[o++] = make_key64(p.key32[i], i);
     if (tid == 0) {
       st->path = 1;
-      st->k = static_cast<int>(k);
+      st->k = static_cast<int>(min(k, n_keep));
+      st->n_sort = static_cast<int>(n_keep);
     }
     return;
   }
@@ -502,7 +522,62 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(const SampleParams p) {
   finish_sorted(p, cand, probs, k);
 }
 
-// Step 4 over the first st->k keys of the sorted vocabulary.
+// Sorts keys[c * kSortChunk ..] (n keys in all) descending, chunk c per CTA,
+// into out (which may be keys).
+__global__ void __launch_bounds__(1024) sort_chunk_kernel(const unsigned long long* keys, int n,
+                                                          unsigned long long* out) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned long long* a = reinterpret_cast<unsigned long long*>(smem);  // [kSortChunk]
+  const int base = blockIdx.x * kSortChunk;
+  const int len = min(kSortChunk, n - base);
+  int N = 64;
+  while (N < len) N <<= 1;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) a[i] = i < len ? keys[base + i] : 0ull;
+  __syncthreads();
+  for (int size = 2; size <= N; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < N / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const unsigned long long x = a[lo], y = a[hi];
+        if ((x < y) == desc) {
+          a[lo] = y;
+          a[hi] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < len; i += blockDim.x) out[base + i] = a[i];
+}
+
+// Key g of the sorted chunks goes to its place in the whole list: its index
+// in its chunk plus, for every other chunk, the number of keys there above it
+// (keys are distinct: the id is part of the key).
+__global__ void rank_place_kernel(const unsigned long long* chunks, int n, unsigned long long* out) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  const unsigned long long x = chunks[g];
+  const int mine = g / kSortChunk;
+  int pos = g - mine * kSortChunk;
+  for (int c = 0; c * kSortChunk < n; ++c) {
+    if (c == mine) continue;
+    const unsigned long long* a = chunks + static_cast<size_t>(c) * kSortChunk;
+    int lo = 0, hi = min(kSortChunk, n - c * kSortChunk);  // first index with a[idx] < x
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (a[mid] > x)
+        lo = mid + 1;
+      else
+        hi = mid;
+    }
+    pos += lo;
+  }
+  out[pos] = x;
+}
+
+// Step 4 over the first st->k keys of the sorted candidates.
 __global__ void __launch_bounds__(kST, 1) sample_long_kernel(const SampleParams p) {
   SampleState* st = p.st;
   const int k = st->k;
@@ -541,7 +616,7 @@ __global__ void __launch_bounds__(kST, 1) sample_long_kernel(const SampleParams 
   if (total2 > 0.0f && isfinite(total2)) {
     const float target = fminf(u, 0.99999994f) * total2;
     float cum = 0.0f;
-    tok = key64_id(keys[count - 1]);
+    tok = key64_id(keys[min(count, k) - 1]);
     for (int j = 0; j < count; ++j) {
       if (negligible(pr[j], cum)) break;
       cum += pr[j];
@@ -569,17 +644,16 @@ cudaError_t launch_sample(const SampleParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-size_t sample_sort_temp_bytes(int V) {
-  size_t bytes = 0;
-  cub::DeviceRadixSort::SortKeysDescending(nullptr, bytes, static_cast<unsigned long long*>(nullptr),
-                                           static_cast<unsigned long long*>(nullptr), V);
-  return bytes;
-}
-
-cudaError_t launch_sample_long(const SampleParams& p, void* temp, size_t temp_bytes, cudaStream_t s) {
-  size_t bytes = temp_bytes;
-  cudaError_t e = cub::DeviceRadixSort::SortKeysDescending(temp, bytes, p.key64, p.key64_sorted, p.V, 0, 64, s);
-  if (e != cudaSuccess) return e;
+cudaError_t launch_sample_long(const SampleParams& p, int n_sort, cudaStream_t s) {
+  if (n_sort < 1 || n_sort > p.V) return cudaErrorInvalidValue;
+  const int chunks = (n_sort + kSortChunk - 1) / kSortChunk;
+  const size_t smem = static_cast<size_t>(kSortChunk) * 8;
+  if (chunks == 1) {
+    sort_chunk_kernel<<<1, 1024, smem, s>>>(p.key64, n_sort, p.key64_sorted);
+  } else {
+    sort_chunk_kernel<<<chunks, 1024, smem, s>>>(p.key64, n_sort, p.key64);
+    rank_place_kernel<<<(n_sort + 255) / 256, 256, 0, s>>>(p.key64, n_sort, p.key64_sorted);
+  }
   sample_long_kernel<<<1, kST, 0, s>>>(p);
   return cudaGetLastError();
 }
@@ -597,6 +671,8 @@ cudaError_t launch_sample_fast(const SampleParams& p, int k, unsigned long long*
 
 cudaError_t configure_sampler() {
   cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSampleSmem));
+  if (e) return e;
+  e = cudaFuncSetAttribute(sort_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSortChunk * 8);
   if (e) return e;
   return cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(static_cast<size_t>(kSampleFastMaxCand) * 8 + kSampleFastK * 4));

@@ -20,8 +20,8 @@ struct SampleState {
   unsigned long long rng[4];  // xoshiro256++ state, advanced when a draw happens
   int token;                  // result
   int path;                   // 0: token is final; 1: the long-candidate path must run
-  int k;                      // candidates of the long path
-  int pad;
+  int k;                      // candidates of the long path's scan
+  int n_sort;                 // keys the long path sorts (those its scan can reach)
 };
 
 struct SampleParams {
@@ -35,8 +35,8 @@ struct SampleParams {
   float temperature, top_p, repeat_penalty;
   unsigned long long top_k;
   unsigned* key32;            // [V] scratch: order-preserving keys of the finite adjusted logits, 0 = none
-  unsigned long long* key64;  // [V] scratch: (key32 << 32) | ~id, input of the long path's sort
-  unsigned long long* key64_sorted;
+  unsigned long long* key64;  // [V] scratch: (key32 << 32) | ~id of the long path's candidates, unsorted
+  unsigned long long* key64_sorted;  // [V] scratch: the same keys, descending
   float* probs;               // [V] scratch of the long path
   SampleState* st;
 };
@@ -47,10 +47,10 @@ cudaError_t launch_sample_mark(const uint32_t* recent, int n, unsigned* stamp, u
 // Greedy-with-penalties or the whole short-candidate sampling path; sets
 // st->path = 1 when the candidate list is longer than kSampleSmallK.
 cudaError_t launch_sample(const SampleParams& p, cudaStream_t s);
-// The long-candidate path: sort the vocabulary's keys, then probabilities,
-// top-p and the draw over the first st->k.
-cudaError_t launch_sample_long(const SampleParams& p, void* temp, size_t temp_bytes, cudaStream_t s);
-size_t sample_sort_temp_bytes(int V);
+// The long-candidate path: sort the st->n_sort keys that launch_sample left
+// in key64 (n_sort, read back by the host), then probabilities, top-p and
+// the draw over the first st->k.
+cudaError_t launch_sample_long(const SampleParams& p, int n_sort, cudaStream_t s);
 // top_k in [1, kSampleFastK] with temperature > 0; cand holds ceil(V / 1024) * k keys,
 // nfin ceil(V / 1024) counts.
 cudaError_t launch_sample_fast(const SampleParams& p, int k, unsigned long long* cand, unsigned* nfin, cudaStream_t s);
