@@ -105,6 +105,27 @@ def test_device_sampler_matches_oracle(oracle, vv, V):
     r.close()
 
 
+@pytest.mark.parametrize("last_n", [256, 257, 4096, 5000])
+def test_device_sampler_long_repeat_windows(oracle, vv, last_n):
+    # The top-k step takes up to 256 recent tokens in its launch parameters,
+    # up to 4096 through one copy, and more as per-token stamps.
+    V = 150000
+    rng = np.random.default_rng(last_n)
+    r = runner_with_vocab(vv, V)
+    state = np.array(S.Xoshiro256(99).s, dtype=np.uint64)
+    recent = rng.integers(0, V, last_n + 10).tolist()
+    for lg in logits_cases(V, rng)[:3]:
+        lg = lg.copy()
+        lg[recent[-5:]] += 20.0  # the penalised tokens would win without the penalty
+        for top_k, rp in ((40, 1.3), (64, 4.0), (1, 1.1)):
+            o = opts(0.9, 0.95, top_k, rp, last_n)
+            want_tok, want_state = expected(oracle, lg, recent, [], o, state)
+            got = r.sample(o, recent[len(recent) - last_n:], state, logits=lg)
+            assert got == want_tok, (last_n, top_k, rp)
+            assert np.array_equal(state, want_state), (last_n, top_k, rp)
+    r.close()
+
+
 def test_device_sampler_on_forward_logits(oracle, vv):
     # The logits of the last forward stay on the device; same result as passing them in.
     from make_golden import fixture_configs

@@ -247,6 +247,9 @@ struct vvli_ctx {
   SampleState* smp_state = nullptr;
   SampleState* h_smp_state = nullptr;
   uint32_t* h_smp_recent = nullptr;  // page-locked staging of the recent tokens
+  SampleState* h_smp_out = nullptr;  // fused top-k step's result: page-locked host memory the kernel writes
+  SampleState* d_smp_out = nullptr;  // its device address
+  unsigned* smp_done = nullptr;      // fused top-k step's CTA counter
   unsigned smp_call = 0;
 };
 
@@ -1049,7 +1052,7 @@ void free_ctx(vvli_ctx* c) {
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
                  c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->w_downT, c->acc, c->pf_x, c->pf_q,
                  c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->pf_kvt, c->smp_stamp, c->smp_key32,
-                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_state,
+                 c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_state, c->smp_done,
                  c->bt_x, c->bt_q, c->bt_logits, c->bt_best, c->bt_all_best, c->bt_part, c->bt_logits_all, c->bt_ahi,
                  c->bt_alo, c->bt_fhi, c->bt_flo, c->bt_tokens, c->bt_pos, c->bt_idx, c->bt_counters};
   for (void* p : dev)
@@ -1057,6 +1060,7 @@ void free_ctx(vvli_ctx* c) {
   if (c->h_st) cudaFreeHost(c->h_st);
   if (c->h_tok) cudaFreeHost(c->h_tok);
   if (c->h_smp_state) cudaFreeHost(c->h_smp_state);  // the recent-token staging lives in the same block
+  if (c->h_smp_out) cudaFreeHost(c->h_smp_out);
   if (c->ev0) cudaEventDestroy(c->ev0);
   if (c->ev1) cudaEventDestroy(c->ev1);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -1879,6 +1883,10 @@ int ensure_sampler(vvli_ctx* c) {
   // page-locked host), so one copy sends both.
   c->smp_recent = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(c->smp_state) + kSampleStateBytes);
   CK(cudaMallocHost(&c->h_smp_state, kSampleStateBytes + kSampleRecentCap * 4));
+  if ((st = alloc(reinterpret_cast<void**>(&c->smp_done), 4))) return st;
+  CK(cudaMemset(c->smp_done, 0, 4));
+  CK(cudaHostAlloc(&c->h_smp_out, kSampleStateBytes, cudaHostAllocMapped));
+  CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->d_smp_out), c->h_smp_out, 0));
   c->h_smp_recent = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(c->h_smp_state) + kSampleStateBytes);
   CK(cudaMemset(c->smp_stamp, 0, V * 4));
   CK(configure_sampler());
@@ -1918,8 +1926,9 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
   const bool penalise = o->repeat_penalty > 1.0f && o->repeat_last_n > 0 && n_recent > 0;
   const uint64_t n_use = penalise ? std::min<uint64_t>(n_recent, o->repeat_last_n) : 0;
   const uint32_t* src = recent + (n_recent - n_use);
-  // The top-k path reads the recent tokens itself (they travel with the step
-  // state); the other paths read per-token stamps marked here.
+  // The top-k path reads the recent tokens itself (in its launch's parameters,
+  // or one copy when there are many); the other paths read per-token stamps
+  // marked here.
   const bool fold = fast && n_use <= static_cast<uint64_t>(kSampleRecentCap);
   if (!fold && ++c->smp_call == 0) {  // the stamps wrapped: start over
     CK(cudaMemsetAsync(c->smp_stamp, 0, static_cast<size_t>(c->V) * 4, c->stream));
@@ -1949,11 +1958,42 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
   p.key64_sorted = c->smp_key64_sorted;
   p.probs = c->smp_probs;
   p.st = c->smp_state;
-  if (fold) {
-    p.stamp = nullptr;
-    p.recent = c->smp_recent;
-    p.n_recent = static_cast<int>(n_use);
-    if (n_use) std::memcpy(c->h_smp_recent, src, n_use * 4);
+  if (fast) {
+    // One launch: the state and up to kSampleArgRecent recent tokens travel in
+    // its parameters, the result comes back through mapped host memory.
+    FastSampleArgs a{};
+    a.p = p;
+    std::memcpy(a.rng, rng_state, sizeof(a.rng));
+    a.k = static_cast<int>(limit);
+    a.nlists = nlists;
+    a.cand = c->smp_key64;  // V keys >= ceil(V / 1024) * 64
+    a.nfin = c->smp_key32;
+    a.done = c->smp_done;
+    a.out = c->d_smp_out;
+    if (fold) {
+      a.p.stamp = nullptr;
+      a.p.n_recent = static_cast<int>(n_use);
+      if (n_use <= static_cast<uint64_t>(kSampleArgRecent)) {
+        a.recent_in_args = 1;
+        if (n_use) std::memcpy(a.recent, src, n_use * 4);
+      } else {
+        std::memcpy(c->h_smp_recent, src, n_use * 4);
+        CK(cudaMemcpyAsync(c->smp_recent, c->h_smp_recent, n_use * 4, cudaMemcpyHostToDevice, c->stream));
+        a.p.recent = c->smp_recent;
+      }
+    }
+    SampleState* h = c->h_smp_out;
+    h->token = -1;
+    CK(launch_sample_fast(a, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    const int tok = reinterpret_cast<volatile SampleState*>(h)->token;
+    if (tok < 0 || tok >= static_cast<int>(c->V)) {
+      g_last_error = "sampler produced no token";
+      return VVLI_ERR_CUDA;
+    }
+    std::memcpy(rng_state, h->rng, sizeof(h->rng));
+    *out_token = static_cast<uint32_t>(tok);
+    return VVLI_OK;
   }
   SampleState* h = c->h_smp_state;
   std::memcpy(h->rng, rng_state, sizeof(h->rng));
@@ -1961,15 +2001,8 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
   h->path = 0;
   h->k = 0;
   h->n_sort = 0;
-  CK(cudaMemcpyAsync(c->smp_state, h, kSampleStateBytes + (fold ? n_use * 4 : 0), cudaMemcpyHostToDevice,
-                     c->stream));
-  if (fast) {
-    // the candidates reuse the long path's buffers (V keys >= ceil(V / 1024) * 64)
-    CK(launch_sample_fast(p, static_cast<int>(limit), c->smp_key64, reinterpret_cast<unsigned*>(c->smp_key32),
-                          c->stream));
-  } else {
-    CK(launch_sample(p, c->stream));
-  }
+  CK(cudaMemcpyAsync(c->smp_state, h, kSampleStateBytes, cudaMemcpyHostToDevice, c->stream));
+  CK(launch_sample(p, c->stream));
   CK(cudaMemcpyAsync(h, c->smp_state, sizeof(SampleState), cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   if (h->path == 1) {

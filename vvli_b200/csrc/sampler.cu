@@ -27,6 +27,8 @@
 // (the published generator) with the float built from 23 mantissa bits and a
 // leading-zero count for the exponent.  It is drawn only when the reference
 // draws it: temperature > 0 and at least one finite candidate.
+#include <algorithm>
+
 #include "common.cuh"
 #include "sampler.cuh"
 
@@ -137,9 +139,9 @@ __device__ int block_argmax(float v, int i, float* wv, int* wi) {
 
 // prepareProbabilities (:428-449) and sampleCandidate (:451-463) over the k
 // keys cand[0, k), sorted descending, in shared memory; every thread calls it.
-__device__ void finish_sorted(const SampleParams& p, const unsigned long long* cand, float* probs, unsigned k) {
+__device__ void finish_sorted(const SampleParams& p, const unsigned long long* rng_in, SampleState* st,
+                              const unsigned long long* cand, float* probs, unsigned k) {
   const int tid = threadIdx.x;
-  SampleState* st = p.st;
   const float t = fmaxf(p.temperature, 1e-6f);
   const float mx = key_value(static_cast<unsigned>(cand[0] >> 32));
   for (int j = tid; j < static_cast<int>(k); j += blockDim.x) probs[j] = prob_of(key_value(static_cast<unsigned>(cand[j] >> 32)), mx, t);
@@ -160,7 +162,7 @@ __device__ void finish_sorted(const SampleParams& p, const unsigned long long* c
         }
       }
     }
-    unsigned long long s[4] = {st->rng[0], st->rng[1], st->rng[2], st->rng[3]};
+    unsigned long long s[4] = {rng_in[0], rng_in[1], rng_in[2], rng_in[3]};
     const float u = xoshiro_float(s);
     float total2 = 0.0f;
     for (unsigned j = 0; j < count; ++j) total2 += probs[j];
@@ -248,21 +250,28 @@ __device__ void merge_lists(unsigned long long* lists, int n) {
   }
 }
 
-// First pass: CTA b takes ids [1024 b, 1024 b + 1024); each warp sorts 64 of
-// them, the CTA merges its 16 lists, and the best k go to cand[b * k ...];
-// nfin_part[b] = the CTA's count of finite adjusted logits.
-__global__ void __launch_bounds__(512) topk_local_kernel(const SampleParams p, int k, unsigned long long* cand,
-                                                         unsigned* nfin_part) {
-  __shared__ unsigned long long lists[16 * 64];
+// CTA b takes ids [1024 b, 1024 b + 1024): each warp sorts 64 of them, the
+// CTA merges its 16 lists and writes its best k to cand[b * k ..] and its
+// count of finite adjusted logits to nfin[b].  The last CTA to finish (a
+// counter) merges every CTA's list in CTA order, so the result does not
+// depend on which CTA that is, and runs the probabilities, top-p and draw.
+__global__ void __launch_bounds__(512) topk_sample_kernel(const __grid_constant__ FastSampleArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned long long* lists = reinterpret_cast<unsigned long long*>(smem);  // [max(16, nlists)][64]
+  float* probs = reinterpret_cast<float*>(lists + static_cast<size_t>(max(16, a.nlists)) * 64);  // [kSampleFastK]
   __shared__ unsigned wcount[16];
   __shared__ unsigned recent_bits[32];  // ids [1024 b, 1024 b + 1024) among the recent tokens
+  __shared__ unsigned last;
+  const SampleParams& p = a.p;
+  const int k = a.k;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int base = blockIdx.x * 1024;
   if (!p.stamp) {
+    const uint32_t* rec = a.recent_in_args ? a.recent : p.recent;
     if (threadIdx.x < 32) recent_bits[threadIdx.x] = 0u;
     __syncthreads();
     for (int i = threadIdx.x; i < p.n_recent; i += blockDim.x) {
-      const int t = static_cast<int>(p.recent[i]) - base;
+      const int t = static_cast<int>(rec[i]) - base;
       if (t >= 0 && t < 1024) atomicOr(&recent_bits[t >> 5], 1u << (t & 31));
     }
     __syncthreads();
@@ -290,27 +299,29 @@ __global__ void __launch_bounds__(512) topk_local_kernel(const SampleParams p, i
   lists[warp * 64 + lane + 32] = r[1];
   __syncthreads();
   merge_lists(lists, 16);
-  for (int i = threadIdx.x; i < k; i += blockDim.x) cand[static_cast<size_t>(blockIdx.x) * k + i] = lists[i];
+  for (int i = threadIdx.x; i < k; i += blockDim.x) a.cand[static_cast<size_t>(blockIdx.x) * k + i] = lists[i];
   if (threadIdx.x == 0) {
     unsigned t = 0;
     for (int w = 0; w < 16; ++w) t += wcount[w];
-    nfin_part[blockIdx.x] = t;
+    a.nfin[blockIdx.x] = t;
   }
-}
-
-// Second pass: the CTAs' lists (k keys each, padded to 64) merged to the best
-// 64, then probabilities, top-p and the draw.
-__global__ void __launch_bounds__(1024) topk_merge_kernel(const SampleParams p, int k_req, int nblk, int nlists,
-                                                          const unsigned long long* cand, const unsigned* nfin_part) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  unsigned long long* lists = reinterpret_cast<unsigned long long*>(smem);  // [nlists][64]
-  float* probs = reinterpret_cast<float*>(lists + static_cast<size_t>(nlists) * 64);  // [kSampleFastK]
-  __shared__ unsigned wsum[32];
-  SampleState* st = p.st;
+  // publish this CTA's list, then count it in
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(a.done, 1u) == gridDim.x - 1 ? 1u : 0u;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int nblk = gridDim.x;
   unsigned c = 0;
-  for (int b = threadIdx.x; b < nblk; b += blockDim.x) c += nfin_part[b];
-  unsigned n_finite;
-  block_excl_scan(c, wsum, &n_finite);
+  for (int b = threadIdx.x; b < nblk; b += blockDim.x) c += __ldcg(a.nfin + b);
+  c = __reduce_add_sync(0xffffffffu, c);
+  if (lane == 0) wcount[warp] = c;
+  __syncthreads();
+  unsigned n_finite = 0;
+  for (int w = 0; w < 16; ++w) n_finite += wcount[w];
+  if (threadIdx.x == 0) *a.done = 0;  // ready for the next call (stream order)
+  SampleState* st = a.out;
   if (n_finite == 0) {  // no candidate: llm.argmax of the raw logits (:115), rare
     if (threadIdx.x == 0) {
       float bv = p.logits[0];
@@ -320,19 +331,20 @@ __global__ void __launch_bounds__(1024) topk_merge_kernel(const SampleParams p, 
           bv = p.logits[i];
           bi = i;
         }
+      for (int q = 0; q < 4; ++q) st->rng[q] = a.rng[q];
       st->token = bi;
       st->path = 0;
     }
     return;
   }
-  for (int i = threadIdx.x; i < nlists * 64; i += blockDim.x) {
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.nlists * 64; i += blockDim.x) {
     const int b = i >> 6, j = i & 63;
-    lists[i] = (b < nblk && j < k_req) ? cand[static_cast<size_t>(b) * k_req + j] : 0ull;
+    lists[i] = (b < nblk && j < k) ? __ldcg(a.cand + static_cast<size_t>(b) * k + j) : 0ull;
   }
   __syncthreads();
-  merge_lists(lists, nlists);
-  const unsigned k = min(static_cast<unsigned>(k_req), n_finite);
-  finish_sorted(p, lists, probs, k);
+  merge_lists(lists, a.nlists);
+  finish_sorted(p, a.rng, st, lists, probs, min(static_cast<unsigned>(k), n_finite));
 }
 
 __global__ void sample_mark_kernel(const uint32_t* recent, int n, unsigned* stamp, unsigned call, int V) {
@@ -519,7 +531,7 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(const SampleParams p) {
       __syncthreads();
     }
   }
-  finish_sorted(p, cand, probs, k);
+  finish_sorted(p, p.st->rng, p.st, cand, probs, k);
 }
 
 // Sorts keys[c * kSortChunk ..] (n keys in all) descending, chunk c per CTA,
@@ -658,14 +670,13 @@ cudaError_t launch_sample_long(const SampleParams& p, int n_sort, cudaStream_t s
   return cudaGetLastError();
 }
 
-cudaError_t launch_sample_fast(const SampleParams& p, int k, unsigned long long* cand, unsigned* nfin, cudaStream_t s) {
-  const int nblk = (p.V + 1023) / 1024;
-  int nlists = 1;
-  while (nlists < nblk) nlists <<= 1;
-  if (k < 1 || k > kSampleFastK || nlists * 64 > kSampleFastMaxCand) return cudaErrorInvalidValue;
-  topk_local_kernel<<<nblk, 512, 0, s>>>(p, k, cand, nfin);
-  const size_t smem = static_cast<size_t>(nlists) * 64 * 8 + kSampleFastK * 4;
-  topk_merge_kernel<<<1, 1024, smem, s>>>(p, k, nblk, nlists, cand, nfin);
+cudaError_t launch_sample_fast(const FastSampleArgs& a, cudaStream_t s) {
+  const int nblk = (a.p.V + 1023) / 1024;
+  if (a.k < 1 || a.k > kSampleFastK || a.nlists < nblk || a.nlists * 64 > kSampleFastMaxCand ||
+      (a.recent_in_args && a.p.n_recent > kSampleArgRecent))
+    return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(std::max(16, a.nlists)) * 64 * 8 + kSampleFastK * 4;
+  topk_sample_kernel<<<nblk, 512, smem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -674,7 +685,7 @@ cudaError_t configure_sampler() {
   if (e) return e;
   e = cudaFuncSetAttribute(sort_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSortChunk * 8);
   if (e) return e;
-  return cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  return cudaFuncSetAttribute(topk_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(static_cast<size_t>(kSampleFastMaxCand) * 8 + kSampleFastK * 4));
 }
 

@@ -41,6 +41,22 @@ struct SampleParams {
   SampleState* st;
 };
 
+// Recent tokens that travel inside the fused top-k kernel's parameters.
+constexpr int kSampleArgRecent = 256;
+
+// The fused top-k step: everything it reads from the host is in here.
+struct FastSampleArgs {
+  SampleParams p;                // p.st unused; p.recent used when n_recent > kSampleArgRecent
+  unsigned long long rng[4];     // xoshiro256++ state before the step
+  int k, nlists;                 // top_k, lists merged by the last CTA (a power of two >= CTAs)
+  unsigned long long* cand;      // [CTAs * k] scratch
+  unsigned* nfin;                // [CTAs] scratch
+  unsigned* done;                // CTA counter, 0 between calls
+  SampleState* out;              // token and the state after the step (page-locked host memory, mapped)
+  int recent_in_args;            // 1: the recent tokens are recent[0, p.n_recent)
+  uint32_t recent[kSampleArgRecent];
+};
+
 // Marks recent[0, n) (tokens >= V skipped) with `call` (buildRepeatCounts
 // only decides whether a token's count is non-zero).
 cudaError_t launch_sample_mark(const uint32_t* recent, int n, unsigned* stamp, unsigned call, int V, cudaStream_t s);
@@ -51,9 +67,10 @@ cudaError_t launch_sample(const SampleParams& p, cudaStream_t s);
 // in key64 (n_sort, read back by the host), then probabilities, top-p and
 // the draw over the first st->k.
 cudaError_t launch_sample_long(const SampleParams& p, int n_sort, cudaStream_t s);
-// top_k in [1, kSampleFastK] with temperature > 0; cand holds ceil(V / 1024) * k keys,
-// nfin ceil(V / 1024) counts.
-cudaError_t launch_sample_fast(const SampleParams& p, int k, unsigned long long* cand, unsigned* nfin, cudaStream_t s);
+// top_k in [1, kSampleFastK] with temperature > 0, one launch: CTA b keeps the
+// best k of ids [1024 b, 1024 b + 1024), the last CTA to finish merges the
+// lists and draws.  cand holds ceil(V / 1024) * k keys, nfin ceil(V / 1024) counts.
+cudaError_t launch_sample_fast(const FastSampleArgs& a, cudaStream_t s);
 cudaError_t configure_sampler();
 
 }  // namespace vvli
