@@ -199,15 +199,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld32(trow + c * 32, v);
           transpose_in(v);
           const int n = n0 + c * 32 + lane;
+          // The rows' steps are independent: fully unrolled, so that each
+          // warp (one per sub-partition) keeps its loads and math in flight
+          // together rather than one row's latency at a time.
+          const int rows = min(32, p.M - wrow0);
           if constexpr (EPI == GE_RESID) {
             if (n < p.N) {
-#pragma unroll 4
-              for (int r = 0; r < 32; ++r) {
-                const int row_r = wrow0 + r;
-                if (row_r >= p.M) break;
-                float* y = p.y + static_cast<size_t>(row_r) * p.ldy + n;
-                *y = (p.add_residual ? *y : 0.f) + epi_t[r * 33 + lane];  // addInto
-              }
+              float* y = p.y + static_cast<size_t>(wrow0) * p.ldy + n;
+              float old[32];
+#pragma unroll
+              for (int r = 0; r < 32; ++r) old[r] = (p.add_residual && r < rows) ? y[static_cast<size_t>(r) * p.ldy] : 0.f;
+#pragma unroll
+              for (int r = 0; r < 32; ++r)
+                if (r < rows) y[static_cast<size_t>(r) * p.ldy] = old[r] + epi_t[r * 33 + lane];  // addInto
             }
           } else {  // GE_QKV: column n of rows wrow0 ..; rotary pairs (n, n ^ 1) sit in neighbouring lanes
             const bool live = n < p.N;
@@ -215,16 +219,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const bool odd = n & 1;
             const float bias = live && p.bias ? bf16_to_f32(p.bias[n]) : 0.f;
             const float inv_freq = rot ? rope_inv_freq(p.rope, (n & ~1) % p.d, p.d) : 0.f;
-            const bool is_k = !(n < p.q_rows) && rot;
-            const int rel = n < p.q_rows ? 0 : (is_k ? n - p.q_rows : n - p.q_rows - p.kv_rows);
+            const bool is_q = n < p.q_rows;
+            const bool is_k = !is_q && rot;
+            const int rel = is_q ? 0 : (is_k ? n - p.q_rows : n - p.q_rows - p.kv_rows);
             float* cache = is_k ? p.k_cache : p.v_cache;
+            // lane r holds the KV page of row wrow0 + r
+            const int my_pos = p.pos0 + wrow0 + lane;
+            const int my_page = (lane < rows && p.page_table) ? p.page_table[my_pos / kPage] : 0;
+            const size_t head_off = static_cast<size_t>(rel / p.d) * kPage * p.d + rel % p.d;
+#pragma unroll 8
             for (int r = 0; r < 32; ++r) {
-              const int row_r = wrow0 + r;
-              if (row_r >= p.M) break;
               float x = epi_t[r * 33 + lane];
               if (p.bias) x = x + bias;
               const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
-              const int pos = p.pos0 + row_r;
+              const int page = __shfl_sync(0xffffffffu, my_page, r);
+              const int pos = p.pos0 + wrow0 + r;
               if (rot) {
                 const float ang = static_cast<float>(pos) * inv_freq;
                 float sn, cs;
@@ -232,11 +241,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const float x0 = odd ? partner : x, x1 = odd ? x : partner;
                 x = odd ? x0 * sn + x1 * cs : x0 * cs - x1 * sn;
               }
-              if (!live) continue;
-              if (n < p.q_rows)
-                p.y[static_cast<size_t>(row_r) * p.ldy + n] = x;
-              else
-                cache[kv_off(p.page_table, pos, rel / p.d, p.nkv, p.d) + rel % p.d] = x;
+              if (live && r < rows) {
+                if (is_q)
+                  p.y[static_cast<size_t>(wrow0 + r) * p.ldy + n] = x;
+                else  // kv_off: [page][kv head][position in page][d]
+                  cache[static_cast<size_t>(page) * p.nkv * kPage * p.d + static_cast<size_t>(pos % kPage) * p.d +
+                        head_off] = x;
+              }
             }
           }
         }
