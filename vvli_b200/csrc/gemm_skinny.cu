@@ -228,51 +228,66 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   if (warp >= 2 && have && crank == 0) {
     const int r = r0 + (warp & 3) * 32 + lane;
     const int M = p.M;
+    // The batch rows' steps are independent: predicated rather than cut
+    // short, so the unrolled loads and math of all rows are in flight together.
     if constexpr (EPI == GE_SILU) {
       if (r < p.N) {
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-          if (b >= M) break;
-          const float g = acc[b];
-          const float f = (g / (1.0f + expf(-g))) * accu[b];  // siluMulInto, src/llm.zig:1382-1387
-          split_bf16(f, p.out_hi[static_cast<size_t>(b) * p.ld_out + r], p.out_lo[static_cast<size_t>(b) * p.ld_out + r]);
+          if (b < M) {
+            const float g = acc[b];
+            const float f = (g / (1.0f + expf(-g))) * accu[b];  // siluMulInto, src/llm.zig:1382-1387
+            split_bf16(f, p.out_hi[static_cast<size_t>(b) * p.ld_out + r], p.out_lo[static_cast<size_t>(b) * p.ld_out + r]);
+          }
         }
       }
     } else if constexpr (EPI == GE_RESID) {
       if (r < p.N) {
+        float old[NB];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          if (b >= M) break;
-          float* y = p.y + static_cast<size_t>(b) * p.ldy + r;
-          *y = (p.add_residual ? *y : 0.f) + acc[b];  // addInto, src/llm.zig:1389-1396
-        }
+        for (int b = 0; b < NB; ++b) old[b] = (p.add_residual && b < M) ? p.y[static_cast<size_t>(b) * p.ldy + r] : 0.f;
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+          if (b < M) p.y[static_cast<size_t>(b) * p.ldy + r] = old[b] + acc[b];  // addInto, src/llm.zig:1389-1396
       }
     } else {  // GE_QKV: batch row b is sequence slot b at position row_pos[b]
-      const bool rot = r < p.q_rows + p.kv_rows;
+      const bool rot = r < p.q_rows + p.kv_rows;  // uniform over the warp (regions are whole heads)
+      const bool odd = r & 1;
       const float inv_freq = rot ? rope_inv_freq(p.rope, (r & ~1) % p.d, p.d) : 0.f;
       const float bias = (p.bias && r < p.N) ? bf16_to_f32(p.bias[r]) : 0.f;
+      const bool is_q = r < p.q_rows;
+      const bool is_k = !is_q && rot;
+      const int rel = is_q ? 0 : (is_k ? r - p.q_rows : r - p.q_rows - p.kv_rows);
+      float* cache = is_k ? p.k_cache : p.v_cache;
+      const size_t head_off = static_cast<size_t>(rel / p.d) * kPage * p.d + rel % p.d;
+      // lane b holds batch row b's position and the KV page it falls in
+      const int my_pos = lane < M ? p.row_pos[lane] : 0;
+      const int my_page = lane < M ? p.page_table[static_cast<size_t>(lane) * p.seq_pages + my_pos / kPage] : 0;
 #pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        if (b >= M) break;  // uniform over the warp
-        float a = acc[b];
-        if (p.bias) a = a + bias;
-        const float other = __shfl_xor_sync(0xffffffffu, a, 1);  // the rotary partner row
-        const int pos = p.row_pos[b];
-        if (rot) {
-          const float ang = static_cast<float>(pos) * inv_freq;
-          float sn, cs;
-          sincosf(ang, &sn, &cs);
-          a = (r & 1) ? other * sn + a * cs : a * cs - other * sn;
-        }
-        if (r < p.N) {
-          if (r < p.q_rows) {
-            p.y[static_cast<size_t>(b) * p.ldy + r] = a;
-          } else {
-            const bool is_k = r < p.q_rows + p.kv_rows;
-            const int rel = is_k ? r - p.q_rows : r - p.q_rows - p.kv_rows;
-            const size_t off = kv_off(p.page_table + static_cast<size_t>(b) * p.seq_pages, pos, rel / p.d, p.nkv, p.d) +
-                               rel % p.d;
-            (is_k ? p.k_cache : p.v_cache)[off] = a;
+      for (int b = 0; b < NB; b += 2) {
+        // the rotary pair's even lane takes row b's angle, the odd lane row b + 1's
+        float sn = 0.f, cs = 1.f;
+        const int pos_mine = __shfl_sync(0xffffffffu, my_pos, b + (odd ? 1 : 0));
+        if (rot) sincosf(static_cast<float>(pos_mine) * inv_freq, &sn, &cs);
+        const float osn = __shfl_xor_sync(0xffffffffu, sn, 1), ocs = __shfl_xor_sync(0xffffffffu, cs, 1);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int bb = b + h;
+          float a = acc[bb];
+          if (p.bias) a = a + bias;
+          const float other = __shfl_xor_sync(0xffffffffu, a, 1);  // the rotary partner row
+          const int pos = __shfl_sync(0xffffffffu, my_pos, bb);
+          const int page = __shfl_sync(0xffffffffu, my_page, bb);
+          if (rot) {
+            const bool own = (h == 1) == odd;
+            const float s1 = own ? sn : osn, c1 = own ? cs : ocs;
+            a = odd ? other * s1 + a * c1 : a * c1 - other * s1;
+          }
+          if (r < p.N && bb < M) {
+            if (is_q)
+              p.y[static_cast<size_t>(bb) * p.ldy + r] = a;
+            else  // kv_off: [page][kv head][position in page][d]
+              cache[static_cast<size_t>(page) * p.nkv * kPage * p.d + static_cast<size_t>(pos % kPage) * p.d + head_off] = a;
           }
         }
       }

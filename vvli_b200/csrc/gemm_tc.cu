@@ -227,26 +227,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int my_pos = p.pos0 + wrow0 + lane;
             const int my_page = (lane < rows && p.page_table) ? p.page_table[my_pos / kPage] : 0;
             const size_t head_off = static_cast<size_t>(rel / p.d) * kPage * p.d + rel % p.d;
-#pragma unroll 8
-            for (int r = 0; r < 32; ++r) {
-              float x = epi_t[r * 33 + lane];
-              if (p.bias) x = x + bias;
-              const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
-              const int page = __shfl_sync(0xffffffffu, my_page, r);
-              const int pos = p.pos0 + wrow0 + r;
-              if (rot) {
-                const float ang = static_cast<float>(pos) * inv_freq;
-                float sn, cs;
-                sincosf(ang, &sn, &cs);
-                const float x0 = odd ? partner : x, x1 = odd ? x : partner;
-                x = odd ? x0 * sn + x1 * cs : x0 * cs - x1 * sn;
-              }
-              if (live && r < rows) {
-                if (is_q)
-                  p.y[static_cast<size_t>(wrow0 + r) * p.ldy + n] = x;
-                else  // kv_off: [page][kv head][position in page][d]
-                  cache[static_cast<size_t>(page) * p.nkv * kPage * p.d + static_cast<size_t>(pos % kPage) * p.d +
-                        head_off] = x;
+            // Rows r and r + 1 together: the pair's even lane takes the angle
+            // of row r, the odd lane that of row r + 1, and they swap
+            // (one sincosf per lane per two rows).
+#pragma unroll 4
+            for (int r = 0; r < 32; r += 2) {
+              float sn = 0.f, cs = 1.f;
+              if (rot) sincosf(static_cast<float>(p.pos0 + wrow0 + r + (odd ? 1 : 0)) * inv_freq, &sn, &cs);
+              const float osn = __shfl_xor_sync(0xffffffffu, sn, 1), ocs = __shfl_xor_sync(0xffffffffu, cs, 1);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int rr = r + h;
+                float x = epi_t[rr * 33 + lane];
+                if (p.bias) x = x + bias;
+                const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
+                const int page = __shfl_sync(0xffffffffu, my_page, rr);
+                const int pos = p.pos0 + wrow0 + rr;
+                if (rot) {
+                  const bool own = (h == 1) == odd;  // this lane computed row rr's angle
+                  const float s1 = own ? sn : osn, c1 = own ? cs : ocs;
+                  const float x0 = odd ? partner : x, x1 = odd ? x : partner;
+                  x = odd ? x0 * s1 + x1 * c1 : x0 * c1 - x1 * s1;
+                }
+                if (live && rr < rows) {
+                  if (is_q)
+                    p.y[static_cast<size_t>(wrow0 + rr) * p.ldy + n] = x;
+                  else  // kv_off: [page][kv head][position in page][d]
+                    cache[static_cast<size_t>(page) * p.nkv * kPage * p.d + static_cast<size_t>(pos % kPage) * p.d +
+                          head_off] = x;
+                }
               }
             }
           }
