@@ -24,6 +24,8 @@ struct BatchAttnParams {
 };
 
 int batch_attention_slots(int d);
+// Resident CTAs per SM of the attention kernel with `slots` pages in flight.
+int batch_attention_ctas_per_sm(int group, int d, int slots);
 size_t batch_attention_smem(int group, int d, int slots);
 // pdl: programmatic edge to the previous kernel (earlier pages are fetched before the wait).
 cudaError_t launch_batch_attention(const BatchAttnParams& p, int B, cudaStream_t s, bool pdl = false);

@@ -9,6 +9,7 @@
 // merges the partial (o, max, sum) triples.  The output is written as the
 // bf16 hi / lo pair the o_proj GEMM reads.
 #include <algorithm>
+#include <cstdlib>
 
 #include "batch.cuh"
 #include "device_fns.cuh"
@@ -30,12 +31,13 @@ VVLI_DEV void split_pair(float v, uint16_t* hi, uint16_t* lo) {
 // CTA = (split s, kv head g, row b).  Split s owns a contiguous range of the
 // row's 64-position pages; each page's K and V rows ([kPage][d] fp32, one
 // contiguous block per kv head) arrive with two cp.async.bulk copies into a
-// ring of `nslots` shared-memory slots, so several pages per SM are in flight
-// while the oldest is computed.  Scores: a warp takes 4 positions, lane l
+// ring of `nslots` shared-memory slots; with one slot, the several CTAs per
+// SM keep pages in flight while others compute.  Scores: a warp takes 4 positions, lane l
 // holds dims [l*DPL, (l+1)*DPL) of the key and of every q head (q stays in
 // registers), and the heads' partial dot products meet in reduce_heads8.
 // P.V: one (head, dim) output per thread, 8 independent partial sums.
-template <int DPL>
+// GH: q heads per kv head held per lane (4 when the group has at most 4, else 8).
+template <int DPL, int GH>
 __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const BatchAttnParams p) {
   extern __shared__ __align__(128) float sm[];
   const int G = p.group, d = p.d, nslot = p.nslots;
@@ -89,9 +91,9 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
     for (; issued < nslot && p_begin + issued < p_end; ++issued) issue(p_begin + issued, issued);
   // this lane's slice of every q head of the group
   const bool lane_on = lane * DPL < d;
-  float qr[8][DPL];
+  float qr[GH][DPL];
 #pragma unroll
-  for (int hh = 0; hh < 8; ++hh)
+  for (int hh = 0; hh < GH; ++hh)
 #pragma unroll
     for (int k = 0; k < DPL; ++k) qr[hh][k] = (hh < G && lane_on) ? qs[hh * d + lane * DPL + k] : 0.f;
   const int nacc = (G * d + kBaThreads - 1) / kBaThreads;  // <= 2 (G * d <= 1024)
@@ -123,17 +125,23 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
       } else {
         kx[0] = (j < n && lane_on) ? ks[j * d + lane] : 0.f;
       }
-      float part[8];
+      float part[GH];
 #pragma unroll
-      for (int hh = 0; hh < 8; ++hh) {
+      for (int hh = 0; hh < GH; ++hh) {
         float a = 0.f;
 #pragma unroll
         for (int k = 0; k < DPL; ++k) a = fmaf(qr[hh][k], kx[k], a);
         part[hh] = a;
       }
-      const float dot = reduce_heads8(part, lane);
-      const int hh = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-      if ((lane & 3) == 0 && hh < G) sc[hh * kBaTile + j] = j < n ? dot * p.inv_sqrt_d : -INFINITY;
+      if constexpr (GH == 8) {
+        const float dot = reduce_heads8(part, lane);
+        const int hh = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+        if ((lane & 3) == 0 && hh < G) sc[hh * kBaTile + j] = j < n ? dot * p.inv_sqrt_d : -INFINITY;
+      } else {
+        const float dot = reduce_heads4(part, lane);
+        const int hh = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+        if ((lane & 7) == 0 && hh < G) sc[hh * kBaTile + j] = j < n ? dot * p.inv_sqrt_d : -INFINITY;
+      }
     }
     __syncthreads();
     // online softmax, one warp per head (softmaxInPlace, src/llm.zig:1408-1419)
@@ -309,8 +317,28 @@ __global__ void rows_argmax_index_kernel(const float* best, int B, int* out) {
 }  // namespace
 
 int batch_attention_slots(int d) {
-  const int page_pair = 2 * kPage * d * 4;  // K and V of one page
-  return std::max(2, std::min(kBaMaxSlots, (200 * 1024) / page_pair));
+  (void)d;
+  const char* env = getenv("VVLI_BATCH_ATTN_SLOTS");
+  if (env && atoi(env) >= 1) return std::min(kBaMaxSlots, atoi(env));
+  // One page in flight per CTA, several CTAs per SM (the splits fill them),
+  // measured ahead of two or three pages per CTA at one CTA per SM: 5.01 vs
+  // 5.03 / 5.06 ms per 8B step at batch 16, context 512.
+  return 1;
+}
+
+int batch_attention_ctas_per_sm(int group, int d, int slots) {
+  const size_t smem = batch_attention_smem(group, d, slots);
+  int n = 0;
+  auto occ = [&](auto kern) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kBaThreads, smem))
+      n = 1;
+  };
+  if (group <= 4)
+    d > 64 ? occ(batch_attention_kernel<4, 4>) : d > 32 ? occ(batch_attention_kernel<2, 4>) : occ(batch_attention_kernel<1, 4>);
+  else
+    d > 64 ? occ(batch_attention_kernel<4, 8>) : d > 32 ? occ(batch_attention_kernel<2, 8>) : occ(batch_attention_kernel<1, 8>);
+  return std::max(1, n);
 }
 
 size_t batch_attention_smem(int group, int d, int slots) {
@@ -335,15 +363,19 @@ static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaSt
 
 cudaError_t launch_batch_attention(const BatchAttnParams& p, int B, cudaStream_t s, bool pdl) {
   const size_t smem = batch_attention_smem(p.group, p.d, p.nslots);
-  cudaError_t e;
-  if ((e = cudaFuncSetAttribute(batch_attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) ||
-      (e = cudaFuncSetAttribute(batch_attention_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) ||
-      (e = cudaFuncSetAttribute(batch_attention_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))))
-    return e;
   const dim3 grid(p.splits, p.nkv, B);
-  if (p.d > 64) return launch_pdl(batch_attention_kernel<4>, grid, dim3(kBaThreads), smem, s, pdl, p);
-  if (p.d > 32) return launch_pdl(batch_attention_kernel<2>, grid, dim3(kBaThreads), smem, s, pdl, p);
-  return launch_pdl(batch_attention_kernel<1>, grid, dim3(kBaThreads), smem, s, pdl, p);
+  auto go = [&](auto kern) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    return e ? e : launch_pdl(kern, grid, dim3(kBaThreads), smem, s, pdl, p);
+  };
+  if (p.group <= 4) {
+    if (p.d > 64) return go(batch_attention_kernel<4, 4>);
+    if (p.d > 32) return go(batch_attention_kernel<2, 4>);
+    return go(batch_attention_kernel<1, 4>);
+  }
+  if (p.d > 64) return go(batch_attention_kernel<4, 8>);
+  if (p.d > 32) return go(batch_attention_kernel<2, 8>);
+  return go(batch_attention_kernel<1, 8>);
 }
 
 cudaError_t launch_rows_argmax(const float* logits, int B, int n, int ld, int row_base, float* best, cudaStream_t s,

@@ -112,4 +112,21 @@ VVLI_DEV float reduce_heads8(const float* p, int lane) {
   return t;
 }
 
+// The same for four heads p[0..3]: two exchange-halving steps leave head
+// (bit3 + 2 bit4) of the lane index in each lane, three more finish the sum.
+VVLI_DEV float reduce_heads4(const float* p, int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8;
+  float q[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float keep = b4 ? p[i + 2] : p[i], send = b4 ? p[i] : p[i + 2];
+    q[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float t = (b3 ? q[1] : q[0]) + __shfl_xor_sync(0xffffffffu, b3 ? q[0] : q[1], 8);
+  t += __shfl_xor_sync(0xffffffffu, t, 4);
+  t += __shfl_xor_sync(0xffffffffu, t, 2);
+  t += __shfl_xor_sync(0xffffffffu, t, 1);
+  return t;
+}
+
 }  // namespace vvli

@@ -230,6 +230,7 @@ struct vvli_ctx {
   // decode batches (allocated on first use): chunks of up to kSkinnyMaxRows rows
   bool bt_ready = false;
   int bt_splits_max = 0;
+  int bt_attn_per_sm = 0;  // resident attention CTAs per SM
   float *bt_x = nullptr, *bt_q = nullptr, *bt_logits = nullptr, *bt_best = nullptr, *bt_all_best = nullptr,
         *bt_part = nullptr, *bt_logits_all = nullptr;
   uint16_t *bt_ahi = nullptr, *bt_alo = nullptr, *bt_fhi = nullptr, *bt_flo = nullptr;
@@ -886,8 +887,11 @@ int forward_batch_chunk(vvli_ctx* c, const uint32_t* tokens, const uint64_t* pos
   RopeParams rope{c->cfg.rope_theta, VVLI_ROPE_INTERLEAVED, static_cast<int>(c->cfg.rope_scaling_type),
                   c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
                   static_cast<float>(c->cfg.rope_original_max_position)};
-  // Attention splits: about one CTA per SM over (row, kv head, split), at least a page each.
-  const int want = std::max(1, (c->sm_count + B * c->nkv_l / 2) / std::max(1, B * c->nkv_l));
+  // Attention splits: (row, kv head, split) CTAs filling the resident slots once, at least a page each.
+  const int slots = batch_attention_slots(c->d);
+  if (!c->bt_attn_per_sm) c->bt_attn_per_sm = batch_attention_ctas_per_sm(c->group, c->d, slots);
+  const int resident = c->sm_count * c->bt_attn_per_sm;
+  const int want = std::max(1, (resident + B * c->nkv_l / 2) / std::max(1, B * c->nkv_l));
   const int splits = std::max(1, std::min({c->bt_splits_max, want, (max_pos + kPage) / kPage}));
   // Programmatic edges between consecutive kernels (weights stream before the
   // dependency wait); none next to NCCL collectives.
@@ -916,7 +920,7 @@ int forward_batch_chunk(vvli_ctx* c, const uint32_t* tokens, const uint64_t* pos
     a.q = c->bt_q, a.k_cache = kc, a.v_cache = vc, a.page_table = c->page_table + static_cast<size_t>(slot0) * pps;
     a.seq_pages = pps, a.row_pos = c->bt_pos, a.part = c->bt_part, a.counters = c->bt_counters;
     a.out_hi = c->bt_ahi, a.out_lo = c->bt_alo, a.nq = c->nq_l, a.nkv = c->nkv_l, a.d = c->d, a.group = c->group;
-    a.splits = splits, a.nslots = batch_attention_slots(c->d), a.inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
+    a.splits = splits, a.nslots = slots, a.inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(c->d));
     a.err = err;
     CK(launch_batch_attention(a, B, s, pdl));
     GemmParams o{};
