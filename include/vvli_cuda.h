@@ -314,8 +314,10 @@ int vvli_cuda_trace(vvli_ctx* ctx, uint64_t* out, uint64_t cap, uint64_t* count)
  * reference: C[M,N] = (A_hi + A_lo)[M,K] . W[N,K]^T on random bf16 data
  * (two_a = 0: A_hi only) against a SIMT fp64-accumulating reference on
  * `device`; `max_rel_err` = max |C - ref| / max |ref|.  kernel 0: the prefill
- * GEMM (128 x 256 tiles); kernel 1: the decode-batch GEMM (M <= 32 rows,
- * weight rows as the MMA's M operand, split-K over a cluster). */
+ * GEMM on single CTAs (128 x 256 tiles); kernel 1: the decode-batch GEMM
+ * (M <= 32 rows, weight rows as the MMA's M operand, split-K over a
+ * cluster); kernel 2: the prefill GEMM on CTA pairs (256 x 256 tiles,
+ * cta_group::2), which prefill uses above 128 rows. */
 int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two_a, uint64_t seed,
                             float* max_rel_err);
 

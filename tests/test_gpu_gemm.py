@@ -25,6 +25,25 @@ def test_gemm_matches_reference(M, N, K, two_a):
 
 
 @pytest.mark.parametrize("M,N,K", [
+    (256, 256, 64),      # one CTA pair, one k-block
+    (256, 256, 1024),    # ring wrap-around (16 k-blocks over 4 stages)
+    (200, 512, 256),     # the second CTA's rows partly past M
+    (384, 1152, 896),    # ragged M and N tails (Qwen q|k|v shape)
+    (512, 6144, 4096),   # Llama-3-8B q|k|v on 512 tokens: 48 pair tiles
+    (1024, 4096, 14336), # long K (down_proj)
+    (4096, 512, 128),    # many row tiles, both accumulators in turn
+])
+def test_cta_pair_gemm_matches_reference(M, N, K):
+    # kernel 2: 256-row tiles on CTA pairs (cta_group::2), each CTA loading its
+    # own rows of A and half of the weight tile
+    from vvli_b200 import _abi
+    err = ctypes.c_float(0)
+    st = _abi.lib().vvli_cuda_gemm_selftest(0, 2, M, N, K, 1, 13, ctypes.byref(err))
+    assert st == 0, _abi.lib().vvli_cuda_last_error()
+    assert err.value < 1e-4, err.value
+
+
+@pytest.mark.parametrize("M,N,K", [
     (1, 256, 64),        # one row, one k-block, no split
     (5, 4096, 4096),     # 32 weight tiles: K split over clusters of 4
     (16, 6144, 4096),    # Llama-3-8B q|k|v, clusters of 3

@@ -56,9 +56,6 @@ VVLI_DEV uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-VVLI_DEV void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 
 template <int NB>
 VVLI_DEV void tmem_ld_nb(uint32_t taddr, float* v) {

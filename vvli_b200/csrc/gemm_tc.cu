@@ -21,6 +21,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "device_fns.cuh"
 #include "gemm_tc.cuh"
@@ -43,6 +44,117 @@ struct TcLayout {
   static constexpr size_t smem =
       static_cast<size_t>(stages) * stage + 1024 /*align*/ + 256 /*barriers*/ + 4 * 32 * 33 * 4 /*epilogue tiles*/;
 };
+
+// Epilogue of one accumulator tile by the four epilogue warps: warp wq owns
+// TMEM lanes (rows) m0 + 32 wq ..; n0 is the tile's first output column.
+template <int EPI, int BN>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow, int m0, int n0, int wq, int lane,
+                                              float* epi_t) {
+  {
+    // The accumulator arrives one row per lane (TMEM lane = row); each
+    // 32 x 32 chunk is turned around in this warp's shared tile so that the
+    // lanes then walk a row's 32 consecutive columns: every global load
+    // and store of the epilogue is a coalesced row segment.
+    tc_fence_after();
+    float v[32];
+    const int wrow0 = m0 + wq * 32;  // first row of this warp's 32
+    auto transpose_in = [&](const float* src) {
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) epi_t[lane * 33 + j] = src[j];
+      __syncwarp();
+    };
+    if constexpr (EPI == GE_SILU) {
+      float u[32];
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(trow + c * 32, v);        // gate columns
+        tmem_ld32(trow + 128 + c * 32, u);  // up columns
+        float g[32];
+        transpose_in(v);
+#pragma unroll
+        for (int r = 0; r < 32; ++r) g[r] = epi_t[r * 33 + lane];
+        transpose_in(u);
+        const int n = n0 + c * 32 + lane;
+        if (n < p.N) {
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const int row_r = wrow0 + r;
+            if (row_r >= p.M) break;
+            const float f = (g[r] / (1.0f + expf(-g[r]))) * epi_t[r * 33 + lane];  // siluMulInto, src/llm.zig:1382-1387
+            const size_t o = static_cast<size_t>(row_r) * p.ld_out + n;
+            split_bf16(f, p.out_hi[o], p.out_lo[o]);
+          }
+        }
+      }
+    } else {
+      for (int c = 0; c < BN / 32; ++c) {
+        tmem_ld32(trow + c * 32, v);
+        transpose_in(v);
+        const int n = n0 + c * 32 + lane;
+        // The rows' steps are independent: fully unrolled, so that each
+        // warp (one per sub-partition) keeps its loads and math in flight
+        // together rather than one row's latency at a time.
+        const int rows = min(32, p.M - wrow0);
+        if constexpr (EPI == GE_RESID) {
+          if (n < p.N) {
+            float* y = p.y + static_cast<size_t>(wrow0) * p.ldy + n;
+            float old[32];
+#pragma unroll
+            for (int r = 0; r < 32; ++r) old[r] = (p.add_residual && r < rows) ? y[static_cast<size_t>(r) * p.ldy] : 0.f;
+#pragma unroll
+            for (int r = 0; r < 32; ++r)
+              if (r < rows) y[static_cast<size_t>(r) * p.ldy] = old[r] + epi_t[r * 33 + lane];  // addInto
+          }
+        } else {  // GE_QKV: column n of rows wrow0 ..; rotary pairs (n, n ^ 1) sit in neighbouring lanes
+          const bool live = n < p.N;
+          const bool rot = n < p.q_rows + p.kv_rows;  // q and k rows hold rotary pairs side by side
+          const bool odd = n & 1;
+          const float bias = live && p.bias ? bf16_to_f32(p.bias[n]) : 0.f;
+          const float inv_freq = rot ? rope_inv_freq(p.rope, (n & ~1) % p.d, p.d) : 0.f;
+          const bool is_q = n < p.q_rows;
+          const bool is_k = !is_q && rot;
+          const int rel = is_q ? 0 : (is_k ? n - p.q_rows : n - p.q_rows - p.kv_rows);
+          float* cache = is_k ? p.k_cache : p.v_cache;
+          // lane r holds the KV page of row wrow0 + r
+          const int my_pos = p.pos0 + wrow0 + lane;
+          const int my_page = (lane < rows && p.page_table) ? p.page_table[my_pos / kPage] : 0;
+          const size_t head_off = static_cast<size_t>(rel / p.d) * kPage * p.d + rel % p.d;
+          // Rows r and r + 1 together: the pair's even lane takes the angle
+          // of row r, the odd lane that of row r + 1, and they swap
+          // (one sincosf per lane per two rows).
+#pragma unroll 4
+          for (int r = 0; r < 32; r += 2) {
+            float sn = 0.f, cs = 1.f;
+            if (rot) sincosf(static_cast<float>(p.pos0 + wrow0 + r + (odd ? 1 : 0)) * inv_freq, &sn, &cs);
+            const float osn = __shfl_xor_sync(0xffffffffu, sn, 1), ocs = __shfl_xor_sync(0xffffffffu, cs, 1);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int rr = r + h;
+              float x = epi_t[rr * 33 + lane];
+              if (p.bias) x = x + bias;
+              const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
+              const int page = __shfl_sync(0xffffffffu, my_page, rr);
+              const int pos = p.pos0 + wrow0 + rr;
+              if (rot) {
+                const bool own = (h == 1) == odd;  // this lane computed row rr's angle
+                const float s1 = own ? sn : osn, c1 = own ? cs : ocs;
+                const float x0 = odd ? partner : x, x1 = odd ? x : partner;
+                x = odd ? x0 * s1 + x1 * c1 : x0 * c1 - x1 * s1;
+              }
+              if (live && rr < rows) {
+                if (is_q)
+                  p.y[static_cast<size_t>(wrow0 + rr) * p.ldy + n] = x;
+                else  // kv_off: [page][kv head][position in page][d]
+                  cache[static_cast<size_t>(page) * p.nkv * kPage * p.d + static_cast<size_t>(pos % kPage) * p.d +
+                        head_off] = x;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+}
 
 // ---------------------------------------------------------------- GEMM kernel
 template <int EPI, int BN>
@@ -158,110 +270,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(buf * BN);
     // tcgen05.ld is warp-collective: the warp goes on only if every lane saw the accumulator.
     if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[buf], (i >> 1) & 1, p.err))) break;
-    {
-      // The accumulator arrives one row per lane (TMEM lane = row); each
-      // 32 x 32 chunk is turned around in this warp's shared tile so that the
-      // lanes then walk a row's 32 consecutive columns: every global load
-      // and store of the epilogue is a coalesced row segment.
-      tc_fence_after();
-      float v[32];
-      const int wrow0 = m0 + wq * 32;  // first row of this warp's 32
-      auto transpose_in = [&](const float* src) {
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) epi_t[lane * 33 + j] = src[j];
-        __syncwarp();
-      };
-      if constexpr (EPI == GE_SILU) {
-        float u[32];
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(trow + c * 32, v);        // gate columns
-          tmem_ld32(trow + 128 + c * 32, u);  // up columns
-          float g[32];
-          transpose_in(v);
-#pragma unroll
-          for (int r = 0; r < 32; ++r) g[r] = epi_t[r * 33 + lane];
-          transpose_in(u);
-          const int n = n0 + c * 32 + lane;
-          if (n < p.N) {
-#pragma unroll
-            for (int r = 0; r < 32; ++r) {
-              const int row_r = wrow0 + r;
-              if (row_r >= p.M) break;
-              const float f = (g[r] / (1.0f + expf(-g[r]))) * epi_t[r * 33 + lane];  // siluMulInto, src/llm.zig:1382-1387
-              const size_t o = static_cast<size_t>(row_r) * p.ld_out + n;
-              split_bf16(f, p.out_hi[o], p.out_lo[o]);
-            }
-          }
-        }
-      } else {
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(trow + c * 32, v);
-          transpose_in(v);
-          const int n = n0 + c * 32 + lane;
-          // The rows' steps are independent: fully unrolled, so that each
-          // warp (one per sub-partition) keeps its loads and math in flight
-          // together rather than one row's latency at a time.
-          const int rows = min(32, p.M - wrow0);
-          if constexpr (EPI == GE_RESID) {
-            if (n < p.N) {
-              float* y = p.y + static_cast<size_t>(wrow0) * p.ldy + n;
-              float old[32];
-#pragma unroll
-              for (int r = 0; r < 32; ++r) old[r] = (p.add_residual && r < rows) ? y[static_cast<size_t>(r) * p.ldy] : 0.f;
-#pragma unroll
-              for (int r = 0; r < 32; ++r)
-                if (r < rows) y[static_cast<size_t>(r) * p.ldy] = old[r] + epi_t[r * 33 + lane];  // addInto
-            }
-          } else {  // GE_QKV: column n of rows wrow0 ..; rotary pairs (n, n ^ 1) sit in neighbouring lanes
-            const bool live = n < p.N;
-            const bool rot = n < p.q_rows + p.kv_rows;  // q and k rows hold rotary pairs side by side
-            const bool odd = n & 1;
-            const float bias = live && p.bias ? bf16_to_f32(p.bias[n]) : 0.f;
-            const float inv_freq = rot ? rope_inv_freq(p.rope, (n & ~1) % p.d, p.d) : 0.f;
-            const bool is_q = n < p.q_rows;
-            const bool is_k = !is_q && rot;
-            const int rel = is_q ? 0 : (is_k ? n - p.q_rows : n - p.q_rows - p.kv_rows);
-            float* cache = is_k ? p.k_cache : p.v_cache;
-            // lane r holds the KV page of row wrow0 + r
-            const int my_pos = p.pos0 + wrow0 + lane;
-            const int my_page = (lane < rows && p.page_table) ? p.page_table[my_pos / kPage] : 0;
-            const size_t head_off = static_cast<size_t>(rel / p.d) * kPage * p.d + rel % p.d;
-            // Rows r and r + 1 together: the pair's even lane takes the angle
-            // of row r, the odd lane that of row r + 1, and they swap
-            // (one sincosf per lane per two rows).
-#pragma unroll 4
-            for (int r = 0; r < 32; r += 2) {
-              float sn = 0.f, cs = 1.f;
-              if (rot) sincosf(static_cast<float>(p.pos0 + wrow0 + r + (odd ? 1 : 0)) * inv_freq, &sn, &cs);
-              const float osn = __shfl_xor_sync(0xffffffffu, sn, 1), ocs = __shfl_xor_sync(0xffffffffu, cs, 1);
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int rr = r + h;
-                float x = epi_t[rr * 33 + lane];
-                if (p.bias) x = x + bias;
-                const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
-                const int page = __shfl_sync(0xffffffffu, my_page, rr);
-                const int pos = p.pos0 + wrow0 + rr;
-                if (rot) {
-                  const bool own = (h == 1) == odd;  // this lane computed row rr's angle
-                  const float s1 = own ? sn : osn, c1 = own ? cs : ocs;
-                  const float x0 = odd ? partner : x, x1 = odd ? x : partner;
-                  x = odd ? x0 * s1 + x1 * c1 : x0 * c1 - x1 * s1;
-                }
-                if (live && rr < rows) {
-                  if (is_q)
-                    p.y[static_cast<size_t>(wrow0 + rr) * p.ldy + n] = x;
-                  else  // kv_off: [page][kv head][position in page][d]
-                    cache[static_cast<size_t>(page) * p.nkv * kPage * p.d + static_cast<size_t>(pos % kPage) * p.d +
-                          head_off] = x;
-                }
-              }
-            }
-          }
-        }
-      }
-    }
+    epilogue_tile<EPI, BN>(p, trow, m0, n0, wq, lane, epi_t);
     tc_fence_before();  // this warp's TMEM loads of the tile come before the MMAs that reuse it
     mbar_arrive(&tmem_empty[buf]);
     }
@@ -271,6 +280,161 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- CTA-pair GEMM (cta_group::2)
+// Tiles of 256 rows x 256 columns per CTA pair (a 2-CTA cluster): CTA r loads
+// rows m0 + 128 r .. of A (hi and lo) and its half of the tile's weight rows
+// (rank 0 the first 128 columns, rank 1 the second; for gate|up, 128 gate and
+// 128 up rows), and one 256 x 256 x 16 MMA of the leader (rank 0) reads A
+// from both CTAs and B from both halves.  Each CTA's TMEM holds its 128 rows
+// x 256 columns, so each SM loads 48 KB per k-block for the work that costs a
+// 128 x 256 tile 64 KB: a quarter less L2-to-SM traffic.  Measured, it is no
+// faster than the single-CTA kernel (which already issues at the measured
+// tensor peak inside a wave), so prefill uses it only when VVLI_GEMM_PAIR=1.
+// Both CTAs' loads complete on the leader's `full` barriers; the
+// leader's commits free both CTAs' stages and announce both accumulators;
+// both CTAs' epilogue warps release an accumulator on the leader's barrier.
+// No load is multicast.  Every wait is bounded (VVLI_ERR_TIMEOUT in p.err).
+struct TcPairLayout {
+  static constexpr uint32_t tile_b = 128 * kGemmBK * 2;        // this CTA's half of B: 16 KB
+  static constexpr uint32_t stage = 2 * kTileA + tile_b;      // A_hi | A_lo | B half: 48 KB
+  static constexpr int stages = 4;
+  static constexpr uint32_t tmem_cols = 512;                  // two 256-column accumulators
+  static constexpr uint32_t idesc = umma_idesc(256, 256);
+  static constexpr size_t smem = static_cast<size_t>(stages) * stage + 1024 + 256 + 4 * 32 * 33 * 4;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
+                        const __grid_constant__ CUtensorMap tm_w, const GemmParams p) {
+  using L = TcPairLayout;
+  constexpr int kStages = L::stages;
+  constexpr bool kPair = EPI == GE_SILU;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sm = smem_raw + (base - raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * L::stage);
+  uint64_t* empty = full + kStages;
+  uint64_t* tmem_full = empty + kStages;  // [2]
+  uint64_t* tmem_empty = tmem_full + 2;   // [2], the leader's counts both CTAs' epilogue warps
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  float* epi_t = reinterpret_cast<float*>(sm + kStages * L::stage + 256) + ((threadIdx.x >> 5) & 3) * 32 * 33;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t cr = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int mt = (p.M + 255) / 256;
+  const int ntiles = mt * p.n_tiles;
+  auto tile_m0 = [&](int t) { return (t % mt) * 256; };
+  auto tile_n0 = [&](int t) { return (t / mt) * (kPair ? 128 : 256); };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(&tmem_full[0], 1);
+    mbar_init(&tmem_full[1], 1);
+    mbar_init(&tmem_empty[0], 8);  // 4 epilogue warps x 2 CTAs
+    mbar_init(&tmem_empty[1], 8);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(L::tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncwarp();        // the cluster barrier is warp-aligned
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer (both CTAs): this CTA's A rows and B half
+      const uint32_t bytes = (p.two_a ? 2 * kTileA : kTileA) + L::tile_b;
+      int issued = 0;
+      bool ok = true;
+      for (int t = pair; t < ntiles && ok; t += npairs) {
+        const int m0 = tile_m0(t) + 128 * static_cast<int>(cr), n0 = tile_n0(t);
+        const int rb = cr == 0 ? n0 : (kPair ? p.pair_offset + n0 : n0 + 128);
+        for (int kb = 0; kb < p.nk; ++kb, ++issued) {
+          const int s = issued % kStages;
+          if (issued >= kStages && !(ok = mbar_wait(&empty[s], ((issued / kStages) - 1) & 1, p.err))) break;
+          if (cr == 0) mbar_arrive_expect_tx(&full[s], 2 * bytes);
+          const uint32_t bar = cluster_addr(smem_u32(&full[s]), 0);
+          const uint32_t st = base + s * L::stage;
+          const int x = kb * kGemmBK;
+          tma_load_2d_pair(st, &tm_a_hi, x, m0, bar);
+          if (p.two_a) tma_load_2d_pair(st + kTileA, &tm_a_lo, x, m0, bar);
+          tma_load_2d_pair(st + 2 * kTileA, &tm_w, x, rb, bar);
+        }
+      }
+      // Before this CTA may exit, its last copies must have landed: the
+      // leader sees them on `full`, the peer through the MMAs' release of its stages.
+      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i) {
+        if (cr == 0)
+          mbar_wait(&full[i % kStages], (i / kStages) & 1, p.err);
+        else
+          mbar_wait(&empty[i % kStages], (i / kStages) & 1, p.err);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && cr == 0) {  // ---- MMA issuer (leader only): tile i into accumulator i % 2 of both CTAs
+      bool ok = true;
+      int used = 0, i = 0;
+      const uint32_t peer_empty0 = cluster_addr(smem_u32(&empty[0]), 1);
+      const uint32_t peer_tfull0 = cluster_addr(smem_u32(&tmem_full[0]), 1);
+      for (int t = pair; t < ntiles && ok; t += npairs, ++i) {
+        const int buf = i & 1;
+        const uint32_t acc = tmem + static_cast<uint32_t>(buf * 256);
+        if (i >= 2 && !(ok = mbar_wait(&tmem_empty[buf], ((i >> 1) - 1) & 1, p.err))) break;
+        tc_fence_after();
+        for (int kb = 0; kb < p.nk; ++kb, ++used) {
+          const int s = used % kStages;
+          if (!(ok = mbar_wait(&full[s], (used / kStages) & 1, p.err))) break;
+          tc_fence_after();
+          const uint32_t st = base + s * L::stage;
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            const uint64_t bdesc = umma_desc(st + 2 * kTileA + k * 32);
+            umma_bf16_pair(acc, umma_desc(st + k * 32), bdesc, L::idesc, (kb | k) != 0);
+            if (p.two_a) umma_bf16_pair(acc, umma_desc(st + kTileA + k * 32), bdesc, L::idesc, 1u);
+          }
+          umma_commit_pair(cluster_addr(smem_u32(&empty[s]), 0));  // both CTAs' stage s is free
+          umma_commit_pair(peer_empty0 + s * 8);
+        }
+        if (ok) {
+          umma_commit_pair(cluster_addr(smem_u32(&tmem_full[buf]), 0));
+          umma_commit_pair(peer_tfull0 + buf * 8);
+        }
+      }
+    }
+  } else {  // ---- epilogue warps 2-5 (both CTAs): this CTA's 128 rows of the tile
+    const int wq = warp & 3;
+    const uint32_t leader_te0 = cluster_addr(smem_u32(&tmem_empty[0]), 0);
+    int i = 0;
+    for (int t = pair; t < ntiles; t += npairs, ++i) {
+      const int buf = i & 1;
+      const int m0 = tile_m0(t) + 128 * static_cast<int>(cr), n0 = tile_n0(t);
+      const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(buf * 256);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[buf], (i >> 1) & 1, p.err))) break;
+      epilogue_tile<EPI, 256>(p, trow, m0, n0, wq, lane, epi_t);
+      tc_fence_before();  // this warp's TMEM loads come before the MMAs that reuse the accumulator
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_te0 + buf * 8);
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // neither CTA leaves while the other may still signal it or use its TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::tmem_cols) : "memory");
   }
 }
 
@@ -296,6 +460,42 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
   }
   const int cols = p.epi == GE_SILU ? 128 : 256;
   q.n_tiles = (p.N + cols - 1) / cols;
+  // CTA pairs (256-row tiles, VVLI_GEMM_PAIR=1 above 128 rows): a quarter
+  // less L2 traffic for the same waves, measured no faster (the single-CTA
+  // kernel already issues at the measured tensor peak inside a wave), so off.
+  static const bool pair_on = getenv("VVLI_GEMM_PAIR") && getenv("VVLI_GEMM_PAIR")[0] == '1';
+  if ((p.M > kGemmBM && pair_on && !p.force_single) || p.force_pair) {
+    static int max_pairs = 0;
+    if (!max_pairs) {
+      cudaLaunchConfig_t oc = {};
+      oc.gridDim = dim3(2 * sms);
+      oc.blockDim = dim3(kGemmThreads);
+      oc.dynamicSmemBytes = TcPairLayout::smem;
+      cudaLaunchAttribute ca[1];
+      ca[0].id = cudaLaunchAttributeClusterDimension;
+      ca[0].val.clusterDim.x = 2, ca[0].val.clusterDim.y = 1, ca[0].val.clusterDim.z = 1;
+      oc.attrs = ca;
+      oc.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&max_pairs, gemm_tc_pair_kernel<GE_RESID>, &oc) != cudaSuccess || max_pairs < 1)
+        max_pairs = sms / 2;
+    }
+    const int pairs = std::min((p.M + 255) / 256 * q.n_tiles, max_pairs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = TcPairLayout::smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    switch (p.epi) {
+      case GE_QKV: return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel<GE_QKV>, a_hi, a_lo, w, q);
+      case GE_RESID: return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel<GE_RESID>, a_hi, a_lo, w, q);
+      default: return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel<GE_SILU>, a_hi, a_lo, w, q);
+    }
+  }
   const int grid = std::min(mt * q.n_tiles, sms);
   constexpr size_t smem = TcLayout<256>::smem;
   switch (p.epi) {
@@ -318,6 +518,14 @@ cudaError_t configure_gemm_tc(int max_smem_optin) {
                                 TcLayout<256>::smem)) ||
       (e = cudaFuncSetAttribute(gemm_tc_kernel<GE_RESID, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 TcLayout<128>::smem)))
+    return e;
+  if (static_cast<int>(TcPairLayout::smem) > max_smem_optin) return cudaErrorInvalidValue;
+  if ((e = cudaFuncSetAttribute(gemm_tc_pair_kernel<GE_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TcPairLayout::smem)) ||
+      (e = cudaFuncSetAttribute(gemm_tc_pair_kernel<GE_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TcPairLayout::smem)) ||
+      (e = cudaFuncSetAttribute(gemm_tc_pair_kernel<GE_SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TcPairLayout::smem)))
     return e;
   return cudaSuccess;
 }
@@ -763,7 +971,8 @@ __global__ void max_rel_err_kernel(const float* a, const float* b, size_t n, flo
 
 // Runs C = A . W^T through the tensor-core GEMM and a SIMT fp64-accumulating
 // reference on random data; *max_rel_err = max |C - ref| / max |ref|.
-cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int skinny, uint64_t seed, float* max_rel_err) {
+cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int kernel, uint64_t seed, float* max_rel_err) {
+  const bool skinny = kernel == 1;
   cudaError_t e;
   int dev = 0, optin = 0;
   if ((e = cudaGetDevice(&dev))) return e;
@@ -797,6 +1006,8 @@ cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int skinny, uint64_
   GemmParams p{};
   p.M = M, p.N = N, p.K = K, p.nk = (K + kGemmBK - 1) / kGemmBK, p.two_a = two_a, p.epi = GE_RESID;
   p.y = c, p.ldy = N, p.add_residual = 0, p.err = err;
+  p.force_pair = kernel == 2 ? 1 : 0;
+  if (kernel == 0 && M > kGemmBM) p.force_single = 1;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if ((e = skinny ? launch_gemm_skinny(mhi, mlo, mw, p, skinny_split(p.epi, M, N, p.nk, sms), 0) : launch_gemm_tc(mhi, mlo, mw, p, 0))) {

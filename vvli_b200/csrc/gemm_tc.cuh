@@ -42,6 +42,8 @@ struct GemmParams {
   // its pages are page_table[b * seq_pages ..]
   const int* row_pos;
   int seq_pages;
+  // gemm_tc self-test: force the CTA-pair kernel (256-row tiles) or the single-CTA one
+  int force_pair, force_single;
 };
 
 // Encodes a 2-D bf16 tensor map [rows, cols] (cols contiguous) with a

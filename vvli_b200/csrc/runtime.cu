@@ -2127,7 +2127,7 @@ int vvli_cuda_attention_selftest(int device, int d, int group, int tokens, int p
 
 int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two_a, uint64_t seed,
                             float* max_rel_err) {
-  if (!max_rel_err || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 2 || kernel < 0 || kernel > 1 ||
+  if (!max_rel_err || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 2 || kernel < 0 || kernel > 2 ||
       (kernel == 1 && M > kSkinnyMaxRows))
     return VVLI_ERR_INVALID_ARGUMENT;
   CK(cudaSetDevice(device));
