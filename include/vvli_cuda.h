@@ -317,7 +317,10 @@ int vvli_cuda_trace(vvli_ctx* ctx, uint64_t* out, uint64_t cap, uint64_t* count)
  * GEMM on single CTAs (128 x 256 tiles); kernel 1: the decode-batch GEMM
  * (M <= 32 rows, weight rows as the MMA's M operand, split-K over a
  * cluster); kernel 2: the prefill GEMM on CTA pairs (256 x 256 tiles,
- * cta_group::2), which prefill uses above 128 rows. */
+ * cta_group::2, opt-in with VVLI_GEMM_PAIR=1); kernel 3: the prefill GEMM
+ * with the stream-K schedule prefill runs (the last waves' k-blocks shared
+ * evenly by all SMs, split tiles summed in k order), run twice to check that
+ * the result repeats bit for bit. */
 int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two_a, uint64_t seed,
                             float* max_rel_err);
 

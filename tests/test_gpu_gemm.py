@@ -25,6 +25,26 @@ def test_gemm_matches_reference(M, N, K, two_a):
 
 
 @pytest.mark.parametrize("M,N,K", [
+    (128, 256, 64),      # one tile, one k-block: a single CTA, nothing split
+    (200, 1152, 896),    # 10 tiles x 14 k-blocks over 35 CTAs: tiles split 4-5 ways
+    (512, 4096, 4096),   # 128 tiles: waves 86% full, whole tiles only
+    (512, 6144, 4096),   # Llama-3-8B q|k|v on 512 tokens: 96 tiles in groups of 4 row tiles
+    (256, 4096, 14336),  # down_proj: 64 tiles x 224 k-blocks
+    (1536, 2048, 256),   # 96 tiles of 4 k-blocks over groups of 12: whole tiles, nothing split
+    (512, 28672, 512),   # 448 tiles (3.03 waves): two waves of whole tiles, then 152 tiles shared
+])
+def test_streamk_gemm_matches_reference(M, N, K):
+    # kernel 3: the stream-K schedule prefill uses; the self-test also runs it
+    # a second time over the same flags (the next epoch) and requires the
+    # same result bit for bit
+    from vvli_b200 import _abi
+    err = ctypes.c_float(0)
+    st = _abi.lib().vvli_cuda_gemm_selftest(0, 3, M, N, K, 1, 5, ctypes.byref(err))
+    assert st == 0, _abi.lib().vvli_cuda_last_error()
+    assert err.value < 1e-4, err.value
+
+
+@pytest.mark.parametrize("M,N,K", [
     (256, 256, 64),      # one CTA pair, one k-block
     (256, 256, 1024),    # ring wrap-around (16 k-blocks over 4 stages)
     (200, 512, 256),     # the second CTA's rows partly past M

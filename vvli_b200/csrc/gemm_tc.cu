@@ -21,6 +21,9 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
+#include <vector>
+#include <climits>
 #include <cstdlib>
 
 #include "device_fns.cuh"
@@ -47,9 +50,46 @@ struct TcLayout {
 
 // Epilogue of one accumulator tile by the four epilogue warps: warp wq owns
 // TMEM lanes (rows) m0 + 32 wq ..; n0 is the tile's first output column.
+// Stream-K hand-off: a writer publishes its part with a release store of the
+// launch's epoch; the finisher's bounded acquire spin reports
+// VVLI_ERR_TIMEOUT through *err when a flag never arrives.
+VVLI_DEV void st_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+VVLI_DEV bool wait_flag_gpu(const unsigned* p, unsigned v, int* err) {
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    unsigned x;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(x) : "l"(p) : "memory");
+    if (x == v) return true;
+    if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+      if (err) atomicExch(err, kErrTimeout);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+size_t gemm_tc_streamk_ws_floats(int sm_count) { return static_cast<size_t>(sm_count) * 256 * kGemmBM; }
+
+// The later parts of a split tile, in k order, are in the sk_ws slots of
+// CTAs j * sk_mt + sk_mem for j in [sk_w0, sk_w1) (none when equal).
 template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow, int m0, int n0, int wq, int lane,
-                                              float* epi_t) {
+                                              float* epi_t, int sk_w0 = 0, int sk_w1 = 0, int sk_mt = 1,
+                                              int sk_mem = 0) {
+  const int lrow = wq * 32 + lane;
+  auto add_parts = [&](float* v, int col0) {
+    for (int j = sk_w0; j < sk_w1; ++j) {
+      const int c = j * sk_mt + sk_mem;  // the writer's CTA
+      const float* ws = p.sk_ws + static_cast<size_t>(c) * BN * kGemmBM + static_cast<size_t>(col0) * kGemmBM + lrow;
+      float w[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) w[j] = __ldcg(ws + j * kGemmBM);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += w[j];
+    }
+  };
   {
     // The accumulator arrives one row per lane (TMEM lane = row); each
     // 32 x 32 chunk is turned around in this warp's shared tile so that the
@@ -69,6 +109,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
       for (int c = 0; c < 4; ++c) {
         tmem_ld32(trow + c * 32, v);        // gate columns
         tmem_ld32(trow + 128 + c * 32, u);  // up columns
+        add_parts(v, c * 32);
+        add_parts(u, 128 + c * 32);
         float g[32];
         transpose_in(v);
 #pragma unroll
@@ -89,6 +131,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
     } else {
       for (int c = 0; c < BN / 32; ++c) {
         tmem_ld32(trow + c * 32, v);
+        add_parts(v, c * 32);
         transpose_in(v);
         const int n = n0 + c * 32 + lane;
         // The rows' steps are independent: fully unrolled, so that each
@@ -188,6 +231,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int ntiles = mt * p.n_tiles;
   auto tile_m0 = [&](int t) { return (t % mt) * kGemmBM; };
   auto tile_n0 = [&](int t) { return (t / mt) * (kPair ? BN / 2 : BN); };  // first output column
+  // Work segments (tile, k-blocks [kb0, kb1)) of this CTA, in order: whole
+  // tiles b, b + G, ... (G = grid); with stream-K, whole tiles for the first
+  // sk_dp_waves waves, then a share of the rest, so that no partial last
+  // wave of whole tiles leaves SMs idle.  The CTAs go in groups of mt (G is a
+  // multiple of mt): group j takes the equal share [j U / NG, (j + 1) U / NG)
+  // of the U = (remaining column tiles) x k-blocks units, and its member m
+  // does row tile m of each, so the mt CTAs reading one weight tile still
+  // read the same k-blocks together (L2 reuse).  A member's share starts
+  // inside a tile only with its first stream-K segment (a writer) and ends
+  // inside one only with its last (the finisher of that tile), so finishers
+  // wait only on writers' first segments: no cycle.
+  const bool sk = p.sk_ws != nullptr;
+  const int dp_waves = sk ? p.sk_dp_waves : INT_MAX;
+  const int t_sk = sk ? dp_waves * static_cast<int>(gridDim.x) : ntiles;  // first stream-K tile (a multiple of mt)
+  const int ng = static_cast<int>(gridDim.x) / mt, grp = blockIdx.x / mt, mem = blockIdx.x % mt;
+  const long long U = static_cast<long long>(ntiles - t_sk) / mt * p.nk;
+  auto share = [&](int j) { return static_cast<long long>(j) * U / ng; };
+  struct Cursor {
+    long long u, uend;
+    int iter;
+  };
+  auto seg_start = [&]() { return Cursor{sk ? share(grp) : 0, sk ? share(grp + 1) : 0, 0}; };
+  auto next_seg = [&](Cursor& cu, int& t, int& kb0, int& kb1) -> bool {
+    if (cu.iter < dp_waves) {
+      t = static_cast<int>(blockIdx.x) + cu.iter++ * static_cast<int>(gridDim.x);
+      kb0 = 0, kb1 = p.nk;
+      if (t < t_sk) return true;
+      cu.iter = dp_waves;  // whole tiles done (without stream-K: all of them)
+    }
+    if (cu.u >= cu.uend) return false;
+    t = t_sk + static_cast<int>(cu.u / p.nk) * mt + mem;
+    kb0 = static_cast<int>(cu.u % p.nk);
+    kb1 = static_cast<int>(min(static_cast<long long>(p.nk), kb0 + (cu.uend - cu.u)));
+    cu.u += kb1 - kb0;
+    return true;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemmStages; ++i) {
@@ -214,13 +293,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {  // ---- TMA producer: every k-block of every tile of this CTA, one ring
       const uint32_t bytes = (p.two_a ? 2 * kTileA : kTileA) + kTileB;
-      int issued = 0;  // k-blocks issued over all tiles
+      int issued = 0;  // k-blocks issued over all segments
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      Cursor cu = seg_start();
+      int t, kb0, kb1;
+      while (ok && next_seg(cu, t, kb0, kb1)) {
         const int m0 = tile_m0(t), n0 = tile_n0(t);
         const int rb0 = n0;
         const int rb1 = kPair ? p.pair_offset + n0 : n0 + BN / 2;
-        for (int kb = 0; kb < p.nk; ++kb, ++issued) {
+        for (int kb = kb0; kb < kb1; ++kb, ++issued) {
           const int s = issued % kGemmStages;
           if (issued >= kGemmStages && !(ok = mbar_wait(&empty[s], ((issued / kGemmStages) - 1) & 1, p.err))) break;
           mbar_arrive_expect_tx(&full[s], bytes);
@@ -238,14 +319,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer: tile i into accumulator i % 2
       bool ok = true;
-      int used = 0;  // k-blocks consumed over all tiles
-      int i = 0;     // tiles of this CTA
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
+      int used = 0;  // k-blocks consumed over all segments
+      int i = 0;     // segments of this CTA
+      Cursor cu = seg_start();
+      int t, kb0, kb1;
+      for (; ok && next_seg(cu, t, kb0, kb1); ++i) {
         const int buf = i & 1;
         const uint32_t acc = tmem + static_cast<uint32_t>(buf * BN);
         if (i >= 2 && !(ok = mbar_wait(&tmem_empty[buf], ((i >> 1) - 1) & 1, p.err))) break;
         tc_fence_after();
-        for (int kb = 0; kb < p.nk; ++kb, ++used) {
+        for (int kb = kb0; kb < kb1; ++kb, ++used) {
           const int s = used % kGemmStages;
           if (!(ok = mbar_wait(&full[s], (used / kGemmStages) & 1, p.err))) break;
           tc_fence_after();
@@ -253,7 +336,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {  // UMMA_K = 16 bf16 = 32 bytes
             const uint64_t bdesc = umma_desc(st + 2 * kTileA + k * 32);
-            umma_bf16(acc, umma_desc(st + k * 32), bdesc, kIdesc, (kb | k) != 0);
+            umma_bf16(acc, umma_desc(st + k * 32), bdesc, kIdesc, (kb != kb0 || k != 0) ? 1u : 0u);
             if (p.two_a) umma_bf16(acc, umma_desc(st + kTileA + k * 32), bdesc, kIdesc, 1u);
           }
           umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
@@ -263,14 +346,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {  // ---- epilogue: warps 2-5, TMEM lanes 32 * (warp % 4) ..
     const int wq = warp & 3;
+    const int lrow = wq * 32 + lane;
+    __shared__ int sk_ok;
     int i = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+    Cursor cu = seg_start();
+    int t, kb0, kb1;
+    for (; next_seg(cu, t, kb0, kb1); ++i) {
     const int buf = i & 1;
     const int m0 = tile_m0(t), n0 = tile_n0(t);
     const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(buf * BN);
     // tcgen05.ld is warp-collective: the warp goes on only if every lane saw the accumulator.
     if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[buf], (i >> 1) & 1, p.err))) break;
-    epilogue_tile<EPI, BN>(p, trow, m0, n0, wq, lane, epi_t);
+    if (kb0 > 0) {
+      // A later part of a split tile: the raw accumulator goes to this CTA's
+      // workspace slot, column-major so that the lanes' stores coalesce.
+      tc_fence_after();
+      float v[32];
+      float* ws = p.sk_ws + static_cast<size_t>(blockIdx.x) * BN * kGemmBM + lrow;
+      for (int c = 0; c < BN / 32; ++c) {
+        tmem_ld32(trow + c * 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ws[static_cast<size_t>(c * 32 + j) * kGemmBM] = v[j];
+      }
+      __threadfence();
+      named_barrier(1, 128);
+      if (threadIdx.x == 64) st_release_gpu(p.sk_flags + blockIdx.x, p.sk_epoch);
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[buf]);
+      continue;
+    }
+    // The first part of a split tile finishes it: the same member of groups
+    // grp + 1 .. g_end - 1 holds the rest of its k-blocks, each as its first
+    // segment (CTA j * mt + mem of group j).
+    int g_end = grp + 1;
+    if (sk && t >= t_sk && kb1 < p.nk) {
+      const long long tend = static_cast<long long>((t - t_sk) / mt + 1) * p.nk;
+      while (g_end < ng && share(g_end) < tend) ++g_end;
+      if (threadIdx.x == 64) {
+        sk_ok = 1;
+        for (int j = grp + 1; j < g_end && sk_ok; ++j)
+          if (!wait_flag_gpu(p.sk_flags + j * mt + mem, p.sk_epoch, p.err)) sk_ok = 0;
+      }
+      named_barrier(1, 128);
+      if (!sk_ok) break;
+    }
+    epilogue_tile<EPI, BN>(p, trow, m0, n0, wq, lane, epi_t, grp + 1, g_end, mt, mem);
     tc_fence_before();  // this warp's TMEM loads of the tile come before the MMAs that reuse it
     mbar_arrive(&tmem_empty[buf]);
     }
@@ -452,9 +572,35 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
     if (sms <= 0) sms = 148;
   }
   GemmParams q = p;
+  // Persistent: one CTA per SM at most.  Stream-K spreads the k-blocks of the
+  // last one to two waves' tiles evenly over all SMs when whole tiles would
+  // leave more than a fifth of the waves' slots idle (measured: 8B gate|up on
+  // 512 tokens, 448 tiles = 3.03 waves, 195 -> 177 us; fuller waves lose a
+  // little to the split parts); at least 4 k-blocks of a tile per CTA keeps
+  // the parts few.
+  static const bool sk_off = getenv("VVLI_STREAMK") && getenv("VVLI_STREAMK")[0] == '0';
+  if (sk_off) q.sk_ws = nullptr;
+  // The grid is a multiple of the row tiles mt (groups of CTAs sharing a weight tile).
+  auto grid_of = [&](int tiles) {
+    const int G = std::max(1, sms / mt) * mt;
+    if (!q.sk_ws || mt > sms) {
+      q.sk_ws = nullptr;
+      return std::min(tiles, sms);
+    }
+    const int waves = (tiles + G - 1) / G;
+    if (!(tiles < 0.8 * waves * G)) {
+      q.sk_ws = nullptr;  // whole-tile waves at least 80% full: splitting costs more than it balances
+      return std::min(tiles, sms);
+    }
+    q.sk_dp_waves = tiles > G ? tiles / G - 1 : 0;
+    if (q.sk_dp_waves) return G;
+    const long long units = static_cast<long long>(tiles / mt) * p.nk;  // per group member
+    const long long groups = std::max(1LL, std::min<long long>(G / mt, units / std::min(p.nk, 4)));
+    return static_cast<int>(groups) * mt;
+  };
   if (narrow) {
     q.n_tiles = (p.N + 127) / 128;
-    const int grid = std::min(mt * q.n_tiles, sms);  // persistent: one CTA per SM at most
+    const int grid = grid_of(mt * q.n_tiles);
     gemm_tc_kernel<GE_RESID, 128><<<grid, kGemmThreads, TcLayout<128>::smem, s>>>(a_hi, a_lo, w, q);
     return cudaGetLastError();
   }
@@ -496,7 +642,7 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
       default: return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel<GE_SILU>, a_hi, a_lo, w, q);
     }
   }
-  const int grid = std::min(mt * q.n_tiles, sms);
+  const int grid = grid_of(mt * q.n_tiles);
   constexpr size_t smem = TcLayout<256>::smem;
   switch (p.epi) {
     case GE_QKV: gemm_tc_kernel<GE_QKV, 256><<<grid, kGemmThreads, smem, s>>>(a_hi, a_lo, w, q); break;
@@ -980,11 +1126,23 @@ cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int kernel, uint64_
   if ((e = configure_gemm_tc(optin))) return e;
   if (skinny && (M > kSkinnyMaxRows || (e = configure_gemm_skinny(optin)))) return e ? e : cudaErrorInvalidValue;
   uint16_t *ahi = nullptr, *alo = nullptr, *w = nullptr;
-  float *c = nullptr, *ref = nullptr, *err_out = nullptr;
+  float *c = nullptr, *ref = nullptr, *err_out = nullptr, *sk_ws = nullptr, *c2 = nullptr;
   int* err = nullptr;
+  unsigned* sk_flags = nullptr;
+  const bool streamk = kernel == 3;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   auto cleanup = [&]() {
     cudaFree(ahi), cudaFree(alo), cudaFree(w), cudaFree(c), cudaFree(ref), cudaFree(err_out), cudaFree(err);
+    cudaFree(sk_ws), cudaFree(sk_flags), cudaFree(c2);
   };
+  if (streamk && ((e = cudaMalloc(&sk_ws, gemm_tc_streamk_ws_floats(sms) * 4)) ||
+                  (e = cudaMalloc(&sk_flags, static_cast<size_t>(sms) * 4)) ||
+                  (e = cudaMemset(sk_flags, 0, static_cast<size_t>(sms) * 4)) ||
+                  (e = cudaMalloc(&c2, static_cast<size_t>(M) * N * 4)))) {
+    cleanup();
+    return e;
+  }
   if ((e = cudaMalloc(&ahi, static_cast<size_t>(M) * K * 2)) || (e = cudaMalloc(&alo, static_cast<size_t>(M) * K * 2)) ||
       (e = cudaMalloc(&w, static_cast<size_t>(N) * K * 2)) || (e = cudaMalloc(&c, static_cast<size_t>(M) * N * 4)) ||
       (e = cudaMalloc(&ref, static_cast<size_t>(M) * N * 4)) || (e = cudaMalloc(&err_out, 4)) ||
@@ -1007,12 +1165,26 @@ cudaError_t gemm_tc_selftest(int M, int N, int K, int two_a, int kernel, uint64_
   p.M = M, p.N = N, p.K = K, p.nk = (K + kGemmBK - 1) / kGemmBK, p.two_a = two_a, p.epi = GE_RESID;
   p.y = c, p.ldy = N, p.add_residual = 0, p.err = err;
   p.force_pair = kernel == 2 ? 1 : 0;
-  if (kernel == 0 && M > kGemmBM) p.force_single = 1;
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if ((kernel == 0 || streamk) && M > kGemmBM) p.force_single = 1;
+  p.sk_ws = sk_ws, p.sk_flags = sk_flags, p.sk_epoch = 1;
   if ((e = skinny ? launch_gemm_skinny(mhi, mlo, mw, p, skinny_split(p.epi, M, N, p.nk, sms), 0) : launch_gemm_tc(mhi, mlo, mw, p, 0))) {
     cleanup();
     return e;
+  }
+  if (streamk) {  // the next launch reuses the flags at the next epoch: the same C, bit for bit
+    p.y = c2, p.sk_epoch = 2;
+    int same = 0;
+    if (!(e = launch_gemm_tc(mhi, mlo, mw, p, 0)) && !(e = cudaDeviceSynchronize())) {
+      std::vector<float> h0(static_cast<size_t>(M) * N), h1(h0.size());
+      if (!(e = cudaMemcpy(h0.data(), c, h0.size() * 4, cudaMemcpyDeviceToHost)) &&
+          !(e = cudaMemcpy(h1.data(), c2, h1.size() * 4, cudaMemcpyDeviceToHost)))
+        same = std::memcmp(h0.data(), h1.data(), h0.size() * 4) == 0;
+    }
+    if (!e && !same) e = cudaErrorUnknown;
+    if (e) {
+      cleanup();
+      return e;
+    }
   }
   gemm_ref_kernel<<<dim3((N + 127) / 128, M), 128>>>(ahi, alo, w, M, N, K, two_a, ref);
   max_rel_err_kernel<<<1, 1024>>>(c, ref, static_cast<size_t>(M) * N, err_out);

@@ -44,7 +44,18 @@ struct GemmParams {
   int seq_pages;
   // gemm_tc self-test: force the CTA-pair kernel (256-row tiles) or the single-CTA one
   int force_pair, force_single;
+  // Stream-K (gemm_tc single-CTA kernel, optional): after sk_dp_waves waves of
+  // whole tiles, every CTA takes an equal share of the remaining (tile,
+  // k-block) units; a tile split across CTAs is finished by the CTA holding
+  // its first k-blocks, which adds the later parts' accumulators (workspace
+  // slot = the writer's CTA index, [BN][128] floats) in k order.
+  float* sk_ws;          // null: whole tiles only
+  unsigned* sk_flags;    // [grid]: slot b holds this launch's part when sk_flags[b] == sk_epoch
+  unsigned sk_epoch;     // > 0, a new value per launch
+  int sk_dp_waves;       // set by launch_gemm_tc
 };
+// Stream-K workspace floats for launch_gemm_tc on `sm_count` SMs (flags: sm_count).
+size_t gemm_tc_streamk_ws_floats(int sm_count);
 
 // Encodes a 2-D bf16 tensor map [rows, cols] (cols contiguous) with a
 // {64, box_rows} box and 128-byte swizzle, the layout the UMMA descriptors use.

@@ -64,9 +64,11 @@ struct Buffers {
   float *x = nullptr, *y = nullptr;
   uint16_t *xhi = nullptr, *xlo = nullptr;
   int* err = nullptr;
+  float* sk_ws = nullptr;  // stream-K parts of the prefill GEMM, as the decoder's prefill has them
+  unsigned* sk_flags = nullptr;
   ~Buffers() {
     for (uint16_t* p : w) cudaFree(p);
-    cudaFree(x), cudaFree(y), cudaFree(xhi), cudaFree(xlo), cudaFree(err);
+    cudaFree(x), cudaFree(y), cudaFree(xhi), cudaFree(xlo), cudaFree(err), cudaFree(sk_ws), cudaFree(sk_flags);
   }
 };
 
@@ -107,6 +109,11 @@ extern "C" int vvli_cuda_op_bench(int device, int M, int N, int K, int reps, flo
       (e = cudaMalloc(&b.xhi, static_cast<size_t>(xrows) * K * 2)) ||
       (e = cudaMalloc(&b.xlo, static_cast<size_t>(xrows) * K * 2)) || (e = cudaMalloc(&b.err, 4)))
     return cuda_err(e, "activations");
+  if (kind == 3 && ((e = cudaMalloc(&b.sk_ws, gemm_tc_streamk_ws_floats(sms) * 4)) ||
+                    (e = cudaMalloc(&b.sk_flags, static_cast<size_t>(sms) * 4)) ||
+                    (e = cudaMemset(b.sk_flags, 0, static_cast<size_t>(sms) * 4))))
+    return cuda_err(e, "stream-K workspace");
+  unsigned sk_epoch = 0;
   cudaMemset(b.err, 0, 4);
   cudaMemset(b.xhi, 0, static_cast<size_t>(xrows) * K * 2);
   cudaMemset(b.xlo, 0, static_cast<size_t>(xrows) * K * 2);
@@ -146,6 +153,7 @@ extern "C" int vvli_cuda_op_bench(int device, int M, int N, int K, int reps, flo
     p.err = b.err, p.ldy = N;
     if (kind == 3) {
       p.M = M, p.y = b.y;
+      p.sk_ws = b.sk_ws, p.sk_flags = b.sk_flags, p.sk_epoch = ++sk_epoch;
       return launch_gemm_tc(th[0], tl[0], tw[i], p, s);
     }
     for (int hf = 0; hf < (kind == 2 ? 2 : 1); ++hf) {

@@ -225,6 +225,9 @@ struct vvli_ctx {
   uint16_t *pf_ahi = nullptr, *pf_alo = nullptr, *pf_fhi = nullptr, *pf_flo = nullptr;
   int* pf_tokens = nullptr;
   uint8_t* pf_kvt = nullptr;  // tensor-core attention: hi / lo images of the layer's K / V tiles
+  float* pf_skws = nullptr;     // stream-K parts of the GEMMs, one slot per SM
+  unsigned* pf_skflags = nullptr;
+  unsigned pf_sk_epoch = 0;     // a new value per GEMM launch
   CUtensorMap tm_ah_hi{}, tm_ah_lo{}, tm_aq_hi{}, tm_aq_lo{}, tm_f_hi{}, tm_f_lo{};
   std::vector<CUtensorMap> tm_w;  // per layer: q|k|v, o, gate|up, down
   // decode batches (allocated on first use): chunks of up to kSkinnyMaxRows rows
@@ -738,6 +741,8 @@ int ensure_prefill_buffers(vvli_ctx* c) {
       (st = dalloc(&c->pf_ahi, cap * ka)) || (st = dalloc(&c->pf_alo, cap * ka)) ||
       (st = dalloc(&c->pf_fhi, static_cast<size_t>(cap) * c->I_l)) ||
       (st = dalloc(&c->pf_flo, static_cast<size_t>(cap) * c->I_l)) || (st = dalloc(&c->pf_tokens, cap)) ||
+      (st = dalloc(&c->pf_skws, gemm_tc_streamk_ws_floats(c->sm_count))) ||
+      (st = dalloc(&c->pf_skflags, static_cast<size_t>(c->sm_count))) ||
       (prefill_attention_tc_supported(c->d, c->group) &&
        (st = dalloc(&c->pf_kvt, prefill_attention_tc_workspace(c->d, c->nkv_l, static_cast<int>(c->max_seq))))))
     return st;
@@ -768,6 +773,12 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start, 
                   c->cfg.rope_scaling_factor, c->cfg.rope_low_freq_factor, c->cfg.rope_high_freq_factor,
                   static_cast<float>(c->cfg.rope_original_max_position)};
   int* err = &c->st->err;
+  // Every GEMM balances its last waves' k-blocks over the SMs (stream-K).
+  auto streamk = [&](GemmParams& g) {
+    g.sk_ws = c->pf_skws, g.sk_flags = c->pf_skflags;
+    if (++c->pf_sk_epoch == 0) ++c->pf_sk_epoch;
+    g.sk_epoch = c->pf_sk_epoch;
+  };
   int M = 0;
   for (uint64_t c0 = 0; c0 < n; c0 += c->pf_cap) {
     M = static_cast<int>(std::min<uint64_t>(c->pf_cap, n - c0));
@@ -786,6 +797,7 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start, 
       g.q_rows = c->q_rows, g.kv_rows = c->kv_rows, g.d = c->d, g.nkv = c->nkv_l, g.pos0 = pos0, g.rope = rope;
       g.k_cache = kc, g.v_cache = vc, g.page_table = page_table;
       g.nk = (g.K + kGemmBK - 1) / kGemmBK;
+      streamk(g);
       CK(launch_gemm_tc(c->tm_ah_hi, c->tm_ah_lo, c->tm_w[4 * l + 0], g, s));
       PrefillAttnParams a{c->pf_q, kc, vc, page_table, c->pf_ahi, c->pf_alo, M, c->nq_l, c->nkv_l, c->d,
                           c->group, pos0, 1.0f / sqrtf(static_cast<float>(c->d)), err, c->pf_kvt};
@@ -793,6 +805,7 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start, 
       GemmParams o{};
       o.M = M, o.two_a = 1, o.err = err, o.N = c->h, o.K = c->q_rows, o.epi = GE_RESID, o.y = c->pf_x, o.ldy = c->h;
       o.add_residual = c->tp_rank == 0 ? 1 : 0, o.nk = (o.K + kGemmBK - 1) / kGemmBK;
+      streamk(o);
       CK(launch_gemm_tc(c->tm_aq_hi, c->tm_aq_lo, c->tm_w[4 * l + 1], o, s));
       if (tp && (st = nccl_wait(c, nccl().AllReduce(c->pf_x, c->pf_x, static_cast<size_t>(M) * c->h, ncclFloat32,
                                                      ncclSum, c->comm, s), "allreduce")))
@@ -801,10 +814,12 @@ int prefill_tc(vvli_ctx* c, const uint32_t* tokens, uint64_t n, uint64_t start, 
       GemmParams gu{};
       gu.M = M, gu.two_a = 1, gu.err = err, gu.N = c->I_l, gu.K = c->h, gu.epi = GE_SILU, gu.pair_offset = c->I_l;
       gu.out_hi = c->pf_fhi, gu.out_lo = c->pf_flo, gu.ld_out = c->I_l, gu.nk = (gu.K + kGemmBK - 1) / kGemmBK;
+      streamk(gu);
       CK(launch_gemm_tc(c->tm_ah_hi, c->tm_ah_lo, c->tm_w[4 * l + 2], gu, s));
       GemmParams dn{};
       dn.M = M, dn.two_a = 1, dn.err = err, dn.N = c->h, dn.K = c->I_l, dn.epi = GE_RESID, dn.y = c->pf_x;
       dn.ldy = c->h, dn.add_residual = c->tp_rank == 0 ? 1 : 0, dn.nk = (dn.K + kGemmBK - 1) / kGemmBK;
+      streamk(dn);
       CK(launch_gemm_tc(c->tm_f_hi, c->tm_f_lo, c->tm_w[4 * l + 3], dn, s));
       if (tp && (st = nccl_wait(c, nccl().AllReduce(c->pf_x, c->pf_x, static_cast<size_t>(M) * c->h, ncclFloat32,
                                                      ncclSum, c->comm, s), "allreduce")))
@@ -1055,7 +1070,7 @@ void free_ctx(vvli_ctx* c) {
   void* dev[] = {c->w, c->kv, c->page_table, c->x, c->qkv, c->attn, c->ff, c->logits, c->logits_full, c->emb_in,
                  c->hidden, c->attn_part, c->amax_val, c->amax_idx, c->best, c->all_best, c->counters,
                  c->seq_tokens, c->st, c->ssq, c->bar, c->epoch, c->d_phases, c->trace, c->w_downT, c->acc, c->pf_x, c->pf_q,
-                 c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->pf_kvt, c->smp_stamp, c->smp_key32,
+                 c->pf_ahi, c->pf_alo, c->pf_fhi, c->pf_flo, c->pf_tokens, c->pf_kvt, c->pf_skws, c->pf_skflags, c->smp_stamp, c->smp_key32,
                  c->smp_key64, c->smp_key64_sorted, c->smp_probs, c->smp_logits, c->smp_state, c->smp_done,
                  c->bt_x, c->bt_q, c->bt_logits, c->bt_best, c->bt_all_best, c->bt_part, c->bt_logits_all, c->bt_ahi,
                  c->bt_alo, c->bt_fhi, c->bt_flo, c->bt_tokens, c->bt_pos, c->bt_idx, c->bt_counters};
@@ -2127,7 +2142,7 @@ int vvli_cuda_attention_selftest(int device, int d, int group, int tokens, int p
 
 int vvli_cuda_gemm_selftest(int device, int kernel, int M, int N, int K, int two_a, uint64_t seed,
                             float* max_rel_err) {
-  if (!max_rel_err || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 2 || kernel < 0 || kernel > 2 ||
+  if (!max_rel_err || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 2 || kernel < 0 || kernel > 3 ||
       (kernel == 1 && M > kSkinnyMaxRows))
     return VVLI_ERR_INVALID_ARGUMENT;
   CK(cudaSetDevice(device));
