@@ -8,7 +8,7 @@
 //   * warp 0: TMA producer (cp.async.bulk.tensor 2-D, no multicast);
 //     warp 1: allocates 256 TMEM columns, one thread issues
 //     tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32 in TMEM) and
-//     frees stages with tcgen05.commit; warps 2-5: epilogue, tcgen05.ld of
+//     frees stages with tcgen05.commit; warps 2-9: epilogue, tcgen05.ld of
 //     the accumulator (TMEM lane = token row);
 //   * activations are fp32 in the reference.  They enter the tensor cores as
 //     two bf16 operands, hi = bf16(a) and lo = bf16(a - hi), and both MMAs
@@ -33,7 +33,9 @@
 namespace vvli {
 
 constexpr uint32_t kTileA = kGemmBM * kGemmBK * 2;   // 16 KB
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;      // single-CTA kernel: producer, MMA, 8 epilogue warps
+constexpr int kPairThreads = 192;      // CTA-pair kernel: producer, MMA, 4 epilogue warps
+constexpr int kEpiTileFloats = 32 * 32;  // an epilogue warp's transpose tile (XOR-swizzled)
 
 // Tile shape per output width BN (256, or 128 for matrices with few column
 // tiles, so the grid still covers the SMs): stages fill ~192 KB.
@@ -45,11 +47,9 @@ struct TcLayout {
   static constexpr uint32_t tmem_cols = 2 * BN;  // two accumulators: tile i + 1's MMAs run during tile i's epilogue
   static constexpr uint32_t idesc = umma_idesc(kGemmBM, BN);
   static constexpr size_t smem =
-      static_cast<size_t>(stages) * stage + 1024 /*align*/ + 256 /*barriers*/ + 4 * 32 * 33 * 4 /*epilogue tiles*/;
+      static_cast<size_t>(stages) * stage + 1024 /*align*/ + 256 /*barriers*/ + 8 * kEpiTileFloats * 4 /*epilogue tiles*/;
 };
 
-// Epilogue of one accumulator tile by the four epilogue warps: warp wq owns
-// TMEM lanes (rows) m0 + 32 wq ..; n0 is the tile's first output column.
 // Stream-K hand-off: a writer publishes its part with a release store of the
 // launch's epoch; the finisher's bounded acquire spin reports
 // VVLI_ERR_TIMEOUT through *err when a flag never arrives.
@@ -72,12 +72,15 @@ VVLI_DEV bool wait_flag_gpu(const unsigned* p, unsigned v, int* err) {
 
 size_t gemm_tc_streamk_ws_floats(int sm_count) { return static_cast<size_t>(sm_count) * 256 * kGemmBM; }
 
+// Epilogue of one accumulator tile: warp wq of each set of four owns TMEM
+// lanes (rows) m0 + 32 wq .. and takes the 32-column chunks half, half +
+// halves, ...; n0 is the tile's first output column.
 // The later parts of a split tile, in k order, are in the sk_ws slots of
 // CTAs j * sk_mt + sk_mem for j in [sk_w0, sk_w1) (none when equal).
 template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow, int m0, int n0, int wq, int lane,
-                                              float* epi_t, int sk_w0 = 0, int sk_w1 = 0, int sk_mt = 1,
-                                              int sk_mem = 0) {
+                                              float* epi_t, int half, int halves, int sk_w0 = 0, int sk_w1 = 0,
+                                              int sk_mt = 1, int sk_mem = 0) {
   const int lrow = wq * 32 + lane;
   auto add_parts = [&](float* v, int col0) {
     for (int j = sk_w0; j < sk_w1; ++j) {
@@ -101,12 +104,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
     auto transpose_in = [&](const float* src) {
       __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) epi_t[lane * 33 + j] = src[j];
+      for (int j = 0; j < 32; ++j) epi_t[lane * 32 + (j ^ lane)] = src[j];
       __syncwarp();
     };
     if constexpr (EPI == GE_SILU) {
       float u[32];
-      for (int c = 0; c < 4; ++c) {
+      for (int c = half; c < 4; c += halves) {
         tmem_ld32(trow + c * 32, v);        // gate columns
         tmem_ld32(trow + 128 + c * 32, u);  // up columns
         add_parts(v, c * 32);
@@ -114,7 +117,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
         float g[32];
         transpose_in(v);
 #pragma unroll
-        for (int r = 0; r < 32; ++r) g[r] = epi_t[r * 33 + lane];
+        for (int r = 0; r < 32; ++r) g[r] = epi_t[r * 32 + (lane ^ r)];
         transpose_in(u);
         const int n = n0 + c * 32 + lane;
         if (n < p.N) {
@@ -122,14 +125,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
           for (int r = 0; r < 32; ++r) {
             const int row_r = wrow0 + r;
             if (row_r >= p.M) break;
-            const float f = (g[r] / (1.0f + expf(-g[r]))) * epi_t[r * 33 + lane];  // siluMulInto, src/llm.zig:1382-1387
+            const float f = (g[r] / (1.0f + expf(-g[r]))) * epi_t[r * 32 + (lane ^ r)];  // siluMulInto, src/llm.zig:1382-1387
             const size_t o = static_cast<size_t>(row_r) * p.ld_out + n;
             split_bf16(f, p.out_hi[o], p.out_lo[o]);
           }
         }
       }
     } else {
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += halves) {
         tmem_ld32(trow + c * 32, v);
         add_parts(v, c * 32);
         transpose_in(v);
@@ -146,7 +149,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
             for (int r = 0; r < 32; ++r) old[r] = (p.add_residual && r < rows) ? y[static_cast<size_t>(r) * p.ldy] : 0.f;
 #pragma unroll
             for (int r = 0; r < 32; ++r)
-              if (r < rows) y[static_cast<size_t>(r) * p.ldy] = old[r] + epi_t[r * 33 + lane];  // addInto
+              if (r < rows) y[static_cast<size_t>(r) * p.ldy] = old[r] + epi_t[r * 32 + (lane ^ r)];  // addInto
           }
         } else {  // GE_QKV: column n of rows wrow0 ..; rotary pairs (n, n ^ 1) sit in neighbouring lanes
           const bool live = n < p.N;
@@ -173,7 +176,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int rr = r + h;
-              float x = epi_t[rr * 33 + lane];
+              float x = epi_t[rr * 32 + (lane ^ rr)];
               if (p.bias) x = x + bias;
               const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
               const int page = __shfl_sync(0xffffffffu, my_page, rr);
@@ -221,7 +224,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tmem_empty = tmem_full + 2;       // [2] the epilogue has read it
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 2);
   // epilogue warps' 32 x 33 transpose tiles, after the 256 bytes of barriers
-  float* epi_t = reinterpret_cast<float*>(sm + kGemmStages * kStageBytes + 256) + ((threadIdx.x >> 5) & 3) * 32 * 33;
+  // epilogue warps' transpose tiles, after the 256 bytes of barriers
+  float* epi_t = reinterpret_cast<float*>(sm + kGemmStages * kStageBytes + 256) +
+                 ((threadIdx.x >> 5) >= 2 ? (threadIdx.x >> 5) - 2 : 0) * kEpiTileFloats;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr bool kPair = EPI == GE_SILU;
   // Persistent: CTA b takes tiles b, b + grid, ...  Row tiles vary fastest,
@@ -275,8 +280,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(&tmem_full[0], 1);
     mbar_init(&tmem_full[1], 1);
-    mbar_init(&tmem_empty[0], 128);
-    mbar_init(&tmem_empty[1], 128);
+    mbar_init(&tmem_empty[0], 256);  // every epilogue thread
+    mbar_init(&tmem_empty[1], 256);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -344,8 +349,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ok) umma_commit(&tmem_full[buf]);
       }
     }
-  } else {  // ---- epilogue: warps 2-5, TMEM lanes 32 * (warp % 4) ..
-    const int wq = warp & 3;
+  } else {  // ---- epilogue: warps 2-9, TMEM lanes 32 * (warp % 4) ..
+    // Two warps per TMEM lane quarter (a warp may read only lanes
+    // 32 (warp % 4) ..), each taking every other 32-column chunk.
+    const int wq = warp & 3, half = (warp - 2) >> 2;
     const int lrow = wq * 32 + lane;
     __shared__ int sk_ok;
     int i = 0;
@@ -363,13 +370,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       float v[32];
       float* ws = p.sk_ws + static_cast<size_t>(blockIdx.x) * BN * kGemmBM + lrow;
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += 2) {
         tmem_ld32(trow + c * 32, v);
 #pragma unroll
         for (int j = 0; j < 32; ++j) ws[static_cast<size_t>(c * 32 + j) * kGemmBM] = v[j];
       }
       __threadfence();
-      named_barrier(1, 128);
+      named_barrier(1, 256);
       if (threadIdx.x == 64) st_release_gpu(p.sk_flags + blockIdx.x, p.sk_epoch);
       tc_fence_before();
       mbar_arrive(&tmem_empty[buf]);
@@ -387,10 +394,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int j = grp + 1; j < g_end && sk_ok; ++j)
           if (!wait_flag_gpu(p.sk_flags + j * mt + mem, p.sk_epoch, p.err)) sk_ok = 0;
       }
-      named_barrier(1, 128);
+      named_barrier(1, 256);
       if (!sk_ok) break;
     }
-    epilogue_tile<EPI, BN>(p, trow, m0, n0, wq, lane, epi_t, grp + 1, g_end, mt, mem);
+    epilogue_tile<EPI, BN>(p, trow, m0, n0, wq, lane, epi_t, half, 2, grp + 1, g_end, mt, mem);
     tc_fence_before();  // this warp's TMEM loads of the tile come before the MMAs that reuse it
     mbar_arrive(&tmem_empty[buf]);
     }
@@ -423,11 +430,11 @@ struct TcPairLayout {
   static constexpr int stages = 4;
   static constexpr uint32_t tmem_cols = 512;                  // two 256-column accumulators
   static constexpr uint32_t idesc = umma_idesc(256, 256);
-  static constexpr size_t smem = static_cast<size_t>(stages) * stage + 1024 + 256 + 4 * 32 * 33 * 4;
+  static constexpr size_t smem = static_cast<size_t>(stages) * stage + 1024 + 256 + 4 * kEpiTileFloats * 4;
 };
 
 template <int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
                         const __grid_constant__ CUtensorMap tm_w, const GemmParams p) {
   using L = TcPairLayout;
@@ -442,7 +449,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tmem_full = empty + kStages;  // [2]
   uint64_t* tmem_empty = tmem_full + 2;   // [2], the leader's counts both CTAs' epilogue warps
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 2);
-  float* epi_t = reinterpret_cast<float*>(sm + kStages * L::stage + 256) + ((threadIdx.x >> 5) & 3) * 32 * 33;
+  float* epi_t = reinterpret_cast<float*>(sm + kStages * L::stage + 256) + ((threadIdx.x >> 5) & 3) * kEpiTileFloats;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t cr = cluster_rank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
@@ -543,7 +550,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m0 = tile_m0(t) + 128 * static_cast<int>(cr), n0 = tile_n0(t);
       const uint32_t trow = tmem + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(buf * 256);
       if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[buf], (i >> 1) & 1, p.err))) break;
-      epilogue_tile<EPI, 256>(p, trow, m0, n0, wq, lane, epi_t);
+      epilogue_tile<EPI, 256>(p, trow, m0, n0, wq, lane, epi_t, 0, 1);
       tc_fence_before();  // this warp's TMEM loads come before the MMAs that reuse the accumulator
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_te0 + buf * 8);
@@ -615,7 +622,7 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
     if (!max_pairs) {
       cudaLaunchConfig_t oc = {};
       oc.gridDim = dim3(2 * sms);
-      oc.blockDim = dim3(kGemmThreads);
+      oc.blockDim = dim3(kPairThreads);
       oc.dynamicSmemBytes = TcPairLayout::smem;
       cudaLaunchAttribute ca[1];
       ca[0].id = cudaLaunchAttributeClusterDimension;
@@ -628,7 +635,7 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
     const int pairs = std::min((p.M + 255) / 256 * q.n_tiles, max_pairs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(kGemmThreads);
+    cfg.blockDim = dim3(kPairThreads);
     cfg.dynamicSmemBytes = TcPairLayout::smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
