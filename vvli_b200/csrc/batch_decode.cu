@@ -31,24 +31,34 @@ VVLI_DEV void split_pair(float v, uint16_t* hi, uint16_t* lo) {
 // CTA = (split s, kv head g, row b).  Split s owns a contiguous range of the
 // row's 64-position pages; each page's K and V rows ([kPage][d] fp32, one
 // contiguous block per kv head) arrive with two cp.async.bulk copies into a
-// ring of `nslots` shared-memory slots; with one slot, the several CTAs per
-// SM keep pages in flight while others compute.  Scores: a warp takes 4 positions, lane l
-// holds dims [l*DPL, (l+1)*DPL) of the key and of every q head (q stays in
-// registers), and the heads' partial dot products meet in reduce_heads8.
-// P.V: one (head, dim) output per thread, 8 independent partial sums.
-// GH: q heads per kv head held per lane (4 when the group has at most 4, else 8).
+// ring of `nslots` shared-memory slots.  Every warp runs its own online
+// softmax over 4 positions of each page (positions 4w .. 4w + 3): lane l holds
+// dims [l*DPL, (l+1)*DPL) of the key, of every q head (q in registers) and of
+// the warp's output accumulators; the heads' dot products meet in a shuffle
+// reduce-scatter, the 5 GH exponentials of a page are computed once each,
+// spread over the lanes.  No block-wide barrier per page: a warp releases a
+// slot on its `empty` barrier and thread 0 refills it once all warps have.
+// At the end the 16 warps' (max, sum, o) triples merge in shared memory.
+template <int GH>
+VVLI_DEV int head_lane(int h) {  // a lane holding head h's sum after reduce_heads4 / reduce_heads8
+  return GH == 4 ? (h >> 1) * 16 + (h & 1) * 8 : (h >> 2) * 16 + ((h >> 1) & 1) * 8 + (h & 1) * 4;
+}
+
 template <int DPL, int GH>
 __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const BatchAttnParams p) {
+  constexpr int kWarps = kBaThreads / 32;
+  constexpr int kPosPerWarp = kBaTile / kWarps;  // 4
   extern __shared__ __align__(128) float sm[];
   const int G = p.group, d = p.d, nslot = p.nslots;
   const int page_floats = kPage * d;
   float* kv = sm;                              // [nslot][K | V][kPage][d]
   float* qs = kv + nslot * 2 * page_floats;    // [G][d]
-  float* sc = qs + G * d;                      // [G][kBaTile]
-  float* mrun = sc + G * kBaTile;
-  float* lrun = mrun + G;
-  float* alpha = lrun + G;
-  __shared__ __align__(8) uint64_t bar[kBaMaxSlots];
+  float* wacc = qs + G * d;                    // [warps][G][d] the warps' output accumulators
+  float* wml = wacc + kWarps * G * d;          // [warps][G][2] their (max, sum)
+  float* mrun = wml + kWarps * G * 2;          // [G] merged max
+  float* lrun = mrun + G;                      // [G] merged sum
+  __shared__ __align__(8) uint64_t full[kBaMaxSlots];
+  __shared__ __align__(8) uint64_t empty[kBaMaxSlots];
   __shared__ int last_flag;
   const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -61,20 +71,24 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
   const int qd = p.nq * d;
   grid_launch_dependents();
   if (tid == 0) {
-    for (int i = 0; i < nslot; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < nslot; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kWarps);
+    }
     fence_barrier_init();
   }
+  __syncthreads();
   auto issue = [&](int page, int slot) {  // thread 0
     const int rows = min(kPage, n_ctx - page * kPage);
     const uint32_t bytes = static_cast<uint32_t>(rows * d * 4);
     const size_t off = kv_off(pt, page * kPage, g, p.nkv, d);
     float* kb = kv + static_cast<size_t>(slot) * 2 * page_floats;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier reads of the slot come first
-    mbar_arrive_expect_tx(&bar[slot], 2 * bytes);
-    bulk_g2s(kb, p.k_cache + off, bytes, &bar[slot]);
-    bulk_g2s(kb + page_floats, p.v_cache + off, bytes, &bar[slot]);
+    mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+    bulk_g2s(kb, p.k_cache + off, bytes, &full[slot]);
+    bulk_g2s(kb + page_floats, p.v_cache + off, bytes, &full[slot]);
   };
-  int issued = 0, waited = 0;
+  int issued = 0;
   // Pages before the row's last one hold earlier positions only, which the
   // previous kernel (the q|k|v GEMM writing position `pos`) does not touch:
   // they are fetched before the dependency wait.
@@ -82,48 +96,45 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
     for (; issued < nslot && p_begin + issued < min(p_end, np - 1); ++issued) issue(p_begin + issued, issued);
   grid_dependency_wait();
   for (int i = tid; i < G * d; i += kBaThreads) qs[i] = p.q[static_cast<size_t>(b) * qd + static_cast<size_t>(g * G) * d + i];
-  for (int i = tid; i < G; i += kBaThreads) {
-    mrun[i] = -INFINITY;
-    lrun[i] = 0.f;
-  }
   __syncthreads();
   if (tid == 0)
     for (; issued < nslot && p_begin + issued < p_end; ++issued) issue(p_begin + issued, issued);
-  // this lane's slice of every q head of the group
+  // this lane's slice of every q head of the group, and of the warp's outputs
   const bool lane_on = lane * DPL < d;
-  float qr[GH][DPL];
+  float qr[GH][DPL], acc[GH][DPL], m[GH], l[GH];
 #pragma unroll
-  for (int hh = 0; hh < GH; ++hh)
+  for (int hh = 0; hh < GH; ++hh) {
+    m[hh] = -INFINITY;
+    l[hh] = 0.f;
 #pragma unroll
-    for (int k = 0; k < DPL; ++k) qr[hh][k] = (hh < G && lane_on) ? qs[hh * d + lane * DPL + k] : 0.f;
-  const int nacc = (G * d + kBaThreads - 1) / kBaThreads;  // <= 2 (G * d <= 1024)
-  float acc[2] = {0.f, 0.f};
+    for (int k = 0; k < DPL; ++k) {
+      qr[hh][k] = (hh < G && lane_on) ? qs[hh * d + lane * DPL + k] : 0.f;
+      acc[hh][k] = 0.f;
+    }
+  }
   bool ok = true;
-  constexpr int kPosPerWarp = kBaTile / (kBaThreads / 32);
   for (int page = p_begin, it = 0; page < p_end; ++page, ++it) {
     const int slot = it % nslot;
-    ok = __syncthreads_and(mbar_wait(&bar[slot], (it / nslot) & 1, p.err) ? 1 : 0) != 0;
-    ++waited;
-    if (!ok) break;
+    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&full[slot], (it / nslot) & 1, p.err)))) break;
     const int n = min(kPage, n_ctx - page * kPage);
     const float* ks = kv + static_cast<size_t>(slot) * 2 * page_floats;
-    float* vs = kv + static_cast<size_t>(slot) * 2 * page_floats + page_floats;
-    // P.V below runs over the whole page: rows past n (never copied) become 0
-    for (int i = n * d + tid; i < page_floats; i += kBaThreads) vs[i] = 0.f;
-    // scores
+    const float* vs = ks + page_floats;
+    // scores of this warp's positions for every head (all lanes)
+    float sc[kPosPerWarp][GH];
 #pragma unroll
     for (int jj = 0; jj < kPosPerWarp; ++jj) {
       const int j = warp * kPosPerWarp + jj;
+      const bool valid = j < n;
       float kx[DPL];
       if constexpr (DPL == 4) {
-        const float4 t = (j < n && lane_on) ? *reinterpret_cast<const float4*>(ks + j * d + lane * 4)
+        const float4 t = (valid && lane_on) ? *reinterpret_cast<const float4*>(ks + j * d + lane * 4)
                                             : make_float4(0.f, 0.f, 0.f, 0.f);
         kx[0] = t.x, kx[1] = t.y, kx[2] = t.z, kx[3] = t.w;
       } else if constexpr (DPL == 2) {
-        const float2 t = (j < n && lane_on) ? *reinterpret_cast<const float2*>(ks + j * d + lane * 2) : make_float2(0.f, 0.f);
+        const float2 t = (valid && lane_on) ? *reinterpret_cast<const float2*>(ks + j * d + lane * 2) : make_float2(0.f, 0.f);
         kx[0] = t.x, kx[1] = t.y;
       } else {
-        kx[0] = (j < n && lane_on) ? ks[j * d + lane] : 0.f;
+        kx[0] = (valid && lane_on) ? ks[j * d + lane] : 0.f;
       }
       float part[GH];
 #pragma unroll
@@ -133,81 +144,140 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
         for (int k = 0; k < DPL; ++k) a = fmaf(qr[hh][k], kx[k], a);
         part[hh] = a;
       }
-      if constexpr (GH == 8) {
-        const float dot = reduce_heads8(part, lane);
-        const int hh = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-        if ((lane & 3) == 0 && hh < G) sc[hh * kBaTile + j] = j < n ? dot * p.inv_sqrt_d : -INFINITY;
+      const float dot = GH == 4 ? reduce_heads4(part, lane) : reduce_heads8(part, lane);
+#pragma unroll
+      for (int hh = 0; hh < GH; ++hh) {
+        const float v = __shfl_sync(0xffffffffu, dot, head_lane<GH>(hh));
+        sc[jj][hh] = valid ? v * p.inv_sqrt_d : -INFINITY;
+      }
+    }
+    // online softmax (softmaxInPlace, src/llm.zig:1408-1419) over the warp's
+    // positions: the page's new maxima, then its 5 GH exponentials, one per
+    // lane (two rounds for GH = 8), shared by shuffles
+    float mnew[GH];
+#pragma unroll
+    for (int hh = 0; hh < GH; ++hh) {
+      float bm = sc[0][hh];
+#pragma unroll
+      for (int jj = 1; jj < kPosPerWarp; ++jj) bm = fmaxf(bm, sc[jj][hh]);
+      mnew[hh] = fmaxf(m[hh], bm);
+    }
+    constexpr int kNexp = (kPosPerWarp + 1) * GH;
+    float e[(kNexp + 31) / 32];
+#pragma unroll
+    for (int r = 0; r < (kNexp + 31) / 32; ++r) {
+      const int vidx = lane + 32 * r;
+      float x = -INFINITY, mm = -INFINITY;
+#pragma unroll
+      for (int hh = 0; hh < GH; ++hh) {
+#pragma unroll
+        for (int jj = 0; jj < kPosPerWarp; ++jj)
+          if (vidx == jj * GH + hh) x = sc[jj][hh], mm = mnew[hh];
+        if (vidx == kPosPerWarp * GH + hh) x = m[hh], mm = mnew[hh];
+      }
+      e[r] = (x == -INFINITY || mm == -INFINITY) ? 0.f : expf(x - mm);
+    }
+    float pr[kPosPerWarp][GH], alpha[GH];
+#pragma unroll
+    for (int hh = 0; hh < GH; ++hh) {
+#pragma unroll
+      for (int jj = 0; jj < kPosPerWarp; ++jj) {
+        const int vidx = jj * GH + hh;
+        pr[jj][hh] = __shfl_sync(0xffffffffu, e[vidx / 32], vidx % 32);
+      }
+      const int vidx = kPosPerWarp * GH + hh;
+      alpha[hh] = __shfl_sync(0xffffffffu, e[vidx / 32], vidx % 32);
+      float ls = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < kPosPerWarp; ++jj) ls += pr[jj][hh];
+      l[hh] = l[hh] * alpha[hh] + ls;
+      m[hh] = mnew[hh];
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) acc[hh][k] *= alpha[hh];
+    }
+    // P.V (addScaled, src/llm.zig:1398-1406)
+#pragma unroll
+    for (int jj = 0; jj < kPosPerWarp; ++jj) {
+      const int j = warp * kPosPerWarp + jj;
+      if (j >= n || !lane_on) continue;  // rows past n were never copied
+      float vx[DPL];
+      if constexpr (DPL == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(vs + j * d + lane * 4);
+        vx[0] = t.x, vx[1] = t.y, vx[2] = t.z, vx[3] = t.w;
+      } else if constexpr (DPL == 2) {
+        const float2 t = *reinterpret_cast<const float2*>(vs + j * d + lane * 2);
+        vx[0] = t.x, vx[1] = t.y;
       } else {
-        const float dot = reduce_heads4(part, lane);
-        const int hh = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
-        if ((lane & 7) == 0 && hh < G) sc[hh * kBaTile + j] = j < n ? dot * p.inv_sqrt_d : -INFINITY;
+        vx[0] = vs[j * d + lane];
       }
-    }
-    __syncthreads();
-    // online softmax, one warp per head (softmaxInPlace, src/llm.zig:1408-1419)
-    for (int hh = warp; hh < G; hh += kBaThreads / 32) {
-      float m = -INFINITY;
-      for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[hh * kBaTile + j]);
-      m = warp_max(m);
-      const float mnew = fmaxf(mrun[hh], m);
-      float l = 0.f;
-      for (int j = lane; j < kBaTile; j += 32) {
-        const float e = j < n ? expf(sc[hh * kBaTile + j] - mnew) : 0.f;
-        sc[hh * kBaTile + j] = e;
-        l += e;
-      }
-      l = warp_sum(l);
-      if (lane == 0) {
-        const float a = mrun[hh] == -INFINITY ? 0.f : expf(mrun[hh] - mnew);
-        alpha[hh] = a;
-        lrun[hh] = lrun[hh] * a + l;
-        mrun[hh] = mnew;
-      }
-    }
-    __syncthreads();
-    // P.V (addScaled, src/llm.zig:1398-1406): probabilities past n are 0
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int idx = tid + k * kBaThreads;
-      if (k < nacc && idx < G * d) {
-        const int hh = idx / d, e = idx % d;
-        const float4* pr4 = reinterpret_cast<const float4*>(sc + hh * kBaTile);
-        float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int hh = 0; hh < GH; ++hh)
 #pragma unroll
-        for (int j4 = 0; j4 < kBaTile / 4; j4 += 2) {
-          const float4 w0 = pr4[j4], w1 = pr4[j4 + 1];
-          const float* vj = vs + (j4 * 4) * d + e;
-          a8[0] = fmaf(w0.x, vj[0], a8[0]);
-          a8[1] = fmaf(w0.y, vj[d], a8[1]);
-          a8[2] = fmaf(w0.z, vj[2 * d], a8[2]);
-          a8[3] = fmaf(w0.w, vj[3 * d], a8[3]);
-          a8[4] = fmaf(w1.x, vj[4 * d], a8[4]);
-          a8[5] = fmaf(w1.y, vj[5 * d], a8[5]);
-          a8[6] = fmaf(w1.z, vj[6 * d], a8[6]);
-          a8[7] = fmaf(w1.w, vj[7 * d], a8[7]);
-        }
-        const float a = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
-        acc[k] = acc[k] * alpha[hh] + a;
+        for (int k = 0; k < DPL; ++k) acc[hh][k] = fmaf(pr[jj][hh], vx[k], acc[hh][k]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);  // this warp is done with the slot
+    if (tid == 0 && p_begin + issued < p_end) {  // all warps done with it: the next page goes in
+      if (!mbar_wait(&empty[slot], (it / nslot) & 1, p.err)) {
+        ok = false;
+      } else {
+        issue(p_begin + issued, slot);
+        ++issued;
       }
     }
-    __syncthreads();
-    if (tid == 0 && p_begin + issued < p_end) {  // the slot is free again: next page into it
-      issue(p_begin + issued, slot);
-      ++issued;
-    }
+    if (!__all_sync(0xffffffffu, ok)) break;
   }
-  if (!ok) {  // a copy that never landed: let the others in flight finish before exiting
+  // a copy that never landed or a slot never released: let the copies in
+  // flight finish before the CTA exits
+  if (__syncthreads_or(ok ? 0 : 1)) {
     if (tid == 0)
-      for (int i = waited; i < issued; ++i) mbar_wait(&bar[i % nslot], (i / nslot) & 1, p.err);
+      for (int i = max(0, issued - nslot); i < issued; ++i) mbar_wait(&full[i % nslot], (i / nslot) & 1, p.err);
     __syncthreads();
     return;
   }
+  // the warps' (max, sum, o) into shared memory, merged per (head, dim)
+#pragma unroll
+  for (int hh = 0; hh < GH; ++hh) {
+    if (hh >= G) break;
+    if (lane_on)
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) wacc[(warp * G + hh) * d + lane * DPL + k] = acc[hh][k];
+    if (lane == 0) {
+      wml[(warp * G + hh) * 2] = m[hh];
+      wml[(warp * G + hh) * 2 + 1] = l[hh];
+    }
+  }
+  __syncthreads();
+  const int nacc = (G * d + kBaThreads - 1) / kBaThreads;  // <= 2 (G * d <= 1024)
+  float o_acc[2] = {0.f, 0.f};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int idx = tid + k * kBaThreads;
+    if (k < nacc && idx < G * d) {
+      const int hh = idx / d, e2 = idx % d;
+      float M = -INFINITY;
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wml[(w * G + hh) * 2]);
+      float L = 0.f, o = 0.f;
+      for (int w = 0; w < kWarps; ++w) {
+        const float mw = wml[(w * G + hh) * 2];
+        const float wt = mw == -INFINITY ? 0.f : expf(mw - M);
+        L = fmaf(wml[(w * G + hh) * 2 + 1], wt, L);
+        o = fmaf(wacc[(w * G + hh) * d + e2], wt, o);
+      }
+      o_acc[k] = o;
+      if (e2 == 0) {
+        mrun[hh] = M;
+        lrun[hh] = L;
+      }
+    }
+  }
+  __syncthreads();
   const size_t out_row = static_cast<size_t>(b) * qd + static_cast<size_t>(g * G) * d;
   if (p.splits == 1) {
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int idx = tid + k * kBaThreads;
-      if (k < nacc && idx < G * d) split_pair(acc[k] / lrun[idx / d], p.out_hi + out_row + idx, p.out_lo + out_row + idx);
+      if (k < nacc && idx < G * d) split_pair(o_acc[k] / lrun[idx / d], p.out_hi + out_row + idx, p.out_lo + out_row + idx);
     }
     return;
   }
@@ -218,7 +288,7 @@ __global__ void __launch_bounds__(kBaThreads) batch_attention_kernel(const Batch
     const int idx = tid + k * kBaThreads;
     if (k < nacc && idx < G * d) {
       const int hh = idx / d, e = idx % d;
-      part_b[(static_cast<size_t>(g * G + hh) * p.splits + s) * (d + 2) + e] = acc[k];
+      part_b[(static_cast<size_t>(g * G + hh) * p.splits + s) * (d + 2) + e] = o_acc[k];
     }
   }
   for (int hh = tid; hh < G; hh += kBaThreads) {
@@ -320,10 +390,9 @@ int batch_attention_slots(int d) {
   (void)d;
   const char* env = getenv("VVLI_BATCH_ATTN_SLOTS");
   if (env && atoi(env) >= 1) return std::min(kBaMaxSlots, atoi(env));
-  // One page in flight per CTA, several CTAs per SM (the splits fill them),
-  // measured ahead of two or three pages per CTA at one CTA per SM: 5.01 vs
-  // 5.03 / 5.06 ms per 8B step at batch 16, context 512.
-  return 1;
+  // Two pages in flight per CTA (one CTA per SM at 512 threads): 4.87 ms per
+  // 8B step at batch 16, context 512, against 5.19 with one and 4.88 with three.
+  return 2;
 }
 
 int batch_attention_ctas_per_sm(int group, int d, int slots) {
@@ -342,8 +411,9 @@ int batch_attention_ctas_per_sm(int group, int d, int slots) {
 }
 
 size_t batch_attention_smem(int group, int d, int slots) {
+  constexpr int kWarps = kBaThreads / 32;
   return (2 * static_cast<size_t>(slots) * kPage * d + static_cast<size_t>(group) * d +
-          static_cast<size_t>(group) * kBaTile + 3 * group) * 4;
+          static_cast<size_t>(kWarps) * group * d + static_cast<size_t>(kWarps) * group * 2 + 2 * group) * 4;
 }
 
 template <typename Kern, typename... Args>
