@@ -58,6 +58,9 @@ def parse_args():
                     help="tokens of the long-prompt prefill on the Llama-3.2-1B architecture (BASELINE config 3; 0: skip)")
     ap.add_argument("--format", choices=["bf16", "q8_0", "q4_0"], default="bf16",
                     help="weight format of the --profile decode case (block-quantised on the device)")
+    ap.add_argument("--trace", action="store_true",
+                    help="print the decode megakernel's phase timeline (VVLI_TRACE=1, every rank) instead of the "
+                         "bench line; the timestamps add stores, so its step time is not a bench figure")
     ap.add_argument("--profile", choices=["none", "prefill", "batch", "decode", "sample"], default="none",
                     help="run one call of that kind inside a CUDA profiler range (for ncu --profile-from-start off) "
                          "on a --layers cut of the model, print nothing, exit")
@@ -539,6 +542,8 @@ def _main(args, out_fd):
     if args.layers:
         cfg.num_hidden_layers = args.layers
     max_seq = min(cfg.max_position_embeddings, args.prompt + args.warmup + args.steps + args.e2e_steps + 16)
+    if args.trace:
+        os.environ["VVLI_TRACE"] = "1"
     runner = vvli_b200.Runner(cfg, max_seq=max_seq, device=local_rank, tp_rank=rank, tp_size=n, nccl_id=nccl_id)
     runner.fill_synthetic(args.seed)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, size=args.prompt).astype(np.uint32)
@@ -552,6 +557,25 @@ def _main(args, out_fd):
             pf.append(runner.last_forward_ms())
     prefill_ms = allmax(float(np.median(pf)))
     runner.decode(max(3, args.warmup))
+    if args.trace:
+        from vvli_b200.trace import summarize
+        runner.decode(4)
+        sms = torch.cuda.get_device_properties(local_rank).multi_processor_count
+        mine = summarize(runner.trace(), sms, cfg.num_hidden_layers) if runner.query("megakernel") == 1 else None
+        allr = [None] * n
+        if n > 1:
+            dist.all_gather_object(allr, mine)
+        else:
+            allr = [mine]
+        if rank == 0:
+            emit({"trace": {str(r): v for r, v in enumerate(allr)}, "n_gpus": n, "config": args.config,
+                  "position": args.prompt + max(3, args.warmup) + 4,
+                  "note": "us per phase kind, mean over layers, of one decode step; VVLI_TRACE build"}, out_fd)
+        runner.close()
+        if n > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
 
     # ---- device-timed decode: K graph replays, inputs resident in HBM
     clocks = Clocks(local_rank)

@@ -548,7 +548,9 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
         for (int s = 0; s < S; ++s) a += part[rl * S + s];
         for (int q = 0; q < P.tp; ++q) P.peer_recv[q][slot_off + static_cast<size_t>(P.rank) * P.h + r0 + rl] = a;
       }
-      __threadfence_system();
+      // The barrier orders every consumer's row stores before the flag
+      // stores below, and a release store makes visible (cumulatively) all
+      // writes ordered before it: no system-wide fence per thread is needed.
       named_barrier(1, kNC);
       const size_t flag_off = static_cast<size_t>(par) * P.tp * gridDim.x;
       if (tid < P.tp) st_release_sys(P.peer_flags[tid] + flag_off + static_cast<size_t>(P.rank) * gridDim.x + blockIdx.x, epoch);

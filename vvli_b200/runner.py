@@ -215,6 +215,16 @@ class Runner:
         return float(v.value)
 
     # ------------------------------------------------------------ debug / timing
+    def trace(self) -> np.ndarray:
+        """Megakernel timeline of the last step (VVLI_TRACE=1 at creation), else an empty array."""
+        n = ctypes.c_uint64(0)
+        check(_abi.lib().vvli_cuda_trace(self._ctx, None, 0, ctypes.byref(n)))
+        out = np.zeros(n.value, dtype=np.uint64)
+        if n.value:
+            check(_abi.lib().vvli_cuda_trace(self._ctx, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), n.value,
+                                             ctypes.byref(n)))
+        return out
+
     def set_debug(self, enabled: bool):
         check(_abi.lib().vvli_cuda_set_debug(self._ctx, int(enabled)))
 
