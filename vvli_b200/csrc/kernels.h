@@ -180,7 +180,7 @@ struct MegaParams {
   // tensor parallelism: every peer's receive rows [2][tp][h], flags [2][tp][grid],
   // argmax slots [tp][2] and their flags [tp]
   int tp, rank;
-  float* peer_recv[kMaxTp];
+  unsigned long long* peer_recv[kMaxTp];  // [2][tp][h] words: epoch << 32 | fp32 bits of a partial row
   unsigned* peer_flags[kMaxTp];
   float* peer_best[kMaxTp];
   unsigned* peer_best_flag[kMaxTp];

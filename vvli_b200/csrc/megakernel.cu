@@ -85,6 +85,24 @@ __device__ bool grid_wait(const unsigned long long* bar, uint64_t target, int* e
   return ok != 0;
 }
 
+VVLI_DEV void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// The fp32 half of *w once its high half is `epoch` (a peer's 8-byte store
+// over NVLink); bounded: on timeout VVLI_ERR_TIMEOUT and 0.
+VVLI_DEV float word_of_epoch(const unsigned long long* w, unsigned epoch, int* err) {
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
+    if (static_cast<unsigned>(v >> 32) == epoch) return __uint_as_float(static_cast<unsigned>(v));
+    if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(err, kErrTimeout);
+      return 0.f;
+    }
+  }
+}
+
 // Bounded wait until *flag == value (a peer's release store over NVLink).
 VVLI_DEV bool wait_flag_sys(const unsigned* flag, unsigned value, int* err) {
   const uint64_t t0 = global_timer_ns();
@@ -543,25 +561,22 @@ __device__ void mega_gemv(const MegaParams& P, const MegaPhase& ph, uint8_t* rin
       const unsigned epoch = epoch0 * static_cast<unsigned>(P.n_ar) + static_cast<unsigned>(ph.ar_index) + 1u;
       const int par = ph.ar_index & 1;
       const size_t slot_off = static_cast<size_t>(par) * P.tp * P.h;
+      // Each partial row travels as one 8-byte word (epoch, fp32 bits) to
+      // every rank; a word is stored and loaded whole, so the receiver
+      // polls the data itself: no fence and no separate flag.  The thread
+      // that sends row rl is the one that sums it, and the same rows on
+      // every rank belong to the same CTA index.
       for (int rl = tid; rl < nrows; rl += kNC) {
         float a = 0.f;
         for (int s = 0; s < S; ++s) a += part[rl * S + s];
-        for (int q = 0; q < P.tp; ++q) P.peer_recv[q][slot_off + static_cast<size_t>(P.rank) * P.h + r0 + rl] = a;
+        const unsigned long long w = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(a);
+        for (int q = 0; q < P.tp; ++q) st_relaxed_sys_u64(P.peer_recv[q] + slot_off + static_cast<size_t>(P.rank) * P.h + r0 + rl, w);
       }
-      // The barrier orders every consumer's row stores before the flag
-      // stores below, and a release store makes visible (cumulatively) all
-      // writes ordered before it: no system-wide fence per thread is needed.
-      named_barrier(1, kNC);
-      const size_t flag_off = static_cast<size_t>(par) * P.tp * gridDim.x;
-      if (tid < P.tp) st_release_sys(P.peer_flags[tid] + flag_off + static_cast<size_t>(P.rank) * gridDim.x + blockIdx.x, epoch);
-      if (tid < P.tp) wait_flag_sys(P.peer_flags[P.rank] + flag_off + static_cast<size_t>(tid) * gridDim.x + blockIdx.x,
-                                    epoch, err);
-      named_barrier(1, kNC);
-      const float* recv = P.peer_recv[P.rank] + slot_off;
+      const unsigned long long* recv = P.peer_recv[P.rank] + slot_off;
       for (int rl = tid; rl < nrows; rl += kNC) {
         const int r = r0 + rl;
         float a = 0.f;
-        for (int q = 0; q < P.tp; ++q) a += __ldcg(recv + static_cast<size_t>(q) * P.h + r);
+        for (int q = 0; q < P.tp; ++q) a += word_of_epoch(recv + static_cast<size_t>(q) * P.h + r, epoch, err);
         const float xn = __ldcg(P.x + r) + a;
         P.x[r] = xn;
         ss = fmaf(xn, xn, ss);

@@ -1299,16 +1299,17 @@ int vvli_cuda_create(const vvli_model_config* cfg, int device, int tp_rank, int 
 }
 
 // Tensor-parallel megakernel: each rank allocates one exchange block — the
-// receive rows of the o_proj / down_proj partial sums [2 parities][tp][h],
-// their arrival flags [2][tp][CTAs], and the LM-head argmax slots [tp][2] with
-// flags [tp] — exports it as a CUDA IPC handle, gathers every rank's handle
-// over NCCL and maps the peers' blocks.  The megakernel then stores its
-// partials straight into every peer's block over NVLink (plain stores, no
-// multicast) and waits, bounded, on its own flags.
+// receive words of the o_proj / down_proj partial sums [2 parities][tp][h]
+// (each an 8-byte word: the exchange's epoch and the row's fp32 bits), flags
+// [2][tp][CTAs], and the LM-head argmax slots [tp][2] with flags [tp] —
+// exports it as a CUDA IPC handle, gathers every rank's handle over NCCL and
+// maps the peers' blocks.  The megakernel then stores its partials straight
+// into every peer's block over NVLink (plain stores, no multicast) and polls,
+// bounded, its own block until every word carries the exchange's epoch.
 static int setup_tp_peers(vvli_ctx* c) {
   const int tp = c->tp_size, grid = c->sm_count;
   auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
-  const size_t recv_off = 0, recv_bytes = 2ull * tp * c->h * 4;
+  const size_t recv_off = 0, recv_bytes = 2ull * tp * c->h * 8;
   const size_t flag_off = up(recv_off + recv_bytes), flag_bytes = 2ull * tp * grid * 4;
   const size_t best_off = up(flag_off + flag_bytes), best_bytes = 2ull * tp * 4;
   const size_t bflag_off = up(best_off + best_bytes), bflag_bytes = static_cast<size_t>(tp) * 4;
@@ -1340,7 +1341,7 @@ static int setup_tp_peers(vvli_ctx* c) {
     }
     c->peer_base[q] = base;
     uint8_t* b = static_cast<uint8_t*>(base);
-    P.peer_recv[q] = reinterpret_cast<float*>(b + recv_off);
+    P.peer_recv[q] = reinterpret_cast<unsigned long long*>(b + recv_off);
     P.peer_flags[q] = reinterpret_cast<unsigned*>(b + flag_off);
     P.peer_best[q] = reinterpret_cast<float*>(b + best_off);
     P.peer_best_flag[q] = reinterpret_cast<unsigned*>(b + bflag_off);
