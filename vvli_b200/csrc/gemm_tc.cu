@@ -569,8 +569,13 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
                            const GemmParams& p, cudaStream_t s) {
   const int mt = (p.M + kGemmBM - 1) / kGemmBM;
   // Residual GEMMs (o_proj, down_proj: few output columns) take 128-wide tiles
-  // when 256-wide ones would leave most SMs idle.
-  const bool narrow = p.epi == GE_RESID && ((p.N + 255) / 256) * mt < 96;
+  // when 256-wide ones would leave most SMs idle, unless the k-blocks are
+  // many (>= 128) and stream-K can spread the 256-wide tiles' k-blocks over
+  // the SMs instead: half the B traffic per MMA of 128-wide tiles (8B
+  // down_proj on 512 tokens 131.7 -> 109.5 us; o_proj, 64 k-blocks, 45.1 ->
+  // 47.5 us, so it keeps the narrow tiles).
+  static const bool sk_disabled = getenv("VVLI_STREAMK") && getenv("VVLI_STREAMK")[0] == '0';
+  const bool narrow = p.epi == GE_RESID && ((p.N + 255) / 256) * mt < 96 && (!p.sk_ws || sk_disabled || p.nk < 128);
   static int sms = 0;
   if (!sms) {
     int dev = 0;
