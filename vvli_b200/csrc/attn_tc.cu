@@ -212,7 +212,9 @@ __global__ void __launch_bounds__(kAtThreads, 1) prefill_attn_tc_kernel(const Pr
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.group, g = blockIdx.x;
   const int BQ = kAtRows / G;
-  const int t0 = blockIdx.y * BQ;
+  // Token blocks in reverse: the later blocks see more keys (causal), so the
+  // longest CTAs start in the first wave and the short ones fill the tail.
+  const int t0 = (gridDim.y - 1 - blockIdx.y) * BQ;
   const int nt = min(BQ, p.M - t0);
   const int rows = G * nt;
   const int last_pos = p.pos0 + t0 + nt - 1;
