@@ -132,6 +132,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
         }
       }
     } else {
+      // q|k|v: lane r holds the KV page of row wrow0 + r, looked up once per tile
+      int my_page = 0;
+      if constexpr (EPI == GE_QKV) {
+        if (lane < p.M - wrow0 && p.page_table) my_page = p.page_table[(p.pos0 + wrow0 + lane) / kPage];
+      }
       for (int c = half; c < BN / 32; c += halves) {
         tmem_ld32(trow + c * 32, v);
         add_parts(v, c * 32);
@@ -161,9 +166,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t trow
           const bool is_k = !is_q && rot;
           const int rel = is_q ? 0 : (is_k ? n - p.q_rows : n - p.q_rows - p.kv_rows);
           float* cache = is_k ? p.k_cache : p.v_cache;
-          // lane r holds the KV page of row wrow0 + r
-          const int my_pos = p.pos0 + wrow0 + lane;
-          const int my_page = (lane < rows && p.page_table) ? p.page_table[my_pos / kPage] : 0;
           const size_t head_off = static_cast<size_t>(rel / p.d) * kPage * p.d + rel % p.d;
           // Rows r and r + 1 together: the pair's even lane takes the angle
           // of row r, the odd lane that of row r + 1, and they swap
