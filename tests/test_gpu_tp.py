@@ -10,14 +10,20 @@ oracle like the single-GPU path does.
 import multiprocessing as mp
 import os
 import sys
+import types
 
 import numpy as np
 import pytest
+
+from vvli_b200 import sampler as S
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "golden"))
 
 pytestmark = pytest.mark.gpu
+
+SAMPLE_OPTS = types.SimpleNamespace(temperature=0.8, top_p=0.95, top_k=40, repeat_penalty=1.1, repeat_last_n=64,
+                                    seed=None)
 
 
 def gpu_count():
@@ -47,6 +53,10 @@ def _rank_main(rank, world, nccl_id, cfg, blob, prompt, n_new, mega, q):
         note(f"created, megakernel={used_mega} ({vvli_b200._abi.lib().vvli_cuda_last_error().decode()})")
         logits = [r.forward_token(t, p) for p, t in enumerate(prompt)]
         note("forward_token done")
+        # Sampler.next on the last token's logits (gathered from every rank)
+        state = np.array([11, 22, 33, 44], dtype=np.uint64)
+        stok = r.sample(SAMPLE_OPTS, list(prompt), state)
+        note("sample done")
         r.reset()
         tokens, _ = r.generate_greedy(prompt, n_new)
         note("generate done")
@@ -54,9 +64,9 @@ def _rank_main(rank, world, nccl_id, cfg, blob, prompt, n_new, mega, q):
         blogits, bam = r.forward_batch(prompt[:3], [0, 0, 0])
         note("forward_batch done")
         r.close()
-        q.put((rank, "ok", np.stack(logits), tokens, used_mega, blogits, bam))
+        q.put((rank, "ok", np.stack(logits), tokens, used_mega, blogits, bam, (stok, state)))
     except Exception as e:  # reported to the parent, which fails the test
-        q.put((rank, repr(e), None, None, None, None, None))
+        q.put((rank, repr(e), None, None, None, None, None, None))
 
 
 def run_tp(cfg, blob, prompt, n_new, world, mega=True):
@@ -73,15 +83,15 @@ def run_tp(cfg, blob, prompt, n_new, world, mega=True):
     results = {}
     try:
         for _ in range(world):
-            rank, status, logits, tokens, used_mega, blogits, bam = q.get(timeout=120)
-            results[rank] = (status, logits, tokens, used_mega, blogits, bam)
+            rank, status, logits, tokens, used_mega, blogits, bam, sampled = q.get(timeout=120)
+            results[rank] = (status, logits, tokens, used_mega, blogits, bam, sampled)
     finally:
         for p in procs:  # the ranks this test started, and only those
             p.join(timeout=30)
             if p.is_alive():
                 p.kill()
                 p.join(timeout=10)
-    for rank, (status, _, _, used_mega, _, _) in results.items():
+    for rank, (status, _, _, used_mega, _, _, _) in results.items():
         assert status == "ok", (rank, status)
         assert used_mega == mega, (rank, used_mega)
     return results
@@ -101,9 +111,17 @@ def test_tp2_matches_oracle(oracle, name, mega):
     ref_tokens = ref.generate_greedy(prompt, 24)
     res = run_tp(cfg, blob, prompt, 24, 2, mega)
     for rank in range(2):
-        _, logits, tokens, _, blogits, bam = res[rank]
+        _, logits, tokens, _, blogits, bam, (stok, state) = res[rank]
         assert np.max(np.abs(logits - ref_logits)) < 1e-4, rank
         assert tokens == ref_tokens, rank
+        # the sampled token and the advanced state: as the oracle's Sampler.next
+        # on the same (gathered) logits with the same draw
+        x = S.Xoshiro256(0)
+        x.s = [11, 22, 33, 44]
+        u = x.float32()
+        assert stok == oracle.sampler_next(logits[-1], prompt, [], SAMPLE_OPTS, u), rank
+        assert [int(v) for v in state] == x.s, rank
+        assert (stok, list(state)) == (res[0][6][0], list(res[0][6][1])), rank
         # batch rows b: token prompt[b] at position 0 of its own sequence
         for b in range(3):
             ref.reset()
@@ -123,6 +141,6 @@ def test_tp2_llama3_2_1b_architecture(oracle):
     ref.reset()
     ref_tokens = ref.generate_greedy(prompt, 16)
     res = run_tp(cfg, blob, prompt, 16, 2)
-    _, logits, tokens, _, _, _ = res[0]
+    _, logits, tokens, _, _, _, _ = res[0]
     assert np.max(np.abs(logits - ref_logits)) < 2e-2
     assert tokens == ref_tokens

@@ -37,4 +37,19 @@ cudaError_t launch_rows_argmax(const float* logits, int B, int n, int ld, int ro
 cudaError_t launch_rows_argmax_merge(const float* all, int ranks, int B, int* out, cudaStream_t s);
 cudaError_t launch_rows_argmax_index(const float* best, int B, int* out, cudaStream_t s, bool pdl = false);
 
+// Tensor-parallel exchange over peer memory (every rank's block mapped in
+// every process): block q holds [2 parities][tp][cap] words, each the
+// exchange's epoch in the high half and an fp32 value in the low half.
+constexpr int kTpxMax = 8;
+struct TpExchange {
+  unsigned long long* block[kTpxMax];
+  int tp, rank, cap;
+  unsigned epoch;  // > 0, a new value per exchange, the same on every rank
+  int* err;        // VVLI_ERR_TIMEOUT when a peer's word never arrives
+};
+// gather = 0: dst[i] = sum over ranks (in rank order) of src[i], i < n;
+// gather = 1: dst[q * n + i] = rank q's src[i].  n <= cap.
+cudaError_t launch_tp_exchange(const float* src, int n, float* dst, int gather, const TpExchange& x, int sm_count,
+                               cudaStream_t s);
+
 }  // namespace vvli

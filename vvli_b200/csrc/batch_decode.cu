@@ -458,6 +458,57 @@ cudaError_t launch_rows_argmax_merge(const float* all, int ranks, int B, int* ou
   return cudaGetLastError();
 }
 
+// Each thread first stores its elements to every rank as one 8-byte word
+// (epoch, value) — stored and loaded whole, so no fence or flag is needed —
+// then polls its own block until every rank's word for those elements has
+// the epoch.  All CTAs are resident (grid <= 2 per SM), so a rank never waits
+// for a peer CTA that has not started.
+__global__ void __launch_bounds__(256) tp_exchange_kernel(const float* src, int n, float* dst, int gather,
+                                                          const TpExchange x) {
+  const int stride = gridDim.x * blockDim.x;
+  const size_t par = static_cast<size_t>(x.epoch & 1) * x.tp * x.cap;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const unsigned long long w = (static_cast<unsigned long long>(x.epoch) << 32) | __float_as_uint(src[i]);
+    for (int q = 0; q < x.tp; ++q)
+      asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(x.block[q] + par + static_cast<size_t>(x.rank) * x.cap + i),
+                   "l"(w)
+                   : "memory");
+  }
+  const unsigned long long* own = x.block[x.rank] + par;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float sum = 0.f;
+    for (int q = 0; q < x.tp; ++q) {
+      const unsigned long long* wp = own + static_cast<size_t>(q) * x.cap + i;
+      unsigned long long v;
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t it = 0;; ++it) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(wp) : "memory");
+        if (static_cast<unsigned>(v >> 32) == x.epoch) break;
+        if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+          atomicExch(x.err, kErrTimeout);
+          v = 0;
+          break;
+        }
+      }
+      const float f = __uint_as_float(static_cast<unsigned>(v));
+      if (gather)
+        dst[static_cast<size_t>(q) * n + i] = f;
+      else
+        sum += f;
+    }
+    if (!gather) dst[i] = sum;
+  }
+}
+
+cudaError_t launch_tp_exchange(const float* src, int n, float* dst, int gather, const TpExchange& x, int sm_count,
+                               cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (n > x.cap || x.tp > kTpxMax || x.epoch == 0) return cudaErrorInvalidValue;
+  const int grid = std::max(1, std::min((n + 255) / 256, 2 * sm_count));
+  tp_exchange_kernel<<<grid, 256, 0, s>>>(src, n, dst, gather, x);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_rows_argmax_index(const float* best, int B, int* out, cudaStream_t s, bool pdl) {
   return launch_pdl(rows_argmax_index_kernel, dim3((B + 127) / 128), dim3(128), 0, s, pdl, best, B, out);
 }

@@ -215,6 +215,7 @@ struct vvli_ctx {
   // tensor-parallel megakernel: this rank's exchange block (receive rows, flags,
   // argmax slots) and every rank's block mapped into this process (CUDA IPC)
   uint8_t* peer_block = nullptr;
+  TpExchange xch{};  // decode batches' all-reduces and logits gathers over the peer blocks (when mapped)
   void* peer_base[kMaxTp] = {};
   uint16_t* w_downT = nullptr;  // fused down_proj: W_down^T per layer [I_l][h]
   long long* acc = nullptr;     // fused down_proj: fixed-point accumulators [2][h]
@@ -297,6 +298,8 @@ int nccl_wait(vvli_ctx* c, ncclResult_t r, const char* what) {
   }
   return VVLI_OK;
 }
+
+int tp_collective(vvli_ctx* c, const float* src, float* dst, size_t n, bool gather, cudaStream_t s, const char* what);
 
 int validate_config(const vvli_model_config& c) {  // Config.validate (src/llm.zig:195-216)
   if (c.vocab_size == 0 || c.hidden_size == 0 || c.intermediate_size == 0 || c.num_hidden_layers == 0 ||
@@ -947,9 +950,7 @@ int forward_batch_chunk(vvli_ctx* c, const uint32_t* tokens, const uint64_t* pos
     GemmParams o{};
     o.N = c->h, o.K = c->q_rows, o.epi = GE_RESID, o.y = c->bt_x, o.ldy = c->h, o.add_residual = c->tp_rank == 0;
     if ((st = gemm(c->tmb_q[v], c->tm_w[4 * l + 1], o, pdl))) return st;
-    if (tp && (st = nccl_wait(c, nccl().AllReduce(c->bt_x, c->bt_x, static_cast<size_t>(B) * c->h, ncclFloat32,
-                                                   ncclSum, c->comm, s), "allreduce")))
-      return st;
+    if (tp && (st = tp_collective(c, c->bt_x, c->bt_x, static_cast<size_t>(B) * c->h, false, s, "allreduce"))) return st;
     CK(launch_norm_split(c->bt_x, W + D.post, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s, pdl));
     GemmParams gu{};
     gu.N = c->I_l, gu.K = c->h, gu.epi = GE_SILU, gu.pair_offset = c->I_l;
@@ -958,9 +959,7 @@ int forward_batch_chunk(vvli_ctx* c, const uint32_t* tokens, const uint64_t* pos
     GemmParams dn{};
     dn.N = c->h, dn.K = c->I_l, dn.epi = GE_RESID, dn.y = c->bt_x, dn.ldy = c->h, dn.add_residual = c->tp_rank == 0;
     if ((st = gemm(c->tmb_f[v], c->tm_w[4 * l + 3], dn, pdl))) return st;
-    if (tp && (st = nccl_wait(c, nccl().AllReduce(c->bt_x, c->bt_x, static_cast<size_t>(B) * c->h, ncclFloat32,
-                                                   ncclSum, c->comm, s), "allreduce")))
-      return st;
+    if (tp && (st = tp_collective(c, c->bt_x, c->bt_x, static_cast<size_t>(B) * c->h, false, s, "allreduce"))) return st;
   }
   // final norm + LM head of every row (src/llm.zig:727-728), then llm.argmax per row
   CK(launch_norm_split(c->bt_x, W + c->off_final, c->cfg.rms_norm_eps, B, c->h, c->bt_ahi, c->bt_alo, s, pdl));
@@ -969,9 +968,7 @@ int forward_batch_chunk(vvli_ctx* c, const uint32_t* tokens, const uint64_t* pos
   if ((st = gemm(c->tmb_h[v], c->tm_lm, lm, pdl))) return st;
   CK(launch_rows_argmax(c->bt_logits, B, c->V_lr, c->V_l, c->v0, c->bt_best, s, pdl));  // this rank's real rows only
   if (tp) {
-    if ((st = nccl_wait(c, nccl().AllGather(c->bt_best, c->bt_all_best, 2 * static_cast<size_t>(B), ncclFloat32, c->comm, s),
-                        "allgather")))
-      return st;
+    if ((st = tp_collective(c, c->bt_best, c->bt_all_best, 2 * static_cast<size_t>(B), true, s, "allgather"))) return st;
     CK(launch_rows_argmax_merge(c->bt_all_best, c->tp_size, B, c->bt_idx, s));
   } else {
     CK(launch_rows_argmax_index(c->bt_best, B, c->bt_idx, s, pdl));
@@ -1051,11 +1048,25 @@ int finish_state(vvli_ctx* c) {
   return VVLI_OK;
 }
 
+// Sum (gather = false) or gather (true) of n floats per rank: through the
+// mapped peer blocks when there are any (one kernel, tagged words, sums in
+// rank order), else NCCL.  Every rank makes the same calls in the same order.
+int tp_collective(vvli_ctx* c, const float* src, float* dst, size_t n, bool gather, cudaStream_t s, const char* what) {
+  if (c->xch.block[0] && n <= static_cast<size_t>(c->xch.cap)) {
+    if (++c->xch.epoch == 0) ++c->xch.epoch;
+    CK(launch_tp_exchange(src, static_cast<int>(n), dst, gather ? 1 : 0, c->xch, c->sm_count, s));
+    return VVLI_OK;
+  }
+  return nccl_wait(c,
+                   gather ? nccl().AllGather(src, dst, n, ncclFloat32, c->comm, s)
+                          : nccl().AllReduce(src, dst, n, ncclFloat32, ncclSum, c->comm, s),
+                   what);
+}
+
 int copy_logits(vvli_ctx* c, float* out) {
   if (!out) return VVLI_OK;
   if (c->tp_size > 1) {
-    int st = nccl_wait(c, nccl().AllGather(c->logits, c->logits_full, c->V_l, ncclFloat32, c->comm, c->stream),
-                       "allgather logits");
+    int st = tp_collective(c, c->logits, c->logits_full, c->V_l, true, c->stream, "allgather logits");
     if (st) return st;
     CK(cudaMemcpyAsync(out, c->logits_full, static_cast<size_t>(c->V) * 4, cudaMemcpyDeviceToHost, c->stream));
   } else {
@@ -1319,7 +1330,9 @@ static int setup_tp_peers(vvli_ctx* c) {
   const size_t flag_off = up(recv_off + recv_bytes), flag_bytes = 2ull * tp * grid * 4;
   const size_t best_off = up(flag_off + flag_bytes), best_bytes = 2ull * tp * 4;
   const size_t bflag_off = up(best_off + best_bytes), bflag_bytes = static_cast<size_t>(tp) * 4;
-  const size_t total = up(bflag_off + bflag_bytes);
+  const int xcap = std::max(c->V_l, kSkinnyMaxRows * c->h);
+  const size_t xch_off = up(bflag_off + bflag_bytes), xch_bytes = 2ull * tp * xcap * 8;
+  const size_t total = up(xch_off + xch_bytes);
   CK(cudaMalloc(&c->peer_block, total));
   CK(cudaMemset(c->peer_block, 0, total));
   cudaIpcMemHandle_t mine;
@@ -1351,7 +1364,9 @@ static int setup_tp_peers(vvli_ctx* c) {
     P.peer_flags[q] = reinterpret_cast<unsigned*>(b + flag_off);
     P.peer_best[q] = reinterpret_cast<float*>(b + best_off);
     P.peer_best_flag[q] = reinterpret_cast<unsigned*>(b + bflag_off);
+    c->xch.block[q] = reinterpret_cast<unsigned long long*>(b + xch_off);
   }
+  c->xch.tp = tp, c->xch.rank = c->tp_rank, c->xch.cap = xcap, c->xch.epoch = 0, c->xch.err = &c->st->err;
   return VVLI_OK;
 }
 
@@ -1937,9 +1952,7 @@ int vvli_cuda_sample(vvli_ctx* c, const vvli_sample_options* o, const float* hos
     CK(cudaMemcpyAsync(c->smp_logits, host_logits, static_cast<size_t>(c->V) * 4, cudaMemcpyHostToDevice, c->stream));
     logits = c->smp_logits;
   } else if (c->tp_size > 1) {
-    if ((st = nccl_wait(c, nccl().AllGather(c->logits, c->logits_full, c->V_l, ncclFloat32, c->comm, c->stream),
-                        "allgather logits")))
-      return st;
+    if ((st = tp_collective(c, c->logits, c->logits_full, c->V_l, true, c->stream, "allgather logits"))) return st;
     logits = c->logits_full;
   }
   const uint64_t limit = o->top_k == 0 ? c->V : std::min<uint64_t>(o->top_k, c->V);
