@@ -576,8 +576,8 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
   // the SMs instead: half the B traffic per MMA of 128-wide tiles (8B
   // down_proj on 512 tokens 131.7 -> 109.5 us; o_proj, 64 k-blocks, 45.1 ->
   // 47.5 us, so it keeps the narrow tiles).
-  static const bool sk_disabled = getenv("VVLI_STREAMK") && getenv("VVLI_STREAMK")[0] == '0';
-  const bool narrow = p.epi == GE_RESID && ((p.N + 255) / 256) * mt < 96 && (!p.sk_ws || sk_disabled || p.nk < 128);
+  static const bool sk_off = getenv("VVLI_STREAMK") && getenv("VVLI_STREAMK")[0] == '0';
+  const bool narrow = p.epi == GE_RESID && ((p.N + 255) / 256) * mt < 96 && (!p.sk_ws || sk_off || p.nk < 128);
   static int sms = 0;
   if (!sms) {
     int dev = 0;
@@ -592,7 +592,6 @@ cudaError_t launch_gemm_tc(const CUtensorMap& a_hi, const CUtensorMap& a_lo, con
   // 512 tokens, 448 tiles = 3.03 waves, 195 -> 177 us; fuller waves lose a
   // little to the split parts); at least 4 k-blocks of a tile per CTA keeps
   // the parts few.
-  static const bool sk_off = getenv("VVLI_STREAMK") && getenv("VVLI_STREAMK")[0] == '0';
   if (sk_off) q.sk_ws = nullptr;
   // The grid is a multiple of the row tiles mt (groups of CTAs sharing a weight tile).
   auto grid_of = [&](int tiles) {
