@@ -6,10 +6,13 @@
 //   * 128 x 256 output tile per CTA, 64-element k-blocks (128-byte rows,
 //     128-byte swizzle), 3-stage ring of shared-memory stages;
 //   * warp 0: TMA producer (cp.async.bulk.tensor 2-D, no multicast);
-//     warp 1: allocates 256 TMEM columns, one thread issues
-//     tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32 in TMEM) and
-//     frees stages with tcgen05.commit; warps 2-9: epilogue, tcgen05.ld of
-//     the accumulator (TMEM lane = token row);
+//     warp 1: allocates 2 x 256 TMEM columns (two accumulators), one thread
+//     issues tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32 in
+//     TMEM) and frees stages with tcgen05.commit; warps 2-9: epilogue,
+//     tcgen05.ld of the accumulator (TMEM lane = token row);
+//   * persistent CTAs (one per SM at most); stream-K shares of the last
+//     waves' k-blocks when whole tiles would leave SMs idle (launch_gemm_tc);
+//     a CTA-pair variant (tcgen05.mma.cta_group::2, 256-row tiles) is opt-in;
 //   * activations are fp32 in the reference.  They enter the tensor cores as
 //     two bf16 operands, hi = bf16(a) and lo = bf16(a - hi), and both MMAs
 //     accumulate into the same TMEM tile, so A is represented to about 16
