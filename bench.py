@@ -365,6 +365,50 @@ OP_SHAPES = [(896, 896), (4864, 896), (896, 4864), (151936, 896), (2048, 2048), 
              (14336, 4096), (4096, 14336), (128256, 4096)]
 
 
+def moe_block(hbm, local_rank, reps=20):
+    """The OLMoE sparse block (vvli_cuda_moe_ffn) at the OLMoE-1B-7B shape: h 2048, 64 experts of
+    I 1024, 8 per token, random bf16 weights on the device.  Per call: device time (CUDA events around
+    the call alone) with L2 flushed before it and new token rows each time; algorithmic bytes = the
+    router + the routed experts' gate|up and down rows (each routed expert once) + activations."""
+    import numpy as np
+    import torch
+    from vvli_b200.moe import MoeFfn
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator(device=dev).manual_seed(7)
+    h, inter, E, k = 2048, 1024, 64, 8
+
+    def bf16(*shape, scale, mean=0.0):
+        return (torch.randn(*shape, device=dev, generator=g) * scale + mean).to(torch.bfloat16).view(torch.int16)
+
+    block = MoeFfn(bf16(h, scale=0.1, mean=1.0), bf16(E, h, scale=1.5 / h ** 0.5),
+                   bf16(E, 2 * inter, h, scale=1 / h ** 0.5), bf16(E, h, inter, scale=1 / inter ** 0.5), k,
+                   False, 1e-5, local_rank)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {"config": "olmoe-1b-7b sparse block (h 2048, 64 experts x I 1024, top-8), random bf16 weights",
+           "path": "vvli_cuda_moe_ffn: route, group, grouped expert GEMVs (only routed experts read), combine"}
+    for T in (1, 16):
+        xs = [torch.randn(T, h, device=dev, generator=g) for _ in range(reps + 3)]
+        times, bytes_ = [], []
+        for i, x in enumerate(xs):
+            flush.fill_(i & 255)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            idx, _ = block(x, routing=True)
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= 3:
+                times.append(e0.elapsed_time(e1))
+                n_exp = int(torch.unique(idx).numel())
+                bytes_.append(E * h * 2 + n_exp * 3 * inter * h * 2 + 2 * T * h * 4)
+        ms = float(np.median(times))
+        b = float(np.median(bytes_))
+        out[f"tokens_{T}"] = {"us_per_call": round(ms * 1e3, 2), "tok_per_s": round(T / (ms * 1e-3), 1),
+                              "routed_experts_median": int(round((b - E * h * 2 - 2 * T * h * 4) / (3 * inter * h * 2))),
+                              "roofline": {"bound": "hbm", "bytes_per_call": b, "achieved": b / (ms * 1e-3) / 1e9,
+                                           "peak": hbm, "unit": "GB/s", "frac": b / (ms * 1e-3) / 1e9 / hbm}}
+    return out
+
+
 def op_sweep(vvli_b200, hbm, tpeak, local_rank, reps=20):
     """y = W.x over (N, K) x M, each through the kernel the decoder uses for M rows,
     weight copies rotated past 2x L2.  GB/s for M <= 64 (HBM-bound), TFLOP/s for M = 512."""
@@ -742,6 +786,7 @@ def _main(args, out_fd):
             "llama3.2-1b-4096": prefill_decode_config(vvli_b200, args.seed, hbm, tpeak, tpeak_src, local_rank),
             "op_sweep": op_sweep(vvli_b200, hbm, tpeak, local_rank),
             "llama3-8b-quantized": quantized_decode(vvli_b200, cfg, prompt, args.seed, hbm, local_rank),
+            "olmoe-moe-block": moe_block(hbm, local_rank),
         }
 
     cpu = None

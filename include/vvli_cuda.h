@@ -412,6 +412,49 @@ int vvli_cuda_forward_batch(vvli_ctx* ctx, const uint32_t* tokens, const uint64_
 int vvli_cuda_argmax_rows_static(int device, const float* logits, uint64_t rows, uint64_t n, int32_t* tokens,
                                  void* stream);
 
+/* ---------------------------------------------------------------- mixture of experts
+ * The sparse feed-forward block of OLMoE, which the reference detects and
+ * rejects (src/llm.zig:45-48, 210-214, 261-264; src/main.zig:590-611):
+ *   x[t] += sum over the top_k experts e of softmax(router . xn)[e] *
+ *           down_e . (silu(gate_e . xn) * (up_e . xn)),  xn = rmsnorm(x[t]) * norm_w
+ * for every token row t, with the experts chosen by router probability
+ * (larger first, lower index on ties) and their weights divided by their
+ * sum when norm_topk_prob is set (the OLMoE block of transformers 5.5.0).
+ * The experts' contributions are added in ascending expert index, so the
+ * result does not depend on timing.  Only the routed experts' weights are
+ * read.  All pointers are device memory of `device`; weights are bf16.
+ * Needs no context; allocates nothing: the caller passes a workspace of
+ * vvli_cuda_moe_workspace_bytes(...) bytes.  Limits: tokens <= 4096,
+ * hidden and inter multiples of 8 up to 8192, experts <= 1024,
+ * top_k <= min(experts, 32); x, router, gate_up and down 16-byte aligned,
+ * the workspace 256-byte aligned.  Other sizes or pointers return
+ * VVLI_ERR_INVALID_ARGUMENT with the reason in vvli_cuda_last_error().
+ * The work is queued on `stream` (a cudaStream_t; NULL = the legacy default
+ * stream); the caller's current device is restored before returning. */
+typedef struct vvli_moe_args {
+  uint64_t tokens;          /* rows of x */
+  uint64_t hidden;          /* h */
+  uint64_t inter;           /* I, one expert's intermediate size */
+  uint64_t experts;         /* E */
+  uint64_t top_k;           /* experts per token */
+  int32_t norm_topk_prob;   /* 1: the chosen weights are divided by their sum (OLMoE: 0) */
+  float rms_eps;
+  float* x;                 /* [tokens][h] f32 residual rows, updated in place */
+  const uint16_t* norm_w;   /* [h] the post-attention RMSNorm weight */
+  const uint16_t* router;   /* [E][h] */
+  const uint16_t* gate_up;  /* [E][2 I][h]: the I gate rows, then the I up rows */
+  const uint16_t* down;     /* [E][h][I] */
+  void* workspace;
+  uint64_t workspace_bytes;
+  int32_t* topk_index;      /* optional [tokens][top_k] out: chosen experts, larger weight first */
+  float* topk_weight;       /* optional [tokens][top_k] out: their weights */
+} vvli_moe_args;
+
+/* Workspace bytes vvli_cuda_moe_ffn needs for these sizes; 0 if it does not take them. */
+uint64_t vvli_cuda_moe_workspace_bytes(uint64_t tokens, uint64_t hidden, uint64_t inter, uint64_t experts,
+                                       uint64_t top_k);
+int vvli_cuda_moe_ffn(int device, const vvli_moe_args* args, void* stream);
+
 /* Device-side timing of the last forward in milliseconds (CUDA events). */
 int vvli_cuda_last_forward_ms(vvli_ctx* ctx, float* out_ms);
 

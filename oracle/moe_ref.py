@@ -79,15 +79,14 @@ def moe_block(x, norm_w, router, gate_up, down, top_k: int, norm_topk_prob: bool
     xn = x / np.sqrt((x * x).mean(axis=1, keepdims=True) + eps) * nw
     _, idx, w = route(xn, bf16_float(router).astype(np.float64), top_k, norm_topk_prob)
     y = np.zeros_like(x)
-    cache = {}
-    for t in range(T):
-        for j in np.argsort(idx[t], kind="stable"):  # ascending expert index
-            e = int(idx[t, j])
-            if e not in cache:
-                cache[e] = (bf16_float(gate_up[e]).astype(np.float64), bf16_float(down[e]).astype(np.float64))
-            gu, dn = cache[e]
-            a = gu @ xn[t]
-            g, u = a[:inter], a[inter:]
-            f = g / (1.0 + np.exp(-g)) * u
-            y[t] += w[t, j] * (dn @ f)
+    # experts in ascending index, each once; a token's contributions are
+    # therefore added in ascending expert index
+    for e in np.unique(idx):
+        rows, slots = np.nonzero(idx == e)
+        gu = bf16_float(gate_up[e]).astype(np.float64)
+        dn = bf16_float(down[e]).astype(np.float64)
+        a = xn[rows] @ gu.T
+        g, u = a[:, :inter], a[:, inter:]
+        f = g / (1.0 + np.exp(-g)) * u
+        y[rows] += w[rows, slots][:, None] * (f @ dn.T)
     return x + y, idx, w

@@ -44,6 +44,28 @@ class CSampleOptions(ctypes.Structure):
     ]
 
 
+class CMoeArgs(ctypes.Structure):
+    """vvli_moe_args (include/vvli_cuda.h)."""
+    _fields_ = [
+        ("tokens", ctypes.c_uint64),
+        ("hidden", ctypes.c_uint64),
+        ("inter", ctypes.c_uint64),
+        ("experts", ctypes.c_uint64),
+        ("top_k", ctypes.c_uint64),
+        ("norm_topk_prob", ctypes.c_int32),
+        ("rms_eps", ctypes.c_float),
+        ("x", ctypes.c_void_p),
+        ("norm_w", ctypes.c_void_p),
+        ("router", ctypes.c_void_p),
+        ("gate_up", ctypes.c_void_p),
+        ("down", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_uint64),
+        ("topk_index", ctypes.c_void_p),
+        ("topk_weight", ctypes.c_void_p),
+    ]
+
+
 # name -> (restype, argtypes); every function declared in include/vvli_cuda.h.
 SIGNATURES = {
     "vvli_cuda_strerror": (ctypes.c_char_p, [ctypes.c_int]),
@@ -83,6 +105,8 @@ SIGNATURES = {
     "vvli_cuda_load_gguf": (ctypes.c_int, [_ctx, ctypes.c_char_p]),
     "vvli_cuda_set_debug": (ctypes.c_int, [_ctx, ctypes.c_int]),
     "vvli_cuda_debug_hidden": (ctypes.c_int, [_ctx, ctypes.c_int, _f32p]),
+    "vvli_cuda_moe_workspace_bytes": (ctypes.c_uint64, [ctypes.c_uint64] * 5),
+    "vvli_cuda_moe_ffn": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(CMoeArgs), ctypes.c_void_p]),
     "vvli_cuda_last_forward_ms": (ctypes.c_int, [_ctx, _f32p]),
     "vvli_cuda_destroy": (ctypes.c_int, [_ctx]),
 }
