@@ -18,9 +18,9 @@ def test_workspace_bytes():
     lib = _abi.lib()
     T, h, inter, E, k = 16, 2048, 1024, 64, 8
     n = lib.vvli_cuda_moe_workspace_bytes(T, h, inter, E, k)
-    # normed rows + the pairs' silu*up rows + the pairs' down rows dominate
+    # normed rows, router logits, the pairs' silu*up rows and down rows dominate
     assert n >= 4 * (T * h + T * k * inter + T * k * h) and n % 256 == 0
-    assert n < 4 * (T * h + T * k * inter + T * k * h) + 16 * 256 + 4 * (3 * E + 4 * T * k)
+    assert n < 4 * (T * h + T * E + T * k * inter + T * k * h) + 16 * 256 + 4 * (3 * E + 4 * T * k)
     for bad in ((0, h, inter, E, k), (4097, h, inter, E, k), (T, 12, inter, E, k), (T, h, 8200, E, k),
                 (T, h, inter, 0, k), (T, h, inter, 1025, k), (T, h, inter, 8, 9), (T, h, inter, 64, 33),
                 (T, h, inter, E, 0)):

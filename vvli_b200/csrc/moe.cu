@@ -8,30 +8,34 @@
 // 5.5.0, models/olmoe/modeling_olmoe.py: OlmoeTopKRouter, OlmoeExperts),
 // restated in oracle/moe_ref.py.
 //
-// Four launches on the caller's stream, all HBM-bound on the expert weights:
-//   1. moe_route_kernel, one CTA per token: RMSNorm into the workspace, the
-//      router's E dot products (a warp per expert), softmax and the top-k
-//      experts (larger probability first, lower index on ties), their
-//      weights (renormalised when norm_topk_prob).
-//   2. moe_group_kernel, one CTA: the (token, slot) pairs grouped by expert
-//      in token order, the experts' counts and offsets, and the list of the
-//      experts that got a token, in ascending order.
+// Five launches on the caller's stream, HBM-bound on the expert weights:
+//   1. moe_logits_kernel, CTA = (8 experts, token): RMSNorm of the row in
+//      shared memory (written to the workspace once), a warp per router
+//      logit.
+//   2. moe_group_kernel, one CTA: softmax and top-k of every token (a warp
+//      per token; larger probability first, lower index on ties; weights
+//      renormalised when norm_topk_prob), then the (token, slot) pairs
+//      grouped by expert in token order, the experts' counts and offsets,
+//      and the list of the routed experts in ascending order.
 //   3. moe_expert_kernel<true>: gate|up rows of every routed expert times its
 //      tokens' normed rows, silu(gate) * up per pair; then
-//      moe_expert_kernel<false>: the down rows times those.  CTA = (row
-//      tile, slot in the routed-expert list): CTAs past the list's length
-//      return at once, so only the routed experts' weights are read.  A
-//      warp streams 8 weight rows with 16-byte loads and multiplies them
-//      with up to 4 tokens staged in shared memory; an expert with more
-//      tokens is taken 4 at a time (its tile comes back from L2).
-//   4. moe_combine_kernel, one CTA per token: x += sum of w_e * down_e(...)
+//      4. moe_expert_kernel<false>: the down rows times those.  Persistent
+//      grids (the CTAs resident at once) walk the (routed expert, row tile)
+//      items, so only the routed experts' weights are read and no CTA is
+//      spent on an expert without tokens.  A warp streams 8 weight rows
+//      with 16-byte loads, two steps in flight, and multiplies them with up
+//      to 4 tokens staged in shared memory; an expert with more tokens is
+//      taken 4 at a time (its tile comes back from L2).
+//   5. moe_combine_kernel, one CTA per token: x += sum of w_e * down_e(...)
 //      over the token's experts in ascending expert index (the order of the
 //      OLMoE experts loop), so the result does not depend on timing.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <climits>
 #include <cmath>
+#include <mutex>
 #include <string>
 
 #include "../../include/vvli_cuda.h"
@@ -65,6 +69,7 @@ struct MoeDev {
   const uint16_t* down;
   // workspace
   float* xn;        // [T][h]
+  float* logits;    // [T][E] router logits (then the group kernel's scratch)
   int* topk_idx;    // [T][k]
   float* topk_w;    // [T][k]
   int* cnt;         // [E]
@@ -81,7 +86,7 @@ struct MoeDev {
 };
 
 struct WsLayout {
-  size_t xn, idx, w, cnt, off, act, nact, pair_tok, slot_q, f, yd, total;
+  size_t xn, logits, idx, w, cnt, off, act, nact, pair_tok, slot_q, f, yd, total;
 };
 
 size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
@@ -95,6 +100,7 @@ WsLayout ws_layout(uint64_t T, uint64_t h, uint64_t I, uint64_t E, uint64_t k) {
     return at;
   };
   L.xn = take(T * h * 4);
+  L.logits = take(T * E * 4);
   L.idx = take(T * k * 4);
   L.w = take(T * k * 4);
   L.cnt = take(E * 4);
@@ -122,15 +128,23 @@ VVLI_DEV float dot8(const uint4& w, const float4& a, const float4& b, float acc)
   return acc;
 }
 
-// 1. RMSNorm, router, softmax, top-k (OlmoeTopKRouter.forward).
-__global__ void __launch_bounds__(kThreads) moe_route_kernel(const MoeDev p) {
-  extern __shared__ float sh[];  // xn [h], router logits / exponentials [E]
-  float* xs = sh;
-  float* lg = sh + p.h;
+// Streaming 16-byte load of read-only weights that the compiler may schedule
+// freely (no volatile): the loads of one chunk go out together.
+VVLI_DEV uint4 ld_weights(const void* p) {
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
+  return r;
+}
+
+// 1. RMSNorm and the router logits (OlmoeTopKRouter.forward, first half).
+//    CTA = (8 experts, token): the row is normalised in shared memory (the
+//    CTA of experts 0-7 also writes it to xn), then a warp per expert.
+__global__ void __launch_bounds__(kThreads) moe_logits_kernel(const MoeDev p) {
+  extern __shared__ float xs[];  // xn [h]
   __shared__ float red[kWarps];
-  __shared__ int sel_i[kMaxTopK];
-  __shared__ float sel_v[kMaxTopK];
-  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* xr = p.x + static_cast<size_t>(t) * p.h;
   float ss = 0.f;
   for (int i = tid; i < p.h; i += kThreads) {
@@ -150,70 +164,68 @@ __global__ void __launch_bounds__(kThreads) moe_route_kernel(const MoeDev p) {
   for (int i = tid; i < p.h; i += kThreads) {
     const float v = xs[i] * scale * bf16_to_f32(p.norm_w[i]);
     xs[i] = v;
-    xo[i] = v;
+    if (blockIdx.x == 0) xo[i] = v;
   }
   __syncthreads();
-  // router logits, a warp per expert (h % 8 == 0: 16-byte rows)
-  for (int e = warp; e < p.E; e += kWarps) {
-    const uint16_t* wr = p.router + static_cast<size_t>(e) * p.h;
-    float a = 0.f;
-    for (int k0 = lane * 8; k0 < p.h; k0 += 256) {
-      const uint4 u = ld_stream(wr + k0);
-      a = dot8(u, *reinterpret_cast<const float4*>(xs + k0), *reinterpret_cast<const float4*>(xs + k0 + 4), a);
+  const int e = blockIdx.x * kWarps + warp;
+  if (e >= p.E) return;
+  const uint16_t* wr = p.router + static_cast<size_t>(e) * p.h;  // h % 8 == 0: 16-byte rows
+  float a = 0.f;
+#pragma unroll 8
+  for (int k0 = lane * 8; k0 < p.h; k0 += 256)
+    a = dot8(ld_weights(wr + k0), *reinterpret_cast<const float4*>(xs + k0),
+             *reinterpret_cast<const float4*>(xs + k0 + 4), a);
+  a = warp_sum(a);
+  if (lane == 0) p.logits[static_cast<size_t>(t) * p.E + e] = a;
+}
+
+// 2. Softmax and top-k of every token (OlmoeTopKRouter.forward, second
+//    half; a warp per token), then the pairs grouped by expert (token order
+//    inside an expert), the experts' counts and offsets and the list of the
+//    routed experts in ascending order.  One CTA.
+__global__ void __launch_bounds__(1024) moe_group_kernel(const MoeDev p) {
+  __shared__ int cnt_s[kMaxExperts], off_s[kMaxExperts];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  for (int t = warp; t < p.T; t += nw) {
+    float* lg = p.logits + static_cast<size_t>(t) * p.E;  // this warp's row, reused as scratch
+    float m = -INFINITY;
+    for (int e = lane; e < p.E; e += 32) m = fmaxf(m, lg[e]);
+    m = warp_max(m);
+    float s = 0.f;
+    for (int e = lane; e < p.E; e += 32) {
+      const float v = expf(lg[e] - m);
+      lg[e] = v;
+      s += v;
     }
-    a = warp_sum(a);
-    if (lane == 0) lg[e] = a;
-  }
-  __syncthreads();
-  if (warp != 0) return;
-  // softmax over all experts, then k rounds of a warp argmax
-  float m = -INFINITY;
-  for (int e = lane; e < p.E; e += 32) m = fmaxf(m, lg[e]);
-  m = warp_max(m);
-  float s = 0.f;
-  for (int e = lane; e < p.E; e += 32) {
-    const float v = expf(lg[e] - m);
-    lg[e] = v;
-    s += v;
-  }
-  s = warp_sum(s);
-  __syncwarp();
-  for (int j = 0; j < p.k; ++j) {
-    float bv = -1.f;
-    int bi = INT_MAX;
-    for (int e = lane; e < p.E; e += 32)
-      if (better(lg[e], e, bv, bi)) bv = lg[e], bi = e;
-    warp_argmax(bv, bi);
-    if (lane == 0) {
-      if (bi >= p.E) bi = 0, bv = 0.f;  // NaN logits leave no candidate: keep the index in range
-      sel_i[j] = bi;
-      sel_v[j] = bv / s;
-      lg[bi] = -2.f;  // below every probability: not chosen again
-    }
+    s = warp_sum(s);
     __syncwarp();
-  }
-  if (lane == 0) {
-    float norm = 1.f;
-    if (p.norm_topk) {
-      float sum = 0.f;
-      for (int j = 0; j < p.k; ++j) sum += sel_v[j];
-      norm = sum;
-    }
+    float sel_v = 0.f, sum = 0.f;  // lane j keeps slot j
+    int sel_i = 0;
     for (int j = 0; j < p.k; ++j) {
-      const float w = p.norm_topk ? sel_v[j] / norm : sel_v[j];
-      const size_t at = static_cast<size_t>(t) * p.k + j;
-      p.topk_idx[at] = sel_i[j];
+      float bv = -1.f;
+      int bi = INT_MAX;
+      for (int e = lane; e < p.E; e += 32)
+        if (better(lg[e], e, bv, bi)) bv = lg[e], bi = e;
+      warp_argmax(bv, bi);
+      if (bi >= p.E) bi = 0, bv = 0.f;  // NaN logits leave no candidate: keep the index in range
+      const float pv = bv / s;
+      if (lane == j) sel_v = pv, sel_i = bi;
+      sum += pv;  // slot order, larger first
+      __syncwarp();
+      if (lane == 0) lg[bi] = -2.f;  // below every probability: not chosen again
+      __syncwarp();
+    }
+    if (lane < p.k) {
+      const float w = p.norm_topk ? sel_v / sum : sel_v;
+      const size_t at = static_cast<size_t>(t) * p.k + lane;
+      p.topk_idx[at] = sel_i;
       p.topk_w[at] = w;
-      if (p.out_idx) p.out_idx[at] = sel_i[j];
+      if (p.out_idx) p.out_idx[at] = sel_i;
       if (p.out_w) p.out_w[at] = w;
     }
   }
-}
-
-// 2. Pairs grouped by expert (token order inside an expert), one CTA.
-__global__ void __launch_bounds__(1024) moe_group_kernel(const MoeDev p) {
-  __shared__ int cnt_s[kMaxExperts], off_s[kMaxExperts];
-  const int n = p.T * p.k, tid = threadIdx.x;
+  __syncthreads();
+  const int n = p.T * p.k;
   for (int e = tid; e < p.E; e += blockDim.x) {
     int c = 0;
     for (int i = 0; i < n; ++i) c += p.topk_idx[i] == e;
@@ -243,88 +255,100 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const MoeDev p) {
   }
 }
 
-// 3. One weight tile of one routed expert times its tokens (OlmoeExperts.forward).
+// 3. Weight tiles of the routed experts times their tokens (OlmoeExperts.forward).
 //    GATEUP: rows r of gate and up (4 output rows per warp: 8 weight rows),
 //            f[q][r] = silu(gate_r . xn) * (up_r . xn);
 //    else:   rows r of down (8 per warp), yd[q][r] = down_r . f[q].
+//    Persistent: CTA b takes items b, b + grid, ... of the list (routed
+//    expert slot, row tile), slot-major, until the slot passes n_act.
 template <bool GATEUP>
 __global__ void __launch_bounds__(kThreads) moe_expert_kernel(const MoeDev p) {
   extern __shared__ float xs[];  // [kTG][kKC]
-  const int slot = blockIdx.y;
-  if (slot >= *p.n_act) return;  // uniform over the CTA
-  const int e = p.act[slot];
-  const int cnt = p.cnt[e], q0 = p.off[e];
   const int K = GATEUP ? p.h : p.I;
-  const int R = GATEUP ? p.I : p.h;  // output rows of the expert
+  const int R = GATEUP ? p.I : p.h;  // output rows of an expert
   constexpr int kOut = GATEUP ? kRowsPerWarp / 2 : kRowsPerWarp;
+  constexpr int kTileRows = kWarps * kOut;
+  const int tiles = (R + kTileRows - 1) / kTileRows;
+  const int n_act = *p.n_act;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int r_base = (blockIdx.x * kWarps + warp) * kOut;
-  const uint16_t* W = GATEUP ? p.gate_up + static_cast<size_t>(e) * 2 * p.I * p.h
-                             : p.down + static_cast<size_t>(e) * p.h * p.I;
-  const uint16_t* rows[kRowsPerWarp];
-  bool live[kRowsPerWarp];
+  for (int item = blockIdx.x;; item += gridDim.x) {
+    const int slot = item / tiles;
+    if (slot >= n_act) break;  // uniform over the CTA
+    const int e = p.act[slot];
+    const int cnt = p.cnt[e], q0 = p.off[e];
+    const int r_base = ((item - slot * tiles) * kWarps + warp) * kOut;
+    const uint16_t* W = GATEUP ? p.gate_up + static_cast<size_t>(e) * 2 * p.I * p.h
+                               : p.down + static_cast<size_t>(e) * p.h * p.I;
+    const uint16_t* rows[kRowsPerWarp];
+    bool live[kRowsPerWarp];
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int out = r_base + (GATEUP ? (i % kOut) : i);
-    live[i] = out < R;
-    const int wrow = GATEUP ? (i < kOut ? out : p.I + out) : out;  // gate rows, then the matching up rows
-    rows[i] = W + static_cast<size_t>(live[i] ? wrow : 0) * K;
-  }
-  for (int g0 = 0; g0 < cnt; g0 += kTG) {
-    const int ng = min(kTG, cnt - g0);
-    float acc[kRowsPerWarp][kTG];
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const int out = r_base + (GATEUP ? (i % kOut) : i);
+      live[i] = out < R;
+      const int wrow = GATEUP ? (i < kOut ? out : p.I + out) : out;  // gate rows, then the matching up rows
+      rows[i] = W + static_cast<size_t>(live[i] ? wrow : 0) * K;
+    }
+    for (int g0 = 0; g0 < cnt; g0 += kTG) {
+      const int ng = min(kTG, cnt - g0);
+      float acc[kRowsPerWarp][kTG];
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i)
+      for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
-      for (int u = 0; u < kTG; ++u) acc[i][u] = 0.f;
-    for (int c0 = 0; c0 < K; c0 += kKC) {
-      const int kc = min(kKC, K - c0);
-      __syncthreads();  // the previous chunk's readers are done
-      for (int idx = tid; idx < kTG * kc; idx += kThreads) {
-        const int u = idx / kc, kk = idx - u * kc;
-        float v = 0.f;
-        if (u < ng) {
+        for (int u = 0; u < kTG; ++u) acc[i][u] = 0.f;
+      for (int c0 = 0; c0 < K; c0 += kKC) {
+        const int kc = min(kKC, K - c0);
+        // the chunk's first weights go out before the activations are staged
+        uint4 cur[kRowsPerWarp];
+#pragma unroll
+        for (int i = 0; i < kRowsPerWarp; ++i)
+          cur[i] = (live[i] && lane * 8 < kc) ? ld_weights(rows[i] + c0 + lane * 8) : make_uint4(0, 0, 0, 0);
+        __syncthreads();  // the previous chunk's readers are done
+        for (int idx = tid; idx < ng * kc; idx += kThreads) {
+          const int u = idx / kc, kk = idx - u * kc;
           const int q = q0 + g0 + u;
           const float* src = GATEUP ? p.xn + static_cast<size_t>(p.pair_tok[q]) * K : p.f + static_cast<size_t>(q) * K;
-          v = src[c0 + kk];
+          xs[u * kKC + kk] = src[c0 + kk];
         }
-        xs[u * kKC + kk] = v;
-      }
-      __syncthreads();
-#pragma unroll 2
-      for (int k0 = lane * 8; k0 < kc; k0 += 256) {
-        uint4 wv[kRowsPerWarp];
+        __syncthreads();
+        for (int k0 = lane * 8; k0 < kc; k0 += 256) {
+          // two steps of weights in flight: the next step's loads before this step's math
+          uint4 nxt[kRowsPerWarp];
+          const bool more = k0 + 256 < kc;
 #pragma unroll
-        for (int i = 0; i < kRowsPerWarp; ++i) wv[i] = live[i] ? ld_stream(rows[i] + c0 + k0) : make_uint4(0, 0, 0, 0);
+          for (int i = 0; i < kRowsPerWarp; ++i)
+            nxt[i] = (live[i] && more) ? ld_weights(rows[i] + c0 + k0 + 256) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int u = 0; u < kTG; ++u) {
+            if (u < ng) {
+              const float4 a = *reinterpret_cast<const float4*>(xs + u * kKC + k0);
+              const float4 b = *reinterpret_cast<const float4*>(xs + u * kKC + k0 + 4);
+#pragma unroll
+              for (int i = 0; i < kRowsPerWarp; ++i) acc[i][u] = dot8(cur[i], a, b, acc[i][u]);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < kRowsPerWarp; ++i) cur[i] = nxt[i];
+        }
+      }
+      // every lane gets the sums; lane (i, u) stores one of them
+#pragma unroll
+      for (int i = 0; i < kOut; ++i) {
 #pragma unroll
         for (int u = 0; u < kTG; ++u) {
-          if (u < ng) {
-            const float4 a = *reinterpret_cast<const float4*>(xs + u * kKC + k0);
-            const float4 b = *reinterpret_cast<const float4*>(xs + u * kKC + k0 + 4);
-#pragma unroll
-            for (int i = 0; i < kRowsPerWarp; ++i) acc[i][u] = dot8(wv[i], a, b, acc[i][u]);
+          const float s0 = warp_sum(acc[i][u]);
+          float val = s0;
+          if constexpr (GATEUP) {
+            const float up = warp_sum(acc[kOut + i][u]);
+            val = (s0 / (1.0f + expf(-s0))) * up;  // silu(gate) * up
           }
-        }
-      }
-    }
-    // every lane gets the sums; lane (i, u) stores one of them
-#pragma unroll
-    for (int i = 0; i < kOut; ++i) {
-#pragma unroll
-      for (int u = 0; u < kTG; ++u) {
-        const float s0 = warp_sum(acc[i][u]);
-        float val = s0;
-        if constexpr (GATEUP) {
-          const float up = warp_sum(acc[kOut + i][u]);
-          val = (s0 / (1.0f + expf(-s0))) * up;  // silu(gate) * up
-        }
-        const int out = r_base + i;
-        if (lane == i * kTG + u && u < ng && out < R) {
-          const size_t q = static_cast<size_t>(q0 + g0 + u);
-          if constexpr (GATEUP)
-            p.f[q * p.I + out] = val;
-          else
-            p.yd[q * p.h + out] = val;
+          const int out = r_base + i;
+          if (lane == i * kTG + u && u < ng && out < R) {
+            const size_t q = static_cast<size_t>(q0 + g0 + u);
+            if constexpr (GATEUP)
+              p.f[q * p.I + out] = val;
+            else
+              p.yd[q * p.h + out] = val;
+          }
         }
       }
     }
@@ -378,6 +402,29 @@ std::string check_sizes(uint64_t T, uint64_t h, uint64_t I, uint64_t E, uint64_t
   return "";
 }
 
+// CTAs of each expert kernel resident at once on `device` (SMs x blocks per
+// SM), looked up once per device.
+cudaError_t expert_residency(int device, int* out) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static int cached[kMaxDevices][2] = {};
+  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cached[device][0]) {
+    int sms = 0, b0 = 0, b1 = 0;
+    const size_t smem = static_cast<size_t>(kTG) * kKC * sizeof(float);
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b0, moe_expert_kernel<true>, kThreads, smem);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b1, moe_expert_kernel<false>, kThreads, smem);
+    if (e != cudaSuccess) return e;
+    cached[device][0] = std::max(1, sms * b0);
+    cached[device][1] = std::max(1, sms * b1);
+  }
+  out[0] = cached[device][0];
+  out[1] = cached[device][1];
+  return cudaSuccess;
+}
+
 struct DeviceGuard {
   int prev = -1;
   ~DeviceGuard() {
@@ -420,6 +467,7 @@ extern "C" int vvli_cuda_moe_ffn(int device, const vvli_moe_args* a, void* strea
   p.x = a->x, p.norm_w = a->norm_w, p.router = a->router, p.gate_up = a->gate_up, p.down = a->down;
   char* ws = static_cast<char*>(a->workspace);
   p.xn = reinterpret_cast<float*>(ws + L.xn);
+  p.logits = reinterpret_cast<float*>(ws + L.logits);
   p.topk_idx = reinterpret_cast<int*>(ws + L.idx);
   p.topk_w = reinterpret_cast<float*>(ws + L.w);
   p.cnt = reinterpret_cast<int*>(ws + L.cnt);
@@ -433,14 +481,18 @@ extern "C" int vvli_cuda_moe_ffn(int device, const vvli_moe_args* a, void* strea
   p.out_idx = a->topk_index, p.out_w = a->topk_weight;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t route_smem = static_cast<size_t>(p.h + p.E) * sizeof(float);  // <= 36 KB
+  int resident[2];
+  if ((e = expert_residency(device, resident)) != cudaSuccess)
+    return fail(VVLI_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
+  const size_t logits_smem = static_cast<size_t>(p.h) * sizeof(float);       // <= 32 KB
   const size_t expert_smem = static_cast<size_t>(kTG) * kKC * sizeof(float);  // 32 KB
-  moe_route_kernel<<<p.T, kThreads, route_smem, s>>>(p);
+  moe_logits_kernel<<<dim3((p.E + kWarps - 1) / kWarps, p.T), kThreads, logits_smem, s>>>(p);
   moe_group_kernel<<<1, 1024, 0, s>>>(p);
-  const unsigned gu_tiles = static_cast<unsigned>((p.I + kWarps * kRowsPerWarp / 2 - 1) / (kWarps * kRowsPerWarp / 2));
-  const unsigned dn_tiles = static_cast<unsigned>((p.h + kWarps * kRowsPerWarp - 1) / (kWarps * kRowsPerWarp));
-  moe_expert_kernel<true><<<dim3(gu_tiles, p.E), kThreads, expert_smem, s>>>(p);
-  moe_expert_kernel<false><<<dim3(dn_tiles, p.E), kThreads, expert_smem, s>>>(p);
+  // persistent grids: no more CTAs than are resident at once, nor than (expert, tile) items
+  const long gu_items = static_cast<long>(p.E) * ((p.I + kWarps * kRowsPerWarp / 2 - 1) / (kWarps * kRowsPerWarp / 2));
+  const long dn_items = static_cast<long>(p.E) * ((p.h + kWarps * kRowsPerWarp - 1) / (kWarps * kRowsPerWarp));
+  moe_expert_kernel<true><<<static_cast<unsigned>(std::min<long>(gu_items, resident[0])), kThreads, expert_smem, s>>>(p);
+  moe_expert_kernel<false><<<static_cast<unsigned>(std::min<long>(dn_items, resident[1])), kThreads, expert_smem, s>>>(p);
   moe_combine_kernel<<<p.T, kThreads, 0, s>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(VVLI_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
