@@ -66,7 +66,7 @@ def test_olmoe_1b_7b_shape(torch, olmoe_inputs, T):
 def test_many_tokens_per_expert_and_ties(torch):
     # a zero router gives every expert the same probability: every token takes
     # experts 0..k-1 (lower index first), so each of them serves all 37 tokens
-    # (ten passes of four tokens over its weight tiles)
+    # (thirteen passes of at most three tokens over its weight tiles)
     inp = make_inputs(31, 37, 512, 256, 16)
     inp["router"] = np.zeros_like(inp["router"])
     want, widx, ww = moe_block(inp["x"], inp["norm_w"], inp["router"], inp["gate_up"], inp["down"], 6, True, 1e-5)

@@ -15,8 +15,9 @@
 //   2. moe_group_kernel, one CTA: softmax and top-k of every token (a warp
 //      per token; larger probability first, lower index on ties; weights
 //      renormalised when norm_topk_prob), then the (token, slot) pairs
-//      grouped by expert in token order, the experts' counts and offsets,
-//      and the list of the routed experts in ascending order.
+//      grouped by expert in token order (warp ballots), the experts'
+//      counts and offsets, the list of the routed experts in ascending
+//      order, and each token's pairs sorted by expert index.
 //   3. moe_expert_kernel<true>: gate|up rows of every routed expert times its
 //      tokens' normed rows, silu(gate) * up per pair; then
 //      4. moe_expert_kernel<false>: the down rows times those.  Persistent
@@ -24,8 +25,10 @@
 //      items, so only the routed experts' weights are read and no CTA is
 //      spent on an expert without tokens.  A warp streams 8 weight rows
 //      with 16-byte loads, two steps in flight, and multiplies them with up
-//      to 4 tokens staged in shared memory; an expert with more tokens is
-//      taken 4 at a time (its tile comes back from L2).
+//      to 3 tokens staged in shared memory (the token count of a pass is a
+//      template parameter; each weight is unpacked once per step); an
+//      expert with more tokens is taken 3 at a time (its tile comes back
+//      from L2).
 //   5. moe_combine_kernel, one CTA per token: x += sum of w_e * down_e(...)
 //      over the token's experts in ascending expert index (the order of the
 //      OLMoE experts loop), so the result does not depend on timing.
@@ -55,7 +58,7 @@ constexpr int kMaxTokens = 4096;
 constexpr int kMaxDim = 8192;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 32;
-constexpr int kTG = 4;           // tokens multiplied per pass over a weight tile
+constexpr int kTG = 3;           // tokens multiplied per pass over a weight tile
 constexpr int kKC = 2048;        // activation elements staged per chunk
 constexpr int kRowsPerWarp = 8;  // weight rows a warp streams together
 
@@ -77,7 +80,9 @@ struct MoeDev {
   int* act;         // [E] routed experts, ascending
   int* n_act;       // [1]
   int* pair_tok;    // [T*k] token of pair q (pairs grouped by expert)
-  int* slot_q;      // [T*k] pair of (token, slot)
+  int* tok_rank;    // [T*k] rank of (token, slot) among the token's experts by index
+  int* tok_q;       // [T][k] the token's pairs, ascending expert index
+  float* tok_w;     // [T][k] their weights
   float* f;         // [T*k][I] silu(gate) * up
   float* yd;        // [T*k][h] down rows . f
   // optional outputs
@@ -86,7 +91,7 @@ struct MoeDev {
 };
 
 struct WsLayout {
-  size_t xn, logits, idx, w, cnt, off, act, nact, pair_tok, slot_q, f, yd, total;
+  size_t xn, logits, idx, w, cnt, off, act, nact, pair_tok, tok_rank, tok_q, tok_w, f, yd, total;
 };
 
 size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
@@ -108,7 +113,9 @@ WsLayout ws_layout(uint64_t T, uint64_t h, uint64_t I, uint64_t E, uint64_t k) {
   L.act = take(E * 4);
   L.nact = take(4);
   L.pair_tok = take(T * k * 4);
-  L.slot_q = take(T * k * 4);
+  L.tok_rank = take(T * k * 4);
+  L.tok_q = take(T * k * 4);
+  L.tok_w = take(T * k * 4);
   L.f = take(T * k * I * 4);
   L.yd = take(T * k * h * 4);
   L.total = o;
@@ -180,78 +187,130 @@ __global__ void __launch_bounds__(kThreads) moe_logits_kernel(const MoeDev p) {
 }
 
 // 2. Softmax and top-k of every token (OlmoeTopKRouter.forward, second
-//    half; a warp per token), then the pairs grouped by expert (token order
-//    inside an expert), the experts' counts and offsets and the list of the
-//    routed experts in ascending order.  One CTA.
+//    half; a warp per token, its router row in registers), then the pairs
+//    grouped by expert in token order (warp ballots), the experts' counts
+//    and offsets, the list of the routed experts in ascending order, and per
+//    token its pairs sorted by expert index for the combine.  One CTA.
 __global__ void __launch_bounds__(1024) moe_group_kernel(const MoeDev p) {
-  __shared__ int cnt_s[kMaxExperts], off_s[kMaxExperts];
+  constexpr int kPerLane = kMaxExperts / 32;
+  __shared__ int cnt_s[kMaxExperts], off_s[kMaxExperts], act_s[kMaxExperts];
+  __shared__ int wsum[32], wact[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const unsigned lt = (1u << lane) - 1u;
   for (int t = warp; t < p.T; t += nw) {
-    float* lg = p.logits + static_cast<size_t>(t) * p.E;  // this warp's row, reused as scratch
+    const float* lg = p.logits + static_cast<size_t>(t) * p.E;
+    float v[kPerLane];  // expert lane + 32 c
     float m = -INFINITY;
-    for (int e = lane; e < p.E; e += 32) m = fmaxf(m, lg[e]);
+#pragma unroll
+    for (int c = 0; c < kPerLane; ++c) {
+      const int e = lane + 32 * c;
+      v[c] = e < p.E ? lg[e] : -INFINITY;
+      m = fmaxf(m, v[c]);
+    }
     m = warp_max(m);
     float s = 0.f;
-    for (int e = lane; e < p.E; e += 32) {
-      const float v = expf(lg[e] - m);
-      lg[e] = v;
-      s += v;
+#pragma unroll
+    for (int c = 0; c < kPerLane; ++c) {
+      const int e = lane + 32 * c;
+      v[c] = e < p.E ? expf(v[c] - m) : -2.f;  // -2: never a candidate
+      if (e < p.E) s += v[c];
     }
     s = warp_sum(s);
-    __syncwarp();
     float sel_v = 0.f, sum = 0.f;  // lane j keeps slot j
-    int sel_i = 0;
+    int sel_i = INT_MAX;
     for (int j = 0; j < p.k; ++j) {
       float bv = -1.f;
       int bi = INT_MAX;
-      for (int e = lane; e < p.E; e += 32)
-        if (better(lg[e], e, bv, bi)) bv = lg[e], bi = e;
+#pragma unroll
+      for (int c = 0; c < kPerLane; ++c)
+        if (better(v[c], lane + 32 * c, bv, bi)) bv = v[c], bi = lane + 32 * c;
       warp_argmax(bv, bi);
       if (bi >= p.E) bi = 0, bv = 0.f;  // NaN logits leave no candidate: keep the index in range
       const float pv = bv / s;
       if (lane == j) sel_v = pv, sel_i = bi;
       sum += pv;  // slot order, larger first
-      __syncwarp();
-      if (lane == 0) lg[bi] = -2.f;  // below every probability: not chosen again
-      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < kPerLane; ++c)
+        if (lane + 32 * c == bi) v[c] = -2.f;  // not chosen again
+    }
+    // rank of slot `lane` among the token's experts by index (ties: slot order)
+    int rank = 0;
+    for (int l = 0; l < p.k; ++l) {
+      const int other = __shfl_sync(0xffffffffu, sel_i, l);
+      rank += (other < sel_i) || (other == sel_i && l < lane);
     }
     if (lane < p.k) {
       const float w = p.norm_topk ? sel_v / sum : sel_v;
       const size_t at = static_cast<size_t>(t) * p.k + lane;
       p.topk_idx[at] = sel_i;
       p.topk_w[at] = w;
+      p.tok_rank[at] = rank;
       if (p.out_idx) p.out_idx[at] = sel_i;
       if (p.out_w) p.out_w[at] = w;
     }
   }
   __syncthreads();
+  // counts: a warp per expert, 32 pairs per ballot
   const int n = p.T * p.k;
-  for (int e = tid; e < p.E; e += blockDim.x) {
+  for (int e = warp; e < p.E; e += nw) {
     int c = 0;
-    for (int i = 0; i < n; ++i) c += p.topk_idx[i] == e;
-    cnt_s[e] = c;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int o = 0, a = 0;
-    for (int e = 0; e < p.E; ++e) {
-      off_s[e] = o;
-      o += cnt_s[e];
-      if (cnt_s[e]) p.act[a++] = e;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int i = i0 + lane;
+      c += __popc(__ballot_sync(0xffffffffu, i < n && p.topk_idx[i] == e));
     }
-    *p.n_act = a;
+    if (lane == 0) cnt_s[e] = c;
   }
   __syncthreads();
-  for (int e = tid; e < p.E; e += blockDim.x) {
-    p.cnt[e] = cnt_s[e];
-    p.off[e] = off_s[e];
-    int q = off_s[e];
-    for (int i = 0; i < n; ++i)
-      if (p.topk_idx[i] == e) {
-        p.pair_tok[q] = i / p.k;
-        p.slot_q[i] = q;
-        ++q;
+  // exclusive scans of the counts and of the routed flags (E <= 1024 = blockDim)
+  {
+    const int c = tid < p.E ? cnt_s[tid] : 0;
+    const int f = c > 0;
+    int sc = c, sf = f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, sc, o), b = __shfl_up_sync(0xffffffffu, sf, o);
+      if (lane >= o) sc += a, sf += b;
+    }
+    if (lane == 31) wsum[warp] = sc, wact[warp] = sf;
+    __syncthreads();
+    if (warp == 0) {
+      int a = wsum[lane], b = wact[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
+        if (lane >= o) a += x, b += y;
       }
+      wsum[lane] = a, wact[lane] = b;  // inclusive over warps
+    }
+    __syncthreads();
+    const int base_c = warp ? wsum[warp - 1] : 0, base_f = warp ? wact[warp - 1] : 0;
+    if (tid < p.E) {
+      off_s[tid] = base_c + sc - c;
+      p.cnt[tid] = c;
+      p.off[tid] = base_c + sc - c;
+      if (f) act_s[base_f + sf - 1] = tid;
+    }
+    if (tid == 0) *p.n_act = wact[31];
+  }
+  __syncthreads();
+  for (int a = tid; a < wact[31]; a += blockDim.x) p.act[a] = act_s[a];
+  // placement: pair i of expert e goes to off[e] + (pairs of e before i)
+  for (int e = warp; e < p.E; e += nw) {
+    int q = off_s[e];
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int i = i0 + lane;
+      const bool mine = i < n && p.topk_idx[i] == e;
+      const unsigned mask = __ballot_sync(0xffffffffu, mine);
+      if (mine) {
+        const int qi = q + __popc(mask & lt);
+        const int t = i / p.k;
+        p.pair_tok[qi] = t;
+        const size_t at = static_cast<size_t>(t) * p.k + p.tok_rank[i];
+        p.tok_q[at] = qi;
+        p.tok_w[at] = p.topk_w[i];
+      }
+      q += __popc(mask);
+    }
   }
 }
 
@@ -261,8 +320,93 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const MoeDev p) {
 //    else:   rows r of down (8 per warp), yd[q][r] = down_r . f[q].
 //    Persistent: CTA b takes items b, b + grid, ... of the list (routed
 //    expert slot, row tile), slot-major, until the slot passes n_act.
+// One pass of a warp's 8 weight rows over K with NG tokens (pairs q .. q+NG-1),
+// then its outputs.  Weight row i: (i < 4 ? b0 : b1) + (i % 4) * K, live when
+// i % 4 < (i < 4 ? n0 : n1).  The tokens' activations are staged in shared
+// memory chunk by chunk; each weight is unpacked once per step and used for
+// all NG tokens; two steps of weights are in flight.  Sums in element order.
+template <bool GATEUP, int NG>
+__device__ __forceinline__ void expert_pass(const MoeDev& p, const uint16_t* b0, const uint16_t* b1, int n0, int n1,
+                                            int K, int R, int r_base, int q, float* xs) {
+  constexpr int kOut = GATEUP ? kRowsPerWarp / 2 : kRowsPerWarp;
+  const int tid = threadIdx.x, lane = tid & 31;
+  auto row = [&](int i) { return (i < 4 ? b0 : b1) + static_cast<size_t>(i & 3) * K; };
+  auto live = [&](int i) { return (i & 3) < (i < 4 ? n0 : n1); };
+  float acc[kRowsPerWarp][NG];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int u = 0; u < NG; ++u) acc[i][u] = 0.f;
+  for (int c0 = 0; c0 < K; c0 += kKC) {
+    const int kc = min(kKC, K - c0);
+    // the chunk's first weights go out before the activations are staged
+    uint4 cur[kRowsPerWarp];
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i)
+      cur[i] = (live(i) && lane * 8 < kc) ? ld_weights(row(i) + c0 + lane * 8) : make_uint4(0, 0, 0, 0);
+    __syncthreads();  // the previous chunk's readers are done
+    const int kc4 = kc >> 2;  // K % 8 == 0: rows and chunks start on 16-byte boundaries
+    for (int idx = tid; idx < NG * kc4; idx += kThreads) {
+      const int u = idx / kc4, kk = (idx - u * kc4) * 4;
+      const float* src = GATEUP ? p.xn + static_cast<size_t>(p.pair_tok[q + u]) * K : p.f + static_cast<size_t>(q + u) * K;
+      *reinterpret_cast<float4*>(xs + u * kKC + kk) = *reinterpret_cast<const float4*>(src + c0 + kk);
+    }
+    __syncthreads();
+    for (int k0 = lane * 8; k0 < kc; k0 += 256) {
+      uint4 nxt[kRowsPerWarp];
+      const bool more = k0 + 256 < kc;
+#pragma unroll
+      for (int i = 0; i < kRowsPerWarp; ++i)
+        nxt[i] = (live(i) && more) ? ld_weights(row(i) + c0 + k0 + 256) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float4 xv[NG];
+#pragma unroll
+        for (int u = 0; u < NG; ++u) xv[u] = *reinterpret_cast<const float4*>(xs + u * kKC + k0 + 4 * half);
+#pragma unroll
+        for (int i = 0; i < kRowsPerWarp; ++i) {
+          const uint32_t w0 = half ? cur[i].z : cur[i].x, w1 = half ? cur[i].w : cur[i].y;
+          const float a0 = bf16_lo(w0), a1 = bf16_hi(w0), a2 = bf16_lo(w1), a3 = bf16_hi(w1);
+#pragma unroll
+          for (int u = 0; u < NG; ++u) {
+            float t = acc[i][u];
+            t = fmaf(a0, xv[u].x, t);
+            t = fmaf(a1, xv[u].y, t);
+            t = fmaf(a2, xv[u].z, t);
+            t = fmaf(a3, xv[u].w, t);
+            acc[i][u] = t;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kRowsPerWarp; ++i) cur[i] = nxt[i];
+    }
+  }
+  // every lane gets the sums; lane (i, u) stores one of them
+#pragma unroll
+  for (int i = 0; i < kOut; ++i) {
+#pragma unroll
+    for (int u = 0; u < NG; ++u) {
+      const float s0 = warp_sum(acc[i][u]);
+      float val = s0;
+      if constexpr (GATEUP) {
+        const float up = warp_sum(acc[kOut + i][u]);
+        val = (s0 / (1.0f + expf(-s0))) * up;  // silu(gate) * up
+      }
+      const int out = r_base + i;
+      if (lane == i * NG + u && out < R) {
+        const size_t qq = static_cast<size_t>(q + u);
+        if constexpr (GATEUP)
+          p.f[qq * p.I + out] = val;
+        else
+          p.yd[qq * p.h + out] = val;
+      }
+    }
+  }
+}
+
 template <bool GATEUP>
-__global__ void __launch_bounds__(kThreads) moe_expert_kernel(const MoeDev p) {
+__global__ void __launch_bounds__(kThreads, 2) moe_expert_kernel(const MoeDev p) {
   extern __shared__ float xs[];  // [kTG][kKC]
   const int K = GATEUP ? p.h : p.I;
   const int R = GATEUP ? p.I : p.h;  // output rows of an expert
@@ -270,7 +414,7 @@ __global__ void __launch_bounds__(kThreads) moe_expert_kernel(const MoeDev p) {
   constexpr int kTileRows = kWarps * kOut;
   const int tiles = (R + kTileRows - 1) / kTileRows;
   const int n_act = *p.n_act;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int warp = threadIdx.x >> 5;
   for (int item = blockIdx.x;; item += gridDim.x) {
     const int slot = item / tiles;
     if (slot >= n_act) break;  // uniform over the CTA
@@ -279,108 +423,30 @@ __global__ void __launch_bounds__(kThreads) moe_expert_kernel(const MoeDev p) {
     const int r_base = ((item - slot * tiles) * kWarps + warp) * kOut;
     const uint16_t* W = GATEUP ? p.gate_up + static_cast<size_t>(e) * 2 * p.I * p.h
                                : p.down + static_cast<size_t>(e) * p.h * p.I;
-    const uint16_t* rows[kRowsPerWarp];
-    bool live[kRowsPerWarp];
-#pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-      const int out = r_base + (GATEUP ? (i % kOut) : i);
-      live[i] = out < R;
-      const int wrow = GATEUP ? (i < kOut ? out : p.I + out) : out;  // gate rows, then the matching up rows
-      rows[i] = W + static_cast<size_t>(live[i] ? wrow : 0) * K;
-    }
+    // GATEUP: gate rows r_base .. +3, then the matching up rows I + r_base .. +3; else rows r_base .. +7
+    const int left = max(0, R - r_base);
+    const int n0 = min(4, left), n1 = GATEUP ? n0 : max(0, min(4, left - 4));
+    const uint16_t* b0 = W + static_cast<size_t>(left ? r_base : 0) * K;
+    const uint16_t* b1 = GATEUP ? W + static_cast<size_t>(left ? p.I + r_base : 0) * K : b0 + 4 * static_cast<size_t>(K);
     for (int g0 = 0; g0 < cnt; g0 += kTG) {
-      const int ng = min(kTG, cnt - g0);
-      float acc[kRowsPerWarp][kTG];
-#pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i)
-#pragma unroll
-        for (int u = 0; u < kTG; ++u) acc[i][u] = 0.f;
-      for (int c0 = 0; c0 < K; c0 += kKC) {
-        const int kc = min(kKC, K - c0);
-        // the chunk's first weights go out before the activations are staged
-        uint4 cur[kRowsPerWarp];
-#pragma unroll
-        for (int i = 0; i < kRowsPerWarp; ++i)
-          cur[i] = (live[i] && lane * 8 < kc) ? ld_weights(rows[i] + c0 + lane * 8) : make_uint4(0, 0, 0, 0);
-        __syncthreads();  // the previous chunk's readers are done
-        for (int idx = tid; idx < ng * kc; idx += kThreads) {
-          const int u = idx / kc, kk = idx - u * kc;
-          const int q = q0 + g0 + u;
-          const float* src = GATEUP ? p.xn + static_cast<size_t>(p.pair_tok[q]) * K : p.f + static_cast<size_t>(q) * K;
-          xs[u * kKC + kk] = src[c0 + kk];
-        }
-        __syncthreads();
-        for (int k0 = lane * 8; k0 < kc; k0 += 256) {
-          // two steps of weights in flight: the next step's loads before this step's math
-          uint4 nxt[kRowsPerWarp];
-          const bool more = k0 + 256 < kc;
-#pragma unroll
-          for (int i = 0; i < kRowsPerWarp; ++i)
-            nxt[i] = (live[i] && more) ? ld_weights(rows[i] + c0 + k0 + 256) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-          for (int u = 0; u < kTG; ++u) {
-            if (u < ng) {
-              const float4 a = *reinterpret_cast<const float4*>(xs + u * kKC + k0);
-              const float4 b = *reinterpret_cast<const float4*>(xs + u * kKC + k0 + 4);
-#pragma unroll
-              for (int i = 0; i < kRowsPerWarp; ++i) acc[i][u] = dot8(cur[i], a, b, acc[i][u]);
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < kRowsPerWarp; ++i) cur[i] = nxt[i];
-        }
-      }
-      // every lane gets the sums; lane (i, u) stores one of them
-#pragma unroll
-      for (int i = 0; i < kOut; ++i) {
-#pragma unroll
-        for (int u = 0; u < kTG; ++u) {
-          const float s0 = warp_sum(acc[i][u]);
-          float val = s0;
-          if constexpr (GATEUP) {
-            const float up = warp_sum(acc[kOut + i][u]);
-            val = (s0 / (1.0f + expf(-s0))) * up;  // silu(gate) * up
-          }
-          const int out = r_base + i;
-          if (lane == i * kTG + u && u < ng && out < R) {
-            const size_t q = static_cast<size_t>(q0 + g0 + u);
-            if constexpr (GATEUP)
-              p.f[q * p.I + out] = val;
-            else
-              p.yd[q * p.h + out] = val;
-          }
-        }
+      switch (min(kTG, cnt - g0)) {  // the pass's token count as a compile-time constant
+        case 1: expert_pass<GATEUP, 1>(p, b0, b1, n0, n1, K, R, r_base, q0 + g0, xs); break;
+        case 2: expert_pass<GATEUP, 2>(p, b0, b1, n0, n1, K, R, r_base, q0 + g0, xs); break;
+        default: expert_pass<GATEUP, 3>(p, b0, b1, n0, n1, K, R, r_base, q0 + g0, xs); break;
       }
     }
   }
 }
 
-// 4. x += sum over the token's experts, ascending expert index, of w * yd.
+// 5. x += sum over the token's experts, ascending expert index, of w * yd.
 __global__ void __launch_bounds__(kThreads) moe_combine_kernel(const MoeDev p) {
-  __shared__ int sq[kMaxTopK];
-  __shared__ float sw[kMaxTopK];
-  const int t = blockIdx.x, tid = threadIdx.x;
-  if (tid == 0) {
-    int es[kMaxTopK];
-    for (int j = 0; j < p.k; ++j) {
-      const size_t at = static_cast<size_t>(t) * p.k + j;
-      int e = p.topk_idx[at], q = p.slot_q[at];
-      float w = p.topk_w[at];
-      int pos = j;
-      while (pos > 0 && es[pos - 1] > e) {  // insertion sort by expert index
-        es[pos] = es[pos - 1];
-        sq[pos] = sq[pos - 1];
-        sw[pos] = sw[pos - 1];
-        --pos;
-      }
-      es[pos] = e, sq[pos] = q, sw[pos] = w;
-    }
-  }
-  __syncthreads();
+  const int t = blockIdx.x;
+  const int* tq = p.tok_q + static_cast<size_t>(t) * p.k;
+  const float* tw = p.tok_w + static_cast<size_t>(t) * p.k;
   float* xr = p.x + static_cast<size_t>(t) * p.h;
-  for (int c = tid; c < p.h; c += kThreads) {
+  for (int c = threadIdx.x; c < p.h; c += kThreads) {
     float y = 0.f;
-    for (int j = 0; j < p.k; ++j) y += sw[j] * p.yd[static_cast<size_t>(sq[j]) * p.h + c];
+    for (int j = 0; j < p.k; ++j) y += tw[j] * p.yd[static_cast<size_t>(tq[j]) * p.h + c];
     xr[c] = xr[c] + y;
   }
 }
@@ -475,7 +541,9 @@ extern "C" int vvli_cuda_moe_ffn(int device, const vvli_moe_args* a, void* strea
   p.act = reinterpret_cast<int*>(ws + L.act);
   p.n_act = reinterpret_cast<int*>(ws + L.nact);
   p.pair_tok = reinterpret_cast<int*>(ws + L.pair_tok);
-  p.slot_q = reinterpret_cast<int*>(ws + L.slot_q);
+  p.tok_rank = reinterpret_cast<int*>(ws + L.tok_rank);
+  p.tok_q = reinterpret_cast<int*>(ws + L.tok_q);
+  p.tok_w = reinterpret_cast<float*>(ws + L.tok_w);
   p.f = reinterpret_cast<float*>(ws + L.f);
   p.yd = reinterpret_cast<float*>(ws + L.yd);
   p.out_idx = a->topk_index, p.out_w = a->topk_weight;
@@ -485,7 +553,7 @@ extern "C" int vvli_cuda_moe_ffn(int device, const vvli_moe_args* a, void* strea
   if ((e = expert_residency(device, resident)) != cudaSuccess)
     return fail(VVLI_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
   const size_t logits_smem = static_cast<size_t>(p.h) * sizeof(float);       // <= 32 KB
-  const size_t expert_smem = static_cast<size_t>(kTG) * kKC * sizeof(float);  // 32 KB
+  const size_t expert_smem = static_cast<size_t>(kTG) * kKC * sizeof(float);  // 24 KB
   moe_logits_kernel<<<dim3((p.E + kWarps - 1) / kWarps, p.T), kThreads, logits_smem, s>>>(p);
   moe_group_kernel<<<1, 1024, 0, s>>>(p);
   // persistent grids: no more CTAs than are resident at once, nor than (expert, tile) items
