@@ -8,7 +8,9 @@
 // 5.5.0, models/olmoe/modeling_olmoe.py: OlmoeTopKRouter, OlmoeExperts),
 // restated in oracle/moe_ref.py.
 //
-// Five launches on the caller's stream, HBM-bound on the expert weights:
+// Five launches on the caller's stream, HBM-bound on the expert weights; the
+// last four are programmatic dependents of the one before (each starts
+// while its predecessor runs and waits for it before reading its output):
 //   1. moe_logits_kernel, CTA = (8 experts, token): RMSNorm of the row in
 //      shared memory (written to the workspace once), a warp per router
 //      logit.
@@ -152,6 +154,7 @@ __global__ void __launch_bounds__(kThreads) moe_logits_kernel(const MoeDev p) {
   extern __shared__ float xs[];  // xn [h]
   __shared__ float red[kWarps];
   const int t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  grid_launch_dependents();  // the next kernel waits for this one's completion before reading
   const float* xr = p.x + static_cast<size_t>(t) * p.h;
   float ss = 0.f;
   for (int i = tid; i < p.h; i += kThreads) {
@@ -197,6 +200,8 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const MoeDev p) {
   __shared__ int wsum[32], wact[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   const unsigned lt = (1u << lane) - 1u;
+  grid_launch_dependents();
+  grid_dependency_wait();  // the router logits come from the previous kernel
   for (int t = warp; t < p.T; t += nw) {
     const float* lg = p.logits + static_cast<size_t>(t) * p.E;
     float v[kPerLane];  // expert lane + 32 c
@@ -413,6 +418,8 @@ __global__ void __launch_bounds__(kThreads, 2) moe_expert_kernel(const MoeDev p)
   constexpr int kOut = GATEUP ? kRowsPerWarp / 2 : kRowsPerWarp;
   constexpr int kTileRows = kWarps * kOut;
   const int tiles = (R + kTileRows - 1) / kTileRows;
+  grid_launch_dependents();
+  grid_dependency_wait();  // the routing (and for down, f) comes from the previous kernels
   const int n_act = *p.n_act;
   const int warp = threadIdx.x >> 5;
   for (int item = blockIdx.x;; item += gridDim.x) {
@@ -439,14 +446,30 @@ __global__ void __launch_bounds__(kThreads, 2) moe_expert_kernel(const MoeDev p)
 }
 
 // 5. x += sum over the token's experts, ascending expert index, of w * yd.
+//    The token's pair list goes to shared memory first; the experts' rows
+//    are loaded eight at a time and added in order.
 __global__ void __launch_bounds__(kThreads) moe_combine_kernel(const MoeDev p) {
-  const int t = blockIdx.x;
-  const int* tq = p.tok_q + static_cast<size_t>(t) * p.k;
-  const float* tw = p.tok_w + static_cast<size_t>(t) * p.k;
+  __shared__ int sq[kMaxTopK];
+  __shared__ float sw[kMaxTopK];
+  const int t = blockIdx.x, tid = threadIdx.x;
+  grid_dependency_wait();  // the pairs and yd come from the previous kernels
+  if (tid < p.k) {
+    sq[tid] = p.tok_q[static_cast<size_t>(t) * p.k + tid];
+    sw[tid] = p.tok_w[static_cast<size_t>(t) * p.k + tid];
+  }
+  __syncthreads();
   float* xr = p.x + static_cast<size_t>(t) * p.h;
-  for (int c = threadIdx.x; c < p.h; c += kThreads) {
+  for (int c = tid; c < p.h; c += kThreads) {
     float y = 0.f;
-    for (int j = 0; j < p.k; ++j) y += tw[j] * p.yd[static_cast<size_t>(tq[j]) * p.h + c];
+    int j = 0;
+    for (; j + 8 <= p.k; j += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = p.yd[static_cast<size_t>(sq[j + u]) * p.h + c];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) y += sw[j + u] * v[u];
+    }
+    for (; j < p.k; ++j) y += sw[j] * p.yd[static_cast<size_t>(sq[j]) * p.h + c];
     xr[c] = xr[c] + y;
   }
 }
@@ -555,13 +578,31 @@ extern "C" int vvli_cuda_moe_ffn(int device, const vvli_moe_args* a, void* strea
   const size_t logits_smem = static_cast<size_t>(p.h) * sizeof(float);       // <= 32 KB
   const size_t expert_smem = static_cast<size_t>(kTG) * kKC * sizeof(float);  // 24 KB
   moe_logits_kernel<<<dim3((p.E + kWarps - 1) / kWarps, p.T), kThreads, logits_smem, s>>>(p);
-  moe_group_kernel<<<1, 1024, 0, s>>>(p);
+  // the later kernels are programmatic dependents: they launch while the
+  // previous one runs and wait (griddepcontrol.wait) before reading its output
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  auto launch = [&](auto kernel, dim3 grid, int threads, size_t smem) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+  };
   // persistent grids: no more CTAs than are resident at once, nor than (expert, tile) items
   const long gu_items = static_cast<long>(p.E) * ((p.I + kWarps * kRowsPerWarp / 2 - 1) / (kWarps * kRowsPerWarp / 2));
   const long dn_items = static_cast<long>(p.E) * ((p.h + kWarps * kRowsPerWarp - 1) / (kWarps * kRowsPerWarp));
-  moe_expert_kernel<true><<<static_cast<unsigned>(std::min<long>(gu_items, resident[0])), kThreads, expert_smem, s>>>(p);
-  moe_expert_kernel<false><<<static_cast<unsigned>(std::min<long>(dn_items, resident[1])), kThreads, expert_smem, s>>>(p);
-  moe_combine_kernel<<<p.T, kThreads, 0, s>>>(p);
+  if ((e = launch(moe_group_kernel, dim3(1), 1024, 0)) == cudaSuccess &&
+      (e = launch(moe_expert_kernel<true>, dim3(static_cast<unsigned>(std::min<long>(gu_items, resident[0]))), kThreads,
+                  expert_smem)) == cudaSuccess &&
+      (e = launch(moe_expert_kernel<false>, dim3(static_cast<unsigned>(std::min<long>(dn_items, resident[1]))), kThreads,
+                  expert_smem)) == cudaSuccess)
+    e = launch(moe_combine_kernel, dim3(p.T), kThreads, 0);
+  if (e != cudaSuccess) return fail(VVLI_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(VVLI_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
   return VVLI_OK;
